@@ -1,0 +1,399 @@
+"""Benchmark: Q8_0 decode tokens/s of the Qwen3 runner on B200 (liblq8.so), one JSON line.
+
+Workload: Qwen3-8B architecture, seeded random-init Q8_0 weights, batch
+B (default 1) of 2048-token seeded prompts prefilled once, then greedy decode steps at
+context 2048+. A step = one decode step of every sequence (B tokens). The timed region
+replays the CUDA-graph decode step K times with tokens and KV caches resident in HBM;
+`e2e` times the same steps through the public C-ABI call lq_qwen3_decode_step with host
+token buffers (host->device copy of the input ids and device->host copy of the next ids
+inside the timed region). Every step streams all 8.1 GB of Q8_0 weights, 64x the 126 MB
+L2, so no L2 flush is needed between steps.
+
+Multi-GPU (torchrun, one rank per GPU): each rank runs its own replica (no data-path
+collective); value = tokens of all ranks / max-over-ranks time ("scaling": "weak").
+
+--impl reference: the reference's CPU path (the C restatement in oracle/, all host threads)
+on the same model config, bounded sample (short prompt), rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "qwen-omni-inference-rs_b200")
+for _p in (REPO, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+CONFIGS = {
+    "qwen3-8b": dict(hidden=4096, layers=36, n_heads=32, n_kv_heads=8, head_dim=128, inter=12288,
+                     vocab=151936, max_pos=40960, tied=0, eps=1e-6, theta=1e6, init_std=0.02, norm_std=0.0),
+    "qwen3-0.6b": dict(hidden=1024, layers=28, n_heads=16, n_kv_heads=8, head_dim=128, inter=3072,
+                       vocab=151936, max_pos=40960, tied=1, eps=1e-6, theta=1e6, init_std=0.02, norm_std=0.0),
+    "qwen3-32b": dict(hidden=5120, layers=64, n_heads=64, n_kv_heads=8, head_dim=128, inter=25600,
+                      vocab=151936, max_pos=40960, tied=0, eps=1e-6, theta=1e6, init_std=0.02, norm_std=0.0),
+}
+SEED = 1234
+METRIC = "Q8_0 decode tok/s"
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------ helpers
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def gemv_bytes(n: int, k: int, m: int) -> int:
+    """Algorithmic bytes of one Q8_0 GEMV launch: weights (qs + fp16 scales) read once, the
+    quantized activations (qs + fp16 scales) and the f32 outputs."""
+    return n * k + n * (k // 32) * 2 + m * k + m * (k // 32) * 2 + m * n * 4
+
+
+def time_gemv_launches(lq8, ctx, model, cfg, B, reps=2):
+    """CUDA-event duration of every decode GEMV launch shape (fused qkv, o, fused gate/up,
+    down) of every layer, on the model's own weights and stream; layers are walked in order so
+    each launch streams its weights from HBM (a layer's 205 MB exceed the L2)."""
+    import ctypes as C
+
+    import torch
+    H, I = cfg["hidden"], cfg["inter"]
+    kmax = max(H, I, cfg["n_heads"] * cfg["head_dim"])
+    dev = torch.device("cuda", ctx.device)
+    xq = torch.randint(-127, 128, (B, kmax), dtype=torch.int8, device=dev)
+    xd = torch.full((B, kmax // 32), 0x2000, dtype=torch.int16, device=dev)  # fp16 ~0.0078
+    nmax = max(2 * I, cfg["n_heads"] * cfg["head_dim"] + 2 * cfg["n_kv_heads"] * cfg["head_dim"], H)
+    y = torch.empty((B, nmax), dtype=torch.float32, device=dev)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=dev)
+    shapes = {}
+    for rep in range(reps):
+        evs = []
+        for layer in range(cfg["layers"]):
+            for kind in ("qkv", "o", "gate_up", "down"):
+                w = model.linear(layer, kind)
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                ctx.call("lq_q8_0_matmul", C.byref(w), xq.data_ptr(), xd.data_ptr(), B, y.data_ptr(), None, w.n)
+                e1.record(stream)
+                evs.append((kind, w.n, w.k, e0, e1))
+        ctx.synchronize()
+        if rep == 0:
+            continue  # warm-up pass
+        for kind, n, k, e0, e1 in evs:
+            s = shapes.setdefault(kind, {"n": n, "k": k, "ms": []})
+            s["ms"].append(e0.elapsed_time(e1))
+    return shapes
+
+
+def cpu_baseline_sample(O, cfgd, threads=1):
+    """The oracle (reference CPU path restated in C) on a bounded sample of the decode step:
+    one decode token after a 16-token prompt through the first 1 and 2 layers + LM head;
+    per-layer time = t2 - t1, extrapolated to the full layer count."""
+    cfg = O.make_config(**cfgd)
+    saved = O.get_threads()
+    times = {}
+    for nl in (1, 2):
+        O.set_threads(saved)
+        m = O.Qwen3Model(cfg, SEED, layers_limit=nl, ctx_max=32)
+        prompt = O.gen_tokens(SEED, 0, 16, cfg.vocab)
+        O.set_threads(threads)
+        m.forward(prompt[:15], 0)
+        t0 = time.perf_counter()
+        m.forward(prompt[15:16], 15)
+        times[nl] = time.perf_counter() - t0
+        m.close()
+    O.set_threads(saved)
+    per_layer = max(times[2] - times[1], 1e-9)
+    step = times[1] - per_layer + cfgd["layers"] * per_layer
+    return 1.0 / step, {"t_1layer_s": times[1], "t_2layer_s": times[2], "per_layer_s": per_layer}
+
+
+# ------------------------------------------------------------------------------ arms
+def run_reference(args, cfgd):
+    """Reference arm: the oracle (C restatement of the reference's Rust CPU path, Q8_0 linears)
+    with all host threads; each step is one greedy decode token of the full model after a
+    16-token prompt (a bounded sample of the 2048-context workload)."""
+    from oracle import oracle as O
+    O.build()
+    threads = os.cpu_count() or 1
+    O.set_threads(threads)
+    cfg = O.make_config(**cfgd)
+    ctx_max = 16 + args.warmup + args.steps + 2
+    m = O.Qwen3Model(cfg, SEED, ctx_max=ctx_max)
+    prompt = O.gen_tokens(SEED, 0, 16, cfg.vocab)
+    logits = m.forward(prompt, 0)
+    tok = O.argmax(logits)
+    pos = 16
+    for _ in range(args.warmup):
+        tok = O.argmax(m.forward(np.array([tok]), pos))
+        pos += 1
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        tok = O.argmax(m.forward(np.array([tok]), pos))
+        pos += 1
+    dt = time.perf_counter() - t0
+    value = args.steps / dt
+    sample = (f"{args.steps} greedy decode steps of the full {args.config} model (batch 1) after a 16-token "
+              f"prompt instead of 2048 (CPU prefill of 2048 tokens is out of reach), {threads} threads")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/f32",
+        "data": "synthetic (seeded random-init weights, seeded token ids)",
+        "config": {"workload": f"{args.config} greedy decode, batch 1", "batch": 1, "prompt": 16},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, cfgd, world, rank, local):
+    import torch
+
+    import build
+    import lq8
+    build.build()
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    B, L, K, W = args.batch, args.prompt, args.steps, args.warmup
+    ctx_max = L + W + 2 * K + 8 + 2
+    ctx = lq8.Context(local)
+    cfg = lq8.make_config(**cfgd)
+    t_create = time.perf_counter()
+    model = lq8.Qwen3ForCausalLM(ctx, cfg, SEED, max_batch=B, ctx_max=ctx_max)
+    t_create = time.perf_counter() - t_create
+    rng_stream = 1000 * rank
+    from oracle import oracle as O  # seeded token ids only (the generator is shared)
+    prompts = np.stack([O.gen_tokens(SEED, rng_stream + b, L, cfgd["vocab"]) for b in range(B)])
+    t_pre = time.perf_counter()
+    nxt = model.prefill(prompts)
+    t_pre = time.perf_counter() - t_pre
+    model.set_batch(B)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", local))
+
+    def barrier():
+        ctx.synchronize()
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident decode (value)
+    model.decode_device(W)
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    model.decode_device(K)
+    e1.record(stream)
+    barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    value = world * B * K / (ms / 1000.0)
+    launches = model.graph_kernels() * K
+
+    # ---- end to end through the host-buffer C-ABI call (e2e)
+    tok_buf = lq8.wrap_device(model.token_buffer_ptr(), (B,), "<i4")
+    ids = tok_buf.cpu().numpy().astype(np.int32)
+    for _ in range(2):
+        ids = model.decode_step(ids)
+    barrier()
+    e2 = torch.cuda.Event(enable_timing=True)
+    e3 = torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for _ in range(K):
+        ids = model.decode_step(ids)
+    e3.record(stream)
+    barrier()
+    ms_e2e = max_over_ranks(e2.elapsed_time(e3))
+    e2e = world * B * K / (ms_e2e / 1000.0)
+
+    # ---- roofline of the dominant kernel: the decode GEMV
+    shapes = time_gemv_launches(lq8, ctx, model, cfgd, B)
+    peak, peak_kind = peaks()
+    tot_b = tot_ms = 0.0
+    per_shape = {}
+    for kind, s in shapes.items():
+        b = gemv_bytes(s["n"], s["k"], B)
+        avg = sum(s["ms"]) / len(s["ms"])
+        per_shape[kind] = {"n": s["n"], "k": s["k"], "bytes": b, "avg_us": 1000 * avg,
+                           "gbs": b / (avg / 1000) / 1e9}
+        tot_b += b * len(s["ms"])
+        tot_ms += sum(s["ms"])
+    dom = per_shape["gate_up"]
+    traffic = None
+    tf = os.path.join(REPO, "profiles", "q8_gemv_traffic.txt")
+    if os.path.exists(tf):
+        for ln in open(tf):
+            if ln.startswith(f"traffic_bytes_per_launch gate_up B={B} "):
+                traffic = float(ln.split()[-1])
+    roofline = {
+        "bound": "hbm", "kernel": f"q8_gemv (gate/up fused, M={B}, N={dom['n']}, K={dom['k']})",
+        "achieved": dom["gbs"], "peak": peak, "unit": "GB/s", "frac": dom["gbs"] / peak,
+        "peak_kind": f"{peak_kind} copy bandwidth", "traffic": traffic,
+        "algorithmic_bytes_per_launch": dom["bytes"],
+        "all_decode_gemv_gbs": tot_b / (tot_ms / 1000) / 1e9,
+        "frac_of_8tbs_spec": dom["gbs"] / 8000.0,
+        "per_shape": per_shape,
+    }
+    wbytes = model.weight_bytes()
+    step_gbs = wbytes / (ms / K / 1000) / 1e9
+
+    # ---- CPU baseline (rank 0, N = 1 only)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        from oracle import oracle as O
+        O.build()
+        v, det = cpu_baseline_sample(O, cfgd, threads=1)
+        cpu = {"value": v, "unit": "tok/s", "cores": 1, "kind": "port",
+               "sample": (f"oracle (C restatement of the reference's single-threaded Rust CPU path with Q8_0 "
+                          f"linears), 1 thread: one decode token after a 16-token prompt through 1 and 2 of "
+                          f"{cfgd['layers']} layers + LM head, per-layer time extrapolated to the full model; "
+                          f"context 16 instead of 2048 (attention at 2048 would add about 9 % CPU time)"),
+               "detail": det}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8/f32",
+            "data": "synthetic (seeded random-init N(0,0.02) weights, seeded uniform token ids)",
+            "config": {"workload": f"{args.config} greedy decode after a {L}-token prefill, batch {B}",
+                       "model": args.config, "global_batch": B * world, "seq_len": L,
+                       "parallelism": f"dp{world} replicas" if world > 1 else "single GPU",
+                       "l2": "no flush: each step streams all Q8_0 weights (64x the L2)",
+                       "context_range": [L + W, L + W + K]},
+            "roofline": roofline,
+            "step_weight_gbs": step_gbs,
+            "weight_bytes_per_step": wbytes,
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B,
+                    "ms_per_step": ms_e2e / K},
+            "clocks": clk,
+            "gpu_launches": launches,
+            "setup_s": {"create": t_create, "prefill": t_pre},
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+    ctx.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="qwen3-8b", choices=sorted(CONFIGS))
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--prompt", type=int, default=2048)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    world, rank, local = dist_env()
+    cfgd = CONFIGS[args.config]
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference(args, cfgd)
+        return
+    run_ours(args, cfgd, world, rank, local)
+
+
+if __name__ == "__main__":
+    main()

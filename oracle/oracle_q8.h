@@ -1,0 +1,118 @@
+/*
+ * oracle_q8.h -- CPU restatement of lluda-inference's Qwen3 forward path with the
+ * Q8_0 linear layers, used ONLY as the checker for the CUDA library.
+ *
+ * TEST INFRASTRUCTURE. Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline /
+ * reference arm may load this code. The product library (liblq8.so) never links or calls it.
+ *
+ * Every function names the reference file:line it restates (paths inside the reference
+ * project, crate `lluda-inference`). The Q8_0 block format has no source in the reference
+ * (it is a roadmap item, README.md:24,32); it follows the published GGML Q8_0 algorithm
+ * (quantize_row_q8_0_ref / ggml_vec_dot_q8_0_q8_0 in ggml-quants.c), pinned here against
+ * gguf-py 0.19.0 `gguf.quants.Q8_0`, which states bit-exactness with that C code.
+ */
+#ifndef ORACLE_Q8_H
+#define ORACLE_Q8_H
+
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ORC_QK 32  /* elements per Q8_0 block */
+
+/* ---- scalar conversions ------------------------------------------------------------ */
+uint16_t orc_f32_to_bf16(float f);          /* bf16.rs:112-131 (bias 0x7FFF + lsb, RNE)     */
+float    orc_bf16_to_f32(uint16_t h);        /* bf16.rs:136-142 (exact shift)                 */
+uint16_t orc_f32_to_f16(float f);            /* IEEE binary16, round to nearest even          */
+float    orc_f16_to_f32(uint16_t h);         /* exact                                         */
+void orc_f32_to_bf16_array(const float* x, int64_t n, uint16_t* out);
+void orc_bf16_to_f32_array(const uint16_t* x, int64_t n, float* out);
+
+/* ---- seeded integer-exact generators (identical bits on CPU and GPU) ---------------- */
+uint64_t orc_splitmix64(uint64_t x);
+/* bf16 values approximating N(0, std^2): Irwin-Hall sum of four 16-bit uniforms, scaled by
+ * one IEEE f32 multiply and rounded RNE to bf16. `scale` = std / 37837.2266... as f32. */
+void orc_gen_bf16(uint64_t seed, uint64_t tensor_id, int64_t offset, int64_t count,
+                  float scale, uint16_t* out);
+/* token ids uniform in [0, vocab) */
+void orc_gen_tokens(uint64_t seed, uint64_t stream, int64_t count, int64_t vocab, int32_t* out);
+float orc_gen_scale(double std_dev);
+
+/* ---- Q8_0 (A6-A8) -------------------------------------------------------------------- */
+/* quantize rows of x[rows][k] (k % 32 == 0) into SoA qs[rows][k] + d[rows][k/32] (fp16 bits) */
+void orc_q8_0_quantize_f32(const float* x, int64_t rows, int64_t k, int8_t* qs, uint16_t* d);
+void orc_q8_0_quantize_bf16(const uint16_t* x, int64_t rows, int64_t k, int8_t* qs, uint16_t* d);
+/* GGML AoS blocks {fp16 d; int8 qs[32]} (34 bytes) <-> SoA */
+void orc_q8_0_pack_blocks(const int8_t* qs, const uint16_t* d, int64_t rows, int64_t k, uint8_t* blocks);
+void orc_q8_0_unpack_blocks(const uint8_t* blocks, int64_t rows, int64_t k, int8_t* qs, uint16_t* d);
+/* y[m][n] = sum_b (float)sumi_b * (dw[n][b] * dx[m][b]), b ascending, one f32 accumulator.
+ * abs_terms (optional) receives sum_b |term_b| per output, used to bound reorder error. */
+void orc_q8_0_matmul(const int8_t* xq, const uint16_t* xd, int64_t m,
+                     const int8_t* wq, const uint16_t* wd, int64_t n, int64_t k,
+                     float* y, float* abs_terms);
+/* Linear::forward with a Q8_0 weight: quantize each row of x, then orc_q8_0_matmul. */
+void orc_q8_0_linear_f32(const float* x, int64_t m, int64_t k,
+                         const int8_t* wq, const uint16_t* wd, int64_t n, float* y);
+void orc_q8_0_linear_bf16(const uint16_t* x, int64_t m, int64_t k,
+                          const int8_t* wq, const uint16_t* wd, int64_t n, float* y);
+
+/* ---- dense reference matmul (tensor.rs:2716-2753), used for the reference's known answers */
+void orc_matmul_2d(const float* a, int64_t m, int64_t k, const float* b, int64_t n, float* c);
+
+/* ---- small ops ------------------------------------------------------------------------ */
+/* RMSNorm (rms_norm.rs:123-177): x rounded to bf16, f32 sum of squares, bf16 output */
+void orc_rmsnorm_f32(const float* x, int64_t rows, int64_t dim, const uint16_t* w, float eps, uint16_t* out);
+void orc_rmsnorm_bf16(const uint16_t* x, int64_t rows, int64_t dim, const uint16_t* w, float eps, uint16_t* out);
+/* RoPE tables (rope.rs:77-128): cos/sin [max_pos][head_dim/2] in f32 from f64 */
+void orc_rope_tables(int64_t head_dim, int64_t max_pos, double theta, float* cos_t, float* sin_t);
+/* apply_rope_to_tensor (rope.rs:245-303) in place on x[bh][seq][head_dim], positions offset.. */
+void orc_rope_apply(float* x, int64_t bh, int64_t seq, int64_t head_dim, int64_t offset,
+                    const float* cos_t, const float* sin_t);
+float orc_silu(float x);                     /* tensor.rs:1955-1990 */
+/* argmax over n values, ties -> last index (tensor.rs:2451-2482, Rust max_by) */
+int64_t orc_argmax(const float* x, int64_t n);
+/* softmax over n values (tensor.rs:1913-1934) */
+void orc_softmax(float* x, int64_t n);
+/* attention for one (q head, query row): q[D], K/V rows [ctx][D] (stride ld), scores scaled,
+ * positions > causal_limit masked with -inf when masked != 0 (attention.rs:368-394). */
+void orc_attend_row(const float* q, const float* k, const float* v, int64_t ctx, int64_t ld,
+                    int64_t d, int masked, int64_t causal_limit, float* scratch, float* out);
+
+/* ---- Qwen3 model (model.rs, transformer.rs, attention.rs, mlp.rs) -------------------- */
+typedef struct {
+    int64_t hidden, layers, n_heads, n_kv_heads, head_dim, inter, vocab, max_pos;
+    int32_t tied;           /* tie_word_embeddings */
+    float eps;
+    double theta;
+    float init_std;         /* weights ~ N(0, init_std) (integer-exact generator) */
+    float norm_std;         /* 0 -> norm weights 1.0; else 1 + N(0,norm_std) */
+} orc_qwen3_config;
+
+typedef struct orc_model orc_model;
+/* Builds the model from the seeded generator. layers_limit>0 truncates the stack (CPU sample). */
+orc_model* orc_qwen3_create(const orc_qwen3_config* cfg, uint64_t seed, int64_t layers_limit,
+                            int64_t ctx_max);
+void orc_qwen3_destroy(orc_model* m);
+void orc_qwen3_clear(orc_model* m);
+/* Qwen3ForCausalLM::forward (model.rs:345-372): ids[L] at offset -> logits[vocab] of last row */
+int orc_qwen3_forward(orc_model* m, const int32_t* ids, int64_t L, int64_t offset, float* logits);
+/* generate() restricted to greedy decoding (generate.rs:611-661) */
+int orc_qwen3_generate(orc_model* m, const int32_t* prompt, int64_t L, int64_t new_tokens,
+                       int32_t* out_tokens, float* last_logits);
+/* Accessors used by the tests to hand the identical weights to the GPU */
+int64_t orc_qwen3_layers(const orc_model* m);
+const uint16_t* orc_qwen3_embed(const orc_model* m);      /* [vocab][hidden] bf16 */
+/* Q8_0 weight of a layer's linear (kind 0 q,1 k,2 v,3 o,4 gate,5 up,6 down; layer -1 kind 7
+ * = lm_head): returns rows, fills *qs / *d with the oracle's buffers. -1 if out of range. */
+int64_t orc_qwen3_linear(const orc_model* m, int64_t layer, int kind, const int8_t** qs,
+                         const uint16_t** d, int64_t* k);
+void orc_set_threads(int n);
+int orc_get_threads(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

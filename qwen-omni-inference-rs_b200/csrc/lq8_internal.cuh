@@ -1,0 +1,186 @@
+// lq8_internal.cuh -- shared host/device helpers of liblq8 (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/lq8.h"
+
+// ------------------------------------------------------------------------------------------
+// context
+// ------------------------------------------------------------------------------------------
+struct lq_ctx {
+    int device = 0;
+    int sm_count = 0;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    std::string last_error;
+    // scratch owned by the context (activation quantization of lq_q8_0_linear, attention
+    // partials); grown with cudaMalloc on demand, freed at lq_destroy
+    void* scratch = nullptr;
+    size_t scratch_bytes = 0;
+    int* err_flag = nullptr;      // device int[4]: kernels report bad inputs here
+};
+
+namespace lq {
+
+int set_error(lq_ctx* ctx, int code, const char* fmt, ...);
+int check_cuda(lq_ctx* ctx, cudaError_t e, const char* what);
+// host-side fault injection: LQ_FAULT=<entry point name> makes that entry fail
+bool fault_injected(const char* entry);
+// grow ctx scratch to at least `bytes`; returns LQ_OK or an error
+int ensure_scratch(lq_ctx* ctx, size_t bytes);
+// read + clear the device error flag (synchronises the stream)
+int consume_device_error(lq_ctx* ctx, const char* what);
+
+}  // namespace lq
+
+#define LQ_ENTRY(ctx, name)                                                                 \
+    do {                                                                                    \
+        if (!(ctx)) return LQ_ERR_INVALID_ARG;                                              \
+        if (lq::fault_injected(name))                                                       \
+            return lq::set_error((ctx), LQ_ERR_INJECTED, "%s: injected fault (LQ_FAULT)", name); \
+    } while (0)
+
+#define LQ_REQUIRE(ctx, cond, ...)                                                          \
+    do {                                                                                    \
+        if (!(cond)) return lq::set_error((ctx), LQ_ERR_INVALID_ARG, __VA_ARGS__);          \
+    } while (0)
+
+#define LQ_CUDA(ctx, expr)                                                                  \
+    do {                                                                                    \
+        cudaError_t e__ = (expr);                                                           \
+        if (e__ != cudaSuccess) return lq::check_cuda((ctx), e__, #expr);                   \
+    } while (0)
+
+#define LQ_LAUNCH_CHECK(ctx, what) LQ_CUDA(ctx, cudaGetLastError())
+
+// ------------------------------------------------------------------------------------------
+// device helpers
+// ------------------------------------------------------------------------------------------
+namespace lq {
+
+constexpr int QK = 32;
+
+// bf16.rs:112-131: f32 -> bf16 with bias 0x7FFF + lsb (wrapping 32-bit add)
+__host__ __device__ __forceinline__ uint16_t f32_to_bf16(float f) {
+#ifdef __CUDA_ARCH__
+    uint32_t bits = __float_as_uint(f);
+#else
+    uint32_t bits;
+    memcpy(&bits, &f, 4);
+#endif
+    return (uint16_t)((bits + 0x7FFFu + ((bits >> 16) & 1u)) >> 16);
+}
+__host__ __device__ __forceinline__ float bf16_to_f32(uint16_t h) {
+#ifdef __CUDA_ARCH__
+    return __uint_as_float((uint32_t)h << 16);
+#else
+    uint32_t u = (uint32_t)h << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+#endif
+}
+// round an f32 to the nearest bf16 value, kept in f32
+__device__ __forceinline__ float round_bf16(float f) { return bf16_to_f32(f32_to_bf16(f)); }
+
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+__device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
+
+// GGML Q8_0 scale for a block whose max |x| is amax: d = amax/127, id = d ? 1/d : 0
+__device__ __forceinline__ void q8_scale(float amax, float& d, float& id) {
+    d = __fdiv_rn(amax, 127.0f);
+    id = d != 0.0f ? __frcp_rn(d) : 0.0f;
+}
+// q = clamp(roundf(x*id), -127, 127) as int
+__device__ __forceinline__ int q8_quant(float x, float id) {
+    float r = roundf(__fmul_rn(x, id));
+    r = fminf(fmaxf(r, -127.0f), 127.0f);
+    return (int)r;
+}
+
+// streaming 128-bit load that does not allocate in L1
+__device__ __forceinline__ int4 ld_stream_v4(const void* p) {
+    int4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.s32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// orderable key of an f32 for "max value, ties -> highest index" 64-bit atomicMax
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+    if (v == 0.0f) v = 0.0f;  // -0 and +0 compare equal in the reference
+    uint32_t u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)u << 32) | (unsigned long long)(uint32_t)idx;
+}
+
+// SplitMix64 and the Irwin-Hall(4) generator shared with the CPU oracle
+__host__ __device__ __forceinline__ uint64_t splitmix64(uint64_t x) {
+    uint64_t z = x + 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+__host__ __device__ __forceinline__ uint64_t gen_key(uint64_t seed, uint64_t tensor_id) {
+    return splitmix64(seed ^ (tensor_id * 0xD1B54A32D192ED03ull));
+}
+inline float gen_scale(double std_dev) { return (float)(std_dev * 1.7320508075688772 / 65536.0); }
+__device__ __forceinline__ float gen_value(uint64_t key, uint64_t idx, float scale) {
+    uint64_t h = splitmix64(key + idx);
+    int32_t s = (int32_t)(h & 0xFFFFu) + (int32_t)((h >> 16) & 0xFFFFu) +
+                (int32_t)((h >> 32) & 0xFFFFu) + (int32_t)((h >> 48) & 0xFFFFu) - 131070;
+    return __fmul_rn((float)s, scale);
+}
+
+inline int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
+
+}  // namespace lq
+
+// kernels launched across translation units
+namespace lq {
+int launch_quantize_rows(lq_ctx* ctx, const void* src, lq_dtype dt, int64_t rows, int64_t k,
+                         int8_t* qs, uint16_t* d);
+int launch_q8_matmul(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd,
+                     int64_t m, float* y, const float* resid, int64_t ldy,
+                     unsigned long long* argmax_keys);
+int launch_fill_bf16(lq_ctx* ctx, uint64_t seed, uint64_t tid, int64_t offset, int64_t count,
+                     float scale, uint16_t* out);
+int launch_fill_norm(lq_ctx* ctx, uint64_t seed, uint64_t tid, int64_t count, float norm_std,
+                     uint16_t* out);
+int launch_argmax_finalize(lq_ctx* ctx, unsigned long long* keys, int64_t rows, int32_t* out,
+                           int32_t* pos_counter);
+size_t attention_scratch_bytes(int64_t rows, int64_t n_heads, int64_t ctx_max, int64_t head_dim);
+int launch_attention(lq_ctx* ctx, const float* q, const float* kc, const float* vc, int64_t B,
+                     int64_t Hq, int64_t Hkv, int64_t L, int64_t pos0, const int32_t* pos0_dev,
+                     int64_t ctx_max, int64_t D, float* out, int8_t* xq, uint16_t* xd,
+                     void* scratch);
+int launch_rmsnorm(lq_ctx* ctx, const void* x, lq_dtype dt, int64_t rows, int64_t dim,
+                   const uint16_t* w, float eps, uint16_t* out, int8_t* xq, uint16_t* xd);
+int launch_qk_norm_rope_kv(lq_ctx* ctx, const float* qkv, int64_t B, int64_t L, int64_t Hq,
+                           int64_t Hkv, int64_t D, const uint16_t* qn, const uint16_t* kn,
+                           float eps, const float* cos_t, const float* sin_t, int64_t pos0,
+                           const int32_t* pos0_dev, float* q_out, float* kc, float* vc,
+                           int64_t ctx_max);
+int launch_silu_mul(lq_ctx* ctx, const float* gu, int64_t m, int64_t inter, float* h, int8_t* xq,
+                    uint16_t* xd);
+int launch_embedding(lq_ctx* ctx, const uint16_t* table, int64_t vocab, int64_t hidden,
+                     const int32_t* ids, int64_t n, float* out);
+}  // namespace lq

@@ -1,0 +1,640 @@
+// lq8_ops.cu -- the small Qwen3 ops that keep activations in HBM, fused with the Q8_0
+// quantization of their output where the next op is a Q8_0 linear.
+#include "lq8_internal.cuh"
+
+#include <cmath>
+#include <vector>
+
+namespace lq {
+
+__device__ __forceinline__ void set_err(int* flag, int code, int value) {
+    if (flag && atomicCAS(flag, 0, code) == 0) flag[1] = value;
+}
+
+// quantize_group8 is defined in lq8_q8.cu; a local copy keeps this unit self-contained
+__device__ __forceinline__ uint32_t quant_group8(const float v[4], int sub, uint16_t* d_out) {
+    float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+    float d, id;
+    q8_scale(amax, d, id);
+    if (sub == 0 && d_out) *d_out = f2h(d);
+    uint32_t q0 = (uint32_t)(q8_quant(v[0], id) & 0xFF), q1 = (uint32_t)(q8_quant(v[1], id) & 0xFF);
+    uint32_t q2 = (uint32_t)(q8_quant(v[2], id) & 0xFF), q3 = (uint32_t)(q8_quant(v[3], id) & 0xFF);
+    return q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
+}
+
+template <int THREADS>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    v = warp_sum(v);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = 0.0f;
+    if (warp == 0) {
+        t = lane < THREADS / 32 ? red[lane] : 0.0f;
+        t = warp_sum(t);
+        if (lane == 0) red[0] = t;
+    }
+    __syncthreads();
+    t = red[0];
+    __syncthreads();
+    return t;
+}
+
+// =========================================================================================
+// RMSNorm (rms_norm.rs:144-176) + optional Q8_0 quantization of the bf16 output.
+// One CTA per row; thread t handles 4 consecutive elements of each 1024-element chunk, so an
+// aligned 8-lane group covers one 32-element Q8_0 block.
+// =========================================================================================
+template <typename T>
+__device__ __forceinline__ void load4_any(const T* p, float v[4]);
+template <>
+__device__ __forceinline__ void load4_any<float>(const float* p, float v[4]) {
+    float4 t = *reinterpret_cast<const float4*>(p);
+    v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+}
+template <>
+__device__ __forceinline__ void load4_any<uint16_t>(const uint16_t* p, float v[4]) {
+    uint2 t = *reinterpret_cast<const uint2*>(p);
+    v[0] = bf16_to_f32((uint16_t)(t.x & 0xFFFF)); v[1] = bf16_to_f32((uint16_t)(t.x >> 16));
+    v[2] = bf16_to_f32((uint16_t)(t.y & 0xFFFF)); v[3] = bf16_to_f32((uint16_t)(t.y >> 16));
+}
+
+template <typename T, int THREADS>
+__global__ void __launch_bounds__(THREADS)
+rmsnorm_kernel(const T* __restrict__ x, int dim, const uint16_t* __restrict__ w, float eps,
+               uint16_t* __restrict__ out, int8_t* __restrict__ xq, uint16_t* __restrict__ xd) {
+    __shared__ float red[32];
+    const int row = blockIdx.x;
+    const T* xr = x + (size_t)row * dim;
+    float ss = 0.0f;
+    for (int base = 0; base < dim; base += THREADS * 4) {
+        int e = base + threadIdx.x * 4;
+        if (e < dim) {
+            float v[4];
+            load4_any<T>(xr + e, v);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                float r = round_bf16(v[i]);  // F32 input is rounded to bf16 first (rms_norm.rs:144)
+                ss = __fadd_rn(ss, __fmul_rn(r, r));
+            }
+        }
+    }
+    ss = block_sum<THREADS>(ss, red);
+    const float mean = __fdiv_rn(ss, (float)dim);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    const int nb = dim >> 5;
+    for (int base = 0; base < dim; base += THREADS * 4) {
+        int e = base + threadIdx.x * 4;
+        bool valid = e < dim;
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        if (valid) {
+            load4_any<T>(xr + e, v);
+            uint2 wt = *reinterpret_cast<const uint2*>(w + e);
+            float wv[4] = {bf16_to_f32((uint16_t)(wt.x & 0xFFFF)), bf16_to_f32((uint16_t)(wt.x >> 16)),
+                           bf16_to_f32((uint16_t)(wt.y & 0xFFFF)), bf16_to_f32((uint16_t)(wt.y >> 16))};
+            uint16_t o[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                float r = round_bf16(v[i]);
+                o[i] = f32_to_bf16(__fmul_rn(__fmul_rn(r, inv), wv[i]));
+                v[i] = bf16_to_f32(o[i]);
+            }
+            if (out) {
+                uint2 ov;
+                ov.x = (uint32_t)o[0] | ((uint32_t)o[1] << 16);
+                ov.y = (uint32_t)o[2] | ((uint32_t)o[3] << 16);
+                *reinterpret_cast<uint2*>(out + (size_t)row * dim + e) = ov;
+            }
+        }
+        if (xq) {  // uniform branch: every lane takes part in the group shuffles
+            int sub = threadIdx.x & 7;
+            uint16_t* dptr = valid ? xd + (size_t)row * nb + (e >> 5) : nullptr;
+            uint32_t q = quant_group8(v, sub, dptr);
+            if (valid) *reinterpret_cast<uint32_t*>(xq + (size_t)row * dim + e) = q;
+        }
+    }
+}
+
+int launch_rmsnorm(lq_ctx* ctx, const void* x, lq_dtype dt, int64_t rows, int64_t dim,
+                   const uint16_t* w, float eps, uint16_t* out, int8_t* xq, uint16_t* xd) {
+    if (rows == 0) return LQ_OK;
+    if (dim <= 1024) {
+        if (dt == LQ_DTYPE_F32)
+            rmsnorm_kernel<float, 128><<<(unsigned)rows, 128, 0, ctx->stream>>>((const float*)x, (int)dim, w, eps, out, xq, xd);
+        else
+            rmsnorm_kernel<uint16_t, 128><<<(unsigned)rows, 128, 0, ctx->stream>>>((const uint16_t*)x, (int)dim, w, eps, out, xq, xd);
+    } else {
+        if (dt == LQ_DTYPE_F32)
+            rmsnorm_kernel<float, 256><<<(unsigned)rows, 256, 0, ctx->stream>>>((const float*)x, (int)dim, w, eps, out, xq, xd);
+        else
+            rmsnorm_kernel<uint16_t, 256><<<(unsigned)rows, 256, 0, ctx->stream>>>((const uint16_t*)x, (int)dim, w, eps, out, xq, xd);
+    }
+    LQ_LAUNCH_CHECK(ctx, "rmsnorm");
+    return LQ_OK;
+}
+
+// =========================================================================================
+// per-head q/k RMSNorm + RoPE + KV-cache append (attention.rs:337-364, rope.rs:245-303).
+// One warp per (token row, head). head_dim = 128: lane p holds dims (2p, 2p+1) and
+// (64+2p, 64+2p+1), which is exactly one RoPE rotation pair set, so the rotation is
+// lane-local. Heads [0,Hq) are q, [Hq,Hq+Hkv) k, [Hq+Hkv, Hq+2Hkv) v (copied).
+// =========================================================================================
+__global__ void __launch_bounds__(256)
+qk_norm_rope_kv_kernel(const float* __restrict__ qkv, int B, int L, int Hq, int Hkv,
+                       const uint16_t* __restrict__ qn, const uint16_t* __restrict__ kn, float eps,
+                       const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                       int pos0, const int32_t* __restrict__ pos0_dev, float* __restrict__ q_out,
+                       float* __restrict__ kc, float* __restrict__ vc, int ctx_max, int* err) {
+    constexpr int D = 128, RD = 64;
+    const int lane = threadIdx.x & 31;
+    const int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int heads = Hq + 2 * Hkv;
+    if (item >= (int64_t)B * L * heads) return;
+    const int h = (int)(item % heads);
+    const int64_t row = item / heads;  // b*L + l
+    const int b = (int)(row / L), l = (int)(row % L);
+    const int p0 = pos0_dev ? *pos0_dev : pos0;
+    const int pos = p0 + l;
+    if (pos < 0 || pos >= ctx_max) {
+        if (lane == 0) set_err(err, 1, pos);
+        return;
+    }
+    const float* src = qkv + row * (int64_t)heads * D + (int64_t)h * D;
+    const int d0 = 2 * lane;
+    float2 a = *reinterpret_cast<const float2*>(src + d0);
+    float2 c = *reinterpret_cast<const float2*>(src + RD + d0);
+    if (h >= Hq + Hkv) {  // v: KvCache::append of the projection output (f32)
+        int kvh = h - Hq - Hkv;
+        float* dst = vc + (((int64_t)b * Hkv + kvh) * ctx_max + pos) * D;
+        *reinterpret_cast<float2*>(dst + d0) = a;
+        *reinterpret_cast<float2*>(dst + RD + d0) = c;
+        return;
+    }
+    const uint16_t* nw = h < Hq ? qn : kn;
+    // RmsNorm::forward on the bf16-rounded head vector
+    float v[4] = {round_bf16(a.x), round_bf16(a.y), round_bf16(c.x), round_bf16(c.y)};
+    float ss = __fadd_rn(__fadd_rn(__fmul_rn(v[0], v[0]), __fmul_rn(v[1], v[1])),
+                         __fadd_rn(__fmul_rn(v[2], v[2]), __fmul_rn(v[3], v[3])));
+    ss = warp_sum(ss);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), eps)));
+    const int dims[4] = {d0, d0 + 1, RD + d0, RD + d0 + 1};
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+        v[i] = round_bf16(__fmul_rn(__fmul_rn(v[i], inv), bf16_to_f32(nw[dims[i]])));
+    // RoPE: x1 = (v0, v1) first half, x2 = (v2, v3) second half; table column 2p
+    const float cs = cos_t[(int64_t)pos * RD + d0], sn = sin_t[(int64_t)pos * RD + d0];
+    float r0 = __fsub_rn(__fmul_rn(v[0], cs), __fmul_rn(v[2], sn));
+    float r1 = __fsub_rn(__fmul_rn(v[1], cs), __fmul_rn(v[3], sn));
+    float r2 = __fadd_rn(__fmul_rn(v[2], cs), __fmul_rn(v[0], sn));
+    float r3 = __fadd_rn(__fmul_rn(v[3], cs), __fmul_rn(v[1], sn));
+    float* dst;
+    if (h < Hq) dst = q_out + (((int64_t)b * Hq + h) * L + l) * D;
+    else dst = kc + (((int64_t)b * Hkv + (h - Hq)) * ctx_max + pos) * D;
+    *reinterpret_cast<float2*>(dst + d0) = make_float2(r0, r1);
+    *reinterpret_cast<float2*>(dst + RD + d0) = make_float2(r2, r3);
+}
+
+int launch_qk_norm_rope_kv(lq_ctx* ctx, const float* qkv, int64_t B, int64_t L, int64_t Hq,
+                           int64_t Hkv, int64_t D, const uint16_t* qn, const uint16_t* kn,
+                           float eps, const float* cos_t, const float* sin_t, int64_t pos0,
+                           const int32_t* pos0_dev, float* q_out, float* kc, float* vc,
+                           int64_t ctx_max) {
+    (void)D;
+    int64_t items = B * L * (Hq + 2 * Hkv);
+    if (items == 0) return LQ_OK;
+    int grid = ceil_div(items, 8);
+    qk_norm_rope_kv_kernel<<<grid, 256, 0, ctx->stream>>>(qkv, (int)B, (int)L, (int)Hq, (int)Hkv, qn, kn, eps,
+                                                          cos_t, sin_t, (int)pos0, pos0_dev, q_out, kc, vc,
+                                                          (int)ctx_max, ctx->err_flag);
+    LQ_LAUNCH_CHECK(ctx, "qk_norm_rope_kv");
+    return LQ_OK;
+}
+
+// =========================================================================================
+// attention (attention.rs:366-399): split over the key positions (flash-decoding). A CTA owns
+// one (query row, kv head, chunk of ATT_C positions) and all G = Hq/Hkv query heads of that
+// kv head (repeat_kv folded in). Partials (max, sum, unnormalised output) go to scratch; the
+// combine kernel merges the chunks and quantizes the [Hq*D] output row to Q8_0.
+// =========================================================================================
+constexpr int ATT_C = 128;  // positions per chunk (= threads per CTA)
+constexpr int ATT_D = 128;
+constexpr int ATT_GMAX = 8;
+
+__global__ void __launch_bounds__(ATT_C)
+attn_partial_kernel(const float* __restrict__ q, const float* __restrict__ kc,
+                    const float* __restrict__ vc, int Hq, int Hkv, int L, int pos0,
+                    const int32_t* __restrict__ pos0_dev, int ctx_max, float* __restrict__ part_o,
+                    float* __restrict__ part_ml, int nsplit) {
+    const int G = Hq / Hkv;
+    const int split = blockIdx.x, kvh = blockIdx.y;
+    const int64_t row = blockIdx.z;  // b*L + l
+    const int b = (int)(row / L), l = (int)(row % L);
+    const int p0 = pos0_dev ? *pos0_dev : pos0;
+    const int limit = p0 + l;  // last visible position (causal)
+    const int j0 = split * ATT_C;
+    const int tid = threadIdx.x;
+    __shared__ float qs[ATT_GMAX][ATT_D];
+    __shared__ float ps[ATT_GMAX][ATT_C];
+    __shared__ float mls[ATT_GMAX][2];
+    const int64_t part_base = ((row * Hq) + (int64_t)kvh * G) * nsplit + split;  // + g*nsplit
+    if (j0 > limit || limit >= ctx_max) {
+        if (tid < G) {
+            part_ml[(part_base + (int64_t)tid * nsplit) * 2] = -INFINITY;
+            part_ml[(part_base + (int64_t)tid * nsplit) * 2 + 1] = 0.0f;
+        }
+        return;
+    }
+    const int j1 = min(j0 + ATT_C, limit + 1);
+    for (int i = tid; i < G * ATT_D; i += ATT_C) {
+        int g = i / ATT_D, d = i % ATT_D;
+        qs[g][d] = q[(((int64_t)b * Hq + kvh * G + g) * L + l) * ATT_D + d];
+    }
+    __syncthreads();
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)ATT_D));
+    const float* kbase = kc + ((int64_t)b * Hkv + kvh) * (int64_t)ctx_max * ATT_D;
+    const float* vbase = vc + ((int64_t)b * Hkv + kvh) * (int64_t)ctx_max * ATT_D;
+    {
+        const int j = j0 + tid;
+        float s[ATT_GMAX];
+#pragma unroll
+        for (int g = 0; g < ATT_GMAX; g++) s[g] = 0.0f;
+        if (j < j1) {
+            const float4* kr = reinterpret_cast<const float4*>(kbase + (int64_t)j * ATT_D);
+#pragma unroll 4
+            for (int d4 = 0; d4 < ATT_D / 4; d4++) {
+                float4 kv = __ldg(kr + d4);
+#pragma unroll
+                for (int g = 0; g < ATT_GMAX; g++) {
+                    if (g < G) {
+                        s[g] = __fadd_rn(s[g], __fmul_rn(qs[g][4 * d4 + 0], kv.x));
+                        s[g] = __fadd_rn(s[g], __fmul_rn(qs[g][4 * d4 + 1], kv.y));
+                        s[g] = __fadd_rn(s[g], __fmul_rn(qs[g][4 * d4 + 2], kv.z));
+                        s[g] = __fadd_rn(s[g], __fmul_rn(qs[g][4 * d4 + 3], kv.w));
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < ATT_GMAX; g++)
+            if (g < G) ps[g][tid] = (j < j1) ? __fmul_rn(s[g], scale) : -INFINITY;
+    }
+    __syncthreads();
+    // per head: chunk max, exp, sum (4 warps share the G heads)
+    const int lane = tid & 31, warp = tid >> 5;
+    for (int g = warp; g < G; g += ATT_C / 32) {
+        float m = -INFINITY;
+        for (int i = lane; i < ATT_C; i += 32) m = fmaxf(m, ps[g][i]);
+        m = warp_max(m);
+        float sum = 0.0f;
+        for (int i = lane; i < ATT_C; i += 32) {
+            float e = expf(__fsub_rn(ps[g][i], m));  // exp(-inf) = 0 for masked slots
+            ps[g][i] = e;
+            sum = __fadd_rn(sum, e);
+        }
+        sum = warp_sum(sum);
+        if (lane == 0) { mls[g][0] = m; mls[g][1] = sum; }
+    }
+    __syncthreads();
+    // out[g][d] = sum_j p[g][j] * v[j][d]; thread = dim
+    {
+        const int d = tid;
+        float acc[ATT_GMAX];
+#pragma unroll
+        for (int g = 0; g < ATT_GMAX; g++) acc[g] = 0.0f;
+        for (int j = j0; j < j1; j++) {
+            float vv = __ldg(vbase + (int64_t)j * ATT_D + d);
+#pragma unroll
+            for (int g = 0; g < ATT_GMAX; g++)
+                if (g < G) acc[g] = __fadd_rn(acc[g], __fmul_rn(ps[g][j - j0], vv));
+        }
+#pragma unroll
+        for (int g = 0; g < ATT_GMAX; g++)
+            if (g < G) part_o[(part_base + (int64_t)g * nsplit) * ATT_D + d] = acc[g];
+        if (tid < G) {
+            part_ml[(part_base + (int64_t)tid * nsplit) * 2] = mls[tid][0];
+            part_ml[(part_base + (int64_t)tid * nsplit) * 2 + 1] = mls[tid][1];
+        }
+    }
+}
+
+// one warp per (row, q head); lane holds dims 4*lane..4*lane+3
+__global__ void __launch_bounds__(256)
+attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
+                    int64_t rows, int Hq, int nsplit, float* __restrict__ out,
+                    int8_t* __restrict__ xq, uint16_t* __restrict__ xd) {
+    const int lane = threadIdx.x & 31;
+    const int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (item >= rows * Hq) return;  // whole warp
+    const int64_t base = item * nsplit;
+    float M = -INFINITY;
+    for (int s = 0; s < nsplit; s++) M = fmaxf(M, part_ml[(base + s) * 2]);
+    float Lsum = 0.0f;
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int s = 0; s < nsplit; s++) {
+        float ms = part_ml[(base + s) * 2];
+        if (ms == -INFINITY) continue;
+        float w = expf(__fsub_rn(ms, M));
+        Lsum = __fadd_rn(Lsum, __fmul_rn(w, part_ml[(base + s) * 2 + 1]));
+        float4 po = *reinterpret_cast<const float4*>(part_o + (base + s) * ATT_D + lane * 4);
+        o[0] = __fadd_rn(o[0], __fmul_rn(w, po.x));
+        o[1] = __fadd_rn(o[1], __fmul_rn(w, po.y));
+        o[2] = __fadd_rn(o[2], __fmul_rn(w, po.z));
+        o[3] = __fadd_rn(o[3], __fmul_rn(w, po.w));
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) o[i] = __fdiv_rn(o[i], Lsum);
+    const int64_t e = item * ATT_D + lane * 4;  // element index in the [rows][Hq*D] output
+    if (out) *reinterpret_cast<float4*>(out + e) = make_float4(o[0], o[1], o[2], o[3]);
+    if (xq) {
+        uint32_t qv = quant_group8(o, lane & 7, xd + (e >> 5));
+        *reinterpret_cast<uint32_t*>(xq + e) = qv;
+    }
+}
+
+size_t attention_scratch_bytes(int64_t rows, int64_t Hq, int64_t ctx_max, int64_t D) {
+    int64_t nsplit = (ctx_max + ATT_C - 1) / ATT_C;
+    size_t o = (size_t)(rows * Hq * nsplit * D) * 4;
+    o = (o + 255) & ~(size_t)255;
+    return o + (size_t)(rows * Hq * nsplit * 2) * 4;
+}
+
+int launch_attention(lq_ctx* ctx, const float* q, const float* kc, const float* vc, int64_t B,
+                     int64_t Hq, int64_t Hkv, int64_t L, int64_t pos0, const int32_t* pos0_dev,
+                     int64_t ctx_max, int64_t D, float* out, int8_t* xq, uint16_t* xd,
+                     void* scratch) {
+    (void)D;
+    int64_t rows = B * L;
+    if (rows == 0) return LQ_OK;
+    // with a host-known position only the chunks up to pos0+L are launched; with a device
+    // position (CUDA-graph decode) the grid covers ctx_max and idle chunks exit at once
+    int64_t span = pos0_dev ? ctx_max : std::min<int64_t>(ctx_max, pos0 + L);
+    int nsplit = ceil_div(span, ATT_C);
+    size_t obytes = (size_t)(rows * Hq * nsplit * ATT_D) * 4;
+    obytes = (obytes + 255) & ~(size_t)255;
+    float* part_o = (float*)scratch;
+    float* part_ml = (float*)((uint8_t*)scratch + obytes);
+    dim3 grid(nsplit, (unsigned)Hkv, (unsigned)rows);
+    attn_partial_kernel<<<grid, ATT_C, 0, ctx->stream>>>(q, kc, vc, (int)Hq, (int)Hkv, (int)L, (int)pos0, pos0_dev,
+                                                         (int)ctx_max, part_o, part_ml, nsplit);
+    LQ_LAUNCH_CHECK(ctx, "attn_partial");
+    int64_t items = rows * Hq;
+    attn_combine_kernel<<<ceil_div(items, 8), 256, 0, ctx->stream>>>(part_o, part_ml, rows, (int)Hq, nsplit, out,
+                                                                     xq, xd);
+    LQ_LAUNCH_CHECK(ctx, "attn_combine");
+    return LQ_OK;
+}
+
+// =========================================================================================
+// SiLU(gate) * up (mlp.rs:153-160; tensor.rs:1977-1986 x/(1+exp(-x)); mul f32) + Q8_0
+// =========================================================================================
+__global__ void __launch_bounds__(256)
+silu_mul_kernel(const float* __restrict__ gu, int64_t m, int inter, float* __restrict__ h,
+                int8_t* __restrict__ xq, uint16_t* __restrict__ xd) {
+    const int64_t nblk = m * (inter >> 5);
+    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t blk = gid >> 3;
+    const int sub = threadIdx.x & 7;
+    const bool valid = blk < nblk;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    int64_t row = 0, col = 0;
+    if (valid) {
+        row = blk / (inter >> 5);
+        col = (blk % (inter >> 5)) * 32 + sub * 4;
+        float4 g = *reinterpret_cast<const float4*>(gu + row * 2 * inter + col);
+        float4 u = *reinterpret_cast<const float4*>(gu + row * 2 * inter + inter + col);
+        float gg[4] = {g.x, g.y, g.z, g.w}, uu[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            float s = __fdiv_rn(gg[i], __fadd_rn(1.0f, expf(-gg[i])));
+            v[i] = __fmul_rn(s, uu[i]);
+        }
+        if (h) *reinterpret_cast<float4*>(h + row * inter + col) = make_float4(v[0], v[1], v[2], v[3]);
+    }
+    if (xq) {
+        uint32_t q = quant_group8(v, sub, valid ? xd + blk : nullptr);
+        if (valid) *reinterpret_cast<uint32_t*>(xq + row * inter + col) = q;
+    }
+}
+
+int launch_silu_mul(lq_ctx* ctx, const float* gu, int64_t m, int64_t inter, float* h, int8_t* xq,
+                    uint16_t* xd) {
+    int64_t threads = m * (inter / 32) * 8;
+    if (threads == 0) return LQ_OK;
+    silu_mul_kernel<<<ceil_div(threads, 256), 256, 0, ctx->stream>>>(gu, m, (int)inter, h, xq, xd);
+    LQ_LAUNCH_CHECK(ctx, "silu_mul");
+    return LQ_OK;
+}
+
+// =========================================================================================
+// embedding gather (embedding.rs:105-153), bf16 rows widened exactly to f32
+// =========================================================================================
+__global__ void embedding_kernel(const uint16_t* __restrict__ table, int64_t vocab, int hidden,
+                                 const int32_t* __restrict__ ids, int64_t n, float* __restrict__ out,
+                                 int* err) {
+    const int64_t row = blockIdx.x;
+    if (row >= n) return;
+    const int32_t id = ids[row];
+    const bool ok = id >= 0 && id < vocab;
+    if (!ok && threadIdx.x == 0) set_err(err, 2, id);
+    for (int c = threadIdx.x * 4; c < hidden; c += blockDim.x * 4) {
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (ok) {
+            uint2 t = *reinterpret_cast<const uint2*>(table + (int64_t)id * hidden + c);
+            o = make_float4(bf16_to_f32((uint16_t)(t.x & 0xFFFF)), bf16_to_f32((uint16_t)(t.x >> 16)),
+                            bf16_to_f32((uint16_t)(t.y & 0xFFFF)), bf16_to_f32((uint16_t)(t.y >> 16)));
+        }
+        *reinterpret_cast<float4*>(out + row * hidden + c) = o;
+    }
+}
+
+int launch_embedding(lq_ctx* ctx, const uint16_t* table, int64_t vocab, int64_t hidden,
+                     const int32_t* ids, int64_t n, float* out) {
+    if (n == 0) return LQ_OK;
+    embedding_kernel<<<(unsigned)n, 256, 0, ctx->stream>>>(table, vocab, (int)hidden, ids, n, out, ctx->err_flag);
+    LQ_LAUNCH_CHECK(ctx, "embedding");
+    return LQ_OK;
+}
+
+// =========================================================================================
+// argmax (tensor.rs:2451-2482): max value, ties -> highest index
+// =========================================================================================
+__global__ void __launch_bounds__(1024)
+argmax_kernel(const float* __restrict__ x, int64_t n, int32_t* __restrict__ out) {
+    __shared__ unsigned long long red[32];
+    const float* xr = x + (int64_t)blockIdx.x * n;
+    unsigned long long best = 0ull;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+        unsigned long long k = argmax_key(xr[i], (int)i);
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+        best = v > best ? v : best;
+    }
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        best = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0ull;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+            best = v > best ? v : best;
+        }
+        if (threadIdx.x == 0) out[blockIdx.x] = (int32_t)(uint32_t)(best & 0xFFFFFFFFull);
+    }
+}
+
+__global__ void argmax_finalize_kernel(unsigned long long* keys, int64_t rows, int32_t* out,
+                                       int32_t* pos_counter) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < rows) {
+        out[i] = (int32_t)(uint32_t)(keys[i] & 0xFFFFFFFFull);
+        keys[i] = 0ull;
+    }
+    if (i == 0 && pos_counter) *pos_counter += 1;
+}
+
+int launch_argmax_finalize(lq_ctx* ctx, unsigned long long* keys, int64_t rows, int32_t* out,
+                           int32_t* pos_counter) {
+    argmax_finalize_kernel<<<ceil_div(std::max<int64_t>(rows, 1), 128), 128, 0, ctx->stream>>>(keys, rows, out,
+                                                                                               pos_counter);
+    LQ_LAUNCH_CHECK(ctx, "argmax_finalize");
+    return LQ_OK;
+}
+
+}  // namespace lq
+
+// =========================================================================================
+// C ABI
+// =========================================================================================
+extern "C" {
+
+int lq_rmsnorm(lq_ctx* ctx, const void* x, lq_dtype dt, int64_t rows, int64_t dim,
+               const uint16_t* w, float eps, uint16_t* out, int8_t* xq, uint16_t* xd) {
+    LQ_ENTRY(ctx, "lq_rmsnorm");
+    LQ_REQUIRE(ctx, dt == LQ_DTYPE_F32 || dt == LQ_DTYPE_BF16, "lq_rmsnorm: dtype must be F32 or BF16");
+    LQ_REQUIRE(ctx, rows >= 0 && dim > 0 && dim % 4 == 0, "lq_rmsnorm: dim=%lld must be a positive multiple of 4",
+               (long long)dim);
+    LQ_REQUIRE(ctx, !xq || dim % 32 == 0, "lq_rmsnorm: Q8_0 output needs dim %% 32 == 0");
+    LQ_REQUIRE(ctx, (xq == nullptr) == (xd == nullptr), "lq_rmsnorm: xq and xd go together");
+    LQ_REQUIRE(ctx, rows < (1ll << 31), "lq_rmsnorm: too many rows");
+    if (rows == 0) return LQ_OK;
+    LQ_REQUIRE(ctx, x && w && (out || xq), "lq_rmsnorm: NULL pointer");
+    return lq::launch_rmsnorm(ctx, x, dt, rows, dim, w, eps, out, xq, xd);
+}
+
+int lq_rope_tables(lq_ctx* ctx, int64_t head_dim, int64_t max_pos, double theta, float* cos_dev,
+                   float* sin_dev) {
+    LQ_ENTRY(ctx, "lq_rope_tables");
+    LQ_REQUIRE(ctx, head_dim > 0 && head_dim % 4 == 0 && max_pos > 0,
+               "lq_rope_tables: head_dim must be a multiple of 4 (rope.rs:77-83 requires even)");
+    LQ_REQUIRE(ctx, cos_dev && sin_dev, "lq_rope_tables: NULL pointer");
+    // rope.rs:89-117, evaluated in double on the host exactly like the reference
+    int64_t rd = head_dim / 2, half = rd / 2;
+    std::vector<double> inv(half);
+    for (int64_t i = 0; i < half; i++) inv[i] = 1.0 / std::pow(theta, (double)(2 * i) / (double)rd);
+    std::vector<float> c((size_t)(max_pos * rd)), s((size_t)(max_pos * rd));
+    for (int64_t p = 0; p < max_pos; p++)
+        for (int64_t i = 0; i < half; i++) {
+            double fr = (double)p * inv[i];
+            float cv = (float)std::cos(fr), sv = (float)std::sin(fr);
+            c[p * rd + 2 * i] = cv; c[p * rd + 2 * i + 1] = cv;
+            s[p * rd + 2 * i] = sv; s[p * rd + 2 * i + 1] = sv;
+        }
+    LQ_CUDA(ctx, cudaMemcpyAsync(cos_dev, c.data(), c.size() * 4, cudaMemcpyHostToDevice, ctx->stream));
+    LQ_CUDA(ctx, cudaMemcpyAsync(sin_dev, s.data(), s.size() * 4, cudaMemcpyHostToDevice, ctx->stream));
+    LQ_CUDA(ctx, cudaStreamSynchronize(ctx->stream));  // host vectors go out of scope
+    return LQ_OK;
+}
+
+int lq_qk_norm_rope_kv(lq_ctx* ctx, const float* qkv, int64_t B, int64_t L, int64_t Hq, int64_t Hkv,
+                       int64_t D, const uint16_t* qn, const uint16_t* kn, float eps, const float* cos_t,
+                       const float* sin_t, int64_t pos0, const int32_t* pos0_dev, float* q_out, float* kc,
+                       float* vc, int64_t ctx_max) {
+    LQ_ENTRY(ctx, "lq_qk_norm_rope_kv");
+    LQ_REQUIRE(ctx, D == 128, "lq_qk_norm_rope_kv: head_dim %lld unsupported (Qwen3 uses 128)", (long long)D);
+    LQ_REQUIRE(ctx, B >= 0 && L >= 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0, "lq_qk_norm_rope_kv: bad head counts");
+    LQ_REQUIRE(ctx, pos0_dev || (pos0 >= 0 && pos0 + L <= ctx_max),
+               "lq_qk_norm_rope_kv: positions [%lld, %lld) exceed ctx_max %lld", (long long)pos0,
+               (long long)(pos0 + L), (long long)ctx_max);
+    if (B == 0 || L == 0) return LQ_OK;
+    LQ_REQUIRE(ctx, qkv && qn && kn && cos_t && sin_t && q_out && kc && vc, "lq_qk_norm_rope_kv: NULL pointer");
+    return lq::launch_qk_norm_rope_kv(ctx, qkv, B, L, Hq, Hkv, D, qn, kn, eps, cos_t, sin_t, pos0, pos0_dev, q_out,
+                                      kc, vc, ctx_max);
+}
+
+int lq_attention(lq_ctx* ctx, const float* q, const float* kc, const float* vc, int64_t B, int64_t Hq,
+                 int64_t Hkv, int64_t L, int64_t pos0, const int32_t* pos0_dev, int64_t ctx_max, int64_t D,
+                 float* out, int8_t* xq, uint16_t* xd) {
+    LQ_ENTRY(ctx, "lq_attention");
+    LQ_REQUIRE(ctx, D == 128, "lq_attention: head_dim %lld unsupported (Qwen3 uses 128)", (long long)D);
+    LQ_REQUIRE(ctx, Hq > 0 && Hkv > 0 && Hq % Hkv == 0 && Hq / Hkv <= 8,
+               "lq_attention: need Hq %% Hkv == 0 and Hq/Hkv <= 8");
+    LQ_REQUIRE(ctx, pos0_dev || (pos0 >= 0 && pos0 + L <= ctx_max), "lq_attention: positions exceed ctx_max");
+    LQ_REQUIRE(ctx, (xq == nullptr) == (xd == nullptr), "lq_attention: xq and xd go together");
+    if (B == 0 || L == 0) return LQ_OK;
+    LQ_REQUIRE(ctx, q && kc && vc && (out || xq), "lq_attention: NULL pointer");
+    size_t need = lq::attention_scratch_bytes(B * L, Hq, ctx_max, D);
+    int rc = lq::ensure_scratch(ctx, need);
+    if (rc) return rc;
+    return lq::launch_attention(ctx, q, kc, vc, B, Hq, Hkv, L, pos0, pos0_dev, ctx_max, D, out, xq, xd,
+                                ctx->scratch);
+}
+
+int lq_silu_mul(lq_ctx* ctx, const float* gu, int64_t m, int64_t inter, float* h, int8_t* xq, uint16_t* xd) {
+    LQ_ENTRY(ctx, "lq_silu_mul");
+    LQ_REQUIRE(ctx, m >= 0 && inter > 0 && inter % 32 == 0, "lq_silu_mul: inter must be a multiple of 32");
+    LQ_REQUIRE(ctx, (xq == nullptr) == (xd == nullptr), "lq_silu_mul: xq and xd go together");
+    if (m == 0) return LQ_OK;
+    LQ_REQUIRE(ctx, gu && (h || xq), "lq_silu_mul: NULL pointer");
+    return lq::launch_silu_mul(ctx, gu, m, inter, h, xq, xd);
+}
+
+}  // extern "C"
+
+namespace lq {
+__global__ void add_kernel(const float* a, const float* b, int64_t n, float* out) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = __fadd_rn(a[i], b[i]);
+}
+}  // namespace lq
+
+extern "C" {
+
+int lq_add(lq_ctx* ctx, const float* a, const float* b, int64_t n, float* out) {
+    LQ_ENTRY(ctx, "lq_add");
+    LQ_REQUIRE(ctx, n >= 0, "lq_add: negative size");
+    if (n == 0) return LQ_OK;
+    LQ_REQUIRE(ctx, a && b && out, "lq_add: NULL pointer");
+    int grid = (int)std::min<int64_t>((n + 255) / 256, (int64_t)ctx->sm_count * 16);
+    lq::add_kernel<<<grid, 256, 0, ctx->stream>>>(a, b, n, out);
+    LQ_LAUNCH_CHECK(ctx, "add");
+    return LQ_OK;
+}
+
+int lq_embedding(lq_ctx* ctx, const uint16_t* table, int64_t vocab, int64_t hidden, const int32_t* ids, int64_t n,
+                 float* out) {
+    LQ_ENTRY(ctx, "lq_embedding");
+    LQ_REQUIRE(ctx, vocab > 0 && hidden > 0 && hidden % 4 == 0 && n >= 0, "lq_embedding: bad shape");
+    if (n == 0) return LQ_OK;
+    LQ_REQUIRE(ctx, table && ids && out, "lq_embedding: NULL pointer");
+    int rc = lq::launch_embedding(ctx, table, vocab, hidden, ids, n, out);
+    if (rc) return rc;
+    return lq::consume_device_error(ctx, "lq_embedding (token id out of range)");
+}
+
+int lq_argmax(lq_ctx* ctx, const float* x, int64_t rows, int64_t n, int32_t* out) {
+    LQ_ENTRY(ctx, "lq_argmax");
+    LQ_REQUIRE(ctx, rows >= 0 && n > 0 && n < (1ll << 31), "lq_argmax: bad shape");
+    if (rows == 0) return LQ_OK;
+    LQ_REQUIRE(ctx, x && out, "lq_argmax: NULL pointer");
+    lq::argmax_kernel<<<(unsigned)rows, 1024, 0, ctx->stream>>>(x, n, out);
+    LQ_LAUNCH_CHECK(ctx, "argmax");
+    return LQ_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,643 @@
+// lq8_q8.cu -- Q8_0 quantization, block packing and the Q8_0 x Q8_0 matmul kernels.
+//
+// Device layout of a Q8_0 tensor [n][k]: qs int8 [n][k] row-major and d fp16 [n][k/32]
+// row-major. Both the decode GEMV and the GEMM read this one layout; weights are written
+// once at load.
+#include "lq8_internal.cuh"
+
+namespace lq {
+
+// =========================================================================================
+// quantization: one 8-lane group per 32-element block, 4 elements per lane
+// =========================================================================================
+template <typename T>
+__device__ __forceinline__ void load4(const T* p, float v[4]);
+template <>
+__device__ __forceinline__ void load4<float>(const float* p, float v[4]) {
+    float4 t = *reinterpret_cast<const float4*>(p);
+    v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+}
+template <>
+__device__ __forceinline__ void load4<uint16_t>(const uint16_t* p, float v[4]) {
+    uint2 t = *reinterpret_cast<const uint2*>(p);
+    v[0] = bf16_to_f32((uint16_t)(t.x & 0xFFFF)); v[1] = bf16_to_f32((uint16_t)(t.x >> 16));
+    v[2] = bf16_to_f32((uint16_t)(t.y & 0xFFFF)); v[3] = bf16_to_f32((uint16_t)(t.y >> 16));
+}
+
+// Quantize 4 values held by each lane of an aligned 8-lane group (one Q8_0 block); returns
+// the packed int8x4 and writes the block scale through lane 0 of the group.
+__device__ __forceinline__ uint32_t quantize_group8(const float v[4], int sub, uint16_t* d_out) {
+    float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+    float d, id;
+    q8_scale(amax, d, id);
+    if (sub == 0 && d_out) *d_out = f2h(d);
+    uint32_t q0 = (uint32_t)(q8_quant(v[0], id) & 0xFF), q1 = (uint32_t)(q8_quant(v[1], id) & 0xFF);
+    uint32_t q2 = (uint32_t)(q8_quant(v[2], id) & 0xFF), q3 = (uint32_t)(q8_quant(v[3], id) & 0xFF);
+    return q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
+}
+
+template <typename T>
+__global__ void quantize_rows_kernel(const T* __restrict__ src, int64_t nblocks, int8_t* __restrict__ qs,
+                                     uint16_t* __restrict__ d) {
+    int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int64_t blk = gid >> 3;
+    int sub = threadIdx.x & 7;
+    bool valid = blk < nblocks;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (valid) load4<T>(src + blk * QK + sub * 4, v);
+    uint32_t q = quantize_group8(v, sub, valid ? d + blk : nullptr);
+    if (valid) reinterpret_cast<uint32_t*>(qs + blk * QK)[sub] = q;
+}
+
+int launch_quantize_rows(lq_ctx* ctx, const void* src, lq_dtype dt, int64_t rows, int64_t k,
+                         int8_t* qs, uint16_t* d) {
+    int64_t nblocks = rows * (k / QK);
+    if (nblocks == 0) return LQ_OK;
+    int64_t threads = nblocks * 8;
+    int grid = (int)((threads + 255) / 256);
+    if (dt == LQ_DTYPE_F32)
+        quantize_rows_kernel<float><<<grid, 256, 0, ctx->stream>>>((const float*)src, nblocks, qs, d);
+    else
+        quantize_rows_kernel<uint16_t><<<grid, 256, 0, ctx->stream>>>((const uint16_t*)src, nblocks, qs, d);
+    LQ_LAUNCH_CHECK(ctx, "quantize_rows");
+    return LQ_OK;
+}
+
+// =========================================================================================
+// GGML block packing: {fp16 d; int8 qs[32]} (34 bytes) <-> SoA
+// =========================================================================================
+__global__ void pack_blocks_kernel(const int8_t* __restrict__ qs, const uint16_t* __restrict__ d,
+                                   int64_t nblocks, uint8_t* __restrict__ out) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // byte index in output
+    if (i >= nblocks * 34) return;
+    int64_t b = i / 34;
+    int o = (int)(i - b * 34);
+    uint8_t v;
+    if (o < 2) v = (uint8_t)(d[b] >> (8 * o));
+    else v = (uint8_t)qs[b * QK + (o - 2)];
+    out[i] = v;
+}
+
+__global__ void unpack_blocks_kernel(const uint8_t* __restrict__ in, int64_t nblocks,
+                                     int8_t* __restrict__ qs, uint16_t* __restrict__ d) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= nblocks * 34) return;
+    int64_t b = i / 34;
+    int o = (int)(i - b * 34);
+    if (o == 0) d[b] = (uint16_t)(in[i] | (in[i + 1] << 8));
+    else if (o >= 2) qs[b * QK + (o - 2)] = (int8_t)in[i];
+}
+
+// =========================================================================================
+// decode GEMV, M <= 4 tokens: CUDA-core dp4a. One warp owns R weight rows over all of K;
+// lane l takes blocks l, l+32, ... (32 contiguous bytes each, two 128-bit streaming loads),
+// so a warp reads 1 KiB contiguous per row per step. Per-lane partial sums are combined by a
+// butterfly reduction. x (quantized activations) is read through L1.
+// =========================================================================================
+template <int M, int R, int U>
+__global__ void __launch_bounds__(256)
+q8_gemv_dp4a_kernel(const int8_t* __restrict__ wq, const uint16_t* __restrict__ wd, int N, int K,
+                    const int8_t* __restrict__ xq, const uint16_t* __restrict__ xd,
+                    const float* resid, float* y, int ldy, unsigned long long* argmax_keys) {
+    const int lane = threadIdx.x & 31;
+    const int row0 = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * R;
+    const int nb = K >> 5;
+    float acc[R][M];
+#pragma unroll
+    for (int r = 0; r < R; r++)
+#pragma unroll
+        for (int m = 0; m < M; m++) acc[r][m] = 0.0f;
+    const bool warp_active = row0 < N;
+    if (warp_active) {
+        const int8_t* wrow[R];
+        const uint16_t* drow[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            int row = min(row0 + r, N - 1);
+            wrow[r] = wq + (size_t)row * K;
+            drow[r] = wd + (size_t)row * nb;
+        }
+        for (int b0 = 0; b0 < nb; b0 += 32 * U) {
+            int4 w[U][R][2];
+            uint16_t dw[U][R];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                int b = b0 + u * 32 + lane;
+                if (b < nb) {
+#pragma unroll
+                    for (int r = 0; r < R; r++) {
+                        w[u][r][0] = ld_stream_v4(wrow[r] + (size_t)b * QK);
+                        w[u][r][1] = ld_stream_v4(wrow[r] + (size_t)b * QK + 16);
+                        dw[u][r] = drow[r][b];
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                int b = b0 + u * 32 + lane;
+                if (b < nb) {
+#pragma unroll
+                    for (int m = 0; m < M; m++) {
+                        const int4* xp = reinterpret_cast<const int4*>(xq + (size_t)m * K + (size_t)b * QK);
+                        int4 x0 = __ldg(xp), x1 = __ldg(xp + 1);
+                        float dx = h2f(xd[(size_t)m * nb + b]);
+#pragma unroll
+                        for (int r = 0; r < R; r++) {
+                            int s = 0;
+                            s = __dp4a(w[u][r][0].x, x0.x, s); s = __dp4a(w[u][r][0].y, x0.y, s);
+                            s = __dp4a(w[u][r][0].z, x0.z, s); s = __dp4a(w[u][r][0].w, x0.w, s);
+                            s = __dp4a(w[u][r][1].x, x1.x, s); s = __dp4a(w[u][r][1].y, x1.y, s);
+                            s = __dp4a(w[u][r][1].z, x1.z, s); s = __dp4a(w[u][r][1].w, x1.w, s);
+                            float sc = __fmul_rn(h2f(dw[u][r]), dx);
+                            acc[r][m] = __fadd_rn(acc[r][m], __fmul_rn((float)s, sc));
+                        }
+                    }
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < R; r++)
+#pragma unroll
+        for (int m = 0; m < M; m++) acc[r][m] = warp_sum(acc[r][m]);
+    // lane i < R*M writes output (i / M, i % M)
+    if (warp_active) {
+#pragma unroll
+        for (int r = 0; r < R; r++)
+#pragma unroll
+            for (int m = 0; m < M; m++) {
+                if (lane == r * M + m && row0 + r < N) {
+                    size_t o = (size_t)m * ldy + row0 + r;
+                    float v = acc[r][m];
+                    if (resid) v = __fadd_rn(resid[o], v);
+                    y[o] = v;
+                }
+            }
+    }
+    if (argmax_keys) {
+        // fused greedy argmax of the LM head: per-CTA max key in shared memory, then one
+        // 64-bit atomicMax per token per CTA (ties resolve to the highest row index)
+        __shared__ unsigned long long cta_keys[M];
+        if (threadIdx.x < M) cta_keys[threadIdx.x] = 0ull;
+        __syncthreads();
+        if (warp_active && lane == 0) {
+#pragma unroll
+            for (int m = 0; m < M; m++) {
+                unsigned long long key = 0ull;
+#pragma unroll
+                for (int r = 0; r < R; r++)
+                    if (row0 + r < N) {
+                        unsigned long long kk = argmax_key(acc[r][m], row0 + r);
+                        key = kk > key ? kk : key;
+                    }
+                atomicMax(&cta_keys[m], key);
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x < M && cta_keys[threadIdx.x]) atomicMax(argmax_keys + threadIdx.x, cta_keys[threadIdx.x]);
+    }
+}
+
+// =========================================================================================
+// Q8_0 GEMM on mma.sync m16n8k32 (s8 x s8 -> s32), one MMA = one Q8_0 block of K.
+// Weights are the MMA "A" operand (16 rows), tokens the "B" operand (8 columns). Tiles are
+// staged in shared memory with cp.async (BK = 64 bytes = 2 blocks per stage). Every output
+// is owned by one thread, which adds the per-block terms (float)sumi * (d_w*d_x) in
+// ascending block order with separately rounded multiply and add -- the oracle's order, so
+// results are bit-identical to it.
+// =========================================================================================
+constexpr int GEMM_BK = 64;            // bytes of K per stage
+constexpr int GEMM_LDS = GEMM_BK + 16; // padded smem row stride (conflict-free ldmatrix)
+constexpr int GEMM_STAGES = 4;
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
+    unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    int n = pred ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(n));
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem, bool pred) {
+    unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    int n = pred ? 4 : 0;
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(s), "l"(gmem), "r"(n));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N)); }
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t r[4], const void* smem) {
+    unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(s));
+}
+__device__ __forceinline__ void ldmatrix_x2(uint32_t r[2], const void* smem) {
+    unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+                 : "=r"(r[0]), "=r"(r[1])
+                 : "r"(s));
+}
+__device__ __forceinline__ void mma_s8(int c[4], const uint32_t a[4], const uint32_t b[2]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%11,%12,%13};"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(0), "r"(0), "r"(0),
+          "r"(0));
+}
+
+template <int BW, int BX, int WW, int WX>
+struct GemmCfg {
+    static constexpr int THREADS = WW * WX * 32;
+    static constexpr int TW = BW / WW;   // weight rows per warp
+    static constexpr int TX = BX / WX;   // tokens per warp
+    static constexpr int MI = TW / 16;   // m16 tiles per warp
+    static constexpr int NJ = TX / 8;    // n8 tiles per warp
+    static constexpr int W_BYTES = BW * GEMM_LDS;
+    static constexpr int X_BYTES = BX * GEMM_LDS;
+    static constexpr int WS_BYTES = BW * 2 * 2;  // 2 fp16 scales per row per stage
+    static constexpr int XS_BYTES = BX * 2 * 2;
+    static constexpr int STAGE = W_BYTES + X_BYTES + WS_BYTES + XS_BYTES;
+    static constexpr int SMEM = STAGE * GEMM_STAGES;
+};
+
+template <int BW, int BX, int WW, int WX>
+__global__ void __launch_bounds__(WW * WX * 32)
+q8_gemm_mma_kernel(const int8_t* __restrict__ wq, const uint16_t* __restrict__ wd, int N, int K,
+                   const int8_t* __restrict__ xq, const uint16_t* __restrict__ xd, int M,
+                   const float* resid, float* y, int ldy, unsigned long long* argmax_keys) {
+    using C = GemmCfg<BW, BX, WW, WX>;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int ww = warp % WW, wx = warp / WW;
+    const int n0 = blockIdx.x * BW;  // weight row base
+    const int m0 = blockIdx.y * BX;  // token base
+    const int nb = K >> 5;
+    const int nstages_k = (K + GEMM_BK - 1) / GEMM_BK;
+
+    auto stage_ptr = [&](int s) { return smem + s * C::STAGE; };
+
+    auto load_stage = [&](int s, int kt) {
+        uint8_t* base = stage_ptr(s);
+        uint8_t* sw = base;
+        uint8_t* sx = base + C::W_BYTES;
+        uint16_t* sws = reinterpret_cast<uint16_t*>(base + C::W_BYTES + C::X_BYTES);
+        uint16_t* sxs = reinterpret_cast<uint16_t*>(base + C::W_BYTES + C::X_BYTES + C::WS_BYTES);
+        const int kb = kt * GEMM_BK;  // byte offset in K
+        // weights: BW rows x 4 chunks of 16 B
+        for (int c = tid; c < BW * 4; c += C::THREADS) {
+            int r = c >> 2, ch = c & 3;
+            int row = n0 + r;
+            int kk = kb + ch * 16;
+            bool p = row < N && kk < K;
+            const int8_t* g = wq + (size_t)(p ? row : 0) * K + (p ? kk : 0);
+            cp_async16(sw + r * GEMM_LDS + ch * 16, g, p);
+        }
+        for (int c = tid; c < BX * 4; c += C::THREADS) {
+            int r = c >> 2, ch = c & 3;
+            int tok = m0 + r;
+            int kk = kb + ch * 16;
+            bool p = tok < M && kk < K;
+            const int8_t* g = xq + (size_t)(p ? tok : 0) * K + (p ? kk : 0);
+            cp_async16(sx + r * GEMM_LDS + ch * 16, g, p);
+        }
+        // scales: 2 blocks per row = 4 bytes; the 4-byte async copy needs an even block count
+        // per row (so that row*nb + b is even); otherwise plain loads
+        const int b = kb >> 5;
+        const bool even = (nb & 1) == 0;
+        for (int r = tid; r < BW; r += C::THREADS) {
+            int row = n0 + r;
+            if (row < N && even) {
+                cp_async4(sws + r * 2, wd + (size_t)row * nb + b, true);
+            } else {
+                sws[r * 2] = (row < N && b < nb) ? wd[(size_t)row * nb + b] : (uint16_t)0;
+                sws[r * 2 + 1] = (row < N && b + 1 < nb) ? wd[(size_t)row * nb + b + 1] : (uint16_t)0;
+            }
+        }
+        for (int r = tid; r < BX; r += C::THREADS) {
+            int tok = m0 + r;
+            if (tok < M && even) {
+                cp_async4(sxs + r * 2, xd + (size_t)tok * nb + b, true);
+            } else {
+                sxs[r * 2] = (tok < M && b < nb) ? xd[(size_t)tok * nb + b] : (uint16_t)0;
+                sxs[r * 2 + 1] = (tok < M && b + 1 < nb) ? xd[(size_t)tok * nb + b + 1] : (uint16_t)0;
+            }
+        }
+    };
+
+    float acc[C::MI][C::NJ][4];
+#pragma unroll
+    for (int i = 0; i < C::MI; i++)
+#pragma unroll
+        for (int j = 0; j < C::NJ; j++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) acc[i][j][e] = 0.0f;
+
+#pragma unroll
+    for (int s = 0; s < GEMM_STAGES - 1; s++) {
+        if (s < nstages_k) load_stage(s, s);
+        cp_async_commit();
+    }
+
+    const int g = lane >> 2, t = lane & 3;
+    for (int kt = 0; kt < nstages_k; kt++) {
+        cp_async_wait<GEMM_STAGES - 2>();
+        __syncthreads();
+        {
+            int nk = kt + GEMM_STAGES - 1;
+            if (nk < nstages_k) load_stage(nk % GEMM_STAGES, nk);
+            cp_async_commit();
+        }
+        const uint8_t* base = stage_ptr(kt % GEMM_STAGES);
+        const uint8_t* sw = base;
+        const uint8_t* sx = base + C::W_BYTES;
+        const uint16_t* sws = reinterpret_cast<const uint16_t*>(base + C::W_BYTES + C::X_BYTES);
+        const uint16_t* sxs = reinterpret_cast<const uint16_t*>(base + C::W_BYTES + C::X_BYTES + C::WS_BYTES);
+#pragma unroll
+        for (int kb = 0; kb < 2; kb++) {
+            uint32_t a[C::MI][4];
+            uint32_t bf[C::NJ][2];
+#pragma unroll
+            for (int i = 0; i < C::MI; i++) {
+                int r = ww * C::TW + i * 16 + (lane & 15);
+                ldmatrix_x4(a[i], sw + r * GEMM_LDS + kb * 32 + (lane >> 4) * 16);
+            }
+#pragma unroll
+            for (int j = 0; j < C::NJ; j++) {
+                int r = wx * C::TX + j * 8 + (lane & 7);
+                ldmatrix_x2(bf[j], sx + r * GEMM_LDS + kb * 32 + ((lane >> 3) & 1) * 16);
+            }
+            float dw[C::MI][2], dx[C::NJ][2];
+#pragma unroll
+            for (int i = 0; i < C::MI; i++) {
+                int r = ww * C::TW + i * 16 + g;
+                dw[i][0] = h2f(sws[r * 2 + kb]);
+                dw[i][1] = h2f(sws[(r + 8) * 2 + kb]);
+            }
+#pragma unroll
+            for (int j = 0; j < C::NJ; j++) {
+                int r = wx * C::TX + j * 8 + 2 * t;
+                dx[j][0] = h2f(sxs[r * 2 + kb]);
+                dx[j][1] = h2f(sxs[(r + 1) * 2 + kb]);
+            }
+#pragma unroll
+            for (int i = 0; i < C::MI; i++)
+#pragma unroll
+                for (int j = 0; j < C::NJ; j++) {
+                    int c[4];
+                    mma_s8(c, a[i], bf[j]);
+                    acc[i][j][0] = __fadd_rn(acc[i][j][0], __fmul_rn((float)c[0], __fmul_rn(dw[i][0], dx[j][0])));
+                    acc[i][j][1] = __fadd_rn(acc[i][j][1], __fmul_rn((float)c[1], __fmul_rn(dw[i][0], dx[j][1])));
+                    acc[i][j][2] = __fadd_rn(acc[i][j][2], __fmul_rn((float)c[2], __fmul_rn(dw[i][1], dx[j][0])));
+                    acc[i][j][3] = __fadd_rn(acc[i][j][3], __fmul_rn((float)c[3], __fmul_rn(dw[i][1], dx[j][1])));
+                }
+        }
+    }
+    cp_async_wait<0>();
+
+    // epilogue: element e of tile (i,j): weight row n = 16i + g + 8*(e>>1), token 8j + 2t + (e&1)
+#pragma unroll
+    for (int i = 0; i < C::MI; i++)
+#pragma unroll
+        for (int j = 0; j < C::NJ; j++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                int n = n0 + ww * C::TW + i * 16 + g + 8 * (e >> 1);
+                int m = m0 + wx * C::TX + j * 8 + 2 * t + (e & 1);
+                if (n < N && m < M) {
+                    size_t o = (size_t)m * ldy + n;
+                    float v = acc[i][j][e];
+                    if (resid) v = __fadd_rn(resid[o], v);
+                    y[o] = v;
+                }
+            }
+    if (argmax_keys) {
+        // per token: max over this thread's rows, then over the 8 lanes sharing t, then over
+        // the CTA in shared memory, then one global atomic per token per CTA
+        __shared__ unsigned long long cta_keys[BX];
+        for (int i = tid; i < BX; i += C::THREADS) cta_keys[i] = 0ull;
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < C::NJ; j++)
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                int m = m0 + wx * C::TX + j * 8 + 2 * t + h;
+                unsigned long long key = 0ull;
+#pragma unroll
+                for (int i = 0; i < C::MI; i++)
+#pragma unroll
+                    for (int e2 = 0; e2 < 2; e2++) {
+                        int n = n0 + ww * C::TW + i * 16 + g + 8 * e2;
+                        if (n < N && m < M) {
+                            unsigned long long kk = argmax_key(acc[i][j][e2 * 2 + h], n);
+                            key = kk > key ? kk : key;
+                        }
+                    }
+#pragma unroll
+                for (int o = 4; o < 32; o <<= 1) {
+                    unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+                    key = other > key ? other : key;
+                }
+                if (g == 0 && m < M) atomicMax(&cta_keys[m - m0], key);
+            }
+        __syncthreads();
+        for (int i = tid; i < BX; i += C::THREADS)
+            if (m0 + i < M && cta_keys[i]) atomicMax(argmax_keys + m0 + i, cta_keys[i]);
+    }
+}
+
+template <int BW, int BX, int WW, int WX>
+static int run_gemm(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd,
+                    int64_t m, float* y, const float* resid, int64_t ldy,
+                    unsigned long long* keys) {
+    using C = GemmCfg<BW, BX, WW, WX>;
+    static bool attr_done = false;  // per process; the attribute is per device function
+    if (!attr_done) {
+        LQ_CUDA(ctx, cudaFuncSetAttribute(q8_gemm_mma_kernel<BW, BX, WW, WX>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        attr_done = true;
+    }
+    dim3 grid(ceil_div(w->n, BW), ceil_div(m, BX));
+    q8_gemm_mma_kernel<BW, BX, WW, WX><<<grid, C::THREADS, C::SMEM, ctx->stream>>>(
+        w->qs, w->d, (int)w->n, (int)w->k, xq, xd, (int)m, resid, y, (int)ldy, keys);
+    LQ_LAUNCH_CHECK(ctx, "q8_gemm_mma");
+    return LQ_OK;
+}
+
+template <int M, int R>
+static int run_gemv(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd,
+                    float* y, const float* resid, int64_t ldy, unsigned long long* keys) {
+    constexpr int U = (R >= 4) ? 2 : 4;
+    int warps = ceil_div(w->n, R);
+    int grid = ceil_div(warps, 8);
+    q8_gemv_dp4a_kernel<M, R, U><<<grid, 256, 0, ctx->stream>>>(
+        w->qs, w->d, (int)w->n, (int)w->k, xq, xd, resid, y, (int)ldy, keys);
+    LQ_LAUNCH_CHECK(ctx, "q8_gemv_dp4a");
+    return LQ_OK;
+}
+
+template <int M>
+static int gemv_rows(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd,
+                     float* y, const float* resid, int64_t ldy, unsigned long long* keys) {
+    // enough warps to fill the SMs at least twice over: 148 SMs x 16 warps
+    int64_t target = (int64_t)ctx->sm_count * 32;
+    if (w->n / 4 >= target) return run_gemv<M, 4>(ctx, w, xq, xd, y, resid, ldy, keys);
+    if (w->n / 2 >= target) return run_gemv<M, 2>(ctx, w, xq, xd, y, resid, ldy, keys);
+    return run_gemv<M, 1>(ctx, w, xq, xd, y, resid, ldy, keys);
+}
+
+int launch_q8_matmul(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd,
+                     int64_t m, float* y, const float* resid, int64_t ldy,
+                     unsigned long long* keys) {
+    if (m <= 0 || w->n <= 0) return LQ_OK;
+    switch (m) {
+        case 1: return gemv_rows<1>(ctx, w, xq, xd, y, resid, ldy, keys);
+        case 2: return gemv_rows<2>(ctx, w, xq, xd, y, resid, ldy, keys);
+        case 3: return gemv_rows<3>(ctx, w, xq, xd, y, resid, ldy, keys);
+        case 4: return gemv_rows<4>(ctx, w, xq, xd, y, resid, ldy, keys);
+        default: break;
+    }
+    if (m <= 16) return run_gemm<128, 16, 8, 1>(ctx, w, xq, xd, m, y, resid, ldy, keys);
+    if (m <= 32) return run_gemm<128, 32, 8, 1>(ctx, w, xq, xd, m, y, resid, ldy, keys);
+    if (m <= 64) return run_gemm<128, 64, 4, 2>(ctx, w, xq, xd, m, y, resid, ldy, keys);
+    return run_gemm<128, 128, 4, 2>(ctx, w, xq, xd, m, y, resid, ldy, keys);
+}
+
+// =========================================================================================
+// seeded generator fill
+// =========================================================================================
+__global__ void fill_bf16_kernel(uint64_t key, int64_t offset, int64_t count, float scale,
+                                 uint16_t* __restrict__ out) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count;
+         i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = f32_to_bf16(gen_value(key, (uint64_t)(offset + i), scale));
+}
+
+__global__ void fill_norm_kernel(uint64_t key, int64_t count, float scale, int unit,
+                                 uint16_t* __restrict__ out) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count;
+         i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = unit ? (uint16_t)0x3F80 : f32_to_bf16(__fadd_rn(1.0f, gen_value(key, (uint64_t)i, scale)));
+}
+
+int launch_fill_bf16(lq_ctx* ctx, uint64_t seed, uint64_t tid, int64_t offset, int64_t count,
+                     float scale, uint16_t* out) {
+    if (count <= 0) return LQ_OK;
+    int grid = (int)std::min<int64_t>((count + 255) / 256, (int64_t)ctx->sm_count * 32);
+    fill_bf16_kernel<<<grid, 256, 0, ctx->stream>>>(gen_key(seed, tid), offset, count, scale, out);
+    LQ_LAUNCH_CHECK(ctx, "fill_bf16");
+    return LQ_OK;
+}
+
+int launch_fill_norm(lq_ctx* ctx, uint64_t seed, uint64_t tid, int64_t count, float norm_std,
+                     uint16_t* out) {
+    if (count <= 0) return LQ_OK;
+    int grid = (int)std::min<int64_t>((count + 255) / 256, 1024);
+    fill_norm_kernel<<<grid, 256, 0, ctx->stream>>>(gen_key(seed, tid), count, gen_scale(norm_std),
+                                                    norm_std == 0.0f, out);
+    LQ_LAUNCH_CHECK(ctx, "fill_norm");
+    return LQ_OK;
+}
+
+}  // namespace lq
+
+// =========================================================================================
+// C ABI
+// =========================================================================================
+extern "C" {
+
+static int check_q8_tensor(lq_ctx* ctx, const lq_q8_tensor* w, const char* what) {
+    LQ_REQUIRE(ctx, w != nullptr, "%s: weight is NULL", what);
+    LQ_REQUIRE(ctx, w->n > 0 && w->k > 0 && w->k % 32 == 0,
+               "%s: weight shape [%lld, %lld] invalid (k must be a positive multiple of 32)",
+               what, (long long)w->n, (long long)w->k);
+    LQ_REQUIRE(ctx, w->n < (1ll << 31) && w->k < (1ll << 31) && w->n * w->k < (1ll << 40),
+               "%s: weight too large", what);
+    LQ_REQUIRE(ctx, w->qs && w->d, "%s: weight buffers are NULL", what);
+    return LQ_OK;
+}
+
+int lq_q8_0_quantize(lq_ctx* ctx, const void* src, lq_dtype dt, int64_t rows, int64_t k,
+                     int8_t* qs, uint16_t* d) {
+    LQ_ENTRY(ctx, "lq_q8_0_quantize");
+    LQ_REQUIRE(ctx, dt == LQ_DTYPE_F32 || dt == LQ_DTYPE_BF16,
+               "lq_q8_0_quantize: source dtype must be F32 or BF16");
+    LQ_REQUIRE(ctx, rows >= 0 && k >= 0 && k % 32 == 0,
+               "lq_q8_0_quantize: k=%lld must be a multiple of 32", (long long)k);
+    if (rows == 0 || k == 0) return LQ_OK;
+    LQ_REQUIRE(ctx, src && qs && d, "lq_q8_0_quantize: NULL pointer");
+    return lq::launch_quantize_rows(ctx, src, dt, rows, k, qs, d);
+}
+
+int lq_q8_0_pack_blocks(lq_ctx* ctx, const int8_t* qs, const uint16_t* d, int64_t rows, int64_t k,
+                        uint8_t* blocks) {
+    LQ_ENTRY(ctx, "lq_q8_0_pack_blocks");
+    LQ_REQUIRE(ctx, rows >= 0 && k >= 0 && k % 32 == 0, "lq_q8_0_pack_blocks: k must be a multiple of 32");
+    int64_t nb = rows * (k / 32);
+    if (nb == 0) return LQ_OK;
+    LQ_REQUIRE(ctx, qs && d && blocks, "lq_q8_0_pack_blocks: NULL pointer");
+    int64_t bytes = nb * 34;
+    lq::pack_blocks_kernel<<<(int)((bytes + 255) / 256), 256, 0, ctx->stream>>>(qs, d, nb, blocks);
+    LQ_LAUNCH_CHECK(ctx, "pack_blocks");
+    return LQ_OK;
+}
+
+int lq_q8_0_unpack_blocks(lq_ctx* ctx, const uint8_t* blocks, int64_t rows, int64_t k, int8_t* qs,
+                          uint16_t* d) {
+    LQ_ENTRY(ctx, "lq_q8_0_unpack_blocks");
+    LQ_REQUIRE(ctx, rows >= 0 && k >= 0 && k % 32 == 0, "lq_q8_0_unpack_blocks: k must be a multiple of 32");
+    int64_t nb = rows * (k / 32);
+    if (nb == 0) return LQ_OK;
+    LQ_REQUIRE(ctx, qs && d && blocks, "lq_q8_0_unpack_blocks: NULL pointer");
+    int64_t bytes = nb * 34;
+    lq::unpack_blocks_kernel<<<(int)((bytes + 255) / 256), 256, 0, ctx->stream>>>(blocks, nb, qs, d);
+    LQ_LAUNCH_CHECK(ctx, "unpack_blocks");
+    return LQ_OK;
+}
+
+int lq_q8_0_matmul(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd,
+                   int64_t m, float* y, const float* resid, int64_t ldy) {
+    LQ_ENTRY(ctx, "lq_q8_0_matmul");
+    int rc = check_q8_tensor(ctx, w, "lq_q8_0_matmul");
+    if (rc) return rc;
+    LQ_REQUIRE(ctx, m >= 0 && m < (1 << 24), "lq_q8_0_matmul: m=%lld out of range", (long long)m);
+    if (ldy == 0) ldy = w->n;
+    LQ_REQUIRE(ctx, ldy >= w->n, "lq_q8_0_matmul: ldy < n");
+    if (m == 0) return LQ_OK;
+    LQ_REQUIRE(ctx, xq && xd && y, "lq_q8_0_matmul: NULL pointer");
+    return lq::launch_q8_matmul(ctx, w, xq, xd, m, y, resid, ldy, nullptr);
+}
+
+int lq_q8_0_linear(lq_ctx* ctx, const lq_q8_tensor* w, const void* x, lq_dtype dt, int64_t m,
+                   float* y) {
+    LQ_ENTRY(ctx, "lq_q8_0_linear");
+    int rc = check_q8_tensor(ctx, w, "lq_q8_0_linear");
+    if (rc) return rc;
+    LQ_REQUIRE(ctx, dt == LQ_DTYPE_F32 || dt == LQ_DTYPE_BF16, "lq_q8_0_linear: x dtype must be F32 or BF16");
+    LQ_REQUIRE(ctx, m >= 0 && m < (1 << 24), "lq_q8_0_linear: m=%lld out of range", (long long)m);
+    if (m == 0) return LQ_OK;
+    LQ_REQUIRE(ctx, x && y, "lq_q8_0_linear: NULL pointer");
+    size_t qbytes = (size_t)(m * w->k);
+    size_t off = (qbytes + 255) & ~(size_t)255;
+    size_t dbytes = (size_t)(m * (w->k / 32)) * 2;
+    rc = lq::ensure_scratch(ctx, off + dbytes);
+    if (rc) return rc;
+    int8_t* xq = (int8_t*)ctx->scratch;
+    uint16_t* xd = (uint16_t*)((uint8_t*)ctx->scratch + off);
+    rc = lq::launch_quantize_rows(ctx, x, dt, m, w->k, xq, xd);
+    if (rc) return rc;
+    return lq::launch_q8_matmul(ctx, w, xq, xd, m, y, nullptr, w->n, nullptr);
+}
+
+int lq_fill_bf16(lq_ctx* ctx, uint64_t seed, uint64_t tid, int64_t offset, int64_t count, double std_dev,
+                 uint16_t* out) {
+    LQ_ENTRY(ctx, "lq_fill_bf16");
+    LQ_REQUIRE(ctx, count >= 0 && offset >= 0, "lq_fill_bf16: negative size");
+    if (count == 0) return LQ_OK;
+    LQ_REQUIRE(ctx, out != nullptr, "lq_fill_bf16: NULL pointer");
+    return lq::launch_fill_bf16(ctx, seed, tid, offset, count, lq::gen_scale(std_dev), out);
+}
+
+}  // extern "C"

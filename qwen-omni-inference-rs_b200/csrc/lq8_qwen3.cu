@@ -1,0 +1,476 @@
+// lq8_qwen3.cu -- Qwen3ForCausalLM runner on the Q8_0 kernels (model.rs:273-372,
+// transformer.rs:180-204, attention.rs:318-403, mlp.rs:151-164, generate.rs:611-661).
+//
+// Weights are random-init from the seeded generator shared with the CPU oracle, quantized to
+// Q8_0 on the device once at creation. q/k/v share one fused [Nq+2Nk][H] Q8_0 buffer and
+// gate/up one [2I][H] buffer (rows are independent, so fusing changes no result), so one
+// decode layer streams four weight matrices. The decode step (L = 1) is captured once per
+// batch size into a CUDA graph that reads the position and the input tokens from device
+// memory and writes the next tokens back in place.
+#include "lq8_internal.cuh"
+
+#include <algorithm>
+#include <vector>
+
+namespace {
+
+enum { K_Q = 0, K_K, K_V, K_O, K_GATE, K_UP, K_DOWN, K_QNORM, K_KNORM, K_INNORM, K_POSTNORM };
+inline uint64_t tid_layer(int64_t l, int kind) { return ((uint64_t)l << 8) | (uint64_t)kind; }
+constexpr uint64_t TID_EMBED = 0x7FFF0001ull;
+constexpr uint64_t TID_LMHEAD = 0x7FFF0002ull;
+constexpr uint64_t TID_FINALNORM = 0x7FFF0003ull;
+
+struct Layer {
+    lq_q8_tensor qkv{}, o{}, gate_up{}, down{};
+    uint16_t *q_norm = nullptr, *k_norm = nullptr, *in_norm = nullptr, *post_norm = nullptr;
+};
+
+}  // namespace
+
+struct lq_model {
+    lq_ctx* ctx = nullptr;
+    lq_qwen3_config c{};
+    int64_t max_batch = 0, ctx_max = 0, rows_cap = 0;
+    int64_t Nq = 0, Nk = 0, Nqkv = 0, Hqd = 0;
+    std::vector<Layer> layers;
+    uint16_t* embed = nullptr;
+    uint16_t* final_norm = nullptr;
+    lq_q8_tensor lm_head{};
+    bool lm_head_owned = true;
+    float *kc = nullptr, *vc = nullptr;  // [layers][max_batch][Hkv][ctx_max][D]
+    float *cos_t = nullptr, *sin_t = nullptr;
+    // activations, sized for rows_cap rows
+    float* x = nullptr;        // residual stream [rows][H]
+    float* x_last = nullptr;   // last rows of each sequence [max_batch][H]
+    int8_t* xq = nullptr;      // quantized activation [rows][max(H, Hq*D, I)]
+    uint16_t* xd = nullptr;
+    float* qkv = nullptr;      // [rows][Nqkv]
+    float* q_rot = nullptr;    // [rows][Hq*D]
+    float* gu = nullptr;       // [rows][2I]
+    float* logits = nullptr;   // [max_batch][V]
+    void* att_scratch = nullptr;
+    size_t att_scratch_bytes = 0;
+    unsigned long long* keys = nullptr;  // argmax keys [max_batch]
+    int32_t* tokens = nullptr;           // [rows_cap]
+    int32_t* pos_dev = nullptr;
+    int64_t pos = 0;
+    cudaGraphExec_t exec = nullptr;
+    int64_t graph_batch = 0;
+    int64_t graph_kernels = 0;   // kernel nodes in the decode graph
+    std::vector<void*> allocs;
+};
+
+namespace {
+
+int dalloc(lq_model* m, void** p, size_t bytes) {
+    if (bytes == 0) bytes = 256;
+    cudaError_t e = cudaMalloc(p, bytes);
+    if (e != cudaSuccess) return lq::check_cuda(m->ctx, e, "cudaMalloc (model)");
+    m->allocs.push_back(*p);
+    return LQ_OK;
+}
+template <typename T>
+int dalloc_t(lq_model* m, T** p, size_t count) {
+    return dalloc(m, reinterpret_cast<void**>(p), count * sizeof(T));
+}
+
+int alloc_q8(lq_model* m, lq_q8_tensor* t, int64_t n, int64_t k) {
+    t->n = n;
+    t->k = k;
+    int rc = dalloc_t(m, &t->qs, (size_t)(n * k));
+    if (rc) return rc;
+    return dalloc_t(m, &t->d, (size_t)(n * (k / 32)));
+}
+
+// view of rows [r0, r0+n) of a Q8_0 tensor
+lq_q8_tensor rows_view(const lq_q8_tensor& t, int64_t r0, int64_t n) {
+    lq_q8_tensor v;
+    v.n = n;
+    v.k = t.k;
+    v.qs = t.qs + r0 * t.k;
+    v.d = t.d + r0 * (t.k / 32);
+    return v;
+}
+
+// generate bf16 weights for tensor id `tid` ([n][k]) and quantize into rows [r0, r0+n) of dst
+int gen_linear(lq_model* m, uint16_t* tmp, size_t tmp_elems, uint64_t seed, uint64_t tid,
+               const lq_q8_tensor& dst, int64_t r0, int64_t n) {
+    float sc = lq::gen_scale(m->c.init_std);
+    int64_t k = dst.k;
+    int64_t chunk_rows = std::max<int64_t>(1, (int64_t)(tmp_elems / (size_t)k));
+    for (int64_t r = 0; r < n; r += chunk_rows) {
+        int64_t rows = std::min(chunk_rows, n - r);
+        int rc = lq::launch_fill_bf16(m->ctx, seed, tid, r * k, rows * k, sc, tmp);
+        if (rc) return rc;
+        rc = lq::launch_quantize_rows(m->ctx, tmp, LQ_DTYPE_BF16, rows, k, dst.qs + (r0 + r) * k,
+                                      dst.d + (r0 + r) * (k / 32));
+        if (rc) return rc;
+    }
+    return LQ_OK;
+}
+
+void destroy_graph(lq_model* m) {
+    if (m->exec) cudaGraphExecDestroy(m->exec);
+    m->exec = nullptr;
+    m->graph_batch = 0;
+}
+
+// One forward pass over B sequences of L new tokens each at positions [pos0, pos0+L)
+// (pos_dev overrides pos0 when set). tokens [B*L] must already be in m->tokens. Writes the
+// greedy next token of each sequence to m->tokens[0..B) and the last-row logits to m->logits.
+int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_dev, bool bump_pos) {
+    lq_ctx* ctx = m->ctx;
+    const lq_qwen3_config& c = m->c;
+    const int64_t H = c.hidden, D = c.head_dim, Hq = c.n_heads, Hkv = c.n_kv_heads, I = c.inter;
+    const int64_t rows = B * L;
+    int rc;
+#define RC(expr) do { rc = (expr); if (rc) return rc; } while (0)
+    RC(lq::launch_embedding(ctx, m->embed, c.vocab, H, m->tokens, rows, m->x));
+    const size_t kv_layer = (size_t)(m->max_batch * Hkv * m->ctx_max * D);
+    for (size_t li = 0; li < m->layers.size(); li++) {
+        Layer& ly = m->layers[li];
+        float* kc = m->kc + li * kv_layer;
+        float* vc = m->vc + li * kv_layer;
+        // input_layernorm -> Q8_0
+        RC(lq::launch_rmsnorm(ctx, m->x, LQ_DTYPE_F32, rows, H, ly.in_norm, c.eps, nullptr, m->xq, m->xd));
+        // fused q/k/v projection
+        RC(lq::launch_q8_matmul(ctx, &ly.qkv, m->xq, m->xd, rows, m->qkv, nullptr, m->Nqkv, nullptr));
+        RC(lq::launch_qk_norm_rope_kv(ctx, m->qkv, B, L, Hq, Hkv, D, ly.q_norm, ly.k_norm, c.eps, m->cos_t,
+                                      m->sin_t, pos0, pos_dev, m->q_rot, kc, vc, m->ctx_max));
+        // attention -> Q8_0 rows [rows][Hq*D]
+        if (L == 1) {
+            RC(lq::launch_attention(ctx, m->q_rot, kc, vc, B, Hq, Hkv, 1, pos0, pos_dev, m->ctx_max, D, nullptr,
+                                    m->xq, m->xd, m->att_scratch));
+        } else {
+            // one sequence at a time keeps the split-K partials within att_scratch
+            for (int64_t b = 0; b < B; b++) {
+                RC(lq::launch_attention(ctx, m->q_rot + b * L * Hq * D, kc + b * Hkv * m->ctx_max * D,
+                                        vc + b * Hkv * m->ctx_max * D, 1, Hq, Hkv, L, pos0, pos_dev, m->ctx_max,
+                                        D, nullptr, m->xq + b * L * m->Hqd, m->xd + b * L * (m->Hqd / 32),
+                                        m->att_scratch));
+            }
+        }
+        // o_proj + residual (transformer.rs:194)
+        RC(lq::launch_q8_matmul(ctx, &ly.o, m->xq, m->xd, rows, m->x, m->x, H, nullptr));
+        // post_attention_layernorm -> Q8_0, gate/up, silu*up -> Q8_0, down + residual
+        RC(lq::launch_rmsnorm(ctx, m->x, LQ_DTYPE_F32, rows, H, ly.post_norm, c.eps, nullptr, m->xq, m->xd));
+        RC(lq::launch_q8_matmul(ctx, &ly.gate_up, m->xq, m->xd, rows, m->gu, nullptr, 2 * I, nullptr));
+        RC(lq::launch_silu_mul(ctx, m->gu, rows, I, nullptr, m->xq, m->xd));
+        RC(lq::launch_q8_matmul(ctx, &ly.down, m->xq, m->xd, rows, m->x, m->x, H, nullptr));
+    }
+    // final norm on the last row of each sequence (model.rs:194, :357-358)
+    const float* xlast = m->x;
+    if (L > 1) {
+        LQ_CUDA(ctx, cudaMemcpy2DAsync(m->x_last, H * sizeof(float), m->x + (L - 1) * H, L * H * sizeof(float),
+                                       H * sizeof(float), B, cudaMemcpyDeviceToDevice, ctx->stream));
+        xlast = m->x_last;
+    }
+    RC(lq::launch_rmsnorm(ctx, xlast, LQ_DTYPE_F32, B, H, m->final_norm, c.eps, nullptr, m->xq, m->xd));
+    // LM head with the greedy argmax fused into its epilogue
+    RC(lq::launch_q8_matmul(ctx, &m->lm_head, m->xq, m->xd, B, m->logits, nullptr, c.vocab, m->keys));
+    RC(lq::launch_argmax_finalize(ctx, m->keys, B, m->tokens, bump_pos ? m->pos_dev : nullptr));
+#undef RC
+    return LQ_OK;
+}
+
+int build_graph(lq_model* m, int64_t B) {
+    lq_ctx* ctx = m->ctx;
+    destroy_graph(m);
+    cudaGraph_t g = nullptr;
+    LQ_CUDA(ctx, cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = forward(m, B, 1, 0, m->pos_dev, true);
+    cudaError_t e = cudaStreamEndCapture(ctx->stream, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return lq::check_cuda(ctx, e, "cudaStreamEndCapture");
+    size_t nn = 0;
+    cudaGraphGetNodes(g, nullptr, &nn);
+    std::vector<cudaGraphNode_t> nodes(nn);
+    if (nn) cudaGraphGetNodes(g, nodes.data(), &nn);
+    m->graph_kernels = 0;
+    for (auto nd : nodes) {
+        cudaGraphNodeType t;
+        if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) m->graph_kernels++;
+    }
+    e = cudaGraphInstantiate(&m->exec, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return lq::check_cuda(ctx, e, "cudaGraphInstantiate");
+    m->graph_batch = B;
+    return LQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int lq_qwen3_destroy(lq_model* m) {
+    if (!m) return LQ_ERR_INVALID_ARG;
+    cudaSetDevice(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    destroy_graph(m);
+    for (void* p : m->allocs) cudaFree(p);
+    delete m;
+    return LQ_OK;
+}
+
+int lq_qwen3_create(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int64_t max_batch, int64_t ctx_max,
+                    lq_model** out) {
+    LQ_ENTRY(ctx, "lq_qwen3_create");
+    LQ_REQUIRE(ctx, cfg && out, "lq_qwen3_create: NULL argument");
+    *out = nullptr;
+    const lq_qwen3_config& c = *cfg;
+    LQ_REQUIRE(ctx, c.head_dim == 128, "lq_qwen3_create: head_dim must be 128");
+    LQ_REQUIRE(ctx, c.hidden > 0 && c.hidden % 32 == 0 && c.inter % 32 == 0 && c.inter > 0,
+               "lq_qwen3_create: hidden and intermediate sizes must be multiples of 32");
+    LQ_REQUIRE(ctx, c.n_heads > 0 && c.n_kv_heads > 0 && c.n_heads % c.n_kv_heads == 0 &&
+                        c.n_heads / c.n_kv_heads <= 8,
+               "lq_qwen3_create: need n_heads %% n_kv_heads == 0 and at most 8 q heads per kv head");
+    LQ_REQUIRE(ctx, c.layers > 0 && c.vocab > 0 && max_batch > 0 && ctx_max > 0, "lq_qwen3_create: bad sizes");
+    LQ_REQUIRE(ctx, c.max_pos <= 0 || ctx_max <= c.max_pos, "lq_qwen3_create: ctx_max exceeds max_pos");
+
+    lq_model* m = new lq_model();
+    m->ctx = ctx;
+    m->c = c;
+    m->max_batch = max_batch;
+    m->ctx_max = ctx_max;
+    const int64_t H = c.hidden, D = c.head_dim, Hq = c.n_heads, Hkv = c.n_kv_heads, I = c.inter, V = c.vocab;
+    m->Nq = Hq * D;
+    m->Nk = Hkv * D;
+    m->Nqkv = m->Nq + 2 * m->Nk;
+    m->Hqd = Hq * D;
+    // rows per forward pass: whole sequences, at most 8192 rows (or one sequence)
+    m->rows_cap = std::max<int64_t>(max_batch, std::min<int64_t>(max_batch * ctx_max, std::max<int64_t>(8192, ctx_max)));
+    int rc = LQ_OK;
+    auto fail = [&](int code) { lq_qwen3_destroy(m); return code; };
+#define RC(expr) do { rc = (expr); if (rc) return fail(rc); } while (0)
+    // weights
+    m->layers.resize((size_t)c.layers);
+    for (auto& ly : m->layers) {
+        RC(alloc_q8(m, &ly.qkv, m->Nqkv, H));
+        RC(alloc_q8(m, &ly.o, H, m->Hqd));
+        RC(alloc_q8(m, &ly.gate_up, 2 * I, H));
+        RC(alloc_q8(m, &ly.down, H, I));
+        RC(dalloc_t(m, &ly.q_norm, (size_t)D));
+        RC(dalloc_t(m, &ly.k_norm, (size_t)D));
+        RC(dalloc_t(m, &ly.in_norm, (size_t)H));
+        RC(dalloc_t(m, &ly.post_norm, (size_t)H));
+    }
+    RC(dalloc_t(m, &m->embed, (size_t)(V * H)));
+    RC(dalloc_t(m, &m->final_norm, (size_t)H));
+    RC(alloc_q8(m, &m->lm_head, V, H));
+    // generation scratch: the largest single weight, capped at 64 Mi elements
+    size_t tmp_elems = (size_t)std::min<int64_t>(std::max({I * H, m->Nq * H, H * m->Hqd}), 64ll << 20);
+    uint16_t* tmp = nullptr;
+    RC(dalloc_t(m, &tmp, tmp_elems));
+    const float sc = lq::gen_scale(c.init_std);
+    for (int64_t l = 0; l < c.layers; l++) {
+        Layer& ly = m->layers[(size_t)l];
+        RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_Q), ly.qkv, 0, m->Nq));
+        RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_K), ly.qkv, m->Nq, m->Nk));
+        RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_V), ly.qkv, m->Nq + m->Nk, m->Nk));
+        RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_O), ly.o, 0, H));
+        RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_GATE), ly.gate_up, 0, I));
+        RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_UP), ly.gate_up, I, I));
+        RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_DOWN), ly.down, 0, H));
+        RC(lq::launch_fill_norm(ctx, seed, tid_layer(l, K_QNORM), D, c.norm_std, ly.q_norm));
+        RC(lq::launch_fill_norm(ctx, seed, tid_layer(l, K_KNORM), D, c.norm_std, ly.k_norm));
+        RC(lq::launch_fill_norm(ctx, seed, tid_layer(l, K_INNORM), H, c.norm_std, ly.in_norm));
+        RC(lq::launch_fill_norm(ctx, seed, tid_layer(l, K_POSTNORM), H, c.norm_std, ly.post_norm));
+    }
+    RC(lq::launch_fill_bf16(ctx, seed, TID_EMBED, 0, V * H, sc, m->embed));
+    RC(lq::launch_fill_norm(ctx, seed, TID_FINALNORM, H, c.norm_std, m->final_norm));
+    if (c.tied) {
+        // tied embeddings: the LM head is the Q8_0 quantization of the bf16 table
+        RC(lq::launch_quantize_rows(ctx, m->embed, LQ_DTYPE_BF16, V, H, m->lm_head.qs, m->lm_head.d));
+    } else {
+        RC(gen_linear(m, tmp, tmp_elems, seed, TID_LMHEAD, m->lm_head, 0, V));
+    }
+    // caches and activations
+    size_t kv = (size_t)(c.layers * max_batch * Hkv * ctx_max * D);
+    RC(dalloc_t(m, &m->kc, kv));
+    RC(dalloc_t(m, &m->vc, kv));
+    RC(dalloc_t(m, &m->cos_t, (size_t)(ctx_max * D / 2)));
+    RC(dalloc_t(m, &m->sin_t, (size_t)(ctx_max * D / 2)));
+    RC(lq_rope_tables(ctx, D, ctx_max, c.theta, m->cos_t, m->sin_t));
+    const int64_t R = m->rows_cap;
+    const int64_t kmax = std::max({H, m->Hqd, I});
+    RC(dalloc_t(m, &m->x, (size_t)(R * H)));
+    RC(dalloc_t(m, &m->x_last, (size_t)(max_batch * H)));
+    RC(dalloc_t(m, &m->xq, (size_t)(R * kmax)));
+    RC(dalloc_t(m, &m->xd, (size_t)(R * kmax / 32)));
+    RC(dalloc_t(m, &m->qkv, (size_t)(R * m->Nqkv)));
+    RC(dalloc_t(m, &m->q_rot, (size_t)(R * m->Hqd)));
+    RC(dalloc_t(m, &m->gu, (size_t)(R * 2 * I)));
+    RC(dalloc_t(m, &m->logits, (size_t)(max_batch * V)));
+    RC(dalloc_t(m, &m->keys, (size_t)max_batch));
+    RC(dalloc_t(m, &m->tokens, (size_t)R));
+    RC(dalloc_t(m, &m->pos_dev, 1));
+    // attention partials: decode (max_batch rows) or one prefill sequence (<= R rows)
+    int64_t att_rows = std::max<int64_t>(max_batch, std::min<int64_t>(R, ctx_max));
+    m->att_scratch_bytes = lq::attention_scratch_bytes(att_rows, Hq, ctx_max, D);
+    RC(dalloc(m, &m->att_scratch, m->att_scratch_bytes));
+    LQ_CUDA(ctx, cudaMemsetAsync(m->keys, 0, (size_t)max_batch * 8, ctx->stream));
+    LQ_CUDA(ctx, cudaMemsetAsync(m->pos_dev, 0, 4, ctx->stream));
+    LQ_CUDA(ctx, cudaMemsetAsync(m->kc, 0, kv * 4, ctx->stream));
+    LQ_CUDA(ctx, cudaMemsetAsync(m->vc, 0, kv * 4, ctx->stream));
+    LQ_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+#undef RC
+    *out = m;
+    return LQ_OK;
+}
+
+int lq_qwen3_reset(lq_model* m) {
+    if (!m) return LQ_ERR_INVALID_ARG;
+    LQ_ENTRY(m->ctx, "lq_qwen3_reset");
+    m->pos = 0;
+    LQ_CUDA(m->ctx, cudaMemsetAsync(m->pos_dev, 0, 4, m->ctx->stream));
+    return LQ_OK;
+}
+
+int lq_qwen3_prefill(lq_model* m, const int32_t* ids, int64_t B, int64_t L, int32_t* next, float* logits) {
+    if (!m) return LQ_ERR_INVALID_ARG;
+    lq_ctx* ctx = m->ctx;
+    LQ_ENTRY(ctx, "lq_qwen3_prefill");
+    LQ_REQUIRE(ctx, ids && next, "lq_qwen3_prefill: NULL argument");
+    LQ_REQUIRE(ctx, B > 0 && B <= m->max_batch && L > 0, "lq_qwen3_prefill: B=%lld (max %lld), L=%lld",
+               (long long)B, (long long)m->max_batch, (long long)L);
+    LQ_REQUIRE(ctx, L <= m->ctx_max && L <= m->rows_cap, "lq_qwen3_prefill: L=%lld exceeds ctx_max %lld",
+               (long long)L, (long long)m->ctx_max);
+    for (int64_t i = 0; i < B * L; i++)
+        LQ_REQUIRE(ctx, ids[i] >= 0 && ids[i] < m->c.vocab, "lq_qwen3_prefill: token id %d out of range", ids[i]);
+    // whole sequences per pass; the KV caches of sequence b live at batch slot b
+    int64_t per_pass = std::max<int64_t>(1, m->rows_cap / L);
+    const int64_t H = m->c.hidden, D = m->c.head_dim, Hkv = m->c.n_kv_heads;
+    for (int64_t b0 = 0; b0 < B; b0 += per_pass) {
+        int64_t nb = std::min(per_pass, B - b0);
+        LQ_CUDA(ctx, cudaMemcpyAsync(m->tokens, ids + b0 * L, (size_t)(nb * L) * 4, cudaMemcpyHostToDevice,
+                                     ctx->stream));
+        // point the per-layer cache views at slot b0 by running forward on shifted caches
+        // (the cache layout is [layer][batch][Hkv][ctx][D]; a pass over sequences
+        // [b0, b0+nb) uses batch offsets b0.. inside each layer)
+        float* kc_save = m->kc;
+        float* vc_save = m->vc;
+        m->kc = kc_save + b0 * Hkv * m->ctx_max * D;
+        m->vc = vc_save + b0 * Hkv * m->ctx_max * D;
+        int rc = forward(m, nb, L, 0, nullptr, false);
+        m->kc = kc_save;
+        m->vc = vc_save;
+        if (rc) return rc;
+        LQ_CUDA(ctx, cudaMemcpyAsync(next + b0, m->tokens, (size_t)nb * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        if (logits)
+            LQ_CUDA(ctx, cudaMemcpyAsync(logits + b0 * m->c.vocab, m->logits, (size_t)(nb * m->c.vocab) * 4,
+                                         cudaMemcpyDeviceToHost, ctx->stream));
+    }
+    (void)H;
+    m->pos = L;
+    int32_t p = (int32_t)L;
+    LQ_CUDA(ctx, cudaMemcpyAsync(m->pos_dev, &p, 4, cudaMemcpyHostToDevice, ctx->stream));
+    LQ_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    return lq::consume_device_error(ctx, "lq_qwen3_prefill");
+}
+
+static int decode_prepare(lq_model* m, int64_t B) {
+    if (m->exec && m->graph_batch == B) return LQ_OK;
+    return build_graph(m, B);
+}
+
+int lq_qwen3_decode_step(lq_model* m, const int32_t* ids, int32_t* next, float* logits) {
+    if (!m) return LQ_ERR_INVALID_ARG;
+    lq_ctx* ctx = m->ctx;
+    LQ_ENTRY(ctx, "lq_qwen3_decode_step");
+    LQ_REQUIRE(ctx, ids && next, "lq_qwen3_decode_step: NULL argument");
+    const int64_t B = m->graph_batch ? m->graph_batch : m->max_batch;
+    LQ_REQUIRE(ctx, m->pos < m->ctx_max, "lq_qwen3_decode_step: context full (%lld)", (long long)m->ctx_max);
+    for (int64_t i = 0; i < B; i++)
+        LQ_REQUIRE(ctx, ids[i] >= 0 && ids[i] < m->c.vocab, "lq_qwen3_decode_step: token id %d out of range", ids[i]);
+    int rc = decode_prepare(m, B);
+    if (rc) return rc;
+    LQ_CUDA(ctx, cudaMemcpyAsync(m->tokens, ids, (size_t)B * 4, cudaMemcpyHostToDevice, ctx->stream));
+    LQ_CUDA(ctx, cudaGraphLaunch(m->exec, ctx->stream));
+    LQ_CUDA(ctx, cudaMemcpyAsync(next, m->tokens, (size_t)B * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    if (logits)
+        LQ_CUDA(ctx, cudaMemcpyAsync(logits, m->logits, (size_t)(B * m->c.vocab) * 4, cudaMemcpyDeviceToHost,
+                                     ctx->stream));
+    LQ_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    m->pos += 1;
+    return LQ_OK;
+}
+
+int lq_qwen3_decode_device(lq_model* m, int64_t n_steps) {
+    if (!m) return LQ_ERR_INVALID_ARG;
+    lq_ctx* ctx = m->ctx;
+    LQ_ENTRY(ctx, "lq_qwen3_decode_device");
+    const int64_t B = m->graph_batch ? m->graph_batch : m->max_batch;
+    LQ_REQUIRE(ctx, n_steps >= 0 && m->pos + n_steps <= m->ctx_max,
+               "lq_qwen3_decode_device: %lld steps from position %lld exceed ctx_max %lld", (long long)n_steps,
+               (long long)m->pos, (long long)m->ctx_max);
+    int rc = decode_prepare(m, B);
+    if (rc) return rc;
+    for (int64_t s = 0; s < n_steps; s++) LQ_CUDA(ctx, cudaGraphLaunch(m->exec, ctx->stream));
+    m->pos += n_steps;
+    return LQ_OK;
+}
+
+int lq_qwen3_set_batch(lq_model* m, int64_t B) {
+    if (!m) return LQ_ERR_INVALID_ARG;
+    LQ_ENTRY(m->ctx, "lq_qwen3_set_batch");
+    LQ_REQUIRE(m->ctx, B > 0 && B <= m->max_batch, "lq_qwen3_set_batch: B=%lld out of range", (long long)B);
+    return decode_prepare(m, B);
+}
+
+int lq_qwen3_token_buffer(lq_model* m, int32_t** tokens) {
+    if (!m || !tokens) return LQ_ERR_INVALID_ARG;
+    *tokens = m->tokens;
+    return LQ_OK;
+}
+
+int lq_qwen3_position(lq_model* m, int64_t* pos) {
+    if (!m || !pos) return LQ_ERR_INVALID_ARG;
+    *pos = m->pos;
+    return LQ_OK;
+}
+
+int lq_qwen3_linear(lq_model* m, int64_t layer, int kind, lq_q8_tensor* out) {
+    if (!m || !out) return LQ_ERR_INVALID_ARG;
+    lq_ctx* ctx = m->ctx;
+    if (layer < 0) {
+        LQ_REQUIRE(ctx, kind == 7, "lq_qwen3_linear: layer -1 needs kind 7 (lm_head)");
+        *out = m->lm_head;
+        return LQ_OK;
+    }
+    LQ_REQUIRE(ctx, layer < (int64_t)m->layers.size(), "lq_qwen3_linear: layer out of range");
+    const Layer& ly = m->layers[(size_t)layer];
+    const int64_t I = m->c.inter;
+    switch (kind) {
+        case K_Q: *out = rows_view(ly.qkv, 0, m->Nq); break;
+        case K_K: *out = rows_view(ly.qkv, m->Nq, m->Nk); break;
+        case K_V: *out = rows_view(ly.qkv, m->Nq + m->Nk, m->Nk); break;
+        case K_O: *out = ly.o; break;
+        case K_GATE: *out = rows_view(ly.gate_up, 0, I); break;
+        case K_UP: *out = rows_view(ly.gate_up, I, I); break;
+        case K_DOWN: *out = ly.down; break;
+        case 8: *out = ly.qkv; break;       // fused q/k/v as streamed by the decode step
+        case 9: *out = ly.gate_up; break;   // fused gate/up
+        default: return lq::set_error(ctx, LQ_ERR_INVALID_ARG, "lq_qwen3_linear: kind %d", kind);
+    }
+    return LQ_OK;
+}
+
+int lq_qwen3_graph_kernels(lq_model* m, int64_t* n) {
+    if (!m || !n) return LQ_ERR_INVALID_ARG;
+    *n = m->graph_kernels;
+    return LQ_OK;
+}
+
+int lq_qwen3_weight_bytes(lq_model* m, int64_t* bytes) {
+    if (!m || !bytes) return LQ_ERR_INVALID_ARG;
+    auto q8b = [](const lq_q8_tensor& t) { return t.n * t.k + t.n * (t.k / 32) * 2; };
+    int64_t s = q8b(m->lm_head);
+    for (auto& ly : m->layers) s += q8b(ly.qkv) + q8b(ly.o) + q8b(ly.gate_up) + q8b(ly.down);
+    *bytes = s;
+    return LQ_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,129 @@
+"""End-to-end parity of the Qwen3 runner against the CPU oracle, through the C ABI.
+
+Both sides build the model from the same seeded integer-exact generator, so the Q8_0
+weights must be bit-identical. Logits are compared with cosine >= 0.99999 and
+max |diff| <= 1e-3 * max |logit|; greedy tokens must be identical (teacher-forced per step,
+and free-running on the small configs, where each step's top-1/top-2 margin is checked to
+exceed the logit tolerance before requiring equality).
+"""
+import numpy as np
+import pytest
+
+from conftest import cos_sim
+from test_gpu_q8 import H
+
+pytestmark = pytest.mark.gpu
+
+TINY = dict(hidden=256, layers=2, n_heads=4, n_kv_heads=2, head_dim=128, inter=512, vocab=1000,
+            tied=1, norm_std=0.1)
+
+
+def _models(lq8, oracle, ctx, seed, cfgd, max_batch=1, ctx_max=64):
+    ocfg = oracle.make_config(**cfgd)
+    gcfg = lq8.make_config(**cfgd)
+    gm = lq8.Qwen3ForCausalLM(ctx, gcfg, seed, max_batch=max_batch, ctx_max=ctx_max)
+    return gm, ocfg
+
+
+def test_weights_bit_identical(ctx, lq8_lib, oracle):
+    gm, ocfg = _models(lq8_lib, oracle, ctx, 1234, TINY)
+    om = oracle.Qwen3Model(ocfg, 1234, ctx_max=64)
+    for layer in range(2):
+        for kind, kid in (("q", 0), ("k", 1), ("v", 2), ("o", 3), ("gate", 4), ("up", 5), ("down", 6)):
+            t = lq8_lib.QTensor.from_struct(gm.linear(layer, kind))
+            oq, od = om.linear(layer, kid)
+            assert np.array_equal(H(t.qs), oq), (layer, kind)
+            assert np.array_equal(H(t.d, np.uint16), od), (layer, kind)
+    t = lq8_lib.QTensor.from_struct(gm.linear(-1, "lm_head"))
+    oq, od = om.linear(-1, 7)
+    assert np.array_equal(H(t.qs), oq) and np.array_equal(H(t.d, np.uint16), od)
+
+
+def _check_logits(g, o):
+    assert cos_sim(g, o) >= 0.99999
+    assert np.max(np.abs(g - o)) <= 1e-3 * np.max(np.abs(o))
+
+
+def _margin(logits):
+    s = np.sort(logits)
+    return s[-1] - s[-2]
+
+
+@pytest.mark.parametrize("cfg_name,seed,L,steps", [("tiny", 1234, 12, 16), ("tiny_untied", 7, 5, 10)])
+def test_generate_matches_oracle(ctx, lq8_lib, oracle, cfg_name, seed, L, steps):
+    cfgd = dict(TINY)
+    if cfg_name == "tiny_untied":
+        cfgd.update(tied=0, norm_std=0.0, n_heads=8, n_kv_heads=1)
+    gm, ocfg = _models(lq8_lib, oracle, ctx, seed, cfgd)
+    om = oracle.Qwen3Model(ocfg, seed, ctx_max=64)
+    prompt = oracle.gen_tokens(seed, 0, L, ocfg.vocab)
+    # teacher-forced: feed the oracle's token at every step, compare logits and argmax
+    nxt, lg = gm.prefill(prompt, want_logits=True)
+    olg = om.forward(prompt, 0)
+    _check_logits(lg[0], olg)
+    assert nxt[0] == oracle.argmax(olg)
+    tok = oracle.argmax(olg)
+    for i in range(1, steps):
+        g_next, g_lg = gm.decode_step(np.array([tok], np.int32), want_logits=True)
+        olg = om.forward(np.array([tok]), L + i - 1)
+        _check_logits(g_lg[0], olg)
+        if _margin(olg) > 2e-3 * np.max(np.abs(olg)):
+            assert g_next[0] == oracle.argmax(olg)
+        tok = oracle.argmax(olg)
+    # free-running greedy generate
+    toks = gm.generate(prompt, steps)[0]
+    otoks, _ = om.generate(prompt, steps)
+    assert np.array_equal(toks, otoks)
+
+
+def test_batched_sequences_are_independent(ctx, lq8_lib, oracle):
+    B, L, steps = 3, 7, 6
+    gm, ocfg = _models(lq8_lib, oracle, ctx, 99, TINY, max_batch=B)
+    prompts = np.stack([oracle.gen_tokens(99, s, L, ocfg.vocab) for s in range(B)])
+    toks = gm.generate(prompts, steps)
+    for b in range(B):
+        om = oracle.Qwen3Model(ocfg, 99, ctx_max=64)
+        otoks, _ = om.generate(prompts[b], steps)
+        assert np.array_equal(toks[b], otoks), b
+
+
+def test_qwen3_0_6b_greedy_tokens(ctx, lq8_lib, oracle):
+    """Config 1: Qwen3-0.6B architecture, random-init N(0,0.02) weights, norms 1.0, tied
+    embeddings, batch 1, 16-token seeded prompt, 32 greedy tokens."""
+    cfgd = dict(lq8_lib.QWEN3_0_6B)
+    gm, ocfg = _models(lq8_lib, oracle, ctx, 1234, cfgd, ctx_max=64)
+    om = oracle.Qwen3Model(ocfg, 1234, ctx_max=64)
+    prompt = oracle.gen_tokens(1234, 0, 16, ocfg.vocab)
+    otoks, olg = om.generate(prompt, 32)
+    toks = gm.generate(prompt, 32)[0]
+    assert np.array_equal(toks, otoks)
+    # last logits agree too
+    _, lg = gm.decode_step(np.array([toks[-1]], np.int32), want_logits=True)
+    ref = om.forward(np.array([otoks[-1]]), 16 + 31)
+    _check_logits(lg[0], ref)
+
+
+def test_decode_past_context_is_an_error(ctx, lq8_lib, oracle):
+    gm, ocfg = _models(lq8_lib, oracle, ctx, 5, TINY, ctx_max=8)
+    prompt = oracle.gen_tokens(5, 0, 6, ocfg.vocab)
+    nxt = gm.prefill(prompt)
+    nxt = gm.decode_step(nxt)
+    nxt = gm.decode_step(nxt)
+    with pytest.raises(lq8_lib.LQ8Error):
+        gm.decode_step(nxt)
+    with pytest.raises(lq8_lib.LQ8Error):
+        gm.prefill(np.full(9, 1, np.int32))
+
+
+def test_device_decode_loop_matches_host_loop(ctx, lq8_lib, oracle):
+    gm, ocfg = _models(lq8_lib, oracle, ctx, 21, TINY, max_batch=2, ctx_max=64)
+    prompts = np.stack([oracle.gen_tokens(21, s, 5, ocfg.vocab) for s in range(2)])
+    host = gm.generate(prompts, 9)
+    gm.clear_kv_cache()
+    nxt = gm.prefill(prompts)
+    gm.decode_device(7)
+    buf = lq8_lib.wrap_device(gm.token_buffer_ptr(), (2,), "<i4")
+    ctx.synchronize()
+    assert H(buf).tolist() == host[:, 7].tolist()
+    assert gm.position() == 5 + 7
+    assert nxt.tolist() == host[:, 0].tolist()

@@ -1,0 +1,173 @@
+"""GPU parity of the Q8_0 kernels against the CPU oracle, through the C ABI.
+
+Quantization is bit-exact (int8 values and fp16 scales). The GEMM path (M > 4) keeps the
+oracle's per-output summation order and is bit-exact; the decode GEMV (M <= 4) reduces over
+K in parallel and is checked against the f32 reordering bound
+|y_gpu - y_oracle| <= 2 * (nb + 1) * 2^-24 * sum_b |term_b|.
+"""
+import ctypes as C
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def T(a):
+    import torch
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.uint16:
+        a = a.view(np.int16)
+    return torch.from_numpy(a).cuda()
+
+
+def H(t, dtype=None):
+    a = t.detach().cpu().numpy()
+    if dtype is not None:
+        a = a.view(dtype)
+    return a
+
+
+def gpu_quantize(ctx, lq8, x: np.ndarray):
+    import torch
+    xt = T(x)
+    rows, k = x.shape
+    qs = torch.empty((rows, k), dtype=torch.int8, device="cuda")
+    d = torch.empty((rows, k // 32), dtype=torch.int16, device="cuda")
+    dt = lq8.DTYPE_F32 if x.dtype == np.float32 else lq8.DTYPE_BF16
+    ctx.call("lq_q8_0_quantize", xt.data_ptr(), dt, rows, k, qs.data_ptr(), d.data_ptr())
+    ctx.synchronize()
+    return qs, d
+
+
+@pytest.mark.parametrize("shape", [(1, 32), (3, 96), (64, 1024), (257, 4096), (5, 25600)])
+@pytest.mark.parametrize("src", ["f32", "bf16"])
+def test_quantize_bit_exact(ctx, lq8_lib, oracle, rng, shape, src):
+    x = (rng.standard_normal(shape) * rng.choice([1e-3, 0.02, 1.0, 50.0])).astype(np.float32)
+    if src == "bf16":
+        x = oracle.f32_to_bf16(x)
+    qs, d = gpu_quantize(ctx, lq8_lib, x)
+    oq, od = oracle.q8_0_quantize(x)
+    assert np.array_equal(H(qs), oq)
+    assert np.array_equal(H(d, np.uint16), od)
+
+
+@pytest.mark.parametrize("name", ["w", "x", "xb", "edge"])
+def test_quantize_matches_gguf_fixture(ctx, lq8_lib, oracle, name):
+    fx = np.load(os.path.join(GOLDEN, "q8_0_gguf.npz"))
+    x = fx[f"{name}_in"]
+    qs, d = gpu_quantize(ctx, lq8_lib, x)
+    assert np.array_equal(oracle.q8_0_pack(H(qs), H(d, np.uint16)), fx[f"{name}_blocks"])
+
+
+def test_pack_unpack_blocks(ctx, lq8_lib, oracle, rng):
+    import torch
+    x = rng.standard_normal((9, 320)).astype(np.float32)
+    qs, d = gpu_quantize(ctx, lq8_lib, x)
+    blocks = torch.empty((9, 10 * 34), dtype=torch.uint8, device="cuda")
+    ctx.call("lq_q8_0_pack_blocks", qs.data_ptr(), d.data_ptr(), 9, 320, blocks.data_ptr())
+    q2 = torch.empty_like(qs)
+    d2 = torch.empty_like(d)
+    ctx.call("lq_q8_0_unpack_blocks", blocks.data_ptr(), 9, 320, q2.data_ptr(), d2.data_ptr())
+    ctx.synchronize()
+    assert np.array_equal(H(blocks), oracle.q8_0_pack(H(qs), H(d, np.uint16)))
+    assert torch.equal(q2, qs) and torch.equal(d2, d)
+
+
+def _weights(oracle, rng, n, k):
+    w = oracle.f32_to_bf16((rng.standard_normal((n, k)) * 0.02).astype(np.float32))
+    return oracle.q8_0_quantize(w)
+
+
+def _matmul(ctx, lq8, wq, wd, xq, xd, resid=None, ldy=None):
+    import torch
+    m, n = xq.shape[0], wq.shape[0]
+    ldy = ldy or n
+    y = torch.full((m, ldy), float("nan"), dtype=torch.float32, device="cuda")
+    r = T(resid) if resid is not None else None
+    if r is not None:
+        y.copy_(r)
+    wq_t, wd_t, xq_t, xd_t = T(wq), T(wd), T(xq), T(xd)
+    w = lq8.Q8Tensor(n, wq.shape[1], wq_t.data_ptr(), wd_t.data_ptr())
+    ctx.call("lq_q8_0_matmul", C.byref(w), xq_t.data_ptr(), xd_t.data_ptr(), m, y.data_ptr(),
+             y.data_ptr() if r is not None else None, ldy)
+    ctx.synchronize()
+    return H(y)
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 4])
+@pytest.mark.parametrize("n,k", [(1, 32), (17, 96), (300, 1024), (1024, 3072), (4096, 4096)])
+def test_gemv_within_reorder_bound(ctx, lq8_lib, oracle, rng, m, n, k):
+    wq, wd = _weights(oracle, rng, n, k)
+    xq, xd = oracle.q8_0_quantize(rng.standard_normal((m, k)).astype(np.float32))
+    y = _matmul(ctx, lq8_lib, wq, wd, xq, xd)
+    ref, absum = oracle.q8_0_matmul(xq, xd, wq, wd, with_abs=True)
+    nb = k // 32
+    bound = 2.0 * (nb + 1) * 2.0 ** -24 * absum + 1e-30
+    assert np.all(np.abs(y - ref) <= bound), float(np.max(np.abs(y - ref) / bound))
+
+
+@pytest.mark.parametrize("m", [5, 16, 17, 33, 64, 100, 257])
+@pytest.mark.parametrize("n,k", [(1, 32), (17, 96), (300, 1024), (640, 3072)])
+def test_gemm_bit_exact(ctx, lq8_lib, oracle, rng, m, n, k):
+    wq, wd = _weights(oracle, rng, n, k)
+    xq, xd = oracle.q8_0_quantize(rng.standard_normal((m, k)).astype(np.float32))
+    y = _matmul(ctx, lq8_lib, wq, wd, xq, xd)
+    assert np.array_equal(y, oracle.q8_0_matmul(xq, xd, wq, wd))
+
+
+@pytest.mark.parametrize("m", [1, 16])
+def test_matmul_residual_and_stride(ctx, lq8_lib, oracle, rng, m):
+    n, k, ldy = 200, 512, 256
+    wq, wd = _weights(oracle, rng, n, k)
+    xq, xd = oracle.q8_0_quantize(rng.standard_normal((m, k)).astype(np.float32))
+    resid = rng.standard_normal((m, ldy)).astype(np.float32)
+    y = _matmul(ctx, lq8_lib, wq, wd, xq, xd, resid=resid, ldy=ldy)
+    ref = oracle.q8_0_matmul(xq, xd, wq, wd)
+    np.testing.assert_allclose(y[:, :n], resid[:, :n] + ref, rtol=1e-5, atol=1e-5)
+    assert np.array_equal(y[:, n:], resid[:, n:])          # columns past n untouched
+    if m > 4:
+        assert np.array_equal(y[:, :n], (resid[:, :n] + ref).astype(np.float32))
+
+
+@pytest.mark.parametrize("m", [1, 3, 12])
+@pytest.mark.parametrize("src", ["f32", "bf16"])
+def test_linear_forward(ctx, lq8_lib, oracle, rng, m, src):
+    import torch
+    n, k = 384, 1024
+    wq, wd = _weights(oracle, rng, n, k)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    if src == "bf16":
+        x = oracle.f32_to_bf16(x)
+    lin = lq8_lib.Linear(ctx, lq8_lib.QTensor(T(wq), T(wd)))
+    xt = T(x) if src == "f32" else T(x).view(torch.bfloat16)
+    y = H(lin.forward(xt))
+    ctx.synchronize()
+    ref = oracle.q8_0_linear(x, wq, wd)
+    xq, xd = oracle.q8_0_quantize(x)
+    _, absum = oracle.q8_0_matmul(xq, xd, wq, wd, with_abs=True)
+    assert np.all(np.abs(y - ref) <= 2.0 * (k // 32 + 1) * 2.0 ** -24 * absum + 1e-30)
+
+
+def test_linear_shape_mismatch_is_an_error(ctx, lq8_lib, oracle, rng):
+    wq, wd = _weights(oracle, rng, 64, 256)
+    lin = lq8_lib.Linear(ctx, lq8_lib.QTensor(T(wq), T(wd)))
+    with pytest.raises(ValueError):
+        lin.forward(T(np.zeros((2, 128), np.float32)))
+    bad = lq8_lib.Q8Tensor(64, 100, T(wq).data_ptr(), T(wd).data_ptr())  # k not a multiple of 32
+    y = T(np.zeros((1, 64), np.float32))
+    with pytest.raises(lq8_lib.LQ8Error) as e:
+        ctx.call("lq_q8_0_linear", C.byref(bad), T(np.zeros((1, 100), np.float32)).data_ptr(),
+                 lq8_lib.DTYPE_F32, 1, y.data_ptr())
+    assert e.value.code == -1
+
+
+def test_fill_bf16_matches_oracle_generator(ctx, lq8_lib, oracle):
+    import torch
+    out = torch.empty(100003, dtype=torch.int16, device="cuda")
+    ctx.call("lq_fill_bf16", 1234, 0x305, 17, 100003, 0.02, out.data_ptr())
+    ctx.synchronize()
+    assert np.array_equal(H(out, np.uint16), oracle.gen_bf16(1234, 0x305, 100003, 0.02, offset=17))
