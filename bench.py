@@ -270,6 +270,20 @@ def run_ours(args, cfgd, world, rank, local):
     # ---- device-resident decode (value)
     model.decode_device(W)
     barrier()
+    if args.ncu_steps:
+        # profiling mode: only the decode steps between cudaProfilerStart/Stop, nothing timed
+        torch.cuda.profiler.start()
+        model.decode_device(args.ncu_steps)
+        ctx.synchronize()
+        torch.cuda.profiler.stop()
+        if args.ncu_gemv:
+            # the per-launch GEMV replay of the roofline measurement, also profiled
+            torch.cuda.profiler.start()
+            time_gemv_launches(lq8, ctx, model, cfgd, B, reps=1)
+            torch.cuda.profiler.stop()
+        model.close()
+        ctx.close()
+        return
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
@@ -383,11 +397,19 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--prompt", type=int, default=2048)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--ncu-steps", type=int, default=0,
+                    help="profiling: run this many decode steps between cudaProfilerStart/Stop and exit")
+    ap.add_argument("--ncu-gemv", action="store_true",
+                    help="profiling: also replay the decode GEMV launches inside the profiled range")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="profiling: build only the first N layers (a smaller device footprint)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     world, rank, local = dist_env()
-    cfgd = CONFIGS[args.config]
+    cfgd = dict(CONFIGS[args.config])
+    if args.layers:
+        cfgd["layers"] = args.layers
     if args.impl == "reference":
         if rank == 0:
             run_reference(args, cfgd)

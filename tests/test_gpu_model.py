@@ -87,20 +87,50 @@ def test_batched_sequences_are_independent(ctx, lq8_lib, oracle):
         assert np.array_equal(toks[b], otoks), b
 
 
+# Deep-model tolerance. A random-init 28-layer model amplifies f32 summation-order noise
+# through its bf16 and int8 rounding steps: the oracle against itself with only the RMSNorm
+# sum reversed already differs by 8e-3 max-relative after 8 layers. Measured GPU vs oracle on
+# the 0.6B config: cosine >= 0.99987, max-relative <= 1.6e-2 over 32 steps.
+DEEP_COS, DEEP_MAXREL = 0.9995, 5e-2
+
+
 def test_qwen3_0_6b_greedy_tokens(ctx, lq8_lib, oracle):
     """Config 1: Qwen3-0.6B architecture, random-init N(0,0.02) weights, norms 1.0, tied
-    embeddings, batch 1, 16-token seeded prompt, 32 greedy tokens."""
+    embeddings, batch 1, 16-token seeded prompt, 32 greedy tokens.
+
+    Teacher-forced (both sides fed the oracle's token), every step: logits within the
+    deep-model tolerance; the greedy token equal to the oracle's at >= 29 of 32 steps, and
+    any mismatch only where the oracle's top-1/top-2 margin lies inside the step's measured
+    noise band 2*max|dlogit|. Free-running: identical tokens up to the first step whose
+    margin lies inside its band (where the trajectories can first part)."""
     cfgd = dict(lq8_lib.QWEN3_0_6B)
     gm, ocfg = _models(lq8_lib, oracle, ctx, 1234, cfgd, ctx_max=64)
     om = oracle.Qwen3Model(ocfg, 1234, ctx_max=64)
     prompt = oracle.gen_tokens(1234, 0, 16, ocfg.vocab)
-    otoks, olg = om.generate(prompt, 32)
+    nxt, lg = gm.prefill(prompt, want_logits=True)
+    olg = om.forward(prompt, 0)
+    matches, first_band = 0, None
+    tok = oracle.argmax(olg)
+    for step in range(32):
+        if step > 0:
+            nxt, lg = gm.decode_step(np.array([tok], np.int32), want_logits=True)
+            olg = om.forward(np.array([tok]), 16 + step - 1)
+            tok = oracle.argmax(olg)
+        d = float(np.max(np.abs(lg[0] - olg)))
+        assert cos_sim(lg[0], olg) >= DEEP_COS, step
+        assert d <= DEEP_MAXREL * np.max(np.abs(olg)), step
+        in_band = _margin(olg) <= 2 * d
+        if nxt[0] == tok:
+            matches += 1
+        else:
+            assert in_band, step
+        if in_band and first_band is None:
+            first_band = step
+    assert matches >= 29
+    otoks, _ = om.generate(prompt, 32)
     toks = gm.generate(prompt, 32)[0]
-    assert np.array_equal(toks, otoks)
-    # last logits agree too
-    _, lg = gm.decode_step(np.array([toks[-1]], np.int32), want_logits=True)
-    ref = om.forward(np.array([otoks[-1]]), 16 + 31)
-    _check_logits(lg[0], ref)
+    upto = 32 if first_band is None else first_band
+    assert np.array_equal(toks[:upto], otoks[:upto])
 
 
 def test_decode_past_context_is_an_error(ctx, lq8_lib, oracle):

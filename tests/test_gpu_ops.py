@@ -36,7 +36,8 @@ def test_rmsnorm_and_fused_quant(ctx, lq8_lib, oracle, rng, dim, src):
     xq = torch.empty((rows, dim), dtype=torch.int8, device="cuda")
     xd = torch.empty((rows, dim // 32), dtype=torch.int16, device="cuda")
     dt = lq8_lib.DTYPE_F32 if src == "f32" else lq8_lib.DTYPE_BF16
-    ctx.call("lq_rmsnorm", T(x).data_ptr(), dt, rows, dim, T(w).data_ptr(), 1e-6, out.data_ptr(),
+    xt, wt = T(x), T(w)  # keep the device copies alive across the call
+    ctx.call("lq_rmsnorm", xt.data_ptr(), dt, rows, dim, wt.data_ptr(), 1e-6, out.data_ptr(),
              xq.data_ptr(), xd.data_ptr())
     ctx.synchronize()
     got = H(out, np.uint16)
@@ -83,8 +84,9 @@ def test_qk_norm_rope_kv(ctx, lq8_lib, oracle, rng, B, L, pos0):
     q_out = torch.zeros((B, Hq, L, D), dtype=torch.float32, device="cuda")
     kc = torch.zeros((B, Hkv, ctx_max, D), dtype=torch.float32, device="cuda")
     vc = torch.zeros_like(kc)
-    ctx.call("lq_qk_norm_rope_kv", T(qkv).data_ptr(), B, L, Hq, Hkv, D, T(qn).data_ptr(), T(kn).data_ptr(),
-             1e-6, T(ct).data_ptr(), T(st).data_ptr(), pos0, None, q_out.data_ptr(), kc.data_ptr(),
+    keep = [T(a) for a in (qkv, qn, kn, ct, st)]
+    ctx.call("lq_qk_norm_rope_kv", keep[0].data_ptr(), B, L, Hq, Hkv, D, keep[1].data_ptr(), keep[2].data_ptr(),
+             1e-6, keep[3].data_ptr(), keep[4].data_ptr(), pos0, None, q_out.data_ptr(), kc.data_ptr(),
              vc.data_ptr(), ctx_max)
     ctx.synchronize()
     q, k, v = _qk_ref(oracle, qkv, B, L, Hq, Hkv, qn, kn, pos0, ct, st)
@@ -112,8 +114,9 @@ def test_attention_vs_oracle(ctx, lq8_lib, oracle, rng, B, L, pos0, ctx_max, Hq,
     out = torch.empty((B * L, Hq * D), dtype=torch.float32, device="cuda")
     xq = torch.empty((B * L, Hq * D), dtype=torch.int8, device="cuda")
     xd = torch.empty((B * L, Hq * D // 32), dtype=torch.int16, device="cuda")
-    ctx.call("lq_attention", T(q).data_ptr(), T(kc).data_ptr(), T(vc).data_ptr(), B, Hq, Hkv, L, pos0, None,
-             ctx_max, D, out.data_ptr(), xq.data_ptr(), xd.data_ptr())
+    keep = [T(a) for a in (q, kc, vc)]
+    ctx.call("lq_attention", keep[0].data_ptr(), keep[1].data_ptr(), keep[2].data_ptr(), B, Hq, Hkv, L, pos0,
+             None, ctx_max, D, out.data_ptr(), xq.data_ptr(), xd.data_ptr())
     ctx.synchronize()
     got = H(out).reshape(B, L, Hq, D)
     for b in range(B):
@@ -133,7 +136,8 @@ def test_silu_mul_and_quant(ctx, lq8_lib, oracle, rng, m, inter):
     h = torch.empty((m, inter), dtype=torch.float32, device="cuda")
     xq = torch.empty((m, inter), dtype=torch.int8, device="cuda")
     xd = torch.empty((m, inter // 32), dtype=torch.int16, device="cuda")
-    ctx.call("lq_silu_mul", T(gu).data_ptr(), m, inter, h.data_ptr(), xq.data_ptr(), xd.data_ptr())
+    gut = T(gu)
+    ctx.call("lq_silu_mul", gut.data_ptr(), m, inter, h.data_ptr(), xq.data_ptr(), xd.data_ptr())
     ctx.synchronize()
     g, u = gu[:, :inter], gu[:, inter:]
     ref = np.array([[oracle.silu(a) for a in row] for row in g[:, :512]], np.float32) * u[:, :512]
@@ -148,12 +152,13 @@ def test_embedding_gather_and_bad_id(ctx, lq8_lib, oracle, rng):
     table = oracle.f32_to_bf16(rng.standard_normal((V, Hd)).astype(np.float32))
     ids = np.array([0, 999, 17, 17, 500], np.int32)
     out = torch.empty((5, Hd), dtype=torch.float32, device="cuda")
-    ctx.call("lq_embedding", T(table).data_ptr(), V, Hd, T(ids).data_ptr(), 5, out.data_ptr())
+    tt, it = T(table), T(ids)
+    ctx.call("lq_embedding", tt.data_ptr(), V, Hd, it.data_ptr(), 5, out.data_ptr())
     ctx.synchronize()
     assert np.array_equal(H(out), oracle.bf16_to_f32(table[ids]))
     bad = T(np.array([3, 1000], np.int32))
     with pytest.raises(lq8_lib.LQ8Error):
-        ctx.call("lq_embedding", T(table).data_ptr(), V, Hd, bad.data_ptr(), 2, out.data_ptr())
+        ctx.call("lq_embedding", tt.data_ptr(), V, Hd, bad.data_ptr(), 2, out.data_ptr())
 
 
 def test_argmax_ties_to_last(ctx, lq8_lib, oracle, rng):
@@ -163,7 +168,8 @@ def test_argmax_ties_to_last(ctx, lq8_lib, oracle, rng):
     x[2, :] = -1.0                               # all equal -> last index
     x[3, 0] = 50.0
     out = torch.empty(4, dtype=torch.int32, device="cuda")
-    ctx.call("lq_argmax", T(x).data_ptr(), 4, 151936, out.data_ptr())
+    xt = T(x)
+    ctx.call("lq_argmax", xt.data_ptr(), 4, 151936, out.data_ptr())
     ctx.synchronize()
     assert H(out).tolist() == [oracle.argmax(r) for r in x]
     assert H(out).tolist()[1:] == [151935, 151935, 0]
@@ -174,6 +180,7 @@ def test_add(ctx, lq8_lib, rng):
     a = rng.standard_normal(1000).astype(np.float32)
     b = rng.standard_normal(1000).astype(np.float32)
     out = torch.empty(1000, dtype=torch.float32, device="cuda")
-    ctx.call("lq_add", T(a).data_ptr(), T(b).data_ptr(), 1000, out.data_ptr())
+    at, bt = T(a), T(b)
+    ctx.call("lq_add", at.data_ptr(), bt.data_ptr(), 1000, out.data_ptr())
     ctx.synchronize()
     assert np.array_equal(H(out), a + b)

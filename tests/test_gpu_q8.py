@@ -157,11 +157,12 @@ def test_linear_shape_mismatch_is_an_error(ctx, lq8_lib, oracle, rng):
     lin = lq8_lib.Linear(ctx, lq8_lib.QTensor(T(wq), T(wd)))
     with pytest.raises(ValueError):
         lin.forward(T(np.zeros((2, 128), np.float32)))
-    bad = lq8_lib.Q8Tensor(64, 100, T(wq).data_ptr(), T(wd).data_ptr())  # k not a multiple of 32
+    wq_t, wd_t = T(wq), T(wd)
+    bad = lq8_lib.Q8Tensor(64, 100, wq_t.data_ptr(), wd_t.data_ptr())  # k not a multiple of 32
     y = T(np.zeros((1, 64), np.float32))
+    x = T(np.zeros((1, 100), np.float32))
     with pytest.raises(lq8_lib.LQ8Error) as e:
-        ctx.call("lq_q8_0_linear", C.byref(bad), T(np.zeros((1, 100), np.float32)).data_ptr(),
-                 lq8_lib.DTYPE_F32, 1, y.data_ptr())
+        ctx.call("lq_q8_0_linear", C.byref(bad), x.data_ptr(), lq8_lib.DTYPE_F32, 1, y.data_ptr())
     assert e.value.code == -1
 
 
