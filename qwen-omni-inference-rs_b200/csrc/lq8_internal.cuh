@@ -24,6 +24,9 @@ struct lq_ctx {
     void* scratch = nullptr;
     size_t scratch_bytes = 0;
     int* err_flag = nullptr;      // device int[4]: kernels report bad inputs here
+    // launch kernels with programmatic stream serialization (PDL): every kernel of the library
+    // calls pdl_wait() before it touches data written by earlier kernels
+    bool pdl = true;
 };
 
 namespace lq {
@@ -152,6 +155,26 @@ __device__ __forceinline__ float gen_value(uint64_t key, uint64_t idx, float sca
 
 inline int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
 
+// Launch on the context's stream; with ctx->pdl the launch may overlap the tail of the
+// preceding kernel (programmatic dependent launch), which the kernel orders with pdl_wait().
+template <typename... KArgs, typename... Args>
+inline int launch_kernel(lq_ctx* ctx, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                         const char* what, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = ctx->pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ((KArgs)args)...);
+    if (e != cudaSuccess) return check_cuda(ctx, e, what);
+    return LQ_OK;
+}
+
 }  // namespace lq
 
 // kernels launched across translation units
@@ -161,6 +184,9 @@ int launch_quantize_rows(lq_ctx* ctx, const void* src, lq_dtype dt, int64_t rows
 int launch_q8_matmul(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd,
                      int64_t m, float* y, const float* resid, int64_t ldy,
                      unsigned long long* argmax_keys);
+bool gemv_stream_supported(int64_t K);
+int launch_gemv_stream(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd, int64_t m,
+                       float* y, const float* resid, int64_t ldy, unsigned long long* keys);
 int launch_fill_bf16(lq_ctx* ctx, uint64_t seed, uint64_t tid, int64_t offset, int64_t count,
                      float scale, uint16_t* out);
 int launch_fill_norm(lq_ctx* ctx, uint64_t seed, uint64_t tid, int64_t count, float norm_std,
@@ -168,10 +194,13 @@ int launch_fill_norm(lq_ctx* ctx, uint64_t seed, uint64_t tid, int64_t count, fl
 int launch_argmax_finalize(lq_ctx* ctx, unsigned long long* keys, int64_t rows, int32_t* out,
                            int32_t* pos_counter);
 size_t attention_scratch_bytes(int64_t rows, int64_t n_heads, int64_t ctx_max, int64_t head_dim);
+int attention_max_ctx();
+// scratch starts with per-(row, kv head) counters that must be zero before the first launch;
+// every launch leaves them zero again (zero_counters re-clears them for shared scratch)
 int launch_attention(lq_ctx* ctx, const float* q, const float* kc, const float* vc, int64_t B,
                      int64_t Hq, int64_t Hkv, int64_t L, int64_t pos0, const int32_t* pos0_dev,
                      int64_t ctx_max, int64_t D, float* out, int8_t* xq, uint16_t* xd,
-                     void* scratch);
+                     void* scratch, bool zero_counters);
 int launch_rmsnorm(lq_ctx* ctx, const void* x, lq_dtype dt, int64_t rows, int64_t dim,
                    const uint16_t* w, float eps, uint16_t* out, int8_t* xq, uint16_t* xd);
 int launch_qk_norm_rope_kv(lq_ctx* ctx, const float* qkv, int64_t B, int64_t L, int64_t Hq,

@@ -1,5 +1,6 @@
 // lq8_ops.cu -- the small Qwen3 ops that keep activations in HBM, fused with the Q8_0
 // quantization of their output where the next op is a Q8_0 linear.
+#include "lq8_async.cuh"
 #include "lq8_internal.cuh"
 
 #include <cmath>
@@ -67,6 +68,8 @@ __global__ void __launch_bounds__(THREADS)
 rmsnorm_kernel(const T* __restrict__ x, int dim, const uint16_t* __restrict__ w, float eps,
                uint16_t* __restrict__ out, int8_t* __restrict__ xq, uint16_t* __restrict__ xd) {
     __shared__ float red[32];
+    pdl_wait();
+    pdl_trigger();
     const int row = blockIdx.x;
     const T* xr = x + (size_t)row * dim;
     float ss = 0.0f;
@@ -121,19 +124,19 @@ rmsnorm_kernel(const T* __restrict__ x, int dim, const uint16_t* __restrict__ w,
 int launch_rmsnorm(lq_ctx* ctx, const void* x, lq_dtype dt, int64_t rows, int64_t dim,
                    const uint16_t* w, float eps, uint16_t* out, int8_t* xq, uint16_t* xd) {
     if (rows == 0) return LQ_OK;
+    const dim3 grid((unsigned)rows);
     if (dim <= 1024) {
         if (dt == LQ_DTYPE_F32)
-            rmsnorm_kernel<float, 128><<<(unsigned)rows, 128, 0, ctx->stream>>>((const float*)x, (int)dim, w, eps, out, xq, xd);
-        else
-            rmsnorm_kernel<uint16_t, 128><<<(unsigned)rows, 128, 0, ctx->stream>>>((const uint16_t*)x, (int)dim, w, eps, out, xq, xd);
-    } else {
-        if (dt == LQ_DTYPE_F32)
-            rmsnorm_kernel<float, 256><<<(unsigned)rows, 256, 0, ctx->stream>>>((const float*)x, (int)dim, w, eps, out, xq, xd);
-        else
-            rmsnorm_kernel<uint16_t, 256><<<(unsigned)rows, 256, 0, ctx->stream>>>((const uint16_t*)x, (int)dim, w, eps, out, xq, xd);
+            return launch_kernel(ctx, rmsnorm_kernel<float, 128>, grid, dim3(128), 0, "rmsnorm", (const float*)x,
+                                 (int)dim, w, eps, out, xq, xd);
+        return launch_kernel(ctx, rmsnorm_kernel<uint16_t, 128>, grid, dim3(128), 0, "rmsnorm", (const uint16_t*)x,
+                             (int)dim, w, eps, out, xq, xd);
     }
-    LQ_LAUNCH_CHECK(ctx, "rmsnorm");
-    return LQ_OK;
+    if (dt == LQ_DTYPE_F32)
+        return launch_kernel(ctx, rmsnorm_kernel<float, 256>, grid, dim3(256), 0, "rmsnorm", (const float*)x,
+                             (int)dim, w, eps, out, xq, xd);
+    return launch_kernel(ctx, rmsnorm_kernel<uint16_t, 256>, grid, dim3(256), 0, "rmsnorm", (const uint16_t*)x,
+                         (int)dim, w, eps, out, xq, xd);
 }
 
 // =========================================================================================
@@ -149,6 +152,8 @@ qk_norm_rope_kv_kernel(const float* __restrict__ qkv, int B, int L, int Hq, int 
                        int pos0, const int32_t* __restrict__ pos0_dev, float* __restrict__ q_out,
                        float* __restrict__ kc, float* __restrict__ vc, int ctx_max, int* err) {
     constexpr int D = 128, RD = 64;
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int heads = Hq + 2 * Hkv;
@@ -205,186 +210,9 @@ int launch_qk_norm_rope_kv(lq_ctx* ctx, const float* qkv, int64_t B, int64_t L, 
     (void)D;
     int64_t items = B * L * (Hq + 2 * Hkv);
     if (items == 0) return LQ_OK;
-    int grid = ceil_div(items, 8);
-    qk_norm_rope_kv_kernel<<<grid, 256, 0, ctx->stream>>>(qkv, (int)B, (int)L, (int)Hq, (int)Hkv, qn, kn, eps,
-                                                          cos_t, sin_t, (int)pos0, pos0_dev, q_out, kc, vc,
-                                                          (int)ctx_max, ctx->err_flag);
-    LQ_LAUNCH_CHECK(ctx, "qk_norm_rope_kv");
-    return LQ_OK;
-}
-
-// =========================================================================================
-// attention (attention.rs:366-399): split over the key positions (flash-decoding). A CTA owns
-// one (query row, kv head, chunk of ATT_C positions) and all G = Hq/Hkv query heads of that
-// kv head (repeat_kv folded in). Partials (max, sum, unnormalised output) go to scratch; the
-// combine kernel merges the chunks and quantizes the [Hq*D] output row to Q8_0.
-// =========================================================================================
-constexpr int ATT_C = 128;  // positions per chunk (= threads per CTA)
-constexpr int ATT_D = 128;
-constexpr int ATT_GMAX = 8;
-
-__global__ void __launch_bounds__(ATT_C)
-attn_partial_kernel(const float* __restrict__ q, const float* __restrict__ kc,
-                    const float* __restrict__ vc, int Hq, int Hkv, int L, int pos0,
-                    const int32_t* __restrict__ pos0_dev, int ctx_max, float* __restrict__ part_o,
-                    float* __restrict__ part_ml, int nsplit) {
-    const int G = Hq / Hkv;
-    const int split = blockIdx.x, kvh = blockIdx.y;
-    const int64_t row = blockIdx.z;  // b*L + l
-    const int b = (int)(row / L), l = (int)(row % L);
-    const int p0 = pos0_dev ? *pos0_dev : pos0;
-    const int limit = p0 + l;  // last visible position (causal)
-    const int j0 = split * ATT_C;
-    const int tid = threadIdx.x;
-    __shared__ float qs[ATT_GMAX][ATT_D];
-    __shared__ float ps[ATT_GMAX][ATT_C];
-    __shared__ float mls[ATT_GMAX][2];
-    const int64_t part_base = ((row * Hq) + (int64_t)kvh * G) * nsplit + split;  // + g*nsplit
-    if (j0 > limit || limit >= ctx_max) {
-        if (tid < G) {
-            part_ml[(part_base + (int64_t)tid * nsplit) * 2] = -INFINITY;
-            part_ml[(part_base + (int64_t)tid * nsplit) * 2 + 1] = 0.0f;
-        }
-        return;
-    }
-    const int j1 = min(j0 + ATT_C, limit + 1);
-    for (int i = tid; i < G * ATT_D; i += ATT_C) {
-        int g = i / ATT_D, d = i % ATT_D;
-        qs[g][d] = q[(((int64_t)b * Hq + kvh * G + g) * L + l) * ATT_D + d];
-    }
-    __syncthreads();
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)ATT_D));
-    const float* kbase = kc + ((int64_t)b * Hkv + kvh) * (int64_t)ctx_max * ATT_D;
-    const float* vbase = vc + ((int64_t)b * Hkv + kvh) * (int64_t)ctx_max * ATT_D;
-    {
-        const int j = j0 + tid;
-        float s[ATT_GMAX];
-#pragma unroll
-        for (int g = 0; g < ATT_GMAX; g++) s[g] = 0.0f;
-        if (j < j1) {
-            const float4* kr = reinterpret_cast<const float4*>(kbase + (int64_t)j * ATT_D);
-#pragma unroll 4
-            for (int d4 = 0; d4 < ATT_D / 4; d4++) {
-                float4 kv = __ldg(kr + d4);
-#pragma unroll
-                for (int g = 0; g < ATT_GMAX; g++) {
-                    if (g < G) {
-                        s[g] = __fadd_rn(s[g], __fmul_rn(qs[g][4 * d4 + 0], kv.x));
-                        s[g] = __fadd_rn(s[g], __fmul_rn(qs[g][4 * d4 + 1], kv.y));
-                        s[g] = __fadd_rn(s[g], __fmul_rn(qs[g][4 * d4 + 2], kv.z));
-                        s[g] = __fadd_rn(s[g], __fmul_rn(qs[g][4 * d4 + 3], kv.w));
-                    }
-                }
-            }
-        }
-#pragma unroll
-        for (int g = 0; g < ATT_GMAX; g++)
-            if (g < G) ps[g][tid] = (j < j1) ? __fmul_rn(s[g], scale) : -INFINITY;
-    }
-    __syncthreads();
-    // per head: chunk max, exp, sum (4 warps share the G heads)
-    const int lane = tid & 31, warp = tid >> 5;
-    for (int g = warp; g < G; g += ATT_C / 32) {
-        float m = -INFINITY;
-        for (int i = lane; i < ATT_C; i += 32) m = fmaxf(m, ps[g][i]);
-        m = warp_max(m);
-        float sum = 0.0f;
-        for (int i = lane; i < ATT_C; i += 32) {
-            float e = expf(__fsub_rn(ps[g][i], m));  // exp(-inf) = 0 for masked slots
-            ps[g][i] = e;
-            sum = __fadd_rn(sum, e);
-        }
-        sum = warp_sum(sum);
-        if (lane == 0) { mls[g][0] = m; mls[g][1] = sum; }
-    }
-    __syncthreads();
-    // out[g][d] = sum_j p[g][j] * v[j][d]; thread = dim
-    {
-        const int d = tid;
-        float acc[ATT_GMAX];
-#pragma unroll
-        for (int g = 0; g < ATT_GMAX; g++) acc[g] = 0.0f;
-        for (int j = j0; j < j1; j++) {
-            float vv = __ldg(vbase + (int64_t)j * ATT_D + d);
-#pragma unroll
-            for (int g = 0; g < ATT_GMAX; g++)
-                if (g < G) acc[g] = __fadd_rn(acc[g], __fmul_rn(ps[g][j - j0], vv));
-        }
-#pragma unroll
-        for (int g = 0; g < ATT_GMAX; g++)
-            if (g < G) part_o[(part_base + (int64_t)g * nsplit) * ATT_D + d] = acc[g];
-        if (tid < G) {
-            part_ml[(part_base + (int64_t)tid * nsplit) * 2] = mls[tid][0];
-            part_ml[(part_base + (int64_t)tid * nsplit) * 2 + 1] = mls[tid][1];
-        }
-    }
-}
-
-// one warp per (row, q head); lane holds dims 4*lane..4*lane+3
-__global__ void __launch_bounds__(256)
-attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
-                    int64_t rows, int Hq, int nsplit, float* __restrict__ out,
-                    int8_t* __restrict__ xq, uint16_t* __restrict__ xd) {
-    const int lane = threadIdx.x & 31;
-    const int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (item >= rows * Hq) return;  // whole warp
-    const int64_t base = item * nsplit;
-    float M = -INFINITY;
-    for (int s = 0; s < nsplit; s++) M = fmaxf(M, part_ml[(base + s) * 2]);
-    float Lsum = 0.0f;
-    float o[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int s = 0; s < nsplit; s++) {
-        float ms = part_ml[(base + s) * 2];
-        if (ms == -INFINITY) continue;
-        float w = expf(__fsub_rn(ms, M));
-        Lsum = __fadd_rn(Lsum, __fmul_rn(w, part_ml[(base + s) * 2 + 1]));
-        float4 po = *reinterpret_cast<const float4*>(part_o + (base + s) * ATT_D + lane * 4);
-        o[0] = __fadd_rn(o[0], __fmul_rn(w, po.x));
-        o[1] = __fadd_rn(o[1], __fmul_rn(w, po.y));
-        o[2] = __fadd_rn(o[2], __fmul_rn(w, po.z));
-        o[3] = __fadd_rn(o[3], __fmul_rn(w, po.w));
-    }
-#pragma unroll
-    for (int i = 0; i < 4; i++) o[i] = __fdiv_rn(o[i], Lsum);
-    const int64_t e = item * ATT_D + lane * 4;  // element index in the [rows][Hq*D] output
-    if (out) *reinterpret_cast<float4*>(out + e) = make_float4(o[0], o[1], o[2], o[3]);
-    if (xq) {
-        uint32_t qv = quant_group8(o, lane & 7, xd + (e >> 5));
-        *reinterpret_cast<uint32_t*>(xq + e) = qv;
-    }
-}
-
-size_t attention_scratch_bytes(int64_t rows, int64_t Hq, int64_t ctx_max, int64_t D) {
-    int64_t nsplit = (ctx_max + ATT_C - 1) / ATT_C;
-    size_t o = (size_t)(rows * Hq * nsplit * D) * 4;
-    o = (o + 255) & ~(size_t)255;
-    return o + (size_t)(rows * Hq * nsplit * 2) * 4;
-}
-
-int launch_attention(lq_ctx* ctx, const float* q, const float* kc, const float* vc, int64_t B,
-                     int64_t Hq, int64_t Hkv, int64_t L, int64_t pos0, const int32_t* pos0_dev,
-                     int64_t ctx_max, int64_t D, float* out, int8_t* xq, uint16_t* xd,
-                     void* scratch) {
-    (void)D;
-    int64_t rows = B * L;
-    if (rows == 0) return LQ_OK;
-    // with a host-known position only the chunks up to pos0+L are launched; with a device
-    // position (CUDA-graph decode) the grid covers ctx_max and idle chunks exit at once
-    int64_t span = pos0_dev ? ctx_max : std::min<int64_t>(ctx_max, pos0 + L);
-    int nsplit = ceil_div(span, ATT_C);
-    size_t obytes = (size_t)(rows * Hq * nsplit * ATT_D) * 4;
-    obytes = (obytes + 255) & ~(size_t)255;
-    float* part_o = (float*)scratch;
-    float* part_ml = (float*)((uint8_t*)scratch + obytes);
-    dim3 grid(nsplit, (unsigned)Hkv, (unsigned)rows);
-    attn_partial_kernel<<<grid, ATT_C, 0, ctx->stream>>>(q, kc, vc, (int)Hq, (int)Hkv, (int)L, (int)pos0, pos0_dev,
-                                                         (int)ctx_max, part_o, part_ml, nsplit);
-    LQ_LAUNCH_CHECK(ctx, "attn_partial");
-    int64_t items = rows * Hq;
-    attn_combine_kernel<<<ceil_div(items, 8), 256, 0, ctx->stream>>>(part_o, part_ml, rows, (int)Hq, nsplit, out,
-                                                                     xq, xd);
-    LQ_LAUNCH_CHECK(ctx, "attn_combine");
-    return LQ_OK;
+    return launch_kernel(ctx, qk_norm_rope_kv_kernel, dim3(ceil_div(items, 8)), dim3(256), 0, "qk_norm_rope_kv",
+                         qkv, (int)B, (int)L, (int)Hq, (int)Hkv, qn, kn, eps, cos_t, sin_t, (int)pos0, pos0_dev,
+                         q_out, kc, vc, (int)ctx_max, ctx->err_flag);
 }
 
 // =========================================================================================
@@ -393,6 +221,8 @@ int launch_attention(lq_ctx* ctx, const float* q, const float* kc, const float* 
 __global__ void __launch_bounds__(256)
 silu_mul_kernel(const float* __restrict__ gu, int64_t m, int inter, float* __restrict__ h,
                 int8_t* __restrict__ xq, uint16_t* __restrict__ xd) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t nblk = m * (inter >> 5);
     const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t blk = gid >> 3;
@@ -423,9 +253,8 @@ int launch_silu_mul(lq_ctx* ctx, const float* gu, int64_t m, int64_t inter, floa
                     uint16_t* xd) {
     int64_t threads = m * (inter / 32) * 8;
     if (threads == 0) return LQ_OK;
-    silu_mul_kernel<<<ceil_div(threads, 256), 256, 0, ctx->stream>>>(gu, m, (int)inter, h, xq, xd);
-    LQ_LAUNCH_CHECK(ctx, "silu_mul");
-    return LQ_OK;
+    return launch_kernel(ctx, silu_mul_kernel, dim3(ceil_div(threads, 256)), dim3(256), 0, "silu_mul", gu, m,
+                         (int)inter, h, xq, xd);
 }
 
 // =========================================================================================
@@ -434,6 +263,8 @@ int launch_silu_mul(lq_ctx* ctx, const float* gu, int64_t m, int64_t inter, floa
 __global__ void embedding_kernel(const uint16_t* __restrict__ table, int64_t vocab, int hidden,
                                  const int32_t* __restrict__ ids, int64_t n, float* __restrict__ out,
                                  int* err) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t row = blockIdx.x;
     if (row >= n) return;
     const int32_t id = ids[row];
@@ -453,9 +284,8 @@ __global__ void embedding_kernel(const uint16_t* __restrict__ table, int64_t voc
 int launch_embedding(lq_ctx* ctx, const uint16_t* table, int64_t vocab, int64_t hidden,
                      const int32_t* ids, int64_t n, float* out) {
     if (n == 0) return LQ_OK;
-    embedding_kernel<<<(unsigned)n, 256, 0, ctx->stream>>>(table, vocab, (int)hidden, ids, n, out, ctx->err_flag);
-    LQ_LAUNCH_CHECK(ctx, "embedding");
-    return LQ_OK;
+    return launch_kernel(ctx, embedding_kernel, dim3((unsigned)n), dim3(256), 0, "embedding", table, vocab,
+                         (int)hidden, ids, n, out, ctx->err_flag);
 }
 
 // =========================================================================================
@@ -464,6 +294,8 @@ int launch_embedding(lq_ctx* ctx, const uint16_t* table, int64_t vocab, int64_t 
 __global__ void __launch_bounds__(1024)
 argmax_kernel(const float* __restrict__ x, int64_t n, int32_t* __restrict__ out) {
     __shared__ unsigned long long red[32];
+    pdl_wait();
+    pdl_trigger();
     const float* xr = x + (int64_t)blockIdx.x * n;
     unsigned long long best = 0ull;
     for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
@@ -490,6 +322,8 @@ argmax_kernel(const float* __restrict__ x, int64_t n, int32_t* __restrict__ out)
 
 __global__ void argmax_finalize_kernel(unsigned long long* keys, int64_t rows, int32_t* out,
                                        int32_t* pos_counter) {
+    pdl_wait();
+    pdl_trigger();
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < rows) {
         out[i] = (int32_t)(uint32_t)(keys[i] & 0xFFFFFFFFull);
@@ -500,10 +334,8 @@ __global__ void argmax_finalize_kernel(unsigned long long* keys, int64_t rows, i
 
 int launch_argmax_finalize(lq_ctx* ctx, unsigned long long* keys, int64_t rows, int32_t* out,
                            int32_t* pos_counter) {
-    argmax_finalize_kernel<<<ceil_div(std::max<int64_t>(rows, 1), 128), 128, 0, ctx->stream>>>(keys, rows, out,
-                                                                                               pos_counter);
-    LQ_LAUNCH_CHECK(ctx, "argmax_finalize");
-    return LQ_OK;
+    return launch_kernel(ctx, argmax_finalize_kernel, dim3(ceil_div(std::max<int64_t>(rows, 1), 128)), dim3(128),
+                         0, "argmax_finalize", keys, rows, out, pos_counter);
 }
 
 }  // namespace lq
@@ -565,24 +397,6 @@ int lq_qk_norm_rope_kv(lq_ctx* ctx, const float* qkv, int64_t B, int64_t L, int6
     LQ_REQUIRE(ctx, qkv && qn && kn && cos_t && sin_t && q_out && kc && vc, "lq_qk_norm_rope_kv: NULL pointer");
     return lq::launch_qk_norm_rope_kv(ctx, qkv, B, L, Hq, Hkv, D, qn, kn, eps, cos_t, sin_t, pos0, pos0_dev, q_out,
                                       kc, vc, ctx_max);
-}
-
-int lq_attention(lq_ctx* ctx, const float* q, const float* kc, const float* vc, int64_t B, int64_t Hq,
-                 int64_t Hkv, int64_t L, int64_t pos0, const int32_t* pos0_dev, int64_t ctx_max, int64_t D,
-                 float* out, int8_t* xq, uint16_t* xd) {
-    LQ_ENTRY(ctx, "lq_attention");
-    LQ_REQUIRE(ctx, D == 128, "lq_attention: head_dim %lld unsupported (Qwen3 uses 128)", (long long)D);
-    LQ_REQUIRE(ctx, Hq > 0 && Hkv > 0 && Hq % Hkv == 0 && Hq / Hkv <= 8,
-               "lq_attention: need Hq %% Hkv == 0 and Hq/Hkv <= 8");
-    LQ_REQUIRE(ctx, pos0_dev || (pos0 >= 0 && pos0 + L <= ctx_max), "lq_attention: positions exceed ctx_max");
-    LQ_REQUIRE(ctx, (xq == nullptr) == (xd == nullptr), "lq_attention: xq and xd go together");
-    if (B == 0 || L == 0) return LQ_OK;
-    LQ_REQUIRE(ctx, q && kc && vc && (out || xq), "lq_attention: NULL pointer");
-    size_t need = lq::attention_scratch_bytes(B * L, Hq, ctx_max, D);
-    int rc = lq::ensure_scratch(ctx, need);
-    if (rc) return rc;
-    return lq::launch_attention(ctx, q, kc, vc, B, Hq, Hkv, L, pos0, pos0_dev, ctx_max, D, out, xq, xd,
-                                ctx->scratch);
 }
 
 int lq_silu_mul(lq_ctx* ctx, const float* gu, int64_t m, int64_t inter, float* h, int8_t* xq, uint16_t* xd) {

@@ -4,6 +4,7 @@
 // row-major. Both the decode GEMV and the GEMM read this one layout; weights are written
 // once at load.
 #include "lq8_internal.cuh"
+#include "lq8_async.cuh"
 
 namespace lq {
 
@@ -213,41 +214,6 @@ constexpr int GEMM_BK = 64;            // bytes of K per stage
 constexpr int GEMM_LDS = GEMM_BK + 16; // padded smem row stride (conflict-free ldmatrix)
 constexpr int GEMM_STAGES = 4;
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
-    unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-    int n = pred ? 16 : 0;
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(n));
-}
-__device__ __forceinline__ void cp_async4(void* smem, const void* gmem, bool pred) {
-    unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-    int n = pred ? 4 : 0;
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(s), "l"(gmem), "r"(n));
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N)); }
-
-__device__ __forceinline__ void ldmatrix_x4(uint32_t r[4], const void* smem) {
-    unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(s));
-}
-__device__ __forceinline__ void ldmatrix_x2(uint32_t r[2], const void* smem) {
-    unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
-                 : "=r"(r[0]), "=r"(r[1])
-                 : "r"(s));
-}
-__device__ __forceinline__ void mma_s8(int c[4], const uint32_t a[4], const uint32_t b[2]) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%10,%11,%12,%13};"
-        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(0), "r"(0), "r"(0),
-          "r"(0));
-}
-
 template <int BW, int BX, int WW, int WX>
 struct GemmCfg {
     static constexpr int THREADS = WW * WX * 32;
@@ -270,6 +236,8 @@ q8_gemm_mma_kernel(const int8_t* __restrict__ wq, const uint16_t* __restrict__ w
                    const float* resid, float* y, int ldy, unsigned long long* argmax_keys) {
     using C = GemmCfg<BW, BX, WW, WX>;
     extern __shared__ __align__(128) uint8_t smem[];
+    pdl_wait();
+    pdl_trigger();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int ww = warp % WW, wx = warp / WW;
     const int n0 = blockIdx.x * BW;  // weight row base
@@ -460,10 +428,8 @@ static int run_gemm(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const 
         attr_done = true;
     }
     dim3 grid(ceil_div(w->n, BW), ceil_div(m, BX));
-    q8_gemm_mma_kernel<BW, BX, WW, WX><<<grid, C::THREADS, C::SMEM, ctx->stream>>>(
-        w->qs, w->d, (int)w->n, (int)w->k, xq, xd, (int)m, resid, y, (int)ldy, keys);
-    LQ_LAUNCH_CHECK(ctx, "q8_gemm_mma");
-    return LQ_OK;
+    return launch_kernel(ctx, q8_gemm_mma_kernel<BW, BX, WW, WX>, grid, dim3(C::THREADS), C::SMEM, "q8_gemm_mma",
+                         w->qs, w->d, (int)w->n, (int)w->k, xq, xd, (int)m, resid, y, (int)ldy, keys);
 }
 
 template <int M, int R>
@@ -492,6 +458,7 @@ int launch_q8_matmul(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const
                      int64_t m, float* y, const float* resid, int64_t ldy,
                      unsigned long long* keys) {
     if (m <= 0 || w->n <= 0) return LQ_OK;
+    if (m <= 4 && gemv_stream_supported(w->k)) return launch_gemv_stream(ctx, w, xq, xd, m, y, resid, ldy, keys);
     switch (m) {
         case 1: return gemv_rows<1>(ctx, w, xq, xd, y, resid, ldy, keys);
         case 2: return gemv_rows<2>(ctx, w, xq, xd, y, resid, ldy, keys);

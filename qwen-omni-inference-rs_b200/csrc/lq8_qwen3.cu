@@ -140,14 +140,14 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
         // attention -> Q8_0 rows [rows][Hq*D]
         if (L == 1) {
             RC(lq::launch_attention(ctx, m->q_rot, kc, vc, B, Hq, Hkv, 1, pos0, pos_dev, m->ctx_max, D, nullptr,
-                                    m->xq, m->xd, m->att_scratch));
+                                    m->xq, m->xd, m->att_scratch, false));
         } else {
             // one sequence at a time keeps the split-K partials within att_scratch
             for (int64_t b = 0; b < B; b++) {
                 RC(lq::launch_attention(ctx, m->q_rot + b * L * Hq * D, kc + b * Hkv * m->ctx_max * D,
                                         vc + b * Hkv * m->ctx_max * D, 1, Hq, Hkv, L, pos0, pos_dev, m->ctx_max,
                                         D, nullptr, m->xq + b * L * m->Hqd, m->xd + b * L * (m->Hqd / 32),
-                                        m->att_scratch));
+                                        m->att_scratch, false));
             }
         }
         // o_proj + residual (transformer.rs:194)
@@ -229,6 +229,8 @@ int lq_qwen3_create(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int6
                "lq_qwen3_create: need n_heads %% n_kv_heads == 0 and at most 8 q heads per kv head");
     LQ_REQUIRE(ctx, c.layers > 0 && c.vocab > 0 && max_batch > 0 && ctx_max > 0, "lq_qwen3_create: bad sizes");
     LQ_REQUIRE(ctx, c.max_pos <= 0 || ctx_max <= c.max_pos, "lq_qwen3_create: ctx_max exceeds max_pos");
+    LQ_REQUIRE(ctx, ctx_max <= lq::attention_max_ctx(), "lq_qwen3_create: ctx_max %lld exceeds %d",
+               (long long)ctx_max, lq::attention_max_ctx());
 
     lq_model* m = new lq_model();
     m->ctx = ctx;
@@ -311,6 +313,7 @@ int lq_qwen3_create(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int6
     int64_t att_rows = std::max<int64_t>(max_batch, std::min<int64_t>(R, ctx_max));
     m->att_scratch_bytes = lq::attention_scratch_bytes(att_rows, Hq, ctx_max, D);
     RC(dalloc(m, &m->att_scratch, m->att_scratch_bytes));
+    LQ_CUDA(ctx, cudaMemsetAsync(m->att_scratch, 0, m->att_scratch_bytes, ctx->stream));  // chunk counters
     LQ_CUDA(ctx, cudaMemsetAsync(m->keys, 0, (size_t)max_batch * 8, ctx->stream));
     LQ_CUDA(ctx, cudaMemsetAsync(m->pos_dev, 0, 4, ctx->stream));
     LQ_CUDA(ctx, cudaMemsetAsync(m->kc, 0, kv * 4, ctx->stream));

@@ -108,6 +108,8 @@ int lq_init(int device, lq_ctx** out) {
         return lq::set_error(nullptr, LQ_ERR_CUDA, "lq_init: stream/flag allocation failed");
     }
     c->stream = c->own_stream;
+    // LQ_NO_PDL=1 launches every kernel with plain stream ordering (no programmatic overlap)
+    c->pdl = getenv("LQ_NO_PDL") == nullptr;
     *out = c;
     return LQ_OK;
 }

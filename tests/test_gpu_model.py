@@ -133,6 +133,22 @@ def test_qwen3_0_6b_greedy_tokens(ctx, lq8_lib, oracle):
     assert np.array_equal(toks[:upto], otoks[:upto])
 
 
+def test_prefill_after_decode_is_reproducible(ctx, lq8_lib, oracle):
+    """Decode graphs and prefills share the attention scratch; a prefill after decode steps
+    must reproduce the first prefill bit for bit (regression: row-count-dependent scratch
+    layout let decode partials overwrite the prefill's chunk counters)."""
+    gm, ocfg = _models(lq8_lib, oracle, ctx, 3, TINY, max_batch=2, ctx_max=64)
+    prompts = np.stack([oracle.gen_tokens(3, s, 11, ocfg.vocab) for s in range(2)])
+    n0, l0 = gm.prefill(prompts, want_logits=True)
+    gm.set_batch(2)
+    t = n0
+    for _ in range(5):
+        t = gm.decode_step(t)
+    gm.clear_kv_cache()
+    n1, l1 = gm.prefill(prompts, want_logits=True)
+    assert np.array_equal(l0, l1) and np.array_equal(n0, n1)
+
+
 def test_decode_past_context_is_an_error(ctx, lq8_lib, oracle):
     gm, ocfg = _models(lq8_lib, oracle, ctx, 5, TINY, ctx_max=8)
     prompt = oracle.gen_tokens(5, 0, 6, ocfg.vocab)
