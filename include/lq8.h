@@ -113,6 +113,19 @@ int lq_q8_0_matmul(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq_dev,
  * quantized into the context's scratch, then multiplied; y [m][n] f32. */
 int lq_q8_0_linear(lq_ctx* ctx, const lq_q8_tensor* w, const void* x_dev, lq_dtype x_dtype,
                    int64_t m, float* y_dev);
+/* lq_q8_0_linear that allocates no device memory. It has no counterpart in the reference.
+ * lq_q8_0_linear grows its scratch with cudaMalloc/cudaFree, which some callers cannot allow
+ * (a latency-bound decode loop -- both calls can synchronise the whole device -- or a host
+ * whose device memory all belongs to its own pool allocator). This variant quantizes x into a
+ * fixed 4 MiB array inside the library's device image instead (present on every GPU that
+ * loads liblq8, until process exit), so m*k + 2*m*(k/32), rounded up to 256, must be at most
+ * 4 MiB; larger calls fail with LQ_ERR_INVALID_ARG. The first call on a device looks the
+ * array's address up (cudaGetSymbolAddress); make that first call before any stream capture.
+ * All calls on a device share the one array, so calls that overlap on the GPU (different
+ * streams or contexts of the same device) race; each call writes every scratch byte it
+ * reads, so nothing needs clearing between calls. Output equals lq_q8_0_linear's. */
+int lq_q8_0_linear_noalloc(lq_ctx* ctx, const lq_q8_tensor* w, const void* x_dev,
+                           lq_dtype x_dtype, int64_t m, float* y_dev);
 
 /* ---------------------------------------------------------------------------------------
  * Small ops that keep activations on the device.

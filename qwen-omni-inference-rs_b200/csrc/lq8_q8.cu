@@ -608,3 +608,74 @@ int lq_fill_bf16(lq_ctx* ctx, uint64_t seed, uint64_t tid, int64_t offset, int64
 }
 
 }  // extern "C"
+
+// =========================================================================================
+// lq_q8_0_linear_noalloc: lq_q8_0_linear for callers that must not allocate device memory.
+//
+// lq_q8_0_linear quantizes x into context scratch that it grows with cudaMalloc (and frees
+// the old buffer with cudaFree) when a call needs more. Some callers cannot allow that: a
+// decode loop with a latency budget (both calls may synchronise the whole device), or a host
+// that has handed all device memory to its own pool and forbids allocations behind its back.
+// This variant keeps the quantized activations in one fixed array in the library's device
+// image instead, so it allocates nothing. The array is 4 MiB on every GPU that loads the
+// library, held until the process exits; it bounds m*k: m*k + m*(k/32)*2 (rounded up to 256)
+// must fit, or the call fails with LQ_ERR_INVALID_ARG.
+// =========================================================================================
+#include <mutex>
+
+namespace {
+constexpr size_t kNoAllocScratchBytes = (size_t)4 << 20;
+// host code only ever uses the device address obtained from cudaGetSymbolAddress below; the
+// name itself is a host-side stand-in
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+constexpr int kMaxDevices = 128;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+// device address of the fixed scratch on ctx->device, looked up once per device with that
+// device current
+int noalloc_scratch(lq_ctx* ctx, void** out) {
+    if (ctx->device < 0 || ctx->device >= kMaxDevices)
+        return lq::set_error(ctx, LQ_ERR_UNSUPPORTED, "lq_q8_0_linear_noalloc: device %d", ctx->device);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[ctx->device]) {
+        int prev = 0;
+        LQ_CUDA(ctx, cudaGetDevice(&prev));
+        if (prev != ctx->device) LQ_CUDA(ctx, cudaSetDevice(ctx->device));
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (prev != ctx->device) cudaSetDevice(prev);
+        if (e != cudaSuccess) return lq::check_cuda(ctx, e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+        g_noalloc_addr[ctx->device] = p;
+    }
+    *out = g_noalloc_addr[ctx->device];
+    return LQ_OK;
+}
+}  // namespace
+
+extern "C" int lq_q8_0_linear_noalloc(lq_ctx* ctx, const lq_q8_tensor* w, const void* x, lq_dtype dt, int64_t m,
+                                      float* y) {
+    LQ_ENTRY(ctx, "lq_q8_0_linear_noalloc");
+    int rc = check_q8_tensor(ctx, w, "lq_q8_0_linear_noalloc");
+    if (rc) return rc;
+    LQ_REQUIRE(ctx, dt == LQ_DTYPE_F32 || dt == LQ_DTYPE_BF16,
+               "lq_q8_0_linear_noalloc: x dtype must be F32 or BF16");
+    LQ_REQUIRE(ctx, m >= 0 && m < (1 << 24), "lq_q8_0_linear_noalloc: m=%lld out of range", (long long)m);
+    if (m == 0) return LQ_OK;
+    LQ_REQUIRE(ctx, x && y, "lq_q8_0_linear_noalloc: NULL pointer");
+    const size_t off = ((size_t)(m * w->k) + 255) & ~(size_t)255;
+    const size_t need = off + (size_t)(m * (w->k / 32)) * 2;
+    LQ_REQUIRE(ctx, need <= kNoAllocScratchBytes,
+               "lq_q8_0_linear_noalloc: m=%lld x k=%lld needs %zu bytes of scratch; the fixed scratch holds "
+               "%zu (use lq_q8_0_linear, or split the rows)",
+               (long long)m, (long long)w->k, need, kNoAllocScratchBytes);
+    void* scratch = nullptr;
+    rc = noalloc_scratch(ctx, &scratch);
+    if (rc) return rc;
+    // every byte the matmul reads is written by the quantization first: nothing to clear
+    int8_t* xq = (int8_t*)scratch;
+    uint16_t* xd = (uint16_t*)((uint8_t*)scratch + off);
+    rc = lq::launch_quantize_rows(ctx, x, dt, m, w->k, xq, xd);
+    if (rc) return rc;
+    return lq::launch_q8_matmul(ctx, w, xq, xd, m, y, nullptr, w->n, nullptr);
+}
