@@ -270,6 +270,36 @@ def run_ours(args, cfgd, world, rank, local):
     # ---- device-resident decode (value)
     model.decode_device(W)
     barrier()
+    if args.trace:
+        # timeline mode: K decode steps under torch.profiler (CUPTI sees the graph's kernels
+        # with their real overlap); prints per-kernel time and the busy/idle split
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            model.decode_device(args.trace)
+            ctx.synchronize()
+        ks = sorted((e.time_range.start, e.time_range.end, e.name.split("(")[0])
+                    for e in prof.events() if e.device_type.name == "CUDA")
+        span = ks[-1][1] - ks[0][0]
+        busy, cs, ce = 0.0, ks[0][0], ks[0][1]
+        for s, e, _ in ks[1:]:
+            if s > ce:
+                busy, cs, ce = busy + ce - cs, s, e
+            else:
+                ce = max(ce, e)
+        busy += ce - cs
+        agg = {}
+        for s, e, n in ks:
+            a = agg.setdefault(n, [0, 0.0])
+            a[0] += 1
+            a[1] += e - s
+        print(json.dumps({"trace_steps": args.trace, "us_per_step": span / args.trace,
+                          "busy_us": busy, "idle_us": span - busy,
+                          "kernels": {n: {"launches": c, "us_per_launch": t / c}
+                                      for n, (c, t) in sorted(agg.items(), key=lambda x: -x[1][1])},
+                          "order": [[round(s - ks[0][0], 2), round(e - s, 2), n] for s, e, n in ks[:12]]}))
+        model.close()
+        ctx.close()
+        return
     if args.ncu_steps:
         # profiling mode: only the decode steps between cudaProfilerStart/Stop, nothing timed
         torch.cuda.profiler.start()
@@ -401,6 +431,8 @@ def main():
                     help="profiling: run this many decode steps between cudaProfilerStart/Stop and exit")
     ap.add_argument("--ncu-gemv", action="store_true",
                     help="profiling: also replay the decode GEMV launches inside the profiled range")
+    ap.add_argument("--trace", type=int, default=0,
+                    help="timeline: run this many decode steps under torch.profiler and print a summary")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling: build only the first N layers (a smaller device footprint)")
     args = ap.parse_args()

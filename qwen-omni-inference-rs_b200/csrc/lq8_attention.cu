@@ -3,12 +3,19 @@
 //
 // A CTA owns (one query row, one kv head, one chunk of ATT_C positions) and all G = Hq/Hkv
 // query heads that share the kv head. It stages the chunk's K and V rows into shared memory
-// with every 16-byte async copy in flight at once, computes the G score rows (each score is
-// the reference's sequential 128-term dot product, then the scale), a chunk softmax
-// (max, exp, sum) and the chunk's P.V. The last CTA of a (row, kv head) to finish -- found
-// with an atomic counter -- merges the chunks (rescaling by exp(m_s - M)) and writes the
-// [Hq*D] output row in f32 and/or Q8_0 for o_proj. One launch, no combine kernel.
+// with every 16-byte async copy in flight at once (rows of earlier positions before pdl_wait,
+// since earlier steps wrote them), computes the G score rows (each score is the reference's
+// sequential 128-term dot product, then the scale), a chunk softmax (max, exp, sum) and the
+// chunk's P.V. The last CTA of a (row, kv head) to finish -- found with an atomic counter --
+// merges the chunks (rescaling by exp(m_s - M)) and writes the [Hq*D] output row in f32
+// and/or Q8_0 for o_proj. One launch, no combine kernel.
+//
+// The decode variant (FUSED) also performs the step before it: from the fused q|k|v
+// projection row it computes the G query heads' RMSNorm + RoPE into shared memory, and the
+// CTA whose chunk holds the new position computes that position's k (RMSNorm + RoPE) and v,
+// uses them from shared memory and appends them to the caches.
 #include "lq8_async.cuh"
+#include "lq8_fused.cuh"
 #include "lq8_internal.cuh"
 
 namespace lq {
@@ -20,6 +27,11 @@ constexpr int ATT_G = 8;            // max query heads per kv head
 constexpr int ATT_THREADS = 128;
 constexpr int ATT_SLICE = 256;      // query rows per launch (bounds the partials)
 constexpr int ATT_MAX_SPLITS = 128; // chunks per row: contexts up to 8192 positions
+constexpr int ATT_MAX_KV = 64;
+// scratch: [counters: fixed ATT_SLICE*ATT_MAX_KV ints][part_ml][part_o]. The counter region
+// has the same place and size for every call, so launches with different row counts sharing
+// one scratch never overlap counters with another launch's partials.
+constexpr size_t ATT_COUNTER_BYTES = (size_t)ATT_SLICE * ATT_MAX_KV * 4;
 
 struct AttSmem {
     float ks[ATT_C][ATT_KS];
@@ -28,8 +40,29 @@ struct AttSmem {
     float ps[ATT_G][ATT_C];
     float ml[ATT_G][2];
     float cm[ATT_G][ATT_MAX_SPLITS];  // combine: per-chunk weights exp(m_s - M)
-    float cl[ATT_G];       // combine: total denominator
+    float cl[ATT_G];                  // combine: total denominator
     int last;
+};
+
+struct AttParams {
+    const float* q;        // [B][Hq][L][D] (unfused)
+    const float* qkv;      // [B][(Hq+2Hkv)*D] (fused decode)
+    const uint16_t* qn;
+    const uint16_t* kn;
+    float eps;
+    const float* cos_t;
+    const float* sin_t;
+    float* kc;             // [B][Hkv][ctx_max][D]
+    float* vc;
+    int Hq, Hkv, L, pos0;
+    const int32_t* pos0_dev;
+    int ctx_max, row0, nsplit;
+    float* part_o;
+    float* part_ml;
+    int* counters;
+    float* out;
+    int8_t* xq;
+    uint16_t* xd;
 };
 
 __device__ __forceinline__ void quant_warp32(float v, int lane, int8_t* q_out, uint16_t* d_out) {
@@ -40,19 +73,16 @@ __device__ __forceinline__ void quant_warp32(float v, int lane, int8_t* q_out, u
     if (lane == 0) *d_out = f2h(d);
 }
 
-__global__ void __launch_bounds__(ATT_THREADS)
-attn_chunk_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
-                  int Hq, int Hkv, int L, int pos0, const int32_t* __restrict__ pos0_dev, int ctx_max,
-                  int row0, int nsplit, float* __restrict__ part_o, float* __restrict__ part_ml,
-                  int* __restrict__ counters, float* __restrict__ out, int8_t* __restrict__ xq,
-                  uint16_t* __restrict__ xd) {
+template <bool FUSED>
+__global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const AttParams p) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     AttSmem& S = *reinterpret_cast<AttSmem*>(smem_raw);
+    const int Hq = p.Hq, Hkv = p.Hkv, L = p.L, ctx_max = p.ctx_max, nsplit = p.nsplit;
     const int G = Hq / Hkv;
     const int split = blockIdx.x, kvh = blockIdx.y, lrow = blockIdx.z;
-    const int row = row0 + lrow;  // b*L + l
+    const int row = p.row0 + lrow;  // b*L + l
     const int b = row / L, l = row - (row / L) * L;
-    const int p0 = pos0_dev ? *pos0_dev : pos0;
+    const int p0 = p.pos0_dev ? *p.pos0_dev : p.pos0;  // written by an earlier step: safe before pdl_wait
     const int limit = p0 + l;  // last visible position
     if (limit < 0 || limit >= ctx_max) return;
     const int n_active = min(limit / ATT_C + 1, nsplit);
@@ -60,14 +90,14 @@ attn_chunk_kernel(const float* __restrict__ q, const float* __restrict__ kc, con
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int j0 = split * ATT_C;
     const int cnt = min(ATT_C, limit + 1 - j0);
-    const float* kbase = kc + ((int64_t)b * Hkv + kvh) * (int64_t)ctx_max * ATT_D + (int64_t)j0 * ATT_D;
-    const float* vbase = vc + ((int64_t)b * Hkv + kvh) * (int64_t)ctx_max * ATT_D + (int64_t)j0 * ATT_D;
+    float* kbase = p.kc + ((int64_t)b * Hkv + kvh) * (int64_t)ctx_max * ATT_D + (int64_t)j0 * ATT_D;
+    float* vbase = p.vc + ((int64_t)b * Hkv + kvh) * (int64_t)ctx_max * ATT_D + (int64_t)j0 * ATT_D;
     // every 16-byte piece of the chunk's K and V rows in flight at once. Rows of positions
     // before p0 were appended by earlier steps and are read before pdl_wait(); the rows of
-    // this launch's positions are written by the preceding kernel and are read after it.
+    // this launch's positions are produced by the preceding kernel (or, fused, right here).
     const int fresh = p0 - j0;  // chunk rows r >= fresh belong to this launch
     for (int i = tid; i < cnt * (ATT_D / 4); i += ATT_THREADS) {
-        int r = i / (ATT_D / 4), c = (i % (ATT_D / 4)) * 4;
+        const int r = i / (ATT_D / 4), c = (i % (ATT_D / 4)) * 4;
         if (r < fresh) {
             cp_async16(&S.ks[r][c], kbase + (int64_t)r * ATT_D + c, true);
             cp_async16(&S.vs[r][c], vbase + (int64_t)r * ATT_D + c, true);
@@ -75,37 +105,62 @@ attn_chunk_kernel(const float* __restrict__ q, const float* __restrict__ kc, con
     }
     pdl_wait();
     pdl_trigger();
-    for (int i = tid; i < cnt * (ATT_D / 4); i += ATT_THREADS) {
-        int r = i / (ATT_D / 4), c = (i % (ATT_D / 4)) * 4;
-        if (r >= fresh) {
-            cp_async16(&S.ks[r][c], kbase + (int64_t)r * ATT_D + c, true);
-            cp_async16(&S.vs[r][c], vbase + (int64_t)r * ATT_D + c, true);
+    if constexpr (FUSED) {
+        // q heads: per-head RMSNorm + RoPE at position p0 (decode: L == 1)
+        const int heads = Hq + 2 * Hkv;
+        const float* qrow = p.qkv + (int64_t)b * heads * ATT_D;
+        const float* cs = p.cos_t + (int64_t)p0 * (ATT_D / 2);
+        const float* sn = p.sin_t + (int64_t)p0 * (ATT_D / 2);
+        for (int g = warp; g < G; g += ATT_THREADS / 32)
+            head_norm_rope(qrow + (int64_t)(kvh * G + g) * ATT_D, p.qn, p.eps, cs, sn, lane, S.qs[g]);
+        if (fresh >= 0 && fresh < cnt) {
+            // this chunk holds the new position: compute its k and v, use and append them
+            if (warp == 0) {
+                head_norm_rope(qrow + (int64_t)(Hq + kvh) * ATT_D, p.kn, p.eps, cs, sn, lane, S.ks[fresh]);
+                __syncwarp();
+                const float4 kk = *reinterpret_cast<const float4*>(&S.ks[fresh][lane * 4]);
+                *reinterpret_cast<float4*>(kbase + (int64_t)fresh * ATT_D + lane * 4) = kk;
+            } else if (warp == 1) {
+                const float4 vv =
+                    *reinterpret_cast<const float4*>(qrow + (int64_t)(Hq + Hkv + kvh) * ATT_D + lane * 4);
+                *reinterpret_cast<float4*>(&S.vs[fresh][lane * 4]) = vv;
+                *reinterpret_cast<float4*>(vbase + (int64_t)fresh * ATT_D + lane * 4) = vv;
+            }
         }
-    }
-    cp_async_commit();
-    for (int i = tid; i < G * ATT_D; i += ATT_THREADS) {
-        int g = i / ATT_D, d = i % ATT_D;
-        S.qs[g][d] = q[(((int64_t)b * Hq + kvh * G + g) * L + l) * ATT_D + d];
+        cp_async_commit();
+    } else {
+        for (int i = tid; i < cnt * (ATT_D / 4); i += ATT_THREADS) {
+            const int r = i / (ATT_D / 4), c = (i % (ATT_D / 4)) * 4;
+            if (r >= fresh) {
+                cp_async16(&S.ks[r][c], kbase + (int64_t)r * ATT_D + c, true);
+                cp_async16(&S.vs[r][c], vbase + (int64_t)r * ATT_D + c, true);
+            }
+        }
+        cp_async_commit();
+        for (int i = tid; i < G * ATT_D; i += ATT_THREADS) {
+            const int g = i / ATT_D, d = i % ATT_D;
+            S.qs[g][d] = p.q[(((int64_t)b * Hq + kvh * G + g) * L + l) * ATT_D + d];
+        }
     }
     cp_async_wait<0>();
     __syncthreads();
 
-    // scores: thread -> (position p, heads half, half+2, ...); sequential 128-term dot
+    // scores: thread -> (position pp, heads half, half+2, ...); sequential 128-term dot
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)ATT_D));
     {
-        const int p = tid % ATT_C, half = tid / ATT_C;
+        const int pp = tid % ATT_C, half = tid / ATT_C;
         float s[ATT_G / 2];
 #pragma unroll
         for (int i = 0; i < ATT_G / 2; i++) s[i] = 0.0f;
-        if (p < cnt) {
+        if (pp < cnt) {
 #pragma unroll 8
             for (int d4 = 0; d4 < ATT_D / 4; d4++) {
-                float4 k4 = *reinterpret_cast<const float4*>(&S.ks[p][4 * d4]);
+                const float4 k4 = *reinterpret_cast<const float4*>(&S.ks[pp][4 * d4]);
 #pragma unroll
                 for (int i = 0; i < ATT_G / 2; i++) {
-                    int g = half + 2 * i;
+                    const int g = half + 2 * i;
                     if (g < G) {
-                        float4 q4 = *reinterpret_cast<const float4*>(&S.qs[g][4 * d4]);
+                        const float4 q4 = *reinterpret_cast<const float4*>(&S.qs[g][4 * d4]);
                         s[i] = __fadd_rn(s[i], __fmul_rn(q4.x, k4.x));
                         s[i] = __fadd_rn(s[i], __fmul_rn(q4.y, k4.y));
                         s[i] = __fadd_rn(s[i], __fmul_rn(q4.z, k4.z));
@@ -116,19 +171,19 @@ attn_chunk_kernel(const float* __restrict__ q, const float* __restrict__ kc, con
         }
 #pragma unroll
         for (int i = 0; i < ATT_G / 2; i++) {
-            int g = half + 2 * i;
-            if (g < G) S.ps[g][p] = p < cnt ? __fmul_rn(s[i], scale) : -INFINITY;
+            const int g = half + 2 * i;
+            if (g < G) S.ps[g][pp] = pp < cnt ? __fmul_rn(s[i], scale) : -INFINITY;
         }
     }
     __syncthreads();
     // chunk softmax per head: max, exp(s - max), sum
     for (int g = warp; g < G; g += ATT_THREADS / 32) {
-        float a = S.ps[g][lane], c = S.ps[g][lane + 32];
-        float m = warp_max(fmaxf(a, c));
-        float ea = expf(__fsub_rn(a, m)), ec = expf(__fsub_rn(c, m));
+        const float a = S.ps[g][lane], c = S.ps[g][lane + 32];
+        const float m = warp_max(fmaxf(a, c));
+        const float ea = expf(__fsub_rn(a, m)), ec = expf(__fsub_rn(c, m));
         S.ps[g][lane] = ea;
         S.ps[g][lane + 32] = ec;
-        float sum = warp_sum(__fadd_rn(ea, ec));
+        const float sum = warp_sum(__fadd_rn(ea, ec));
         if (lane == 0) { S.ml[g][0] = m; S.ml[g][1] = sum; }
     }
     __syncthreads();
@@ -139,7 +194,7 @@ attn_chunk_kernel(const float* __restrict__ q, const float* __restrict__ kc, con
 #pragma unroll
         for (int g = 0; g < ATT_G; g++) acc[g] = 0.0f;
         for (int j = 0; j < cnt; j++) {
-            float vv = S.vs[j][d];
+            const float vv = S.vs[j][d];
 #pragma unroll
             for (int g = 0; g < ATT_G; g++)
                 if (g < G) acc[g] = __fadd_rn(acc[g], __fmul_rn(S.ps[g][j], vv));
@@ -147,32 +202,52 @@ attn_chunk_kernel(const float* __restrict__ q, const float* __restrict__ kc, con
         const int64_t hbase = ((int64_t)lrow * Hq + (int64_t)kvh * G) * nsplit + split;
 #pragma unroll
         for (int g = 0; g < ATT_G; g++)
-            if (g < G) part_o[(hbase + (int64_t)g * nsplit) * ATT_D + d] = acc[g];
+            if (g < G) p.part_o[(hbase + (int64_t)g * nsplit) * ATT_D + d] = acc[g];
         if (tid < G) {
-            part_ml[(hbase + (int64_t)tid * nsplit) * 2] = S.ml[tid][0];
-            part_ml[(hbase + (int64_t)tid * nsplit) * 2 + 1] = S.ml[tid][1];
+            p.part_ml[(hbase + (int64_t)tid * nsplit) * 2] = S.ml[tid][0];
+            p.part_ml[(hbase + (int64_t)tid * nsplit) * 2 + 1] = S.ml[tid][1];
         }
     }
     // the last chunk CTA of this (row, kv head) merges the chunks
     __threadfence();
     __syncthreads();
     if (tid == 0) {
-        int prev = atomicAdd(&counters[lrow * Hkv + kvh], 1);
+        const int prev = atomicAdd(&p.counters[lrow * Hkv + kvh], 1);
         S.last = (prev == n_active - 1);
     }
     __syncthreads();
     if (!S.last) return;
     __threadfence();
     const int64_t hbase0 = ((int64_t)lrow * Hq + (int64_t)kvh * G) * nsplit;
+    // bring each head's chunk partials into shared memory (the free K/V staging area, two head
+    // buffers) with all 16-byte copies of a head in flight at once, the next head's copies
+    // overlapping the current head's sum: one L2 round trip per head instead of a chain of
+    // dependent loads
+    float* po = &S.ks[0][0];
+    const size_t head_floats = (size_t)n_active * ATT_D;
+    const bool staged = 2 * head_floats * 4 <= sizeof(S.ks) + sizeof(S.vs);
+    auto stage_head = [&](int g) {
+        float* dst = po + (size_t)(g & 1) * head_floats;
+        for (int i = tid; i < n_active * (ATT_D / 4); i += ATT_THREADS) {
+            const int s = i / (ATT_D / 4), c = (i % (ATT_D / 4)) * 4;
+            cp_async16(dst + (size_t)s * ATT_D + c, p.part_o + (hbase0 + (int64_t)g * nsplit + s) * ATT_D + c, true);
+        }
+        cp_async_commit();
+    };
+    if (staged) {
+        stage_head(0);
+        if (G > 1) stage_head(1);
+    }
     for (int g = warp; g < G; g += ATT_THREADS / 32) {
         float m = -INFINITY;
-        for (int s = lane; s < n_active; s += 32) m = fmaxf(m, ld_cg(&part_ml[(hbase0 + (int64_t)g * nsplit + s) * 2]));
+        for (int s = lane; s < n_active; s += 32)
+            m = fmaxf(m, ld_cg(&p.part_ml[(hbase0 + (int64_t)g * nsplit + s) * 2]));
         m = warp_max(m);
         float lsum = 0.0f;
         for (int s = lane; s < n_active; s += 32) {
-            float w = expf(__fsub_rn(ld_cg(&part_ml[(hbase0 + (int64_t)g * nsplit + s) * 2]), m));
+            const float w = expf(__fsub_rn(ld_cg(&p.part_ml[(hbase0 + (int64_t)g * nsplit + s) * 2]), m));
             S.cm[g][s] = w;
-            lsum = __fadd_rn(lsum, __fmul_rn(w, ld_cg(&part_ml[(hbase0 + (int64_t)g * nsplit + s) * 2 + 1])));
+            lsum = __fadd_rn(lsum, __fmul_rn(w, ld_cg(&p.part_ml[(hbase0 + (int64_t)g * nsplit + s) * 2 + 1])));
         }
         lsum = warp_sum(lsum);
         if (lane == 0) S.cl[g] = lsum;
@@ -181,37 +256,62 @@ attn_chunk_kernel(const float* __restrict__ q, const float* __restrict__ kc, con
     const int d = tid;
     for (int g = 0; g < G; g++) {
         float o = 0.0f;
+        if (staged) {
+            if (g + 1 < G) cp_async_wait<1>();
+            else cp_async_wait<0>();
+            __syncthreads();
+            const float* pg = po + (size_t)(g & 1) * head_floats + d;
+            for (int s = 0; s < n_active; s++) o = __fadd_rn(o, __fmul_rn(S.cm[g][s], pg[(size_t)s * ATT_D]));
+            __syncthreads();  // this buffer is refilled next
+            if (g + 2 < G) stage_head(g + 2);
+        } else {
 #pragma unroll 8
-        for (int s = 0; s < n_active; s++)
-            o = __fadd_rn(o, __fmul_rn(S.cm[g][s], ld_cg(&part_o[(hbase0 + (int64_t)g * nsplit + s) * ATT_D + d])));
+            for (int s = 0; s < n_active; s++)
+                o = __fadd_rn(o, __fmul_rn(S.cm[g][s],
+                                           ld_cg(&p.part_o[(hbase0 + (int64_t)g * nsplit + s) * ATT_D + d])));
+        }
         o = __fdiv_rn(o, S.cl[g]);
         const int64_t e = (int64_t)row * Hq * ATT_D + (int64_t)(kvh * G + g) * ATT_D + d;
-        if (out) out[e] = o;
-        if (xq) quant_warp32(o, lane, xq + (e - lane), xd + (e >> 5));
+        if (p.out) p.out[e] = o;
+        if (p.xq) quant_warp32(o, lane, p.xq + (e - lane), p.xd + (e >> 5));
     }
-    if (tid == 0) counters[lrow * Hkv + kvh] = 0;  // ready for the next launch
+    if (tid == 0) p.counters[lrow * Hkv + kvh] = 0;  // ready for the next launch
 }
 
 int attention_max_ctx() { return ATT_C * ATT_MAX_SPLITS; }
 
-static int attn_nsplit(int64_t ctx_max, int64_t pos0, int64_t L, bool dev_pos) {
-    int64_t span = dev_pos ? ctx_max : std::min<int64_t>(ctx_max, pos0 + L);
-    return ceil_div(span, ATT_C);
-}
-
-// scratch: [counters: fixed ATT_SLICE*ATT_MAX_KV ints][part_ml slice*Hq*nsplit*2]
-// [part_o slice*Hq*nsplit*D]. The counter region has the same place and size for every call,
-// so launches with different row counts sharing one scratch never overlap counters with
-// another launch's partials.
-constexpr int ATT_MAX_KV = 64;
-constexpr size_t ATT_COUNTER_BYTES = (size_t)ATT_SLICE * ATT_MAX_KV * 4;
-
 size_t attention_scratch_bytes(int64_t rows, int64_t Hq, int64_t ctx_max, int64_t D) {
     (void)D;
-    int64_t slice = std::min<int64_t>(rows, ATT_SLICE);
-    int64_t nsplit = (ctx_max + ATT_C - 1) / ATT_C;
-    size_t ml = ((size_t)(slice * Hq * nsplit * 2) * 4 + 255) & ~(size_t)255;
+    const int64_t slice = std::min<int64_t>(rows, ATT_SLICE);
+    const int64_t nsplit = (ctx_max + ATT_C - 1) / ATT_C;
+    const size_t ml = ((size_t)(slice * Hq * nsplit * 2) * 4 + 255) & ~(size_t)255;
     return ATT_COUNTER_BYTES + ml + (size_t)(slice * Hq * nsplit * ATT_D) * 4;
+}
+
+template <bool FUSED>
+static int launch_chunks(lq_ctx* ctx, AttParams p, int64_t rows, void* scratch, bool zero_counters) {
+    const int64_t slice = std::min<int64_t>(rows, ATT_SLICE);
+    p.counters = (int*)scratch;
+    p.part_ml = (float*)((uint8_t*)scratch + ATT_COUNTER_BYTES);
+    const size_t ml = ((size_t)(slice * p.Hq * p.nsplit * 2) * 4 + 255) & ~(size_t)255;
+    p.part_o = (float*)((uint8_t*)scratch + ATT_COUNTER_BYTES + ml);
+    static bool attr = false;
+    if (!attr) {
+        LQ_CUDA(ctx, cudaFuncSetAttribute(attn_chunk_kernel<FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)sizeof(AttSmem)));
+        attr = true;
+    }
+    if (zero_counters)
+        LQ_CUDA(ctx, cudaMemsetAsync(p.counters, 0, (size_t)(slice * p.Hkv) * 4, ctx->stream));
+    for (int64_t r0 = 0; r0 < rows; r0 += slice) {
+        const int64_t n = std::min(slice, rows - r0);
+        p.row0 = (int)r0;
+        const dim3 grid(p.nsplit, (unsigned)p.Hkv, (unsigned)n);
+        const int rc = launch_kernel(ctx, attn_chunk_kernel<FUSED>, grid, dim3(ATT_THREADS), sizeof(AttSmem),
+                                     "attn_chunk", p);
+        if (rc) return rc;
+    }
+    return LQ_OK;
 }
 
 int launch_attention(lq_ctx* ctx, const float* q, const float* kc, const float* vc, int64_t B,
@@ -221,28 +321,49 @@ int launch_attention(lq_ctx* ctx, const float* q, const float* kc, const float* 
     (void)D;
     const int64_t rows = B * L;
     if (rows == 0) return LQ_OK;
-    const int nsplit = attn_nsplit(ctx_max, pos0, L, pos0_dev != nullptr);
-    const int64_t slice = std::min<int64_t>(rows, ATT_SLICE);
-    int* counters = (int*)scratch;
-    float* part_ml = (float*)((uint8_t*)scratch + ATT_COUNTER_BYTES);
-    size_t ml = ((size_t)(slice * Hq * nsplit * 2) * 4 + 255) & ~(size_t)255;
-    float* part_o = (float*)((uint8_t*)scratch + ATT_COUNTER_BYTES + ml);
-    static bool attr = false;
-    if (!attr) {
-        LQ_CUDA(ctx, cudaFuncSetAttribute(attn_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)sizeof(AttSmem)));
-        attr = true;
-    }
-    if (zero_counters) LQ_CUDA(ctx, cudaMemsetAsync(counters, 0, (size_t)(slice * Hkv) * 4, ctx->stream));
-    for (int64_t r0 = 0; r0 < rows; r0 += slice) {
-        int64_t n = std::min(slice, rows - r0);
-        dim3 grid(nsplit, (unsigned)Hkv, (unsigned)n);
-        int rc = launch_kernel(ctx, attn_chunk_kernel, grid, dim3(ATT_THREADS), sizeof(AttSmem), "attn_chunk", q,
-                               kc, vc, (int)Hq, (int)Hkv, (int)L, (int)pos0, pos0_dev, (int)ctx_max, (int)r0,
-                               nsplit, part_o, part_ml, counters, out, xq, xd);
-        if (rc) return rc;
-    }
-    return LQ_OK;
+    AttParams p = {};
+    p.q = q;
+    p.kc = const_cast<float*>(kc);
+    p.vc = const_cast<float*>(vc);
+    p.Hq = (int)Hq;
+    p.Hkv = (int)Hkv;
+    p.L = (int)L;
+    p.pos0 = (int)pos0;
+    p.pos0_dev = pos0_dev;
+    p.ctx_max = (int)ctx_max;
+    // with a host-known position only the chunks up to pos0+L are launched; with a device
+    // position (CUDA-graph decode) the grid covers ctx_max and idle chunks exit at once
+    const int64_t span = pos0_dev ? ctx_max : std::min<int64_t>(ctx_max, pos0 + L);
+    p.nsplit = ceil_div(span, ATT_C);
+    p.out = out;
+    p.xq = xq;
+    p.xd = xd;
+    return launch_chunks<false>(ctx, p, rows, scratch, zero_counters);
+}
+
+int launch_attention_decode_fused(lq_ctx* ctx, const float* qkv, const uint16_t* qn, const uint16_t* kn,
+                                  float eps, const float* cos_t, const float* sin_t, float* kc, float* vc,
+                                  int64_t B, int64_t Hq, int64_t Hkv, const int32_t* pos_dev, int64_t ctx_max,
+                                  int8_t* xq, uint16_t* xd, void* scratch) {
+    if (B == 0) return LQ_OK;
+    AttParams p = {};
+    p.qkv = qkv;
+    p.qn = qn;
+    p.kn = kn;
+    p.eps = eps;
+    p.cos_t = cos_t;
+    p.sin_t = sin_t;
+    p.kc = kc;
+    p.vc = vc;
+    p.Hq = (int)Hq;
+    p.Hkv = (int)Hkv;
+    p.L = 1;
+    p.pos0_dev = pos_dev;
+    p.ctx_max = (int)ctx_max;
+    p.nsplit = ceil_div(ctx_max, ATT_C);
+    p.xq = xq;
+    p.xd = xd;
+    return launch_chunks<true>(ctx, p, B, scratch, false);
 }
 
 }  // namespace lq
@@ -261,8 +382,8 @@ extern "C" int lq_attention(lq_ctx* ctx, const float* q, const float* kc, const 
     LQ_REQUIRE(ctx, (xq == nullptr) == (xd == nullptr), "lq_attention: xq and xd go together");
     if (B == 0 || L == 0) return LQ_OK;
     LQ_REQUIRE(ctx, q && kc && vc && (out || xq), "lq_attention: NULL pointer");
-    size_t need = lq::attention_scratch_bytes(B * L, Hq, ctx_max, D);
-    int rc = lq::ensure_scratch(ctx, need);
+    const size_t need = lq::attention_scratch_bytes(B * L, Hq, ctx_max, D);
+    const int rc = lq::ensure_scratch(ctx, need);
     if (rc) return rc;
     return lq::launch_attention(ctx, q, kc, vc, B, Hq, Hkv, L, pos0, pos0_dev, ctx_max, D, out, xq, xd,
                                 ctx->scratch, true);

@@ -185,8 +185,26 @@ int launch_q8_matmul(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const
                      int64_t m, float* y, const float* resid, int64_t ldy,
                      unsigned long long* argmax_keys);
 bool gemv_stream_supported(int64_t K);
+size_t gemv_stream_smem(int64_t m, int64_t K);
+// decode GEMV (m <= 4, K % 256 == 0) on pre-quantized activations
 int launch_gemv_stream(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd, int64_t m,
                        float* y, const float* resid, int64_t ldy, unsigned long long* keys);
+// decode GEMV whose prologue is RMSNorm + Q8_0 of the f32 rows x [m][K]
+int launch_gemv_norm(lq_ctx* ctx, const lq_q8_tensor* w, const float* x, const uint16_t* norm_w, float eps,
+                     int64_t m, float* y, const float* resid, int64_t ldy, unsigned long long* keys);
+// decode GEMV of the fused [gate; up] weight (2I rows) with the RMSNorm prologue and the
+// SwiGLU epilogue: h [m][I] (row stride ldh) = silu(x.gate^T) * (x.up^T)
+int launch_gemv_norm_swiglu(lq_ctx* ctx, const lq_q8_tensor* w, const float* x, const uint16_t* norm_w, float eps,
+                            int64_t m, float* h, int64_t ldh);
+// decode GEMV whose prologue is the Q8_0 quantization of the f32 rows x [m][K]
+int launch_gemv_quant(lq_ctx* ctx, const lq_q8_tensor* w, const float* x, int64_t m, float* y, const float* resid,
+                      int64_t ldy);
+// decode attention (L = 1) with q/k RMSNorm, RoPE and the KV-cache append fused in; reads the
+// fused q|k|v projection rows qkv [B][(Hq+2Hkv)*128]
+int launch_attention_decode_fused(lq_ctx* ctx, const float* qkv, const uint16_t* qn, const uint16_t* kn,
+                                  float eps, const float* cos_t, const float* sin_t, float* kc, float* vc,
+                                  int64_t B, int64_t Hq, int64_t Hkv, const int32_t* pos_dev, int64_t ctx_max,
+                                  int8_t* xq, uint16_t* xd, void* scratch);
 int launch_fill_bf16(lq_ctx* ctx, uint64_t seed, uint64_t tid, int64_t offset, int64_t count,
                      float scale, uint16_t* out);
 int launch_fill_norm(lq_ctx* ctx, uint64_t seed, uint64_t tid, int64_t count, float norm_std,

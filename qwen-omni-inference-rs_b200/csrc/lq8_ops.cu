@@ -1,6 +1,8 @@
 // lq8_ops.cu -- the small Qwen3 ops that keep activations in HBM, fused with the Q8_0
-// quantization of their output where the next op is a Q8_0 linear.
+// quantization of their output where the next op is a Q8_0 linear. The row math lives in
+// lq8_fused.cuh and is shared with the fused prologues of the decode kernels.
 #include "lq8_async.cuh"
+#include "lq8_fused.cuh"
 #include "lq8_internal.cuh"
 
 #include <cmath>
@@ -12,138 +14,38 @@ __device__ __forceinline__ void set_err(int* flag, int code, int value) {
     if (flag && atomicCAS(flag, 0, code) == 0) flag[1] = value;
 }
 
-// quantize_group8 is defined in lq8_q8.cu; a local copy keeps this unit self-contained
-__device__ __forceinline__ uint32_t quant_group8(const float v[4], int sub, uint16_t* d_out) {
-    float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-    float d, id;
-    q8_scale(amax, d, id);
-    if (sub == 0 && d_out) *d_out = f2h(d);
-    uint32_t q0 = (uint32_t)(q8_quant(v[0], id) & 0xFF), q1 = (uint32_t)(q8_quant(v[1], id) & 0xFF);
-    uint32_t q2 = (uint32_t)(q8_quant(v[2], id) & 0xFF), q3 = (uint32_t)(q8_quant(v[3], id) & 0xFF);
-    return q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
-}
-
-template <int THREADS>
-__device__ __forceinline__ float block_sum(float v, float* red) {
-    v = warp_sum(v);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    float t = 0.0f;
-    if (warp == 0) {
-        t = lane < THREADS / 32 ? red[lane] : 0.0f;
-        t = warp_sum(t);
-        if (lane == 0) red[0] = t;
-    }
-    __syncthreads();
-    t = red[0];
-    __syncthreads();
-    return t;
-}
+constexpr int NORM_THREADS = 256;
 
 // =========================================================================================
-// RMSNorm (rms_norm.rs:144-176) + optional Q8_0 quantization of the bf16 output.
-// One CTA per row; thread t handles 4 consecutive elements of each 1024-element chunk, so an
-// aligned 8-lane group covers one 32-element Q8_0 block.
+// RMSNorm (rms_norm.rs:144-176) + optional Q8_0 quantization of the bf16 output; one CTA
+// of 256 threads per row (the same row function as the fused GEMV prologue).
 // =========================================================================================
 template <typename T>
-__device__ __forceinline__ void load4_any(const T* p, float v[4]);
-template <>
-__device__ __forceinline__ void load4_any<float>(const float* p, float v[4]) {
-    float4 t = *reinterpret_cast<const float4*>(p);
-    v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
-}
-template <>
-__device__ __forceinline__ void load4_any<uint16_t>(const uint16_t* p, float v[4]) {
-    uint2 t = *reinterpret_cast<const uint2*>(p);
-    v[0] = bf16_to_f32((uint16_t)(t.x & 0xFFFF)); v[1] = bf16_to_f32((uint16_t)(t.x >> 16));
-    v[2] = bf16_to_f32((uint16_t)(t.y & 0xFFFF)); v[3] = bf16_to_f32((uint16_t)(t.y >> 16));
-}
-
-template <typename T, int THREADS>
-__global__ void __launch_bounds__(THREADS)
+__global__ void __launch_bounds__(NORM_THREADS)
 rmsnorm_kernel(const T* __restrict__ x, int dim, const uint16_t* __restrict__ w, float eps,
                uint16_t* __restrict__ out, int8_t* __restrict__ xq, uint16_t* __restrict__ xd) {
     __shared__ float red[32];
     pdl_wait();
     pdl_trigger();
-    const int row = blockIdx.x;
-    const T* xr = x + (size_t)row * dim;
-    float ss = 0.0f;
-    for (int base = 0; base < dim; base += THREADS * 4) {
-        int e = base + threadIdx.x * 4;
-        if (e < dim) {
-            float v[4];
-            load4_any<T>(xr + e, v);
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                float r = round_bf16(v[i]);  // F32 input is rounded to bf16 first (rms_norm.rs:144)
-                ss = __fadd_rn(ss, __fmul_rn(r, r));
-            }
-        }
-    }
-    ss = block_sum<THREADS>(ss, red);
-    const float mean = __fdiv_rn(ss, (float)dim);
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
-    const int nb = dim >> 5;
-    for (int base = 0; base < dim; base += THREADS * 4) {
-        int e = base + threadIdx.x * 4;
-        bool valid = e < dim;
-        float v[4] = {0.f, 0.f, 0.f, 0.f};
-        if (valid) {
-            load4_any<T>(xr + e, v);
-            uint2 wt = *reinterpret_cast<const uint2*>(w + e);
-            float wv[4] = {bf16_to_f32((uint16_t)(wt.x & 0xFFFF)), bf16_to_f32((uint16_t)(wt.x >> 16)),
-                           bf16_to_f32((uint16_t)(wt.y & 0xFFFF)), bf16_to_f32((uint16_t)(wt.y >> 16))};
-            uint16_t o[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                float r = round_bf16(v[i]);
-                o[i] = f32_to_bf16(__fmul_rn(__fmul_rn(r, inv), wv[i]));
-                v[i] = bf16_to_f32(o[i]);
-            }
-            if (out) {
-                uint2 ov;
-                ov.x = (uint32_t)o[0] | ((uint32_t)o[1] << 16);
-                ov.y = (uint32_t)o[2] | ((uint32_t)o[3] << 16);
-                *reinterpret_cast<uint2*>(out + (size_t)row * dim + e) = ov;
-            }
-        }
-        if (xq) {  // uniform branch: every lane takes part in the group shuffles
-            int sub = threadIdx.x & 7;
-            uint16_t* dptr = valid ? xd + (size_t)row * nb + (e >> 5) : nullptr;
-            uint32_t q = quant_group8(v, sub, dptr);
-            if (valid) *reinterpret_cast<uint32_t*>(xq + (size_t)row * dim + e) = q;
-        }
-    }
+    const int64_t row = blockIdx.x;
+    rms_row<T, NORM_THREADS, 0>(x + row * dim, dim, w, eps, threadIdx.x, red, out ? out + row * dim : nullptr,
+                                xq ? xq + row * dim : nullptr, xq ? xd + row * (dim >> 5) : nullptr);
 }
 
 int launch_rmsnorm(lq_ctx* ctx, const void* x, lq_dtype dt, int64_t rows, int64_t dim,
                    const uint16_t* w, float eps, uint16_t* out, int8_t* xq, uint16_t* xd) {
     if (rows == 0) return LQ_OK;
     const dim3 grid((unsigned)rows);
-    if (dim <= 1024) {
-        if (dt == LQ_DTYPE_F32)
-            return launch_kernel(ctx, rmsnorm_kernel<float, 128>, grid, dim3(128), 0, "rmsnorm", (const float*)x,
-                                 (int)dim, w, eps, out, xq, xd);
-        return launch_kernel(ctx, rmsnorm_kernel<uint16_t, 128>, grid, dim3(128), 0, "rmsnorm", (const uint16_t*)x,
-                             (int)dim, w, eps, out, xq, xd);
-    }
     if (dt == LQ_DTYPE_F32)
-        return launch_kernel(ctx, rmsnorm_kernel<float, 256>, grid, dim3(256), 0, "rmsnorm", (const float*)x,
+        return launch_kernel(ctx, rmsnorm_kernel<float>, grid, dim3(NORM_THREADS), 0, "rmsnorm", (const float*)x,
                              (int)dim, w, eps, out, xq, xd);
-    return launch_kernel(ctx, rmsnorm_kernel<uint16_t, 256>, grid, dim3(256), 0, "rmsnorm", (const uint16_t*)x,
-                         (int)dim, w, eps, out, xq, xd);
+    return launch_kernel(ctx, rmsnorm_kernel<uint16_t>, grid, dim3(NORM_THREADS), 0, "rmsnorm",
+                         (const uint16_t*)x, (int)dim, w, eps, out, xq, xd);
 }
 
 // =========================================================================================
 // per-head q/k RMSNorm + RoPE + KV-cache append (attention.rs:337-364, rope.rs:245-303).
-// One warp per (token row, head). head_dim = 128: lane p holds dims (2p, 2p+1) and
-// (64+2p, 64+2p+1), which is exactly one RoPE rotation pair set, so the rotation is
-// lane-local. Heads [0,Hq) are q, [Hq,Hq+Hkv) k, [Hq+Hkv, Hq+2Hkv) v (copied).
+// One warp per (token row, head). Heads [0,Hq) are q, [Hq,Hq+Hkv) k, [Hq+Hkv, Hq+2Hkv) v.
 // =========================================================================================
 __global__ void __launch_bounds__(256)
 qk_norm_rope_kv_kernel(const float* __restrict__ qkv, int B, int L, int Hq, int Hkv,
@@ -168,38 +70,17 @@ qk_norm_rope_kv_kernel(const float* __restrict__ qkv, int B, int L, int Hq, int 
         return;
     }
     const float* src = qkv + row * (int64_t)heads * D + (int64_t)h * D;
-    const int d0 = 2 * lane;
-    float2 a = *reinterpret_cast<const float2*>(src + d0);
-    float2 c = *reinterpret_cast<const float2*>(src + RD + d0);
     if (h >= Hq + Hkv) {  // v: KvCache::append of the projection output (f32)
-        int kvh = h - Hq - Hkv;
+        const int kvh = h - Hq - Hkv;
         float* dst = vc + (((int64_t)b * Hkv + kvh) * ctx_max + pos) * D;
-        *reinterpret_cast<float2*>(dst + d0) = a;
-        *reinterpret_cast<float2*>(dst + RD + d0) = c;
+        const int d0 = 2 * lane;
+        *reinterpret_cast<float2*>(dst + d0) = *reinterpret_cast<const float2*>(src + d0);
+        *reinterpret_cast<float2*>(dst + RD + d0) = *reinterpret_cast<const float2*>(src + RD + d0);
         return;
     }
-    const uint16_t* nw = h < Hq ? qn : kn;
-    // RmsNorm::forward on the bf16-rounded head vector
-    float v[4] = {round_bf16(a.x), round_bf16(a.y), round_bf16(c.x), round_bf16(c.y)};
-    float ss = __fadd_rn(__fadd_rn(__fmul_rn(v[0], v[0]), __fmul_rn(v[1], v[1])),
-                         __fadd_rn(__fmul_rn(v[2], v[2]), __fmul_rn(v[3], v[3])));
-    ss = warp_sum(ss);
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), eps)));
-    const int dims[4] = {d0, d0 + 1, RD + d0, RD + d0 + 1};
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-        v[i] = round_bf16(__fmul_rn(__fmul_rn(v[i], inv), bf16_to_f32(nw[dims[i]])));
-    // RoPE: x1 = (v0, v1) first half, x2 = (v2, v3) second half; table column 2p
-    const float cs = cos_t[(int64_t)pos * RD + d0], sn = sin_t[(int64_t)pos * RD + d0];
-    float r0 = __fsub_rn(__fmul_rn(v[0], cs), __fmul_rn(v[2], sn));
-    float r1 = __fsub_rn(__fmul_rn(v[1], cs), __fmul_rn(v[3], sn));
-    float r2 = __fadd_rn(__fmul_rn(v[2], cs), __fmul_rn(v[0], sn));
-    float r3 = __fadd_rn(__fmul_rn(v[3], cs), __fmul_rn(v[1], sn));
-    float* dst;
-    if (h < Hq) dst = q_out + (((int64_t)b * Hq + h) * L + l) * D;
-    else dst = kc + (((int64_t)b * Hkv + (h - Hq)) * ctx_max + pos) * D;
-    *reinterpret_cast<float2*>(dst + d0) = make_float2(r0, r1);
-    *reinterpret_cast<float2*>(dst + RD + d0) = make_float2(r2, r3);
+    float* dst = h < Hq ? q_out + (((int64_t)b * Hq + h) * L + l) * D
+                        : kc + (((int64_t)b * Hkv + (h - Hq)) * ctx_max + pos) * D;
+    head_norm_rope(src, h < Hq ? qn : kn, eps, cos_t + (int64_t)pos * RD, sin_t + (int64_t)pos * RD, lane, dst);
 }
 
 int launch_qk_norm_rope_kv(lq_ctx* ctx, const float* qkv, int64_t B, int64_t L, int64_t Hq,
@@ -208,7 +89,7 @@ int launch_qk_norm_rope_kv(lq_ctx* ctx, const float* qkv, int64_t B, int64_t L, 
                            const int32_t* pos0_dev, float* q_out, float* kc, float* vc,
                            int64_t ctx_max) {
     (void)D;
-    int64_t items = B * L * (Hq + 2 * Hkv);
+    const int64_t items = B * L * (Hq + 2 * Hkv);
     if (items == 0) return LQ_OK;
     return launch_kernel(ctx, qk_norm_rope_kv_kernel, dim3(ceil_div(items, 8)), dim3(256), 0, "qk_norm_rope_kv",
                          qkv, (int)B, (int)L, (int)Hq, (int)Hkv, qn, kn, eps, cos_t, sin_t, (int)pos0, pos0_dev,
@@ -216,45 +97,24 @@ int launch_qk_norm_rope_kv(lq_ctx* ctx, const float* qkv, int64_t B, int64_t L, 
 }
 
 // =========================================================================================
-// SiLU(gate) * up (mlp.rs:153-160; tensor.rs:1977-1986 x/(1+exp(-x)); mul f32) + Q8_0
+// SiLU(gate) * up + Q8_0, one CTA of 256 threads per row (the same row function as the fused
+// down-projection prologue)
 // =========================================================================================
 __global__ void __launch_bounds__(256)
-silu_mul_kernel(const float* __restrict__ gu, int64_t m, int inter, float* __restrict__ h,
-                int8_t* __restrict__ xq, uint16_t* __restrict__ xd) {
+silu_mul_kernel(const float* __restrict__ gu, int inter, float* __restrict__ h, int8_t* __restrict__ xq,
+                uint16_t* __restrict__ xd) {
     pdl_wait();
     pdl_trigger();
-    const int64_t nblk = m * (inter >> 5);
-    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const int64_t blk = gid >> 3;
-    const int sub = threadIdx.x & 7;
-    const bool valid = blk < nblk;
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
-    int64_t row = 0, col = 0;
-    if (valid) {
-        row = blk / (inter >> 5);
-        col = (blk % (inter >> 5)) * 32 + sub * 4;
-        float4 g = *reinterpret_cast<const float4*>(gu + row * 2 * inter + col);
-        float4 u = *reinterpret_cast<const float4*>(gu + row * 2 * inter + inter + col);
-        float gg[4] = {g.x, g.y, g.z, g.w}, uu[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            float s = __fdiv_rn(gg[i], __fadd_rn(1.0f, expf(-gg[i])));
-            v[i] = __fmul_rn(s, uu[i]);
-        }
-        if (h) *reinterpret_cast<float4*>(h + row * inter + col) = make_float4(v[0], v[1], v[2], v[3]);
-    }
-    if (xq) {
-        uint32_t q = quant_group8(v, sub, valid ? xd + blk : nullptr);
-        if (valid) *reinterpret_cast<uint32_t*>(xq + row * inter + col) = q;
-    }
+    const int64_t row = blockIdx.x;
+    silu_row<256>(gu + row * 2 * inter, inter, threadIdx.x, h ? h + row * inter : nullptr,
+                  xq ? xq + row * inter : nullptr, xq ? xd + row * (inter >> 5) : nullptr);
 }
 
 int launch_silu_mul(lq_ctx* ctx, const float* gu, int64_t m, int64_t inter, float* h, int8_t* xq,
                     uint16_t* xd) {
-    int64_t threads = m * (inter / 32) * 8;
-    if (threads == 0) return LQ_OK;
-    return launch_kernel(ctx, silu_mul_kernel, dim3(ceil_div(threads, 256)), dim3(256), 0, "silu_mul", gu, m,
-                         (int)inter, h, xq, xd);
+    if (m == 0) return LQ_OK;
+    return launch_kernel(ctx, silu_mul_kernel, dim3((unsigned)m), dim3(256), 0, "silu_mul", gu, (int)inter, h, xq,
+                         xd);
 }
 
 // =========================================================================================
@@ -273,7 +133,7 @@ __global__ void embedding_kernel(const uint16_t* __restrict__ table, int64_t voc
     for (int c = threadIdx.x * 4; c < hidden; c += blockDim.x * 4) {
         float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
         if (ok) {
-            uint2 t = *reinterpret_cast<const uint2*>(table + (int64_t)id * hidden + c);
+            const uint2 t = *reinterpret_cast<const uint2*>(table + (int64_t)id * hidden + c);
             o = make_float4(bf16_to_f32((uint16_t)(t.x & 0xFFFF)), bf16_to_f32((uint16_t)(t.x >> 16)),
                             bf16_to_f32((uint16_t)(t.y & 0xFFFF)), bf16_to_f32((uint16_t)(t.y >> 16)));
         }
@@ -299,12 +159,12 @@ argmax_kernel(const float* __restrict__ x, int64_t n, int32_t* __restrict__ out)
     const float* xr = x + (int64_t)blockIdx.x * n;
     unsigned long long best = 0ull;
     for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
-        unsigned long long k = argmax_key(xr[i], (int)i);
+        const unsigned long long k = argmax_key(xr[i], (int)i);
         best = k > best ? k : best;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-        unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+        const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
         best = v > best ? v : best;
     }
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
@@ -313,18 +173,20 @@ argmax_kernel(const float* __restrict__ x, int64_t n, int32_t* __restrict__ out)
         best = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0ull;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
-            unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+            const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
             best = v > best ? v : best;
         }
         if (threadIdx.x == 0) out[blockIdx.x] = (int32_t)(uint32_t)(best & 0xFFFFFFFFull);
     }
 }
 
+// next token ids from the LM head's fused argmax keys; clears the keys for the next step and
+// advances the device position of the decode graph
 __global__ void argmax_finalize_kernel(unsigned long long* keys, int64_t rows, int32_t* out,
                                        int32_t* pos_counter) {
     pdl_wait();
     pdl_trigger();
-    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < rows) {
         out[i] = (int32_t)(uint32_t)(keys[i] & 0xFFFFFFFFull);
         keys[i] = 0ull;
@@ -336,6 +198,13 @@ int launch_argmax_finalize(lq_ctx* ctx, unsigned long long* keys, int64_t rows, 
                            int32_t* pos_counter) {
     return launch_kernel(ctx, argmax_finalize_kernel, dim3(ceil_div(std::max<int64_t>(rows, 1), 128)), dim3(128),
                          0, "argmax_finalize", keys, rows, out, pos_counter);
+}
+
+__global__ void add_kernel(const float* a, const float* b, int64_t n, float* out) {
+    pdl_wait();
+    pdl_trigger();
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = __fadd_rn(a[i], b[i]);
 }
 
 }  // namespace lq
@@ -366,14 +235,14 @@ int lq_rope_tables(lq_ctx* ctx, int64_t head_dim, int64_t max_pos, double theta,
                "lq_rope_tables: head_dim must be a multiple of 4 (rope.rs:77-83 requires even)");
     LQ_REQUIRE(ctx, cos_dev && sin_dev, "lq_rope_tables: NULL pointer");
     // rope.rs:89-117, evaluated in double on the host exactly like the reference
-    int64_t rd = head_dim / 2, half = rd / 2;
+    const int64_t rd = head_dim / 2, half = rd / 2;
     std::vector<double> inv(half);
     for (int64_t i = 0; i < half; i++) inv[i] = 1.0 / std::pow(theta, (double)(2 * i) / (double)rd);
     std::vector<float> c((size_t)(max_pos * rd)), s((size_t)(max_pos * rd));
     for (int64_t p = 0; p < max_pos; p++)
         for (int64_t i = 0; i < half; i++) {
-            double fr = (double)p * inv[i];
-            float cv = (float)std::cos(fr), sv = (float)std::sin(fr);
+            const double fr = (double)p * inv[i];
+            const float cv = (float)std::cos(fr), sv = (float)std::sin(fr);
             c[p * rd + 2 * i] = cv; c[p * rd + 2 * i + 1] = cv;
             s[p * rd + 2 * i] = sv; s[p * rd + 2 * i + 1] = sv;
         }
@@ -402,32 +271,20 @@ int lq_qk_norm_rope_kv(lq_ctx* ctx, const float* qkv, int64_t B, int64_t L, int6
 int lq_silu_mul(lq_ctx* ctx, const float* gu, int64_t m, int64_t inter, float* h, int8_t* xq, uint16_t* xd) {
     LQ_ENTRY(ctx, "lq_silu_mul");
     LQ_REQUIRE(ctx, m >= 0 && inter > 0 && inter % 32 == 0, "lq_silu_mul: inter must be a multiple of 32");
+    LQ_REQUIRE(ctx, m < (1ll << 31), "lq_silu_mul: too many rows");
     LQ_REQUIRE(ctx, (xq == nullptr) == (xd == nullptr), "lq_silu_mul: xq and xd go together");
     if (m == 0) return LQ_OK;
     LQ_REQUIRE(ctx, gu && (h || xq), "lq_silu_mul: NULL pointer");
     return lq::launch_silu_mul(ctx, gu, m, inter, h, xq, xd);
 }
 
-}  // extern "C"
-
-namespace lq {
-__global__ void add_kernel(const float* a, const float* b, int64_t n, float* out) {
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-        out[i] = __fadd_rn(a[i], b[i]);
-}
-}  // namespace lq
-
-extern "C" {
-
 int lq_add(lq_ctx* ctx, const float* a, const float* b, int64_t n, float* out) {
     LQ_ENTRY(ctx, "lq_add");
     LQ_REQUIRE(ctx, n >= 0, "lq_add: negative size");
     if (n == 0) return LQ_OK;
     LQ_REQUIRE(ctx, a && b && out, "lq_add: NULL pointer");
-    int grid = (int)std::min<int64_t>((n + 255) / 256, (int64_t)ctx->sm_count * 16);
-    lq::add_kernel<<<grid, 256, 0, ctx->stream>>>(a, b, n, out);
-    LQ_LAUNCH_CHECK(ctx, "add");
-    return LQ_OK;
+    const int grid = (int)std::min<int64_t>((n + 255) / 256, (int64_t)ctx->sm_count * 16);
+    return lq::launch_kernel(ctx, lq::add_kernel, dim3(grid), dim3(256), 0, "add", a, b, n, out);
 }
 
 int lq_embedding(lq_ctx* ctx, const uint16_t* table, int64_t vocab, int64_t hidden, const int32_t* ids, int64_t n,
@@ -446,9 +303,7 @@ int lq_argmax(lq_ctx* ctx, const float* x, int64_t rows, int64_t n, int32_t* out
     LQ_REQUIRE(ctx, rows >= 0 && n > 0 && n < (1ll << 31), "lq_argmax: bad shape");
     if (rows == 0) return LQ_OK;
     LQ_REQUIRE(ctx, x && out, "lq_argmax: NULL pointer");
-    lq::argmax_kernel<<<(unsigned)rows, 1024, 0, ctx->stream>>>(x, n, out);
-    LQ_LAUNCH_CHECK(ctx, "argmax");
-    return LQ_OK;
+    return lq::launch_kernel(ctx, lq::argmax_kernel, dim3((unsigned)rows), dim3(1024), 0, "argmax", x, n, out);
 }
 
 }  // extern "C"

@@ -5,6 +5,7 @@
 // once at load.
 #include "lq8_internal.cuh"
 #include "lq8_async.cuh"
+#include "lq8_fused.cuh"
 
 namespace lq {
 
@@ -25,21 +26,6 @@ __device__ __forceinline__ void load4<uint16_t>(const uint16_t* p, float v[4]) {
     v[2] = bf16_to_f32((uint16_t)(t.y & 0xFFFF)); v[3] = bf16_to_f32((uint16_t)(t.y >> 16));
 }
 
-// Quantize 4 values held by each lane of an aligned 8-lane group (one Q8_0 block); returns
-// the packed int8x4 and writes the block scale through lane 0 of the group.
-__device__ __forceinline__ uint32_t quantize_group8(const float v[4], int sub, uint16_t* d_out) {
-    float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-    float d, id;
-    q8_scale(amax, d, id);
-    if (sub == 0 && d_out) *d_out = f2h(d);
-    uint32_t q0 = (uint32_t)(q8_quant(v[0], id) & 0xFF), q1 = (uint32_t)(q8_quant(v[1], id) & 0xFF);
-    uint32_t q2 = (uint32_t)(q8_quant(v[2], id) & 0xFF), q3 = (uint32_t)(q8_quant(v[3], id) & 0xFF);
-    return q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
-}
-
 template <typename T>
 __global__ void quantize_rows_kernel(const T* __restrict__ src, int64_t nblocks, int8_t* __restrict__ qs,
                                      uint16_t* __restrict__ d) {
@@ -49,7 +35,7 @@ __global__ void quantize_rows_kernel(const T* __restrict__ src, int64_t nblocks,
     bool valid = blk < nblocks;
     float v[4] = {0.f, 0.f, 0.f, 0.f};
     if (valid) load4<T>(src + blk * QK + sub * 4, v);
-    uint32_t q = quantize_group8(v, sub, valid ? d + blk : nullptr);
+    uint32_t q = quant_group8(v, sub, valid ? d + blk : nullptr);
     if (valid) reinterpret_cast<uint32_t*>(qs + blk * QK)[sub] = q;
 }
 
@@ -458,7 +444,9 @@ int launch_q8_matmul(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const
                      int64_t m, float* y, const float* resid, int64_t ldy,
                      unsigned long long* keys) {
     if (m <= 0 || w->n <= 0) return LQ_OK;
-    if (m <= 4 && gemv_stream_supported(w->k)) return launch_gemv_stream(ctx, w, xq, xd, m, y, resid, ldy, keys);
+    if (m <= 4 && gemv_stream_supported(w->k) && ((uintptr_t)xq % 16) == 0 && ((uintptr_t)xd % 16) == 0 &&
+        gemv_stream_smem(m, w->k) <= 227 * 1024)
+        return launch_gemv_stream(ctx, w, xq, xd, m, y, resid, ldy, keys);
     switch (m) {
         case 1: return gemv_rows<1>(ctx, w, xq, xd, y, resid, ldy, keys);
         case 2: return gemv_rows<2>(ctx, w, xq, xd, y, resid, ldy, keys);

@@ -10,6 +10,7 @@
 #include "lq8_internal.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 #include <vector>
 
 namespace {
@@ -57,6 +58,7 @@ struct lq_model {
     cudaGraphExec_t exec = nullptr;
     int64_t graph_batch = 0;
     int64_t graph_kernels = 0;   // kernel nodes in the decode graph
+    bool fused_decode = false;   // the decode GEMVs can take every K of this model
     std::vector<void*> allocs;
 };
 
@@ -127,6 +129,25 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
 #define RC(expr) do { rc = (expr); if (rc) return rc; } while (0)
     RC(lq::launch_embedding(ctx, m->embed, c.vocab, H, m->tokens, rows, m->x));
     const size_t kv_layer = (size_t)(m->max_batch * Hkv * m->ctx_max * D);
+    if (L == 1 && pos_dev && m->fused_decode && B <= 4) {
+        // decode, five kernels per layer: [norm -> q|k|v] [q/k norm, RoPE, KV append,
+        // attention -> Q8_0] [o + residual] [norm -> gate|up -> SiLU*up] [down + residual]
+        for (size_t li = 0; li < m->layers.size(); li++) {
+            Layer& ly = m->layers[li];
+            float* kc = m->kc + li * kv_layer;
+            float* vc = m->vc + li * kv_layer;
+            RC(lq::launch_gemv_norm(ctx, &ly.qkv, m->x, ly.in_norm, c.eps, B, m->qkv, nullptr, m->Nqkv, nullptr));
+            RC(lq::launch_attention_decode_fused(ctx, m->qkv, ly.q_norm, ly.k_norm, c.eps, m->cos_t, m->sin_t, kc, vc,
+                                                 B, Hq, Hkv, pos_dev, m->ctx_max, m->xq, m->xd, m->att_scratch));
+            RC(lq::launch_gemv_stream(ctx, &ly.o, m->xq, m->xd, B, m->x, m->x, H, nullptr));
+            RC(lq::launch_gemv_norm_swiglu(ctx, &ly.gate_up, m->x, ly.post_norm, c.eps, B, m->gu, I));
+            RC(lq::launch_gemv_quant(ctx, &ly.down, m->gu, B, m->x, m->x, H));
+        }
+        RC(lq::launch_gemv_norm(ctx, &m->lm_head, m->x, m->final_norm, c.eps, B, m->logits, nullptr, c.vocab,
+                                m->keys));
+        RC(lq::launch_argmax_finalize(ctx, m->keys, B, m->tokens, bump_pos ? m->pos_dev : nullptr));
+        return LQ_OK;
+    }
     for (size_t li = 0; li < m->layers.size(); li++) {
         Layer& ly = m->layers[li];
         float* kc = m->kc + li * kv_layer;
@@ -320,6 +341,14 @@ int lq_qwen3_create(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int6
     LQ_CUDA(ctx, cudaMemsetAsync(m->vc, 0, kv * 4, ctx->stream));
     LQ_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
 #undef RC
+    {
+        // the fused decode path needs every matmul K on the streaming GEMV (K % 256 == 0,
+        // 4 tokens of activations in shared memory); LQ_UNFUSED=1 forces the separate kernels
+        bool ok = getenv("LQ_UNFUSED") == nullptr;
+        for (int64_t k : {H, m->Hqd, I})
+            ok = ok && lq::gemv_stream_supported(k) && lq::gemv_stream_smem(4, k) <= 227 * 1024;
+        m->fused_decode = ok;
+    }
     *out = m;
     return LQ_OK;
 }

@@ -149,6 +149,32 @@ def test_prefill_after_decode_is_reproducible(ctx, lq8_lib, oracle):
     assert np.array_equal(l0, l1) and np.array_equal(n0, n1)
 
 
+@pytest.mark.parametrize("B", [1, 3])
+def test_fused_decode_equals_separate_kernels(ctx, lq8_lib, oracle, monkeypatch, B):
+    """The batch <= 4 decode step runs five fused kernels per layer (RMSNorm and SiLU as GEMV
+    prologues, q/k norm + RoPE + KV append inside attention). They reuse the standalone row
+    functions, so logits must equal the separate-kernel path bit for bit."""
+    cfgd = dict(TINY, tied=0)
+    prompts = np.stack([oracle.gen_tokens(8, s, 9, cfgd["vocab"]) for s in range(B)])
+    outs = []
+    for unfused in (False, True):
+        if unfused:
+            monkeypatch.setenv("LQ_UNFUSED", "1")
+        else:
+            monkeypatch.delenv("LQ_UNFUSED", raising=False)
+        gm = lq8_lib.Qwen3ForCausalLM(ctx, lq8_lib.make_config(**cfgd), 8, max_batch=B, ctx_max=32)
+        gm.set_batch(B)
+        t = gm.prefill(prompts)
+        lgs = []
+        for _ in range(4):
+            t, lg = gm.decode_step(t, want_logits=True)
+            lgs.append(lg)
+        outs.append(np.stack(lgs))
+        gm.close()
+    monkeypatch.delenv("LQ_UNFUSED", raising=False)
+    assert np.array_equal(outs[0], outs[1])
+
+
 def test_decode_past_context_is_an_error(ctx, lq8_lib, oracle):
     gm, ocfg = _models(lq8_lib, oracle, ctx, 5, TINY, ctx_max=8)
     prompt = oracle.gen_tokens(5, 0, 6, ocfg.vocab)
