@@ -76,6 +76,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, long l
         if (mbar_try_wait(bar, parity)) return true;
     return false;
 }
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Wait bounded by wall time (ns on the global timer) rather than by a poll count.
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t* bar, unsigned parity, uint64_t limit_ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (global_ns() - t0 > limit_ns) return false;
+    }
+}
 // one bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned); no multicast
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
     asm volatile(

@@ -185,6 +185,10 @@ int launch_q8_matmul(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const
                      int64_t m, float* y, const float* resid, int64_t ldy,
                      unsigned long long* argmax_keys);
 bool gemv_stream_supported(int64_t K);
+// prefill GEMM on tcgen05 (m >= 64 tokens, K % 256 == 0, 16-byte aligned operands)
+bool gemm_tc_supported(int64_t m, int64_t K, const void* wq, const void* xq, const void* wd, const void* xd);
+int launch_gemm_tc(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd, int64_t m, float* y,
+                   const float* resid, int64_t ldy);
 size_t gemv_stream_smem(int64_t m, int64_t K);
 // decode GEMV (m <= 4, K % 256 == 0) on pre-quantized activations
 int launch_gemv_stream(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd, int64_t m,

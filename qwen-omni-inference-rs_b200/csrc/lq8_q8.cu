@@ -454,6 +454,8 @@ int launch_q8_matmul(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const
         case 4: return gemv_rows<4>(ctx, w, xq, xd, y, resid, ldy, keys);
         default: break;
     }
+    if (!keys && gemm_tc_supported(m, w->k, w->qs, xq, w->d, xd))
+        return launch_gemm_tc(ctx, w, xq, xd, m, y, resid, ldy);
     if (m <= 16) return run_gemm<128, 16, 8, 1>(ctx, w, xq, xd, m, y, resid, ldy, keys);
     if (m <= 32) return run_gemm<128, 32, 8, 1>(ctx, w, xq, xd, m, y, resid, ldy, keys);
     if (m <= 64) return run_gemm<128, 64, 4, 2>(ctx, w, xq, xd, m, y, resid, ldy, keys);

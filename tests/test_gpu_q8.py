@@ -119,6 +119,49 @@ def test_gemm_bit_exact(ctx, lq8_lib, oracle, rng, m, n, k):
     assert np.array_equal(y, oracle.q8_0_matmul(xq, xd, wq, wd))
 
 
+@pytest.mark.parametrize("m", [64, 65, 127, 128, 300, 513])
+@pytest.mark.parametrize("n,k", [(128, 256), (129, 512), (1000, 4096), (4096, 1024)])
+def test_gemm_tcgen05_bit_exact(ctx, lq8_lib, oracle, rng, m, n, k):
+    """The tcgen05 prefill GEMM (m >= 64, k % 256 == 0): ragged row/token tiles, one stage
+    (k = 256) up to many, scales across a wide dynamic range, all-zero blocks."""
+    w = rng.standard_normal((n, k)) * 0.02
+    w[:, :32] *= 1e3
+    w[n // 2, 64:96] = 0.0
+    wq, wd = oracle.q8_0_quantize(oracle.f32_to_bf16(w.astype(np.float32)))
+    x = rng.standard_normal((m, k)) * rng.choice([1e-2, 1.0, 30.0], size=(m, 1))
+    x[m // 3, 32:64] = 0.0
+    xq, xd = oracle.q8_0_quantize(x.astype(np.float32))
+    y = _matmul(ctx, lq8_lib, wq, wd, xq, xd)
+    assert np.array_equal(y, oracle.q8_0_matmul(xq, xd, wq, wd))
+
+
+@pytest.mark.parametrize("m", [64, 200])
+def test_gemm_tcgen05_residual_and_stride(ctx, lq8_lib, oracle, rng, m):
+    n, k, ldy = 300, 768, 320
+    wq, wd = _weights(oracle, rng, n, k)
+    xq, xd = oracle.q8_0_quantize(rng.standard_normal((m, k)).astype(np.float32))
+    resid = rng.standard_normal((m, ldy)).astype(np.float32)
+    y = _matmul(ctx, lq8_lib, wq, wd, xq, xd, resid=resid, ldy=ldy)
+    ref = oracle.q8_0_matmul(xq, xd, wq, wd)
+    assert np.array_equal(y[:, :n], (resid[:, :n] + ref).astype(np.float32))
+    assert np.array_equal(y[:, n:], resid[:, n:])
+
+
+def test_gemm_tcgen05_matches_mma_sync_path(ctx, lq8_lib, oracle, rng, monkeypatch):
+    """Both prefill GEMM paths keep the oracle's summation order: identical bits at a
+    model-sized shape (LQ_NO_TCGEN05 routes the same call to the mma.sync kernel)."""
+    m, n, k = 256, 4096, 4096
+    wq, wd = _weights(oracle, rng, n, k)
+    xq, xd = oracle.q8_0_quantize(rng.standard_normal((m, k)).astype(np.float32))
+    y_tc = _matmul(ctx, lq8_lib, wq, wd, xq, xd)
+    monkeypatch.setenv("LQ_NO_TCGEN05", "1")
+    y_mma = _matmul(ctx, lq8_lib, wq, wd, xq, xd)
+    monkeypatch.delenv("LQ_NO_TCGEN05")
+    assert np.array_equal(y_tc, y_mma)
+    rows = rng.choice(m, 8, replace=False)
+    assert np.array_equal(y_tc[rows], oracle.q8_0_matmul(xq[rows], xd[rows], wq, wd))
+
+
 @pytest.mark.parametrize("m", [1, 16])
 def test_matmul_residual_and_stride(ctx, lq8_lib, oracle, rng, m):
     n, k, ldy = 200, 512, 256
