@@ -321,6 +321,8 @@ int launch_attention(lq_ctx* ctx, const float* q, const float* kc, const float* 
     (void)D;
     const int64_t rows = B * L;
     if (rows == 0) return LQ_OK;
+    if (attention_prefill_supported(L, Hq, Hkv))
+        return launch_attention_prefill(ctx, q, kc, vc, B, Hq, Hkv, L, pos0, pos0_dev, ctx_max, out, xq, xd);
     AttParams p = {};
     p.q = q;
     p.kc = const_cast<float*>(kc);

@@ -215,6 +215,11 @@ int launch_fill_norm(lq_ctx* ctx, uint64_t seed, uint64_t tid, int64_t count, fl
                      uint16_t* out);
 int launch_argmax_finalize(lq_ctx* ctx, unsigned long long* keys, int64_t rows, int32_t* out,
                            int32_t* pos_counter);
+// prefill attention (L >= 16 query positions per sequence): tiles of 128 (position, head) rows
+bool attention_prefill_supported(int64_t L, int64_t Hq, int64_t Hkv);
+int launch_attention_prefill(lq_ctx* ctx, const float* q, const float* kc, const float* vc, int64_t B, int64_t Hq,
+                             int64_t Hkv, int64_t L, int64_t pos0, const int32_t* pos0_dev, int64_t ctx_max,
+                             float* out, int8_t* xq, uint16_t* xd);
 size_t attention_scratch_bytes(int64_t rows, int64_t n_heads, int64_t ctx_max, int64_t head_dim);
 int attention_max_ctx();
 // scratch starts with per-(row, kv head) counters that must be zero before the first launch;

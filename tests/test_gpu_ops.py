@@ -129,6 +129,43 @@ def test_attention_vs_oracle(ctx, lq8_lib, oracle, rng, B, L, pos0, ctx_max, Hq,
     assert np.array_equal(H(xq), oq) and np.array_equal(H(xd, np.uint16), od)
 
 
+@pytest.mark.parametrize("B,L,pos0,ctx_max", [(1, 16, 0, 64), (2, 47, 0, 128), (1, 200, 70, 300),
+                                              (2, 129, 5, 2304), (1, 2048, 0, 2304)])
+@pytest.mark.parametrize("Hq,Hkv", [(16, 8), (32, 8), (64, 8), (32, 4), (8, 8)])
+def test_attention_prefill_tiles_vs_oracle(ctx, lq8_lib, oracle, rng, B, L, pos0, ctx_max, Hq, Hkv):
+    """Prefill attention (L >= 16: tiles of 128 (position, head) rows, online softmax over
+    64-key chunks): ragged last tiles, a prompt appended after cached positions, every GQA
+    group size Qwen3 uses. Rows are checked against the oracle's full-row softmax (all rows
+    for small cases, a seeded sample at L = 2048)."""
+    import torch
+    D = 128
+    G = Hq // Hkv
+    T_ = pos0 + L
+    q = rng.standard_normal((B, Hq, L, D)).astype(np.float32)
+    kc = np.zeros((B, Hkv, ctx_max, D), np.float32)
+    vc = np.zeros((B, Hkv, ctx_max, D), np.float32)
+    kc[:, :, :T_] = rng.standard_normal((B, Hkv, T_, D)) * 1.5
+    vc[:, :, :T_] = rng.standard_normal((B, Hkv, T_, D))
+    out = torch.empty((B * L, Hq * D), dtype=torch.float32, device="cuda")
+    xq = torch.empty((B * L, Hq * D), dtype=torch.int8, device="cuda")
+    xd = torch.empty((B * L, Hq * D // 32), dtype=torch.int16, device="cuda")
+    keep = [T(a) for a in (q, kc, vc)]
+    ctx.call("lq_attention", keep[0].data_ptr(), keep[1].data_ptr(), keep[2].data_ptr(), B, Hq, Hkv, L, pos0,
+             None, ctx_max, D, out.data_ptr(), xq.data_ptr(), xd.data_ptr())
+    ctx.synchronize()
+    got = H(out).reshape(B, L, Hq, D)
+    rows = [(b, l, h) for b in range(B) for l in range(L) for h in range(Hq)]
+    if len(rows) > 3000:
+        pick = rng.choice(len(rows), 400, replace=False)
+        rows = [rows[i] for i in pick] + [(0, L - 1, Hq - 1), (B - 1, 0, 0)]
+    for b, l, h in rows:
+        ref = oracle.attend_row(q[b, h, l], kc[b, h // G, :T_], vc[b, h // G, :T_], masked=True,
+                                causal_limit=pos0 + l)
+        np.testing.assert_allclose(got[b, l, h], ref, rtol=0, atol=2e-5 * np.abs(ref).max())
+    oq, od = oracle.q8_0_quantize(H(out))
+    assert np.array_equal(H(xq), oq) and np.array_equal(H(xd, np.uint16), od)
+
+
 @pytest.mark.parametrize("m,inter", [(1, 3072), (5, 768), (16, 12288)])
 def test_silu_mul_and_quant(ctx, lq8_lib, oracle, rng, m, inter):
     import torch
