@@ -417,6 +417,69 @@ def run_ours(args, cfgd, world, rank, local):
         dist.destroy_process_group()
 
 
+SWEEP_M = (1, 16, 128, 512, 2048)
+SWEEP_KN = ((1024, 3072), (3072, 1024), (4096, 12288), (12288, 4096), (5120, 25600))
+
+
+def run_sweep(args):
+    """Linear sweep: y = x . W^T through lq_q8_0_linear (activation quantization + Q8_0
+    matmul), x = N(0,1) in f32 and bf16, W = N(0,0.02) packed to Q8_0. Rotates through
+    >= 512 MB of distinct weight copies so every launch reads its weights from HBM; the
+    median of per-launch CUDA-event times after warm-up. One JSON line per case."""
+    import ctypes as C
+
+    import torch
+
+    import build
+    import lq8
+    build.build()
+    ctx = lq8.Context(0)
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=dev)
+    hbm, hbm_kind = peaks()
+    cases = []
+    if args.sweep_case:
+        m, n, k = (int(v) for v in args.sweep_case.split(","))
+        cases = [(m, k, n)]
+    else:
+        cases = [(m, k, n) for (k, n) in SWEEP_KN for m in SWEEP_M]
+    reps = max(args.sweep_reps, 3)
+    for (m, k, n) in cases:
+        wbytes = n * k * 34 // 32
+        copies = max(2, -(-512 * 2**20 // wbytes)) if not args.sweep_case else 2
+        g = torch.Generator(device=dev).manual_seed(SEED)
+        ws = []
+        for _ in range(copies):
+            wf = (torch.randn((n, k), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+            ws.append(lq8.QTensor.quantize(ctx, wf))
+            del wf
+        for src in ("f32", "bf16"):
+            x = torch.randn((m, k), generator=g, device=dev)
+            if src == "bf16":
+                x = x.to(torch.bfloat16)
+            dt = lq8.DTYPE_F32 if src == "f32" else lq8.DTYPE_BF16
+            y = torch.empty((m, n), dtype=torch.float32, device=dev)
+            structs = [w.struct() for w in ws]
+            for i in range(3):
+                ctx.call("lq_q8_0_linear", C.byref(structs[i % copies]), x.data_ptr(), dt, m, y.data_ptr())
+            ctx.synchronize()
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+            for i in range(reps):
+                ev[i][0].record(stream)
+                ctx.call("lq_q8_0_linear", C.byref(structs[i % copies]), x.data_ptr(), dt, m, y.data_ptr())
+                ev[i][1].record(stream)
+            ctx.synchronize()
+            us = statistics.median(a.elapsed_time(b) for a, b in ev) * 1e3
+            byts = wbytes + m * k * (4 if src == "f32" else 2) + m * n * 4
+            flops = 2.0 * m * n * k
+            print(json.dumps({"sweep": "q8_0_linear", "m": m, "k": k, "n": n, "x": src, "us": round(us, 2),
+                              "GB/s": round(byts / us / 1e3, 1), "TOPS": round(flops / us / 1e6, 1),
+                              "hbm_frac": round(byts / us / 1e3 / hbm, 3), "hbm_peak": hbm,
+                              "peak_kind": hbm_kind, "weight_copies": copies}), flush=True)
+        del ws
+        torch.cuda.empty_cache()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -435,9 +498,17 @@ def main():
                     help="timeline: run this many decode steps under torch.profiler and print a summary")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling: build only the first N layers (a smaller device footprint)")
+    ap.add_argument("--sweep", action="store_true",
+                    help="run the Linear sweep (M x (K, N) grid, f32 and bf16 inputs) and exit")
+    ap.add_argument("--sweep-case", default="",
+                    help="with --sweep: one case 'm,n,k' (two weight copies; for profiling)")
+    ap.add_argument("--sweep-reps", type=int, default=20)
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.sweep:
+        run_sweep(args)
+        return
     world, rank, local = dist_env()
     cfgd = dict(CONFIGS[args.config])
     if args.layers:

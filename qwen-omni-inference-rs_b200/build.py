@@ -38,6 +38,7 @@ def _nvcc() -> str:
 def _deps() -> list[str]:
     files = [os.path.join(CSRC, f) for f in os.listdir(CSRC)]
     files.append(os.path.join(INCLUDE, "lq8.h"))
+    files.append(os.path.abspath(__file__))
     return files
 
 

@@ -5,12 +5,15 @@
 // One MMA per Q8_0 block: tcgen05.mma.kind::i8 with K = 32 computes the exact int32 block
 // dot products of a 128-row weight tile (MMA M) by a 64-token tile (MMA N) into a fresh TMEM
 // accumulator. The per-block scales differ per (row, block) and per (token, block), so the
-// block results cannot be summed inside TMEM; 8 epilogue warps read every block's int32 tile
+// block results cannot be summed inside TMEM; 16 epilogue warps read every block's int32 tile
 // from TMEM (tcgen05.ld) and add (float)sumi * (d_w * d_x) to f32 registers in ascending
-// block order -- the oracle's order, so results are bit-identical to it.
+// block order -- the oracle's order, so results are bit-identical to it. The epilogue is the
+// bound (3 FP operations per output per block against one MMA per block): it converts the
+// int32 sums exactly without the conversion unit and multiplies f32 pairs (f32x2, each lane
+// rounded like the scalar operation); the accumulating adds are scalar.
 //
-// Roles (10 warps): warps 0-7 epilogue (warp w reads TMEM lanes 32*(w%4).. and token columns
-// 32*(w/4)..), warp 8 TMA producer, warp 9 TMEM allocator + MMA issuer (one elected lane).
+// Roles (18 warps): warps 0-15 epilogue (warp w reads TMEM lanes 32*(w%4).. and token columns
+// 16*(w/4)..), warp 16 TMA producer, warp 17 TMEM allocator + MMA issuer (one elected lane).
 // Shared-memory stages of 256 bytes of K (8 blocks): weights 2 x [128 x 128 B] and tokens
 // 2 x [64 x 128 B], 128-byte swizzled by TMA, plus the stage's fp16 scales. A stage is freed
 // when its MMAs have completed (tcgen05.commit) and the epilogue has used its scales. TMEM
@@ -31,12 +34,14 @@ constexpr int TC_BN = 64;             // tokens per CTA (MMA N)
 constexpr int TC_KS = 256;            // K bytes per stage (8 Q8_0 blocks)
 constexpr int TC_STAGES = 4;
 constexpr int TC_BUFS = 8;            // TMEM block accumulators (64 columns each)
-constexpr int TC_EPI_WARPS = 8;
+constexpr int TC_EPI_WARPS = 16;
+constexpr int TC_EW = TC_BN / (TC_EPI_WARPS / 4);  // tokens per epilogue warp
 constexpr int TC_THREADS = (TC_EPI_WARPS + 2) * 32;
 constexpr int TC_A_SUB = TC_BM * 128;  // bytes of one 128-byte-wide weight sub-tile
 constexpr int TC_B_SUB = TC_BN * 128;
 constexpr int TC_STAGE = 2 * TC_A_SUB + 2 * TC_B_SUB + TC_BM * 16 + TC_BN * 16;  // 52224
-constexpr int TC_SMEM = TC_STAGES * TC_STAGE + 1024 /*barriers*/ + 1024 /*alignment*/;
+constexpr int TC_SMEM = TC_STAGES * TC_STAGE + 1024 /*barriers*/ + TC_EPI_WARPS * 8 * TC_EW * 4 /*f32 token scales*/ +
+                        1024 /*alignment*/;
 
 struct TcBars {
     uint64_t full[TC_STAGES];
@@ -75,6 +80,27 @@ __host__ __device__ constexpr uint32_t tc_idesc() {
 // every wait in this kernel is legitimately microseconds long; 2 s means a lost copy or MMA
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, unsigned parity) {
     return mbar_wait_ns(bar, parity, 2000000000ull);
+}
+
+// f32 pair multiply, each lane rounded to nearest like __fmul_rn. The accumulation stays
+// scalar (__fadd_rn): an f32x2 multiply feeding an f32x2 add is contracted into an f32x2 FMA
+// by the code generator even with explicit .rn and -fmad=false, which would change the
+// rounding of acc + sumi * scale; a packed multiply feeding scalar adds measured bit-exact.
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+    float2 d;
+    asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+        " mul.rn.f32x2 rd, ra, rb;\n mov.b64 {%0, %1}, rd;\n}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+    float2 d;
+    asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+        " add.rn.f32x2 rd, ra, rb;\n mov.b64 {%0, %1}, rd;\n}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -194,12 +220,13 @@ q8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_constant_
         }
     } else {
         // ------------------------------ epilogue ------------------------------
-        const int q = warp & 3;       // TMEM lane quarter
-        const int h = warp >> 2;      // token half: columns 32h..32h+31
+        const int q = warp & 3;   // TMEM lane quarter: weight rows 32q .. 32q+31
+        const int h = warp >> 2;  // token slice: columns TC_EW*h .. +TC_EW-1
         const int row = q * 32 + lane;
-        float acc[32];
+        float* dxf = reinterpret_cast<float*>(sm + TC_STAGES * TC_STAGE + 1024) + warp * (8 * TC_EW);
+        float2 acc[TC_EW / 2];
 #pragma unroll
-        for (int c = 0; c < 32; c++) acc[c] = 0.0f;
+        for (int c = 0; c < TC_EW / 2; c++) acc[c] = make_float2(0.0f, 0.0f);
         for (int ks = 0; ks < nstages && ok; ks++) {
             const int s = ks % TC_STAGES;
             if (!__all_sync(0xffffffffu, tc_wait(&B.full[s], (unsigned)(ks / TC_STAGES) & 1u))) {
@@ -209,6 +236,12 @@ q8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_constant_
             }
             const uint16_t* sdw = reinterpret_cast<const uint16_t*>(sm + s * TC_STAGE + 2 * TC_A_SUB + 2 * TC_B_SUB);
             const uint16_t* sdx = sdw + TC_BM * 8;
+            // this warp's token scales of the stage as f32, [block][token]
+            for (int e = lane; e < 8 * TC_EW; e += 32) {
+                const int jj = e / TC_EW, tok = e % TC_EW;
+                dxf[e] = h2f(sdx[(h * TC_EW + tok) * 8 + jj]);
+            }
+            __syncwarp();
             for (int j = 0; j < 8; j++) {
                 const int g = ks * 8 + j;
                 const int buf = g % TC_BUFS;
@@ -218,26 +251,40 @@ q8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_constant_
                     break;
                 }
                 tc_fence_after();
-                uint32_t r[32];
-                const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * TC_BN + h * 32);
+                uint32_t r[TC_EW];
+                const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * TC_BN + h * TC_EW);
                 asm volatile(
-                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
+                    "[%16];"
                     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
                       "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
-                      "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
-                      "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
-                      "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                      "=r"(r[15])
                     : "r"(taddr));
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&B.tempty[buf]);  // the accumulator is in registers now
                 const float dw = h2f(sdw[row * 8 + j]);
+                const float2 dw2 = make_float2(dw, dw);
+                const float4* dx4 = reinterpret_cast<const float4*>(dxf + j * TC_EW);
 #pragma unroll
-                for (int c = 0; c < 32; c++) {
-                    const float sc = __fmul_rn(dw, h2f(sdx[(h * 32 + c) * 8 + j]));
-                    acc[c] = __fadd_rn(acc[c], __fmul_rn((float)(int)r[c], sc));
+                for (int c = 0; c < TC_EW / 4; c++) {
+                    const float4 x = dx4[c];
+                    // exact int -> float: |sumi| <= 32*127*127 < 2^22, so 1.5*2^23 + sumi is an
+                    // exactly representable float whose bit pattern is the integer sum
+                    const float2 s01 = add2_rn(make_float2(__int_as_float((int)r[4 * c] + 0x4B400000),
+                                                              __int_as_float((int)r[4 * c + 1] + 0x4B400000)),
+                                                  make_float2(-12582912.0f, -12582912.0f));
+                    const float2 s23 = add2_rn(make_float2(__int_as_float((int)r[4 * c + 2] + 0x4B400000),
+                                                              __int_as_float((int)r[4 * c + 3] + 0x4B400000)),
+                                                  make_float2(-12582912.0f, -12582912.0f));
+                    const float2 sc01 = mul2_rn(dw2, make_float2(x.x, x.y));
+                    const float2 sc23 = mul2_rn(dw2, make_float2(x.z, x.w));
+                    const float2 p01 = mul2_rn(s01, sc01), p23 = mul2_rn(s23, sc23);
+                    acc[2 * c].x = __fadd_rn(acc[2 * c].x, p01.x);
+                    acc[2 * c].y = __fadd_rn(acc[2 * c].y, p01.y);
+                    acc[2 * c + 1].x = __fadd_rn(acc[2 * c + 1].x, p23.x);
+                    acc[2 * c + 1].y = __fadd_rn(acc[2 * c + 1].y, p23.y);
                 }
             }
             __syncwarp();
@@ -247,11 +294,12 @@ q8_gemm_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_constant_
             const int n = n0 + row;
             if (n < p.N) {
 #pragma unroll
-                for (int c = 0; c < 32; c++) {
-                    const int m = m0 + h * 32 + c;
+                for (int c = 0; c < TC_EW; c++) {
+                    const int m = m0 + h * TC_EW + c;
+                    const float a = (c & 1) ? acc[c / 2].y : acc[c / 2].x;
                     if (m < p.M) {
                         const size_t o = (size_t)m * p.ldy + n;
-                        p.y[o] = p.resid ? __fadd_rn(p.resid[o], acc[c]) : acc[c];
+                        p.y[o] = p.resid ? __fadd_rn(p.resid[o], a) : a;
                     }
                 }
             }
