@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define LQ8_ABI_VERSION 1
+#define LQ8_ABI_VERSION 2
 
 typedef enum {
     LQ_OK = 0,
@@ -178,6 +178,28 @@ int lq_fill_bf16(lq_ctx* ctx, uint64_t seed, uint64_t tensor_id, int64_t offset,
                  double std_dev, uint16_t* out_dev);
 
 /* ---------------------------------------------------------------------------------------
+ * Mixture of experts (Qwen3-MoE sparse MLP). The reference has no MoE code (its architecture
+ * notes plan one); this follows the Qwen3-MoE sparse block so that a MoE checkpoint's layer
+ * is one call: router logits x.R^T (Q8_0), softmax, top_k experts by logit (ties -> lower
+ * expert index), weights renormalised over the top_k when norm_topk, expert SwiGLU on Q8_0
+ * weights, contributions added in ascending expert index.
+ * ------------------------------------------------------------------------------------- */
+typedef struct {
+    int64_t n_experts, inter, hidden;
+    lq_q8_tensor gate_up;   /* [n_experts * 2 * inter][hidden]: expert e's gate rows, then up rows */
+    lq_q8_tensor down;      /* [n_experts * hidden][inter] */
+} lq_moe_experts;
+
+/* out [rows][hidden] f32 = residual (may be NULL; may equal out) + sum_e w_e * expert_e(x),
+ * x given as Q8_0 rows (xq_dev [rows][hidden], xd_dev [rows][hidden/32], e.g. from lq_rmsnorm).
+ * ids_out / weights_out [rows][top_k] (selection order; device, may be NULL). Uses the
+ * context scratch. */
+int lq_moe_forward(lq_ctx* ctx, const lq_q8_tensor* router, const lq_moe_experts* experts,
+                   const int8_t* xq_dev, const uint16_t* xd_dev, int64_t rows, int64_t top_k,
+                   int norm_topk, float* out_dev, const float* residual_dev, int32_t* ids_out_dev,
+                   float* weights_out_dev);
+
+/* ---------------------------------------------------------------------------------------
  * Qwen3 model runner (Qwen3ForCausalLM, model.rs:273-372; generate.rs:611-661).
  * ------------------------------------------------------------------------------------- */
 typedef struct {
@@ -187,6 +209,11 @@ typedef struct {
     double theta;
     float init_std;     /* random-init weights ~ N(0, init_std) (seeded generator) */
     float norm_std;     /* 0 -> norm weights 1.0 */
+    /* Qwen3-MoE: n_experts > 0 replaces every layer's MLP by the sparse block (lq_moe_forward)
+     * with top_k experts of moe_inter; inter is then unused. */
+    int64_t n_experts, top_k, moe_inter;
+    int32_t norm_topk;  /* renormalise the top-k routing weights */
+    int32_t pad_;
 } lq_qwen3_config;
 
 /* Builds the model with seeded random-init weights, all linears Q8_0 (Qwen3ForCausalLM::load,
@@ -221,6 +248,9 @@ int lq_qwen3_linear(lq_model* model, int64_t layer, int kind, lq_q8_tensor* out)
 int lq_qwen3_weight_bytes(lq_model* model, int64_t* bytes);
 /* Kernel launches in one decode step (kernel nodes of the captured CUDA graph; 0 before the
  * first decode step or lq_qwen3_set_batch). */
+/* MoE weights of a layer: kind 10 router (expert ignored), 11 gate, 12 up, 13 down of
+ * `expert` (views into the stacked expert tensors). */
+int lq_qwen3_expert(lq_model* model, int64_t layer, int64_t expert, int kind, lq_q8_tensor* out);
 int lq_qwen3_graph_kernels(lq_model* model, int64_t* n);
 
 #ifdef __cplusplus

@@ -42,7 +42,8 @@ class Qwen3Config(C.Structure):
         ("n_kv_heads", C.c_int64), ("head_dim", C.c_int64), ("inter", C.c_int64),
         ("vocab", C.c_int64), ("max_pos", C.c_int64), ("tied", C.c_int32),
         ("eps", C.c_float), ("theta", C.c_double), ("init_std", C.c_float),
-        ("norm_std", C.c_float),
+        ("norm_std", C.c_float), ("n_experts", C.c_int64), ("top_k", C.c_int64),
+        ("moe_inter", C.c_int64), ("norm_topk", C.c_int32), ("pad_", C.c_int32),
     ]
 
 
@@ -99,6 +100,10 @@ def _declare(L):
     L.orc_qwen3_embed.argtypes = [_P]
     L.orc_qwen3_linear.restype = _I64
     L.orc_qwen3_linear.argtypes = [_P, _I64, C.c_int, C.POINTER(_P), C.POINTER(_P), C.POINTER(_I64)]
+    L.orc_qwen3_expert.restype = _I64
+    L.orc_qwen3_expert.argtypes = [_P, _I64, _I64, C.c_int, C.POINTER(_P), C.POINTER(_P), C.POINTER(_I64)]
+    L.orc_moe_forward.argtypes = [_P, _I64, _I64, _I64, _I64, _I64, C.c_int, _P, _P, _P, _P, _P, _P, _P, _P,
+                                  _P, _P, _P]
     L.orc_set_threads.argtypes = [C.c_int]
     L.orc_get_threads.restype = C.c_int
 
@@ -274,7 +279,7 @@ def make_config(**kw) -> Qwen3Config:
     c = Qwen3Config()
     defaults = dict(hidden=1024, layers=28, n_heads=16, n_kv_heads=8, head_dim=128, inter=3072,
                     vocab=VOCAB_QWEN3, max_pos=40960, tied=1, eps=1e-6, theta=1e6,
-                    init_std=0.02, norm_std=0.0)
+                    init_std=0.02, norm_std=0.0, n_experts=0, top_k=0, moe_inter=0, norm_topk=0)
     defaults.update(kw)
     for k, v in defaults.items():
         setattr(c, k, v)
@@ -320,6 +325,16 @@ class Qwen3Model:
         dd = np.ctypeslib.as_array(C.cast(d, C.POINTER(C.c_uint16)), shape=(n, k.value // QK)).copy()
         return q, dd
 
+    def expert(self, layer: int, expert: int, kind: int):
+        """(qs, d) copies of a MoE weight: kind 10 router, 11 gate, 12 up, 13 down of `expert`."""
+        qs, d, k = C.c_void_p(), C.c_void_p(), C.c_int64()
+        n = lib().orc_qwen3_expert(self._h, layer, expert, kind, C.byref(qs), C.byref(d), C.byref(k))
+        if n < 0:
+            raise IndexError((layer, expert, kind))
+        q = np.ctypeslib.as_array(C.cast(qs, C.POINTER(C.c_int8)), shape=(n, k.value)).copy()
+        dd = np.ctypeslib.as_array(C.cast(d, C.POINTER(C.c_uint16)), shape=(n, k.value // QK)).copy()
+        return q, dd
+
     def generate(self, prompt, new_tokens: int):
         prompt = np.ascontiguousarray(prompt, dtype=np.int32)
         out = np.empty(new_tokens, dtype=np.int32)
@@ -328,3 +343,34 @@ class Qwen3Model:
         if rc:
             raise ValueError("orc_qwen3_generate failed")
         return out, logits
+
+
+# ---------------------------------------------------------------------------- MoE
+def moe_forward(xn_bf16: np.ndarray, router, gate, up, down, top_k: int, norm_topk: bool = True):
+    """Mixture-of-experts MLP of one layer (orc_moe_forward). xn_bf16 [rows][H] uint16;
+    router = (qs [E][H], d); gate/up/down = lists of per-expert (qs, d). Returns
+    (out [rows][H] f32, ids [rows][top_k] int32, weights [rows][top_k] f32)."""
+    xn = np.ascontiguousarray(xn_bf16, dtype=np.uint16)
+    rows, H = xn.shape
+    E = router[0].shape[0]
+    inter = gate[0][0].shape[0]
+    keep = []
+
+    def ptrs(lst, i):
+        arr = (C.c_void_p * E)()
+        for e in range(E):
+            a = np.ascontiguousarray(lst[e][i])
+            keep.append(a)
+            arr[e] = a.ctypes.data
+        keep.append(arr)
+        return C.cast(arr, C.c_void_p)
+
+    out = np.empty((rows, H), np.float32)
+    ids = np.empty((rows, top_k), np.int32)
+    w = np.empty((rows, top_k), np.float32)
+    rq = np.ascontiguousarray(router[0])
+    rd = np.ascontiguousarray(router[1])
+    lib().orc_moe_forward(_p(xn), rows, H, E, top_k, inter, int(norm_topk), _p(rq), _p(rd),
+                          ptrs(gate, 0), ptrs(gate, 1), ptrs(up, 0), ptrs(up, 1), ptrs(down, 0),
+                          ptrs(down, 1), _p(out), _p(ids), _p(w))
+    return out, ids, w

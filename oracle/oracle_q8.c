@@ -364,8 +364,10 @@ void orc_attend_row(const float* q, const float* k, const float* v, int64_t ctx,
 /* ====================================================================================== */
 
 /* Tensor ids of the seeded generator; the CUDA library uses the same numbering. */
-enum { K_Q = 0, K_K, K_V, K_O, K_GATE, K_UP, K_DOWN, K_QNORM, K_KNORM, K_INNORM, K_POSTNORM };
+enum { K_Q = 0, K_K, K_V, K_O, K_GATE, K_UP, K_DOWN, K_QNORM, K_KNORM, K_INNORM, K_POSTNORM, K_ROUTER };
 #define TID_LAYER(l, kind) (((uint64_t)(l) << 8) | (uint64_t)(kind))
+/* expert weights: kind 0 gate, 1 up, 2 down */
+#define TID_EXPERT(l, e, kind) ((1ull << 40) | ((uint64_t)(l) << 20) | ((uint64_t)(e) << 4) | (uint64_t)(kind))
 #define TID_EMBED 0x7FFF0001ull
 #define TID_LMHEAD 0x7FFF0002ull
 #define TID_FINALNORM 0x7FFF0003ull
@@ -375,6 +377,8 @@ typedef struct { int64_t n, k; int8_t* qs; uint16_t* d; } qw_t;
 typedef struct {
     qw_t q, k, v, o, gate, up, down;
     uint16_t *q_norm, *k_norm, *in_norm, *post_norm;
+    qw_t router;             /* MoE: [E][H] */
+    qw_t *eg, *eu, *ed;      /* MoE: per-expert gate [moe_inter][H], up, down [H][moe_inter] */
 } layer_t;
 
 struct orc_model {
@@ -440,9 +444,22 @@ orc_model* orc_qwen3_create(const orc_qwen3_config* cfg, uint64_t seed, int64_t 
         make_linear(&ly->k, seed, TID_LAYER(l, K_K), c->n_kv_heads * D, H, sc);
         make_linear(&ly->v, seed, TID_LAYER(l, K_V), c->n_kv_heads * D, H, sc);
         make_linear(&ly->o, seed, TID_LAYER(l, K_O), H, c->n_heads * D, sc);
-        make_linear(&ly->gate, seed, TID_LAYER(l, K_GATE), c->inter, H, sc);
-        make_linear(&ly->up, seed, TID_LAYER(l, K_UP), c->inter, H, sc);
-        make_linear(&ly->down, seed, TID_LAYER(l, K_DOWN), H, c->inter, sc);
+        if (c->n_experts > 0) {
+            int64_t E = c->n_experts, I = c->moe_inter;
+            make_linear(&ly->router, seed, TID_LAYER(l, K_ROUTER), E, H, sc);
+            ly->eg = (qw_t*)calloc((size_t)E, sizeof(qw_t));
+            ly->eu = (qw_t*)calloc((size_t)E, sizeof(qw_t));
+            ly->ed = (qw_t*)calloc((size_t)E, sizeof(qw_t));
+            for (int64_t e = 0; e < E; e++) {
+                make_linear(&ly->eg[e], seed, TID_EXPERT(l, e, 0), I, H, sc);
+                make_linear(&ly->eu[e], seed, TID_EXPERT(l, e, 1), I, H, sc);
+                make_linear(&ly->ed[e], seed, TID_EXPERT(l, e, 2), H, I, sc);
+            }
+        } else {
+            make_linear(&ly->gate, seed, TID_LAYER(l, K_GATE), c->inter, H, sc);
+            make_linear(&ly->up, seed, TID_LAYER(l, K_UP), c->inter, H, sc);
+            make_linear(&ly->down, seed, TID_LAYER(l, K_DOWN), H, c->inter, sc);
+        }
         ly->q_norm = make_norm(c, seed, TID_LAYER(l, K_QNORM), D);
         ly->k_norm = make_norm(c, seed, TID_LAYER(l, K_KNORM), D);
         ly->in_norm = make_norm(c, seed, TID_LAYER(l, K_INNORM), H);
@@ -467,6 +484,13 @@ void orc_qwen3_destroy(orc_model* m) {
         free_lin(&ly->q); free_lin(&ly->k); free_lin(&ly->v); free_lin(&ly->o);
         free_lin(&ly->gate); free_lin(&ly->up); free_lin(&ly->down);
         free(ly->q_norm); free(ly->k_norm); free(ly->in_norm); free(ly->post_norm);
+        if (ly->eg) {
+            for (int64_t e = 0; e < m->c.n_experts; e++) {
+                free_lin(&ly->eg[e]); free_lin(&ly->eu[e]); free_lin(&ly->ed[e]);
+            }
+            free(ly->eg); free(ly->eu); free(ly->ed);
+            free_lin(&ly->router);
+        }
     }
     free(m->L); free(m->embed); free(m->final_norm); free_lin(&m->lm_head);
     free(m->kc); free(m->vc); free(m->cos_t); free(m->sin_t);
@@ -492,9 +516,78 @@ int64_t orc_qwen3_linear(const orc_model* m, int64_t layer, int kind, const int8
         const qw_t* all[7] = {&ly->q, &ly->k, &ly->v, &ly->o, &ly->gate, &ly->up, &ly->down};
         if (kind >= 0 && kind < 7) w = all[kind];
     }
-    if (!w) return -1;
+    if (!w || !w->qs) return -1;
     *qs = w->qs; *d = w->d; *k = w->k;
     return w->n;
+}
+
+int64_t orc_qwen3_expert(const orc_model* m, int64_t layer, int64_t expert, int kind, const int8_t** qs,
+                         const uint16_t** d, int64_t* k) {
+    if (layer < 0 || layer >= m->nl || m->c.n_experts <= 0) return -1;
+    const layer_t* ly = &m->L[layer];
+    const qw_t* w = NULL;
+    if (kind == 10) w = &ly->router;
+    else if (expert >= 0 && expert < m->c.n_experts) {
+        if (kind == 11) w = &ly->eg[expert];
+        else if (kind == 12) w = &ly->eu[expert];
+        else if (kind == 13) w = &ly->ed[expert];
+    }
+    if (!w || !w->qs) return -1;
+    *qs = w->qs; *d = w->d; *k = w->k;
+    return w->n;
+}
+
+void orc_moe_forward(const uint16_t* xn, int64_t rows, int64_t H, int64_t E, int64_t top_k, int64_t inter,
+                     int norm_topk, const int8_t* rq, const uint16_t* rd, const int8_t* const* gq,
+                     const uint16_t* const* gd, const int8_t* const* uq, const uint16_t* const* ud,
+                     const int8_t* const* dq, const uint16_t* const* dd, float* out, int32_t* ids,
+                     float* weights) {
+    float* logits = (float*)malloc(sizeof(float) * (size_t)(rows * E));
+    orc_q8_0_linear_bf16(xn, rows, H, rq, rd, E, logits);
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int64_t t = 0; t < rows; t++) {
+        const float* lg = logits + t * E;
+        float* p = (float*)malloc(sizeof(float) * (size_t)E);
+        int32_t* sel = (int32_t*)malloc(sizeof(int32_t) * (size_t)top_k);
+        float* w = (float*)malloc(sizeof(float) * (size_t)top_k);
+        char* used = (char*)calloc((size_t)E, 1);
+        float* g = (float*)malloc(sizeof(float) * (size_t)inter);
+        float* u = (float*)malloc(sizeof(float) * (size_t)inter);
+        float* y = (float*)malloc(sizeof(float) * (size_t)H);
+        float* acc = (float*)calloc((size_t)H, sizeof(float));
+        memcpy(p, lg, sizeof(float) * (size_t)E);
+        orc_softmax(p, E);
+        /* top-k by logit; on equal logits the lower expert index first */
+        for (int64_t j = 0; j < top_k; j++) {
+            int64_t best = -1;
+            for (int64_t e = 0; e < E; e++)
+                if (!used[e] && (best < 0 || lg[e] > lg[best])) best = e;
+            used[best] = 1;
+            sel[j] = (int32_t)best;
+            w[j] = p[best];
+        }
+        if (norm_topk) {
+            float s = 0.0f;
+            for (int64_t j = 0; j < top_k; j++) s = s + w[j];
+            for (int64_t j = 0; j < top_k; j++) w[j] = w[j] / s;
+        }
+        if (ids) for (int64_t j = 0; j < top_k; j++) ids[t * top_k + j] = sel[j];
+        if (weights) for (int64_t j = 0; j < top_k; j++) weights[t * top_k + j] = w[j];
+        /* experts in ascending index (the index_add order of the sparse block) */
+        for (int64_t e = 0; e < E; e++) {
+            if (!used[e]) continue;
+            float we = 0.0f;
+            for (int64_t j = 0; j < top_k; j++) if (sel[j] == e) we = w[j];
+            orc_q8_0_linear_bf16(xn + t * H, 1, H, gq[e], gd[e], inter, g);
+            orc_q8_0_linear_bf16(xn + t * H, 1, H, uq[e], ud[e], inter, u);
+            for (int64_t i = 0; i < inter; i++) { float s = orc_silu(g[i]); g[i] = s * u[i]; }
+            orc_q8_0_linear_f32(g, 1, inter, dq[e], dd[e], H, y);
+            for (int64_t i = 0; i < H; i++) acc[i] = acc[i] + we * y[i];
+        }
+        memcpy(out + t * H, acc, sizeof(float) * (size_t)H);
+        free(p); free(sel); free(w); free(used); free(g); free(u); free(y); free(acc);
+    }
+    free(logits);
 }
 
 static void lin_bf16(const qw_t* w, const uint16_t* x, int64_t rows, float* y) {
@@ -561,6 +654,26 @@ static void layer_forward(orc_model* m, int64_t li, float* x, int64_t L, int64_t
     for (int64_t i = 0; i < L * H; i++) x[i] = x[i] + o[i];
     /* MLP */
     orc_rmsnorm_f32(x, L, H, ly->post_norm, c->eps, xn);
+    if (c->n_experts > 0) {
+        int64_t E = c->n_experts;
+        const int8_t** gq = (const int8_t**)malloc(sizeof(void*) * (size_t)E * 6);
+        const uint16_t** gd = (const uint16_t**)(gq + E);
+        const int8_t** uq = (const int8_t**)(gq + 2 * E);
+        const uint16_t** ud = (const uint16_t**)(gq + 3 * E);
+        const int8_t** dq = (const int8_t**)(gq + 4 * E);
+        const uint16_t** dd = (const uint16_t**)(gq + 5 * E);
+        for (int64_t e = 0; e < E; e++) {
+            gq[e] = ly->eg[e].qs; gd[e] = ly->eg[e].d;
+            uq[e] = ly->eu[e].qs; ud[e] = ly->eu[e].d;
+            dq[e] = ly->ed[e].qs; dd[e] = ly->ed[e].d;
+        }
+        orc_moe_forward(xn, L, H, E, c->top_k, c->moe_inter, c->norm_topk, ly->router.qs, ly->router.d,
+                        gq, gd, uq, ud, dq, dd, o, NULL, NULL);
+        free((void*)gq);
+        for (int64_t i = 0; i < L * H; i++) x[i] = x[i] + o[i];
+        free(xn); free(q); free(k); free(v); free(qh); free(kh); free(att); free(o);
+        return;
+    }
     float* g = (float*)malloc(sizeof(float) * (size_t)(L * I));
     float* u = (float*)malloc(sizeof(float) * (size_t)(L * I));
     lin_bf16(&ly->gate, xn, L, g);

@@ -89,6 +89,11 @@ typedef struct {
     double theta;
     float init_std;         /* weights ~ N(0, init_std) (integer-exact generator) */
     float norm_std;         /* 0 -> norm weights 1.0; else 1 + N(0,norm_std) */
+    /* Mixture of experts (Qwen3-MoE); n_experts == 0 -> dense MLP. Not in the reference:
+     * the spec is the Qwen3-MoE sparse block restated in orc_moe_forward below. */
+    int64_t n_experts, top_k, moe_inter;
+    int32_t norm_topk;      /* renormalise the top-k routing weights to sum 1 */
+    int32_t pad_;
 } orc_qwen3_config;
 
 typedef struct orc_model orc_model;
@@ -102,12 +107,29 @@ int orc_qwen3_forward(orc_model* m, const int32_t* ids, int64_t L, int64_t offse
 /* generate() restricted to greedy decoding (generate.rs:611-661) */
 int orc_qwen3_generate(orc_model* m, const int32_t* prompt, int64_t L, int64_t new_tokens,
                        int32_t* out_tokens, float* last_logits);
+/* Mixture-of-experts MLP of one layer (Qwen3-MoE convention; the reference has no MoE code):
+ * xn [rows][H] bf16 (post_attention_layernorm output), router R [E][H] Q8_0;
+ *   logits[e] = Q8_0 dot (the Linear rule, blocks ascending);
+ *   p = softmax(logits) in f32 (max, exp, sum ascending, divide);
+ *   the top_k experts by logit (ties -> lower expert index), in that order;
+ *   w_j = p[e_j], and with norm_topk w_j = w_j / (w_0 + ... + w_{k-1}) (sum in selection order);
+ *   expert e: h = silu(gate_e . xn) * (up_e . xn) (f32), y_e = down_e . h (h quantized per row);
+ *   out[t] = sum over the selected experts in ascending expert index of w_e * y_e[t] (f32).
+ * Writes out [rows][H]; ids/weights [rows][top_k] (selection order) when not NULL. */
+void orc_moe_forward(const uint16_t* xn, int64_t rows, int64_t H, int64_t E, int64_t top_k, int64_t inter,
+                     int norm_topk, const int8_t* rq, const uint16_t* rd, const int8_t* const* gq,
+                     const uint16_t* const* gd, const int8_t* const* uq, const uint16_t* const* ud,
+                     const int8_t* const* dq, const uint16_t* const* dd, float* out, int32_t* ids,
+                     float* weights);
 /* Accessors used by the tests to hand the identical weights to the GPU */
 int64_t orc_qwen3_layers(const orc_model* m);
 const uint16_t* orc_qwen3_embed(const orc_model* m);      /* [vocab][hidden] bf16 */
 /* Q8_0 weight of a layer's linear (kind 0 q,1 k,2 v,3 o,4 gate,5 up,6 down; layer -1 kind 7
  * = lm_head): returns rows, fills *qs / *d with the oracle's buffers. -1 if out of range. */
 int64_t orc_qwen3_linear(const orc_model* m, int64_t layer, int kind, const int8_t** qs,
+                         const uint16_t** d, int64_t* k);
+/* MoE weights: kind 10 router (expert ignored), 11 expert gate, 12 expert up, 13 expert down. */
+int64_t orc_qwen3_expert(const orc_model* m, int64_t layer, int64_t expert, int kind, const int8_t** qs,
                          const uint16_t** d, int64_t* k);
 void orc_set_threads(int n);
 int orc_get_threads(void);

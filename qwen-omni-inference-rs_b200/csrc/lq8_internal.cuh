@@ -220,6 +220,13 @@ bool attention_prefill_supported(int64_t L, int64_t Hq, int64_t Hkv);
 int launch_attention_prefill(lq_ctx* ctx, const float* q, const float* kc, const float* vc, int64_t B, int64_t Hq,
                              int64_t Hkv, int64_t L, int64_t pos0, const int32_t* pos0_dev, int64_t ctx_max,
                              float* out, int8_t* xq, uint16_t* xd);
+// Qwen3-MoE sparse MLP (router, top-k, grouped expert GEMVs, combine); scratch from
+// moe_scratch_bytes for `rows` tokens
+size_t moe_scratch_bytes(int64_t rows, int64_t E, int64_t top_k, int64_t H, int64_t inter);
+int launch_moe(lq_ctx* ctx, const lq_q8_tensor* router, const lq_q8_tensor* gate_up, const lq_q8_tensor* down,
+               int64_t E, int64_t inter, int64_t top_k, int norm_topk, const int8_t* xq, const uint16_t* xd,
+               int64_t rows, int64_t H, float* out, const float* resid, void* scratch, int32_t* ids_out,
+               float* w_out);
 size_t attention_scratch_bytes(int64_t rows, int64_t n_heads, int64_t ctx_max, int64_t head_dim);
 int attention_max_ctx();
 // scratch starts with per-(row, kv head) counters that must be zero before the first launch;

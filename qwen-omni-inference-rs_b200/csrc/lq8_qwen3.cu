@@ -15,8 +15,12 @@
 
 namespace {
 
-enum { K_Q = 0, K_K, K_V, K_O, K_GATE, K_UP, K_DOWN, K_QNORM, K_KNORM, K_INNORM, K_POSTNORM };
+enum { K_Q = 0, K_K, K_V, K_O, K_GATE, K_UP, K_DOWN, K_QNORM, K_KNORM, K_INNORM, K_POSTNORM, K_ROUTER };
 inline uint64_t tid_layer(int64_t l, int kind) { return ((uint64_t)l << 8) | (uint64_t)kind; }
+// expert weights: kind 0 gate, 1 up, 2 down
+inline uint64_t tid_expert(int64_t l, int64_t e, int kind) {
+    return (1ull << 40) | ((uint64_t)l << 20) | ((uint64_t)e << 4) | (uint64_t)kind;
+}
 constexpr uint64_t TID_EMBED = 0x7FFF0001ull;
 constexpr uint64_t TID_LMHEAD = 0x7FFF0002ull;
 constexpr uint64_t TID_FINALNORM = 0x7FFF0003ull;
@@ -24,6 +28,9 @@ constexpr uint64_t TID_FINALNORM = 0x7FFF0003ull;
 struct Layer {
     lq_q8_tensor qkv{}, o{}, gate_up{}, down{};
     uint16_t *q_norm = nullptr, *k_norm = nullptr, *in_norm = nullptr, *post_norm = nullptr;
+    // MoE: router [E][H], experts stacked: gate/up [E*2I][H] (per expert gate rows then up
+    // rows), down [E*H][I]
+    lq_q8_tensor router{}, moe_gate_up{}, moe_down{};
 };
 
 }  // namespace
@@ -51,6 +58,8 @@ struct lq_model {
     float* logits = nullptr;   // [max_batch][V]
     void* att_scratch = nullptr;
     size_t att_scratch_bytes = 0;
+    void* moe_scratch = nullptr;         // MoE layers: route/dispatch/expert buffers for rows_cap
+    bool moe = false;
     unsigned long long* keys = nullptr;  // argmax keys [max_batch]
     int32_t* tokens = nullptr;           // [rows_cap]
     int32_t* pos_dev = nullptr;
@@ -111,6 +120,16 @@ int gen_linear(lq_model* m, uint16_t* tmp, size_t tmp_elems, uint64_t seed, uint
     return LQ_OK;
 }
 
+// post_attention_layernorm -> Q8_0, sparse MoE MLP, residual (in place on m->x)
+int moe_mlp(lq_model* m, const Layer& ly, int64_t rows) {
+    const lq_qwen3_config& c = m->c;
+    int rc = lq::launch_rmsnorm(m->ctx, m->x, LQ_DTYPE_F32, rows, c.hidden, ly.post_norm, c.eps, nullptr, m->xq,
+                                m->xd);
+    if (rc) return rc;
+    return lq::launch_moe(m->ctx, &ly.router, &ly.moe_gate_up, &ly.moe_down, c.n_experts, c.moe_inter, c.top_k,
+                          c.norm_topk, m->xq, m->xd, rows, c.hidden, m->x, m->x, m->moe_scratch, nullptr, nullptr);
+}
+
 void destroy_graph(lq_model* m) {
     if (m->exec) cudaGraphExecDestroy(m->exec);
     m->exec = nullptr;
@@ -140,6 +159,10 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
             RC(lq::launch_attention_decode_fused(ctx, m->qkv, ly.q_norm, ly.k_norm, c.eps, m->cos_t, m->sin_t, kc, vc,
                                                  B, Hq, Hkv, pos_dev, m->ctx_max, m->xq, m->xd, m->att_scratch));
             RC(lq::launch_gemv_stream(ctx, &ly.o, m->xq, m->xd, B, m->x, m->x, H, nullptr));
+            if (m->moe) {
+                RC(moe_mlp(m, ly, B));
+                continue;
+            }
             RC(lq::launch_gemv_norm_swiglu(ctx, &ly.gate_up, m->x, ly.post_norm, c.eps, B, m->gu, I));
             RC(lq::launch_gemv_quant(ctx, &ly.down, m->gu, B, m->x, m->x, H));
         }
@@ -173,6 +196,10 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
         }
         // o_proj + residual (transformer.rs:194)
         RC(lq::launch_q8_matmul(ctx, &ly.o, m->xq, m->xd, rows, m->x, m->x, H, nullptr));
+        if (m->moe) {
+            RC(moe_mlp(m, ly, rows));
+            continue;
+        }
         // post_attention_layernorm -> Q8_0, gate/up, silu*up -> Q8_0, down + residual
         RC(lq::launch_rmsnorm(ctx, m->x, LQ_DTYPE_F32, rows, H, ly.post_norm, c.eps, nullptr, m->xq, m->xd));
         RC(lq::launch_q8_matmul(ctx, &ly.gate_up, m->xq, m->xd, rows, m->gu, nullptr, 2 * I, nullptr));
@@ -243,8 +270,12 @@ int lq_qwen3_create(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int6
     *out = nullptr;
     const lq_qwen3_config& c = *cfg;
     LQ_REQUIRE(ctx, c.head_dim == 128, "lq_qwen3_create: head_dim must be 128");
-    LQ_REQUIRE(ctx, c.hidden > 0 && c.hidden % 32 == 0 && c.inter % 32 == 0 && c.inter > 0,
+    const bool moe = c.n_experts > 0;
+    LQ_REQUIRE(ctx, c.hidden > 0 && c.hidden % 32 == 0 && (moe || (c.inter % 32 == 0 && c.inter > 0)),
                "lq_qwen3_create: hidden and intermediate sizes must be multiples of 32");
+    LQ_REQUIRE(ctx, !moe || (c.top_k > 0 && c.top_k <= 16 && c.top_k <= c.n_experts && c.n_experts <= 512 &&
+                             c.moe_inter > 0 && c.moe_inter % 32 == 0 && c.hidden <= 16384),
+               "lq_qwen3_create: MoE needs 0 < top_k <= min(16, n_experts), n_experts <= 512, moe_inter %% 32 == 0");
     LQ_REQUIRE(ctx, c.n_heads > 0 && c.n_kv_heads > 0 && c.n_heads % c.n_kv_heads == 0 &&
                         c.n_heads / c.n_kv_heads <= 8,
                "lq_qwen3_create: need n_heads %% n_kv_heads == 0 and at most 8 q heads per kv head");
@@ -258,13 +289,17 @@ int lq_qwen3_create(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int6
     m->c = c;
     m->max_batch = max_batch;
     m->ctx_max = ctx_max;
-    const int64_t H = c.hidden, D = c.head_dim, Hq = c.n_heads, Hkv = c.n_kv_heads, I = c.inter, V = c.vocab;
+    m->moe = moe;
+    const int64_t H = c.hidden, D = c.head_dim, Hq = c.n_heads, Hkv = c.n_kv_heads, V = c.vocab;
+    const int64_t I = moe ? c.moe_inter : c.inter, E = moe ? c.n_experts : 0;
     m->Nq = Hq * D;
     m->Nk = Hkv * D;
     m->Nqkv = m->Nq + 2 * m->Nk;
     m->Hqd = Hq * D;
     // rows per forward pass: whole sequences, at most 8192 rows (or one sequence)
-    m->rows_cap = std::max<int64_t>(max_batch, std::min<int64_t>(max_batch * ctx_max, std::max<int64_t>(8192, ctx_max)));
+    // (MoE: 2048, which bounds the per-pair expert outputs rows * top_k * hidden)
+    const int64_t pass_rows = moe ? 2048 : 8192;
+    m->rows_cap = std::max<int64_t>(max_batch, std::min<int64_t>(max_batch * ctx_max, std::max<int64_t>(pass_rows, ctx_max)));
     int rc = LQ_OK;
     auto fail = [&](int code) { lq_qwen3_destroy(m); return code; };
 #define RC(expr) do { rc = (expr); if (rc) return fail(rc); } while (0)
@@ -273,8 +308,14 @@ int lq_qwen3_create(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int6
     for (auto& ly : m->layers) {
         RC(alloc_q8(m, &ly.qkv, m->Nqkv, H));
         RC(alloc_q8(m, &ly.o, H, m->Hqd));
-        RC(alloc_q8(m, &ly.gate_up, 2 * I, H));
-        RC(alloc_q8(m, &ly.down, H, I));
+        if (moe) {
+            RC(alloc_q8(m, &ly.router, E, H));
+            RC(alloc_q8(m, &ly.moe_gate_up, E * 2 * I, H));
+            RC(alloc_q8(m, &ly.moe_down, E * H, I));
+        } else {
+            RC(alloc_q8(m, &ly.gate_up, 2 * I, H));
+            RC(alloc_q8(m, &ly.down, H, I));
+        }
         RC(dalloc_t(m, &ly.q_norm, (size_t)D));
         RC(dalloc_t(m, &ly.k_norm, (size_t)D));
         RC(dalloc_t(m, &ly.in_norm, (size_t)H));
@@ -294,9 +335,18 @@ int lq_qwen3_create(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int6
         RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_K), ly.qkv, m->Nq, m->Nk));
         RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_V), ly.qkv, m->Nq + m->Nk, m->Nk));
         RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_O), ly.o, 0, H));
-        RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_GATE), ly.gate_up, 0, I));
-        RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_UP), ly.gate_up, I, I));
-        RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_DOWN), ly.down, 0, H));
+        if (moe) {
+            RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_ROUTER), ly.router, 0, E));
+            for (int64_t e = 0; e < E; e++) {
+                RC(gen_linear(m, tmp, tmp_elems, seed, tid_expert(l, e, 0), ly.moe_gate_up, e * 2 * I, I));
+                RC(gen_linear(m, tmp, tmp_elems, seed, tid_expert(l, e, 1), ly.moe_gate_up, e * 2 * I + I, I));
+                RC(gen_linear(m, tmp, tmp_elems, seed, tid_expert(l, e, 2), ly.moe_down, e * H, H));
+            }
+        } else {
+            RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_GATE), ly.gate_up, 0, I));
+            RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_UP), ly.gate_up, I, I));
+            RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_DOWN), ly.down, 0, H));
+        }
         RC(lq::launch_fill_norm(ctx, seed, tid_layer(l, K_QNORM), D, c.norm_std, ly.q_norm));
         RC(lq::launch_fill_norm(ctx, seed, tid_layer(l, K_KNORM), D, c.norm_std, ly.k_norm));
         RC(lq::launch_fill_norm(ctx, seed, tid_layer(l, K_INNORM), H, c.norm_std, ly.in_norm));
@@ -334,6 +384,7 @@ int lq_qwen3_create(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int6
     int64_t att_rows = std::max<int64_t>(max_batch, std::min<int64_t>(R, ctx_max));
     m->att_scratch_bytes = lq::attention_scratch_bytes(att_rows, Hq, ctx_max, D);
     RC(dalloc(m, &m->att_scratch, m->att_scratch_bytes));
+    if (moe) RC(dalloc(m, &m->moe_scratch, lq::moe_scratch_bytes(R, E, c.top_k, H, I)));
     LQ_CUDA(ctx, cudaMemsetAsync(m->att_scratch, 0, m->att_scratch_bytes, ctx->stream));  // chunk counters
     LQ_CUDA(ctx, cudaMemsetAsync(m->keys, 0, (size_t)max_batch * 8, ctx->stream));
     LQ_CUDA(ctx, cudaMemsetAsync(m->pos_dev, 0, 4, ctx->stream));
@@ -345,7 +396,7 @@ int lq_qwen3_create(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int6
         // the fused decode path needs every matmul K on the streaming GEMV (K % 256 == 0,
         // 4 tokens of activations in shared memory); LQ_UNFUSED=1 forces the separate kernels
         bool ok = getenv("LQ_UNFUSED") == nullptr;
-        for (int64_t k : {H, m->Hqd, I})
+        for (int64_t k : {H, m->Hqd, moe ? H : I})
             ok = ok && lq::gemv_stream_supported(k) && lq::gemv_stream_smem(4, k) <= 227 * 1024;
         m->fused_decode = ok;
     }
@@ -473,6 +524,8 @@ int lq_qwen3_linear(lq_model* m, int64_t layer, int kind, lq_q8_tensor* out) {
         return LQ_OK;
     }
     LQ_REQUIRE(ctx, layer < (int64_t)m->layers.size(), "lq_qwen3_linear: layer out of range");
+    LQ_REQUIRE(ctx, !m->moe || (kind != K_GATE && kind != K_UP && kind != K_DOWN && kind != 9),
+               "lq_qwen3_linear: a MoE model has no dense MLP (use lq_qwen3_expert)");
     const Layer& ly = m->layers[(size_t)layer];
     const int64_t I = m->c.inter;
     switch (kind) {
@@ -490,6 +543,27 @@ int lq_qwen3_linear(lq_model* m, int64_t layer, int kind, lq_q8_tensor* out) {
     return LQ_OK;
 }
 
+int lq_qwen3_expert(lq_model* m, int64_t layer, int64_t expert, int kind, lq_q8_tensor* out) {
+    if (!m || !out) return LQ_ERR_INVALID_ARG;
+    lq_ctx* ctx = m->ctx;
+    LQ_REQUIRE(ctx, m->moe, "lq_qwen3_expert: not a MoE model");
+    LQ_REQUIRE(ctx, layer >= 0 && layer < (int64_t)m->layers.size(), "lq_qwen3_expert: layer out of range");
+    const Layer& ly = m->layers[(size_t)layer];
+    const int64_t I = m->c.moe_inter, H = m->c.hidden;
+    if (kind == 10) {
+        *out = ly.router;
+        return LQ_OK;
+    }
+    LQ_REQUIRE(ctx, expert >= 0 && expert < m->c.n_experts, "lq_qwen3_expert: expert out of range");
+    switch (kind) {
+        case 11: *out = rows_view(ly.moe_gate_up, expert * 2 * I, I); break;
+        case 12: *out = rows_view(ly.moe_gate_up, expert * 2 * I + I, I); break;
+        case 13: *out = rows_view(ly.moe_down, expert * H, H); break;
+        default: return lq::set_error(ctx, LQ_ERR_INVALID_ARG, "lq_qwen3_expert: kind %d", kind);
+    }
+    return LQ_OK;
+}
+
 int lq_qwen3_graph_kernels(lq_model* m, int64_t* n) {
     if (!m || !n) return LQ_ERR_INVALID_ARG;
     *n = m->graph_kernels;
@@ -500,7 +574,9 @@ int lq_qwen3_weight_bytes(lq_model* m, int64_t* bytes) {
     if (!m || !bytes) return LQ_ERR_INVALID_ARG;
     auto q8b = [](const lq_q8_tensor& t) { return t.n * t.k + t.n * (t.k / 32) * 2; };
     int64_t s = q8b(m->lm_head);
-    for (auto& ly : m->layers) s += q8b(ly.qkv) + q8b(ly.o) + q8b(ly.gate_up) + q8b(ly.down);
+    for (auto& ly : m->layers)
+        s += q8b(ly.qkv) + q8b(ly.o) + q8b(ly.gate_up) + q8b(ly.down) + q8b(ly.router) + q8b(ly.moe_gate_up) +
+             q8b(ly.moe_down);
     *bytes = s;
     return LQ_OK;
 }

@@ -46,8 +46,15 @@ class Qwen3Config(C.Structure):
         ("n_kv_heads", C.c_int64), ("head_dim", C.c_int64), ("inter", C.c_int64),
         ("vocab", C.c_int64), ("max_pos", C.c_int64), ("tied", C.c_int32),
         ("eps", C.c_float), ("theta", C.c_double), ("init_std", C.c_float),
-        ("norm_std", C.c_float),
+        ("norm_std", C.c_float), ("n_experts", C.c_int64), ("top_k", C.c_int64),
+        ("moe_inter", C.c_int64), ("norm_topk", C.c_int32), ("pad_", C.c_int32),
     ]
+
+
+class MoeExperts(C.Structure):
+    """lq_moe_experts: stacked expert weights (gate/up [E*2I][H], down [E*H][I])."""
+    _fields_ = [("n_experts", C.c_int64), ("inter", C.c_int64), ("hidden", C.c_int64),
+                ("gate_up", Q8Tensor), ("down", Q8Tensor)]
 
 
 # Qwen3 architectures of the benchmark configurations
@@ -57,6 +64,9 @@ QWEN3_8B = dict(hidden=4096, layers=36, n_heads=32, n_kv_heads=8, head_dim=128, 
                 vocab=151936, max_pos=40960, tied=0, eps=1e-6, theta=1e6, init_std=0.02, norm_std=0.0)
 QWEN3_32B = dict(hidden=5120, layers=64, n_heads=64, n_kv_heads=8, head_dim=128, inter=25600,
                  vocab=151936, max_pos=40960, tied=0, eps=1e-6, theta=1e6, init_std=0.02, norm_std=0.0)
+QWEN3_30B_A3B = dict(hidden=2048, layers=48, n_heads=32, n_kv_heads=4, head_dim=128, inter=0,
+                     vocab=151936, max_pos=40960, tied=0, eps=1e-6, theta=1e6, init_std=0.02, norm_std=0.0,
+                     n_experts=128, top_k=8, moe_inter=768, norm_topk=1)
 
 
 def make_config(**kw) -> Qwen3Config:
@@ -73,6 +83,8 @@ _I64 = C.c_int64
 _lib = None
 
 # name -> (restype, argtypes); the single source of the binding, checked against lq8.h
+ABI_VERSION = 2   # LQ8_ABI_VERSION of the struct layouts below
+
 SIGNATURES = {
     "lq_abi_version": (C.c_int, []),
     "lq_init": (C.c_int, [C.c_int, C.POINTER(_P)]),
@@ -116,6 +128,9 @@ SIGNATURES = {
     "lq_qwen3_linear": (C.c_int, [_P, _I64, C.c_int, C.POINTER(Q8Tensor)]),
     "lq_qwen3_weight_bytes": (C.c_int, [_P, C.POINTER(_I64)]),
     "lq_qwen3_graph_kernels": (C.c_int, [_P, C.POINTER(_I64)]),
+    "lq_qwen3_expert": (C.c_int, [_P, _I64, _I64, C.c_int, C.POINTER(Q8Tensor)]),
+    "lq_moe_forward": (C.c_int, [_P, C.POINTER(Q8Tensor), C.POINTER(MoeExperts), _P, _P, _I64, _I64, C.c_int,
+                                 _P, _P, _P, _P]),
 }
 
 
@@ -130,6 +145,8 @@ def load():
             f = getattr(lib, name)
             f.restype = res
             f.argtypes = args
+        if lib.lq_abi_version() != ABI_VERSION:
+            raise OSError(f"liblq8.so ABI {lib.lq_abi_version()} != binding ABI {ABI_VERSION}; rebuild")
         _lib = lib
     return _lib
 
@@ -339,6 +356,12 @@ class Qwen3ForCausalLM:
     def linear(self, layer: int, kind: str) -> Q8Tensor:
         t = Q8Tensor()
         self._check(self.ctx.lib.lq_qwen3_linear(self.h, layer, KIND[kind], C.byref(t)))
+        return t
+
+    def expert(self, layer: int, expert: int, kind: int) -> Q8Tensor:
+        """MoE weight view: kind 10 router, 11 gate, 12 up, 13 down of `expert`."""
+        t = Q8Tensor()
+        self._check(self.ctx.lib.lq_qwen3_expert(self.h, layer, expert, kind, C.byref(t)))
         return t
 
     def graph_kernels(self) -> int:

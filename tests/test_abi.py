@@ -34,7 +34,10 @@ def test_binding_covers_header(lq8_lib):
 
 
 def test_abi_version(lq8_lib):
-    assert lq8_lib.load().lq_abi_version() == 1
+    import re
+    hdr = open(os.path.join(REPO, "include", "lq8.h")).read()
+    want = int(re.search(r"#define LQ8_ABI_VERSION (\d+)", hdr).group(1))
+    assert lq8_lib.load().lq_abi_version() == want == lq8_lib.ABI_VERSION
 
 
 def test_init_failure_is_a_status_not_an_abort(lq8_lib, monkeypatch):

@@ -1,0 +1,122 @@
+"""GPU parity of the Qwen3-MoE sparse MLP (lq_moe_forward) and of a MoE model, through the
+C ABI, against the CPU oracle (orc_moe_forward).
+
+Router logits and every expert's Q8_0 products keep the oracle's block order, so the chosen
+experts must be identical; routing weights carry the softmax's exp (CUDA expf against the C
+library's, a few ulp), so they and the combined output are checked with an f32 tolerance.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from conftest import cos_sim
+from test_gpu_q8 import H, T
+
+pytestmark = pytest.mark.gpu
+
+
+def _rand_q8(rng, n, k, scale_lo=0x1400, scale_hi=0x2000):
+    """A random Q8_0 tensor: int8 values in [-127, 127], fp16 scales in [scale_lo, scale_hi)."""
+    qs = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
+    d = rng.integers(scale_lo, scale_hi, size=(n, k // 32)).astype(np.uint16)
+    return qs, d
+
+
+def _moe_case(ctx, lq8, oracle, rng, rows, Hd, E, K, I, norm_topk=1):
+    xf = rng.standard_normal((rows, Hd)).astype(np.float32)
+    xb = oracle.f32_to_bf16(xf)
+    router = _rand_q8(rng, E, Hd)
+    gate = [_rand_q8(rng, I, Hd) for _ in range(E)]
+    up = [_rand_q8(rng, I, Hd) for _ in range(E)]
+    down = [_rand_q8(rng, Hd, I) for _ in range(E)]
+    o_out, o_ids, o_w = oracle.moe_forward(xb, router, gate, up, down, K, bool(norm_topk))
+    # device: stacked experts, activations quantized like the Linear path (bf16 rows)
+    gu_q = np.concatenate([np.concatenate([gate[e][0], up[e][0]]) for e in range(E)])
+    gu_d = np.concatenate([np.concatenate([gate[e][1], up[e][1]]) for e in range(E)])
+    dn_q = np.concatenate([down[e][0] for e in range(E)])
+    dn_d = np.concatenate([down[e][1] for e in range(E)])
+    xq, xd = oracle.q8_0_quantize(xb)
+    keep = [T(a) for a in (router[0], router[1], gu_q, gu_d, dn_q, dn_d, xq, xd)]
+    rt = lq8.Q8Tensor(E, Hd, keep[0].data_ptr(), keep[1].data_ptr())
+    ex = lq8.MoeExperts(E, I, Hd, lq8.Q8Tensor(E * 2 * I, Hd, keep[2].data_ptr(), keep[3].data_ptr()),
+                        lq8.Q8Tensor(E * Hd, I, keep[4].data_ptr(), keep[5].data_ptr()))
+    import torch
+    resid = rng.standard_normal((rows, Hd)).astype(np.float32)
+    out = T(resid.copy())
+    ids = torch.empty((rows, K), dtype=torch.int32, device="cuda")
+    w = torch.empty((rows, K), dtype=torch.float32, device="cuda")
+    ctx.call("lq_moe_forward", C.byref(rt), C.byref(ex), keep[6].data_ptr(), keep[7].data_ptr(), rows, K,
+             norm_topk, out.data_ptr(), out.data_ptr(), ids.data_ptr(), w.data_ptr())
+    ctx.synchronize()
+    return H(out), H(ids), H(w), resid + o_out, o_ids, o_w
+
+
+@pytest.mark.parametrize("rows,Hd,E,K,I", [(1, 256, 16, 4, 128), (5, 256, 16, 4, 128), (37, 512, 32, 8, 96),
+                                           (64, 2048, 32, 8, 768)])
+def test_moe_forward_vs_oracle(ctx, lq8_lib, oracle, rng, rows, Hd, E, K, I):
+    """Router top-k identical, routing weights and the combined residual output within f32
+    tolerance; the last case has the Qwen3-30B-A3B expert shape (hidden 2048, experts of
+    768, top-8) at decode batch 64 over 32 experts."""
+    got, gids, gw, ref, oids, ow = _moe_case(ctx, lq8_lib, oracle, rng, rows, Hd, E, K, I)
+    assert np.array_equal(gids, oids)
+    np.testing.assert_allclose(gw, ow, rtol=2e-6, atol=0)
+    np.testing.assert_allclose(got, ref, rtol=0, atol=2e-5 * np.max(np.abs(ref)))
+
+
+def test_moe_without_renormalisation(ctx, lq8_lib, oracle, rng):
+    got, gids, gw, ref, oids, ow = _moe_case(ctx, lq8_lib, oracle, rng, 9, 256, 16, 2, 64, norm_topk=0)
+    assert np.array_equal(gids, oids)
+    assert np.all(gw.sum(axis=1) < 1.0)
+    np.testing.assert_allclose(got, ref, rtol=0, atol=2e-5 * np.max(np.abs(ref)))
+
+
+def test_moe_bad_shapes_are_errors(ctx, lq8_lib):
+    rt = lq8_lib.Q8Tensor(16, 256, 1, 1)
+    ex = lq8_lib.MoeExperts(16, 128, 256, lq8_lib.Q8Tensor(16 * 2 * 128, 256, 1, 1),
+                            lq8_lib.Q8Tensor(16 * 256, 100, 1, 1))
+    with pytest.raises(lq8_lib.LQ8Error) as e:
+        ctx.call("lq_moe_forward", C.byref(rt), C.byref(ex), 1, 1, 4, 4, 1, 1, None, None, None)
+    assert e.value.code == -1
+    ex.down.k = 128
+    with pytest.raises(lq8_lib.LQ8Error):
+        ctx.call("lq_moe_forward", C.byref(rt), C.byref(ex), 1, 1, 4, 17, 1, 1, None, None, None)  # top_k > 16
+
+
+TINY_MOE = dict(hidden=256, layers=2, n_heads=4, n_kv_heads=2, head_dim=128, inter=0, vocab=1000, tied=0,
+                norm_std=0.1, n_experts=16, top_k=4, moe_inter=128, norm_topk=1)
+
+
+def test_moe_model_weights_bit_identical(ctx, lq8_lib, oracle):
+    gm = lq8_lib.Qwen3ForCausalLM(ctx, lq8_lib.make_config(**TINY_MOE), 42, max_batch=1, ctx_max=64)
+    om = oracle.Qwen3Model(oracle.make_config(**TINY_MOE), 42, ctx_max=64)
+    for layer in range(2):
+        for e, kind in [(0, 10), (0, 11), (0, 12), (0, 13), (7, 11), (15, 12), (15, 13)]:
+            t = lq8_lib.QTensor.from_struct(gm.expert(layer, e, kind))
+            oq, od = om.expert(layer, e, kind)
+            assert np.array_equal(H(t.qs), oq), (layer, e, kind)
+            assert np.array_equal(H(t.d, np.uint16), od), (layer, e, kind)
+    with pytest.raises(lq8_lib.LQ8Error):
+        gm.linear(0, "gate")
+
+
+@pytest.mark.parametrize("B", [1, 3, 6])
+def test_moe_model_generate_matches_oracle(ctx, lq8_lib, oracle, B):
+    """Prefill + greedy decode of a 2-layer MoE model (16 experts, top-4): B = 1 and 3 take
+    the fused decode path, B = 6 the separate kernels; logits within tolerance at every
+    step, free-running tokens identical to the oracle's."""
+    L, steps = 12, 8
+    gm = lq8_lib.Qwen3ForCausalLM(ctx, lq8_lib.make_config(**TINY_MOE), 11, max_batch=B, ctx_max=64)
+    ocfg = oracle.make_config(**TINY_MOE)
+    prompts = np.stack([oracle.gen_tokens(11, s, L, ocfg.vocab) for s in range(B)])
+    nxt, lg = gm.prefill(prompts, want_logits=True)
+    for b in range(B):
+        om = oracle.Qwen3Model(ocfg, 11, ctx_max=64)
+        olg = om.forward(prompts[b], 0)
+        assert cos_sim(lg[b], olg) >= 0.99999
+        assert np.max(np.abs(lg[b] - olg)) <= 1e-3 * np.max(np.abs(olg))
+    toks = gm.generate(prompts, steps)
+    for b in range(B):
+        om = oracle.Qwen3Model(ocfg, 11, ctx_max=64)
+        otoks, _ = om.generate(prompts[b], steps)
+        assert np.array_equal(toks[b], otoks), b
