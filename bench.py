@@ -41,6 +41,10 @@ CONFIGS = {
                        vocab=151936, max_pos=40960, tied=1, eps=1e-6, theta=1e6, init_std=0.02, norm_std=0.0),
     "qwen3-32b": dict(hidden=5120, layers=64, n_heads=64, n_kv_heads=8, head_dim=128, inter=25600,
                       vocab=151936, max_pos=40960, tied=0, eps=1e-6, theta=1e6, init_std=0.02, norm_std=0.0),
+    # Qwen3-30B-A3B: 48 MoE layers of 128 experts (moe_inter 768), top-8, renormalised
+    "qwen3-30b-a3b": dict(hidden=2048, layers=48, n_heads=32, n_kv_heads=4, head_dim=128, inter=0,
+                          vocab=151936, max_pos=40960, tied=0, eps=1e-6, theta=1e6, init_std=0.02,
+                          norm_std=0.0, n_experts=128, top_k=8, moe_inter=768, norm_topk=1),
 }
 SEED = 1234
 METRIC = "Q8_0 decode tok/s"
@@ -344,9 +348,13 @@ def run_ours(args, cfgd, world, rank, local):
     ms_e2e = max_over_ranks(e2.elapsed_time(e3))
     e2e = world * B * K / (ms_e2e / 1000.0)
 
+    peak, peak_kind = peaks()
+    if cfgd.get("n_experts", 0) > 0:
+        roofline, step_gbs, wbytes = moe_step_roofline(cfgd, B, L + W + K, ms / K, peak, peak_kind)
+        return finish(args, cfgd, world, rank, L, B, K, W, ms, value, e2e, ms_e2e, clk, launches, roofline,
+                      step_gbs, wbytes, t_create, t_pre, model, ctx, dist)
     # ---- roofline of the dominant kernel: the decode GEMV
     shapes = time_gemv_launches(lq8, ctx, model, cfgd, B)
-    peak, peak_kind = peaks()
     tot_b = tot_ms = 0.0
     per_shape = {}
     for kind, s in shapes.items():
@@ -374,7 +382,34 @@ def run_ours(args, cfgd, world, rank, local):
     }
     wbytes = model.weight_bytes()
     step_gbs = wbytes / (ms / K / 1000) / 1e9
+    return finish(args, cfgd, world, rank, L, B, K, W, ms, value, e2e, ms_e2e, clk, launches, roofline, step_gbs,
+                  wbytes, t_create, t_pre, model, ctx, dist)
 
+
+def moe_step_roofline(cfgd, B, ctx_len, step_s_ms, peak, peak_kind):
+    """MoE decode: the whole step against the HBM roofline. Bytes per step = attention
+    weights + router + LM head + the experts a batch of B tokens touches (expected count
+    E * (1 - (1 - k/E)^B) under uniform routing) + the f32 KV cache read at the mid context."""
+    H, D, Hq, Hkv, E, k, I = (cfgd[x] for x in ("hidden", "head_dim", "n_heads", "n_kv_heads", "n_experts",
+                                                "top_k", "moe_inter"))
+    q8 = lambda n, kk: n * kk * 34 // 32
+    layers = cfgd["layers"]
+    attn = q8((Hq + 2 * Hkv) * D, H) + q8(H, Hq * D)
+    router = q8(E, H)
+    expert = q8(2 * I, H) + q8(H, I)
+    touched = E * (1.0 - (1.0 - k / E) ** B)
+    kv = 2 * Hkv * D * ctx_len * 4 * B
+    lm = q8(cfgd["vocab"], H)
+    step_bytes = layers * (attn + router + touched * expert + kv) + lm
+    gbs = step_bytes / (step_s_ms / 1000) / 1e9
+    roofline = {"bound": "hbm", "kernel": f"whole MoE decode step (B={B})", "achieved": gbs, "peak": peak,
+                "unit": "GB/s", "frac": gbs / peak, "peak_kind": f"{peak_kind} copy bandwidth", "traffic": None,
+                "algorithmic_bytes_per_step": step_bytes, "expected_experts_touched_per_layer": touched}
+    return roofline, gbs, int(layers * (attn + router + touched * expert) + lm)
+
+
+def finish(args, cfgd, world, rank, L, B, K, W, ms, value, e2e, ms_e2e, clk, launches, roofline, step_gbs, wbytes,
+           t_create, t_pre, model, ctx, dist):
     # ---- CPU baseline (rank 0, N = 1 only)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -385,7 +420,7 @@ def run_ours(args, cfgd, world, rank, local):
                "sample": (f"oracle (C restatement of the reference's single-threaded Rust CPU path with Q8_0 "
                           f"linears), 1 thread: one decode token after a 16-token prompt through 1 and 2 of "
                           f"{cfgd['layers']} layers + LM head, per-layer time extrapolated to the full model; "
-                          f"context 16 instead of 2048 (attention at 2048 would add about 9 % CPU time)"),
+                          f"context 16 instead of {L} (attention over the longer context is left out)"),
                "detail": det}
 
     if rank == 0:
@@ -397,7 +432,7 @@ def run_ours(args, cfgd, world, rank, local):
             "config": {"workload": f"{args.config} greedy decode after a {L}-token prefill, batch {B}",
                        "model": args.config, "global_batch": B * world, "seq_len": L,
                        "parallelism": f"dp{world} replicas" if world > 1 else "single GPU",
-                       "l2": "no flush: each step streams all Q8_0 weights (64x the L2)",
+                       "l2": "no flush: each step streams the Q8_0 weights (GBs, far above the 126 MB L2)",
                        "context_range": [L + W, L + W + K]},
             "roofline": roofline,
             "step_weight_gbs": step_gbs,
@@ -480,6 +515,65 @@ def run_sweep(args):
         torch.cuda.empty_cache()
 
 
+def run_moe(args):
+    """MoE layer alone: lq_moe_forward (router, top-k, grouped expert GEMVs, combine) at the
+    Qwen3-30B-A3B expert shape (128 experts, hidden 2048, moe_inter 768, top-8) with random
+    Q8_0 weights, for rows in --moe-rows. Reports per call time, the touched expert bytes
+    (experts actually selected) and their rate. One JSON line per row count."""
+    import ctypes as C
+
+    import torch
+
+    import build
+    import lq8
+    build.build()
+    ctx = lq8.Context(0)
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=dev)
+    E, H, I, K = 128, 2048, 768, 8
+    g = torch.Generator(device=dev).manual_seed(SEED)
+
+    def q8(n, k):
+        qs = torch.randint(-127, 128, (n, k), dtype=torch.int8, device=dev, generator=g)
+        d = torch.randint(0x1400, 0x2000, (n, k // 32), dtype=torch.int16, device=dev, generator=g)
+        return qs, d
+
+    rq, rd = q8(E, H)
+    gq, gd = q8(E * 2 * I, H)
+    dq, dd = q8(E * H, I)
+    router = lq8.Q8Tensor(E, H, rq.data_ptr(), rd.data_ptr())
+    ex = lq8.MoeExperts(E, I, H, lq8.Q8Tensor(E * 2 * I, H, gq.data_ptr(), gd.data_ptr()),
+                        lq8.Q8Tensor(E * H, I, dq.data_ptr(), dd.data_ptr()))
+    expert_bytes = (2 * I * H + H * I) * 34 // 32
+    for rows in (int(r) for r in args.moe_rows.split(",")):
+        x = (torch.randn((rows, H), generator=g, device=dev)).to(torch.bfloat16)
+        xq = torch.empty((rows, H), dtype=torch.int8, device=dev)
+        xd = torch.empty((rows, H // 32), dtype=torch.int16, device=dev)
+        ctx.call("lq_q8_0_quantize", x.data_ptr(), lq8.DTYPE_BF16, rows, H, xq.data_ptr(), xd.data_ptr())
+        out = torch.zeros((rows, H), dtype=torch.float32, device=dev)
+        ids = torch.empty((rows, K), dtype=torch.int32, device=dev)
+        reps = max(args.sweep_reps, 3)
+        for _ in range(3):
+            ctx.call("lq_moe_forward", C.byref(router), C.byref(ex), xq.data_ptr(), xd.data_ptr(), rows, K, 1,
+                     out.data_ptr(), None, ids.data_ptr(), None)
+        ctx.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            ctx.call("lq_moe_forward", C.byref(router), C.byref(ex), xq.data_ptr(), xd.data_ptr(), rows, K, 1,
+                     out.data_ptr(), None, ids.data_ptr(), None)
+        e1.record(stream)
+        ctx.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        touched = int(torch.unique(ids).numel())
+        byts = touched * expert_bytes + E * H * 34 // 32
+        print(json.dumps({"moe": "lq_moe_forward", "rows": rows, "experts": E, "hidden": H, "moe_inter": I,
+                          "top_k": K, "us": round(us, 2), "experts_touched": touched,
+                          "weight_bytes": byts, "GB/s": round(byts / us / 1e3, 1),
+                          "tokens_per_s": round(rows / us * 1e6, 1)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -503,11 +597,17 @@ def main():
     ap.add_argument("--sweep-case", default="",
                     help="with --sweep: one case 'm,n,k' (two weight copies; for profiling)")
     ap.add_argument("--sweep-reps", type=int, default=20)
+    ap.add_argument("--moe", action="store_true",
+                    help="time lq_moe_forward alone at the Qwen3-30B-A3B expert shape and exit")
+    ap.add_argument("--moe-rows", default="1,8,64,512")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.sweep:
         run_sweep(args)
+        return
+    if args.moe:
+        run_moe(args)
         return
     world, rank, local = dist_env()
     cfgd = dict(CONFIGS[args.config])

@@ -24,8 +24,7 @@
 // TMA loads here read only this GPU's memory and use no multicast.
 #include "lq8_async.cuh"
 #include "lq8_internal.cuh"
-
-#include <cuda.h>
+#include "lq8_tma.cuh"
 
 namespace lq {
 
@@ -53,13 +52,6 @@ struct TcBars {
     int abort;
 };
 
-__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            smem_addr(smem_dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
-        : "memory");
-}
 
 // K-major, 128-byte swizzled operand tile: rows of 128 B, 8-row groups 1024 B apart
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
@@ -333,7 +325,7 @@ static EncodeTiledFn encode_fn(lq_ctx* ctx) {
     return fn;
 }
 
-static int make_map(lq_ctx* ctx, CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
+int make_tensor_map_2d(lq_ctx* ctx, CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
                     uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
                     CUtensorMapSwizzle swz) {
     EncodeTiledFn fn = encode_fn(ctx);
@@ -361,15 +353,15 @@ int launch_gemm_tc(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const u
     const int64_t N = w->n, K = w->k, nb = K / 32;
     CUtensorMap mw, mx, mdw, mdx;
     int rc;
-    if ((rc = make_map(ctx, &mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->qs, K, N, K, 128, TC_BM,
+    if ((rc = make_tensor_map_2d(ctx, &mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->qs, K, N, K, 128, TC_BM,
                        CU_TENSOR_MAP_SWIZZLE_128B)))
         return rc;
-    if ((rc = make_map(ctx, &mx, CU_TENSOR_MAP_DATA_TYPE_UINT8, xq, K, m, K, 128, TC_BN, CU_TENSOR_MAP_SWIZZLE_128B)))
+    if ((rc = make_tensor_map_2d(ctx, &mx, CU_TENSOR_MAP_DATA_TYPE_UINT8, xq, K, m, K, 128, TC_BN, CU_TENSOR_MAP_SWIZZLE_128B)))
         return rc;
-    if ((rc = make_map(ctx, &mdw, CU_TENSOR_MAP_DATA_TYPE_UINT16, w->d, nb, N, nb * 2, 8, TC_BM,
+    if ((rc = make_tensor_map_2d(ctx, &mdw, CU_TENSOR_MAP_DATA_TYPE_UINT16, w->d, nb, N, nb * 2, 8, TC_BM,
                        CU_TENSOR_MAP_SWIZZLE_NONE)))
         return rc;
-    if ((rc = make_map(ctx, &mdx, CU_TENSOR_MAP_DATA_TYPE_UINT16, xd, nb, m, nb * 2, 8, TC_BN,
+    if ((rc = make_tensor_map_2d(ctx, &mdx, CU_TENSOR_MAP_DATA_TYPE_UINT16, xd, nb, m, nb * 2, 8, TC_BN,
                        CU_TENSOR_MAP_SWIZZLE_NONE)))
         return rc;
     static bool attr[64] = {};

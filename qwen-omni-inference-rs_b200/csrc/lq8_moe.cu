@@ -1,6 +1,7 @@
 // lq8_moe.cu -- Qwen3-MoE sparse MLP on Q8_0 experts (router, top-k, grouped expert GEMVs,
 // combine). The reference has no MoE code; the convention follows the Qwen3-MoE sparse block:
-//   logits = x . R^T (Q8_0, blocks ascending, bit-identical to the oracle);
+//   logits = x . R^T (Q8_0, blocks ascending: bit-identical to the oracle, so the same experts
+//   are chosen);
 //   p = softmax(logits) (f32); the top_k experts by logit, ties to the lower expert index;
 //   w_j = p[e_j], renormalised by their sum (selection order) when norm_topk;
 //   y_e = down_e . (silu(gate_e . x) * (up_e . x)), h quantized to Q8_0 per 32-block;
@@ -8,25 +9,24 @@
 //
 // All counts live in device memory, so the whole layer is one fixed sequence of launches
 // (CUDA-graph capturable):
-//   moe_route     one CTA per token: logits (a thread per expert, sequential over blocks),
+//   moe_route     one CTA per token: logits (a warp per expert, block terms in parallel, summed
+//                 in ascending block order),
 //                 softmax, top-k, weights; also the token's experts in ascending order.
 //   moe_dispatch  one CTA: per-expert pair lists in token order (warp ballots, deterministic),
 //                 offsets, the list of active experts, each pair's slot for the combine.
-//   moe_expert    persistent grouped GEMV over work items (active expert, tile of 256 weight
-//                 rows): a thread owns a weight row (gate/up: the row pair r, I+r) and up to 8
-//                 tokens of the expert at a time, accumulating blocks in ascending order
-//                 (bit-identical per output to the oracle's Q8_0 dot). The gate/up pass fuses
-//                 SiLU * up and the Q8_0 quantization of h (a warp's 32 rows are one block).
+//   moe_stream    persistent grouped GEMV streaming the touched experts' weights through a
+//                 shared-memory ring (see below); the gate/up pass fuses SiLU * up and the
+//                 Q8_0 quantization of h.
 //   moe_combine   per token: residual + sum_e w_e * y_e in ascending expert order.
 #include "lq8_async.cuh"
+#include "lq8_fused.cuh"
 #include "lq8_internal.cuh"
+#include "lq8_tma.cuh"
 
 namespace lq {
 
 constexpr int MOE_MAX_E = 512;
 constexpr int MOE_MAX_K = 16;
-constexpr int MOE_TG = 8;          // tokens per pass of a work item
-constexpr int MOE_ROWS = 256;      // weight rows per work item (one per thread)
 
 __device__ __forceinline__ int dot32(const int4 a0, const int4 a1, const int4 b0, const int4 b1) {
     int s = 0;
@@ -42,7 +42,7 @@ __device__ __forceinline__ int dot32(const int4 a0, const int4 a1, const int4 b0
 }
 
 // ---------------------------------------------------------------------------------------
-// route: one CTA (max(E, 128) threads, multiple of 32) per token
+// route: one CTA per token (min(1024, max(128, 8E)) threads)
 // ---------------------------------------------------------------------------------------
 __global__ void moe_route_kernel(const int8_t* __restrict__ xq, const uint16_t* __restrict__ xd, int H,
                                  const int8_t* __restrict__ rq, const uint16_t* __restrict__ rd, int E, int top_k,
@@ -53,7 +53,7 @@ __global__ void moe_route_kernel(const int8_t* __restrict__ xq, const uint16_t* 
     int8_t* sx = reinterpret_cast<int8_t*>(smem_raw);                       // [H]
     float* sdx = reinterpret_cast<float*>(smem_raw + H);                     // [nb]
     float* lg = sdx + nb;                                                    // [E]
-    float* pe = lg + E;                                                      // [E]
+    float* pe = lg + E;                                                      // [E], then terms
     __shared__ int sel[MOE_MAX_K];
     __shared__ float selw[MOE_MAX_K];
     const int t = blockIdx.x, tid = threadIdx.x;
@@ -63,61 +63,79 @@ __global__ void moe_route_kernel(const int8_t* __restrict__ xq, const uint16_t* 
         *reinterpret_cast<int4*>(sx + i) = *reinterpret_cast<const int4*>(xq + (size_t)t * H + i);
     for (int b = tid; b < nb; b += blockDim.x) sdx[b] = h2f(xd[(size_t)t * nb + b]);
     __syncthreads();
-    for (int e = tid; e < E; e += blockDim.x) {
+    // logits: a warp per expert; lanes form the block terms (int dot, scale product) in
+    // parallel, then lane 0 adds them in ascending block order (the oracle's sum)
+    float* terms = pe + E + (size_t)(tid >> 5) * nb;   // [warps][nb]
+    const int warp = tid >> 5, lane = tid & 31, nwarps = blockDim.x >> 5;
+    for (int e = warp; e < E; e += nwarps) {
         const int8_t* wr = rq + (size_t)e * H;
         const uint16_t* wd = rd + (size_t)e * nb;
-        float acc = 0.0f;
-        for (int b = 0; b < nb; b++) {
+        for (int b = lane; b < nb; b += 32) {
             const int4 w0 = __ldg(reinterpret_cast<const int4*>(wr + b * 32));
             const int4 w1 = __ldg(reinterpret_cast<const int4*>(wr + b * 32 + 16));
             const int4 x0 = *reinterpret_cast<const int4*>(sx + b * 32);
             const int4 x1 = *reinterpret_cast<const int4*>(sx + b * 32 + 16);
-            const int s = dot32(w0, w1, x0, x1);
-            acc = __fadd_rn(acc, __fmul_rn((float)s, __fmul_rn(h2f(wd[b]), sdx[b])));
+            terms[b] = __fmul_rn((float)dot32(w0, w1, x0, x1), __fmul_rn(h2f(__ldg(wd + b)), sdx[b]));
         }
-        lg[e] = acc;
+        __syncwarp();
+        if (lane == 0) {
+            float acc = 0.0f;
+            for (int b = 0; b < nb; b++) acc = __fadd_rn(acc, terms[b]);
+            lg[e] = acc;
+        }
+        __syncwarp();
     }
     __syncthreads();
-    if (tid == 0) {
-        // softmax (max, exp(l - max), sum ascending, divide), then top-k by logit
-        float mx = -INFINITY;
-        for (int e = 0; e < E; e++) mx = fmaxf(mx, lg[e]);
-        float sum = 0.0f;
-        for (int e = 0; e < E; e++) {
-            pe[e] = expf(__fsub_rn(lg[e], mx));
-            sum = __fadd_rn(sum, pe[e]);
+    if (warp != 0) return;
+    // softmax: max (warp), exp in parallel, sum in ascending expert order (lane 0), divide
+    float mx = -INFINITY;
+    for (int e = lane; e < E; e += 32) mx = fmaxf(mx, lg[e]);
+    mx = warp_max(mx);
+    for (int e = lane; e < E; e += 32) pe[e] = expf(__fsub_rn(lg[e], mx));
+    __syncwarp();
+    float sum = 0.0f;
+    if (lane == 0)
+        for (int e = 0; e < E; e++) sum = __fadd_rn(sum, pe[e]);
+    sum = __shfl_sync(0xffffffffu, sum, 0);
+    for (int e = lane; e < E; e += 32) pe[e] = __fdiv_rn(pe[e], sum);
+    __syncwarp();
+    // top-k by logit, ties to the lower expert index: k rounds of a warp argmax
+    unsigned used = 0u;  // bit i: expert lane + 32 i taken (E <= 512 -> 16 bits)
+    for (int j = 0; j < top_k; j++) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int i = 0, e = lane; e < E; i++, e += 32)
+            if (!((used >> i) & 1u) && (lg[e] > bv || bi == 0x7fffffff)) { bv = lg[e]; bi = e; }
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (oi != 0x7fffffff && (bi == 0x7fffffff || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
         }
-        for (int e = 0; e < E; e++) pe[e] = __fdiv_rn(pe[e], sum);
-        unsigned used[MOE_MAX_E / 32];
-        for (int i = 0; i < MOE_MAX_E / 32; i++) used[i] = 0u;
-        for (int j = 0; j < top_k; j++) {
-            int best = -1;
-            for (int e = 0; e < E; e++)
-                if (!((used[e >> 5] >> (e & 31)) & 1u) && (best < 0 || lg[e] > lg[best])) best = e;
-            used[best >> 5] |= 1u << (best & 31);
-            sel[j] = best;
-            selw[j] = pe[best];
-        }
+        if ((bi & 31) == lane) used |= 1u << (bi >> 5);
+        if (lane == 0) { sel[j] = bi; selw[j] = pe[bi]; }
+    }
+    __syncwarp();
+    if (lane == 0) {
         if (norm_topk) {
             float s = 0.0f;
             for (int j = 0; j < top_k; j++) s = __fadd_rn(s, selw[j]);
             for (int j = 0; j < top_k; j++) selw[j] = __fdiv_rn(selw[j], s);
         }
+        int se[MOE_MAX_K];
+        float sw[MOE_MAX_K];
         for (int j = 0; j < top_k; j++) {
             ids[(size_t)t * top_k + j] = sel[j];
             wts[(size_t)t * top_k + j] = selw[j];
+            // insertion into ascending expert order (for the combine)
+            int q = j;
+            while (q > 0 && se[q - 1] > sel[j]) { se[q] = se[q - 1]; sw[q] = sw[q - 1]; q--; }
+            se[q] = sel[j];
+            sw[q] = selw[j];
         }
-        // ascending expert order for the combine
-        int jj = 0;
-        for (int e = 0; e < E && jj < top_k; e++)
-            if ((used[e >> 5] >> (e & 31)) & 1u) {
-                float we = 0.0f;
-                for (int j = 0; j < top_k; j++)
-                    if (sel[j] == e) we = selw[j];
-                ids_sorted[(size_t)t * top_k + jj] = e;
-                w_sorted[(size_t)t * top_k + jj] = we;
-                jj++;
-            }
+        for (int j = 0; j < top_k; j++) {
+            ids_sorted[(size_t)t * top_k + j] = se[j];
+            w_sorted[(size_t)t * top_k + j] = sw[j];
+        }
     }
 }
 
@@ -132,13 +150,16 @@ struct MoeLists {
     int32_t* pair_slot;    // [rows][k] pair index of the token's jj-th expert (ascending expert)
 };
 
-__global__ void __launch_bounds__(1024) moe_dispatch_kernel(const int32_t* __restrict__ ids_sorted, int rows, int E,
+__global__ void __launch_bounds__(1024) moe_dispatch_kernel(const int32_t* __restrict__ ids_g, int rows, int E,
                                                             int top_k, MoeLists L) {
     __shared__ int cnt[MOE_MAX_E];
     __shared__ int off[MOE_MAX_E + 1];
+    extern __shared__ int ids_sorted[];  // [rows][top_k] staged from global
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     pdl_wait();
     pdl_trigger();
+    for (int i = threadIdx.x; i < rows * top_k; i += blockDim.x) ids_sorted[i] = ids_g[i];
+    __syncthreads();
     // pass 1: counts
     for (int e = warp; e < E; e += 32) {
         int c = 0;
@@ -189,15 +210,37 @@ __global__ void __launch_bounds__(1024) moe_dispatch_kernel(const int32_t* __res
 }
 
 // ---------------------------------------------------------------------------------------
-// grouped expert GEMV
+// grouped expert GEMV, streamed
+//
+// Work item = (active expert, 128 output rows); each CTA takes a contiguous range of items,
+// so consecutive items mostly share the expert and its activations stay in shared memory.
+// One producer lane streams the item's weight rows (gate/up: the 128 gate rows and the 128
+// matching up rows) in K-chunks of 256 bytes (8 Q8_0 blocks) into a shared-memory ring with
+// 2-D TMA loads: per group of 128 rows two 128-byte-wide boxes (128-byte swizzle, so the
+// row-per-lane 16-byte reads are bank-conflict free) and one box of the chunk's scales.
+// Consumer warp w owns rows 32 (w % 4) + lane and one half of the pass's tokens (16 tokens
+// per pass, split evenly between the halves; more tokens take more passes), so all eight
+// warps work even for two tokens per expert, and every (row, token) output is accumulated
+// by one thread in ascending block order: bit-identical to the oracle (which keeps the next
+// layer's routing identical). Epilogue: gate/up -> h = silu(g) * u quantized to Q8_0 (a
+// warp's 32 rows are one block); down -> y [pair][row] f32.
 // ---------------------------------------------------------------------------------------
+constexpr int ME_KC = 256;                   // K bytes per stage
+constexpr int ME_R = 128;                    // output rows per item
+constexpr int ME_TG = 16;                    // tokens per pass
+constexpr int ME_TH = ME_TG / 2;             // tokens per consumer half
+constexpr int ME_CONSUMERS = 8;
+constexpr int ME_THREADS = (ME_CONSUMERS + 1) * 32;
+constexpr int ME_MAX_STAGES = 8;
+constexpr int ME_BOX = ME_R * 128;           // one 128-byte-wide box of a group
+constexpr int ME_GROUP_W = 2 * ME_BOX;       // weight bytes of one group per stage
+constexpr int ME_GROUP_D = ME_R * 16;        // scale bytes of one group per stage
+
 struct MoeExpertParams {
-    const int8_t* wq;        // stacked expert weights [E * rows_per_expert][K]
-    const uint16_t* wd;
-    int rows_per_expert;     // gate/up: 2I (a thread computes rows r and I + r); down: H
-    int out_rows;            // gate/up: I; down: H
-    int K;
-    int gate_up;             // 1: SiLU * up epilogue + Q8_0 output; 0: f32 output per pair
+    int rows_per_expert;     // gate/up: 2I (gate rows then up rows); down: H
+    int out_rows;            // gate/up: I; down: H (multiples of 128)
+    int K;                   // multiple of 256
+    int stages;
     const int8_t* xq;        // activations: gate/up [rows][K] by token; down [pairs][K] by pair
     const uint16_t* xd;
     const int32_t* pair_token;
@@ -208,94 +251,177 @@ struct MoeExpertParams {
     int8_t* hq;              // gate/up output [pairs][I]
     uint16_t* hd;
     float* y;                // down output [pairs][H]
+    int* err;
 };
 
-__global__ void __launch_bounds__(MOE_ROWS) moe_expert_kernel(const MoeExpertParams p) {
+// fp16 bits j (0..7) of an int4 holding 8 halves (j known at compile time after unrolling)
+__device__ __forceinline__ uint16_t half_at(const int4 v, int j) {
+    const unsigned w = (unsigned)(j < 2 ? v.x : j < 4 ? v.y : j < 6 ? v.z : v.w);
+    return (uint16_t)((j & 1) ? (w >> 16) : (w & 0xFFFFu));
+}
+
+// stage: NG groups of [2 boxes][128 rows][128 B] (swizzled), then NG x [128 rows][8 fp16]
+template <bool GU>
+__host__ __device__ constexpr int me_stage_bytes() {
+    return ((GU ? 2 : 1) * (ME_GROUP_W + ME_GROUP_D) + 1023) / 1024 * 1024;
+}
+
+// 16-byte chunk `c` (0..15 over the 256-byte chunk) of row r in a group laid out by the
+// 128-byte swizzle: box c/8, row r, chunk (c%8) ^ (r%8)
+__device__ __forceinline__ int4 me_ld(const uint8_t* group, int r, int c) {
+    return *reinterpret_cast<const int4*>(group + (c >> 3) * ME_BOX + r * 128 + ((((c & 7) ^ (r & 7))) << 4));
+}
+
+template <bool GU>
+__global__ void __launch_bounds__(ME_THREADS) moe_stream_kernel(const __grid_constant__ CUtensorMap mw,
+                                                                const __grid_constant__ CUtensorMap md,
+                                                                const MoeExpertParams p) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
-    const int K = p.K, nb = K / 32;
-    int8_t* sx = reinterpret_cast<int8_t*>(smem_raw);                          // [MOE_TG][K]
-    float* sdx = reinterpret_cast<float*>(smem_raw + (size_t)MOE_TG * K);      // [MOE_TG][nb]
-    const int tid = threadIdx.x, lane = tid & 31;
+    const uint32_t raw = smem_addr(smem_raw);
+    uint8_t* sm = smem_raw + (((raw + 1023) & ~1023u) - raw);  // swizzled boxes need 1024-byte alignment
+    constexpr int NG = GU ? 2 : 1;
+    constexpr int SB = me_stage_bytes<GU>();
+    const int K = p.K, nb = K / 32, nchunks = K / ME_KC, S = p.stages;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + (size_t)S * SB);
+    uint64_t* empty = full + ME_MAX_STAGES;
+    int8_t* xs = reinterpret_cast<int8_t*>(empty + ME_MAX_STAGES);           // [ME_TG][K]
+    float* xdf = reinterpret_cast<float*>(xs + (size_t)ME_TG * K);           // [ME_TG][nb]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], ME_CONSUMERS);
+        }
+        mbar_fence_init();
+    }
+    __syncthreads();
     pdl_wait();
     pdl_trigger();
     const int n_active = p.active[p.E];
-    const int tiles = (p.out_rows + MOE_ROWS - 1) / MOE_ROWS;
-    const int items = n_active * tiles;
-    for (int it = blockIdx.x; it < items; it += gridDim.x) {
-        const int e = p.active[it / tiles];
-        const int r = (it % tiles) * MOE_ROWS + tid;
-        const bool row_ok = r < p.out_rows;
-        const int cnt = p.counts[e], p0 = p.offsets[e];
-        const size_t wrow0 = (size_t)e * p.rows_per_expert + (row_ok ? r : 0);
-        const int8_t* w0 = p.wq + wrow0 * K;
-        const uint16_t* d0 = p.wd + wrow0 * nb;
-        const int8_t* w1 = w0 + (size_t)p.out_rows * K;          // up row (gate/up only)
-        const uint16_t* d1 = d0 + (size_t)p.out_rows * nb;
-        for (int g0 = 0; g0 < cnt; g0 += MOE_TG) {
-            const int ng = min(MOE_TG, cnt - g0);
-            __syncthreads();  // the previous group's activations are no longer read
-            for (int i = tid; i < ng * (K / 16); i += MOE_ROWS) {
-                const int tk = i / (K / 16), c = (i % (K / 16)) * 16;
-                const int src = p.gate_up ? p.pair_token[p0 + g0 + tk] : p0 + g0 + tk;
-                cp_async16(sx + (size_t)tk * K + c, p.xq + (size_t)src * K + c, true);
-            }
-            cp_async_commit();
-            for (int i = tid; i < ng * nb; i += MOE_ROWS) {
-                const int tk = i / nb, b = i % nb;
-                const int src = p.gate_up ? p.pair_token[p0 + g0 + tk] : p0 + g0 + tk;
-                sdx[tk * nb + b] = h2f(p.xd[(size_t)src * nb + b]);
-            }
-            cp_async_wait<0>();
-            __syncthreads();
-            float acc0[MOE_TG], acc1[MOE_TG];
-#pragma unroll
-            for (int j = 0; j < MOE_TG; j++) acc0[j] = acc1[j] = 0.0f;
-            if (row_ok) {
-#pragma unroll 2
-                for (int b = 0; b < nb; b++) {
-                    const int4 a0 = __ldcs(reinterpret_cast<const int4*>(w0 + b * 32));
-                    const int4 a1 = __ldcs(reinterpret_cast<const int4*>(w0 + b * 32 + 16));
-                    const float dw0 = h2f(__ldg(d0 + b));
-                    int4 c0 = make_int4(0, 0, 0, 0), c1 = c0;
-                    float dw1 = 0.0f;
-                    if (p.gate_up) {
-                        c0 = __ldcs(reinterpret_cast<const int4*>(w1 + b * 32));
-                        c1 = __ldcs(reinterpret_cast<const int4*>(w1 + b * 32 + 16));
-                        dw1 = h2f(__ldg(d1 + b));
+    const int tiles = p.out_rows / ME_R;
+    const long long items = (long long)n_active * tiles;
+    const long long i0 = items * blockIdx.x / gridDim.x, i1 = items * (blockIdx.x + 1) / gridDim.x;
+
+    if (warp == ME_CONSUMERS) {
+        // ---------------- producer (one lane) ----------------
+        if (lane != 0) return;
+        int it = 0;
+        for (long long item = i0; item < i1; item++) {
+            const int e = p.active[item / tiles];
+            const int r0 = (int)(item % tiles) * ME_R;
+            const int passes = (p.counts[e] + ME_TG - 1) / ME_TG;
+            for (int ps = 0; ps < passes; ps++)
+                for (int c = 0; c < nchunks; c++, it++) {
+                    const int s = it % S;
+                    if (!mbar_wait(&empty[s], ((unsigned)(it / S) & 1u) ^ 1u)) {
+                        atomicCAS(p.err, 0, 21);
+                        return;
                     }
+                    uint8_t* st = sm + (size_t)s * SB;
+                    mbar_expect_tx(&full[s], (unsigned)(NG * (ME_GROUP_W + ME_GROUP_D)));
+                    for (int g = 0; g < NG; g++) {
+                        const int row = e * p.rows_per_expert + g * p.out_rows + r0;
+                        tma_load_2d(st + g * ME_GROUP_W, &mw, c * ME_KC, row, &full[s]);
+                        tma_load_2d(st + g * ME_GROUP_W + ME_BOX, &mw, c * ME_KC + 128, row, &full[s]);
+                        tma_load_2d(st + NG * ME_GROUP_W + g * ME_GROUP_D, &md, c * 8, row, &full[s]);
+                    }
+                }
+        }
+        return;
+    }
+    // ---------------- consumers ----------------
+    const int rq = warp & 3, half = warp >> 2;
+    const int row = rq * 32 + lane;  // row within the item
+    int it = 0, cur_e = -1, cur_g0 = -1;
+    for (long long item = i0; item < i1; item++) {
+        const int e = p.active[item / tiles];
+        const int r0 = (int)(item % tiles) * ME_R;
+        const int cnt = p.counts[e], p0 = p.offsets[e];
+        for (int g0 = 0; g0 < cnt; g0 += ME_TG) {
+            const int ng = min(ME_TG, cnt - g0);
+            if (e != cur_e || g0 != cur_g0) {
+                group_sync<ME_CONSUMERS * 32, 1>();  // nobody still reads the previous tokens
+                for (int i = threadIdx.x; i < ng * (K / 16); i += ME_CONSUMERS * 32) {
+                    const int tk = i / (K / 16), c16 = (i % (K / 16)) * 16;
+                    const int src = GU ? p.pair_token[p0 + g0 + tk] : p0 + g0 + tk;
+                    cp_async16(xs + (size_t)tk * K + c16, p.xq + (size_t)src * K + c16, true);
+                }
+                cp_async_commit();
+                for (int i = threadIdx.x; i < ng * nb; i += ME_CONSUMERS * 32) {
+                    const int tk = i / nb, b = i % nb;
+                    const int src = GU ? p.pair_token[p0 + g0 + tk] : p0 + g0 + tk;
+                    xdf[tk * nb + b] = h2f(p.xd[(size_t)src * nb + b]);
+                }
+                cp_async_wait<0>();
+                group_sync<ME_CONSUMERS * 32, 1>();
+                cur_e = e;
+                cur_g0 = g0;
+            }
+            // this warp's tokens: the first ceil(ng/2) for half 0, the rest for half 1
+            const int h0 = (ng + 1) >> 1;
+            const int tb = half ? h0 : 0, nt = half ? ng - h0 : h0;
+            float ga[ME_TH], ua[ME_TH];
 #pragma unroll
-                    for (int j = 0; j < MOE_TG; j++) {
-                        if (j < ng) {
-                            const int4 x0 = *reinterpret_cast<const int4*>(sx + (size_t)j * K + b * 32);
-                            const int4 x1 = *reinterpret_cast<const int4*>(sx + (size_t)j * K + b * 32 + 16);
-                            const float dx = sdx[j * nb + b];
-                            acc0[j] = __fadd_rn(acc0[j], __fmul_rn((float)dot32(a0, a1, x0, x1), __fmul_rn(dw0, dx)));
-                            if (p.gate_up)
-                                acc1[j] = __fadd_rn(acc1[j],
-                                                    __fmul_rn((float)dot32(c0, c1, x0, x1), __fmul_rn(dw1, dx)));
+            for (int q = 0; q < ME_TH; q++) ga[q] = ua[q] = 0.0f;
+            for (int c = 0; c < nchunks; c++, it++) {
+                const int s = it % S;
+                bool ok = true;
+                if (lane == 0) ok = mbar_wait(&full[s], (unsigned)(it / S) & 1u);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) {
+                    if (lane == 0) atomicCAS(p.err, 0, 22);
+                    return;
+                }
+                const uint8_t* st = sm + (size_t)s * SB;
+                if (nt > 0) {
+                    const int4 dgv = *reinterpret_cast<const int4*>(st + NG * ME_GROUP_W + row * 16);
+                    int4 duv = make_int4(0, 0, 0, 0);
+                    if (GU) duv = *reinterpret_cast<const int4*>(st + NG * ME_GROUP_W + ME_GROUP_D + row * 16);
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const int4 w0 = me_ld(st, row, 2 * j), w1 = me_ld(st, row, 2 * j + 1);
+                        const float dwg = h2f(half_at(dgv, j));
+                        int4 v0 = make_int4(0, 0, 0, 0), v1 = v0;
+                        float dwu = 0.f;
+                        if (GU) {
+                            v0 = me_ld(st + ME_GROUP_W, row, 2 * j);
+                            v1 = me_ld(st + ME_GROUP_W, row, 2 * j + 1);
+                            dwu = h2f(half_at(duv, j));
+                        }
+                        const int blk = c * 8 + j;
+#pragma unroll
+                        for (int q = 0; q < ME_TH; q++) {
+                            if (q < nt) {
+                                const int8_t* xp = xs + (size_t)(tb + q) * K + (size_t)blk * 32;
+                                const int4 x0 = *reinterpret_cast<const int4*>(xp);
+                                const int4 x1 = *reinterpret_cast<const int4*>(xp + 16);
+                                const float dx = xdf[(tb + q) * nb + blk];
+                                ga[q] = __fadd_rn(ga[q], __fmul_rn((float)dot32(w0, w1, x0, x1), __fmul_rn(dwg, dx)));
+                                if (GU)
+                                    ua[q] = __fadd_rn(ua[q],
+                                                      __fmul_rn((float)dot32(v0, v1, x0, x1), __fmul_rn(dwu, dx)));
+                            }
                         }
                     }
                 }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
             }
-            // epilogue per token of the group
+            // epilogue (warp-uniform: nt depends on the warp only)
 #pragma unroll
-            for (int j = 0; j < MOE_TG; j++) {
-                if (j < ng) {
-                    const int pr = p0 + g0 + j;
-                    if (p.gate_up) {
-                        // h = silu(g) * u, quantized per 32 rows (this warp's rows form one block)
-                        const float s = acc0[j] / (1.0f + expf(-acc0[j]));
-                        const float h = row_ok ? __fmul_rn(s, acc1[j]) : 0.0f;
-                        const float amax = warp_max(fabsf(h));
-                        float d, id;
-                        q8_scale(amax, d, id);
-                        if (row_ok) {
-                            p.hq[(size_t)pr * p.out_rows + r] = (int8_t)q8_quant(h, id);
-                            if (lane == 0) p.hd[(size_t)pr * (p.out_rows / 32) + r / 32] = f2h(d);
-                        }
-                    } else if (row_ok) {
-                        p.y[(size_t)pr * p.out_rows + r] = acc0[j];
-                    }
+            for (int q = 0; q < ME_TH; q++) {
+                if (q >= nt) continue;
+                const int pr = p0 + g0 + tb + q;
+                if (GU) {
+                    const float g = ga[q];
+                    const float h = __fmul_rn(g / (1.0f + expf(-g)), ua[q]);
+                    const float amax = warp_max(fabsf(h));
+                    float d, id;
+                    q8_scale(amax, d, id);
+                    p.hq[(size_t)pr * p.out_rows + r0 + row] = (int8_t)q8_quant(h, id);
+                    if (lane == 0) p.hd[(size_t)pr * (p.out_rows / 32) + (r0 + rq * 32) / 32] = f2h(d);
+                } else {
+                    p.y[(size_t)pr * p.out_rows + r0 + row] = ga[q];
                 }
             }
         }
@@ -327,11 +453,45 @@ __global__ void moe_combine_kernel(const float* __restrict__ y, const int32_t* _
 // ---------------------------------------------------------------------------------------
 static size_t al256(size_t b) { return (b + 255) & ~(size_t)255; }
 
+static size_t me_x_bytes(int K) { return (size_t)ME_TG * K + (size_t)ME_TG * (K / 32) * 4; }
+
+template <bool GU>
+static int launch_moe_stream(lq_ctx* ctx, MoeExpertParams p, const int8_t* wq, const uint16_t* wd,
+                             int64_t total_rows) {
+    const size_t sb = (size_t)me_stage_bytes<GU>();
+    const size_t fixed = 2 * ME_MAX_STAGES * 8 + me_x_bytes(p.K) + 1024 /*alignment*/;
+    const size_t budget = 227 * 1024;
+    int stages = (int)std::min<size_t>(GU ? 2 : 4, (budget - fixed) / sb);
+    stages = std::min(stages, ME_MAX_STAGES);
+    if (stages < 2) return set_error(ctx, LQ_ERR_UNSUPPORTED, "moe: K=%d leaves no room for the weight ring", p.K);
+    p.stages = stages;
+    CUtensorMap mw, md;
+    int rc = make_tensor_map_2d(ctx, &mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)p.K, (uint64_t)total_rows,
+                                (uint64_t)p.K, 128, ME_R, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = make_tensor_map_2d(ctx, &md, CU_TENSOR_MAP_DATA_TYPE_UINT16, wd, (uint64_t)(p.K / 32), (uint64_t)total_rows,
+                            (uint64_t)(p.K / 32) * 2, 8, ME_R, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    const size_t smem = (size_t)stages * sb + fixed;
+    static bool attr[2][64] = {};
+    if (ctx->device < 0 || ctx->device >= 64 || !attr[GU][ctx->device]) {
+        LQ_CUDA(ctx, cudaFuncSetAttribute(moe_stream_kernel<GU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)budget));
+        if (ctx->device >= 0 && ctx->device < 64) attr[GU][ctx->device] = true;
+    }
+    int per_sm = 1;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, moe_stream_kernel<GU>, ME_THREADS, smem);
+    per_sm = std::max(1, std::min(per_sm, 2));
+    return launch_kernel(ctx, moe_stream_kernel<GU>, dim3(ctx->sm_count * per_sm), dim3(ME_THREADS), smem,
+                         GU ? "moe_gate_up" : "moe_down", mw, md, p);
+}
+
 size_t moe_scratch_bytes(int64_t rows, int64_t E, int64_t top_k, int64_t H, int64_t inter) {
     const int64_t P = rows * top_k;
     return al256((size_t)P * 4) * 4 /*ids, wts, ids_sorted, w_sorted*/ + al256((size_t)E * 4) /*counts*/ +
-           al256((size_t)(E + 1) * 4) * 2 /*active, offsets*/ + al256((size_t)P * 4) * 2 + al256((size_t)P * inter) +
-           al256((size_t)P * (inter / 32) * 2) + al256((size_t)P * H * 4);
+           al256((size_t)(E + 1) * 4) * 2 /*active, offsets*/ + al256((size_t)P * 4) * 2 /*pair lists*/ +
+           al256((size_t)P * inter) + al256((size_t)P * (inter / 32) * 2) /*h as Q8_0*/ +
+           al256((size_t)P * H * 4) /*y*/;
 }
 
 int launch_moe(lq_ctx* ctx, const lq_q8_tensor* router, const lq_q8_tensor* gate_up, const lq_q8_tensor* down,
@@ -356,14 +516,24 @@ int launch_moe(lq_ctx* ctx, const lq_q8_tensor* router, const lq_q8_tensor* gate
     uint16_t* hd = (uint16_t*)take((size_t)P * (inter / 32) * 2);
     float* y = (float*)take((size_t)P * H * 4);
 
-    const int route_threads = (int)std::max<int64_t>(128, ((E + 31) / 32) * 32);
-    const size_t route_smem = (size_t)H + (size_t)(H / 32) * 4 + (size_t)E * 8;
+    const int route_threads = (int)std::min<int64_t>(1024, std::max<int64_t>(128, E * 8));
+    const size_t route_smem = (size_t)H + (size_t)(H / 32) * 4 + (size_t)E * 8 +
+                              (size_t)(route_threads / 32) * (size_t)(H / 32) * 4;
     int rc = launch_kernel(ctx, moe_route_kernel, dim3((unsigned)rows), dim3(route_threads), route_smem, "moe_route",
                            xq, xd, (int)H, router->qs, router->d, (int)E, (int)top_k, norm_topk,
                            ids_out ? ids_out : ids, w_out ? w_out : wts, ids_sorted, w_sorted);
     if (rc) return rc;
-    rc = launch_kernel(ctx, moe_dispatch_kernel, dim3(1), dim3(1024), 0, "moe_dispatch", (const int32_t*)ids_sorted,
-                       (int)rows, (int)E, (int)top_k, L);
+    const size_t disp_smem = (size_t)rows * top_k * 4;
+    if (disp_smem > 48 * 1024) {
+        static bool dattr[64] = {};
+        if (ctx->device < 0 || ctx->device >= 64 || !dattr[ctx->device]) {
+            LQ_CUDA(ctx, cudaFuncSetAttribute(moe_dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              200 * 1024));
+            if (ctx->device >= 0 && ctx->device < 64) dattr[ctx->device] = true;
+        }
+    }
+    rc = launch_kernel(ctx, moe_dispatch_kernel, dim3(1), dim3(1024), disp_smem, "moe_dispatch",
+                       (const int32_t*)ids_sorted, (int)rows, (int)E, (int)top_k, L);
     if (rc) return rc;
     MoeExpertParams p = {};
     p.E = (int)E;
@@ -371,38 +541,25 @@ int launch_moe(lq_ctx* ctx, const lq_q8_tensor* router, const lq_q8_tensor* gate
     p.offsets = L.offsets;
     p.counts = L.counts;
     p.active = L.active;
-    const int grid = ctx->sm_count * 2;
-    // gate/up -> h (Q8_0)
-    p.wq = gate_up->qs;
-    p.wd = gate_up->d;
+    p.err = ctx->err_flag;
+    // gate/up -> h = silu(g) * u as Q8_0 per pair
     p.rows_per_expert = (int)(2 * inter);
     p.out_rows = (int)inter;
     p.K = (int)H;
-    p.gate_up = 1;
     p.xq = xq;
     p.xd = xd;
     p.hq = hq;
     p.hd = hd;
-    size_t smem = (size_t)MOE_TG * H + (size_t)MOE_TG * (H / 32) * 4;
-    static bool attr[64] = {};
-    if (ctx->device < 0 || ctx->device >= 64 || !attr[ctx->device]) {
-        LQ_CUDA(ctx, cudaFuncSetAttribute(moe_expert_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        if (ctx->device >= 0 && ctx->device < 64) attr[ctx->device] = true;
-    }
-    rc = launch_kernel(ctx, moe_expert_kernel, dim3(grid), dim3(MOE_ROWS), smem, "moe_gate_up", p);
+    rc = launch_moe_stream<true>(ctx, p, gate_up->qs, gate_up->d, gate_up->n);
     if (rc) return rc;
     // down -> y (f32 per pair)
-    p.wq = down->qs;
-    p.wd = down->d;
     p.rows_per_expert = (int)H;
     p.out_rows = (int)H;
     p.K = (int)inter;
-    p.gate_up = 0;
     p.xq = hq;
     p.xd = hd;
     p.y = y;
-    smem = (size_t)MOE_TG * inter + (size_t)MOE_TG * (inter / 32) * 4;
-    rc = launch_kernel(ctx, moe_expert_kernel, dim3(grid), dim3(MOE_ROWS), smem, "moe_down", p);
+    rc = launch_moe_stream<false>(ctx, p, down->qs, down->d, down->n);
     if (rc) return rc;
     return launch_kernel(ctx, moe_combine_kernel, dim3((unsigned)rows), dim3(256), 0, "moe_combine", (const float*)y,
                          (const int32_t*)L.pair_slot, (const float*)w_sorted, (int)top_k, (int)H, resid, out);
@@ -418,15 +575,13 @@ extern "C" int lq_moe_forward(lq_ctx* ctx, const lq_q8_tensor* router, const lq_
     const int64_t E = experts->n_experts, I = experts->inter, H = experts->hidden;
     LQ_REQUIRE(ctx, E > 0 && E <= lq::MOE_MAX_E && top_k > 0 && top_k <= lq::MOE_MAX_K && top_k <= E,
                "lq_moe_forward: need 0 < top_k <= min(E, %d) and E <= %d", lq::MOE_MAX_K, lq::MOE_MAX_E);
-    LQ_REQUIRE(ctx, H > 0 && H % 32 == 0 && I > 0 && I % 32 == 0 && H % 16 == 0,
-               "lq_moe_forward: hidden and inter must be multiples of 32");
+    LQ_REQUIRE(ctx, H > 0 && H % 256 == 0 && H <= 8192 && I > 0 && I % 256 == 0 && I <= 8192,
+               "lq_moe_forward: hidden and inter must be multiples of 256 (at most 8192)");
     LQ_REQUIRE(ctx, router->n == E && router->k == H, "lq_moe_forward: router must be [E][hidden]");
     LQ_REQUIRE(ctx, experts->gate_up.n == E * 2 * I && experts->gate_up.k == H,
                "lq_moe_forward: gate_up must be [E*2*inter][hidden]");
     LQ_REQUIRE(ctx, experts->down.n == E * H && experts->down.k == I, "lq_moe_forward: down must be [E*hidden][inter]");
-    LQ_REQUIRE(ctx, (size_t)8 * H + (size_t)8 * (H / 32) * 4 <= 200 * 1024 && (size_t)8 * I <= 200 * 1024,
-               "lq_moe_forward: hidden/inter too large for the expert kernel");
-    LQ_REQUIRE(ctx, rows >= 0 && rows * top_k < (1ll << 31), "lq_moe_forward: bad rows");
+    LQ_REQUIRE(ctx, rows >= 0 && rows * top_k <= 49152, "lq_moe_forward: rows * top_k must be at most 49152");
     if (rows == 0) return LQ_OK;
     LQ_REQUIRE(ctx, xq && xd && out, "lq_moe_forward: NULL activation");
     const int rc = lq::ensure_scratch(ctx, lq::moe_scratch_bytes(rows, E, top_k, H, I));

@@ -274,8 +274,10 @@ int lq_qwen3_create(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int6
     LQ_REQUIRE(ctx, c.hidden > 0 && c.hidden % 32 == 0 && (moe || (c.inter % 32 == 0 && c.inter > 0)),
                "lq_qwen3_create: hidden and intermediate sizes must be multiples of 32");
     LQ_REQUIRE(ctx, !moe || (c.top_k > 0 && c.top_k <= 16 && c.top_k <= c.n_experts && c.n_experts <= 512 &&
-                             c.moe_inter > 0 && c.moe_inter % 32 == 0 && c.hidden <= 16384),
-               "lq_qwen3_create: MoE needs 0 < top_k <= min(16, n_experts), n_experts <= 512, moe_inter %% 32 == 0");
+                             c.moe_inter > 0 && c.moe_inter % 256 == 0 && c.moe_inter <= 8192 &&
+                             c.hidden % 256 == 0 && c.hidden <= 8192),
+               "lq_qwen3_create: MoE needs 0 < top_k <= min(16, n_experts), n_experts <= 512, hidden and "
+               "moe_inter multiples of 256 (at most 8192)");
     LQ_REQUIRE(ctx, c.n_heads > 0 && c.n_kv_heads > 0 && c.n_heads % c.n_kv_heads == 0 &&
                         c.n_heads / c.n_kv_heads <= 8,
                "lq_qwen3_create: need n_heads %% n_kv_heads == 0 and at most 8 q heads per kv head");
