@@ -246,10 +246,17 @@ def run_ours(args, cfgd, world, rank, local):
     ctx_max = L + W + 2 * K + 8 + 2
     ctx = lq8.Context(local)
     cfg = lq8.make_config(**cfgd)
+    comm = None
+    tp = args.tp if world > 1 else 1
+    if tp > 1:
+        if tp != world:
+            raise SystemExit(f"--tp {tp} needs exactly {tp} ranks (got {world})")
+        comm = lq8.Comm.from_process_group(ctx)
     t_create = time.perf_counter()
-    model = lq8.Qwen3ForCausalLM(ctx, cfg, SEED, max_batch=B, ctx_max=ctx_max)
+    model = lq8.Qwen3ForCausalLM(ctx, cfg, SEED, max_batch=B, ctx_max=ctx_max, comm=comm)
     t_create = time.perf_counter() - t_create
-    rng_stream = 1000 * rank
+    # replicas run their own prompts; a tensor-parallel group shares one batch
+    rng_stream = 1000 * rank if tp == 1 else 0
     from oracle import oracle as O  # seeded token ids only (the generator is shared)
     prompts = np.stack([O.gen_tokens(SEED, rng_stream + b, L, cfgd["vocab"]) for b in range(B)])
     t_pre = time.perf_counter()
@@ -329,7 +336,8 @@ def run_ours(args, cfgd, world, rank, local):
     barrier()
     clk = clocks.stop()
     ms = max_over_ranks(e0.elapsed_time(e1))
-    value = world * B * K / (ms / 1000.0)
+    groups = world // tp
+    value = groups * B * K / (ms / 1000.0)
     launches = model.graph_kernels() * K
 
     # ---- end to end through the host-buffer C-ABI call (e2e)
@@ -346,13 +354,13 @@ def run_ours(args, cfgd, world, rank, local):
     e3.record(stream)
     barrier()
     ms_e2e = max_over_ranks(e2.elapsed_time(e3))
-    e2e = world * B * K / (ms_e2e / 1000.0)
+    e2e = groups * B * K / (ms_e2e / 1000.0)
 
     peak, peak_kind = peaks()
     if cfgd.get("n_experts", 0) > 0:
         roofline, step_gbs, wbytes = moe_step_roofline(cfgd, B, L + W + K, ms / K, peak, peak_kind)
         return finish(args, cfgd, world, rank, L, B, K, W, ms, value, e2e, ms_e2e, clk, launches, roofline,
-                      step_gbs, wbytes, t_create, t_pre, model, ctx, dist)
+                      step_gbs, wbytes, t_create, t_pre, model, ctx, dist, comm)
     # ---- roofline of the dominant kernel: the decode GEMV
     shapes = time_gemv_launches(lq8, ctx, model, cfgd, B)
     tot_b = tot_ms = 0.0
@@ -383,7 +391,7 @@ def run_ours(args, cfgd, world, rank, local):
     wbytes = model.weight_bytes()
     step_gbs = wbytes / (ms / K / 1000) / 1e9
     return finish(args, cfgd, world, rank, L, B, K, W, ms, value, e2e, ms_e2e, clk, launches, roofline, step_gbs,
-                  wbytes, t_create, t_pre, model, ctx, dist)
+                  wbytes, t_create, t_pre, model, ctx, dist, comm)
 
 
 def moe_step_roofline(cfgd, B, ctx_len, step_s_ms, peak, peak_kind):
@@ -409,7 +417,8 @@ def moe_step_roofline(cfgd, B, ctx_len, step_s_ms, peak, peak_kind):
 
 
 def finish(args, cfgd, world, rank, L, B, K, W, ms, value, e2e, ms_e2e, clk, launches, roofline, step_gbs, wbytes,
-           t_create, t_pre, model, ctx, dist):
+           t_create, t_pre, model, ctx, dist, comm=None):
+    tp = comm.world if comm is not None else 1
     # ---- CPU baseline (rank 0, N = 1 only)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -426,12 +435,14 @@ def finish(args, cfgd, world, rank, L, B, K, W, ms, value, e2e, ms_e2e, clk, lau
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
-            "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong" if tp > 1 else "weak",
+            "vs_baseline": None,
             "dtype": "int8/f32",
             "data": "synthetic (seeded random-init N(0,0.02) weights, seeded uniform token ids)",
             "config": {"workload": f"{args.config} greedy decode after a {L}-token prefill, batch {B}",
-                       "model": args.config, "global_batch": B * world, "seq_len": L,
-                       "parallelism": f"dp{world} replicas" if world > 1 else "single GPU",
+                       "model": args.config, "global_batch": B * (world // tp), "seq_len": L,
+                       "parallelism": (f"tp{tp}" + (f" x dp{world // tp}" if world > tp else "")) if tp > 1
+                       else (f"dp{world} replicas" if world > 1 else "single GPU"),
                        "l2": "no flush: each step streams the Q8_0 weights (GBs, far above the 126 MB L2)",
                        "context_range": [L + W, L + W + K]},
             "roofline": roofline,
@@ -445,7 +456,9 @@ def finish(args, cfgd, world, rank, L, B, K, W, ms, value, e2e, ms_e2e, clk, lau
             "setup_s": {"create": t_create, "prefill": t_pre},
         }
         print(json.dumps(line), flush=True)
-    model.close()
+    model.close()  # releases the decode graph (it holds NCCL calls) before the communicator
+    if comm is not None:
+        comm.close()
     ctx.close()
     if dist is not None:
         dist.barrier()
@@ -597,6 +610,8 @@ def main():
     ap.add_argument("--sweep-case", default="",
                     help="with --sweep: one case 'm,n,k' (two weight copies; for profiling)")
     ap.add_argument("--sweep-reps", type=int, default=20)
+    ap.add_argument("--tp", type=int, default=1,
+                    help="tensor parallelism over the torchrun ranks (NCCL); 1 = independent replicas")
     ap.add_argument("--moe", action="store_true",
                     help="time lq_moe_forward alone at the Qwen3-30B-A3B expert shape and exit")
     ap.add_argument("--moe-rows", default="1,8,64,512")

@@ -178,6 +178,26 @@ int lq_fill_bf16(lq_ctx* ctx, uint64_t seed, uint64_t tensor_id, int64_t offset,
                  double std_dev, uint16_t* out_dev);
 
 /* ---------------------------------------------------------------------------------------
+ * Tensor parallelism over NCCL (one process per GPU; the reference is single-device).
+ * NCCL is opened at run time (libnccl.so.2). Rank 0 creates the id, the host hands it to the
+ * other ranks (e.g. torch.distributed), every rank calls lq_comm_init on its own context.
+ * Collectives run on the context's stream.
+ * ------------------------------------------------------------------------------------- */
+#define LQ_COMM_ID_BYTES 128
+typedef struct lq_comm lq_comm;
+int lq_comm_unique_id(lq_ctx* ctx, uint8_t* id_out /* [LQ_COMM_ID_BYTES] */);
+int lq_comm_init(lq_ctx* ctx, const uint8_t* id, int rank, int world, lq_comm** out);
+int lq_comm_destroy(lq_comm* comm);
+int lq_comm_rank(lq_comm* comm, int* rank, int* world);
+/* in-place sum over the ranks of buf_dev [count] f32 */
+int lq_comm_allreduce_f32(lq_comm* comm, float* buf_dev, int64_t count);
+/* Row-parallel Linear (o_proj / down_proj under TP): w is this rank's K-slice [n][k/world]
+ * (whole Q8_0 blocks), x this rank's Q8_0 slice [m][k/world]; y [m][n] f32 = residual
+ * (may be NULL, may equal y) + the sum over ranks of x_r . w_r^T. */
+int lq_q8_0_matmul_allreduce(lq_ctx* ctx, lq_comm* comm, const lq_q8_tensor* w, const int8_t* xq_dev,
+                             const uint16_t* xd_dev, int64_t m, float* y_dev, const float* residual_dev);
+
+/* ---------------------------------------------------------------------------------------
  * Mixture of experts (Qwen3-MoE sparse MLP). The reference has no MoE code (its architecture
  * notes plan one); this follows the Qwen3-MoE sparse block so that a MoE checkpoint's layer
  * is one call: router logits x.R^T (Q8_0), softmax, top_k experts by logit (ties -> lower
@@ -221,6 +241,13 @@ typedef struct {
  * for max_batch sequences of ctx_max positions. */
 int lq_qwen3_create(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int64_t max_batch,
                     int64_t ctx_max, lq_model** out);
+/* Tensor-parallel shard of the same model on this rank of comm: q/k/v and gate/up split by
+ * output rows (heads, intermediate), o and down by K (whole Q8_0 blocks) followed by a sum
+ * all-reduce, the LM head by vocabulary rows with a global greedy argmax (ties -> highest
+ * index). Needs n_heads, n_kv_heads, inter/32 and vocab divisible by the world size and an
+ * untied LM head; dense models only. Every rank makes the same calls with the same ids. */
+int lq_qwen3_create_tp(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int64_t max_batch,
+                       int64_t ctx_max, lq_comm* comm, lq_model** out);
 int lq_qwen3_destroy(lq_model* model);
 /* clear_kv_cache (model.rs:396) */
 int lq_qwen3_reset(lq_model* model);

@@ -1,0 +1,171 @@
+// lq8_comm.cu -- NCCL communicator for tensor parallelism (one process per GPU).
+//
+// NCCL is opened at run time (dlopen of libnccl.so.2): the library loads without it, and a
+// process that already loaded NCCL (PyTorch's) shares that copy. The bootstrap is NCCL's own:
+// rank 0 makes a unique id (lq_comm_unique_id), the host side hands it to the other ranks
+// (e.g. torch.distributed over gloo), every rank calls lq_comm_init. Collectives run on the
+// context's stream, so they order with the kernels and can be captured in the decode graph.
+#include "lq8_internal.cuh"
+
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cstring>
+#include <mutex>
+
+struct lq_comm {
+    lq_ctx* ctx = nullptr;
+    ncclComm_t comm = nullptr;
+    int rank = 0, world = 1;
+};
+
+namespace lq {
+
+struct NcclApi {
+    bool ok = false;
+    ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                               cudaStream_t) = nullptr;
+    ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    const char* (*error_string)(ncclResult_t) = nullptr;
+};
+
+static NcclApi& nccl() {
+    static NcclApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return;
+        api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+        api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+        api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+        api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+        api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
+        api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
+        api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.all_reduce && api.all_gather &&
+                 api.error_string;
+    });
+    return api;
+}
+
+static int nccl_check(lq_ctx* ctx, ncclResult_t r, const char* what) {
+    if (r == ncclSuccess) return LQ_OK;
+    return set_error(ctx, LQ_ERR_NCCL, "%s: %s", what, nccl().error_string ? nccl().error_string(r) : "NCCL error");
+}
+
+// (callers pass a valid communicator)
+int comm_allreduce_sum_f32(lq_comm* c, const float* send, float* recv, int64_t count) {
+    if (c->world == 1) {
+        if (send != recv)
+            LQ_CUDA(c->ctx, cudaMemcpyAsync(recv, send, (size_t)count * 4, cudaMemcpyDeviceToDevice, c->ctx->stream));
+        return LQ_OK;
+    }
+    return nccl_check(c->ctx, nccl().all_reduce(send, recv, (size_t)count, ncclFloat32, ncclSum, c->comm, c->ctx->stream),
+                      "ncclAllReduce");
+}
+
+int comm_allreduce_max_u64(lq_comm* c, unsigned long long* buf, int64_t count) {
+    if (c->world == 1) return LQ_OK;
+    return nccl_check(c->ctx, nccl().all_reduce(buf, buf, (size_t)count, ncclUint64, ncclMax, c->comm, c->ctx->stream),
+                      "ncclAllReduce(max)");
+}
+
+int comm_allgather_f32(lq_comm* c, const float* send, float* recv, int64_t count) {
+    if (c->world == 1) {
+        LQ_CUDA(c->ctx, cudaMemcpyAsync(recv, send, (size_t)count * 4, cudaMemcpyDeviceToDevice, c->ctx->stream));
+        return LQ_OK;
+    }
+    return nccl_check(c->ctx, nccl().all_gather(send, recv, (size_t)count, ncclFloat32, c->comm, c->ctx->stream),
+                      "ncclAllGather");
+}
+
+int comm_rank(const lq_comm* c) { return c ? c->rank : 0; }
+int comm_world(const lq_comm* c) { return c ? c->world : 1; }
+lq_ctx* comm_ctx(const lq_comm* c) { return c ? c->ctx : nullptr; }
+
+}  // namespace lq
+
+extern "C" {
+
+int lq_comm_unique_id(lq_ctx* ctx, uint8_t* id_out) {
+    LQ_ENTRY(ctx, "lq_comm_unique_id");
+    LQ_REQUIRE(ctx, id_out, "lq_comm_unique_id: NULL output");
+    if (!lq::nccl().ok) return lq::set_error(ctx, LQ_ERR_UNSUPPORTED, "lq_comm_unique_id: libnccl.so.2 not found");
+    ncclUniqueId id;
+    int rc = lq::nccl_check(ctx, lq::nccl().get_unique_id(&id), "ncclGetUniqueId");
+    if (rc) return rc;
+    static_assert(sizeof(ncclUniqueId) == LQ_COMM_ID_BYTES, "NCCL unique id size");
+    memcpy(id_out, &id, sizeof id);
+    return LQ_OK;
+}
+
+int lq_comm_init(lq_ctx* ctx, const uint8_t* id, int rank, int world, lq_comm** out) {
+    LQ_ENTRY(ctx, "lq_comm_init");
+    LQ_REQUIRE(ctx, id && out, "lq_comm_init: NULL argument");
+    LQ_REQUIRE(ctx, world >= 1 && rank >= 0 && rank < world, "lq_comm_init: rank %d of %d", rank, world);
+    *out = nullptr;
+    lq_comm* c = new lq_comm();
+    c->ctx = ctx;
+    c->rank = rank;
+    c->world = world;
+    if (world > 1) {
+        if (!lq::nccl().ok) {
+            delete c;
+            return lq::set_error(ctx, LQ_ERR_UNSUPPORTED, "lq_comm_init: libnccl.so.2 not found");
+        }
+        ncclUniqueId uid;
+        memcpy(&uid, id, sizeof uid);
+        cudaSetDevice(ctx->device);
+        int rc = lq::nccl_check(ctx, lq::nccl().comm_init_rank(&c->comm, world, uid, rank), "ncclCommInitRank");
+        if (rc) {
+            delete c;
+            return rc;
+        }
+    }
+    *out = c;
+    return LQ_OK;
+}
+
+int lq_comm_destroy(lq_comm* comm) {
+    if (!comm) return LQ_ERR_INVALID_ARG;
+    if (comm->comm) {
+        cudaStreamSynchronize(comm->ctx->stream);
+        lq::nccl().comm_destroy(comm->comm);
+    }
+    delete comm;
+    return LQ_OK;
+}
+
+int lq_comm_rank(lq_comm* comm, int* rank, int* world) {
+    if (!comm || !rank || !world) return LQ_ERR_INVALID_ARG;
+    *rank = comm->rank;
+    *world = comm->world;
+    return LQ_OK;
+}
+
+int lq_q8_0_matmul_allreduce(lq_ctx* ctx, lq_comm* comm, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd,
+                             int64_t m, float* y, const float* residual) {
+    LQ_ENTRY(ctx, "lq_q8_0_matmul_allreduce");
+    LQ_REQUIRE(ctx, comm && comm->ctx == ctx, "lq_q8_0_matmul_allreduce: communicator of another context");
+    LQ_REQUIRE(ctx, w && w->n > 0 && w->k > 0 && w->k % 32 == 0 && w->qs && w->d,
+               "lq_q8_0_matmul_allreduce: bad weight shard");
+    LQ_REQUIRE(ctx, m >= 0 && (m == 0 || (xq && xd && y)), "lq_q8_0_matmul_allreduce: bad activations");
+    if (m == 0) return LQ_OK;
+    // rank 0 folds the residual into its partial; the sum over ranks is residual + x.W^T
+    int rc = lq::launch_q8_matmul(ctx, w, xq, xd, m, y, comm->rank == 0 ? residual : nullptr, w->n, nullptr);
+    if (rc) return rc;
+    return lq::comm_allreduce_sum_f32(comm, y, y, m * w->n);
+}
+
+int lq_comm_allreduce_f32(lq_comm* comm, float* buf, int64_t count) {
+    if (!comm) return LQ_ERR_INVALID_ARG;
+    LQ_ENTRY(comm->ctx, "lq_comm_allreduce_f32");
+    LQ_REQUIRE(comm->ctx, count >= 0 && (count == 0 || buf), "lq_comm_allreduce_f32: bad buffer");
+    if (count == 0) return LQ_OK;
+    return lq::comm_allreduce_sum_f32(comm, buf, buf, count);
+}
+
+}  // extern "C"

@@ -211,6 +211,9 @@ int launch_attention_decode_fused(lq_ctx* ctx, const float* qkv, const uint16_t*
                                   int8_t* xq, uint16_t* xd, void* scratch);
 int launch_fill_bf16(lq_ctx* ctx, uint64_t seed, uint64_t tid, int64_t offset, int64_t count,
                      float scale, uint16_t* out);
+// rows x cols slice, at (row0, col0), of the generated tensor `tid` whose rows are src_ld long
+int launch_fill_bf16_2d(lq_ctx* ctx, uint64_t seed, uint64_t tid, int64_t rows, int64_t cols, int64_t src_ld,
+                        int64_t row0, int64_t col0, float scale, uint16_t* out);
 int launch_fill_norm(lq_ctx* ctx, uint64_t seed, uint64_t tid, int64_t count, float norm_std,
                      uint16_t* out);
 int launch_argmax_finalize(lq_ctx* ctx, unsigned long long* keys, int64_t rows, int32_t* out,
@@ -220,6 +223,15 @@ bool attention_prefill_supported(int64_t L, int64_t Hq, int64_t Hkv);
 int launch_attention_prefill(lq_ctx* ctx, const float* q, const float* kc, const float* vc, int64_t B, int64_t Hq,
                              int64_t Hkv, int64_t L, int64_t pos0, const int32_t* pos0_dev, int64_t ctx_max,
                              float* out, int8_t* xq, uint16_t* xd);
+// tensor-parallel collectives on the communicator's context stream (lq8_comm.cu)
+int comm_allreduce_sum_f32(lq_comm* c, const float* send, float* recv, int64_t count);
+int comm_allreduce_max_u64(lq_comm* c, unsigned long long* buf, int64_t count);
+int comm_allgather_f32(lq_comm* c, const float* send, float* recv, int64_t count);
+int comm_rank(const lq_comm* c);
+int comm_world(const lq_comm* c);
+lq_ctx* comm_ctx(const lq_comm* c);
+// add `offset` to the index half of the non-zero argmax keys (a vocabulary shard's base)
+int launch_keys_offset(lq_ctx* ctx, unsigned long long* keys, int64_t n, int64_t offset);
 // Qwen3-MoE sparse MLP (router, top-k, grouped expert GEMVs, combine); scratch from
 // moe_scratch_bytes for `rows` tokens
 size_t moe_scratch_bytes(int64_t rows, int64_t E, int64_t top_k, int64_t H, int64_t inter);

@@ -207,6 +207,17 @@ __global__ void add_kernel(const float* a, const float* b, int64_t n, float* out
         out[i] = __fadd_rn(a[i], b[i]);
 }
 
+__global__ void keys_offset_kernel(unsigned long long* keys, int64_t n, long long offset) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n && keys[i]) keys[i] += (unsigned long long)offset;
+}
+
+int launch_keys_offset(lq_ctx* ctx, unsigned long long* keys, int64_t n, int64_t offset) {
+    if (n <= 0 || offset == 0) return LQ_OK;
+    return launch_kernel(ctx, keys_offset_kernel, dim3((unsigned)ceil_div(n, 128)), dim3(128), 0, "keys_offset", keys, n,
+                         (long long)offset);
+}
+
 }  // namespace lq
 
 // =========================================================================================

@@ -472,6 +472,16 @@ __global__ void fill_bf16_kernel(uint64_t key, int64_t offset, int64_t count, fl
         out[i] = f32_to_bf16(gen_value(key, (uint64_t)(offset + i), scale));
 }
 
+// rows x cols slice of a [*][src_ld] generated tensor starting at (row0, col0)
+__global__ void fill_bf16_2d_kernel(uint64_t key, int64_t rows, int64_t cols, int64_t src_ld, int64_t row0,
+                                    int64_t col0, float scale, uint16_t* __restrict__ out) {
+    const int64_t count = rows * cols;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / cols, c = i - (i / cols) * cols;
+        out[i] = f32_to_bf16(gen_value(key, (uint64_t)((row0 + r) * src_ld + col0 + c), scale));
+    }
+}
+
 __global__ void fill_norm_kernel(uint64_t key, int64_t count, float scale, int unit,
                                  uint16_t* __restrict__ out) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count;
@@ -485,6 +495,16 @@ int launch_fill_bf16(lq_ctx* ctx, uint64_t seed, uint64_t tid, int64_t offset, i
     int grid = (int)std::min<int64_t>((count + 255) / 256, (int64_t)ctx->sm_count * 32);
     fill_bf16_kernel<<<grid, 256, 0, ctx->stream>>>(gen_key(seed, tid), offset, count, scale, out);
     LQ_LAUNCH_CHECK(ctx, "fill_bf16");
+    return LQ_OK;
+}
+
+int launch_fill_bf16_2d(lq_ctx* ctx, uint64_t seed, uint64_t tid, int64_t rows, int64_t cols, int64_t src_ld,
+                        int64_t row0, int64_t col0, float scale, uint16_t* out) {
+    const int64_t count = rows * cols;
+    if (count <= 0) return LQ_OK;
+    int grid = (int)std::min<int64_t>((count + 255) / 256, (int64_t)ctx->sm_count * 32);
+    fill_bf16_2d_kernel<<<grid, 256, 0, ctx->stream>>>(gen_key(seed, tid), rows, cols, src_ld, row0, col0, scale, out);
+    LQ_LAUNCH_CHECK(ctx, "fill_bf16_2d");
     return LQ_OK;
 }
 

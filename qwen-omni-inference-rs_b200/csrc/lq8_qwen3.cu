@@ -60,6 +60,12 @@ struct lq_model {
     size_t att_scratch_bytes = 0;
     void* moe_scratch = nullptr;         // MoE layers: route/dispatch/expert buffers for rows_cap
     bool moe = false;
+    // tensor parallelism: this rank's shard sizes (the whole model when tp == 1)
+    lq_comm* comm = nullptr;
+    int tp = 1, rank = 0;
+    int64_t Hq_l = 0, Hkv_l = 0, I_l = 0, V_l = 0, vocab_off = 0;
+    float* part = nullptr;       // row-parallel partial sums [rows][H] (tp > 1)
+    float* logits_all = nullptr; // gathered logits [tp][max_batch][V_l] (tp > 1)
     unsigned long long* keys = nullptr;  // argmax keys [max_batch]
     int32_t* tokens = nullptr;           // [rows_cap]
     int32_t* pos_dev = nullptr;
@@ -103,15 +109,16 @@ lq_q8_tensor rows_view(const lq_q8_tensor& t, int64_t r0, int64_t n) {
     return v;
 }
 
-// generate bf16 weights for tensor id `tid` ([n][k]) and quantize into rows [r0, r0+n) of dst
+// generate bf16 weights for tensor id `tid` (rows [src_r0, src_r0+n) of a [*][k] tensor) and
+// quantize into rows [r0, r0+n) of dst
 int gen_linear(lq_model* m, uint16_t* tmp, size_t tmp_elems, uint64_t seed, uint64_t tid,
-               const lq_q8_tensor& dst, int64_t r0, int64_t n) {
+               const lq_q8_tensor& dst, int64_t r0, int64_t n, int64_t src_r0 = 0) {
     float sc = lq::gen_scale(m->c.init_std);
     int64_t k = dst.k;
     int64_t chunk_rows = std::max<int64_t>(1, (int64_t)(tmp_elems / (size_t)k));
     for (int64_t r = 0; r < n; r += chunk_rows) {
         int64_t rows = std::min(chunk_rows, n - r);
-        int rc = lq::launch_fill_bf16(m->ctx, seed, tid, r * k, rows * k, sc, tmp);
+        int rc = lq::launch_fill_bf16(m->ctx, seed, tid, (src_r0 + r) * k, rows * k, sc, tmp);
         if (rc) return rc;
         rc = lq::launch_quantize_rows(m->ctx, tmp, LQ_DTYPE_BF16, rows, k, dst.qs + (r0 + r) * k,
                                       dst.d + (r0 + r) * (k / 32));
@@ -130,6 +137,39 @@ int moe_mlp(lq_model* m, const Layer& ly, int64_t rows) {
                           c.norm_topk, m->xq, m->xd, rows, c.hidden, m->x, m->x, m->moe_scratch, nullptr, nullptr);
 }
 
+// columns [col0, col0 + dst.k) of every row of the [dst.n][src_k] tensor `tid` (a K-slice for
+// a row-parallel shard; col0 and dst.k are whole Q8_0 blocks, so the blocks are the full
+// tensor's blocks)
+int gen_linear_cols(lq_model* m, uint16_t* tmp, size_t tmp_elems, uint64_t seed, uint64_t tid, const lq_q8_tensor& dst,
+                    int64_t src_k, int64_t col0) {
+    float sc = lq::gen_scale(m->c.init_std);
+    const int64_t k = dst.k, n = dst.n;
+    int64_t chunk_rows = std::max<int64_t>(1, (int64_t)(tmp_elems / (size_t)k));
+    for (int64_t r = 0; r < n; r += chunk_rows) {
+        int64_t rows = std::min(chunk_rows, n - r);
+        int rc = lq::launch_fill_bf16_2d(m->ctx, seed, tid, rows, k, src_k, r, col0, sc, tmp);
+        if (rc) return rc;
+        rc = lq::launch_quantize_rows(m->ctx, tmp, LQ_DTYPE_BF16, rows, k, dst.qs + r * k, dst.d + r * (k / 32));
+        if (rc) return rc;
+    }
+    return LQ_OK;
+}
+
+// row-parallel output: y = x + partial on one rank, the sum over ranks into x
+inline float* rp_out(lq_model* m) { return m->tp > 1 ? m->part : m->x; }
+inline const float* rp_resid(lq_model* m) { return (m->tp > 1 && m->rank != 0) ? nullptr : m->x; }
+inline int rp_reduce(lq_model* m, int64_t rows) {
+    if (m->tp == 1) return LQ_OK;
+    return lq::comm_allreduce_sum_f32(m->comm, m->part, m->x, rows * m->c.hidden);
+}
+// greedy argmax over the vocabulary shards: global indices, max over ranks
+inline int lm_keys_reduce(lq_model* m, int64_t B) {
+    if (m->tp == 1) return LQ_OK;
+    int rc = lq::launch_keys_offset(m->ctx, m->keys, B, m->vocab_off);
+    if (rc) return rc;
+    return lq::comm_allreduce_max_u64(m->comm, m->keys, B);
+}
+
 void destroy_graph(lq_model* m) {
     if (m->exec) cudaGraphExecDestroy(m->exec);
     m->exec = nullptr;
@@ -142,7 +182,7 @@ void destroy_graph(lq_model* m) {
 int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_dev, bool bump_pos) {
     lq_ctx* ctx = m->ctx;
     const lq_qwen3_config& c = m->c;
-    const int64_t H = c.hidden, D = c.head_dim, Hq = c.n_heads, Hkv = c.n_kv_heads, I = c.inter;
+    const int64_t H = c.hidden, D = c.head_dim, Hq = m->Hq_l, Hkv = m->Hkv_l, I = m->I_l;
     const int64_t rows = B * L;
     int rc;
 #define RC(expr) do { rc = (expr); if (rc) return rc; } while (0)
@@ -158,16 +198,19 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
             RC(lq::launch_gemv_norm(ctx, &ly.qkv, m->x, ly.in_norm, c.eps, B, m->qkv, nullptr, m->Nqkv, nullptr));
             RC(lq::launch_attention_decode_fused(ctx, m->qkv, ly.q_norm, ly.k_norm, c.eps, m->cos_t, m->sin_t, kc, vc,
                                                  B, Hq, Hkv, pos_dev, m->ctx_max, m->xq, m->xd, m->att_scratch));
-            RC(lq::launch_gemv_stream(ctx, &ly.o, m->xq, m->xd, B, m->x, m->x, H, nullptr));
+            RC(lq::launch_gemv_stream(ctx, &ly.o, m->xq, m->xd, B, rp_out(m), rp_resid(m), H, nullptr));
+            RC(rp_reduce(m, B));
             if (m->moe) {
                 RC(moe_mlp(m, ly, B));
                 continue;
             }
             RC(lq::launch_gemv_norm_swiglu(ctx, &ly.gate_up, m->x, ly.post_norm, c.eps, B, m->gu, I));
-            RC(lq::launch_gemv_quant(ctx, &ly.down, m->gu, B, m->x, m->x, H));
+            RC(lq::launch_gemv_quant(ctx, &ly.down, m->gu, B, rp_out(m), rp_resid(m), H));
+            RC(rp_reduce(m, B));
         }
-        RC(lq::launch_gemv_norm(ctx, &m->lm_head, m->x, m->final_norm, c.eps, B, m->logits, nullptr, c.vocab,
+        RC(lq::launch_gemv_norm(ctx, &m->lm_head, m->x, m->final_norm, c.eps, B, m->logits, nullptr, m->V_l,
                                 m->keys));
+        RC(lm_keys_reduce(m, B));
         RC(lq::launch_argmax_finalize(ctx, m->keys, B, m->tokens, bump_pos ? m->pos_dev : nullptr));
         return LQ_OK;
     }
@@ -195,7 +238,8 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
             }
         }
         // o_proj + residual (transformer.rs:194)
-        RC(lq::launch_q8_matmul(ctx, &ly.o, m->xq, m->xd, rows, m->x, m->x, H, nullptr));
+        RC(lq::launch_q8_matmul(ctx, &ly.o, m->xq, m->xd, rows, rp_out(m), rp_resid(m), H, nullptr));
+        RC(rp_reduce(m, rows));
         if (m->moe) {
             RC(moe_mlp(m, ly, rows));
             continue;
@@ -204,7 +248,8 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
         RC(lq::launch_rmsnorm(ctx, m->x, LQ_DTYPE_F32, rows, H, ly.post_norm, c.eps, nullptr, m->xq, m->xd));
         RC(lq::launch_q8_matmul(ctx, &ly.gate_up, m->xq, m->xd, rows, m->gu, nullptr, 2 * I, nullptr));
         RC(lq::launch_silu_mul(ctx, m->gu, rows, I, nullptr, m->xq, m->xd));
-        RC(lq::launch_q8_matmul(ctx, &ly.down, m->xq, m->xd, rows, m->x, m->x, H, nullptr));
+        RC(lq::launch_q8_matmul(ctx, &ly.down, m->xq, m->xd, rows, rp_out(m), rp_resid(m), H, nullptr));
+        RC(rp_reduce(m, rows));
     }
     // final norm on the last row of each sequence (model.rs:194, :357-358)
     const float* xlast = m->x;
@@ -215,7 +260,8 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
     }
     RC(lq::launch_rmsnorm(ctx, xlast, LQ_DTYPE_F32, B, H, m->final_norm, c.eps, nullptr, m->xq, m->xd));
     // LM head with the greedy argmax fused into its epilogue
-    RC(lq::launch_q8_matmul(ctx, &m->lm_head, m->xq, m->xd, B, m->logits, nullptr, c.vocab, m->keys));
+    RC(lq::launch_q8_matmul(ctx, &m->lm_head, m->xq, m->xd, B, m->logits, nullptr, m->V_l, m->keys));
+    RC(lm_keys_reduce(m, B));
     RC(lq::launch_argmax_finalize(ctx, m->keys, B, m->tokens, bump_pos ? m->pos_dev : nullptr));
 #undef RC
     return LQ_OK;
@@ -263,11 +309,11 @@ int lq_qwen3_destroy(lq_model* m) {
     return LQ_OK;
 }
 
-int lq_qwen3_create(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int64_t max_batch, int64_t ctx_max,
-                    lq_model** out) {
-    LQ_ENTRY(ctx, "lq_qwen3_create");
+static int create_model(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int64_t max_batch, int64_t ctx_max,
+                        lq_comm* comm, lq_model** out) {
     LQ_REQUIRE(ctx, cfg && out, "lq_qwen3_create: NULL argument");
     *out = nullptr;
+    const int T = lq::comm_world(comm), rank = lq::comm_rank(comm);
     const lq_qwen3_config& c = *cfg;
     LQ_REQUIRE(ctx, c.head_dim == 128, "lq_qwen3_create: head_dim must be 128");
     const bool moe = c.n_experts > 0;
@@ -285,15 +331,29 @@ int lq_qwen3_create(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int6
     LQ_REQUIRE(ctx, c.max_pos <= 0 || ctx_max <= c.max_pos, "lq_qwen3_create: ctx_max exceeds max_pos");
     LQ_REQUIRE(ctx, ctx_max <= lq::attention_max_ctx(), "lq_qwen3_create: ctx_max %lld exceeds %d",
                (long long)ctx_max, lq::attention_max_ctx());
+    LQ_REQUIRE(ctx, !comm || lq::comm_ctx(comm) == ctx, "lq_qwen3_create_tp: communicator of another context");
+    LQ_REQUIRE(ctx, T == 1 || (!moe && !c.tied && c.n_heads % T == 0 && c.n_kv_heads % T == 0 &&
+                               c.inter % (32 * T) == 0 && c.vocab % T == 0),
+               "lq_qwen3_create_tp: %d ranks need a dense untied model with n_heads, n_kv_heads, inter/32 and "
+               "vocab divisible by the world size", T);
 
     lq_model* m = new lq_model();
+    m->comm = comm;
+    m->tp = T;
+    m->rank = rank;
     m->ctx = ctx;
     m->c = c;
     m->max_batch = max_batch;
     m->ctx_max = ctx_max;
     m->moe = moe;
-    const int64_t H = c.hidden, D = c.head_dim, Hq = c.n_heads, Hkv = c.n_kv_heads, V = c.vocab;
-    const int64_t I = moe ? c.moe_inter : c.inter, E = moe ? c.n_experts : 0;
+    // this rank's shard (the whole model when T == 1)
+    const int64_t H = c.hidden, D = c.head_dim, Hq = c.n_heads / T, Hkv = c.n_kv_heads / T, V = c.vocab;
+    const int64_t I = moe ? c.moe_inter : c.inter / T, E = moe ? c.n_experts : 0, Vl = V / T;
+    m->Hq_l = Hq;
+    m->Hkv_l = Hkv;
+    m->I_l = I;
+    m->V_l = Vl;
+    m->vocab_off = (int64_t)rank * Vl;
     m->Nq = Hq * D;
     m->Nk = Hkv * D;
     m->Nqkv = m->Nq + 2 * m->Nk;
@@ -325,7 +385,7 @@ int lq_qwen3_create(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int6
     }
     RC(dalloc_t(m, &m->embed, (size_t)(V * H)));
     RC(dalloc_t(m, &m->final_norm, (size_t)H));
-    RC(alloc_q8(m, &m->lm_head, V, H));
+    RC(alloc_q8(m, &m->lm_head, Vl, H));
     // generation scratch: the largest single weight, capped at 64 Mi elements
     size_t tmp_elems = (size_t)std::min<int64_t>(std::max({I * H, m->Nq * H, H * m->Hqd}), 64ll << 20);
     uint16_t* tmp = nullptr;
@@ -333,10 +393,12 @@ int lq_qwen3_create(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int6
     const float sc = lq::gen_scale(c.init_std);
     for (int64_t l = 0; l < c.layers; l++) {
         Layer& ly = m->layers[(size_t)l];
-        RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_Q), ly.qkv, 0, m->Nq));
-        RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_K), ly.qkv, m->Nq, m->Nk));
-        RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_V), ly.qkv, m->Nq + m->Nk, m->Nk));
-        RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_O), ly.o, 0, H));
+        // column-parallel q/k/v: this rank's heads; row-parallel o: its heads' K columns
+        RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_Q), ly.qkv, 0, m->Nq, rank * m->Nq));
+        RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_K), ly.qkv, m->Nq, m->Nk, rank * m->Nk));
+        RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_V), ly.qkv, m->Nq + m->Nk, m->Nk, rank * m->Nk));
+        if (T > 1) RC(gen_linear_cols(m, tmp, tmp_elems, seed, tid_layer(l, K_O), ly.o, c.n_heads * D, rank * m->Hqd));
+        else RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_O), ly.o, 0, H));
         if (moe) {
             RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_ROUTER), ly.router, 0, E));
             for (int64_t e = 0; e < E; e++) {
@@ -345,9 +407,10 @@ int lq_qwen3_create(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int6
                 RC(gen_linear(m, tmp, tmp_elems, seed, tid_expert(l, e, 2), ly.moe_down, e * H, H));
             }
         } else {
-            RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_GATE), ly.gate_up, 0, I));
-            RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_UP), ly.gate_up, I, I));
-            RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_DOWN), ly.down, 0, H));
+            RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_GATE), ly.gate_up, 0, I, rank * I));
+            RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_UP), ly.gate_up, I, I, rank * I));
+            if (T > 1) RC(gen_linear_cols(m, tmp, tmp_elems, seed, tid_layer(l, K_DOWN), ly.down, c.inter, rank * I));
+            else RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_DOWN), ly.down, 0, H));
         }
         RC(lq::launch_fill_norm(ctx, seed, tid_layer(l, K_QNORM), D, c.norm_std, ly.q_norm));
         RC(lq::launch_fill_norm(ctx, seed, tid_layer(l, K_KNORM), D, c.norm_std, ly.k_norm));
@@ -360,7 +423,7 @@ int lq_qwen3_create(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int6
         // tied embeddings: the LM head is the Q8_0 quantization of the bf16 table
         RC(lq::launch_quantize_rows(ctx, m->embed, LQ_DTYPE_BF16, V, H, m->lm_head.qs, m->lm_head.d));
     } else {
-        RC(gen_linear(m, tmp, tmp_elems, seed, TID_LMHEAD, m->lm_head, 0, V));
+        RC(gen_linear(m, tmp, tmp_elems, seed, TID_LMHEAD, m->lm_head, 0, Vl, rank * Vl));
     }
     // caches and activations
     size_t kv = (size_t)(c.layers * max_batch * Hkv * ctx_max * D);
@@ -378,7 +441,11 @@ int lq_qwen3_create(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int6
     RC(dalloc_t(m, &m->qkv, (size_t)(R * m->Nqkv)));
     RC(dalloc_t(m, &m->q_rot, (size_t)(R * m->Hqd)));
     RC(dalloc_t(m, &m->gu, (size_t)(R * 2 * I)));
-    RC(dalloc_t(m, &m->logits, (size_t)(max_batch * V)));
+    RC(dalloc_t(m, &m->logits, (size_t)(max_batch * Vl)));
+    if (T > 1) {
+        RC(dalloc_t(m, &m->part, (size_t)(R * H)));
+        RC(dalloc_t(m, &m->logits_all, (size_t)(T * max_batch * Vl)));
+    }
     RC(dalloc_t(m, &m->keys, (size_t)max_batch));
     RC(dalloc_t(m, &m->tokens, (size_t)R));
     RC(dalloc_t(m, &m->pos_dev, 1));
@@ -406,6 +473,36 @@ int lq_qwen3_create(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int6
     return LQ_OK;
 }
 
+int lq_qwen3_create(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int64_t max_batch, int64_t ctx_max,
+                    lq_model** out) {
+    LQ_ENTRY(ctx, "lq_qwen3_create");
+    return create_model(ctx, cfg, seed, max_batch, ctx_max, nullptr, out);
+}
+
+int lq_qwen3_create_tp(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int64_t max_batch, int64_t ctx_max,
+                       lq_comm* comm, lq_model** out) {
+    LQ_ENTRY(ctx, "lq_qwen3_create_tp");
+    LQ_REQUIRE(ctx, comm, "lq_qwen3_create_tp: NULL communicator");
+    return create_model(ctx, cfg, seed, max_batch, ctx_max, comm, out);
+}
+
+// copy the last-row logits [nb][vocab] to the host, gathering the vocabulary shards (a
+// collective under TP: every rank calls it)
+static int logits_to_host(lq_model* m, int64_t nb, float* host) {
+    lq_ctx* ctx = m->ctx;
+    const int64_t V = m->c.vocab, Vl = m->V_l;
+    if (m->tp == 1) {
+        LQ_CUDA(ctx, cudaMemcpyAsync(host, m->logits, (size_t)(nb * V) * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        return LQ_OK;
+    }
+    int rc = lq::comm_allgather_f32(m->comm, m->logits, m->logits_all, nb * Vl);
+    if (rc) return rc;
+    for (int t = 0; t < m->tp; t++)
+        LQ_CUDA(ctx, cudaMemcpy2DAsync(host + (size_t)t * Vl, (size_t)V * 4, m->logits_all + (size_t)t * nb * Vl,
+                                       (size_t)Vl * 4, (size_t)Vl * 4, (size_t)nb, cudaMemcpyDeviceToHost, ctx->stream));
+    return LQ_OK;
+}
+
 int lq_qwen3_reset(lq_model* m) {
     if (!m) return LQ_ERR_INVALID_ARG;
     LQ_ENTRY(m->ctx, "lq_qwen3_reset");
@@ -427,7 +524,7 @@ int lq_qwen3_prefill(lq_model* m, const int32_t* ids, int64_t B, int64_t L, int3
         LQ_REQUIRE(ctx, ids[i] >= 0 && ids[i] < m->c.vocab, "lq_qwen3_prefill: token id %d out of range", ids[i]);
     // whole sequences per pass; the KV caches of sequence b live at batch slot b
     int64_t per_pass = std::max<int64_t>(1, m->rows_cap / L);
-    const int64_t H = m->c.hidden, D = m->c.head_dim, Hkv = m->c.n_kv_heads;
+    const int64_t H = m->c.hidden, D = m->c.head_dim, Hkv = m->Hkv_l;
     for (int64_t b0 = 0; b0 < B; b0 += per_pass) {
         int64_t nb = std::min(per_pass, B - b0);
         LQ_CUDA(ctx, cudaMemcpyAsync(m->tokens, ids + b0 * L, (size_t)(nb * L) * 4, cudaMemcpyHostToDevice,
@@ -444,9 +541,10 @@ int lq_qwen3_prefill(lq_model* m, const int32_t* ids, int64_t B, int64_t L, int3
         m->vc = vc_save;
         if (rc) return rc;
         LQ_CUDA(ctx, cudaMemcpyAsync(next + b0, m->tokens, (size_t)nb * 4, cudaMemcpyDeviceToHost, ctx->stream));
-        if (logits)
-            LQ_CUDA(ctx, cudaMemcpyAsync(logits + b0 * m->c.vocab, m->logits, (size_t)(nb * m->c.vocab) * 4,
-                                         cudaMemcpyDeviceToHost, ctx->stream));
+        if (logits) {
+            rc = logits_to_host(m, nb, logits + b0 * m->c.vocab);
+            if (rc) return rc;
+        }
     }
     (void)H;
     m->pos = L;
@@ -475,9 +573,10 @@ int lq_qwen3_decode_step(lq_model* m, const int32_t* ids, int32_t* next, float* 
     LQ_CUDA(ctx, cudaMemcpyAsync(m->tokens, ids, (size_t)B * 4, cudaMemcpyHostToDevice, ctx->stream));
     LQ_CUDA(ctx, cudaGraphLaunch(m->exec, ctx->stream));
     LQ_CUDA(ctx, cudaMemcpyAsync(next, m->tokens, (size_t)B * 4, cudaMemcpyDeviceToHost, ctx->stream));
-    if (logits)
-        LQ_CUDA(ctx, cudaMemcpyAsync(logits, m->logits, (size_t)(B * m->c.vocab) * 4, cudaMemcpyDeviceToHost,
-                                     ctx->stream));
+    if (logits) {
+        rc = logits_to_host(m, B, logits);
+        if (rc) return rc;
+    }
     LQ_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
     m->pos += 1;
     return LQ_OK;
@@ -529,7 +628,7 @@ int lq_qwen3_linear(lq_model* m, int64_t layer, int kind, lq_q8_tensor* out) {
     LQ_REQUIRE(ctx, !m->moe || (kind != K_GATE && kind != K_UP && kind != K_DOWN && kind != 9),
                "lq_qwen3_linear: a MoE model has no dense MLP (use lq_qwen3_expert)");
     const Layer& ly = m->layers[(size_t)layer];
-    const int64_t I = m->c.inter;
+    const int64_t I = m->I_l;
     switch (kind) {
         case K_Q: *out = rows_view(ly.qkv, 0, m->Nq); break;
         case K_K: *out = rows_view(ly.qkv, m->Nq, m->Nk); break;

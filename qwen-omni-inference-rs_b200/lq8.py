@@ -117,6 +117,13 @@ SIGNATURES = {
     "lq_argmax": (C.c_int, [_P, _P, _I64, _I64, _P]),
     "lq_fill_bf16": (C.c_int, [_P, C.c_uint64, C.c_uint64, _I64, _I64, C.c_double, _P]),
     "lq_qwen3_create": (C.c_int, [_P, C.POINTER(Qwen3Config), C.c_uint64, _I64, _I64, C.POINTER(_P)]),
+    "lq_qwen3_create_tp": (C.c_int, [_P, C.POINTER(Qwen3Config), C.c_uint64, _I64, _I64, _P, C.POINTER(_P)]),
+    "lq_comm_unique_id": (C.c_int, [_P, _P]),
+    "lq_comm_init": (C.c_int, [_P, _P, C.c_int, C.c_int, C.POINTER(_P)]),
+    "lq_comm_destroy": (C.c_int, [_P]),
+    "lq_comm_rank": (C.c_int, [_P, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    "lq_comm_allreduce_f32": (C.c_int, [_P, _P, _I64]),
+    "lq_q8_0_matmul_allreduce": (C.c_int, [_P, _P, C.POINTER(Q8Tensor), _P, _P, _I64, _P, _P]),
     "lq_qwen3_destroy": (C.c_int, [_P]),
     "lq_qwen3_reset": (C.c_int, [_P]),
     "lq_qwen3_prefill": (C.c_int, [_P, _P, _I64, _I64, _P, _P]),
@@ -289,16 +296,61 @@ def matmul_q8(ctx: Context, w: QTensor, xq, xd, residual=None, out=None):
     return y
 
 
-class Qwen3ForCausalLM:
-    """Qwen3 model runner with seeded random-init Q8_0 weights (model.rs:273-372)."""
+COMM_ID_BYTES = 128
 
-    def __init__(self, ctx: Context, cfg: Qwen3Config, seed: int, max_batch: int = 1, ctx_max: int = 64):
+
+class Comm:
+    """NCCL communicator of this rank (lq_comm_*). `from_process_group` makes rank 0's NCCL id
+    and hands it to the other ranks over an initialised torch.distributed process group."""
+
+    def __init__(self, ctx: Context, uid: bytes, rank: int, world: int):
+        self.ctx = ctx
+        buf = (C.c_uint8 * COMM_ID_BYTES).from_buffer_copy(uid)
+        h = _P()
+        ctx.check(ctx.lib.lq_comm_init(ctx.h, buf, rank, world, C.byref(h)))
+        self.h = h
+        self.rank, self.world = rank, world
+
+    @staticmethod
+    def unique_id(ctx: Context) -> bytes:
+        buf = (C.c_uint8 * COMM_ID_BYTES)()
+        ctx.check(ctx.lib.lq_comm_unique_id(ctx.h, buf))
+        return bytes(buf)
+
+    @classmethod
+    def from_process_group(cls, ctx: Context) -> "Comm":
+        import torch.distributed as dist
+        rank, world = dist.get_rank(), dist.get_world_size()
+        obj = [cls.unique_id(ctx) if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        return cls(ctx, obj[0], rank, world)
+
+    def allreduce_(self, t) -> None:
+        """In-place sum over the ranks of a contiguous f32 CUDA tensor."""
+        self.ctx.check(self.ctx.lib.lq_comm_allreduce_f32(self.h, _ptr(t), t.numel()))
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.ctx.lib.lq_comm_destroy(self.h)
+            self.h = None
+
+
+class Qwen3ForCausalLM:
+    """Qwen3 model runner with seeded random-init Q8_0 weights (model.rs:273-372). With `comm`
+    this rank's tensor-parallel shard (every rank makes the same calls in the same order)."""
+
+    def __init__(self, ctx: Context, cfg: Qwen3Config, seed: int, max_batch: int = 1, ctx_max: int = 64,
+                 comm: "Comm | None" = None):
         self.ctx = ctx
         self.cfg = cfg
         self.max_batch = max_batch
         self.ctx_max = ctx_max
+        self.comm = comm
         h = _P()
-        ctx.check(ctx.lib.lq_qwen3_create(ctx.h, C.byref(cfg), seed, max_batch, ctx_max, C.byref(h)))
+        if comm is None:
+            ctx.check(ctx.lib.lq_qwen3_create(ctx.h, C.byref(cfg), seed, max_batch, ctx_max, C.byref(h)))
+        else:
+            ctx.check(ctx.lib.lq_qwen3_create_tp(ctx.h, C.byref(cfg), seed, max_batch, ctx_max, comm.h, C.byref(h)))
         self.h = h
 
     def close(self):
