@@ -23,6 +23,10 @@ struct lq_ctx {
     // partials); grown with cudaMalloc on demand, freed at lq_destroy
     void* scratch = nullptr;
     size_t scratch_bytes = 0;
+    // K-split partial sums of the small-M GEMM (separate from scratch, which may hold that
+    // GEMM's activations); reserved ahead by models so that graph capture never allocates
+    void* split = nullptr;
+    size_t split_bytes = 0;
     int* err_flag = nullptr;      // device int[4]: kernels report bad inputs here
     // launch kernels with programmatic stream serialization (PDL): every kernel of the library
     // calls pdl_wait() before it touches data written by earlier kernels
@@ -37,6 +41,10 @@ int check_cuda(lq_ctx* ctx, cudaError_t e, const char* what);
 bool fault_injected(const char* entry);
 // grow ctx scratch to at least `bytes`; returns LQ_OK or an error
 int ensure_scratch(lq_ctx* ctx, size_t bytes);
+// grows ctx->split (an error while the stream is capturing a graph)
+int ensure_split(lq_ctx* ctx, size_t bytes);
+// partial-sum bytes the M x (N, K) Q8_0 GEMM needs when it splits K (0: no split)
+size_t gemm_split_bytes(lq_ctx* ctx, int64_t n, int64_t k, int64_t m);
 // read + clear the device error flag (synchronises the stream)
 int consume_device_error(lq_ctx* ctx, const char* what);
 

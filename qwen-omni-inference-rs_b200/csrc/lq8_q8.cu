@@ -219,7 +219,8 @@ template <int BW, int BX, int WW, int WX>
 __global__ void __launch_bounds__(WW * WX * 32)
 q8_gemm_mma_kernel(const int8_t* __restrict__ wq, const uint16_t* __restrict__ wd, int N, int K,
                    const int8_t* __restrict__ xq, const uint16_t* __restrict__ xd, int M,
-                   const float* resid, float* y, int ldy, unsigned long long* argmax_keys) {
+                   const float* resid, float* y, int ldy, unsigned long long* argmax_keys, int kslice,
+                   float* part) {
     using C = GemmCfg<BW, BX, WW, WX>;
     extern __shared__ __align__(128) uint8_t smem[];
     pdl_wait();
@@ -229,7 +230,11 @@ q8_gemm_mma_kernel(const int8_t* __restrict__ wq, const uint16_t* __restrict__ w
     const int n0 = blockIdx.x * BW;  // weight row base
     const int m0 = blockIdx.y * BX;  // token base
     const int nb = K >> 5;
-    const int nstages_k = (K + GEMM_BK - 1) / GEMM_BK;
+    // K-split (part != nullptr): this CTA covers K bytes [k_lo, k_hi) and writes its partial
+    // sums to part[blockIdx.z][M][N]; a second kernel adds the slices in order
+    const int k_lo = part ? blockIdx.z * kslice : 0;
+    const int k_hi = part ? min(K, k_lo + kslice) : K;
+    const int nstages_k = (k_hi - k_lo + GEMM_BK - 1) / GEMM_BK;
 
     auto stage_ptr = [&](int s) { return smem + s * C::STAGE; };
 
@@ -239,13 +244,13 @@ q8_gemm_mma_kernel(const int8_t* __restrict__ wq, const uint16_t* __restrict__ w
         uint8_t* sx = base + C::W_BYTES;
         uint16_t* sws = reinterpret_cast<uint16_t*>(base + C::W_BYTES + C::X_BYTES);
         uint16_t* sxs = reinterpret_cast<uint16_t*>(base + C::W_BYTES + C::X_BYTES + C::WS_BYTES);
-        const int kb = kt * GEMM_BK;  // byte offset in K
+        const int kb = k_lo + kt * GEMM_BK;  // byte offset in K
         // weights: BW rows x 4 chunks of 16 B
         for (int c = tid; c < BW * 4; c += C::THREADS) {
             int r = c >> 2, ch = c & 3;
             int row = n0 + r;
             int kk = kb + ch * 16;
-            bool p = row < N && kk < K;
+            bool p = row < N && kk < k_hi;
             const int8_t* g = wq + (size_t)(p ? row : 0) * K + (p ? kk : 0);
             cp_async16(sw + r * GEMM_LDS + ch * 16, g, p);
         }
@@ -253,21 +258,21 @@ q8_gemm_mma_kernel(const int8_t* __restrict__ wq, const uint16_t* __restrict__ w
             int r = c >> 2, ch = c & 3;
             int tok = m0 + r;
             int kk = kb + ch * 16;
-            bool p = tok < M && kk < K;
+            bool p = tok < M && kk < k_hi;
             const int8_t* g = xq + (size_t)(p ? tok : 0) * K + (p ? kk : 0);
             cp_async16(sx + r * GEMM_LDS + ch * 16, g, p);
         }
         // scales: 2 blocks per row = 4 bytes; the 4-byte async copy needs an even block count
         // per row (so that row*nb + b is even); otherwise plain loads
-        const int b = kb >> 5;
-        const bool even = (nb & 1) == 0;
+        const int b = kb >> 5, bhi = k_hi >> 5;
+        const bool even = (nb & 1) == 0 && b + 1 < bhi;
         for (int r = tid; r < BW; r += C::THREADS) {
             int row = n0 + r;
             if (row < N && even) {
                 cp_async4(sws + r * 2, wd + (size_t)row * nb + b, true);
             } else {
-                sws[r * 2] = (row < N && b < nb) ? wd[(size_t)row * nb + b] : (uint16_t)0;
-                sws[r * 2 + 1] = (row < N && b + 1 < nb) ? wd[(size_t)row * nb + b + 1] : (uint16_t)0;
+                sws[r * 2] = (row < N && b < bhi) ? wd[(size_t)row * nb + b] : (uint16_t)0;
+                sws[r * 2 + 1] = (row < N && b + 1 < bhi) ? wd[(size_t)row * nb + b + 1] : (uint16_t)0;
             }
         }
         for (int r = tid; r < BX; r += C::THREADS) {
@@ -275,8 +280,8 @@ q8_gemm_mma_kernel(const int8_t* __restrict__ wq, const uint16_t* __restrict__ w
             if (tok < M && even) {
                 cp_async4(sxs + r * 2, xd + (size_t)tok * nb + b, true);
             } else {
-                sxs[r * 2] = (tok < M && b < nb) ? xd[(size_t)tok * nb + b] : (uint16_t)0;
-                sxs[r * 2 + 1] = (tok < M && b + 1 < nb) ? xd[(size_t)tok * nb + b + 1] : (uint16_t)0;
+                sxs[r * 2] = (tok < M && b < bhi) ? xd[(size_t)tok * nb + b] : (uint16_t)0;
+                sxs[r * 2 + 1] = (tok < M && b + 1 < bhi) ? xd[(size_t)tok * nb + b + 1] : (uint16_t)0;
             }
         }
     };
@@ -361,13 +366,17 @@ q8_gemm_mma_kernel(const int8_t* __restrict__ wq, const uint16_t* __restrict__ w
                 int n = n0 + ww * C::TW + i * 16 + g + 8 * (e >> 1);
                 int m = m0 + wx * C::TX + j * 8 + 2 * t + (e & 1);
                 if (n < N && m < M) {
+                    if (part) {
+                        part[((size_t)blockIdx.z * M + m) * N + n] = acc[i][j][e];
+                        continue;
+                    }
                     size_t o = (size_t)m * ldy + n;
                     float v = acc[i][j][e];
                     if (resid) v = __fadd_rn(resid[o], v);
                     y[o] = v;
                 }
             }
-    if (argmax_keys) {
+    if (argmax_keys && !part) {
         // per token: max over this thread's rows, then over the 8 lanes sharing t, then over
         // the CTA in shared memory, then one global atomic per token per CTA
         __shared__ unsigned long long cta_keys[BX];
@@ -402,6 +411,61 @@ q8_gemm_mma_kernel(const int8_t* __restrict__ wq, const uint16_t* __restrict__ w
     }
 }
 
+// K-split combine: y[m][n] = resid + sum over the slices in ascending order; the greedy
+// argmax keys (if any) per token over the CTA's outputs
+__global__ void gemm_split_reduce_kernel(const float* __restrict__ part, int splits, int M, int N, const float* resid,
+                                         float* y, int ldy, unsigned long long* keys) {
+    pdl_wait();
+    pdl_trigger();
+    const int m = blockIdx.y;
+    __shared__ unsigned long long ck;
+    if (threadIdx.x == 0) ck = 0ull;
+    __syncthreads();
+    unsigned long long key = 0ull;
+    for (int n = blockIdx.x * blockDim.x + threadIdx.x; n < N; n += gridDim.x * blockDim.x) {
+        float v = 0.0f;
+        for (int s = 0; s < splits; s++) v = __fadd_rn(v, part[((size_t)s * M + m) * N + n]);
+        const size_t o = (size_t)m * ldy + n;
+        if (resid) v = __fadd_rn(resid[o], v);
+        y[o] = v;
+        if (keys) {
+            const unsigned long long kk = argmax_key(v, n);
+            key = kk > key ? kk : key;
+        }
+    }
+    if (keys) {
+        atomicMax(&ck, key);
+        __syncthreads();
+        if (threadIdx.x == 0 && ck) atomicMax(keys + m, ck);
+    }
+}
+
+// splits of K (whole 64-byte stages) that give the grid about three waves of CTAs when the
+// plain grid of a small-M (<= 64 tokens) GEMM is short of two; 1 = no split (bit-identical to
+// the oracle; LQ_GEMM_NO_SPLIT=1 forces it)
+static int gemm_splits(lq_ctx* ctx, int64_t tiles, int64_t K, int64_t m) {
+    if (m > 64 || tiles >= 2 * ctx->sm_count || getenv("LQ_GEMM_NO_SPLIT")) return 1;
+    int64_t s = (3 * (int64_t)ctx->sm_count + tiles - 1) / tiles;
+    const int64_t kst = (K + GEMM_BK - 1) / GEMM_BK;
+    s = std::min<int64_t>(s, std::max<int64_t>(1, kst / 4));  // at least 4 stages per slice
+    return (int)std::max<int64_t>(1, std::min<int64_t>(s, 32));
+}
+
+static int split_slice(int64_t K, int splits) {
+    const int64_t kst = (K + GEMM_BK - 1) / GEMM_BK;
+    return (int)(((kst + splits - 1) / splits) * GEMM_BK);
+}
+
+// mirrors run_gemm's choice (128-row tiles; 16/32/64-token tiles for m <= 64)
+size_t gemm_split_bytes(lq_ctx* ctx, int64_t n, int64_t k, int64_t m) {
+    if (m <= 4 || m > 64) return 0;
+    const int64_t bx = m <= 16 ? 16 : m <= 32 ? 32 : 64;
+    const int splits0 = gemm_splits(ctx, (int64_t)ceil_div(n, 128) * ceil_div(m, bx), k, m);
+    if (splits0 <= 1) return 0;
+    const int splits = ceil_div(k, split_slice(k, splits0));
+    return (size_t)splits * m * n * 4;
+}
+
 template <int BW, int BX, int WW, int WX>
 static int run_gemm(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd,
                     int64_t m, float* y, const float* resid, int64_t ldy,
@@ -413,9 +477,23 @@ static int run_gemm(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const 
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
         attr_done = true;
     }
-    dim3 grid(ceil_div(w->n, BW), ceil_div(m, BX));
-    return launch_kernel(ctx, q8_gemm_mma_kernel<BW, BX, WW, WX>, grid, dim3(C::THREADS), C::SMEM, "q8_gemm_mma",
-                         w->qs, w->d, (int)w->n, (int)w->k, xq, xd, (int)m, resid, y, (int)ldy, keys);
+    const int64_t tiles = (int64_t)ceil_div(w->n, BW) * ceil_div(m, BX);
+    int splits = gemm_splits(ctx, tiles, w->k, m);
+    int kslice = 0;
+    float* part = nullptr;
+    if (splits > 1) {
+        kslice = split_slice(w->k, splits);
+        splits = ceil_div(w->k, kslice);
+        const int rc = ensure_split(ctx, (size_t)splits * m * w->n * 4);
+        if (rc) return rc;
+        part = reinterpret_cast<float*>(ctx->split);
+    }
+    dim3 grid(ceil_div(w->n, BW), ceil_div(m, BX), splits);
+    int rc = launch_kernel(ctx, q8_gemm_mma_kernel<BW, BX, WW, WX>, grid, dim3(C::THREADS), C::SMEM, "q8_gemm_mma",
+                           w->qs, w->d, (int)w->n, (int)w->k, xq, xd, (int)m, resid, y, (int)ldy, keys, kslice, part);
+    if (rc || splits == 1) return rc;
+    return launch_kernel(ctx, gemm_split_reduce_kernel, dim3((unsigned)ceil_div(w->n, 1024), (unsigned)m), dim3(256), 0,
+                         "gemm_split_reduce", (const float*)part, splits, (int)m, (int)w->n, resid, y, (int)ldy, keys);
 }
 
 template <int M, int R>
@@ -454,7 +532,7 @@ int launch_q8_matmul(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const
         case 4: return gemv_rows<4>(ctx, w, xq, xd, y, resid, ldy, keys);
         default: break;
     }
-    if (!keys && gemm_tc_supported(m, w->k, w->qs, xq, w->d, xd))
+    if (!keys && m > 64 && gemm_tc_supported(m, w->k, w->qs, xq, w->d, xd))
         return launch_gemm_tc(ctx, w, xq, xd, m, y, resid, ldy);
     if (m <= 16) return run_gemm<128, 16, 8, 1>(ctx, w, xq, xd, m, y, resid, ldy, keys);
     if (m <= 32) return run_gemm<128, 32, 8, 1>(ctx, w, xq, xd, m, y, resid, ldy, keys);

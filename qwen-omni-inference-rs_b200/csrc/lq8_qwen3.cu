@@ -455,6 +455,14 @@ static int create_model(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, 
     RC(dalloc(m, &m->att_scratch, m->att_scratch_bytes));
     if (moe) RC(dalloc(m, &m->moe_scratch, lq::moe_scratch_bytes(R, E, c.top_k, H, I)));
     LQ_CUDA(ctx, cudaMemsetAsync(m->att_scratch, 0, m->att_scratch_bytes, ctx->stream));  // chunk counters
+    {
+        // the small-M GEMM's K-split partials, reserved now: graph capture cannot allocate
+        size_t need = 0;
+        const int64_t shapes[5][2] = {{m->Nqkv, H}, {H, m->Hqd}, {2 * I, H}, {H, I}, {Vl, H}};
+        for (int64_t rows = 5; rows <= std::min<int64_t>(R, 64); rows++)
+            for (const auto& sh : shapes) need = std::max(need, lq::gemm_split_bytes(ctx, sh[0], sh[1], rows));
+        if (need) RC(lq::ensure_split(ctx, need));
+    }
     LQ_CUDA(ctx, cudaMemsetAsync(m->keys, 0, (size_t)max_batch * 8, ctx->stream));
     LQ_CUDA(ctx, cudaMemsetAsync(m->pos_dev, 0, 4, ctx->stream));
     LQ_CUDA(ctx, cudaMemsetAsync(m->kc, 0, kv * 4, ctx->stream));

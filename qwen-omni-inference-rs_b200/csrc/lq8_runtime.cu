@@ -57,6 +57,22 @@ int ensure_scratch(lq_ctx* ctx, size_t bytes) {
     return LQ_OK;
 }
 
+int ensure_split(lq_ctx* ctx, size_t bytes) {
+    if (bytes <= ctx->split_bytes) return LQ_OK;
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    LQ_CUDA(ctx, cudaStreamIsCapturing(ctx->stream, &st));
+    if (st != cudaStreamCaptureStatusNone)
+        return set_error(ctx, LQ_ERR_STATE, "split-K buffer (%zu bytes) too small while capturing a graph", bytes);
+    LQ_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    if (ctx->split) LQ_CUDA(ctx, cudaFree(ctx->split));
+    ctx->split = nullptr;
+    ctx->split_bytes = 0;
+    size_t sz = (bytes + 0xFFFFF) & ~(size_t)0xFFFFF;
+    LQ_CUDA(ctx, cudaMalloc(&ctx->split, sz));
+    ctx->split_bytes = sz;
+    return LQ_OK;
+}
+
 int consume_device_error(lq_ctx* ctx, const char* what) {
     int h[4];
     LQ_CUDA(ctx, cudaMemcpyAsync(h, ctx->err_flag, sizeof h, cudaMemcpyDeviceToHost, ctx->stream));
@@ -119,6 +135,7 @@ int lq_destroy(lq_ctx* ctx) {
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->stream);
     if (ctx->scratch) cudaFree(ctx->scratch);
+    if (ctx->split) cudaFree(ctx->split);
     if (ctx->err_flag) cudaFree(ctx->err_flag);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;

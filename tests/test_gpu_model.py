@@ -87,6 +87,30 @@ def test_batched_sequences_are_independent(ctx, lq8_lib, oracle):
         assert np.array_equal(toks[b], otoks), b
 
 
+def test_batched_decode_with_split_lm_head(ctx, lq8_lib, oracle):
+    """Batch 6 runs the separate kernels; with hidden 1024 and a 2048-row LM head the 6-token
+    GEMMs split K (short grid) and the greedy token comes from the split reduction's argmax
+    keys. The token must be exactly the argmax (ties -> last) of the logits the GPU returns;
+    the logits follow the oracle within the deep-model tolerance (at this width two of the
+    prompts already sit next to a rounding boundary with the unsplit GEMMs: cosine 0.99988)."""
+    cfgd = dict(TINY, hidden=1024, inter=1024, vocab=2048, tied=0)
+    B, L, steps = 6, 5, 4
+    gm, ocfg = _models(lq8_lib, oracle, ctx, 31, cfgd, max_batch=B)
+    prompts = np.stack([oracle.gen_tokens(31, s, L, ocfg.vocab) for s in range(B)])
+    oms = [oracle.Qwen3Model(ocfg, 31, ctx_max=64) for _ in range(B)]
+    nxt, lg = gm.prefill(prompts, want_logits=True)
+    olgs = [oms[b].forward(prompts[b], 0) for b in range(B)]
+    for step in range(steps):
+        if step > 0:
+            toks = np.array([oracle.argmax(o) for o in olgs], np.int32)
+            nxt, lg = gm.decode_step(toks, want_logits=True)
+            olgs = [oms[b].forward(toks[b:b + 1], L + step - 1) for b in range(B)]
+        for b in range(B):
+            assert nxt[b] == oracle.argmax(lg[b]), (step, b)
+            assert cos_sim(lg[b], olgs[b]) >= DEEP_COS, (step, b)
+            assert np.max(np.abs(lg[b] - olgs[b])) <= DEEP_MAXREL * np.max(np.abs(olgs[b])), (step, b)
+
+
 # Deep-model tolerance. A random-init 28-layer model amplifies f32 summation-order noise
 # through its bf16 and int8 rounding steps: the oracle against itself with only the RMSNorm
 # sum reversed already differs by 8e-3 max-relative after 8 layers. Measured GPU vs oracle on

@@ -110,14 +110,13 @@ def test_moe_model_weights_bit_identical(ctx, lq8_lib, oracle):
         gm.linear(0, "gate")
 
 
-# Prefill (bit-exact Q8_0 GEMMs and experts) leaves only exp ulps between the two sides: the
-# dense model's tolerance. Decode steps run the dense projections through the decode GEMV,
-# whose bounded reordering moves the next layer's router inputs by ulps; a router near-tie
+# Identical inputs give identical routing (the op tests), but the dense projections of decode
+# steps (the decode GEMV) and of short prefills (the K-split GEMM) regroup their f32 sums,
+# which moves the next layer's router inputs by ulps; a router near-tie
 # can then pick another expert for one token, which moves that step's logits by more
 # (measured on this config: cosine 0.9985, max 6 % of the largest logit) and, through the
-# KV cache, every later step of that sequence. So each sequence is held to the dense
-# tolerance up to its first step outside it, and from there on to the flip bound.
-PREFILL_COS, PREFILL_MAXREL = 0.99999, 1e-3
+# KV cache, every later step of that sequence. Every step is held to that flip bound, and
+# the greedy token to the oracle's wherever the oracle's margin exceeds the step's noise.
 MOE_COS, MOE_MAXREL = 0.99, 0.15
 
 
@@ -125,11 +124,9 @@ MOE_COS, MOE_MAXREL = 0.99, 0.15
 def test_moe_model_generate_matches_oracle(ctx, lq8_lib, oracle, B):
     """Prefill + greedy decode of a 2-layer MoE model (16 experts, top-4): B = 1 and 3 take
     the fused decode path, B = 6 the separate kernels. Teacher-forced (every sequence fed the
-    oracle's token): each sequence's logits within the dense tolerance up to its first step
-    outside it (a router near-tie) and within the route-flip bound from there on; the greedy
-    token
+    oracle's token): logits within the route-flip bound at every step, and the greedy token
     equal to the oracle's wherever the oracle's top-1/top-2 margin exceeds twice the step's
-    measured difference."""
+    measured difference. Identical routing for identical inputs is the op tests' check."""
     L, steps = 12, 8
     gm = lq8_lib.Qwen3ForCausalLM(ctx, lq8_lib.make_config(**TINY_MOE), 11, max_batch=B, ctx_max=64)
     ocfg = oracle.make_config(**TINY_MOE)
@@ -137,10 +134,6 @@ def test_moe_model_generate_matches_oracle(ctx, lq8_lib, oracle, B):
     oms = [oracle.Qwen3Model(ocfg, 11, ctx_max=64) for _ in range(B)]
     nxt, lg = gm.prefill(prompts, want_logits=True)
     olgs = [oms[b].forward(prompts[b], 0) for b in range(B)]
-    for b in range(B):
-        assert cos_sim(lg[b], olgs[b]) >= PREFILL_COS, b
-        assert np.max(np.abs(lg[b] - olgs[b])) <= PREFILL_MAXREL * np.max(np.abs(olgs[b])), b
-    diverged = [False] * B
     for step in range(steps):
         if step > 0:
             toks = np.array([oracle.argmax(o) for o in olgs], np.int32)
@@ -151,8 +144,6 @@ def test_moe_model_generate_matches_oracle(ctx, lq8_lib, oracle, B):
             c = cos_sim(lg[b], olgs[b])
             assert c >= MOE_COS, (step, b, c)
             assert d <= MOE_MAXREL * np.max(np.abs(olgs[b])), (step, b)
-            if not (c >= PREFILL_COS and d <= PREFILL_MAXREL * np.max(np.abs(olgs[b]))):
-                diverged[b] = True
             s_ = np.sort(olgs[b])
             if s_[-1] - s_[-2] > 2 * d:
                 assert nxt[b] == oracle.argmax(olgs[b]), (step, b)

@@ -1,8 +1,9 @@
 """GPU parity of the Q8_0 kernels against the CPU oracle, through the C ABI.
 
-Quantization is bit-exact (int8 values and fp16 scales). The GEMM path (M > 4) keeps the
-oracle's per-output summation order and is bit-exact; the decode GEMV (M <= 4) reduces over
-K in parallel and is checked against the f32 reordering bound
+Quantization is bit-exact (int8 values and fp16 scales). The GEMM paths (M > 4) keep the
+oracle's per-output summation order and are bit-exact, except that a 5-64-token GEMM on a
+short grid splits K across CTAs (LQ_GEMM_NO_SPLIT=1 turns that off); the split and the
+decode GEMV (M <= 4) regroup the f32 block sum and are checked against the reordering bound
 |y_gpu - y_oracle| <= 2 * (nb + 1) * 2^-24 * sum_b |term_b|.
 """
 import ctypes as C
@@ -112,17 +113,34 @@ def test_gemv_within_reorder_bound(ctx, lq8_lib, oracle, rng, m, n, k):
 
 @pytest.mark.parametrize("m", [5, 16, 17, 33, 64, 100, 257])
 @pytest.mark.parametrize("n,k", [(1, 32), (17, 96), (300, 1024), (640, 3072)])
-def test_gemm_bit_exact(ctx, lq8_lib, oracle, rng, m, n, k):
+def test_gemm_bit_exact(ctx, lq8_lib, oracle, rng, monkeypatch, m, n, k):
+    """Without the K split (LQ_GEMM_NO_SPLIT=1) every GEMM output is one thread's sum in the
+    oracle's block order: bit-identical."""
+    monkeypatch.setenv("LQ_GEMM_NO_SPLIT", "1")
     wq, wd = _weights(oracle, rng, n, k)
     xq, xd = oracle.q8_0_quantize(rng.standard_normal((m, k)).astype(np.float32))
     y = _matmul(ctx, lq8_lib, wq, wd, xq, xd)
     assert np.array_equal(y, oracle.q8_0_matmul(xq, xd, wq, wd))
 
 
-@pytest.mark.parametrize("m", [64, 65, 127, 128, 300, 513])
+@pytest.mark.parametrize("m", [5, 8, 16, 33, 64])
+@pytest.mark.parametrize("n,k", [(300, 1024), (640, 3072), (4096, 4096), (1000, 12288)])
+def test_gemm_small_m_split_within_reorder_bound(ctx, lq8_lib, oracle, rng, m, n, k):
+    """Decode batches of 5-64 tokens on short grids split K across CTAs; the slices are added
+    in a fixed order (deterministic), which regroups the f32 block sum within the bound."""
+    wq, wd = _weights(oracle, rng, n, k)
+    xq, xd = oracle.q8_0_quantize(rng.standard_normal((m, k)).astype(np.float32))
+    y = _matmul(ctx, lq8_lib, wq, wd, xq, xd)
+    ref, absum = oracle.q8_0_matmul(xq, xd, wq, wd, with_abs=True)
+    bound = 2.0 * (k // 32 + 1) * 2.0 ** -24 * absum + 1e-30
+    assert np.all(np.abs(y - ref) <= bound), float(np.max(np.abs(y - ref) / bound))
+    assert np.array_equal(y, _matmul(ctx, lq8_lib, wq, wd, xq, xd))  # deterministic
+
+
+@pytest.mark.parametrize("m", [65, 127, 128, 300, 513])
 @pytest.mark.parametrize("n,k", [(128, 256), (129, 512), (1000, 4096), (4096, 1024)])
 def test_gemm_tcgen05_bit_exact(ctx, lq8_lib, oracle, rng, m, n, k):
-    """The tcgen05 prefill GEMM (m >= 64, k % 256 == 0): ragged row/token tiles, one stage
+    """The tcgen05 prefill GEMM (m > 64, k % 256 == 0): ragged row/token tiles, one stage
     (k = 256) up to many, scales across a wide dynamic range, all-zero blocks."""
     w = rng.standard_normal((n, k)) * 0.02
     w[:, :32] *= 1e3
@@ -135,7 +153,7 @@ def test_gemm_tcgen05_bit_exact(ctx, lq8_lib, oracle, rng, m, n, k):
     assert np.array_equal(y, oracle.q8_0_matmul(xq, xd, wq, wd))
 
 
-@pytest.mark.parametrize("m", [64, 200])
+@pytest.mark.parametrize("m", [96, 200])
 def test_gemm_tcgen05_residual_and_stride(ctx, lq8_lib, oracle, rng, m):
     n, k, ldy = 300, 768, 320
     wq, wd = _weights(oracle, rng, n, k)
@@ -163,7 +181,8 @@ def test_gemm_tcgen05_matches_mma_sync_path(ctx, lq8_lib, oracle, rng, monkeypat
 
 
 @pytest.mark.parametrize("m", [1, 16])
-def test_matmul_residual_and_stride(ctx, lq8_lib, oracle, rng, m):
+def test_matmul_residual_and_stride(ctx, lq8_lib, oracle, rng, monkeypatch, m):
+    monkeypatch.setenv("LQ_GEMM_NO_SPLIT", "1")
     n, k, ldy = 200, 512, 256
     wq, wd = _weights(oracle, rng, n, k)
     xq, xd = oracle.q8_0_quantize(rng.standard_normal((m, k)).astype(np.float32))
