@@ -441,7 +441,8 @@ def finish(args, cfgd, world, rank, L, B, K, W, ms, value, e2e, ms_e2e, clk, lau
             "data": "synthetic (seeded random-init N(0,0.02) weights, seeded uniform token ids)",
             "config": {"workload": f"{args.config} greedy decode after a {L}-token prefill, batch {B}",
                        "model": args.config, "global_batch": B * (world // tp), "seq_len": L,
-                       "parallelism": (f"tp{tp}" + (f" x dp{world // tp}" if world > tp else "")) if tp > 1
+                       "parallelism": ((f"ep{tp}" if cfgd.get("n_experts", 0) else f"tp{tp}") +
+                                       (f" x dp{world // tp}" if world > tp else "")) if tp > 1
                        else (f"dp{world} replicas" if world > 1 else "single GPU"),
                        "l2": "no flush: each step streams the Q8_0 weights (GBs, far above the 126 MB L2)",
                        "context_range": [L + W, L + W + K]},
@@ -611,7 +612,8 @@ def main():
                     help="with --sweep: one case 'm,n,k' (two weight copies; for profiling)")
     ap.add_argument("--sweep-reps", type=int, default=20)
     ap.add_argument("--tp", type=int, default=1,
-                    help="tensor parallelism over the torchrun ranks (NCCL); 1 = independent replicas")
+                    help="model parallelism over the torchrun ranks (NCCL): tensor-parallel for dense "
+                         "configs, expert-parallel for MoE; 1 = independent replicas")
     ap.add_argument("--moe", action="store_true",
                     help="time lq_moe_forward alone at the Qwen3-30B-A3B expert shape and exit")
     ap.add_argument("--moe-rows", default="1,8,64,512")

@@ -219,6 +219,13 @@ int lq_moe_forward(lq_ctx* ctx, const lq_q8_tensor* router, const lq_moe_experts
                    int norm_topk, float* out_dev, const float* residual_dev, int32_t* ids_out_dev,
                    float* weights_out_dev);
 
+/* Expert-parallel MoE layer (each rank holds experts [first_expert, first_expert + n_experts)
+ * of `local`; the router is replicated): out = residual + sum over ALL experts, the same on
+ * every rank (this rank's experts, then a sum all-reduce over comm). */
+int lq_moe_forward_ep(lq_ctx* ctx, lq_comm* comm, const lq_q8_tensor* router, const lq_moe_experts* local,
+                      int64_t first_expert, const int8_t* xq_dev, const uint16_t* xd_dev, int64_t rows,
+                      int64_t top_k, int norm_topk, float* out_dev, const float* residual_dev);
+
 /* ---------------------------------------------------------------------------------------
  * Qwen3 model runner (Qwen3ForCausalLM, model.rs:273-372; generate.rs:611-661).
  * ------------------------------------------------------------------------------------- */
@@ -245,7 +252,9 @@ int lq_qwen3_create(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int6
  * output rows (heads, intermediate), o and down by K (whole Q8_0 blocks) followed by a sum
  * all-reduce, the LM head by vocabulary rows with a global greedy argmax (ties -> highest
  * index). Needs n_heads, n_kv_heads, inter/32 and vocab divisible by the world size and an
- * untied LM head; dense models only. Every rank makes the same calls with the same ids. */
+ * untied LM head. For a MoE config the split is expert-parallel instead: attention, router
+ * and LM head replicated, n_experts / world experts per rank, one sum all-reduce per MoE
+ * layer. Every rank makes the same calls with the same ids. */
 int lq_qwen3_create_tp(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, int64_t max_batch,
                        int64_t ctx_max, lq_comm* comm, lq_model** out);
 int lq_qwen3_destroy(lq_model* model);

@@ -246,7 +246,7 @@ size_t moe_scratch_bytes(int64_t rows, int64_t E, int64_t top_k, int64_t H, int6
 int launch_moe(lq_ctx* ctx, const lq_q8_tensor* router, const lq_q8_tensor* gate_up, const lq_q8_tensor* down,
                int64_t E, int64_t inter, int64_t top_k, int norm_topk, const int8_t* xq, const uint16_t* xd,
                int64_t rows, int64_t H, float* out, const float* resid, void* scratch, int32_t* ids_out,
-               float* w_out);
+               float* w_out, int64_t e_lo, int64_t e_hi);  // experts [e_lo, e_hi) only (e_hi <= e_lo: all)
 size_t attention_scratch_bytes(int64_t rows, int64_t n_heads, int64_t ctx_max, int64_t head_dim);
 int attention_max_ctx();
 // scratch starts with per-(row, kv head) counters that must be zero before the first launch;

@@ -150,18 +150,26 @@ struct MoeLists {
     int32_t* pair_slot;    // [rows][k] pair index of the token's jj-th expert (ascending expert)
 };
 
+// (expert parallelism: only experts [e_lo, e_hi) get lists; the other pairs keep slot -1)
 __global__ void __launch_bounds__(1024) moe_dispatch_kernel(const int32_t* __restrict__ ids_g, int rows, int E,
-                                                            int top_k, MoeLists L) {
+                                                            int top_k, MoeLists L, int e_lo, int e_hi) {
     __shared__ int cnt[MOE_MAX_E];
     __shared__ int off[MOE_MAX_E + 1];
     extern __shared__ int ids_sorted[];  // [rows][top_k] staged from global
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     pdl_wait();
     pdl_trigger();
-    for (int i = threadIdx.x; i < rows * top_k; i += blockDim.x) ids_sorted[i] = ids_g[i];
+    for (int i = threadIdx.x; i < rows * top_k; i += blockDim.x) {
+        ids_sorted[i] = ids_g[i];
+        L.pair_slot[i] = -1;
+    }
     __syncthreads();
     // pass 1: counts
     for (int e = warp; e < E; e += 32) {
+        if (e < e_lo || e >= e_hi) {
+            if (lane == 0) cnt[e] = 0;
+            continue;
+        }
         int c = 0;
         for (int t0 = 0; t0 < rows; t0 += 32) {
             const int t = t0 + lane;
@@ -190,7 +198,7 @@ __global__ void __launch_bounds__(1024) moe_dispatch_kernel(const int32_t* __res
     }
     if (threadIdx.x == 0) L.offsets[E] = off[E];
     // pass 2: fill in token order
-    for (int e = warp; e < E; e += 32) {
+    for (int e = e_lo + warp; e < e_hi; e += 32) {
         int pos = off[e];
         for (int t0 = 0; t0 < rows; t0 += 32) {
             const int t = t0 + lane;
@@ -248,6 +256,7 @@ struct MoeExpertParams {
     const int32_t* counts;
     const int32_t* active;   // [E] + n_active at [E]
     int E;
+    int e_base;              // first expert held in the weight stack (expert parallelism)
     int8_t* hq;              // gate/up output [pairs][I]
     uint16_t* hd;
     float* y;                // down output [pairs][H]
@@ -320,7 +329,7 @@ __global__ void __launch_bounds__(ME_THREADS) moe_stream_kernel(const __grid_con
                     uint8_t* st = sm + (size_t)s * SB;
                     mbar_expect_tx(&full[s], (unsigned)(NG * (ME_GROUP_W + ME_GROUP_D)));
                     for (int g = 0; g < NG; g++) {
-                        const int row = e * p.rows_per_expert + g * p.out_rows + r0;
+                        const int row = (e - p.e_base) * p.rows_per_expert + g * p.out_rows + r0;
                         tma_load_2d(st + g * ME_GROUP_W, &mw, c * ME_KC, row, &full[s]);
                         tma_load_2d(st + g * ME_GROUP_W + ME_BOX, &mw, c * ME_KC + 128, row, &full[s]);
                         tma_load_2d(st + NG * ME_GROUP_W + g * ME_GROUP_D, &md, c * 8, row, &full[s]);
@@ -441,6 +450,7 @@ __global__ void moe_combine_kernel(const float* __restrict__ y, const int32_t* _
         float acc = 0.0f;
         for (int jj = 0; jj < top_k; jj++) {
             const int pr = pair_slot[(size_t)t * top_k + jj];
+            if (pr < 0) continue;  // an expert of another rank
             acc = __fadd_rn(acc, __fmul_rn(w_sorted[(size_t)t * top_k + jj], y[(size_t)pr * H + c]));
         }
         const size_t o = (size_t)t * H + c;
@@ -497,7 +507,11 @@ size_t moe_scratch_bytes(int64_t rows, int64_t E, int64_t top_k, int64_t H, int6
 int launch_moe(lq_ctx* ctx, const lq_q8_tensor* router, const lq_q8_tensor* gate_up, const lq_q8_tensor* down,
                int64_t E, int64_t inter, int64_t top_k, int norm_topk, const int8_t* xq, const uint16_t* xd,
                int64_t rows, int64_t H, float* out, const float* resid, void* scratch, int32_t* ids_out,
-               float* w_out) {
+               float* w_out, int64_t e_lo, int64_t e_hi) {
+    if (e_hi <= e_lo) {
+        e_lo = 0;
+        e_hi = E;
+    }
     if (rows <= 0) return LQ_OK;
     const int64_t P = rows * top_k;
     uint8_t* s = (uint8_t*)scratch;
@@ -533,7 +547,7 @@ int launch_moe(lq_ctx* ctx, const lq_q8_tensor* router, const lq_q8_tensor* gate
         }
     }
     rc = launch_kernel(ctx, moe_dispatch_kernel, dim3(1), dim3(1024), disp_smem, "moe_dispatch",
-                       (const int32_t*)ids_sorted, (int)rows, (int)E, (int)top_k, L);
+                       (const int32_t*)ids_sorted, (int)rows, (int)E, (int)top_k, L, (int)e_lo, (int)e_hi);
     if (rc) return rc;
     MoeExpertParams p = {};
     p.E = (int)E;
@@ -542,6 +556,7 @@ int launch_moe(lq_ctx* ctx, const lq_q8_tensor* router, const lq_q8_tensor* gate
     p.counts = L.counts;
     p.active = L.active;
     p.err = ctx->err_flag;
+    p.e_base = (int)e_lo;
     // gate/up -> h = silu(g) * u as Q8_0 per pair
     p.rows_per_expert = (int)(2 * inter);
     p.out_rows = (int)inter;
@@ -587,5 +602,35 @@ extern "C" int lq_moe_forward(lq_ctx* ctx, const lq_q8_tensor* router, const lq_
     const int rc = lq::ensure_scratch(ctx, lq::moe_scratch_bytes(rows, E, top_k, H, I));
     if (rc) return rc;
     return lq::launch_moe(ctx, router, &experts->gate_up, &experts->down, E, I, top_k, norm_topk, xq, xd, rows, H, out,
-                          residual, ctx->scratch, ids_out, weights_out);
+                          residual, ctx->scratch, ids_out, weights_out, 0, E);
+}
+
+extern "C" int lq_moe_forward_ep(lq_ctx* ctx, lq_comm* comm, const lq_q8_tensor* router, const lq_moe_experts* local,
+                                 int64_t first_expert, const int8_t* xq, const uint16_t* xd, int64_t rows,
+                                 int64_t top_k, int norm_topk, float* out, const float* residual) {
+    LQ_ENTRY(ctx, "lq_moe_forward_ep");
+    LQ_REQUIRE(ctx, comm && lq::comm_ctx(comm) == ctx, "lq_moe_forward_ep: communicator of another context");
+    LQ_REQUIRE(ctx, router && local, "lq_moe_forward_ep: NULL weights");
+    const int64_t E = router->n, El = local->n_experts, I = local->inter, H = local->hidden;
+    LQ_REQUIRE(ctx, E > 0 && E <= lq::MOE_MAX_E && top_k > 0 && top_k <= lq::MOE_MAX_K && top_k <= E,
+               "lq_moe_forward_ep: need 0 < top_k <= min(E, %d) and E <= %d", lq::MOE_MAX_K, lq::MOE_MAX_E);
+    LQ_REQUIRE(ctx, El > 0 && first_expert >= 0 && first_expert + El <= E,
+               "lq_moe_forward_ep: local experts [%lld, %lld) outside [0, %lld)", (long long)first_expert,
+               (long long)(first_expert + El), (long long)E);
+    LQ_REQUIRE(ctx, H > 0 && H % 256 == 0 && H <= 8192 && I > 0 && I % 256 == 0 && I <= 8192 && router->k == H,
+               "lq_moe_forward_ep: hidden and inter must be multiples of 256 (at most 8192)");
+    LQ_REQUIRE(ctx, local->gate_up.n == El * 2 * I && local->gate_up.k == H && local->down.n == El * H &&
+                        local->down.k == I,
+               "lq_moe_forward_ep: local expert stacks must be [El*2*inter][hidden] and [El*hidden][inter]");
+    LQ_REQUIRE(ctx, rows >= 0 && rows * top_k <= 49152, "lq_moe_forward_ep: rows * top_k must be at most 49152");
+    if (rows == 0) return LQ_OK;
+    LQ_REQUIRE(ctx, xq && xd && out, "lq_moe_forward_ep: NULL activation");
+    int rc = lq::ensure_scratch(ctx, lq::moe_scratch_bytes(rows, E, top_k, H, I));
+    if (rc) return rc;
+    // this rank's experts, the residual on rank 0 only, then the sum over ranks
+    rc = lq::launch_moe(ctx, router, &local->gate_up, &local->down, E, I, top_k, norm_topk, xq, xd, rows, H, out,
+                        lq::comm_rank(comm) == 0 ? residual : nullptr, ctx->scratch, nullptr, nullptr, first_expert,
+                        first_expert + El);
+    if (rc) return rc;
+    return lq::comm_allreduce_sum_f32(comm, out, out, rows * H);
 }

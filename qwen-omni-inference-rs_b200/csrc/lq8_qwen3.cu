@@ -63,6 +63,8 @@ struct lq_model {
     // tensor parallelism: this rank's shard sizes (the whole model when tp == 1)
     lq_comm* comm = nullptr;
     int tp = 1, rank = 0;
+    bool ep = false;             // MoE under a communicator: experts split, the rest replicated
+    int64_t E_l = 0, e_lo = 0;   // this rank's experts [e_lo, e_lo + E_l)
     int64_t Hq_l = 0, Hkv_l = 0, I_l = 0, V_l = 0, vocab_off = 0;
     float* part = nullptr;       // row-parallel partial sums [rows][H] (tp > 1)
     float* logits_all = nullptr; // gathered logits [tp][max_batch][V_l] (tp > 1)
@@ -127,14 +129,37 @@ int gen_linear(lq_model* m, uint16_t* tmp, size_t tmp_elems, uint64_t seed, uint
     return LQ_OK;
 }
 
-// post_attention_layernorm -> Q8_0, sparse MoE MLP, residual (in place on m->x)
+// row-parallel output (dense TP's o/down, EP's MoE layer): y = x + partial on rank 0, the
+// partial elsewhere, the sum over ranks into x
+inline bool split_out(const lq_model* m, bool moe_layer) { return m->tp > 1 && (m->ep == moe_layer); }
+inline float* rp_out(lq_model* m, bool moe_layer = false) { return split_out(m, moe_layer) ? m->part : m->x; }
+inline const float* rp_resid(lq_model* m, bool moe_layer = false) {
+    return (split_out(m, moe_layer) && m->rank != 0) ? nullptr : m->x;
+}
+inline int rp_reduce(lq_model* m, int64_t rows, bool moe_layer = false) {
+    if (!split_out(m, moe_layer)) return LQ_OK;
+    return lq::comm_allreduce_sum_f32(m->comm, m->part, m->x, rows * m->c.hidden);
+}
+// greedy argmax over the vocabulary shards (dense TP): global indices, max over ranks
+inline int lm_keys_reduce(lq_model* m, int64_t B) {
+    if (m->tp == 1 || m->ep) return LQ_OK;
+    int rc = lq::launch_keys_offset(m->ctx, m->keys, B, m->vocab_off);
+    if (rc) return rc;
+    return lq::comm_allreduce_max_u64(m->comm, m->keys, B);
+}
+
+// post_attention_layernorm -> Q8_0, sparse MoE MLP, residual (in place on m->x); under EP
+// this rank's experts and a sum all-reduce
 int moe_mlp(lq_model* m, const Layer& ly, int64_t rows) {
     const lq_qwen3_config& c = m->c;
     int rc = lq::launch_rmsnorm(m->ctx, m->x, LQ_DTYPE_F32, rows, c.hidden, ly.post_norm, c.eps, nullptr, m->xq,
                                 m->xd);
     if (rc) return rc;
-    return lq::launch_moe(m->ctx, &ly.router, &ly.moe_gate_up, &ly.moe_down, c.n_experts, c.moe_inter, c.top_k,
-                          c.norm_topk, m->xq, m->xd, rows, c.hidden, m->x, m->x, m->moe_scratch, nullptr, nullptr);
+    rc = lq::launch_moe(m->ctx, &ly.router, &ly.moe_gate_up, &ly.moe_down, c.n_experts, c.moe_inter, c.top_k,
+                        c.norm_topk, m->xq, m->xd, rows, c.hidden, rp_out(m, true), rp_resid(m, true), m->moe_scratch,
+                        nullptr, nullptr, m->e_lo, m->e_lo + m->E_l);
+    if (rc) return rc;
+    return rp_reduce(m, rows, true);
 }
 
 // columns [col0, col0 + dst.k) of every row of the [dst.n][src_k] tensor `tid` (a K-slice for
@@ -153,21 +178,6 @@ int gen_linear_cols(lq_model* m, uint16_t* tmp, size_t tmp_elems, uint64_t seed,
         if (rc) return rc;
     }
     return LQ_OK;
-}
-
-// row-parallel output: y = x + partial on one rank, the sum over ranks into x
-inline float* rp_out(lq_model* m) { return m->tp > 1 ? m->part : m->x; }
-inline const float* rp_resid(lq_model* m) { return (m->tp > 1 && m->rank != 0) ? nullptr : m->x; }
-inline int rp_reduce(lq_model* m, int64_t rows) {
-    if (m->tp == 1) return LQ_OK;
-    return lq::comm_allreduce_sum_f32(m->comm, m->part, m->x, rows * m->c.hidden);
-}
-// greedy argmax over the vocabulary shards: global indices, max over ranks
-inline int lm_keys_reduce(lq_model* m, int64_t B) {
-    if (m->tp == 1) return LQ_OK;
-    int rc = lq::launch_keys_offset(m->ctx, m->keys, B, m->vocab_off);
-    if (rc) return rc;
-    return lq::comm_allreduce_max_u64(m->comm, m->keys, B);
 }
 
 void destroy_graph(lq_model* m) {
@@ -332,10 +342,12 @@ static int create_model(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, 
     LQ_REQUIRE(ctx, ctx_max <= lq::attention_max_ctx(), "lq_qwen3_create: ctx_max %lld exceeds %d",
                (long long)ctx_max, lq::attention_max_ctx());
     LQ_REQUIRE(ctx, !comm || lq::comm_ctx(comm) == ctx, "lq_qwen3_create_tp: communicator of another context");
-    LQ_REQUIRE(ctx, T == 1 || (!moe && !c.tied && c.n_heads % T == 0 && c.n_kv_heads % T == 0 &&
-                               c.inter % (32 * T) == 0 && c.vocab % T == 0),
+    LQ_REQUIRE(ctx, T == 1 || moe || (!c.tied && c.n_heads % T == 0 && c.n_kv_heads % T == 0 &&
+                                       c.inter % (32 * T) == 0 && c.vocab % T == 0),
                "lq_qwen3_create_tp: %d ranks need a dense untied model with n_heads, n_kv_heads, inter/32 and "
                "vocab divisible by the world size", T);
+    LQ_REQUIRE(ctx, T == 1 || !moe || c.n_experts % T == 0,
+               "lq_qwen3_create_tp: expert parallelism needs n_experts divisible by the world size (%d)", T);
 
     lq_model* m = new lq_model();
     m->comm = comm;
@@ -346,14 +358,21 @@ static int create_model(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, 
     m->max_batch = max_batch;
     m->ctx_max = ctx_max;
     m->moe = moe;
-    // this rank's shard (the whole model when T == 1)
-    const int64_t H = c.hidden, D = c.head_dim, Hq = c.n_heads / T, Hkv = c.n_kv_heads / T, V = c.vocab;
-    const int64_t I = moe ? c.moe_inter : c.inter / T, E = moe ? c.n_experts : 0, Vl = V / T;
+    // this rank's shard (the whole model when T == 1; MoE under T > 1: experts only)
+    const bool ep = moe && T > 1;
+    const int Ta = ep ? 1 : T;  // the attention / dense-MLP / vocabulary split
+    const int64_t H = c.hidden, D = c.head_dim, Hq = c.n_heads / Ta, Hkv = c.n_kv_heads / Ta, V = c.vocab;
+    const int64_t I = moe ? c.moe_inter : c.inter / T, E = moe ? c.n_experts : 0, Vl = V / Ta;
+    const int64_t El = moe ? E / T : 0;
+    m->ep = ep;
+    m->E_l = El;
+    m->e_lo = (int64_t)rank * El;
     m->Hq_l = Hq;
     m->Hkv_l = Hkv;
     m->I_l = I;
     m->V_l = Vl;
-    m->vocab_off = (int64_t)rank * Vl;
+    m->vocab_off = ep ? 0 : (int64_t)rank * Vl;
+    const int rank_a = ep ? 0 : rank;  // shard index of the attention / vocabulary split
     m->Nq = Hq * D;
     m->Nk = Hkv * D;
     m->Nqkv = m->Nq + 2 * m->Nk;
@@ -372,8 +391,8 @@ static int create_model(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, 
         RC(alloc_q8(m, &ly.o, H, m->Hqd));
         if (moe) {
             RC(alloc_q8(m, &ly.router, E, H));
-            RC(alloc_q8(m, &ly.moe_gate_up, E * 2 * I, H));
-            RC(alloc_q8(m, &ly.moe_down, E * H, I));
+            RC(alloc_q8(m, &ly.moe_gate_up, El * 2 * I, H));
+            RC(alloc_q8(m, &ly.moe_down, El * H, I));
         } else {
             RC(alloc_q8(m, &ly.gate_up, 2 * I, H));
             RC(alloc_q8(m, &ly.down, H, I));
@@ -394,17 +413,18 @@ static int create_model(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, 
     for (int64_t l = 0; l < c.layers; l++) {
         Layer& ly = m->layers[(size_t)l];
         // column-parallel q/k/v: this rank's heads; row-parallel o: its heads' K columns
-        RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_Q), ly.qkv, 0, m->Nq, rank * m->Nq));
-        RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_K), ly.qkv, m->Nq, m->Nk, rank * m->Nk));
-        RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_V), ly.qkv, m->Nq + m->Nk, m->Nk, rank * m->Nk));
-        if (T > 1) RC(gen_linear_cols(m, tmp, tmp_elems, seed, tid_layer(l, K_O), ly.o, c.n_heads * D, rank * m->Hqd));
+        RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_Q), ly.qkv, 0, m->Nq, rank_a * m->Nq));
+        RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_K), ly.qkv, m->Nq, m->Nk, rank_a * m->Nk));
+        RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_V), ly.qkv, m->Nq + m->Nk, m->Nk, rank_a * m->Nk));
+        if (Ta > 1) RC(gen_linear_cols(m, tmp, tmp_elems, seed, tid_layer(l, K_O), ly.o, c.n_heads * D, rank * m->Hqd));
         else RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_O), ly.o, 0, H));
         if (moe) {
             RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_ROUTER), ly.router, 0, E));
-            for (int64_t e = 0; e < E; e++) {
-                RC(gen_linear(m, tmp, tmp_elems, seed, tid_expert(l, e, 0), ly.moe_gate_up, e * 2 * I, I));
-                RC(gen_linear(m, tmp, tmp_elems, seed, tid_expert(l, e, 1), ly.moe_gate_up, e * 2 * I + I, I));
-                RC(gen_linear(m, tmp, tmp_elems, seed, tid_expert(l, e, 2), ly.moe_down, e * H, H));
+            for (int64_t j = 0; j < El; j++) {  // local slot j holds expert e_lo + j
+                const int64_t e = m->e_lo + j;
+                RC(gen_linear(m, tmp, tmp_elems, seed, tid_expert(l, e, 0), ly.moe_gate_up, j * 2 * I, I));
+                RC(gen_linear(m, tmp, tmp_elems, seed, tid_expert(l, e, 1), ly.moe_gate_up, j * 2 * I + I, I));
+                RC(gen_linear(m, tmp, tmp_elems, seed, tid_expert(l, e, 2), ly.moe_down, j * H, H));
             }
         } else {
             RC(gen_linear(m, tmp, tmp_elems, seed, tid_layer(l, K_GATE), ly.gate_up, 0, I, rank * I));
@@ -423,7 +443,7 @@ static int create_model(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, 
         // tied embeddings: the LM head is the Q8_0 quantization of the bf16 table
         RC(lq::launch_quantize_rows(ctx, m->embed, LQ_DTYPE_BF16, V, H, m->lm_head.qs, m->lm_head.d));
     } else {
-        RC(gen_linear(m, tmp, tmp_elems, seed, TID_LMHEAD, m->lm_head, 0, Vl, rank * Vl));
+        RC(gen_linear(m, tmp, tmp_elems, seed, TID_LMHEAD, m->lm_head, 0, Vl, rank_a * Vl));
     }
     // caches and activations
     size_t kv = (size_t)(c.layers * max_batch * Hkv * ctx_max * D);
@@ -442,10 +462,8 @@ static int create_model(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, 
     RC(dalloc_t(m, &m->q_rot, (size_t)(R * m->Hqd)));
     RC(dalloc_t(m, &m->gu, (size_t)(R * 2 * I)));
     RC(dalloc_t(m, &m->logits, (size_t)(max_batch * Vl)));
-    if (T > 1) {
-        RC(dalloc_t(m, &m->part, (size_t)(R * H)));
-        RC(dalloc_t(m, &m->logits_all, (size_t)(T * max_batch * Vl)));
-    }
+    if (T > 1) RC(dalloc_t(m, &m->part, (size_t)(R * H)));
+    if (Ta > 1) RC(dalloc_t(m, &m->logits_all, (size_t)(T * max_batch * Vl)));
     RC(dalloc_t(m, &m->keys, (size_t)max_batch));
     RC(dalloc_t(m, &m->tokens, (size_t)R));
     RC(dalloc_t(m, &m->pos_dev, 1));
@@ -499,7 +517,7 @@ int lq_qwen3_create_tp(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, i
 static int logits_to_host(lq_model* m, int64_t nb, float* host) {
     lq_ctx* ctx = m->ctx;
     const int64_t V = m->c.vocab, Vl = m->V_l;
-    if (m->tp == 1) {
+    if (m->tp == 1 || m->ep) {
         LQ_CUDA(ctx, cudaMemcpyAsync(host, m->logits, (size_t)(nb * V) * 4, cudaMemcpyDeviceToHost, ctx->stream));
         return LQ_OK;
     }
@@ -663,11 +681,13 @@ int lq_qwen3_expert(lq_model* m, int64_t layer, int64_t expert, int kind, lq_q8_
         *out = ly.router;
         return LQ_OK;
     }
-    LQ_REQUIRE(ctx, expert >= 0 && expert < m->c.n_experts, "lq_qwen3_expert: expert out of range");
+    LQ_REQUIRE(ctx, expert >= m->e_lo && expert < m->e_lo + m->E_l,
+               "lq_qwen3_expert: expert %lld not held by this rank", (long long)expert);
+    const int64_t j = expert - m->e_lo;
     switch (kind) {
-        case 11: *out = rows_view(ly.moe_gate_up, expert * 2 * I, I); break;
-        case 12: *out = rows_view(ly.moe_gate_up, expert * 2 * I + I, I); break;
-        case 13: *out = rows_view(ly.moe_down, expert * H, H); break;
+        case 11: *out = rows_view(ly.moe_gate_up, j * 2 * I, I); break;
+        case 12: *out = rows_view(ly.moe_gate_up, j * 2 * I + I, I); break;
+        case 13: *out = rows_view(ly.moe_down, j * H, H); break;
         default: return lq::set_error(ctx, LQ_ERR_INVALID_ARG, "lq_qwen3_expert: kind %d", kind);
     }
     return LQ_OK;

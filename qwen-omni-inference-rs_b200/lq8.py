@@ -138,6 +138,8 @@ SIGNATURES = {
     "lq_qwen3_expert": (C.c_int, [_P, _I64, _I64, C.c_int, C.POINTER(Q8Tensor)]),
     "lq_moe_forward": (C.c_int, [_P, C.POINTER(Q8Tensor), C.POINTER(MoeExperts), _P, _P, _I64, _I64, C.c_int,
                                  _P, _P, _P, _P]),
+    "lq_moe_forward_ep": (C.c_int, [_P, _P, C.POINTER(Q8Tensor), C.POINTER(MoeExperts), _I64, _P, _P, _I64, _I64,
+                                    C.c_int, _P, _P]),
 }
 
 

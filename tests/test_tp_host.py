@@ -127,3 +127,61 @@ def test_tp_collectives_gloo_world2():
         assert ok_sum, rank
         assert tok == want, (rank, tok, want)
         assert want[1] == 40 * 2 - 3  # the tie went to the higher index
+
+
+def _ep_rank(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import sys
+        sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
+        from oracle import oracle as O
+        rng = np.random.default_rng(9)  # same weights and tokens on every rank
+        rows, H, E, K, I = 7, 256, 8, 2, 256
+
+        def q8(n, k):
+            return (rng.integers(-127, 128, size=(n, k), dtype=np.int8),
+                    rng.integers(0x1400, 0x2000, size=(n, k // 32)).astype(np.uint16))
+
+        xb = O.f32_to_bf16(rng.standard_normal((rows, H)).astype(np.float32))
+        router = q8(E, H)
+        gate = [q8(I, H) for _ in range(E)]
+        up = [q8(I, H) for _ in range(E)]
+        down = [q8(H, I) for _ in range(E)]
+        full, ids, _ = O.moe_forward(xb, router, gate, up, down, K)
+        # this rank's experts only: the others contribute zero (routing is unchanged)
+        El = E // world
+        zero = lambda w: (np.zeros_like(w[0]), np.zeros_like(w[1]))
+        mine = lambda lst: [w if rank * El <= e < (rank + 1) * El else zero(w) for e, w in enumerate(lst)]
+        part, ids_r, _ = O.moe_forward(xb, router, mine(gate), mine(up), mine(down), K)
+        t = torch.from_numpy(part)
+        dist.all_reduce(t)
+        scale = float(np.max(np.abs(full)))
+        q.put((rank, bool(np.array_equal(ids, ids_r)), float(np.max(np.abs(t.numpy() - full)) / scale)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_combine_gloo_world2():
+    """Expert parallelism on world_size-2 gloo ranks with the oracle: with the router
+    replicated every rank routes identically; each rank adds only its experts'
+    contributions and a sum all-reduce recovers the full MoE layer up to the regrouping of
+    the f32 expert sum."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ep_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, same_ids, rel in res:
+        assert same_ids, rank
+        assert rel <= 1e-6, (rank, rel)
