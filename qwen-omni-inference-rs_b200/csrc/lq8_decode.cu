@@ -1,0 +1,926 @@
+// lq8_decode.cu -- the whole decode step of a dense Qwen3 model (batch M <= 4) as one
+// persistent kernel: every layer's q|k|v GEMV, attention, o GEMV, gate|up GEMV and down GEMV,
+// then the LM head with the greedy argmax keys.
+//
+// One CTA per SM (cooperative launch, so every CTA is resident). Its producer warp streams the
+// tiles of every weight matrix of the step, in step order, into an 8-stage shared-memory ring:
+// a stage is 16 rows x up to 1 KiB of K plus their fp16 scales (17 KiB), two 2-D TMA boxes (the
+// weights viewed as 8-byte elements, so one box carries 16 x 1 KiB). The producer never waits
+// for activations: while the consumer warps sit at a grid barrier or in attention, the ring
+// fills with the next matrix's tiles, so HBM keeps streaming across the phase boundaries that
+// separate kernels elsewhere.
+//
+// The consumer warps walk the phases, with a grid barrier (a global counter, bounded spin)
+// wherever a phase reads what other CTAs wrote:
+//   QKV  RMSNorm + Q8_0 of x (every CTA, redundantly), q|k|v rows                      | barrier
+//   ATT  items (row, kv head, 64-position chunk): q/k RMSNorm + RoPE, the new position's
+//        k/v appended to the caches, scores, chunk softmax, P.V; the last item of a
+//        (row, kv head) merges the chunks and writes the Q8_0 attention output         | barrier
+//   O    o rows + residual -> x                                                       | barrier
+//   GU   RMSNorm prologue, gate|up rows, SiLU(gate)*up -> h, quantized per unit      | barrier
+//   DN   h (Q8_0) as activations, down rows + residual -> x                           | barrier
+//   LM   final RMSNorm, LM-head rows -> logits, greedy argmax keys
+// GEMV units (16 output rows; 32 for gate|up, one Q8_0 block of h) are dealt to CTAs
+// round-robin over one sequence that runs through all phases, so the CTAs' totals differ by
+// one unit; the producer tags each stage with its unit and closes each phase with a marker
+// stage. Attention items are claimed from a per-layer counter as CTAs become free.
+// Every arithmetic step is the one of the five-kernel decode path (the same row functions,
+// the same per-lane block order and warp sums, the same attention order), so the logits are
+// bit-identical to it. Data written by other CTAs is read through L2 (ld.cg / cp.async.cg).
+#include "lq8_async.cuh"
+#include "lq8_fused.cuh"
+#include "lq8_internal.cuh"
+#include "lq8_tma.cuh"
+
+#include <algorithm>
+#include <cstdlib>
+#include <vector>
+
+namespace lq {
+
+constexpr int PD_ROWS = 16;  // weight rows per stage (two per consumer warp)
+constexpr int PD_KC = 1024;  // K bytes per stage (one Q8_0 block per lane and row)
+constexpr int PD_STAGE = PD_ROWS * PD_KC + PD_ROWS * (PD_KC / 32) * 2;  // 17 KiB
+constexpr int PD_STAGES = 8;
+constexpr int PD_CONS = 8;
+constexpr int PD_CTHREADS = PD_CONS * 32;
+constexpr int PD_THREADS = PD_CTHREADS + 32;
+constexpr int PD_ATT_C = 64;
+constexpr int PD_KS = 128 + 4;  // padded K row (floats): conflict-free float4 reads
+constexpr int PD_MAX_SPLITS = 128;
+constexpr int PD_MAX_G = 8;
+constexpr uint64_t PD_WAIT_NS = 2000000000ull;
+
+// one weight matrix: its Q8_0 rows viewed as [N][K/8] 8-byte elements and its scales [N][K/32]
+struct alignas(64) PdMat {
+    CUtensorMap wq;
+    CUtensorMap wd;
+};
+
+// the device descriptor of one layer; the LM head is mat[0] of the entry after the last layer
+struct alignas(64) PdLayer {
+    PdMat mat[4];  // q|k|v, o, gate|up, down
+    const uint16_t *in_norm, *post_norm, *q_norm, *k_norm;
+    float *kc, *vc;  // [M][Hkv][ctx_max][128]
+};
+
+struct PdParams {
+    const PdLayer* layers;  // [n_layers + 1]
+    int n_layers;
+    const uint16_t* final_norm;
+    int H, Hq, Hkv, I, V, Nqkv, ctx_max;
+    float eps;
+    const float* cos_t;
+    const float* sin_t;
+    const int32_t* pos_dev;
+    float* x;                  // [M][H]
+    float* qkv;                // [M][Nqkv]
+    int8_t* att_q;             // [M][Hq*128]
+    uint16_t* att_d;
+    int8_t* hq;                // [M][I] Q8_0 of SiLU(gate)*up
+    uint16_t* hd;              // [M][I/32]
+    float* part_o;             // [M][Hq][PD_MAX_SPLITS][128]
+    float* part_ml;            // [M][Hq][PD_MAX_SPLITS][2]
+    float* logits;             // [M][V]
+    unsigned long long* keys;  // [M]
+    unsigned* bar;             // [0] grid barrier, [1 + b*Hkv + kvh] chunk counters, then the
+                               // attention item counters (one per layer); zero at launch
+    int* err;
+};
+
+// attention staging (the union area during ATT)
+struct PdAtt {
+    float ks[PD_ATT_C][PD_KS];
+    float vs[PD_ATT_C][128];
+    float qraw[PD_MAX_G][128];
+    float qs[PD_MAX_G][128];
+    float kvraw[2][128];
+    float ps[PD_MAX_G][PD_ATT_C];
+    float ml[PD_MAX_G][2];
+    float cm[PD_MAX_G][PD_MAX_SPLITS];
+    float cl[PD_MAX_G];
+    int last;
+};
+
+// 128-byte multiple: the union area behind it takes 16-byte vector and cp.async accesses
+struct alignas(128) PdSmem {
+    uint8_t stage[PD_STAGES][PD_STAGE];
+    uint64_t full[PD_STAGES];
+    uint64_t empty[PD_STAGES];
+    float red[32];
+    unsigned long long keys[4];
+    int tag[PD_STAGES];    // the unit a stage belongs to (-1: the phase has no more units for us)
+    uint64_t hfull[2];     // gate|up: hbuf[b] written by the 8 consumer warps
+    uint64_t hfree[2];     // gate|up: hbuf[b] quantized by warp 0
+    float hbuf[2][4][32];  // gate|up: one Q8_0 block of SiLU(gate)*up per row (two units in turn)
+    int item;              // attention: the next item of this CTA
+    int flag;  // grid barrier outcome
+    int fail;  // a consumer warp gave up waiting for a stage
+    int pad_[2];
+    // followed by the union area: the GEMV activations or PdAtt
+};
+
+static_assert(sizeof(PdSmem) % 128 == 0 && PD_STAGE % 128 == 0, "shared-memory regions must stay 128-byte aligned");
+
+enum { PH_QKV = 0, PH_O = 1, PH_GU = 2, PH_DN = 3, PH_LM = 4 };
+
+struct PdGemv {
+    const PdMat* mat;
+    int N, K;
+    bool swi;
+};
+
+__device__ __forceinline__ PdGemv pd_gemv(const PdParams& p, int layer, int kind) {
+    PdGemv g;
+    g.swi = false;
+    if (kind == PH_LM) {
+        g.mat = &p.layers[p.n_layers].mat[0];
+        g.N = p.V;
+        g.K = p.H;
+        return g;
+    }
+    g.mat = &p.layers[layer].mat[kind];
+    switch (kind) {
+        case PH_QKV: g.N = p.Nqkv; g.K = p.H; break;
+        case PH_O: g.N = p.H; g.K = p.Hq * 128; break;
+        case PH_GU: g.N = 2 * p.I; g.K = p.H; g.swi = true; break;
+        default: g.N = p.H; g.K = p.I; break;
+    }
+    return g;
+}
+
+// a unit is PD_ROWS output rows; for gate|up 32 outputs (one Q8_0 block of h): two groups of
+// 16 rows, each as its gate rows and then its up rows
+__device__ __forceinline__ int pd_unit_rows(const PdGemv& g) { return g.swi ? 2 * PD_ROWS : PD_ROWS; }
+__device__ __forceinline__ int pd_units(const PdGemv& g) {
+    const int nout = g.swi ? g.N / 2 : g.N;
+    return (nout + pd_unit_rows(g) - 1) / pd_unit_rows(g);
+}
+// attention item counter of layer l
+__device__ __forceinline__ unsigned* pd_att_ctr(const PdParams& p, int M, int l) {
+    return p.bar + 1 + M * p.Hkv + l;
+}
+
+__device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
+
+// bounded mbarrier wait that also gives up once another CTA has flagged an error
+__device__ __forceinline__ bool pd_wait(uint64_t* bar, unsigned parity, const int* err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (int i = 1;; i++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 15) == 0 && (ld_volatile(err) != 0 || global_ns() - t0 > PD_WAIT_NS)) return false;
+    }
+}
+
+// the first unit of this CTA in a phase whose units start at position `off` of the sequence
+__device__ __forceinline__ int pd_first(unsigned off) {
+    const unsigned G = gridDim.x;
+    return (int)((blockIdx.x + G - off % G) % G);
+}
+
+// ---- producer: the units of one GEMV phase dealt to this CTA, their tiles streamed ----
+// (Claiming units from a counter instead balanced worse: the producers claim ahead by up to a
+// ring of tiles, so the first CTAs to reach a phase took most of its units.)
+__device__ __forceinline__ bool pd_produce(PdSmem& S, const PdGemv& g, unsigned off, int& it, int* err) {
+    const int K = g.K;
+    const int kc = K < PD_KC ? K : PD_KC;
+    const int nchunks = (K + kc - 1) / kc;
+    const int nout = g.swi ? g.N / 2 : g.N;
+    const int units = pd_units(g);
+    const int halves = g.swi ? 2 : 1;
+    const unsigned bytes = (unsigned)(PD_ROWS * kc + PD_ROWS * (kc / 16));  // whole boxes (OOB zero-filled)
+    for (int u = pd_first(off);; u += gridDim.x) {
+        const int s0 = it % PD_STAGES;
+        if (u >= units) {
+            // phase end marker: a stage without data
+            if (!pd_wait(&S.empty[s0], ((unsigned)(it / PD_STAGES) & 1u) ^ 1u, err)) {
+                atomicCAS(err, 0, 41);
+                return false;
+            }
+            S.tag[s0] = -1;
+            mbar_arrive(&S.full[s0]);
+            it++;
+            return true;
+        }
+        for (int grp = 0; grp < halves; grp++)
+            for (int half = 0; half < halves; half++) {
+                const int r0 = half * nout + u * pd_unit_rows(g) + grp * PD_ROWS;
+                for (int c = 0; c < nchunks; c++, it++) {
+                    const int s = it % PD_STAGES;
+                    if (!pd_wait(&S.empty[s], ((unsigned)(it / PD_STAGES) & 1u) ^ 1u, err)) {
+                        atomicCAS(err, 0, 41);
+                        return false;
+                    }
+                    uint8_t* st = S.stage[s];
+                    S.tag[s] = u;
+                    mbar_expect_tx(&S.full[s], bytes);
+                    tma_load_2d(st, &g.mat->wq, c * (kc / 8), r0, &S.full[s]);
+                    tma_load_2d(st + PD_ROWS * kc, &g.mat->wd, c * (kc / 32), r0, &S.full[s]);
+                }
+            }
+    }
+}
+
+// ---- consumers ----
+__device__ __forceinline__ void pd_csync() { group_sync<PD_CTHREADS, 1>(); }
+
+// grid barrier of the consumer groups: the k-th barrier completes when the counter reaches
+// k * gridDim.x. Returns false when it gave up (~2 s) or another CTA flagged an error.
+__device__ __forceinline__ bool pd_grid_barrier(const PdParams& p, PdSmem& S, unsigned& epoch) {
+    pd_csync();
+    epoch++;
+    if (threadIdx.x == 0) {
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
+        const unsigned target = epoch * gridDim.x;
+        const uint64_t t0 = global_ns();
+        int ok = 1;
+        for (int i = 1;; i++) {
+            unsigned v;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p.bar) : "memory");
+            if (v >= target) break;
+            if ((i & 63) == 0) {
+                if (ld_volatile(p.err) != 0) { ok = 0; break; }
+                if (global_ns() - t0 > PD_WAIT_NS) { atomicCAS(p.err, 0, 42); ok = 0; break; }
+            }
+        }
+        S.flag = ok;
+    }
+    pd_csync();
+    return S.flag != 0;
+}
+
+// `bytes` (a multiple of 16) into shared memory through L2 with every 16-byte copy in flight;
+// completes at the next cp_async_wait
+__device__ __forceinline__ void pd_prefetch(void* dst, const void* src, int bytes, int tid) {
+    for (int i = tid * 16; i < bytes; i += PD_CTHREADS * 16)
+        cp_async16(static_cast<uint8_t*>(dst) + i, static_cast<const uint8_t*>(src) + i, true);
+    cp_async_commit();
+}
+
+// f32 values written by other CTAs into shared memory through L2, every 16-byte copy in
+// flight at once (one round trip); the caller syncs the consumers before reading dst
+__device__ __forceinline__ void pd_stage_f32(float* dst, const float* src, int n, int tid) {
+    for (int i = tid * 4; i < n; i += PD_CTHREADS * 4) cp_async16(dst + i, src + i, true);
+    cp_async_commit();
+    cp_async_wait<0>();
+}
+
+// Q8_0 of 32 values, one per lane (GGML's block quantization: d = amax/127, q = round(v/d))
+__device__ __forceinline__ void pd_quant_warp32(float v, int lane, int8_t* q_out, uint16_t* d_out) {
+    const float amax = warp_max(fabsf(v));
+    float d, id;
+    q8_scale(amax, d, id);
+    q_out[lane] = (int8_t)q8_quant(v, id);
+    if (lane == 0) *d_out = f2h(d);
+}
+
+// The integer sum of a Q8_0 block, w . x over 32 int8 pairs. Lanes 4-7 of each quarter-warp
+// read the second 16 bytes first (sw = 1) and pair them with the same half of the other
+// operand: the 16-byte shared-memory reads of a quarter-warp then cover all 32 banks once,
+// and the (exact, integer) sum is the same in either order.
+__device__ __forceinline__ int pd_block_sum(const int4 wa, const int4 wb, const int4 xa, const int4 xb) {
+    int sum = 0;
+    sum = __dp4a(wa.x, xa.x, sum); sum = __dp4a(wa.y, xa.y, sum);
+    sum = __dp4a(wa.z, xa.z, sum); sum = __dp4a(wa.w, xa.w, sum);
+    sum = __dp4a(wb.x, xb.x, sum); sum = __dp4a(wb.y, xb.y, sum);
+    sum = __dp4a(wb.z, xb.z, sum); sum = __dp4a(wb.w, xb.w, sum);
+    return sum;
+}
+
+// the units of one GEMV phase that this CTA's producer claimed, against the activations
+// xs/xds in shared memory: out[m][row] (+ the residual already in out), logits + argmax keys,
+// or h = SiLU(gate)*up quantized to Q8_0 (hq, hd).
+// A stage holds 16 rows x kc (<= 1 KiB) of K; warp w takes rows 2w and 2w+1 against one read
+// of the activations, lane l block l of the chunk. Per output the lane accumulates the blocks
+// l, 32+l, 64+l, ... in order and a butterfly sums the lanes: the decode GEMV's order.
+// hn counts this CTA's gate|up units over the whole step (it indexes the h handoff buffers).
+template <int M>
+__device__ __forceinline__ bool pd_consume(PdSmem& S, const PdGemv& g, const int8_t* xs, const uint16_t* xds,
+                                           int& it, int& hn, float* out, int ldo, bool resid, bool keys,
+                                           int8_t* hq, uint16_t* hd, int* err) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int sw = (lane >> 2) & 1;
+    const int K = g.K, nb = K >> 5;
+    const int kc = K < PD_KC ? K : PD_KC;
+    const int nchunks = (K + kc - 1) / kc;
+    const int nout = g.swi ? g.N / 2 : g.N;
+    const int halves = g.swi ? 2 : 1;
+    float acc[2][M], gate[2][M];
+#pragma unroll
+    for (int r = 0; r < 2; r++)
+#pragma unroll
+        for (int m = 0; m < M; m++) acc[r][m] = gate[r][m] = 0.0f;
+    // a warp that gives up waiting leaves the phase at once; every warp then meets the others
+    // at the closing consumer barrier (all waits below are bounded)
+    bool failed = false;
+    auto wait_full = [&](int s) {
+        int ok = 1;
+        if (lane == 0) ok = pd_wait(&S.full[s], (unsigned)(it / PD_STAGES) & 1u, err);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        __syncwarp();  // the other lanes read the stage after lane 0 saw it complete
+        if (!ok) {
+            if (lane == 0) {
+                atomicCAS(err, 0, 43);
+                S.fail = 1;
+            }
+            failed = true;
+        }
+        return ok != 0;
+    };
+    while (!failed) {
+        const int s0 = it % PD_STAGES;
+        if (!wait_full(s0)) break;
+        int u = 0;
+        if (lane == 0) u = S.tag[s0];
+        u = __shfl_sync(0xffffffffu, u, 0);
+        if (u < 0) {  // no more units: release the marker stage
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.empty[s0]);
+            it++;
+            break;
+        }
+        const int hb = hn & 1, huse = hn >> 1;
+        if (g.swi && huse > 0) {  // warp 0 is done with this buffer's previous unit
+            int ok = 1;
+            if (lane == 0) ok = pd_wait(&S.hfree[hb], (unsigned)(huse - 1) & 1u, err);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) {
+                if (lane == 0) {
+                    atomicCAS(err, 0, 45);
+                    S.fail = 1;
+                }
+                failed = true;
+            }
+        }
+        // the residual of the output this lane writes (lane 8r + m: row 2w + r, token m), read
+        // now so that its L2 round trip overlaps the unit
+        float res = 0.0f;
+        if (resid && !g.swi && (lane & 7) < M && 2 * warp + (lane >> 3) < min(PD_ROWS, nout - u * PD_ROWS) &&
+            lane < 16)
+            res = __ldcg(out + (size_t)(lane & 7) * ldo + u * PD_ROWS + 2 * warp + (lane >> 3));
+        for (int grp = 0; grp < halves && !failed; grp++)
+        for (int half = 0; half < halves && !failed; half++) {
+            const int r0 = u * pd_unit_rows(g) + grp * PD_ROWS;
+            const int rows = min(PD_ROWS, nout - r0);
+            for (int c = 0; c < nchunks; c++, it++) {
+                const int s = it % PD_STAGES;
+                if ((grp | half | c) != 0 && !wait_full(s)) break;
+                const int k0 = c * kc, nbc = min(kc, K - k0) >> 5;
+                const bool act = lane < nbc;
+                const int8_t* wst = reinterpret_cast<const int8_t*>(S.stage[s]) + (2 * warp) * kc + lane * 32;
+                const uint16_t* dst = reinterpret_cast<const uint16_t*>(S.stage[s] + PD_ROWS * kc) + (2 * warp) * (kc / 32) + lane;
+                int4 w[2][2];
+                float dw[2] = {0.f, 0.f};
+                if (act) {
+#pragma unroll
+                    for (int r = 0; r < 2; r++) {
+                        w[r][0] = *reinterpret_cast<const int4*>(wst + r * kc + sw * 16);
+                        w[r][1] = *reinterpret_cast<const int4*>(wst + r * kc + (sw ^ 1) * 16);
+                        dw[r] = h2f(dst[r * (kc / 32)]);
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.empty[s]);
+                if (act) {
+                    const int gb = (k0 >> 5) + lane;
+#pragma unroll
+                    for (int m = 0; m < M; m++) {
+                        const int4* xp = reinterpret_cast<const int4*>(xs + (size_t)m * K + (size_t)gb * 32);
+                        const int4 xa = xp[sw], xb = xp[sw ^ 1];
+                        const float dx = h2f(xds[(size_t)m * nb + gb]);
+#pragma unroll
+                        for (int r = 0; r < 2; r++) {
+                            const int sum = pd_block_sum(w[r][0], w[r][1], xa, xb);
+                            acc[r][m] = __fadd_rn(acc[r][m], __fmul_rn((float)sum, __fmul_rn(dw[r], dx)));
+                        }
+                    }
+                }
+                if (c == nchunks - 1) {
+#pragma unroll
+                    for (int r = 0; r < 2; r++) {
+                        const int rr = 2 * warp + r, row = r0 + rr;
+#pragma unroll
+                        for (int m = 0; m < M; m++) {
+                            const float v = warp_sum(acc[r][m]);
+                            acc[r][m] = 0.0f;
+                            if (g.swi) {
+                                if (half == 0) gate[r][m] = v;
+                                else if (lane == 0) S.hbuf[hb][m][grp * PD_ROWS + rr] = swiglu(gate[r][m], v);
+                            } else if (rr < rows) {
+                                if (lane == 8 * r + m) {
+                                    const size_t o = (size_t)m * ldo + row;
+                                    out[o] = resid ? __fadd_rn(res, v) : v;
+                                }
+                                if (keys && lane == 8 * r) atomicMax(&S.keys[m], argmax_key(v, row));
+                            }
+                        }
+                    }
+                }
+            }
+        }
+        if (g.swi && !failed) {
+            // the unit's 32 outputs are one Q8_0 block of h per row (quant_row's arithmetic):
+            // every warp hands its values over, warp 0 quantizes
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.hfull[hb]);
+            if (warp == 0) {
+                int ok = 1;
+                if (lane == 0) ok = pd_wait(&S.hfull[hb], (unsigned)huse & 1u, err);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                __syncwarp();
+                if (ok) {
+#pragma unroll
+                    for (int m = 0; m < M; m++) {
+                        const size_t e = (size_t)m * nout + (size_t)u * 32;
+                        pd_quant_warp32(S.hbuf[hb][m][lane], lane, hq + e, hd + (e >> 5));
+                    }
+                } else if (lane == 0) {
+                    atomicCAS(err, 0, 46);
+                    S.fail = 1;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.hfree[hb]);
+            }
+        }
+        if (g.swi) hn++;
+    }
+    pd_csync();
+    return S.fail == 0;
+}
+
+// ---- attention (the decode attention kernel's arithmetic, on 256 threads) ----
+
+template <int M>
+__device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdAtt& A, int p0, int nsplit,
+                             unsigned* ctr) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int Hq = p.Hq, Hkv = p.Hkv, G = Hq / Hkv, D = 128;
+    const int heads = Hq + 2 * Hkv;
+    const int n_items = M * Hkv * nsplit;
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
+    const float* cs = p.cos_t + (int64_t)p0 * (D / 2);
+    const float* sn = p.sin_t + (int64_t)p0 * (D / 2);
+    // items are claimed from the phase counter; the next claim is issued while this item runs
+    if (tid == 0) S.item = (int)atomicAdd(ctr, 1u);
+    pd_csync();
+    int item = S.item;
+    while (item < n_items) {
+        int next = 0;
+        if (tid == 0) next = (int)atomicAdd(ctr, 1u);
+        const int split = item % nsplit, kvh = (item / nsplit) % Hkv, b = item / (nsplit * Hkv);
+        const int j0 = split * PD_ATT_C;
+        const int cnt = min(PD_ATT_C, p0 + 1 - j0);
+        const int fresh = p0 - j0;  // chunk row of the new position (when < cnt)
+        float* kbase = L.kc + ((int64_t)b * Hkv + kvh) * (int64_t)p.ctx_max * D + (int64_t)j0 * D;
+        float* vbase = L.vc + ((int64_t)b * Hkv + kvh) * (int64_t)p.ctx_max * D + (int64_t)j0 * D;
+        pd_csync();  // the staging area is free
+        for (int i = tid; i < cnt * (D / 4); i += PD_CTHREADS) {
+            const int r = i / (D / 4), c = (i % (D / 4)) * 4;
+            if (r < fresh) {
+                cp_async16(&A.ks[r][c], kbase + (int64_t)r * D + c, true);
+                cp_async16(&A.vs[r][c], vbase + (int64_t)r * D + c, true);
+            }
+        }
+        cp_async_commit();
+        // this kv head's q heads (and, for the chunk of the new position, its k and v) from
+        // the q|k|v rows
+        const float* qrow = p.qkv + (int64_t)b * heads * D;
+        for (int i = tid; i < G * (D / 4); i += PD_CTHREADS) {
+            const int g = i / (D / 4), c = (i % (D / 4)) * 4;
+            *reinterpret_cast<float4*>(&A.qraw[g][c]) =
+                __ldcg(reinterpret_cast<const float4*>(qrow + (int64_t)(kvh * G + g) * D + c));
+        }
+        const bool has_new = fresh >= 0 && fresh < cnt;
+        if (has_new && tid < 2 * (D / 4)) {
+            const int which = tid / (D / 4), c = (tid % (D / 4)) * 4;  // 0: k, 1: v
+            *reinterpret_cast<float4*>(&A.kvraw[which][c]) =
+                __ldcg(reinterpret_cast<const float4*>(qrow + (int64_t)(Hq + which * Hkv + kvh) * D + c));
+        }
+        pd_csync();
+        for (int g = warp; g < G; g += PD_CONS) head_norm_rope(A.qraw[g], L.q_norm, p.eps, cs, sn, lane, A.qs[g]);
+        if (has_new) {
+            if (warp == 0) {
+                head_norm_rope(A.kvraw[0], L.k_norm, p.eps, cs, sn, lane, A.ks[fresh]);
+                __syncwarp();
+                const float4 kk = *reinterpret_cast<const float4*>(&A.ks[fresh][lane * 4]);
+                *reinterpret_cast<float4*>(kbase + (int64_t)fresh * D + lane * 4) = kk;
+            } else if (warp == 1) {
+                const float4 vv = *reinterpret_cast<const float4*>(&A.kvraw[1][lane * 4]);
+                *reinterpret_cast<float4*>(&A.vs[fresh][lane * 4]) = vv;
+                *reinterpret_cast<float4*>(vbase + (int64_t)fresh * D + lane * 4) = vv;
+            }
+        }
+        cp_async_wait<0>();
+        pd_csync();
+        // scores: thread -> position pp and heads q4, q4 + 4; sequential 128-term dots, then the
+        // scale. K and q are read 32 dims at a time into registers ahead of the add chain.
+        {
+            const int pp = tid % PD_ATT_C, q4 = tid / PD_ATT_C;
+            float s[2] = {0.f, 0.f};
+            if (pp < cnt) {
+#pragma unroll 1
+                for (int d0 = 0; d0 < D; d0 += 32) {
+                    float4 kk[8];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) kk[i] = *reinterpret_cast<const float4*>(&A.ks[pp][d0 + 4 * i]);
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        const int g = q4 + 4 * h;
+                        if (g < G) {
+                            float4 qq[8];
+#pragma unroll
+                            for (int i = 0; i < 8; i++) qq[i] = *reinterpret_cast<const float4*>(&A.qs[g][d0 + 4 * i]);
+#pragma unroll
+                            for (int i = 0; i < 8; i++) {
+                                s[h] = __fadd_rn(s[h], __fmul_rn(qq[i].x, kk[i].x));
+                                s[h] = __fadd_rn(s[h], __fmul_rn(qq[i].y, kk[i].y));
+                                s[h] = __fadd_rn(s[h], __fmul_rn(qq[i].z, kk[i].z));
+                                s[h] = __fadd_rn(s[h], __fmul_rn(qq[i].w, kk[i].w));
+                            }
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                const int g = q4 + 4 * i;
+                if (g < G) A.ps[g][pp] = pp < cnt ? __fmul_rn(s[i], scale) : -INFINITY;
+            }
+        }
+        pd_csync();
+        // chunk softmax per head: max, exp(s - max), sum
+        for (int g = warp; g < G; g += PD_CONS) {
+            const float a = A.ps[g][lane], c = A.ps[g][lane + 32];
+            const float mx = warp_max(fmaxf(a, c));
+            const float ea = expf(__fsub_rn(a, mx)), ec = expf(__fsub_rn(c, mx));
+            A.ps[g][lane] = ea;
+            A.ps[g][lane + 32] = ec;
+            const float sum = warp_sum(__fadd_rn(ea, ec));
+            if (lane == 0) { A.ml[g][0] = mx; A.ml[g][1] = sum; }
+        }
+        pd_csync();
+        // chunk P.V: thread -> dim d and heads hh, hh + 2, ...
+        const int64_t hb0 = ((int64_t)b * Hq + (int64_t)kvh * G) * PD_MAX_SPLITS;
+        {
+            // positions in order, 8 at a time with their V and P values read ahead
+            const int d = tid & (D - 1), hh = tid >> 7;
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            int j0 = 0;
+#pragma unroll 1
+            for (; j0 + 8 <= cnt; j0 += 8) {
+                float vv[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) vv[j] = A.vs[j0 + j][d];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int g = hh + 2 * i;
+                    if (g < G) {
+                        const float4 pa = *reinterpret_cast<const float4*>(&A.ps[g][j0]);
+                        const float4 pb = *reinterpret_cast<const float4*>(&A.ps[g][j0 + 4]);
+                        const float pj[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+                        for (int j = 0; j < 8; j++) acc[i] = __fadd_rn(acc[i], __fmul_rn(pj[j], vv[j]));
+                    }
+                }
+            }
+            for (int j = j0; j < cnt; j++) {
+                const float vv = A.vs[j][d];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int g = hh + 2 * i;
+                    if (g < G) acc[i] = __fadd_rn(acc[i], __fmul_rn(A.ps[g][j], vv));
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int g = hh + 2 * i;
+                if (g < G) p.part_o[(hb0 + (int64_t)g * PD_MAX_SPLITS + split) * D + d] = acc[i];
+            }
+            if (tid < G) {
+                p.part_ml[(hb0 + (int64_t)tid * PD_MAX_SPLITS + split) * 2] = A.ml[tid][0];
+                p.part_ml[(hb0 + (int64_t)tid * PD_MAX_SPLITS + split) * 2 + 1] = A.ml[tid][1];
+            }
+        }
+        // the last chunk of this (row, kv head) to finish merges the chunks
+        unsigned* counter = p.bar + 1 + b * Hkv + kvh;
+        __threadfence();
+        pd_csync();
+        if (tid == 0) A.last = atomicAdd(counter, 1u) == (unsigned)(nsplit - 1);
+        pd_csync();
+        if (A.last) {
+            __threadfence();
+            // the heads' chunk partials into the free staging area (K, V, q rows), as many heads at
+            // a time as fit, every 16-byte copy in flight at once; the first batch lands while the
+            // merge weights are computed
+            float* po_s = &A.ks[0][0];
+            const int hcap = (int)((sizeof(A.ks) + sizeof(A.vs) + sizeof(A.qraw) + sizeof(A.qs)) / 4 /
+                                   ((size_t)nsplit * D));
+            auto stage = [&](int g0) {
+                const int ng = min(hcap, G - g0);
+                for (int i = tid; i < ng * nsplit * (D / 4); i += PD_CTHREADS) {
+                    const int gi = i / (nsplit * (D / 4)), r = i % (nsplit * (D / 4));
+                    cp_async16(po_s + (size_t)gi * nsplit * D + (size_t)r * 4,
+                               p.part_o + (hb0 + (int64_t)(g0 + gi) * PD_MAX_SPLITS) * D + (int64_t)r * 4, true);
+                }
+                cp_async_commit();
+            };
+            stage(0);
+            if (warp < G) {
+                // merge weights exp(m_s - max) and the denominator; each lane's (m, l) pairs are read
+                // at once, then summed in the order s = lane, lane + 32, ...
+                const int g = warp;
+                const float* ml = p.part_ml + (hb0 + (int64_t)g * PD_MAX_SPLITS) * 2;
+                float mv[PD_MAX_SPLITS / 32], lv[PD_MAX_SPLITS / 32];
+    #pragma unroll
+                for (int i = 0; i < PD_MAX_SPLITS / 32; i++) {
+                    const int s2 = lane + 32 * i;
+                    mv[i] = s2 < nsplit ? __ldcg(ml + 2 * s2) : -INFINITY;
+                    lv[i] = s2 < nsplit ? __ldcg(ml + 2 * s2 + 1) : 0.0f;
+                }
+                float mx = -INFINITY;
+    #pragma unroll
+                for (int i = 0; i < PD_MAX_SPLITS / 32; i++) mx = fmaxf(mx, mv[i]);
+                mx = warp_max(mx);
+                float lsum = 0.0f;
+    #pragma unroll
+                for (int i = 0; i < PD_MAX_SPLITS / 32; i++) {
+                    const int s2 = lane + 32 * i;
+                    if (s2 < nsplit) {
+                        const float w = expf(__fsub_rn(mv[i], mx));
+                        A.cm[g][s2] = w;
+                        lsum = __fadd_rn(lsum, __fmul_rn(w, lv[i]));
+                    }
+                }
+                lsum = warp_sum(lsum);
+                if (lane == 0) A.cl[g] = lsum;
+            }
+            for (int g0 = 0; g0 < G; g0 += hcap) {
+                const int ng = min(hcap, G - g0);
+                if (g0 > 0) stage(g0);
+                cp_async_wait<0>();
+                pd_csync();
+                const int d = tid & (D - 1);
+                for (int g = g0 + (tid >> 7); g < g0 + ng; g += 2) {
+                    const float* po = po_s + (size_t)(g - g0) * nsplit * D + d;
+                    float o = 0.0f;
+                    for (int s = 0; s < nsplit; s++) o = __fadd_rn(o, __fmul_rn(A.cm[g][s], po[(size_t)s * D]));
+                    o = __fdiv_rn(o, A.cl[g]);
+                    const int64_t e = (int64_t)b * Hq * D + (int64_t)(kvh * G + g) * D + d;
+                    pd_quant_warp32(o, lane, p.att_q + (e - lane), p.att_d + (e >> 5));
+                }
+                pd_csync();  // the staging area is refilled next
+            }
+            if (tid == 0) *counter = 0u;  // ready for the next layer
+        }
+        if (tid == 0) S.item = next;
+        pd_csync();
+        item = S.item;
+    }
+}
+
+// ---- the kernel ----
+template <int M>
+__global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    PdSmem& S = *reinterpret_cast<PdSmem*>(smem_raw);
+    uint8_t* area = smem_raw + sizeof(PdSmem);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int p0 = *p.pos_dev;
+    if (p0 < 0 || p0 >= p.ctx_max) {  // every CTA leaves before any copy or barrier
+        if (tid == 0) atomicCAS(p.err, 0, 44);
+        return;
+    }
+    if (tid == 0) {
+        for (int s = 0; s < PD_STAGES; s++) {
+            mbar_init(&S.full[s], 1);
+            mbar_init(&S.empty[s], PD_CONS);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&S.hfull[b], PD_CONS);
+            mbar_init(&S.hfree[b], 1);
+        }
+        mbar_fence_init();
+    }
+    if (tid < 4) S.keys[tid] = 0ull;
+    if (tid == 0) S.fail = 0;
+    __syncthreads();
+    if (warp == PD_CONS) {
+        // producer: every matrix of the step, in order, never waiting for activations
+        if (lane == 0) {
+            int it = 0;
+            unsigned off = 0;
+            bool ok = true;
+            for (int l = 0; l < p.n_layers && ok; l++)
+                for (int k = PH_QKV; k <= PH_DN && ok; k++) {
+                    const PdGemv g = pd_gemv(p, l, k);
+                    ok = pd_produce(S, g, off, it, p.err);
+                    off += (unsigned)pd_units(g);
+                }
+            if (ok) pd_produce(S, pd_gemv(p, 0, PH_LM), off, it, p.err);
+            // leave only after the copies in flight have landed (bounded)
+            for (int j = max(0, it - PD_STAGES); j < it; j++)
+                mbar_wait_ns(&S.full[j % PD_STAGES], (unsigned)(j / PD_STAGES) & 1u, PD_WAIT_NS);
+        }
+        return;
+    }
+    const int nsplit = p0 / PD_ATT_C + 1;
+    const int H = p.H, I = p.I;
+    const int Kmax = max(max(H, p.Hq * 128), I);
+    // union area, GEMV phases: activations xs [M][K] int8 and xds [M][K/32] fp16, the norm
+    // weight nws [H] bf16 (prefetched before the barrier that precedes its prologue) and the
+    // f32 staging row xrow [H]
+    int8_t* xs = reinterpret_cast<int8_t*>(area);
+    uint16_t* xds = reinterpret_cast<uint16_t*>(area + (size_t)M * Kmax);
+    uint16_t* nws = reinterpret_cast<uint16_t*>(area + (size_t)M * Kmax + (size_t)M * (Kmax / 32) * 2);
+    float* xrow = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(nws) + (size_t)H * 2);
+    PdAtt& A = *reinterpret_cast<PdAtt*>(area);
+    // RMSNorm + Q8_0 of the M rows of x (written by other CTAs) into xs/xds; the norm weight's
+    // copies are already in flight
+    auto norm_rows = [&]() {
+        for (int m = 0; m < M; m++) {
+            pd_csync();
+            pd_stage_f32(xrow, p.x + (size_t)m * H, H, tid);
+            pd_csync();
+            rms_row<float, PD_CTHREADS, 1>(xrow, H, nws, p.eps, tid, S.red, nullptr, xs + (size_t)m * H,
+                                           xds + (size_t)m * (H / 32));
+        }
+        pd_csync();
+    };
+    int it = 0, hn = 0;
+    unsigned epoch = 0;
+    pd_prefetch(nws, p.layers[0].in_norm, H * 2, tid);
+    for (int l = 0; l < p.n_layers; l++) {
+        const PdLayer& L = p.layers[l];
+        // QKV: input RMSNorm + Q8_0 of x, the q|k|v rows
+        norm_rows();
+        if (!pd_consume<M>(S, pd_gemv(p, l, PH_QKV), xs, xds, it, hn, p.qkv, p.Nqkv, false, false, nullptr,
+                           nullptr, p.err))
+            return;
+        if (!pd_grid_barrier(p, S, epoch)) return;
+        // attention -> Q8_0 rows
+        pd_attention<M>(p, L, S, A, p0, nsplit, pd_att_ctr(p, M, l));
+        if (!pd_grid_barrier(p, S, epoch)) return;
+        // O: the attention output as activations, residual into x
+        {
+            const int Ko = p.Hq * 128;
+            pd_prefetch(xs, p.att_q, M * Ko, tid);
+            pd_prefetch(xds, p.att_d, M * (Ko / 32) * 2, tid);
+            cp_async_wait<0>();
+            pd_csync();
+            if (!pd_consume<M>(S, pd_gemv(p, l, PH_O), xs, xds, it, hn, p.x, H, true, false, nullptr, nullptr,
+                               p.err))
+                return;
+        }
+        pd_prefetch(nws, L.post_norm, H * 2, tid);
+        if (!pd_grid_barrier(p, S, epoch)) return;
+        // GU: post-attention RMSNorm, gate|up, SiLU(gate)*up -> h as Q8_0
+        norm_rows();
+        if (!pd_consume<M>(S, pd_gemv(p, l, PH_GU), xs, xds, it, hn, nullptr, 0, false, false, p.hq, p.hd, p.err))
+            return;
+        if (!pd_grid_barrier(p, S, epoch)) return;
+        // DN: h (already Q8_0) as activations, residual into x
+        pd_prefetch(xs, p.hq, M * I, tid);
+        pd_prefetch(xds, p.hd, M * (I / 32) * 2, tid);
+        cp_async_wait<0>();
+        pd_csync();
+        if (!pd_consume<M>(S, pd_gemv(p, l, PH_DN), xs, xds, it, hn, p.x, H, true, false, nullptr, nullptr, p.err))
+            return;
+        pd_prefetch(nws, l + 1 < p.n_layers ? p.layers[l + 1].in_norm : p.final_norm, H * 2, tid);
+        if (!pd_grid_barrier(p, S, epoch)) return;
+    }
+    // LM head: final RMSNorm, logits, greedy argmax keys
+    norm_rows();
+    if (!pd_consume<M>(S, pd_gemv(p, 0, PH_LM), xs, xds, it, hn, p.logits, p.V, false, true, nullptr, nullptr,
+                       p.err))
+        return;
+    pd_csync();
+    if (tid < M && S.keys[tid]) atomicMax(p.keys + tid, S.keys[tid]);
+}
+
+// ---- host ----
+static size_t pd_area_bytes(int64_t m, int64_t H, int64_t Hqd, int64_t I) {
+    const int64_t Kmax = std::max({H, Hqd, I});
+    const size_t gemv = (size_t)(m * Kmax + m * (Kmax / 32) * 2 + H * 2 + H * 4);
+    return std::max(gemv, sizeof(PdAtt));
+}
+
+static size_t pd_smem(int64_t m, int64_t H, int64_t Hqd, int64_t I) {
+    return sizeof(PdSmem) + pd_area_bytes(m, H, Hqd, I);
+}
+
+bool decode_persist_supported(lq_ctx* ctx, int64_t m, int64_t H, int64_t Hq, int64_t Hkv, int64_t I,
+                              int64_t ctx_max) {
+    if (m < 1 || m > 4 || getenv("LQ_NO_PERSIST")) return false;
+    if (H % 256 || I % 256 || Hq % Hkv || Hq / Hkv > PD_MAX_G) return false;
+    if (ctx_max > (int64_t)PD_ATT_C * PD_MAX_SPLITS) return false;
+    int coop = 0;
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, ctx->device);
+    return coop && pd_smem(m, H, Hq * 128, I) <= 227 * 1024;
+}
+
+size_t decode_persist_desc_bytes(int64_t n_layers) { return (size_t)(n_layers + 1) * sizeof(PdLayer); }
+size_t decode_persist_part_bytes(int64_t m, int64_t Hq) { return (size_t)(m * Hq * PD_MAX_SPLITS) * (128 + 2) * 4; }
+size_t decode_persist_counter_bytes(int64_t m, int64_t Hkv, int64_t n_layers) {
+    return (size_t)(1 + m * Hkv + n_layers) * 4;
+}
+
+static int pd_map(lq_ctx* ctx, PdMat* out, const lq_q8_tensor& w) {
+    const int64_t N = w.n, K = w.k, nb = K / 32;
+    const uint32_t kc = (uint32_t)std::min<int64_t>(K, PD_KC);
+    int rc = make_tensor_map_2d(ctx, &out->wq, CU_TENSOR_MAP_DATA_TYPE_UINT64, w.qs, (uint64_t)(K / 8), (uint64_t)N,
+                                (uint64_t)K, kc / 8, PD_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    return make_tensor_map_2d(ctx, &out->wd, CU_TENSOR_MAP_DATA_TYPE_UINT16, w.d, (uint64_t)nb, (uint64_t)N,
+                              (uint64_t)(nb * 2), kc / 32, PD_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+int decode_persist_write_desc(lq_ctx* ctx, void* dev, const PdHostLayer* layers, int64_t n_layers,
+                              const lq_q8_tensor* lm_head) {
+    std::vector<PdLayer> h((size_t)n_layers + 1);
+    memset(static_cast<void*>(h.data()), 0, h.size() * sizeof(PdLayer));
+    for (int64_t l = 0; l < n_layers; l++) {
+        const PdHostLayer& s = layers[l];
+        const lq_q8_tensor* mats[4] = {s.qkv, s.o, s.gate_up, s.down};
+        for (int k = 0; k < 4; k++) {
+            for (const void* ptr : {(const void*)mats[k]->qs, (const void*)mats[k]->d})
+                if ((uintptr_t)ptr % 16) return set_error(ctx, LQ_ERR_UNSUPPORTED, "decode_step: unaligned weights");
+            int rc = pd_map(ctx, &h[l].mat[k], *mats[k]);
+            if (rc) return rc;
+        }
+        h[l].in_norm = s.in_norm;
+        h[l].post_norm = s.post_norm;
+        h[l].q_norm = s.q_norm;
+        h[l].k_norm = s.k_norm;
+        h[l].kc = s.kc;
+        h[l].vc = s.vc;
+    }
+    int rc = pd_map(ctx, &h[n_layers].mat[0], *lm_head);
+    if (rc) return rc;
+    LQ_CUDA(ctx, cudaMemcpy(dev, h.data(), h.size() * sizeof(PdLayer), cudaMemcpyHostToDevice));
+    return LQ_OK;
+}
+
+template <int M>
+static int launch_pd(lq_ctx* ctx, const PdParams& p, size_t smem) {
+    auto kern = decode_step_kernel<M>;
+    static bool attr[64] = {};
+    if (ctx->device < 0 || ctx->device >= 64 || !attr[ctx->device]) {
+        LQ_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        if (ctx->device >= 0 && ctx->device < 64) attr[ctx->device] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ctx->sm_count);
+    cfg.blockDim = dim3(PD_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeCooperative;  // all CTAs resident at once: the grid barriers rely on it
+    at[0].val.cooperative = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+    if (e != cudaSuccess) return check_cuda(ctx, e, "decode_step (cooperative launch)");
+    return LQ_OK;
+}
+
+int launch_decode_persist(lq_ctx* ctx, const PdLaunch& a) {
+    if (a.m < 1 || a.m > 4) return set_error(ctx, LQ_ERR_INVALID_ARG, "decode_step: batch %lld > 4", (long long)a.m);
+    PdParams p = {};
+    p.layers = reinterpret_cast<const PdLayer*>(a.desc);
+    p.n_layers = (int)a.n_layers;
+    p.final_norm = a.final_norm;
+    p.H = (int)a.H;
+    p.Hq = (int)a.Hq;
+    p.Hkv = (int)a.Hkv;
+    p.I = (int)a.I;
+    p.V = (int)a.V;
+    p.Nqkv = (int)((a.Hq + 2 * a.Hkv) * 128);
+    p.ctx_max = (int)a.ctx_max;
+    p.eps = a.eps;
+    p.cos_t = a.cos_t;
+    p.sin_t = a.sin_t;
+    p.pos_dev = a.pos_dev;
+    p.x = a.x;
+    p.qkv = a.qkv;
+    p.att_q = a.att_q;
+    p.att_d = a.att_d;
+    p.hq = a.hq;
+    p.hd = a.hd;
+    p.part_o = a.part;
+    p.part_ml = a.part + (size_t)(a.m * a.Hq * PD_MAX_SPLITS) * 128;
+    p.logits = a.logits;
+    p.keys = a.keys;
+    p.bar = a.counters;
+    p.err = ctx->err_flag;
+    LQ_CUDA(ctx, cudaMemsetAsync(a.counters, 0, decode_persist_counter_bytes(a.m, a.Hkv, a.n_layers), ctx->stream));
+    const size_t smem = pd_smem(a.m, a.H, a.Hq * 128, a.I);
+    switch (a.m) {
+        case 1: return launch_pd<1>(ctx, p, smem);
+        case 2: return launch_pd<2>(ctx, p, smem);
+        case 3: return launch_pd<3>(ctx, p, smem);
+        default: return launch_pd<4>(ctx, p, smem);
+    }
+}
+
+}  // namespace lq

@@ -76,8 +76,12 @@ __device__ __forceinline__ void dot_block(const int4 w0, const int4 w1, float dw
                                           const uint16_t* xds, int K, int nb, int gb, float acc[M]) {
 #pragma unroll
     for (int m = 0; m < M; m++) {
+        // lanes 4-7 of each quarter-warp take the block's second half first: the 16-byte
+        // reads of a quarter-warp then cover all 32 banks once (blocks are 32 bytes apart)
+        const int sw = (threadIdx.x >> 2) & 1;
         const int4* xp = reinterpret_cast<const int4*>(xs + (size_t)m * K + (size_t)gb * 32);
-        const int4 x0 = xp[0], x1 = xp[1];
+        const int4 xa = xp[sw], xb = xp[sw ^ 1];
+        const int4 x0 = sw ? xb : xa, x1 = sw ? xa : xb;
         int sum = 0;
         sum = __dp4a(w0.x, x0.x, sum); sum = __dp4a(w0.y, x0.y, sum);
         sum = __dp4a(w0.z, x0.z, sum); sum = __dp4a(w0.w, x0.w, sum);
@@ -183,6 +187,10 @@ __global__ void __launch_bounds__(GV_THREADS) q8_gemv_stream_kernel(const GvPara
     for (int half = 0; half < HALVES && ok; half++) {
         const int r0 = rg * GV_ROWS;  // output row base
         const int rows = min(GV_ROWS, nout - r0);
+        // the residual this lane adds (lane m: token m), read now so that its round trip
+        // overlaps the row's chunks
+        float res = 0.0f;
+        if (!SWI && p.resid && lane < M && warp < rows) res = p.resid[(size_t)lane * p.ldy + r0 + warp];
         for (int c = 0; c < nchunks; c++, it++) {
             const int s = it % STAGES;
             const unsigned ph = (unsigned)(it / STAGES) & 1u;
@@ -205,8 +213,11 @@ __global__ void __launch_bounds__(GV_THREADS) q8_gemv_stream_kernel(const GvPara
                 for (int j = 0; j < 2; j++) {
                     const int b = lane + 32 * j;
                     if (mine && b < nbc) {
-                        w[j][0] = *reinterpret_cast<const int4*>(wrow + b * 32);
-                        w[j][1] = *reinterpret_cast<const int4*>(wrow + b * 32 + 16);
+                        const int sw = (lane >> 2) & 1;  // conflict-free order, as in dot_block
+                        const int4 wa = *reinterpret_cast<const int4*>(wrow + b * 32 + sw * 16);
+                        const int4 wb = *reinterpret_cast<const int4*>(wrow + b * 32 + (sw ^ 1) * 16);
+                        w[j][0] = sw ? wb : wa;
+                        w[j][1] = sw ? wa : wb;
                         dw[j] = h2f(drow[b]);
                     }
                 }
@@ -238,7 +249,7 @@ __global__ void __launch_bounds__(GV_THREADS) q8_gemv_stream_kernel(const GvPara
                         if (lane == m) {
                             const size_t o = (size_t)m * p.ldy + row;
                             if (SWI) p.y[o] = swiglu(gate[m], v);
-                            else p.y[o] = p.resid ? __fadd_rn(p.resid[o], v) : v;
+                            else p.y[o] = p.resid ? __fadd_rn(res, v) : v;
                         }
                         if (!SWI && p.keys && lane == 0) atomicMax(&S.keys[m], argmax_key(v, row));
                     }

@@ -266,4 +266,37 @@ int launch_silu_mul(lq_ctx* ctx, const float* gu, int64_t m, int64_t inter, floa
                     uint16_t* xd);
 int launch_embedding(lq_ctx* ctx, const uint16_t* table, int64_t vocab, int64_t hidden,
                      const int32_t* ids, int64_t n, float* out);
+
+// the whole dense decode step as one persistent kernel (lq8_decode.cu)
+struct PdHostLayer {
+    const lq_q8_tensor *qkv, *o, *gate_up, *down;
+    const uint16_t *in_norm, *post_norm, *q_norm, *k_norm;
+    float *kc, *vc;
+};
+struct PdLaunch {
+    const void* desc;  // decode_persist_desc_bytes, written by decode_persist_write_desc
+    int64_t n_layers, m, H, Hq, Hkv, I, V, ctx_max;
+    float eps;
+    const uint16_t* final_norm;
+    const float *cos_t, *sin_t;
+    const int32_t* pos_dev;
+    float* x;          // [m][H] residual stream (embedded input rows)
+    float* qkv;        // [m][(Hq+2Hkv)*128]
+    int8_t* att_q;     // [m][Hq*128]
+    uint16_t* att_d;   // [m][Hq*4]
+    int8_t* hq;        // [m][I] Q8_0 of SiLU(gate)*up (may share att_q's buffer)
+    uint16_t* hd;      // [m][I/32]
+    float* part;       // decode_persist_part_bytes
+    float* logits;     // [m][V]
+    unsigned long long* keys;
+    unsigned* counters;  // decode_persist_counter_bytes, zeroed by the launch
+};
+bool decode_persist_supported(lq_ctx* ctx, int64_t m, int64_t H, int64_t Hq, int64_t Hkv, int64_t I,
+                              int64_t ctx_max);
+size_t decode_persist_desc_bytes(int64_t n_layers);
+size_t decode_persist_part_bytes(int64_t m, int64_t Hq);
+size_t decode_persist_counter_bytes(int64_t m, int64_t Hkv, int64_t n_layers);
+int decode_persist_write_desc(lq_ctx* ctx, void* dev, const PdHostLayer* layers, int64_t n_layers,
+                              const lq_q8_tensor* lm_head);
+int launch_decode_persist(lq_ctx* ctx, const PdLaunch& a);
 }  // namespace lq

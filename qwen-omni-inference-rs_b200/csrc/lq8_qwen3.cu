@@ -76,6 +76,12 @@ struct lq_model {
     int64_t graph_batch = 0;
     int64_t graph_kernels = 0;   // kernel nodes in the decode graph
     bool fused_decode = false;   // the decode GEMVs can take every K of this model
+    // the whole decode step as one persistent kernel (dense, one GPU, batch <= persist_batch)
+    bool persist = false;
+    int64_t persist_batch = 0;
+    void* pd_desc = nullptr;         // per-layer tensor maps and pointers
+    float* pd_part = nullptr;        // attention chunk partials
+    unsigned* pd_counters = nullptr; // grid barrier + chunk counters
     std::vector<void*> allocs;
 };
 
@@ -198,6 +204,37 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
 #define RC(expr) do { rc = (expr); if (rc) return rc; } while (0)
     RC(lq::launch_embedding(ctx, m->embed, c.vocab, H, m->tokens, rows, m->x));
     const size_t kv_layer = (size_t)(m->max_batch * Hkv * m->ctx_max * D);
+    if (L == 1 && pos_dev && m->persist && B <= m->persist_batch) {
+        // decode, one persistent kernel for every layer and the LM head
+        lq::PdLaunch a = {};
+        a.desc = m->pd_desc;
+        a.n_layers = c.layers;
+        a.m = B;
+        a.H = H;
+        a.Hq = Hq;
+        a.Hkv = Hkv;
+        a.I = I;
+        a.V = m->V_l;
+        a.ctx_max = m->ctx_max;
+        a.eps = c.eps;
+        a.final_norm = m->final_norm;
+        a.cos_t = m->cos_t;
+        a.sin_t = m->sin_t;
+        a.pos_dev = pos_dev;
+        a.x = m->x;
+        a.qkv = m->qkv;
+        a.att_q = m->xq;
+        a.att_d = m->xd;
+        a.hq = m->xq;  // the attention output is consumed (o) before h is written (gate|up)
+        a.hd = m->xd;
+        a.part = m->pd_part;
+        a.logits = m->logits;
+        a.keys = m->keys;
+        a.counters = m->pd_counters;
+        RC(lq::launch_decode_persist(ctx, a));
+        RC(lq::launch_argmax_finalize(ctx, m->keys, B, m->tokens, bump_pos ? m->pos_dev : nullptr));
+        return LQ_OK;
+    }
     if (L == 1 && pos_dev && m->fused_decode && B <= 4) {
         // decode, five kernels per layer: [norm -> q|k|v] [q/k norm, RoPE, KV append,
         // attention -> Q8_0] [o + residual] [norm -> gate|up -> SiLU*up] [down + residual]
@@ -495,6 +532,31 @@ static int create_model(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, 
             ok = ok && lq::gemv_stream_supported(k) && lq::gemv_stream_smem(4, k) <= 227 * 1024;
         m->fused_decode = ok;
     }
+    {
+        // the persistent decode step (dense models on one GPU); LQ_NO_PERSIST=1 keeps the
+        // per-layer kernels
+        const int64_t pb = std::min<int64_t>(max_batch, 4);
+        if (!moe && T == 1 && m->fused_decode && lq::decode_persist_supported(ctx, pb, H, Hq, Hkv, I, ctx_max)) {
+            std::vector<lq::PdHostLayer> hl(m->layers.size());
+            const size_t kv_layer = (size_t)(max_batch * Hkv * ctx_max * D);
+            for (size_t l = 0; l < m->layers.size(); l++) {
+                const Layer& ly = m->layers[l];
+                hl[l] = {&ly.qkv, &ly.o, &ly.gate_up, &ly.down, ly.in_norm, ly.post_norm, ly.q_norm, ly.k_norm,
+                         m->kc + l * kv_layer, m->vc + l * kv_layer};
+            }
+            int prc = dalloc(m, &m->pd_desc, lq::decode_persist_desc_bytes(c.layers));
+            if (!prc) prc = dalloc(m, reinterpret_cast<void**>(&m->pd_part), lq::decode_persist_part_bytes(pb, Hq));
+            if (!prc)
+                prc = dalloc(m, reinterpret_cast<void**>(&m->pd_counters), lq::decode_persist_counter_bytes(pb, Hkv, c.layers));
+            if (!prc) prc = lq::decode_persist_write_desc(ctx, m->pd_desc, hl.data(), c.layers, &m->lm_head);
+            if (prc) {
+                lq_qwen3_destroy(m);
+                return prc;
+            }
+            m->persist = true;
+            m->persist_batch = pb;
+        }
+    }
     *out = m;
     return LQ_OK;
 }
@@ -603,7 +665,9 @@ int lq_qwen3_decode_step(lq_model* m, const int32_t* ids, int32_t* next, float* 
         rc = logits_to_host(m, B, logits);
         if (rc) return rc;
     }
-    LQ_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    // synchronises; a kernel that gave up waiting (a stalled copy or grid barrier) reports here
+    rc = lq::consume_device_error(ctx, "lq_qwen3_decode_step");
+    if (rc) return rc;
     m->pos += 1;
     return LQ_OK;
 }
