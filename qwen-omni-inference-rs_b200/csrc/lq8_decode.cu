@@ -14,8 +14,9 @@
 // wherever a phase reads what other CTAs wrote:
 //   QKV  RMSNorm + Q8_0 of x (every CTA, redundantly), q|k|v rows                      | barrier
 //   ATT  items (row, kv head, 64-position chunk): q/k RMSNorm + RoPE, the new position's
-//        k/v appended to the caches, scores, chunk softmax, P.V; the last item of a
-//        (row, kv head) merges the chunks and writes the Q8_0 attention output         | barrier
+//        k/v appended to the caches, scores, chunk softmax, P.V -> published partials;
+//        then merge tasks (row, q head), taken by CTAs out of items, each waiting for its
+//        kv head's chunks: merge, Q8_0 of the head's output                            | barrier
 //   O    o rows + residual -> x                                                       | barrier
 //   GU   RMSNorm prologue, gate|up rows, SiLU(gate)*up -> h, quantized per unit      | barrier
 //   DN   h (Q8_0) as activations, down rows + residual -> x                           | barrier
@@ -83,8 +84,8 @@ struct PdParams {
     float* part_ml;            // [M][Hq][PD_MAX_SPLITS][2]
     float* logits;             // [M][V]
     unsigned long long* keys;  // [M]
-    unsigned* bar;             // [0] grid barrier, [1 + b*Hkv + kvh] chunk counters, then the
-                               // attention item counters (one per layer); zero at launch
+    unsigned* bar;             // [0] grid barrier, [1 + b*Hkv + kvh] published-chunk counters,
+                               // then per layer the chunk-item and merge-task counters; zero at launch
     int* err;
 };
 
@@ -99,7 +100,6 @@ struct PdAtt {
     float ml[PD_MAX_G][2];
     float cm[PD_MAX_G][PD_MAX_SPLITS];
     float cl[PD_MAX_G];
-    int last;
 };
 
 // 128-byte multiple: the union area behind it takes 16-byte vector and cp.async accesses
@@ -156,9 +156,9 @@ __device__ __forceinline__ int pd_units(const PdGemv& g) {
     const int nout = g.swi ? g.N / 2 : g.N;
     return (nout + pd_unit_rows(g) - 1) / pd_unit_rows(g);
 }
-// attention item counter of layer l
-__device__ __forceinline__ unsigned* pd_att_ctr(const PdParams& p, int M, int l) {
-    return p.bar + 1 + M * p.Hkv + l;
+// attention chunk-item (k = 0) and merge-task (k = 1) counters of layer l
+__device__ __forceinline__ unsigned* pd_att_ctr(const PdParams& p, int M, int l, int k) {
+    return p.bar + 1 + M * p.Hkv + 2 * l + k;
 }
 
 __device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
@@ -451,9 +451,11 @@ __device__ __forceinline__ bool pd_consume(PdSmem& S, const PdGemv& g, const int
 
 // ---- attention (the decode attention kernel's arithmetic, on 256 threads) ----
 
+// ctr / mctr: this layer's chunk-item and merge-task counters; target: the chunk counters'
+// value once this layer's chunks are all published ((layer + 1) * nsplit)
 template <int M>
 __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdAtt& A, int p0, int nsplit,
-                             unsigned* ctr) {
+                             unsigned* ctr, unsigned* mctr, unsigned target) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int Hq = p.Hq, Hkv = p.Hkv, G = Hq / Hkv, D = 128;
     const int heads = Hq + 2 * Hkv;
@@ -513,13 +515,14 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
         }
         cp_async_wait<0>();
         pd_csync();
-        // scores: thread -> position pp and heads q4, q4 + 4; sequential 128-term dots, then the
-        // scale. K and q are read 32 dims at a time into registers ahead of the add chain.
+        // scores: thread -> position pp and heads q4, q4 + 4 (a warp shares one head, so its q
+        // reads are broadcasts); sequential 128-term dots, then the scale. K and q are read 32
+        // dims at a time into registers ahead of the add chain.
         {
             const int pp = tid % PD_ATT_C, q4 = tid / PD_ATT_C;
             float s[2] = {0.f, 0.f};
             if (pp < cnt) {
-#pragma unroll 1
+#pragma unroll
                 for (int d0 = 0; d0 < D; d0 += 32) {
                     float4 kk[8];
 #pragma unroll
@@ -543,9 +546,9 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
                 }
             }
 #pragma unroll
-            for (int i = 0; i < 2; i++) {
-                const int g = q4 + 4 * i;
-                if (g < G) A.ps[g][pp] = pp < cnt ? __fmul_rn(s[i], scale) : -INFINITY;
+            for (int h = 0; h < 2; h++) {
+                const int g = q4 + 4 * h;
+                if (g < G) A.ps[g][pp] = pp < cnt ? __fmul_rn(s[h], scale) : -INFINITY;
             }
         }
         pd_csync();
@@ -603,79 +606,90 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
             }
         }
         // the last chunk of this (row, kv head) to finish merges the chunks
-        unsigned* counter = p.bar + 1 + b * Hkv + kvh;
+        // publish the chunk: the (row, kv head)'s counter grows by nsplit per layer
         __threadfence();
         pd_csync();
-        if (tid == 0) A.last = atomicAdd(counter, 1u) == (unsigned)(nsplit - 1);
+        if (tid == 0) atomicAdd(p.bar + 1 + b * Hkv + kvh, 1u);
+        if (tid == 0) S.item = next;
         pd_csync();
-        if (A.last) {
-            __threadfence();
-            // the heads' chunk partials into the free staging area (K, V, q rows), as many heads at
-            // a time as fit, every 16-byte copy in flight at once; the first batch lands while the
-            // merge weights are computed
-            float* po_s = &A.ks[0][0];
-            const int hcap = (int)((sizeof(A.ks) + sizeof(A.vs) + sizeof(A.qraw) + sizeof(A.qs)) / 4 /
-                                   ((size_t)nsplit * D));
-            auto stage = [&](int g0) {
-                const int ng = min(hcap, G - g0);
-                for (int i = tid; i < ng * nsplit * (D / 4); i += PD_CTHREADS) {
-                    const int gi = i / (nsplit * (D / 4)), r = i % (nsplit * (D / 4));
-                    cp_async16(po_s + (size_t)gi * nsplit * D + (size_t)r * 4,
-                               p.part_o + (hb0 + (int64_t)(g0 + gi) * PD_MAX_SPLITS) * D + (int64_t)r * 4, true);
+        item = S.item;
+    }
+    // merge tasks (row, q head), claimed by CTAs that ran out of chunk items: wait until the
+    // kv head's chunks of this layer are all published, then merge them (rescale by
+    // exp(m_s - max), sum in chunk order, divide) and write the head's Q8_0 output
+    const int n_tasks = M * Hq;
+    if (tid == 0) S.item = (int)atomicAdd(mctr, 1u);
+    pd_csync();
+    int task = S.item;
+    while (task < n_tasks) {
+        int next = 0;
+        if (tid == 0) next = (int)atomicAdd(mctr, 1u);
+        const int b = task / Hq, head = task % Hq, kvh = head / G;
+        const int64_t hb = ((int64_t)b * Hq + head) * PD_MAX_SPLITS;
+        if (tid == 0) {
+            const unsigned* cnt = p.bar + 1 + b * Hkv + kvh;
+            const uint64_t t0 = global_ns();
+            int ok = 1;
+            for (int i = 1;; i++) {
+                unsigned v;
+                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(cnt) : "memory");
+                if (v >= target) break;
+                if ((i & 63) == 0) {
+                    if (ld_volatile(p.err) != 0) { ok = 0; break; }
+                    if (global_ns() - t0 > PD_WAIT_NS) { atomicCAS(p.err, 0, 47); ok = 0; break; }
                 }
-                cp_async_commit();
-            };
-            stage(0);
-            if (warp < G) {
-                // merge weights exp(m_s - max) and the denominator; each lane's (m, l) pairs are read
-                // at once, then summed in the order s = lane, lane + 32, ...
-                const int g = warp;
-                const float* ml = p.part_ml + (hb0 + (int64_t)g * PD_MAX_SPLITS) * 2;
+            }
+            S.flag = ok;
+        }
+        pd_csync();
+        if (S.flag) {
+            // the head's chunk partials into the staging area, all copies in flight, landing
+            // while warp 0 computes the merge weights
+            float* po_s = &A.ks[0][0];
+            for (int i = tid; i < nsplit * (D / 4); i += PD_CTHREADS)
+                cp_async16(po_s + (size_t)i * 4, p.part_o + hb * D + (int64_t)i * 4, true);
+            cp_async_commit();
+            if (warp == 0) {
+                // each lane's (m, l) pairs read at once, summed in the order s = lane, lane + 32, ...
+                const float* ml = p.part_ml + hb * 2;
                 float mv[PD_MAX_SPLITS / 32], lv[PD_MAX_SPLITS / 32];
-    #pragma unroll
+#pragma unroll
                 for (int i = 0; i < PD_MAX_SPLITS / 32; i++) {
                     const int s2 = lane + 32 * i;
                     mv[i] = s2 < nsplit ? __ldcg(ml + 2 * s2) : -INFINITY;
                     lv[i] = s2 < nsplit ? __ldcg(ml + 2 * s2 + 1) : 0.0f;
                 }
                 float mx = -INFINITY;
-    #pragma unroll
+#pragma unroll
                 for (int i = 0; i < PD_MAX_SPLITS / 32; i++) mx = fmaxf(mx, mv[i]);
                 mx = warp_max(mx);
                 float lsum = 0.0f;
-    #pragma unroll
+#pragma unroll
                 for (int i = 0; i < PD_MAX_SPLITS / 32; i++) {
                     const int s2 = lane + 32 * i;
                     if (s2 < nsplit) {
                         const float w = expf(__fsub_rn(mv[i], mx));
-                        A.cm[g][s2] = w;
+                        A.cm[0][s2] = w;
                         lsum = __fadd_rn(lsum, __fmul_rn(w, lv[i]));
                     }
                 }
                 lsum = warp_sum(lsum);
-                if (lane == 0) A.cl[g] = lsum;
+                if (lane == 0) A.cl[0] = lsum;
             }
-            for (int g0 = 0; g0 < G; g0 += hcap) {
-                const int ng = min(hcap, G - g0);
-                if (g0 > 0) stage(g0);
-                cp_async_wait<0>();
-                pd_csync();
-                const int d = tid & (D - 1);
-                for (int g = g0 + (tid >> 7); g < g0 + ng; g += 2) {
-                    const float* po = po_s + (size_t)(g - g0) * nsplit * D + d;
-                    float o = 0.0f;
-                    for (int s = 0; s < nsplit; s++) o = __fadd_rn(o, __fmul_rn(A.cm[g][s], po[(size_t)s * D]));
-                    o = __fdiv_rn(o, A.cl[g]);
-                    const int64_t e = (int64_t)b * Hq * D + (int64_t)(kvh * G + g) * D + d;
-                    pd_quant_warp32(o, lane, p.att_q + (e - lane), p.att_d + (e >> 5));
-                }
-                pd_csync();  // the staging area is refilled next
+            cp_async_wait<0>();
+            pd_csync();
+            if (tid < D) {
+                const int d = tid;
+                float o = 0.0f;
+                for (int s2 = 0; s2 < nsplit; s2++) o = __fadd_rn(o, __fmul_rn(A.cm[0][s2], po_s[(size_t)s2 * D + d]));
+                o = __fdiv_rn(o, A.cl[0]);
+                const int64_t e = (int64_t)b * Hq * D + (int64_t)head * D + d;
+                pd_quant_warp32(o, lane, p.att_q + (e - lane), p.att_d + (e >> 5));
             }
-            if (tid == 0) *counter = 0u;  // ready for the next layer
         }
         if (tid == 0) S.item = next;
         pd_csync();
-        item = S.item;
+        task = S.item;
     }
 }
 
@@ -759,7 +773,8 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
             return;
         if (!pd_grid_barrier(p, S, epoch)) return;
         // attention -> Q8_0 rows
-        pd_attention<M>(p, L, S, A, p0, nsplit, pd_att_ctr(p, M, l));
+        pd_attention<M>(p, L, S, A, p0, nsplit, pd_att_ctr(p, M, l, 0), pd_att_ctr(p, M, l, 1),
+                        (unsigned)((l + 1) * nsplit));
         if (!pd_grid_barrier(p, S, epoch)) return;
         // O: the attention output as activations, residual into x
         {
@@ -822,7 +837,7 @@ bool decode_persist_supported(lq_ctx* ctx, int64_t m, int64_t H, int64_t Hq, int
 size_t decode_persist_desc_bytes(int64_t n_layers) { return (size_t)(n_layers + 1) * sizeof(PdLayer); }
 size_t decode_persist_part_bytes(int64_t m, int64_t Hq) { return (size_t)(m * Hq * PD_MAX_SPLITS) * (128 + 2) * 4; }
 size_t decode_persist_counter_bytes(int64_t m, int64_t Hkv, int64_t n_layers) {
-    return (size_t)(1 + m * Hkv + n_layers) * 4;
+    return (size_t)(1 + m * Hkv + 2 * n_layers) * 4;
 }
 
 static int pd_map(lq_ctx* ctx, PdMat* out, const lq_q8_tensor& w) {
