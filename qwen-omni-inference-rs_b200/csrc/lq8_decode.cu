@@ -451,11 +451,46 @@ __device__ __forceinline__ bool pd_consume(PdSmem& S, const PdGemv& g, const int
 
 // ---- attention (the decode attention kernel's arithmetic, on 256 threads) ----
 
+// an attention item's K/V cache rows of earlier steps (those before the new position) into
+// the staging area, every copy in flight; they depend on nothing this step computes
+template <int M>
+__device__ __forceinline__ void pd_item_kv(const PdParams& p, const PdLayer& L, PdAtt& A, int p0, int nsplit,
+                                           int item) {
+    const int D = 128, Hkv = p.Hkv;
+    const int split = item % nsplit, kvh = (item / nsplit) % Hkv, b = item / (nsplit * Hkv);
+    const int j0 = split * PD_ATT_C;
+    const int cnt = min(PD_ATT_C, p0 + 1 - j0);
+    const int fresh = p0 - j0;
+    const float* kbase = L.kc + ((int64_t)b * Hkv + kvh) * (int64_t)p.ctx_max * D + (int64_t)j0 * D;
+    const float* vbase = L.vc + ((int64_t)b * Hkv + kvh) * (int64_t)p.ctx_max * D + (int64_t)j0 * D;
+    for (int i = threadIdx.x; i < cnt * (D / 4); i += PD_CTHREADS) {
+        const int r = i / (D / 4), c = (i % (D / 4)) * 4;
+        if (r < fresh) {
+            cp_async16(&A.ks[r][c], kbase + (int64_t)r * D + c, true);
+            cp_async16(&A.vs[r][c], vbase + (int64_t)r * D + c, true);
+        }
+    }
+    cp_async_commit();
+}
+
+// claims this CTA's first attention item of the layer and starts its cache-row copies (called
+// before the grid barrier that precedes attention, so the copies overlap it)
+template <int M>
+__device__ __forceinline__ int pd_attention_begin(const PdParams& p, const PdLayer& L, PdSmem& S, PdAtt& A, int p0,
+                                                  int nsplit, unsigned* ctr) {
+    if (threadIdx.x == 0) S.item = (int)atomicAdd(ctr, 1u);
+    pd_csync();
+    const int item = S.item;
+    if (item < M * p.Hkv * nsplit) pd_item_kv<M>(p, L, A, p0, nsplit, item);
+    return item;
+}
+
 // ctr / mctr: this layer's chunk-item and merge-task counters; target: the chunk counters'
-// value once this layer's chunks are all published ((layer + 1) * nsplit)
+// value once this layer's chunks are all published ((layer + 1) * nsplit); first: the item
+// claimed by pd_attention_begin (its cache-row copies already in flight)
 template <int M>
 __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdAtt& A, int p0, int nsplit,
-                             unsigned* ctr, unsigned* mctr, unsigned target) {
+                             unsigned* ctr, unsigned* mctr, unsigned target, int first) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int Hq = p.Hq, Hkv = p.Hkv, G = Hq / Hkv, D = 128;
     const int heads = Hq + 2 * Hkv;
@@ -464,9 +499,8 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
     const float* cs = p.cos_t + (int64_t)p0 * (D / 2);
     const float* sn = p.sin_t + (int64_t)p0 * (D / 2);
     // items are claimed from the phase counter; the next claim is issued while this item runs
-    if (tid == 0) S.item = (int)atomicAdd(ctr, 1u);
-    pd_csync();
-    int item = S.item;
+    int item = first;
+    bool kv_issued = true;
     while (item < n_items) {
         int next = 0;
         if (tid == 0) next = (int)atomicAdd(ctr, 1u);
@@ -477,14 +511,8 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
         float* kbase = L.kc + ((int64_t)b * Hkv + kvh) * (int64_t)p.ctx_max * D + (int64_t)j0 * D;
         float* vbase = L.vc + ((int64_t)b * Hkv + kvh) * (int64_t)p.ctx_max * D + (int64_t)j0 * D;
         pd_csync();  // the staging area is free
-        for (int i = tid; i < cnt * (D / 4); i += PD_CTHREADS) {
-            const int r = i / (D / 4), c = (i % (D / 4)) * 4;
-            if (r < fresh) {
-                cp_async16(&A.ks[r][c], kbase + (int64_t)r * D + c, true);
-                cp_async16(&A.vs[r][c], vbase + (int64_t)r * D + c, true);
-            }
-        }
-        cp_async_commit();
+        if (!kv_issued) pd_item_kv<M>(p, L, A, p0, nsplit, item);
+        kv_issued = false;
         // this kv head's q heads (and, for the chunk of the new position, its k and v) from
         // the q|k|v rows
         const float* qrow = p.qkv + (int64_t)b * heads * D;
@@ -771,10 +799,12 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
         if (!pd_consume<M>(S, pd_gemv(p, l, PH_QKV), xs, xds, it, hn, p.qkv, p.Nqkv, false, false, nullptr,
                            nullptr, p.err))
             return;
+        // the first attention item's cache rows start loading before the barrier
+        const int first = pd_attention_begin<M>(p, L, S, A, p0, nsplit, pd_att_ctr(p, M, l, 0));
         if (!pd_grid_barrier(p, S, epoch)) return;
         // attention -> Q8_0 rows
         pd_attention<M>(p, L, S, A, p0, nsplit, pd_att_ctr(p, M, l, 0), pd_att_ctr(p, M, l, 1),
-                        (unsigned)((l + 1) * nsplit));
+                        (unsigned)((l + 1) * nsplit), first);
         if (!pd_grid_barrier(p, S, epoch)) return;
         // O: the attention output as activations, residual into x
         {
