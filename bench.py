@@ -361,7 +361,9 @@ def run_ours(args, cfgd, world, rank, local):
         roofline, step_gbs, wbytes = moe_step_roofline(cfgd, B, L + W + K, ms / K, peak, peak_kind)
         return finish(args, cfgd, world, rank, L, B, K, W, ms, value, e2e, ms_e2e, clk, launches, roofline,
                       step_gbs, wbytes, t_create, t_pre, model, ctx, dist, comm)
-    # ---- roofline of the dominant kernel: the decode GEMV
+    # ---- roofline of the dominant kernel: the persistent decode step when the graph runs it
+    # (embedding, decode_step_kernel, argmax finalisation), else the decode GEMV
+    persistent = model.graph_kernels() == 3
     shapes = time_gemv_launches(lq8, ctx, model, cfgd, B)
     tot_b = tot_ms = 0.0
     per_shape = {}
@@ -389,6 +391,28 @@ def run_ours(args, cfgd, world, rank, local):
         "per_shape": per_shape,
     }
     wbytes = model.weight_bytes()
+    if persistent:
+        # one launch per step streams every Q8_0 weight once and reads the KV cache rows of the
+        # attended positions (K and V, f32); timed as the whole decode graph, of which the
+        # persistent kernel is all but a few microseconds of device time (ncu launch list)
+        hkv = cfgd["n_kv_heads"]
+        ctx_avg = L + W + (K + 1) / 2.0
+        kv_bytes = cfgd["layers"] * B * hkv * ctx_avg * 128 * 4 * 2
+        alg = wbytes + kv_bytes
+        ach = alg / (ms / K / 1000) / 1e9
+        ptraffic = None
+        if os.path.exists(tf):
+            for ln in open(tf):
+                if ln.startswith(f"traffic_bytes_per_launch decode_step {args.config} B={B} "):
+                    ptraffic = float(ln.split()[-1])
+        roofline = {
+            "bound": "hbm", "kernel": f"decode_step_kernel<{B}> (persistent: every layer + LM head per launch)",
+            "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+            "peak_kind": f"{peak_kind} copy bandwidth", "traffic": ptraffic,
+            "algorithmic_bytes_per_launch": alg, "weight_bytes": wbytes, "kv_bytes": kv_bytes,
+            "timed_as": "decode graph per step (memset, embedding, decode_step_kernel, argmax finalize)",
+            "per_layer_gemv_kernels": per_shape,
+        }
     step_gbs = wbytes / (ms / K / 1000) / 1e9
     return finish(args, cfgd, world, rank, L, B, K, W, ms, value, e2e, ms_e2e, clk, launches, roofline, step_gbs,
                   wbytes, t_create, t_pre, model, ctx, dist, comm)
