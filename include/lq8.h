@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define LQ8_ABI_VERSION 2
+#define LQ8_ABI_VERSION 3
 
 typedef enum {
     LQ_OK = 0,
@@ -172,6 +172,23 @@ int lq_embedding(lq_ctx* ctx, const uint16_t* table_dev, int64_t vocab, int64_t 
 /* sample_greedy / argmax_last_dim (generate.rs:153-174, tensor.rs:2451-2482): per row,
  * index of the maximum, ties -> highest index. */
 int lq_argmax(lq_ctx* ctx, const float* x_dev, int64_t rows, int64_t n, int32_t* out_dev);
+/* Token choice of the reference's generate loop (generate.rs:687-705 sample_with_config after
+ * :374-411 apply_repetition_penalty): temperature 0 -> greedy (ties -> last index);
+ * top_k > 0 -> the largest logit (ties -> first index); top_p < 1 -> the largest probability
+ * of softmax(x / T) (ties -> first index); else the largest x * (1/T) (ties -> last). The
+ * penalty (>= 1) divides positive and multiplies negative logits of generated tokens, once per
+ * occurrence. Validated like GenerationConfig::new (generate.rs:93-126). */
+typedef struct lq_sampling {
+    float temperature;         /* >= 0; 0: greedy */
+    int32_t top_k;             /* >= 0; 0: off */
+    float top_p;               /* [0, 1]; 1: off */
+    float repetition_penalty;  /* >= 1; 1: off */
+} lq_sampling;
+/* rows of logits [rows][ld] (device), generated tokens [rows][gen_ld] (device; the first
+ * n_generated of each row count), out_dev [rows] (device) */
+int lq_sample(lq_ctx* ctx, const float* logits_dev, int64_t rows, int64_t vocab, int64_t ld,
+              const int32_t* generated_dev, int64_t gen_ld, int64_t n_generated, const lq_sampling* cfg,
+              int32_t* out_dev);
 /* Integer-exact seeded generator (bf16 values approximating N(0, std^2)); the CPU oracle
  * implements the same function. */
 int lq_fill_bf16(lq_ctx* ctx, uint64_t seed, uint64_t tensor_id, int64_t offset, int64_t count,
@@ -273,6 +290,11 @@ int lq_qwen3_decode_step(lq_model* model, const int32_t* ids_host, int32_t* next
 int lq_qwen3_decode_device(lq_model* model, int64_t n_steps);
 /* Batch size (1..max_batch) of the decode graph; the default is max_batch. */
 int lq_qwen3_set_batch(lq_model* model, int64_t B);
+/* Token choice for the following prefill and decode steps (see lq_sampling; default greedy).
+ * The device keeps each sequence's generated tokens (reset by every prefill) for the
+ * repetition penalty. Non-greedy choices need the whole vocabulary on the rank (not under
+ * tensor parallelism). */
+int lq_qwen3_set_sampling(lq_model* model, const lq_sampling* cfg);
 /* The device token buffer [max_batch] int32 used by lq_qwen3_decode_device. */
 int lq_qwen3_token_buffer(lq_model* model, int32_t** tokens_dev);
 int lq_qwen3_position(lq_model* model, int64_t* pos);

@@ -87,6 +87,12 @@ def _declare(L):
     L.orc_softmax.argtypes = [_P, _I64]
     L.orc_attend_row.argtypes = [_P, _P, _P, _I64, _I64, _I64, C.c_int, _I64, _P, _P]
     L.orc_qwen3_create.restype = _P
+    L.orc_sample.argtypes = [_P, _I64, _P, _I64, C.c_float, _I64, C.c_float, C.c_float]
+    L.orc_sample.restype = C.c_int32
+    L.orc_sample_ex.argtypes = [_P, _I64, _P, _I64, C.c_float, _I64, C.c_float, C.c_float, C.c_int]
+    L.orc_sample_ex.restype = C.c_int32
+    L.orc_qwen3_generate_cfg.argtypes = [_P, _P, _I64, _I64, C.c_float, _I64, C.c_float, C.c_float, _P, _P]
+    L.orc_qwen3_generate_cfg.restype = C.c_int
     L.orc_qwen3_create.argtypes = [C.POINTER(Qwen3Config), C.c_uint64, _I64, _I64]
     L.orc_qwen3_destroy.argtypes = [_P]
     L.orc_qwen3_clear.argtypes = [_P]
@@ -286,6 +292,17 @@ def make_config(**kw) -> Qwen3Config:
     return c
 
 
+def sample(logits, generated=(), temperature: float = 0.0, top_k: int = 0, top_p: float = 1.0,
+           repetition_penalty: float = 1.0, exact_exp: bool = False) -> int:
+    """sample_with_config (generate.rs:687-705) after apply_repetition_penalty (:374-411) for
+    one row of logits (orc_sample); `generated` = the tokens generated so far. exact_exp:
+    top-p's exponentials correctly rounded instead of libm's expf (orc_sample_ex)."""
+    lg = np.ascontiguousarray(logits, dtype=np.float32).ravel()
+    gen = np.ascontiguousarray(np.asarray(generated, dtype=np.int32).ravel())
+    return int(lib().orc_sample_ex(_p(lg), lg.size, _p(gen) if gen.size else None, gen.size, temperature, top_k,
+                                   top_p, repetition_penalty, 1 if exact_exp else 0))
+
+
 class Qwen3Model:
     """Oracle Qwen3ForCausalLM with Q8_0 linears (model.rs:273-372)."""
 
@@ -335,11 +352,20 @@ class Qwen3Model:
         dd = np.ctypeslib.as_array(C.cast(d, C.POINTER(C.c_uint16)), shape=(n, k.value // QK)).copy()
         return q, dd
 
-    def generate(self, prompt, new_tokens: int):
+    def generate(self, prompt, new_tokens: int, sampling: dict | None = None):
+        """Greedy generate, or with `sampling` = dict(temperature, top_k, top_p,
+        repetition_penalty) the reference's sample_with_config at every step."""
         prompt = np.ascontiguousarray(prompt, dtype=np.int32)
         out = np.empty(new_tokens, dtype=np.int32)
         logits = np.empty(self.cfg.vocab, dtype=np.float32)
-        rc = lib().orc_qwen3_generate(self._h, _p(prompt), prompt.size, new_tokens, _p(out), _p(logits))
+        if sampling is None:
+            rc = lib().orc_qwen3_generate(self._h, _p(prompt), prompt.size, new_tokens, _p(out), _p(logits))
+        else:
+            sc = {"temperature": 0.0, "top_k": 0, "top_p": 1.0, "repetition_penalty": 1.0}
+            sc.update(sampling)
+            rc = lib().orc_qwen3_generate_cfg(self._h, _p(prompt), prompt.size, new_tokens, sc["temperature"],
+                                              sc["top_k"], sc["top_p"], sc["repetition_penalty"], _p(out),
+                                              _p(logits))
         if rc:
             raise ValueError("orc_qwen3_generate failed")
         return out, logits

@@ -720,6 +720,99 @@ int orc_qwen3_generate(orc_model* m, const int32_t* prompt, int64_t L, int64_t n
     return 0;
 }
 
+/* ---- sampling (generate.rs) ----------------------------------------------------------
+ * Every strategy of the reference picks a token deterministically ("Phase 0"):
+ *   sample_greedy (generate.rs:153-175): argmax, ties -> the last index (orc_argmax);
+ *   sample_temperature (:190-210): T == 1 (within 1e-6) -> greedy, else greedy over
+ *     x * (1/T) (mul_scalar, tensor.rs:1515-1519);
+ *   sample_top_k (:228-257): a stable sort by value descending, the first element: the
+ *     maximum, ties -> the first index (temperature unused);
+ *   sample_top_p (:274-326): p == 1 -> sample_temperature; else s = x / T when T != 1,
+ *     probabilities exp(s - max) / sum (sum in index order), a stable sort by probability
+ *     descending, the first element: ties -> the first index;
+ *   apply_repetition_penalty (:374-411): for every generated token in order (repeats
+ *     included), x > 0 -> x / penalty, x < 0 -> x * penalty;
+ *   sample_with_config (:687-705): penalty, then greedy when T == 0 or (T == 1 and k == 0
+ *     and p == 1), else top-k when k > 0, else top-p when p != 1, else temperature.
+ * Logits are assumed finite (the reference's partial_cmp makes NaN order unspecified). */
+static int64_t argmax_first(const float* x, int64_t n) {
+    int64_t best = 0;
+    for (int64_t i = 1; i < n; i++)
+        if (x[i] > x[best]) best = i;
+    return best;
+}
+
+/* exp as the reference's f32::exp (libm expf), or correctly rounded (exp in double, rounded
+ * once to f32) -- the device's choice for top-p, see orc_sample_ex */
+static float exp_f32(float x, int cr) { return cr ? (float)exp((double)x) : expf(x); }
+
+int32_t orc_sample(const float* logits, int64_t V, const int32_t* generated, int64_t n_generated,
+                   float temperature, int64_t top_k, float top_p, float penalty) {
+    return orc_sample_ex(logits, V, generated, n_generated, temperature, top_k, top_p, penalty, 0);
+}
+
+int32_t orc_sample_ex(const float* logits, int64_t V, const int32_t* generated, int64_t n_generated,
+                      float temperature, int64_t top_k, float top_p, float penalty, int cr_exp) {
+    float* x = (float*)malloc(sizeof(float) * (size_t)V);
+    memcpy(x, logits, sizeof(float) * (size_t)V);
+    if (!(fabsf(penalty - 1.0f) < 1e-6f) && n_generated > 0) {
+        for (int64_t i = 0; i < n_generated; i++) {
+            const int64_t t = (int64_t)(uint32_t)generated[i];
+            if (t < V) {
+                const float v = x[t];
+                if (v > 0.0f) x[t] = v / penalty;
+                else if (v < 0.0f) x[t] = v * penalty;
+            }
+        }
+    }
+    int64_t tok;
+    const int temp_one = fabsf(temperature - 1.0f) < 1e-6f;
+    const int p_one = fabsf(top_p - 1.0f) < 1e-6f;
+    if (temperature == 0.0f || (temp_one && top_k == 0 && p_one)) {
+        tok = orc_argmax(x, V);
+    } else if (top_k > 0) {
+        tok = argmax_first(x, V);
+    } else if (!p_one) {
+        if (!temp_one)
+            for (int64_t i = 0; i < V; i++) x[i] = x[i] / temperature;
+        float mx = x[0];
+        for (int64_t i = 1; i < V; i++)
+            if (!(mx > x[i])) mx = x[i];
+        float sum = 0.0f;
+        for (int64_t i = 0; i < V; i++) sum = sum + exp_f32(x[i] - mx, cr_exp);
+        for (int64_t i = 0; i < V; i++) x[i] = exp_f32(x[i] - mx, cr_exp) / sum;
+        tok = argmax_first(x, V);
+    } else {
+        const float inv = 1.0f / temperature;
+        for (int64_t i = 0; i < V; i++) x[i] = x[i] * inv;
+        tok = orc_argmax(x, V);
+    }
+    free(x);
+    return (int32_t)tok;
+}
+
+/* generate (generate.rs:611-661) with a sampling configuration: the first token from the
+ * prompt's logits with no history, then one token per step with the history of every token
+ * generated so far (the prompt is not part of it); EOS is not checked. */
+int orc_qwen3_generate_cfg(orc_model* m, const int32_t* prompt, int64_t L, int64_t new_tokens,
+                           float temperature, int64_t top_k, float top_p, float penalty,
+                           int32_t* out_tokens, float* last_logits) {
+    int64_t V = m->c.vocab;
+    float* logits = (float*)malloc(sizeof(float) * (size_t)V);
+    orc_qwen3_clear(m);
+    if (orc_qwen3_forward(m, prompt, L, 0, logits)) { free(logits); return -1; }
+    int32_t next = orc_sample(logits, V, out_tokens, 0, temperature, top_k, top_p, penalty);
+    out_tokens[0] = next;
+    for (int64_t i = 1; i < new_tokens; i++) {
+        if (orc_qwen3_forward(m, &next, 1, L + i - 1, logits)) { free(logits); return -1; }
+        next = orc_sample(logits, V, out_tokens, i, temperature, top_k, top_p, penalty);
+        out_tokens[i] = next;
+    }
+    if (last_logits) memcpy(last_logits, logits, sizeof(float) * (size_t)V);
+    free(logits);
+    return 0;
+}
+
 void orc_set_threads(int n) {
 #ifdef _OPENMP
     omp_set_num_threads(n > 0 ? n : 1);

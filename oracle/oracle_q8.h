@@ -131,6 +131,18 @@ int64_t orc_qwen3_linear(const orc_model* m, int64_t layer, int kind, const int8
 /* MoE weights: kind 10 router (expert ignored), 11 expert gate, 12 expert up, 13 expert down. */
 int64_t orc_qwen3_expert(const orc_model* m, int64_t layer, int64_t expert, int kind, const int8_t** qs,
                          const uint16_t** d, int64_t* k);
+/* sample_with_config (generate.rs:687-705) after apply_repetition_penalty (:374-411) for one
+ * row of logits; generated = the tokens generated so far (repeats count) */
+int32_t orc_sample(const float* logits, int64_t V, const int32_t* generated, int64_t n_generated,
+                   float temperature, int64_t top_k, float top_p, float penalty);
+/* the same with cr_exp != 0: top-p's exponentials correctly rounded instead of libm's expf
+ * (they differ in the last bit for a few inputs; only near-ties at the maximum can see it) */
+int32_t orc_sample_ex(const float* logits, int64_t V, const int32_t* generated, int64_t n_generated,
+                      float temperature, int64_t top_k, float top_p, float penalty, int cr_exp);
+/* generate (generate.rs:611-661) with a sampling configuration */
+int orc_qwen3_generate_cfg(orc_model* m, const int32_t* prompt, int64_t L, int64_t new_tokens,
+                           float temperature, int64_t top_k, float top_p, float penalty,
+                           int32_t* out_tokens, float* last_logits);
 void orc_set_threads(int n);
 int orc_get_threads(void);
 

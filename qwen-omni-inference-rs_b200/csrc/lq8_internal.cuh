@@ -224,8 +224,11 @@ int launch_fill_bf16_2d(lq_ctx* ctx, uint64_t seed, uint64_t tid, int64_t rows, 
                         int64_t row0, int64_t col0, float scale, uint16_t* out);
 int launch_fill_norm(lq_ctx* ctx, uint64_t seed, uint64_t tid, int64_t count, float norm_std,
                      uint16_t* out);
+// out: tokens from the keys (NULL: keep what a sampler wrote); gen: generated-token history
+// [rows][gen_ld] appended at n (n_host, or *pos_counter - *gen_base + 1 when n_host < 0)
 int launch_argmax_finalize(lq_ctx* ctx, unsigned long long* keys, int64_t rows, int32_t* out,
-                           int32_t* pos_counter);
+                           int32_t* pos_counter, int32_t* gen = nullptr, int64_t gen_ld = 0, int n_host = 0,
+                           const int32_t* gen_base = nullptr);
 // prefill attention (L >= 16 query positions per sequence): tiles of 128 (position, head) rows
 bool attention_prefill_supported(int64_t L, int64_t Hq, int64_t Hkv);
 int launch_attention_prefill(lq_ctx* ctx, const float* q, const float* kc, const float* vc, int64_t B, int64_t Hq,
@@ -299,4 +302,12 @@ size_t decode_persist_counter_bytes(int64_t m, int64_t Hkv, int64_t n_layers);
 int decode_persist_write_desc(lq_ctx* ctx, void* dev, const PdHostLayer* layers, int64_t n_layers,
                               const lq_q8_tensor* lm_head);
 int launch_decode_persist(lq_ctx* ctx, const PdLaunch& a);
+// token choice of the reference's generate loop (lq8_sample.cu); n_host < 0: the number of
+// generated tokens is *pos - *gen_base + 1 (a decode step of the graph)
+int check_sampling(lq_ctx* ctx, const lq_sampling* c);
+bool sampling_is_greedy(const lq_sampling& c);
+size_t sample_scratch_bytes(int64_t rows, int64_t V);
+int launch_sample(lq_ctx* ctx, const float* logits, int64_t rows, int64_t V, int64_t ld, const int32_t* gen,
+                  int64_t gen_ld, int n_host, const int32_t* pos, const int32_t* gen_base, const lq_sampling& c,
+                  float* scratch, int32_t* out, int32_t* gen_out);
 }  // namespace lq

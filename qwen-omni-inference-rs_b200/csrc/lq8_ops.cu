@@ -180,24 +180,32 @@ argmax_kernel(const float* __restrict__ x, int64_t n, int32_t* __restrict__ out)
     }
 }
 
-// next token ids from the LM head's fused argmax keys; clears the keys for the next step and
-// advances the device position of the decode graph
-__global__ void argmax_finalize_kernel(unsigned long long* keys, int64_t rows, int32_t* out,
-                                       int32_t* pos_counter) {
+// next token ids from the LM head's fused argmax keys (out may be NULL when a sampler chose
+// them); clears the keys for the next step, appends each row's token to its generated-token
+// history gen[row][n] (n = n_host, or *pos_counter - *gen_base + 1 when n_host < 0) and then
+// advances the device position of the decode graph. One block, so the position is read by
+// every thread before it is advanced.
+__global__ void argmax_finalize_kernel(unsigned long long* keys, int64_t rows, int32_t* out, int32_t* pos_counter,
+                                       int32_t* gen, int64_t gen_ld, int n_host, const int32_t* gen_base) {
     pdl_wait();
     pdl_trigger();
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < rows) {
-        out[i] = (int32_t)(uint32_t)(keys[i] & 0xFFFFFFFFull);
+    int n = n_host;
+    if (gen && n < 0) n = *pos_counter - *gen_base + 1;
+    for (int64_t i = threadIdx.x; i < rows; i += blockDim.x) {
+        const int32_t t = (int32_t)(uint32_t)(keys[i] & 0xFFFFFFFFull);
+        if (out) out[i] = t;
+        if (gen && n >= 0 && n < gen_ld) gen[i * gen_ld + n] = t;
         keys[i] = 0ull;
     }
-    if (i == 0 && pos_counter) *pos_counter += 1;
+    __syncthreads();
+    if (threadIdx.x == 0 && pos_counter) *pos_counter += 1;
 }
 
 int launch_argmax_finalize(lq_ctx* ctx, unsigned long long* keys, int64_t rows, int32_t* out,
-                           int32_t* pos_counter) {
-    return launch_kernel(ctx, argmax_finalize_kernel, dim3(ceil_div(std::max<int64_t>(rows, 1), 128)), dim3(128),
-                         0, "argmax_finalize", keys, rows, out, pos_counter);
+                           int32_t* pos_counter, int32_t* gen, int64_t gen_ld, int n_host, const int32_t* gen_base) {
+    const int threads = (int)std::min<int64_t>(1024, std::max<int64_t>(32, (rows + 31) / 32 * 32));
+    return launch_kernel(ctx, argmax_finalize_kernel, dim3(1), dim3(threads), 0, "argmax_finalize", keys, rows, out,
+                         pos_counter, gen, gen_ld, n_host, gen_base);
 }
 
 __global__ void add_kernel(const float* a, const float* b, int64_t n, float* out) {

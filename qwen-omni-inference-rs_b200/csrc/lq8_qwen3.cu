@@ -82,6 +82,11 @@ struct lq_model {
     void* pd_desc = nullptr;         // per-layer tensor maps and pointers
     float* pd_part = nullptr;        // attention chunk partials
     unsigned* pd_counters = nullptr; // grid barrier + chunk counters
+    // token choice (generate.rs sample_with_config); greedy keeps the LM head's fused argmax
+    lq_sampling samp{0.0f, 0, 1.0f, 1.0f};
+    int32_t* gen = nullptr;          // generated tokens [max_batch][ctx_max] (the penalty's history)
+    int32_t* gen_base = nullptr;     // device position of the first decode step after prefill
+    float* samp_scratch = nullptr;   // [max_batch][vocab] penalized logits
     std::vector<void*> allocs;
 };
 
@@ -195,6 +200,22 @@ void destroy_graph(lq_model* m) {
 // One forward pass over B sequences of L new tokens each at positions [pos0, pos0+L)
 // (pos_dev overrides pos0 when set). tokens [B*L] must already be in m->tokens. Writes the
 // greedy next token of each sequence to m->tokens[0..B) and the last-row logits to m->logits.
+// the next token of each row from the last-row logits: the LM head's fused argmax keys when
+// the configuration is greedy, else the sampler over m->logits; both append the token to the
+// generated-token history (index 0 after a prefill, else position - gen_base + 1) and advance
+// the device position when asked
+int finish_tokens(lq_model* m, int64_t B, const int32_t* pos_dev, bool bump_pos) {
+    lq_ctx* ctx = m->ctx;
+    const int n_host = pos_dev ? -1 : 0;
+    if (lq::sampling_is_greedy(m->samp))
+        return lq::launch_argmax_finalize(ctx, m->keys, B, m->tokens, bump_pos ? m->pos_dev : nullptr, m->gen,
+                                          m->ctx_max, n_host, m->gen_base);
+    int rc = lq::launch_sample(ctx, m->logits, B, m->c.vocab, m->V_l, m->gen, m->ctx_max, n_host, m->pos_dev,
+                               m->gen_base, m->samp, m->samp_scratch, m->tokens, m->gen);
+    if (rc) return rc;
+    return lq::launch_argmax_finalize(ctx, m->keys, B, nullptr, bump_pos ? m->pos_dev : nullptr);
+}
+
 int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_dev, bool bump_pos) {
     lq_ctx* ctx = m->ctx;
     const lq_qwen3_config& c = m->c;
@@ -232,7 +253,7 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
         a.keys = m->keys;
         a.counters = m->pd_counters;
         RC(lq::launch_decode_persist(ctx, a));
-        RC(lq::launch_argmax_finalize(ctx, m->keys, B, m->tokens, bump_pos ? m->pos_dev : nullptr));
+        RC(finish_tokens(m, B, pos_dev, bump_pos));
         return LQ_OK;
     }
     if (L == 1 && pos_dev && m->fused_decode && B <= 4) {
@@ -258,7 +279,7 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
         RC(lq::launch_gemv_norm(ctx, &m->lm_head, m->x, m->final_norm, c.eps, B, m->logits, nullptr, m->V_l,
                                 m->keys));
         RC(lm_keys_reduce(m, B));
-        RC(lq::launch_argmax_finalize(ctx, m->keys, B, m->tokens, bump_pos ? m->pos_dev : nullptr));
+        RC(finish_tokens(m, B, pos_dev, bump_pos));
         return LQ_OK;
     }
     for (size_t li = 0; li < m->layers.size(); li++) {
@@ -309,7 +330,7 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
     // LM head with the greedy argmax fused into its epilogue
     RC(lq::launch_q8_matmul(ctx, &m->lm_head, m->xq, m->xd, B, m->logits, nullptr, m->V_l, m->keys));
     RC(lm_keys_reduce(m, B));
-    RC(lq::launch_argmax_finalize(ctx, m->keys, B, m->tokens, bump_pos ? m->pos_dev : nullptr));
+    RC(finish_tokens(m, B, pos_dev, bump_pos));
 #undef RC
     return LQ_OK;
 }
@@ -503,6 +524,8 @@ static int create_model(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, 
     if (Ta > 1) RC(dalloc_t(m, &m->logits_all, (size_t)(T * max_batch * Vl)));
     RC(dalloc_t(m, &m->keys, (size_t)max_batch));
     RC(dalloc_t(m, &m->tokens, (size_t)R));
+    RC(dalloc_t(m, &m->gen, (size_t)(max_batch * ctx_max)));
+    RC(dalloc_t(m, &m->gen_base, 1));
     RC(dalloc_t(m, &m->pos_dev, 1));
     // attention partials: decode (max_batch rows) or one prefill sequence (<= R rows)
     int64_t att_rows = std::max<int64_t>(max_batch, std::min<int64_t>(R, ctx_max));
@@ -622,11 +645,14 @@ int lq_qwen3_prefill(lq_model* m, const int32_t* ids, int64_t B, int64_t L, int3
         // [b0, b0+nb) uses batch offsets b0.. inside each layer)
         float* kc_save = m->kc;
         float* vc_save = m->vc;
+        int32_t* gen_save = m->gen;
         m->kc = kc_save + b0 * Hkv * m->ctx_max * D;
         m->vc = vc_save + b0 * Hkv * m->ctx_max * D;
+        m->gen = gen_save + b0 * m->ctx_max;
         int rc = forward(m, nb, L, 0, nullptr, false);
         m->kc = kc_save;
         m->vc = vc_save;
+        m->gen = gen_save;
         if (rc) return rc;
         LQ_CUDA(ctx, cudaMemcpyAsync(next + b0, m->tokens, (size_t)nb * 4, cudaMemcpyDeviceToHost, ctx->stream));
         if (logits) {
@@ -638,6 +664,8 @@ int lq_qwen3_prefill(lq_model* m, const int32_t* ids, int64_t B, int64_t L, int3
     m->pos = L;
     int32_t p = (int32_t)L;
     LQ_CUDA(ctx, cudaMemcpyAsync(m->pos_dev, &p, 4, cudaMemcpyHostToDevice, ctx->stream));
+    // the first decode step (position L) samples with one generated token in the history
+    LQ_CUDA(ctx, cudaMemcpyAsync(m->gen_base, &p, 4, cudaMemcpyHostToDevice, ctx->stream));
     LQ_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
     return lq::consume_device_error(ctx, "lq_qwen3_prefill");
 }
@@ -754,6 +782,27 @@ int lq_qwen3_expert(lq_model* m, int64_t layer, int64_t expert, int kind, lq_q8_
         case 13: *out = rows_view(ly.moe_down, j * H, H); break;
         default: return lq::set_error(ctx, LQ_ERR_INVALID_ARG, "lq_qwen3_expert: kind %d", kind);
     }
+    return LQ_OK;
+}
+
+int lq_qwen3_set_sampling(lq_model* m, const lq_sampling* cfg) {
+    if (!m) return LQ_ERR_INVALID_ARG;
+    lq_ctx* ctx = m->ctx;
+    LQ_ENTRY(ctx, "lq_qwen3_set_sampling");
+    int rc = lq::check_sampling(ctx, cfg);
+    if (rc) return rc;
+    if (!lq::sampling_is_greedy(*cfg)) {
+        LQ_REQUIRE(ctx, m->V_l == m->c.vocab, "lq_qwen3_set_sampling: a vocabulary-sharded LM head (tensor parallel) "
+                                              "supports greedy decoding only");
+        if (!m->samp_scratch) {
+            void* buf = nullptr;
+            rc = dalloc(m, &buf, lq::sample_scratch_bytes(m->max_batch, m->c.vocab));
+            if (rc) return rc;
+            m->samp_scratch = static_cast<float*>(buf);
+        }
+    }
+    m->samp = *cfg;
+    destroy_graph(m);  // the decode graph holds the token-choice kernels
     return LQ_OK;
 }
 

@@ -51,6 +51,16 @@ class Qwen3Config(C.Structure):
     ]
 
 
+class Sampling(C.Structure):
+    """lq_sampling: the reference's GenerationConfig knobs (generate.rs:38-64)."""
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_int32), ("top_p", C.c_float),
+                ("repetition_penalty", C.c_float)]
+
+
+def sampling(temperature: float = 0.0, top_k: int = 0, top_p: float = 1.0, repetition_penalty: float = 1.0):
+    return Sampling(temperature, top_k, top_p, repetition_penalty)
+
+
 class MoeExperts(C.Structure):
     """lq_moe_experts: stacked expert weights (gate/up [E*2I][H], down [E*H][I])."""
     _fields_ = [("n_experts", C.c_int64), ("inter", C.c_int64), ("hidden", C.c_int64),
@@ -83,7 +93,7 @@ _I64 = C.c_int64
 _lib = None
 
 # name -> (restype, argtypes); the single source of the binding, checked against lq8.h
-ABI_VERSION = 2   # LQ8_ABI_VERSION of the struct layouts below
+ABI_VERSION = 3   # LQ8_ABI_VERSION of the struct layouts below
 
 SIGNATURES = {
     "lq_abi_version": (C.c_int, []),
@@ -135,6 +145,8 @@ SIGNATURES = {
     "lq_qwen3_linear": (C.c_int, [_P, _I64, C.c_int, C.POINTER(Q8Tensor)]),
     "lq_qwen3_weight_bytes": (C.c_int, [_P, C.POINTER(_I64)]),
     "lq_qwen3_graph_kernels": (C.c_int, [_P, C.POINTER(_I64)]),
+    "lq_qwen3_set_sampling": (C.c_int, [_P, C.POINTER(Sampling)]),
+    "lq_sample": (C.c_int, [_P, _P, _I64, _I64, _I64, _P, _I64, _I64, C.POINTER(Sampling), _P]),
     "lq_qwen3_expert": (C.c_int, [_P, _I64, _I64, C.c_int, C.POINTER(Q8Tensor)]),
     "lq_moe_forward": (C.c_int, [_P, C.POINTER(Q8Tensor), C.POINTER(MoeExperts), _P, _P, _I64, _I64, C.c_int,
                                  _P, _P, _P, _P]),
@@ -287,6 +299,21 @@ class Linear:
         return y.reshape(*x.shape[:-1], self.weight.n)
 
 
+def sample(ctx: Context, logits, generated=None, n_generated: int = 0, out=None, **cfg):
+    """lq_sample: the reference's token choice (sample_with_config after the repetition
+    penalty) for rows of device logits [rows][V] (torch CUDA tensor, f32); generated: device
+    int32 [rows][gen_ld] of which the first n_generated per row count. Returns int32 [rows]."""
+    import torch
+    rows, V = logits.shape
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int32, device=logits.device)
+    sc = sampling(**cfg)
+    gen_ld = generated.shape[1] if generated is not None else 0
+    ctx.call("lq_sample", logits.data_ptr(), rows, V, logits.stride(0), _ptr(generated), gen_ld, n_generated,
+             C.byref(sc), out.data_ptr())
+    return out
+
+
 def matmul_q8(ctx: Context, w: QTensor, xq, xd, residual=None, out=None):
     """Q8_0 x Q8_0 matmul with pre-quantized activations (optionally y = residual + x.W^T)."""
     import torch
@@ -382,6 +409,12 @@ class Qwen3ForCausalLM:
         self._check(self.ctx.lib.lq_qwen3_prefill(self.h, ids.ctypes.data, B, L, nxt.ctypes.data,
                                                   lg.ctypes.data if lg is not None else None))
         return (nxt, lg) if want_logits else nxt
+
+    def set_sampling(self, **cfg):
+        """Token choice for the following steps (temperature, top_k, top_p,
+        repetition_penalty; defaults greedy), as the reference's sample_with_config."""
+        sc = sampling(**cfg)
+        self._check(self.ctx.lib.lq_qwen3_set_sampling(self.h, C.byref(sc)))
 
     def set_batch(self, B: int):
         self._check(self.ctx.lib.lq_qwen3_set_batch(self.h, B))
