@@ -304,6 +304,10 @@ int lq_qwen3_position(lq_model* model, int64_t* pos);
 int lq_qwen3_linear(lq_model* model, int64_t layer, int kind, lq_q8_tensor* out);
 /* Bytes of Q8_0 weights streamed per decode step (for rooflines). */
 int lq_qwen3_weight_bytes(lq_model* model, int64_t* bytes);
+/* Access to a bf16 parameter: kind 20 input norm, 21 post-attention norm, 22 q norm, 23 k norm
+ * of a layer; layer -1 with kind 24 final norm, 25 embedding table [vocab][hidden]. *dev_out
+ * aliases the model's buffer (load a checkpoint by writing into it); *count = elements. */
+int lq_qwen3_tensor(lq_model* model, int64_t layer, int kind, uint16_t** dev_out, int64_t* count);
 /* Kernel launches in one decode step (kernel nodes of the captured CUDA graph; 0 before the
  * first decode step or lq_qwen3_set_batch). */
 /* MoE weights of a layer: kind 10 router (expert ignored), 11 gate, 12 up, 13 down of

@@ -785,6 +785,29 @@ int lq_qwen3_expert(lq_model* m, int64_t layer, int64_t expert, int kind, lq_q8_
     return LQ_OK;
 }
 
+int lq_qwen3_tensor(lq_model* m, int64_t layer, int kind, uint16_t** dev_out, int64_t* count) {
+    if (!m || !dev_out || !count) return LQ_ERR_INVALID_ARG;
+    lq_ctx* ctx = m->ctx;
+    const int64_t H = m->c.hidden, D = m->c.head_dim;
+    if (layer < 0) {
+        switch (kind) {
+            case 24: *dev_out = m->final_norm; *count = H; return LQ_OK;
+            case 25: *dev_out = m->embed; *count = m->c.vocab * H; return LQ_OK;
+            default: return lq::set_error(ctx, LQ_ERR_INVALID_ARG, "lq_qwen3_tensor: layer -1 needs kind 24 or 25");
+        }
+    }
+    LQ_REQUIRE(ctx, layer < (int64_t)m->layers.size(), "lq_qwen3_tensor: layer out of range");
+    const Layer& ly = m->layers[(size_t)layer];
+    switch (kind) {
+        case 20: *dev_out = ly.in_norm; *count = H; break;
+        case 21: *dev_out = ly.post_norm; *count = H; break;
+        case 22: *dev_out = ly.q_norm; *count = D; break;
+        case 23: *dev_out = ly.k_norm; *count = D; break;
+        default: return lq::set_error(ctx, LQ_ERR_INVALID_ARG, "lq_qwen3_tensor: kind %d", kind);
+    }
+    return LQ_OK;
+}
+
 int lq_qwen3_set_sampling(lq_model* m, const lq_sampling* cfg) {
     if (!m) return LQ_ERR_INVALID_ARG;
     lq_ctx* ctx = m->ctx;

@@ -146,6 +146,7 @@ SIGNATURES = {
     "lq_qwen3_weight_bytes": (C.c_int, [_P, C.POINTER(_I64)]),
     "lq_qwen3_graph_kernels": (C.c_int, [_P, C.POINTER(_I64)]),
     "lq_qwen3_set_sampling": (C.c_int, [_P, C.POINTER(Sampling)]),
+    "lq_qwen3_tensor": (C.c_int, [_P, _I64, C.c_int, C.POINTER(_P), C.POINTER(_I64)]),
     "lq_sample": (C.c_int, [_P, _P, _I64, _I64, _I64, _P, _I64, _I64, C.POINTER(Sampling), _P]),
     "lq_qwen3_expert": (C.c_int, [_P, _I64, _I64, C.c_int, C.POINTER(Q8Tensor)]),
     "lq_moe_forward": (C.c_int, [_P, C.POINTER(Q8Tensor), C.POINTER(MoeExperts), _P, _P, _I64, _I64, C.c_int,
@@ -450,6 +451,14 @@ class Qwen3ForCausalLM:
         t = Q8Tensor()
         self._check(self.ctx.lib.lq_qwen3_expert(self.h, layer, expert, kind, C.byref(t)))
         return t
+
+    def tensor(self, layer: int, kind: str):
+        """Device (pointer, count) of a bf16 parameter: 'in_norm', 'post_norm', 'q_norm',
+        'k_norm' of a layer; layer -1: 'final_norm', 'embed'."""
+        kid = {"in_norm": 20, "post_norm": 21, "q_norm": 22, "k_norm": 23, "final_norm": 24, "embed": 25}[kind]
+        p, n = _P(), _I64()
+        self._check(self.ctx.lib.lq_qwen3_tensor(self.h, layer, kid, C.byref(p), C.byref(n)))
+        return p.value, n.value
 
     def graph_kernels(self) -> int:
         n = _I64()
