@@ -14,9 +14,9 @@
 //                 softmax, top-k, weights; also the token's experts in ascending order.
 //   moe_dispatch  one CTA: per-expert pair lists in token order (warp ballots, deterministic),
 //                 offsets, the list of active experts, each pair's slot for the combine.
-//   moe_stream    persistent grouped GEMV streaming the touched experts' weights through a
-//                 shared-memory ring (see below); the gate/up pass fuses SiLU * up and the
-//                 Q8_0 quantization of h.
+//   moe_mma       persistent grouped GEMV on the int8 tensor cores streaming the touched
+//                 experts' weights through a shared-memory ring (see below); the gate/up pass
+//                 fuses SiLU * up and the Q8_0 quantization of h.
 //   moe_combine   per token: residual + sum_e w_e * y_e in ascending expert order.
 #include "lq8_async.cuh"
 #include "lq8_fused.cuh"
@@ -218,35 +218,46 @@ __global__ void __launch_bounds__(1024) moe_dispatch_kernel(const int32_t* __res
 }
 
 // ---------------------------------------------------------------------------------------
-// grouped expert GEMV, streamed
+// grouped expert GEMV on the int8 tensor cores (mma.sync m16n8k32, s8 x s8 -> s32)
 //
-// Work item = (active expert, 128 output rows); each CTA takes a contiguous range of items,
-// so consecutive items mostly share the expert and its activations stay in shared memory.
-// One producer lane streams the item's weight rows (gate/up: the 128 gate rows and the 128
-// matching up rows) in K-chunks of 256 bytes (8 Q8_0 blocks) into a shared-memory ring with
-// 2-D TMA loads: per group of 128 rows two 128-byte-wide boxes (128-byte swizzle, so the
-// row-per-lane 16-byte reads are bank-conflict free) and one box of the chunk's scales.
-// Consumer warp w owns rows 32 (w % 4) + lane and one half of the pass's tokens (16 tokens
-// per pass, split evenly between the halves; more tokens take more passes), so all eight
-// warps work even for two tokens per expert, and every (row, token) output is accumulated
-// by one thread in ascending block order: bit-identical to the oracle (which keeps the next
-// layer's routing identical). Epilogue: gate/up -> h = silu(g) * u quantized to Q8_0 (a
-// warp's 32 rows are one block); down -> y [pair][row] f32.
+// Work item = (active expert, a tile of output rows): gate/up streams 32 gate rows and the
+// 32 matching up rows (32 rows of h), down streams 64 rows of the down projection -- 64
+// weight rows either way. Each CTA takes a contiguous range of items, so consecutive items
+// mostly share the expert and its activations stay in shared memory. One producer lane
+// streams the item's rows in K-chunks of 256 bytes (8 Q8_0 blocks) into a shared-memory ring
+// with 2-D TMA loads: per 32-row group two 128-byte-wide boxes (128-byte swizzle) and one box
+// of the chunk's fp16 scales, 17 KiB per stage. Consumer warp w owns stage rows 16w..16w+15
+// (one m16 tile) and the pass's tokens as up to two n8 tiles (16 tokens per pass; more
+// tokens take more passes over the weights). One MMA covers one Q8_0 block of 16 rows x 8
+// tokens; its int32 dots are scaled per block and added to f32 accumulators that each thread
+// keeps for fixed (row, token) pairs, in ascending block order with separately rounded
+// multiply and add: the oracle's order, so every output is bit-identical to it.
+//
+// The MMA's 32 k positions are a permutation of the block's bytes: thread t of a quad holds
+// bytes 8t..8t+3 of its rows (and tokens) in the register the MMA reads as k = 4t..4t+3 and
+// bytes 8t+4..8t+7 in the one read as k = 16+4t..16+4t+3. A and B use the same permutation,
+// so the integer dot is unchanged, and each operand is a single 8-byte shared load (2
+// wavefronts per warp: the swizzle spreads the weight rows, a 16-byte pad the token rows).
+//
+// Epilogue: gate/up -> the gate and up accumulators meet in shared memory, then
+// h = silu(g) * u is quantized to Q8_0 (the item's 32 rows are one block of h); down -> y
+// [pair][row] f32.
 // ---------------------------------------------------------------------------------------
-constexpr int ME_KC = 256;                   // K bytes per stage
-constexpr int ME_R = 128;                    // output rows per item
-constexpr int ME_TG = 16;                    // tokens per pass
-constexpr int ME_TH = ME_TG / 2;             // tokens per consumer half
-constexpr int ME_CONSUMERS = 8;
+constexpr int ME_KC = 256;                            // K bytes per stage
+constexpr int ME_GRP = 32;                            // rows per group (one TMA box tall)
+constexpr int ME_BOX = ME_GRP * 128;                  // one 128-byte-wide box (4 KiB)
+constexpr int ME_W_BYTES = 2 * ME_GRP * ME_KC;        // two groups: 16 KiB of weights
+constexpr int ME_STAGE = ME_W_BYTES + 2 * ME_GRP * 16;  // + fp16 scales [64 rows][8]: 17 KiB
+constexpr int ME_CONSUMERS = 4;
 constexpr int ME_THREADS = (ME_CONSUMERS + 1) * 32;
 constexpr int ME_MAX_STAGES = 8;
-constexpr int ME_BOX = ME_R * 128;           // one 128-byte-wide box of a group
-constexpr int ME_GROUP_W = 2 * ME_BOX;       // weight bytes of one group per stage
-constexpr int ME_GROUP_D = ME_R * 16;        // scale bytes of one group per stage
+constexpr int ME_TOK = 16;                            // tokens per pass (two n8 tiles)
+constexpr int ME_XCH = 33;                            // row stride (floats) of the gate/up exchange
+static_assert(ME_STAGE % 1024 == 0, "swizzled boxes need 1024-byte aligned stages");
 
 struct MoeExpertParams {
     int rows_per_expert;     // gate/up: 2I (gate rows then up rows); down: H
-    int out_rows;            // gate/up: I; down: H (multiples of 128)
+    int out_rows;            // gate/up: I; down: H
     int K;                   // multiple of 256
     int stages;
     const int8_t* xq;        // activations: gate/up [rows][K] by token; down [pairs][K] by pair
@@ -263,38 +274,29 @@ struct MoeExpertParams {
     int* err;
 };
 
-// fp16 bits j (0..7) of an int4 holding 8 halves (j known at compile time after unrolling)
-__device__ __forceinline__ uint16_t half_at(const int4 v, int j) {
-    const unsigned w = (unsigned)(j < 2 ? v.x : j < 4 ? v.y : j < 6 ? v.z : v.w);
-    return (uint16_t)((j & 1) ? (w >> 16) : (w & 0xFFFFu));
+// shared memory after the stages: barriers, the gate/up exchange, the pass's tokens
+__host__ __device__ constexpr size_t me_fixed_bytes(bool gu, int K) {
+    return (size_t)2 * ME_MAX_STAGES * 8 + (gu ? (size_t)2 * ME_TOK * ME_XCH * 4 : 0) +
+           (size_t)ME_TOK * (K + 16) + (size_t)(K / 32) * ME_TOK * 4;
 }
 
-// stage: NG groups of [2 boxes][128 rows][128 B] (swizzled), then NG x [128 rows][8 fp16]
-template <bool GU>
-__host__ __device__ constexpr int me_stage_bytes() {
-    return ((GU ? 2 : 1) * (ME_GROUP_W + ME_GROUP_D) + 1023) / 1024 * 1024;
-}
-
-// 16-byte chunk `c` (0..15 over the 256-byte chunk) of row r in a group laid out by the
-// 128-byte swizzle: box c/8, row r, chunk (c%8) ^ (r%8)
-__device__ __forceinline__ int4 me_ld(const uint8_t* group, int r, int c) {
-    return *reinterpret_cast<const int4*>(group + (c >> 3) * ME_BOX + r * 128 + ((((c & 7) ^ (r & 7))) << 4));
+__device__ __forceinline__ float h2f_bits(uint32_t w, int hi) {
+    return h2f((uint16_t)(hi ? (w >> 16) : (w & 0xFFFFu)));
 }
 
 template <bool GU>
-__global__ void __launch_bounds__(ME_THREADS) moe_stream_kernel(const __grid_constant__ CUtensorMap mw,
-                                                                const __grid_constant__ CUtensorMap md,
-                                                                const MoeExpertParams p) {
+__global__ void __launch_bounds__(ME_THREADS) moe_mma_kernel(const __grid_constant__ CUtensorMap mw,
+                                                             const __grid_constant__ CUtensorMap md,
+                                                             const MoeExpertParams p) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     const uint32_t raw = smem_addr(smem_raw);
     uint8_t* sm = smem_raw + (((raw + 1023) & ~1023u) - raw);  // swizzled boxes need 1024-byte alignment
-    constexpr int NG = GU ? 2 : 1;
-    constexpr int SB = me_stage_bytes<GU>();
-    const int K = p.K, nb = K / 32, nchunks = K / ME_KC, S = p.stages;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sm + (size_t)S * SB);
+    const int K = p.K, nb = K / 32, nchunks = K / ME_KC, S = p.stages, XS = K + 16;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + (size_t)S * ME_STAGE);
     uint64_t* empty = full + ME_MAX_STAGES;
-    int8_t* xs = reinterpret_cast<int8_t*>(empty + ME_MAX_STAGES);           // [ME_TG][K]
-    float* xdf = reinterpret_cast<float*>(xs + (size_t)ME_TG * K);           // [ME_TG][nb]
+    float* xch = reinterpret_cast<float*>(empty + ME_MAX_STAGES);                 // [2][ME_TOK][ME_XCH]
+    int8_t* xs = reinterpret_cast<int8_t*>(xch + (GU ? 2 * ME_TOK * ME_XCH : 0));  // [ME_TOK][K + 16]
+    float* xdf = reinterpret_cast<float*>(xs + (size_t)ME_TOK * XS);               // [nb][ME_TOK]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
@@ -307,7 +309,8 @@ __global__ void __launch_bounds__(ME_THREADS) moe_stream_kernel(const __grid_con
     pdl_wait();
     pdl_trigger();
     const int n_active = p.active[p.E];
-    const int tiles = p.out_rows / ME_R;
+    const int item_rows = GU ? ME_GRP : 2 * ME_GRP;  // output rows per item
+    const int tiles = p.out_rows / item_rows;
     const long long items = (long long)n_active * tiles;
     const long long i0 = items * blockIdx.x / gridDim.x, i1 = items * (blockIdx.x + 1) / gridDim.x;
 
@@ -317,8 +320,9 @@ __global__ void __launch_bounds__(ME_THREADS) moe_stream_kernel(const __grid_con
         int it = 0;
         for (long long item = i0; item < i1; item++) {
             const int e = p.active[item / tiles];
-            const int r0 = (int)(item % tiles) * ME_R;
-            const int passes = (p.counts[e] + ME_TG - 1) / ME_TG;
+            const int r0 = (int)(item % tiles) * item_rows;
+            const int passes = (p.counts[e] + ME_TOK - 1) / ME_TOK;
+            const int base = (e - p.e_base) * p.rows_per_expert;
             for (int ps = 0; ps < passes; ps++)
                 for (int c = 0; c < nchunks; c++, it++) {
                     const int s = it % S;
@@ -326,112 +330,134 @@ __global__ void __launch_bounds__(ME_THREADS) moe_stream_kernel(const __grid_con
                         atomicCAS(p.err, 0, 21);
                         return;
                     }
-                    uint8_t* st = sm + (size_t)s * SB;
-                    mbar_expect_tx(&full[s], (unsigned)(NG * (ME_GROUP_W + ME_GROUP_D)));
-                    for (int g = 0; g < NG; g++) {
-                        const int row = (e - p.e_base) * p.rows_per_expert + g * p.out_rows + r0;
-                        tma_load_2d(st + g * ME_GROUP_W, &mw, c * ME_KC, row, &full[s]);
-                        tma_load_2d(st + g * ME_GROUP_W + ME_BOX, &mw, c * ME_KC + 128, row, &full[s]);
-                        tma_load_2d(st + NG * ME_GROUP_W + g * ME_GROUP_D, &md, c * 8, row, &full[s]);
+                    uint8_t* st = sm + (size_t)s * ME_STAGE;
+                    mbar_expect_tx(&full[s], (unsigned)ME_STAGE);
+                    for (int q = 0; q < 2; q++) {
+                        const int row = base + (GU ? q * p.out_rows + r0 : r0 + q * ME_GRP);
+                        tma_load_2d(st + q * 2 * ME_BOX, &mw, c * ME_KC, row, &full[s]);
+                        tma_load_2d(st + q * 2 * ME_BOX + ME_BOX, &mw, c * ME_KC + 128, row, &full[s]);
+                        tma_load_2d(st + ME_W_BYTES + q * ME_GRP * 16, &md, c * 8, row, &full[s]);
                     }
                 }
         }
         return;
     }
     // ---------------- consumers ----------------
-    const int rq = warp & 3, half = warp >> 2;
-    const int row = rq * 32 + lane;  // row within the item
+    const int g = lane >> 2, t = lane & 3;
+    const int q = warp >> 1;                    // group: gate/up -> 0 gate, 1 up; down -> rows 32q..
+    const int ra = 16 * (warp & 1) + g;         // rows ra and ra + 8 of the group
+    // byte offsets in a stage: the two 8-byte A pieces of block j (swizzle key g = ra & 7)
+    const int a_row = q * 2 * ME_BOX + ra * 128 + (t & 1) * 8;
+    const int sc_off = ME_W_BYTES + q * ME_GRP * 16 + ra * 16;
     int it = 0, cur_e = -1, cur_g0 = -1;
+    bool bad = false;
     for (long long item = i0; item < i1; item++) {
         const int e = p.active[item / tiles];
-        const int r0 = (int)(item % tiles) * ME_R;
+        const int r0 = (int)(item % tiles) * item_rows;
         const int cnt = p.counts[e], p0 = p.offsets[e];
-        for (int g0 = 0; g0 < cnt; g0 += ME_TG) {
-            const int ng = min(ME_TG, cnt - g0);
+        for (int g0 = 0; g0 < cnt; g0 += ME_TOK) {
+            const int ng = min(ME_TOK, cnt - g0);
             if (e != cur_e || g0 != cur_g0) {
                 group_sync<ME_CONSUMERS * 32, 1>();  // nobody still reads the previous tokens
                 for (int i = threadIdx.x; i < ng * (K / 16); i += ME_CONSUMERS * 32) {
                     const int tk = i / (K / 16), c16 = (i % (K / 16)) * 16;
                     const int src = GU ? p.pair_token[p0 + g0 + tk] : p0 + g0 + tk;
-                    cp_async16(xs + (size_t)tk * K + c16, p.xq + (size_t)src * K + c16, true);
+                    cp_async16(xs + (size_t)tk * XS + c16, p.xq + (size_t)src * K + c16, true);
                 }
                 cp_async_commit();
                 for (int i = threadIdx.x; i < ng * nb; i += ME_CONSUMERS * 32) {
                     const int tk = i / nb, b = i % nb;
                     const int src = GU ? p.pair_token[p0 + g0 + tk] : p0 + g0 + tk;
-                    xdf[tk * nb + b] = h2f(p.xd[(size_t)src * nb + b]);
+                    xdf[b * ME_TOK + tk] = h2f(p.xd[(size_t)src * nb + b]);
                 }
                 cp_async_wait<0>();
                 group_sync<ME_CONSUMERS * 32, 1>();
                 cur_e = e;
                 cur_g0 = g0;
             }
-            // this warp's tokens: the first ceil(ng/2) for half 0, the rest for half 1
-            const int h0 = (ng + 1) >> 1;
-            const int tb = half ? h0 : 0, nt = half ? ng - h0 : h0;
-            float ga[ME_TH], ua[ME_TH];
+            const bool two = ng > 8;  // second n8 tile (warp-uniform)
+            float acc[2][4];
 #pragma unroll
-            for (int q = 0; q < ME_TH; q++) ga[q] = ua[q] = 0.0f;
+            for (int n = 0; n < 2; n++)
+#pragma unroll
+                for (int v = 0; v < 4; v++) acc[n][v] = 0.0f;
             for (int c = 0; c < nchunks; c++, it++) {
                 const int s = it % S;
-                bool ok = true;
-                if (lane == 0) ok = mbar_wait(&full[s], (unsigned)(it / S) & 1u);
-                ok = __shfl_sync(0xffffffffu, ok, 0);
-                if (!ok) {
-                    if (lane == 0) atomicCAS(p.err, 0, 22);
-                    return;
-                }
-                const uint8_t* st = sm + (size_t)s * SB;
-                if (nt > 0) {
-                    const int4 dgv = *reinterpret_cast<const int4*>(st + NG * ME_GROUP_W + row * 16);
-                    int4 duv = make_int4(0, 0, 0, 0);
-                    if (GU) duv = *reinterpret_cast<const int4*>(st + NG * ME_GROUP_W + ME_GROUP_D + row * 16);
-#pragma unroll
-                    for (int j = 0; j < 8; j++) {
-                        const int4 w0 = me_ld(st, row, 2 * j), w1 = me_ld(st, row, 2 * j + 1);
-                        const float dwg = h2f(half_at(dgv, j));
-                        int4 v0 = make_int4(0, 0, 0, 0), v1 = v0;
-                        float dwu = 0.f;
-                        if (GU) {
-                            v0 = me_ld(st + ME_GROUP_W, row, 2 * j);
-                            v1 = me_ld(st + ME_GROUP_W, row, 2 * j + 1);
-                            dwu = h2f(half_at(duv, j));
-                        }
-                        const int blk = c * 8 + j;
-#pragma unroll
-                        for (int q = 0; q < ME_TH; q++) {
-                            if (q < nt) {
-                                const int8_t* xp = xs + (size_t)(tb + q) * K + (size_t)blk * 32;
-                                const int4 x0 = *reinterpret_cast<const int4*>(xp);
-                                const int4 x1 = *reinterpret_cast<const int4*>(xp + 16);
-                                const float dx = xdf[(tb + q) * nb + blk];
-                                ga[q] = __fadd_rn(ga[q], __fmul_rn((float)dot32(w0, w1, x0, x1), __fmul_rn(dwg, dx)));
-                                if (GU)
-                                    ua[q] = __fadd_rn(ua[q],
-                                                      __fmul_rn((float)dot32(v0, v1, x0, x1), __fmul_rn(dwu, dx)));
-                            }
-                        }
+                if (!bad) {
+                    bool ok = true;
+                    if (lane == 0) ok = mbar_wait(&full[s], (unsigned)(it / S) & 1u);
+                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                    if (!ok) {
+                        if (lane == 0) atomicCAS(p.err, 0, 22);
+                        bad = true;
                     }
                 }
+                if (bad) continue;
+                const uint8_t* st = sm + (size_t)s * ME_STAGE;
+                // this warp's slice of the stage into registers, then release the stage
+                uint2 wa[8], wb[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const int ch = ((2 * (j & 3) + (t >> 1)) ^ g) << 4;
+                    wa[j] = *reinterpret_cast<const uint2*>(st + a_row + (j >> 2) * ME_BOX + ch);
+                    wb[j] = *reinterpret_cast<const uint2*>(st + a_row + 8 * 128 + (j >> 2) * ME_BOX + ch);
+                }
+                const uint4 sa = *reinterpret_cast<const uint4*>(st + sc_off);
+                const uint4 sb = *reinterpret_cast<const uint4*>(st + sc_off + 8 * 16);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[s]);
-            }
-            // epilogue (warp-uniform: nt depends on the warp only)
 #pragma unroll
-            for (int q = 0; q < ME_TH; q++) {
-                if (q >= nt) continue;
-                const int pr = p0 + g0 + tb + q;
-                if (GU) {
-                    const float g = ga[q];
-                    const float h = __fmul_rn(g / (1.0f + expf(-g)), ua[q]);
-                    const float amax = warp_max(fabsf(h));
-                    float d, id;
-                    q8_scale(amax, d, id);
-                    p.hq[(size_t)pr * p.out_rows + r0 + row] = (int8_t)q8_quant(h, id);
-                    if (lane == 0) p.hd[(size_t)pr * (p.out_rows / 32) + (r0 + rq * 32) / 32] = f2h(d);
-                } else {
-                    p.y[(size_t)pr * p.out_rows + r0 + row] = ga[q];
+                for (int j = 0; j < 8; j++) {
+                    const uint32_t a[4] = {wa[j].x, wb[j].x, wa[j].y, wb[j].y};
+                    const uint32_t wsa = j < 2 ? sa.x : j < 4 ? sa.y : j < 6 ? sa.z : sa.w;
+                    const uint32_t wsb = j < 2 ? sb.x : j < 4 ? sb.y : j < 6 ? sb.z : sb.w;
+                    const float dwa = h2f_bits(wsa, j & 1), dwb = h2f_bits(wsb, j & 1);
+                    const int blk = c * 8 + j;
+#pragma unroll
+                    for (int n = 0; n < 2; n++) {
+                        if (n == 1 && !two) break;
+                        const uint2 xv =
+                            *reinterpret_cast<const uint2*>(xs + (size_t)(8 * n + g) * XS + blk * 32 + 8 * t);
+                        const uint32_t b[2] = {xv.x, xv.y};
+                        int d[4];
+                        mma_s8(d, a, b);
+                        const float2 dx = *reinterpret_cast<const float2*>(xdf + blk * ME_TOK + 8 * n + 2 * t);
+                        acc[n][0] = __fadd_rn(acc[n][0], __fmul_rn((float)d[0], __fmul_rn(dwa, dx.x)));
+                        acc[n][1] = __fadd_rn(acc[n][1], __fmul_rn((float)d[1], __fmul_rn(dwa, dx.y)));
+                        acc[n][2] = __fadd_rn(acc[n][2], __fmul_rn((float)d[2], __fmul_rn(dwb, dx.x)));
+                        acc[n][3] = __fadd_rn(acc[n][3], __fmul_rn((float)d[3], __fmul_rn(dwb, dx.y)));
+                    }
                 }
+            }
+            // epilogue: accumulator v of n-tile n is (row ra + 8 (v >> 1), token 8n + 2t + (v & 1))
+            if (GU) {
+#pragma unroll
+                for (int n = 0; n < 2; n++)
+#pragma unroll
+                    for (int v = 0; v < 4; v++)
+                        xch[(q * ME_TOK + 8 * n + 2 * t + (v & 1)) * ME_XCH + ra + 8 * (v >> 1)] = acc[n][v];
+                group_sync<ME_CONSUMERS * 32, 1>();
+                if (!bad)
+                    for (int tk = warp; tk < ng; tk += ME_CONSUMERS) {
+                        const float gv = xch[tk * ME_XCH + lane], uv = xch[(ME_TOK + tk) * ME_XCH + lane];
+                        const float h = __fmul_rn(gv / (1.0f + expf(-gv)), uv);
+                        const float amax = warp_max(fabsf(h));
+                        float d, id;
+                        q8_scale(amax, d, id);
+                        const int pr = p0 + g0 + tk;
+                        p.hq[(size_t)pr * p.out_rows + r0 + lane] = (int8_t)q8_quant(h, id);
+                        if (lane == 0) p.hd[(size_t)pr * (p.out_rows / 32) + r0 / 32] = f2h(d);
+                    }
+                group_sync<ME_CONSUMERS * 32, 1>();  // the exchange is rewritten by the next item
+            } else if (!bad) {
+                const int row = r0 + 32 * q + ra;
+#pragma unroll
+                for (int n = 0; n < 2; n++)
+#pragma unroll
+                    for (int v = 0; v < 4; v++) {
+                        const int tk = 8 * n + 2 * t + (v & 1);
+                        if (tk < ng) p.y[(size_t)(p0 + g0 + tk) * p.out_rows + row + 8 * (v >> 1)] = acc[n][v];
+                    }
             }
         }
     }
@@ -463,36 +489,39 @@ __global__ void moe_combine_kernel(const float* __restrict__ y, const int32_t* _
 // ---------------------------------------------------------------------------------------
 static size_t al256(size_t b) { return (b + 255) & ~(size_t)255; }
 
-static size_t me_x_bytes(int K) { return (size_t)ME_TG * K + (size_t)ME_TG * (K / 32) * 4; }
-
 template <bool GU>
 static int launch_moe_stream(lq_ctx* ctx, MoeExpertParams p, const int8_t* wq, const uint16_t* wd,
                              int64_t total_rows) {
-    const size_t sb = (size_t)me_stage_bytes<GU>();
-    const size_t fixed = 2 * ME_MAX_STAGES * 8 + me_x_bytes(p.K) + 1024 /*alignment*/;
-    const size_t budget = 227 * 1024;
-    int stages = (int)std::min<size_t>(GU ? 2 : 4, (budget - fixed) / sb);
+    // two CTAs per SM when their rings still hold three stages each, else one with a deeper ring
+    const size_t fixed = me_fixed_bytes(GU, p.K) + 1024 /*alignment*/;
+    const size_t pair_budget = 113 * 1024, solo_budget = 227 * 1024;
+    int per_sm = 2;
+    int stages = pair_budget > fixed ? (int)((pair_budget - fixed) / ME_STAGE) : 0;
+    if (stages < 3) {
+        per_sm = 1;
+        stages = solo_budget > fixed ? (int)((solo_budget - fixed) / ME_STAGE) : 0;
+    }
     stages = std::min(stages, ME_MAX_STAGES);
     if (stages < 2) return set_error(ctx, LQ_ERR_UNSUPPORTED, "moe: K=%d leaves no room for the weight ring", p.K);
     p.stages = stages;
     CUtensorMap mw, md;
     int rc = make_tensor_map_2d(ctx, &mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)p.K, (uint64_t)total_rows,
-                                (uint64_t)p.K, 128, ME_R, CU_TENSOR_MAP_SWIZZLE_128B);
+                                (uint64_t)p.K, 128, ME_GRP, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
     rc = make_tensor_map_2d(ctx, &md, CU_TENSOR_MAP_DATA_TYPE_UINT16, wd, (uint64_t)(p.K / 32), (uint64_t)total_rows,
-                            (uint64_t)(p.K / 32) * 2, 8, ME_R, CU_TENSOR_MAP_SWIZZLE_NONE);
+                            (uint64_t)(p.K / 32) * 2, 8, ME_GRP, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
-    const size_t smem = (size_t)stages * sb + fixed;
+    const size_t smem = (size_t)stages * ME_STAGE + fixed;
     static bool attr[2][64] = {};
     if (ctx->device < 0 || ctx->device >= 64 || !attr[GU][ctx->device]) {
-        LQ_CUDA(ctx, cudaFuncSetAttribute(moe_stream_kernel<GU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)budget));
+        LQ_CUDA(ctx, cudaFuncSetAttribute(moe_mma_kernel<GU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)solo_budget));
         if (ctx->device >= 0 && ctx->device < 64) attr[GU][ctx->device] = true;
     }
-    int per_sm = 1;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, moe_stream_kernel<GU>, ME_THREADS, smem);
-    per_sm = std::max(1, std::min(per_sm, 2));
-    return launch_kernel(ctx, moe_stream_kernel<GU>, dim3(ctx->sm_count * per_sm), dim3(ME_THREADS), smem,
+    int occ = 1;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, moe_mma_kernel<GU>, ME_THREADS, smem);
+    per_sm = std::max(1, std::min(per_sm, occ));
+    return launch_kernel(ctx, moe_mma_kernel<GU>, dim3(ctx->sm_count * per_sm), dim3(ME_THREADS), smem,
                          GU ? "moe_gate_up" : "moe_down", mw, md, p);
 }
 
