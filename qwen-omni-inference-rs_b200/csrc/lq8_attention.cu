@@ -14,6 +14,8 @@
 // projection row it computes the G query heads' RMSNorm + RoPE into shared memory, and the
 // CTA whose chunk holds the new position computes that position's k (RMSNorm + RoPE) and v,
 // uses them from shared memory and appends them to the caches.
+#include <type_traits>
+
 #include "lq8_async.cuh"
 #include "lq8_fused.cuh"
 #include "lq8_internal.cuh"
@@ -44,6 +46,22 @@ struct AttSmem {
     int last;
 };
 
+// The unfused variant (query rows from a q tensor: batched decode and short prefills) has its
+// own layout: q heads with the second half of the dims shifted by 4 floats (so that the two
+// halves of a warp read q with one broadcast wavefront), scores by position (so that P.V reads
+// a position's 8 probabilities with two broadcast loads). Its merge weights live in the last
+// 4 KiB of the V staging area, which keeps the struct small enough for three CTAs per SM.
+struct AttSmemR {
+    float ks[ATT_C][ATT_KS];
+    float vs[ATT_C][ATT_D];
+    float qp[ATT_G][ATT_KS];
+    float pt[ATT_C][ATT_G];
+    float ml[ATT_G][2];
+    float cl[ATT_G];
+    int last;
+};
+constexpr int ATT_CM_FLOATS = ATT_G * ATT_MAX_SPLITS;
+
 struct AttParams {
     const float* q;        // [B][Hq][L][D] (unfused)
     const float* qkv;      // [B][(Hq+2Hkv)*D] (fused decode)
@@ -73,12 +91,97 @@ __device__ __forceinline__ void quant_warp32(float v, int lane, int8_t* q_out, u
     if (lane == 0) *d_out = f2h(d);
 }
 
-template <bool FUSED>
+__device__ __forceinline__ float* att_cm(AttSmem& S) { return &S.cm[0][0]; }
+__device__ __forceinline__ float* att_cm(AttSmemR& S) { return &S.vs[0][0] + ATT_C * ATT_D - ATT_CM_FLOATS; }
+
+// Unfused chunk: scores (thread -> position tid/2 and one 64-dim half, all GN heads; the halves
+// meet by a shuffle), per-head chunk softmax, P.V (thread -> dim, all heads), partials out.
+template <int GN>
+__device__ __forceinline__ void attn_chunk_fma(AttSmemR& S, int G, int cnt, float scale, int tid,
+                                               const AttParams& p, int64_t hbase, int nsplit) {
+    const int lane = tid & 31, warp = tid >> 5;
+    {
+        const int pp = tid >> 1, hf = tid & 1;
+        float s[GN];
+#pragma unroll
+        for (int g = 0; g < GN; g++) s[g] = 0.0f;
+        if (pp < cnt) {
+            const float* kr = &S.ks[pp][hf * (ATT_D / 2)];
+            const float* qr = &S.qp[0][hf * (ATT_D / 2 + 4)];
+#pragma unroll 4
+            for (int d4 = 0; d4 < ATT_D / 8; d4++) {
+                const float4 k4 = *reinterpret_cast<const float4*>(kr + 4 * d4);
+#pragma unroll
+                for (int g = 0; g < GN; g++) {
+                    if (g < G) {
+                        const float4 q4 = *reinterpret_cast<const float4*>(qr + g * ATT_KS + 4 * d4);
+                        s[g] = fmaf(q4.x, k4.x, s[g]);
+                        s[g] = fmaf(q4.y, k4.y, s[g]);
+                        s[g] = fmaf(q4.z, k4.z, s[g]);
+                        s[g] = fmaf(q4.w, k4.w, s[g]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < GN; g++) s[g] = __fadd_rn(s[g], __shfl_xor_sync(0xffffffffu, s[g], 1));
+        // half 0 stores heads 0..3, half 1 heads 4..7
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int g = 4 * hf + i;
+            float v = 0.0f;
+            if (i < GN) v = s[i < GN ? i : 0];
+            if (GN > 4 && hf) v = s[4 + i < GN ? 4 + i : 0];
+            if (g < G) S.pt[pp][g] = pp < cnt ? __fmul_rn(v, scale) : -INFINITY;
+        }
+    }
+    __syncthreads();
+    for (int g = warp; g < G; g += ATT_THREADS / 32) {
+        const float a = S.pt[lane][g], c = S.pt[lane + 32][g];
+        const float m = warp_max(fmaxf(a, c));
+        const float ea = expf(__fsub_rn(a, m)), ec = expf(__fsub_rn(c, m));
+        S.pt[lane][g] = ea;
+        S.pt[lane + 32][g] = ec;
+        const float sum = warp_sum(__fadd_rn(ea, ec));
+        if (lane == 0) { S.ml[g][0] = m; S.ml[g][1] = sum; }
+    }
+    __syncthreads();
+    {
+        const int d = tid;
+        float acc[GN];
+#pragma unroll
+        for (int g = 0; g < GN; g++) acc[g] = 0.0f;
+#pragma unroll 4
+        for (int j = 0; j < cnt; j++) {
+            const float vv = S.vs[j][d];
+            const float4 pa = *reinterpret_cast<const float4*>(&S.pt[j][0]);
+            float4 pb = pa;
+            if constexpr (GN > 4) pb = *reinterpret_cast<const float4*>(&S.pt[j][4]);
+            const float pj[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+            for (int g = 0; g < GN; g++) acc[g] = fmaf(pj[g], vv, acc[g]);
+        }
+#pragma unroll
+        for (int g = 0; g < GN; g++)
+            if (g < G) p.part_o[(hbase + (int64_t)g * nsplit) * ATT_D + d] = acc[g];
+        if (tid < G) {
+            p.part_ml[(hbase + (int64_t)tid * nsplit) * 2] = S.ml[tid][0];
+            p.part_ml[(hbase + (int64_t)tid * nsplit) * 2 + 1] = S.ml[tid][1];
+        }
+    }
+}
+
+// FUSED: the decode step's fused variant, every sum in the reference's order (sequential
+// 128-term dots, separately rounded multiply and add; the persistent decode kernel repeats it
+// bit for bit). Unfused: GT query heads per kv head (0: any G <= 8), dots and P.V with fused
+// multiply-add and each score's two 64-dim halves added at the end.
+template <bool FUSED, int GT>
 __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const AttParams p) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
-    AttSmem& S = *reinterpret_cast<AttSmem*>(smem_raw);
+    using Smem = typename std::conditional<FUSED, AttSmem, AttSmemR>::type;
+    Smem& S = *reinterpret_cast<Smem*>(smem_raw);
     const int Hq = p.Hq, Hkv = p.Hkv, L = p.L, ctx_max = p.ctx_max, nsplit = p.nsplit;
-    const int G = Hq / Hkv;
+    const int G = GT ? GT : Hq / Hkv;
     const int split = blockIdx.x, kvh = blockIdx.y, lrow = blockIdx.z;
     const int row = p.row0 + lrow;  // b*L + l
     const int b = row / L, l = row - (row / L) * L;
@@ -139,14 +242,18 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const AttParams
         cp_async_commit();
         for (int i = tid; i < G * ATT_D; i += ATT_THREADS) {
             const int g = i / ATT_D, d = i % ATT_D;
-            S.qs[g][d] = p.q[(((int64_t)b * Hq + kvh * G + g) * L + l) * ATT_D + d];
+            S.qp[g][d + (d >= ATT_D / 2 ? 4 : 0)] = p.q[(((int64_t)b * Hq + kvh * G + g) * L + l) * ATT_D + d];
         }
     }
     cp_async_wait<0>();
     __syncthreads();
 
-    // scores: thread -> (position pp, heads half, half+2, ...); sequential 128-term dot
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)ATT_D));
+    if constexpr (!FUSED) {
+        attn_chunk_fma<GT ? GT : ATT_G>(S, G, cnt, scale, tid, p, ((int64_t)lrow * Hq + (int64_t)kvh * G) * nsplit + split,
+                                        nsplit);
+    } else {
+    // scores: thread -> (position pp, heads half, half+2, ...); sequential 128-term dot
     {
         const int pp = tid % ATT_C, half = tid / ATT_C;
         float s[ATT_G / 2];
@@ -208,6 +315,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const AttParams
             p.part_ml[(hbase + (int64_t)tid * nsplit) * 2 + 1] = S.ml[tid][1];
         }
     }
+    }
     // the last chunk CTA of this (row, kv head) merges the chunks
     __threadfence();
     __syncthreads();
@@ -224,8 +332,9 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const AttParams
     // overlapping the current head's sum: one L2 round trip per head instead of a chain of
     // dependent loads
     float* po = &S.ks[0][0];
+    float* cm = att_cm(S);  // [G][ATT_MAX_SPLITS]
     const size_t head_floats = (size_t)n_active * ATT_D;
-    const bool staged = 2 * head_floats * 4 <= sizeof(S.ks) + sizeof(S.vs);
+    const bool staged = 2 * head_floats * 4 <= sizeof(S.ks) + sizeof(S.vs) - (FUSED ? 0 : ATT_CM_FLOATS * 4);
     auto stage_head = [&](int g) {
         float* dst = po + (size_t)(g & 1) * head_floats;
         for (int i = tid; i < n_active * (ATT_D / 4); i += ATT_THREADS) {
@@ -246,7 +355,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const AttParams
         float lsum = 0.0f;
         for (int s = lane; s < n_active; s += 32) {
             const float w = expf(__fsub_rn(ld_cg(&p.part_ml[(hbase0 + (int64_t)g * nsplit + s) * 2]), m));
-            S.cm[g][s] = w;
+            cm[g * ATT_MAX_SPLITS + s] = w;
             lsum = __fadd_rn(lsum, __fmul_rn(w, ld_cg(&p.part_ml[(hbase0 + (int64_t)g * nsplit + s) * 2 + 1])));
         }
         lsum = warp_sum(lsum);
@@ -261,13 +370,14 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const AttParams
             else cp_async_wait<0>();
             __syncthreads();
             const float* pg = po + (size_t)(g & 1) * head_floats + d;
-            for (int s = 0; s < n_active; s++) o = __fadd_rn(o, __fmul_rn(S.cm[g][s], pg[(size_t)s * ATT_D]));
+            for (int s = 0; s < n_active; s++)
+                o = __fadd_rn(o, __fmul_rn(cm[g * ATT_MAX_SPLITS + s], pg[(size_t)s * ATT_D]));
             __syncthreads();  // this buffer is refilled next
             if (g + 2 < G) stage_head(g + 2);
         } else {
 #pragma unroll 8
             for (int s = 0; s < n_active; s++)
-                o = __fadd_rn(o, __fmul_rn(S.cm[g][s],
+                o = __fadd_rn(o, __fmul_rn(cm[g * ATT_MAX_SPLITS + s],
                                            ld_cg(&p.part_o[(hbase0 + (int64_t)g * nsplit + s) * ATT_D + d])));
         }
         o = __fdiv_rn(o, S.cl[g]);
@@ -288,8 +398,9 @@ size_t attention_scratch_bytes(int64_t rows, int64_t Hq, int64_t ctx_max, int64_
     return ATT_COUNTER_BYTES + ml + (size_t)(slice * Hq * nsplit * ATT_D) * 4;
 }
 
-template <bool FUSED>
+template <bool FUSED, int GT>
 static int launch_chunks(lq_ctx* ctx, AttParams p, int64_t rows, void* scratch, bool zero_counters) {
+    using Smem = typename std::conditional<FUSED, AttSmem, AttSmemR>::type;
     const int64_t slice = std::min<int64_t>(rows, ATT_SLICE);
     p.counters = (int*)scratch;
     p.part_ml = (float*)((uint8_t*)scratch + ATT_COUNTER_BYTES);
@@ -297,8 +408,8 @@ static int launch_chunks(lq_ctx* ctx, AttParams p, int64_t rows, void* scratch, 
     p.part_o = (float*)((uint8_t*)scratch + ATT_COUNTER_BYTES + ml);
     static bool attr = false;
     if (!attr) {
-        LQ_CUDA(ctx, cudaFuncSetAttribute(attn_chunk_kernel<FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)sizeof(AttSmem)));
+        LQ_CUDA(ctx, cudaFuncSetAttribute(attn_chunk_kernel<FUSED, GT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)sizeof(Smem)));
         attr = true;
     }
     if (zero_counters)
@@ -307,7 +418,7 @@ static int launch_chunks(lq_ctx* ctx, AttParams p, int64_t rows, void* scratch, 
         const int64_t n = std::min(slice, rows - r0);
         p.row0 = (int)r0;
         const dim3 grid(p.nsplit, (unsigned)p.Hkv, (unsigned)n);
-        const int rc = launch_kernel(ctx, attn_chunk_kernel<FUSED>, grid, dim3(ATT_THREADS), sizeof(AttSmem),
+        const int rc = launch_kernel(ctx, attn_chunk_kernel<FUSED, GT>, grid, dim3(ATT_THREADS), sizeof(Smem),
                                      "attn_chunk", p);
         if (rc) return rc;
     }
@@ -340,7 +451,13 @@ int launch_attention(lq_ctx* ctx, const float* q, const float* kc, const float* 
     p.out = out;
     p.xq = xq;
     p.xd = xd;
-    return launch_chunks<false>(ctx, p, rows, scratch, zero_counters);
+    switch (Hq / Hkv) {
+        case 8: return launch_chunks<false, 8>(ctx, p, rows, scratch, zero_counters);
+        case 4: return launch_chunks<false, 4>(ctx, p, rows, scratch, zero_counters);
+        case 2: return launch_chunks<false, 2>(ctx, p, rows, scratch, zero_counters);
+        case 1: return launch_chunks<false, 1>(ctx, p, rows, scratch, zero_counters);
+        default: return launch_chunks<false, 0>(ctx, p, rows, scratch, zero_counters);
+    }
 }
 
 int launch_attention_decode_fused(lq_ctx* ctx, const float* qkv, const uint16_t* qn, const uint16_t* kn,
@@ -365,7 +482,7 @@ int launch_attention_decode_fused(lq_ctx* ctx, const float* qkv, const uint16_t*
     p.nsplit = ceil_div(ctx_max, ATT_C);
     p.xq = xq;
     p.xd = xd;
-    return launch_chunks<true>(ctx, p, B, scratch, false);
+    return launch_chunks<true, 0>(ctx, p, B, scratch, false);
 }
 
 }  // namespace lq
