@@ -284,6 +284,34 @@ __device__ __forceinline__ float h2f_bits(uint32_t w, int hi) {
     return h2f((uint16_t)(hi ? (w >> 16) : (w & 0xFFFFu)));
 }
 
+// One stage's 8 blocks for NT n8 tiles: A pieces wa/wb (rows ra, ra + 8) and their scales
+// sa/sb (8 fp16 each) in registers; xb -> this thread's 8 bytes of token g's first block
+// (n-tile stride xstride), db -> the f32 scales of tokens 2t, 2t+1 of the first block.
+template <int NT>
+__device__ __forceinline__ void me_blocks(float (&acc)[2][4], const uint2 (&wa)[8], const uint2 (&wb)[8],
+                                          const uint4 sa, const uint4 sb, const int8_t* xb, int xstride,
+                                          const float* db) {
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const uint32_t a[4] = {wa[j].x, wb[j].x, wa[j].y, wb[j].y};
+        const uint32_t wsa = j < 2 ? sa.x : j < 4 ? sa.y : j < 6 ? sa.z : sa.w;
+        const uint32_t wsb = j < 2 ? sb.x : j < 4 ? sb.y : j < 6 ? sb.z : sb.w;
+        const float dwa = h2f_bits(wsa, j & 1), dwb = h2f_bits(wsb, j & 1);
+#pragma unroll
+        for (int n = 0; n < NT; n++) {
+            const uint2 xv = *reinterpret_cast<const uint2*>(xb + n * xstride + j * 32);
+            const uint32_t b[2] = {xv.x, xv.y};
+            int d[4];
+            mma_s8(d, a, b);
+            const float2 dx = *reinterpret_cast<const float2*>(db + j * ME_TOK + 8 * n);
+            acc[n][0] = __fadd_rn(acc[n][0], __fmul_rn((float)d[0], __fmul_rn(dwa, dx.x)));
+            acc[n][1] = __fadd_rn(acc[n][1], __fmul_rn((float)d[1], __fmul_rn(dwa, dx.y)));
+            acc[n][2] = __fadd_rn(acc[n][2], __fmul_rn((float)d[2], __fmul_rn(dwb, dx.x)));
+            acc[n][3] = __fadd_rn(acc[n][3], __fmul_rn((float)d[3], __fmul_rn(dwb, dx.y)));
+        }
+    }
+}
+
 template <bool GU>
 __global__ void __launch_bounds__(ME_THREADS) moe_mma_kernel(const __grid_constant__ CUtensorMap mw,
                                                              const __grid_constant__ CUtensorMap md,
@@ -406,28 +434,12 @@ __global__ void __launch_bounds__(ME_THREADS) moe_mma_kernel(const __grid_consta
                 const uint4 sb = *reinterpret_cast<const uint4*>(st + sc_off + 8 * 16);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[s]);
-#pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    const uint32_t a[4] = {wa[j].x, wb[j].x, wa[j].y, wb[j].y};
-                    const uint32_t wsa = j < 2 ? sa.x : j < 4 ? sa.y : j < 6 ? sa.z : sa.w;
-                    const uint32_t wsb = j < 2 ? sb.x : j < 4 ? sb.y : j < 6 ? sb.z : sb.w;
-                    const float dwa = h2f_bits(wsa, j & 1), dwb = h2f_bits(wsb, j & 1);
-                    const int blk = c * 8 + j;
-#pragma unroll
-                    for (int n = 0; n < 2; n++) {
-                        if (n == 1 && !two) break;
-                        const uint2 xv =
-                            *reinterpret_cast<const uint2*>(xs + (size_t)(8 * n + g) * XS + blk * 32 + 8 * t);
-                        const uint32_t b[2] = {xv.x, xv.y};
-                        int d[4];
-                        mma_s8(d, a, b);
-                        const float2 dx = *reinterpret_cast<const float2*>(xdf + blk * ME_TOK + 8 * n + 2 * t);
-                        acc[n][0] = __fadd_rn(acc[n][0], __fmul_rn((float)d[0], __fmul_rn(dwa, dx.x)));
-                        acc[n][1] = __fadd_rn(acc[n][1], __fmul_rn((float)d[1], __fmul_rn(dwa, dx.y)));
-                        acc[n][2] = __fadd_rn(acc[n][2], __fmul_rn((float)d[2], __fmul_rn(dwb, dx.x)));
-                        acc[n][3] = __fadd_rn(acc[n][3], __fmul_rn((float)d[3], __fmul_rn(dwb, dx.y)));
-                    }
-                }
+                // straight-line code for the chunk's 8 blocks (the n8-tile count is decided
+                // once, outside), so loads and MMAs of different blocks can overlap
+                const int8_t* xb = xs + (size_t)g * XS + c * ME_KC + 8 * t;
+                const float* db = xdf + c * 8 * ME_TOK + 2 * t;
+                if (two) me_blocks<2>(acc, wa, wb, sa, sb, xb, 8 * XS, db);
+                else me_blocks<1>(acc, wa, wb, sa, sb, xb, 8 * XS, db);
             }
             // epilogue: accumulator v of n-tile n is (row ra + 8 (v >> 1), token 8n + 2t + (v & 1))
             if (GU) {
