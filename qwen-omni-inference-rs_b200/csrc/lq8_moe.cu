@@ -44,7 +44,7 @@ __device__ __forceinline__ int dot32(const int4 a0, const int4 a1, const int4 b0
 // ---------------------------------------------------------------------------------------
 // route: one CTA per token (min(1024, max(128, 8E)) threads)
 // ---------------------------------------------------------------------------------------
-__global__ void moe_route_kernel(const int8_t* __restrict__ xq, const uint16_t* __restrict__ xd, int H,
+__global__ void __launch_bounds__(1024) moe_route_kernel(const int8_t* __restrict__ xq, const uint16_t* __restrict__ xd, int H,
                                  const int8_t* __restrict__ rq, const uint16_t* __restrict__ rd, int E, int top_k,
                                  int norm_topk, int32_t* __restrict__ ids, float* __restrict__ wts,
                                  int32_t* __restrict__ ids_sorted, float* __restrict__ w_sorted) {
@@ -63,25 +63,49 @@ __global__ void moe_route_kernel(const int8_t* __restrict__ xq, const uint16_t* 
         *reinterpret_cast<int4*>(sx + i) = *reinterpret_cast<const int4*>(xq + (size_t)t * H + i);
     for (int b = tid; b < nb; b += blockDim.x) sdx[b] = h2f(xd[(size_t)t * nb + b]);
     __syncthreads();
-    // logits: a warp per expert; lanes form the block terms (int dot, scale product) in
-    // parallel, then lane 0 adds them in ascending block order (the oracle's sum)
-    float* terms = pe + E + (size_t)(tid >> 5) * nb;   // [warps][nb]
+    // logits: warp w takes experts 4w..4w+3 (then 4 (w + nwarps) ...). Lanes form the block
+    // terms (int dot, scale product) of all four experts with every load of a pass in flight
+    // at once; then lane q adds expert q's terms in ascending block order (the oracle's sum).
     const int warp = tid >> 5, lane = tid & 31, nwarps = blockDim.x >> 5;
-    for (int e = warp; e < E; e += nwarps) {
-        const int8_t* wr = rq + (size_t)e * H;
-        const uint16_t* wd = rd + (size_t)e * nb;
-        for (int b = lane; b < nb; b += 32) {
-            const int4 w0 = __ldg(reinterpret_cast<const int4*>(wr + b * 32));
-            const int4 w1 = __ldg(reinterpret_cast<const int4*>(wr + b * 32 + 16));
-            const int4 x0 = *reinterpret_cast<const int4*>(sx + b * 32);
-            const int4 x1 = *reinterpret_cast<const int4*>(sx + b * 32 + 16);
-            terms[b] = __fmul_rn((float)dot32(w0, w1, x0, x1), __fmul_rn(h2f(__ldg(wd + b)), sdx[b]));
+    const int ts = nb + 1;                              // padded term row (conflict-free sums)
+    float* terms = pe + E + (size_t)warp * 4 * ts;      // [4][nb + 1]
+    for (int e0 = 4 * warp; e0 < E; e0 += 4 * nwarps) {
+        for (int b0 = 0; b0 < nb; b0 += 32) {
+            int4 w[4][1][2];
+            float dw[4][1];
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+#pragma unroll
+                for (int i = 0; i < 1; i++) {
+                    const int e = e0 + q, b = b0 + lane + 32 * i;
+                    w[q][i][0] = w[q][i][1] = make_int4(0, 0, 0, 0);
+                    dw[q][i] = 0.0f;
+                    if (e < E && b < nb) {
+                        const int8_t* wr = rq + (size_t)e * H + (size_t)b * 32;
+                        w[q][i][0] = __ldg(reinterpret_cast<const int4*>(wr));
+                        w[q][i][1] = __ldg(reinterpret_cast<const int4*>(wr + 16));
+                        dw[q][i] = h2f(__ldg(rd + (size_t)e * nb + b));
+                    }
+                }
+#pragma unroll
+            for (int i = 0; i < 1; i++) {
+                const int b = b0 + lane + 32 * i;
+                if (b < nb) {
+                    const int4 x0 = *reinterpret_cast<const int4*>(sx + b * 32);
+                    const int4 x1 = *reinterpret_cast<const int4*>(sx + b * 32 + 16);
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+                        if (e0 + q < E)
+                            terms[q * ts + b] = __fmul_rn((float)dot32(w[q][i][0], w[q][i][1], x0, x1),
+                                                          __fmul_rn(dw[q][i], sdx[b]));
+                }
+            }
         }
         __syncwarp();
-        if (lane == 0) {
+        if (lane < 4 && e0 + lane < E) {
             float acc = 0.0f;
-            for (int b = 0; b < nb; b++) acc = __fadd_rn(acc, terms[b]);
-            lg[e] = acc;
+            for (int b = 0; b < nb; b++) acc = __fadd_rn(acc, terms[lane * ts + b]);
+            lg[e0 + lane] = acc;
         }
         __syncwarp();
     }
@@ -151,69 +175,91 @@ struct MoeLists {
 };
 
 // (expert parallelism: only experts [e_lo, e_hi) get lists; the other pairs keep slot -1)
+// Counts by shared-memory atomics, offsets and the active list by block-wide scans, then one
+// warp walks the pairs 32 at a time in pair order (= token order within every expert): a
+// pair's place is its expert's offset + the pairs already placed + its rank among the
+// warp's lanes holding the same expert.
 __global__ void __launch_bounds__(1024) moe_dispatch_kernel(const int32_t* __restrict__ ids_g, int rows, int E,
                                                             int top_k, MoeLists L, int e_lo, int e_hi) {
     __shared__ int cnt[MOE_MAX_E];
-    __shared__ int off[MOE_MAX_E + 1];
-    extern __shared__ int ids_sorted[];  // [rows][top_k] staged from global
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __shared__ int off[MOE_MAX_E];
+    __shared__ int placed[MOE_MAX_E];
+    __shared__ int wsum[32], wact[32];
+    extern __shared__ int ids_s[];  // [rows][top_k] staged from global
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int P = rows * top_k;
+    for (int e = tid; e < E; e += blockDim.x) {
+        cnt[e] = 0;
+        placed[e] = 0;
+    }
     pdl_wait();
     pdl_trigger();
-    for (int i = threadIdx.x; i < rows * top_k; i += blockDim.x) {
-        ids_sorted[i] = ids_g[i];
-        L.pair_slot[i] = -1;
+    __syncthreads();
+    for (int i = tid; i < P; i += blockDim.x) {
+        const int e = ids_g[i];
+        ids_s[i] = e;
+        if (e >= e_lo && e < e_hi) atomicAdd(&cnt[e], 1);
     }
     __syncthreads();
-    // pass 1: counts
-    for (int e = warp; e < E; e += 32) {
-        if (e < e_lo || e >= e_hi) {
-            if (lane == 0) cnt[e] = 0;
-            continue;
+    // exclusive scans of the counts and of the active flags (E <= 1024: one pass)
+    const int c = tid < E ? cnt[tid] : 0, a = c > 0;
+    int cs = c, as = a;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, cs, o), z = __shfl_up_sync(0xffffffffu, as, o);
+        if (lane >= o) {
+            cs += y;
+            as += z;
         }
-        int c = 0;
-        for (int t0 = 0; t0 < rows; t0 += 32) {
-            const int t = t0 + lane;
-            bool has = false;
-            if (t < rows)
-                for (int j = 0; j < top_k; j++) has |= ids_sorted[(size_t)t * top_k + j] == e;
-            c += __popc(__ballot_sync(0xffffffffu, has));
-        }
-        if (lane == 0) cnt[e] = c;
+    }
+    if (lane == 31) {
+        wsum[warp] = cs;
+        wact[warp] = as;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int s = 0, na = 0;
-        for (int e = 0; e < E; e++) {
-            off[e] = s;
-            s += cnt[e];
-            if (cnt[e] > 0) L.active[na++] = e;
-        }
-        off[E] = s;
-        L.active[E] = na;
-    }
-    __syncthreads();
-    for (int e = threadIdx.x; e < E; e += blockDim.x) {
-        L.counts[e] = cnt[e];
-        L.offsets[e] = off[e];
-    }
-    if (threadIdx.x == 0) L.offsets[E] = off[E];
-    // pass 2: fill in token order
-    for (int e = e_lo + warp; e < e_hi; e += 32) {
-        int pos = off[e];
-        for (int t0 = 0; t0 < rows; t0 += 32) {
-            const int t = t0 + lane;
-            int jj = -1;
-            if (t < rows)
-                for (int j = 0; j < top_k; j++)
-                    if (ids_sorted[(size_t)t * top_k + j] == e) jj = j;
-            const unsigned m = __ballot_sync(0xffffffffu, jj >= 0);
-            if (jj >= 0) {
-                const int p = pos + __popc(m & ((1u << lane) - 1u));
-                L.pair_token[p] = t;
-                L.pair_slot[(size_t)t * top_k + jj] = p;
+    if (warp == 0) {
+        int ws = wsum[lane], wa = wact[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, ws, o), z = __shfl_up_sync(0xffffffffu, wa, o);
+            if (lane >= o) {
+                ws += y;
+                wa += z;
             }
-            pos += __popc(m);
         }
+        wsum[lane] = ws - wsum[lane];  // exclusive
+        wact[lane] = wa - wact[lane];
+        if (lane == 31) {
+            L.offsets[E] = ws;
+            L.active[E] = wa;
+        }
+    }
+    __syncthreads();
+    if (tid < E) {
+        const int ex = wsum[warp] + cs - c;
+        off[tid] = ex;
+        L.offsets[tid] = ex;
+        L.counts[tid] = c;
+        if (a) L.active[wact[warp] + as - 1] = tid;
+    }
+    __syncthreads();
+    if (warp != 0) return;
+    for (int i0 = 0; i0 < P; i0 += 32) {
+        const int i = i0 + lane;
+        const int e = i < P ? ids_s[i] : -1;
+        const bool loc = e >= e_lo && e < e_hi;
+        const unsigned peers = __match_any_sync(0xffffffffu, loc ? e : -1 - lane);
+        const unsigned below = peers & ((1u << lane) - 1u);
+        if (loc) {
+            const int pos = off[e] + placed[e] + __popc(below);
+            L.pair_token[pos] = i / top_k;
+            L.pair_slot[i] = pos;
+        } else if (i < P) {
+            L.pair_slot[i] = -1;
+        }
+        __syncwarp();
+        if (loc && below == 0) placed[e] += __popc(peers);
+        __syncwarp();
     }
 }
 
@@ -481,19 +527,39 @@ __global__ void __launch_bounds__(ME_THREADS) moe_mma_kernel(const __grid_consta
 __global__ void moe_combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ pair_slot,
                                    const float* __restrict__ w_sorted, int top_k, int H, const float* resid,
                                    float* out) {
-    const int t = blockIdx.x;
+    // grid (H / 1024 column blocks, tokens); thread -> 4 columns, all the token's pairs in flight
+    __shared__ int sp[MOE_MAX_K];
+    __shared__ float sw[MOE_MAX_K];
+    const int t = blockIdx.y;
     pdl_wait();
     pdl_trigger();
-    for (int c = threadIdx.x; c < H; c += blockDim.x) {
-        float acc = 0.0f;
-        for (int jj = 0; jj < top_k; jj++) {
-            const int pr = pair_slot[(size_t)t * top_k + jj];
-            if (pr < 0) continue;  // an expert of another rank
-            acc = __fadd_rn(acc, __fmul_rn(w_sorted[(size_t)t * top_k + jj], y[(size_t)pr * H + c]));
-        }
-        const size_t o = (size_t)t * H + c;
-        out[o] = resid ? __fadd_rn(resid[o], acc) : acc;
+    if (threadIdx.x < top_k) {
+        sp[threadIdx.x] = pair_slot[(size_t)t * top_k + threadIdx.x];
+        sw[threadIdx.x] = w_sorted[(size_t)t * top_k + threadIdx.x];
     }
+    __syncthreads();
+    const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (c >= H) return;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int jj = 0; jj < top_k; jj++) {
+        const int pr = sp[jj];
+        if (pr < 0) continue;  // an expert of another rank
+        const float w = sw[jj];
+        const float4 v = *reinterpret_cast<const float4*>(y + (size_t)pr * H + c);
+        acc.x = __fadd_rn(acc.x, __fmul_rn(w, v.x));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(w, v.y));
+        acc.z = __fadd_rn(acc.z, __fmul_rn(w, v.z));
+        acc.w = __fadd_rn(acc.w, __fmul_rn(w, v.w));
+    }
+    const size_t o = (size_t)t * H + c;
+    if (resid) {
+        const float4 r = *reinterpret_cast<const float4*>(resid + o);
+        acc.x = __fadd_rn(r.x, acc.x);
+        acc.y = __fadd_rn(r.y, acc.y);
+        acc.z = __fadd_rn(r.z, acc.z);
+        acc.w = __fadd_rn(r.w, acc.w);
+    }
+    *reinterpret_cast<float4*>(out + o) = acc;
 }
 
 // ---------------------------------------------------------------------------------------
@@ -573,7 +639,15 @@ int launch_moe(lq_ctx* ctx, const lq_q8_tensor* router, const lq_q8_tensor* gate
 
     const int route_threads = (int)std::min<int64_t>(1024, std::max<int64_t>(128, E * 8));
     const size_t route_smem = (size_t)H + (size_t)(H / 32) * 4 + (size_t)E * 8 +
-                              (size_t)(route_threads / 32) * (size_t)(H / 32) * 4;
+                              (size_t)(route_threads / 32) * 4 * (size_t)(H / 32 + 1) * 4;
+    if (route_smem > 48 * 1024) {
+        static bool rattr[64] = {};
+        if (ctx->device < 0 || ctx->device >= 64 || !rattr[ctx->device]) {
+            LQ_CUDA(ctx, cudaFuncSetAttribute(moe_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              200 * 1024));
+            if (ctx->device >= 0 && ctx->device < 64) rattr[ctx->device] = true;
+        }
+    }
     int rc = launch_kernel(ctx, moe_route_kernel, dim3((unsigned)rows), dim3(route_threads), route_smem, "moe_route",
                            xq, xd, (int)H, router->qs, router->d, (int)E, (int)top_k, norm_topk,
                            ids_out ? ids_out : ids, w_out ? w_out : wts, ids_sorted, w_sorted);
@@ -617,7 +691,8 @@ int launch_moe(lq_ctx* ctx, const lq_q8_tensor* router, const lq_q8_tensor* gate
     p.y = y;
     rc = launch_moe_stream<false>(ctx, p, down->qs, down->d, down->n);
     if (rc) return rc;
-    return launch_kernel(ctx, moe_combine_kernel, dim3((unsigned)rows), dim3(256), 0, "moe_combine", (const float*)y,
+    return launch_kernel(ctx, moe_combine_kernel, dim3((unsigned)ceil_div(H, 1024), (unsigned)rows), dim3(256), 0,
+                         "moe_combine", (const float*)y,
                          (const int32_t*)L.pair_slot, (const float*)w_sorted, (int)top_k, (int)H, resid, out);
 }
 
@@ -640,6 +715,8 @@ extern "C" int lq_moe_forward(lq_ctx* ctx, const lq_q8_tensor* router, const lq_
     LQ_REQUIRE(ctx, rows >= 0 && rows * top_k <= 49152, "lq_moe_forward: rows * top_k must be at most 49152");
     if (rows == 0) return LQ_OK;
     LQ_REQUIRE(ctx, xq && xd && out, "lq_moe_forward: NULL activation");
+    LQ_REQUIRE(ctx, ((uintptr_t)out & 15) == 0 && ((uintptr_t)residual & 15) == 0,
+               "lq_moe_forward: out and residual must be 16-byte aligned");
     const int rc = lq::ensure_scratch(ctx, lq::moe_scratch_bytes(rows, E, top_k, H, I));
     if (rc) return rc;
     return lq::launch_moe(ctx, router, &experts->gate_up, &experts->down, E, I, top_k, norm_topk, xq, xd, rows, H, out,
@@ -666,6 +743,8 @@ extern "C" int lq_moe_forward_ep(lq_ctx* ctx, lq_comm* comm, const lq_q8_tensor*
     LQ_REQUIRE(ctx, rows >= 0 && rows * top_k <= 49152, "lq_moe_forward_ep: rows * top_k must be at most 49152");
     if (rows == 0) return LQ_OK;
     LQ_REQUIRE(ctx, xq && xd && out, "lq_moe_forward_ep: NULL activation");
+    LQ_REQUIRE(ctx, ((uintptr_t)out & 15) == 0 && ((uintptr_t)residual & 15) == 0,
+               "lq_moe_forward_ep: out and residual must be 16-byte aligned");
     int rc = lq::ensure_scratch(ctx, lq::moe_scratch_bytes(rows, E, top_k, H, I));
     if (rc) return rc;
     // this rank's experts, the residual on rank 0 only, then the sum over ranks
