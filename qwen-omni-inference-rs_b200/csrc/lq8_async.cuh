@@ -42,6 +42,15 @@ __device__ __forceinline__ void mma_s8(int c[4], const uint32_t a[4], const uint
           "r"(0));
 }
 
+// D = A * B + bias (bias in all four s32 accumulators)
+__device__ __forceinline__ void mma_s8_bias(int c[4], const uint32_t a[4], const uint32_t b[2], int bias) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(bias));
+}
+
 // L2-coherent loads for data written by other CTAs of the same launch
 __device__ __forceinline__ float ld_cg(const float* p) { return __ldcg(p); }
 __device__ __forceinline__ float4 ld_cg4(const float4* p) { return __ldcg(p); }

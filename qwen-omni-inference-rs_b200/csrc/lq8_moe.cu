@@ -334,7 +334,7 @@ __device__ __forceinline__ float h2f_bits(uint32_t w, int hi) {
 // sa/sb (8 fp16 each) in registers; xb -> this thread's 8 bytes of token g's first block
 // (n-tile stride xstride), db -> the f32 scales of tokens 2t, 2t+1 of the first block.
 template <int NT>
-__device__ __forceinline__ void me_blocks(float (&acc)[2][4], const uint2 (&wa)[8], const uint2 (&wb)[8],
+__device__ __forceinline__ void me_blocks(float2 (&acc)[2][2], const uint2 (&wa)[8], const uint2 (&wb)[8],
                                           const uint4 sa, const uint4 sb, const int8_t* xb, int xstride,
                                           const float* db) {
 #pragma unroll
@@ -347,19 +347,26 @@ __device__ __forceinline__ void me_blocks(float (&acc)[2][4], const uint2 (&wa)[
         for (int n = 0; n < NT; n++) {
             const uint2 xv = *reinterpret_cast<const uint2*>(xb + n * xstride + j * 32);
             const uint32_t b[2] = {xv.x, xv.y};
+            // the MMA adds the dots to 0x4B400000 (1.5 * 2^23 as a float): |dot| <= 32*127*127 <
+            // 2^22, so the bits read as a float are 1.5 * 2^23 + dot exactly, and one subtraction
+            // gives (float)dot -- no int-to-float conversions
             int d[4];
-            mma_s8(d, a, b);
+            mma_s8_bias(d, a, b, 0x4B400000);
             const float2 dx = *reinterpret_cast<const float2*>(db + j * ME_TOK + 8 * n);
-            acc[n][0] = __fadd_rn(acc[n][0], __fmul_rn((float)d[0], __fmul_rn(dwa, dx.x)));
-            acc[n][1] = __fadd_rn(acc[n][1], __fmul_rn((float)d[1], __fmul_rn(dwa, dx.y)));
-            acc[n][2] = __fadd_rn(acc[n][2], __fmul_rn((float)d[2], __fmul_rn(dwb, dx.x)));
-            acc[n][3] = __fadd_rn(acc[n][3], __fmul_rn((float)d[3], __fmul_rn(dwb, dx.y)));
+            const float f0 = __fsub_rn(__int_as_float(d[0]), 12582912.0f);
+            const float f1 = __fsub_rn(__int_as_float(d[1]), 12582912.0f);
+            const float f2 = __fsub_rn(__int_as_float(d[2]), 12582912.0f);
+            const float f3 = __fsub_rn(__int_as_float(d[3]), 12582912.0f);
+            acc[n][0].x = __fadd_rn(acc[n][0].x, __fmul_rn(f0, __fmul_rn(dwa, dx.x)));
+            acc[n][0].y = __fadd_rn(acc[n][0].y, __fmul_rn(f1, __fmul_rn(dwa, dx.y)));
+            acc[n][1].x = __fadd_rn(acc[n][1].x, __fmul_rn(f2, __fmul_rn(dwb, dx.x)));
+            acc[n][1].y = __fadd_rn(acc[n][1].y, __fmul_rn(f3, __fmul_rn(dwb, dx.y)));
         }
     }
 }
 
 template <bool GU>
-__global__ void __launch_bounds__(ME_THREADS) moe_mma_kernel(const __grid_constant__ CUtensorMap mw,
+__global__ void __launch_bounds__(ME_THREADS, 2) moe_mma_kernel(const __grid_constant__ CUtensorMap mw,
                                                              const __grid_constant__ CUtensorMap md,
                                                              const MoeExpertParams p) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -392,10 +399,14 @@ __global__ void __launch_bounds__(ME_THREADS) moe_mma_kernel(const __grid_consta
         // ---------------- producer (one lane) ----------------
         if (lane != 0) return;
         int it = 0;
+        int ai = -1, e = 0, passes = 0;
         for (long long item = i0; item < i1; item++) {
-            const int e = p.active[item / tiles];
+            if (item / tiles != ai) {  // consecutive items mostly share the expert
+                ai = (int)(item / tiles);
+                e = p.active[ai];
+                passes = (p.counts[e] + ME_TOK - 1) / ME_TOK;
+            }
             const int r0 = (int)(item % tiles) * item_rows;
-            const int passes = (p.counts[e] + ME_TOK - 1) / ME_TOK;
             const int base = (e - p.e_base) * p.rows_per_expert;
             for (int ps = 0; ps < passes; ps++)
                 for (int c = 0; c < nchunks; c++, it++) {
@@ -425,10 +436,15 @@ __global__ void __launch_bounds__(ME_THREADS) moe_mma_kernel(const __grid_consta
     const int sc_off = ME_W_BYTES + q * ME_GRP * 16 + ra * 16;
     int it = 0, cur_e = -1, cur_g0 = -1;
     bool bad = false;
+    int ai = -1, e = 0, cnt = 0, p0 = 0;
     for (long long item = i0; item < i1; item++) {
-        const int e = p.active[item / tiles];
+        if (item / tiles != ai) {
+            ai = (int)(item / tiles);
+            e = p.active[ai];
+            cnt = p.counts[e];
+            p0 = p.offsets[e];
+        }
         const int r0 = (int)(item % tiles) * item_rows;
-        const int cnt = p.counts[e], p0 = p.offsets[e];
         for (int g0 = 0; g0 < cnt; g0 += ME_TOK) {
             const int ng = min(ME_TOK, cnt - g0);
             if (e != cur_e || g0 != cur_g0) {
@@ -450,11 +466,9 @@ __global__ void __launch_bounds__(ME_THREADS) moe_mma_kernel(const __grid_consta
                 cur_g0 = g0;
             }
             const bool two = ng > 8;  // second n8 tile (warp-uniform)
-            float acc[2][4];
+            float2 acc[2][2];  // [n-tile][row ra, ra + 8] x tokens (2t, 2t + 1)
 #pragma unroll
-            for (int n = 0; n < 2; n++)
-#pragma unroll
-                for (int v = 0; v < 4; v++) acc[n][v] = 0.0f;
+            for (int n = 0; n < 2; n++) acc[n][0] = acc[n][1] = make_float2(0.0f, 0.0f);
             for (int c = 0; c < nchunks; c++, it++) {
                 const int s = it % S;
                 if (!bad) {
@@ -487,13 +501,14 @@ __global__ void __launch_bounds__(ME_THREADS) moe_mma_kernel(const __grid_consta
                 if (two) me_blocks<2>(acc, wa, wb, sa, sb, xb, 8 * XS, db);
                 else me_blocks<1>(acc, wa, wb, sa, sb, xb, 8 * XS, db);
             }
-            // epilogue: accumulator v of n-tile n is (row ra + 8 (v >> 1), token 8n + 2t + (v & 1))
+            // epilogue: value v of n-tile n is (row ra + 8 (v >> 1), token 8n + 2t + (v & 1))
             if (GU) {
 #pragma unroll
                 for (int n = 0; n < 2; n++)
 #pragma unroll
                     for (int v = 0; v < 4; v++)
-                        xch[(q * ME_TOK + 8 * n + 2 * t + (v & 1)) * ME_XCH + ra + 8 * (v >> 1)] = acc[n][v];
+                        xch[(q * ME_TOK + 8 * n + 2 * t + (v & 1)) * ME_XCH + ra + 8 * (v >> 1)] =
+                            (v & 1) ? acc[n][v >> 1].y : acc[n][v >> 1].x;
                 group_sync<ME_CONSUMERS * 32, 1>();
                 if (!bad)
                     for (int tk = warp; tk < ng; tk += ME_CONSUMERS) {
@@ -514,7 +529,9 @@ __global__ void __launch_bounds__(ME_THREADS) moe_mma_kernel(const __grid_consta
 #pragma unroll
                     for (int v = 0; v < 4; v++) {
                         const int tk = 8 * n + 2 * t + (v & 1);
-                        if (tk < ng) p.y[(size_t)(p0 + g0 + tk) * p.out_rows + row + 8 * (v >> 1)] = acc[n][v];
+                        if (tk < ng)
+                            p.y[(size_t)(p0 + g0 + tk) * p.out_rows + row + 8 * (v >> 1)] =
+                                (v & 1) ? acc[n][v >> 1].y : acc[n][v >> 1].x;
                     }
             }
         }
