@@ -83,6 +83,16 @@ struct AttParams {
     uint16_t* xd;
 };
 
+// two-lane fused multiply-add (sm_100 packed f32x2): (a.x*b.x + c.x, a.y*b.y + c.y)
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+    float2 r;
+    asm("{\n .reg .b64 ra, rb, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+        " mov.b64 rc, {%6, %7};\n fma.rn.f32x2 rd, ra, rb, rc;\n mov.b64 {%0, %1}, rd;\n}"
+        : "=f"(r.x), "=f"(r.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return r;
+}
+
 __device__ __forceinline__ void quant_warp32(float v, int lane, int8_t* q_out, uint16_t* d_out) {
     float amax = warp_max(fabsf(v));
     float d, id;
@@ -103,8 +113,9 @@ __device__ __forceinline__ void attn_chunk_fma(AttSmemR& S, int G, int cnt, floa
     {
         const int pp = tid >> 1, hf = tid & 1;
         float s[GN];
+        float2 s2[GN];  // even and odd dims apart (two-lane fused multiply-add)
 #pragma unroll
-        for (int g = 0; g < GN; g++) s[g] = 0.0f;
+        for (int g = 0; g < GN; g++) s2[g] = make_float2(0.0f, 0.0f);
         if (pp < cnt) {
             const float* kr = &S.ks[pp][hf * (ATT_D / 2)];
             const float* qr = &S.qp[0][hf * (ATT_D / 2 + 4)];
@@ -115,16 +126,17 @@ __device__ __forceinline__ void attn_chunk_fma(AttSmemR& S, int G, int cnt, floa
                 for (int g = 0; g < GN; g++) {
                     if (g < G) {
                         const float4 q4 = *reinterpret_cast<const float4*>(qr + g * ATT_KS + 4 * d4);
-                        s[g] = fmaf(q4.x, k4.x, s[g]);
-                        s[g] = fmaf(q4.y, k4.y, s[g]);
-                        s[g] = fmaf(q4.z, k4.z, s[g]);
-                        s[g] = fmaf(q4.w, k4.w, s[g]);
+                        s2[g] = fma2(make_float2(q4.x, q4.y), make_float2(k4.x, k4.y), s2[g]);
+                        s2[g] = fma2(make_float2(q4.z, q4.w), make_float2(k4.z, k4.w), s2[g]);
                     }
                 }
             }
         }
 #pragma unroll
-        for (int g = 0; g < GN; g++) s[g] = __fadd_rn(s[g], __shfl_xor_sync(0xffffffffu, s[g], 1));
+        for (int g = 0; g < GN; g++) {
+            s[g] = __fadd_rn(s2[g].x, s2[g].y);
+            s[g] = __fadd_rn(s[g], __shfl_xor_sync(0xffffffffu, s[g], 1));
+        }
         // half 0 stores heads 0..3, half 1 heads 4..7
 #pragma unroll
         for (int i = 0; i < 4; i++) {
@@ -149,18 +161,25 @@ __device__ __forceinline__ void attn_chunk_fma(AttSmemR& S, int G, int cnt, floa
     {
         const int d = tid;
         float acc[GN];
+        constexpr int GP = (GN + 1) / 2;  // head pairs (two-lane fused multiply-add)
+        float2 a2[GP];
 #pragma unroll
-        for (int g = 0; g < GN; g++) acc[g] = 0.0f;
+        for (int i = 0; i < GP; i++) a2[i] = make_float2(0.0f, 0.0f);
 #pragma unroll 4
         for (int j = 0; j < cnt; j++) {
             const float vv = S.vs[j][d];
+            const float2 v2 = make_float2(vv, vv);
             const float4 pa = *reinterpret_cast<const float4*>(&S.pt[j][0]);
-            float4 pb = pa;
-            if constexpr (GN > 4) pb = *reinterpret_cast<const float4*>(&S.pt[j][4]);
-            const float pj[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
-#pragma unroll
-            for (int g = 0; g < GN; g++) acc[g] = fmaf(pj[g], vv, acc[g]);
+            a2[0] = fma2(make_float2(pa.x, pa.y), v2, a2[0]);
+            if constexpr (GN > 2) a2[1] = fma2(make_float2(pa.z, pa.w), v2, a2[1]);
+            if constexpr (GN > 4) {
+                const float4 pb = *reinterpret_cast<const float4*>(&S.pt[j][4]);
+                a2[2] = fma2(make_float2(pb.x, pb.y), v2, a2[2]);
+                a2[3] = fma2(make_float2(pb.z, pb.w), v2, a2[3]);
+            }
         }
+#pragma unroll
+        for (int g = 0; g < GN; g++) acc[g] = (g & 1) ? a2[g >> 1].y : a2[g >> 1].x;
 #pragma unroll
         for (int g = 0; g < GN; g++)
             if (g < G) p.part_o[(hbase + (int64_t)g * nsplit) * ATT_D + d] = acc[g];
