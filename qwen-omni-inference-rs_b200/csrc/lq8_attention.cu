@@ -335,6 +335,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const AttParams
         }
     }
     }
+    // unfused: attn_merge_kernel, launched next, merges the chunks
+    if constexpr (!FUSED) return;
     // the last chunk CTA of this (row, kv head) merges the chunks
     __threadfence();
     __syncthreads();
@@ -407,6 +409,53 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const AttParams
     if (tid == 0) p.counters[lrow * Hkv + kvh] = 0;  // ready for the next launch
 }
 
+// the unfused path's merge: one CTA per (kv head, query row) rescales its chunks' partials by
+// exp(m_s - M), adds them in chunk order and divides by the summed denominators (the same
+// arithmetic as the fused kernel's last-CTA merge). A kernel of its own, so that the chunk
+// CTAs end without a fence and an atomic.
+__global__ void __launch_bounds__(256, 4) attn_merge_kernel(const AttParams p) {
+    __shared__ float cm[ATT_G][ATT_MAX_SPLITS];
+    __shared__ float cl[ATT_G];
+    const int Hq = p.Hq, Hkv = p.Hkv, L = p.L, nsplit = p.nsplit, G = Hq / Hkv;
+    const int kvh = blockIdx.x, lrow = blockIdx.y;
+    const int row = p.row0 + lrow, l = row % L;
+    pdl_wait();
+    pdl_trigger();
+    const int p0 = p.pos0_dev ? *p.pos0_dev : p.pos0;
+    const int limit = p0 + l;
+    if (limit < 0 || limit >= p.ctx_max) return;
+    const int n_active = min(limit / ATT_C + 1, nsplit);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t hbase0 = ((int64_t)lrow * Hq + (int64_t)kvh * G) * nsplit;
+    if (warp < G) {
+        const int g = warp;
+        const float* ml = p.part_ml + (hbase0 + (int64_t)g * nsplit) * 2;
+        float m = -INFINITY;
+        for (int s = lane; s < n_active; s += 32) m = fmaxf(m, ml[2 * s]);
+        m = warp_max(m);
+        float lsum = 0.0f;
+        for (int s = lane; s < n_active; s += 32) {
+            const float w = expf(__fsub_rn(ml[2 * s], m));
+            cm[g][s] = w;
+            lsum = __fadd_rn(lsum, __fmul_rn(w, ml[2 * s + 1]));
+        }
+        lsum = warp_sum(lsum);
+        if (lane == 0) cl[g] = lsum;
+    }
+    __syncthreads();
+    const int d = tid & (ATT_D - 1), hh = tid >> 7;
+    for (int g = hh; g < G; g += 2) {
+        const float* po = p.part_o + (hbase0 + (int64_t)g * nsplit) * ATT_D + d;
+        float o = 0.0f;
+#pragma unroll 8
+        for (int s = 0; s < n_active; s++) o = __fadd_rn(o, __fmul_rn(cm[g][s], po[(int64_t)s * ATT_D]));
+        o = __fdiv_rn(o, cl[g]);
+        const int64_t e = (int64_t)row * Hq * ATT_D + (int64_t)(kvh * G + g) * ATT_D + d;
+        if (p.out) p.out[e] = o;
+        if (p.xq) quant_warp32(o, lane, p.xq + (e - lane), p.xd + (e >> 5));
+    }
+}
+
 int attention_max_ctx() { return ATT_C * ATT_MAX_SPLITS; }
 
 size_t attention_scratch_bytes(int64_t rows, int64_t Hq, int64_t ctx_max, int64_t D) {
@@ -437,9 +486,14 @@ static int launch_chunks(lq_ctx* ctx, AttParams p, int64_t rows, void* scratch, 
         const int64_t n = std::min(slice, rows - r0);
         p.row0 = (int)r0;
         const dim3 grid(p.nsplit, (unsigned)p.Hkv, (unsigned)n);
-        const int rc = launch_kernel(ctx, attn_chunk_kernel<FUSED, GT>, grid, dim3(ATT_THREADS), sizeof(Smem),
-                                     "attn_chunk", p);
+        int rc = launch_kernel(ctx, attn_chunk_kernel<FUSED, GT>, grid, dim3(ATT_THREADS), sizeof(Smem),
+                               "attn_chunk", p);
         if (rc) return rc;
+        if (!FUSED) {
+            rc = launch_kernel(ctx, attn_merge_kernel, dim3((unsigned)p.Hkv, (unsigned)n), dim3(256), 0,
+                               "attn_merge", p);
+            if (rc) return rc;
+        }
     }
     return LQ_OK;
 }
