@@ -195,6 +195,30 @@ def test_matmul_residual_and_stride(ctx, lq8_lib, oracle, rng, monkeypatch, m):
         assert np.array_equal(y[:, :n], (resid[:, :n] + ref).astype(np.float32))
 
 
+@pytest.mark.parametrize("m", [5, 16, 40, 64])
+@pytest.mark.parametrize("split", [False, True])
+def test_gemm_stream_residual_and_stride(ctx, lq8_lib, oracle, rng, monkeypatch, m, split):
+    """The streamed small-M GEMM (5 <= m <= 64, n % 64 == 0, k % 256 == 0): passes of 16
+    tokens with a ragged last pass, y = residual + W.x into a wider row stride, columns past n
+    untouched. Unsplit it is bit-identical to the oracle; with K slices (a 5-tile grid) within
+    the regrouping bound and deterministic."""
+    if not split:
+        monkeypatch.setenv("LQ_GEMM_NO_SPLIT", "1")
+    n, k, ldy = 320, 2048, 384
+    wq, wd = _weights(oracle, rng, n, k)
+    xq, xd = oracle.q8_0_quantize(rng.standard_normal((m, k)).astype(np.float32))
+    resid = rng.standard_normal((m, ldy)).astype(np.float32)
+    y = _matmul(ctx, lq8_lib, wq, wd, xq, xd, resid=resid, ldy=ldy)
+    ref, absum = oracle.q8_0_matmul(xq, xd, wq, wd, with_abs=True)
+    assert np.array_equal(y[:, n:], resid[:, n:])
+    if not split:
+        assert np.array_equal(y[:, :n], (resid[:, :n] + ref).astype(np.float32))
+    else:
+        bound = 2.0 * (k // 32 + 1) * 2.0 ** -24 * absum + 1e-30 + 2.0 ** -23 * np.abs(resid[:, :n] + ref)
+        assert np.all(np.abs(y[:, :n] - (resid[:, :n] + ref)) <= bound)
+        assert np.array_equal(y, _matmul(ctx, lq8_lib, wq, wd, xq, xd, resid=resid, ldy=ldy))
+
+
 @pytest.mark.parametrize("m", [1, 3, 12])
 @pytest.mark.parametrize("src", ["f32", "bf16"])
 def test_linear_forward(ctx, lq8_lib, oracle, rng, m, src):
