@@ -465,7 +465,7 @@ size_t gemm_split_bytes(lq_ctx* ctx, int64_t n, int64_t k, int64_t m) {
     // the streamed GEMM's slices when the shape qualifies (its alignment is checked per call, so
     // the mma.sync GEMM's need counts too)
     size_t gs = 0;
-    if (k % 256 == 0 && n % 64 == 0) {
+    if (m <= 32 && k % 256 == 0 && n % 64 == 0) {
         const int s0 = gs_slices(ctx, n, k, m);
         const int64_t chunks = k / 256, ks = ((chunks + s0 - 1) / s0) * 256;
         if (s0 > 1) gs = (size_t)((k + ks - 1) / ks) * m * n * 4;
@@ -530,7 +530,7 @@ static int gemv_rows(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const
 }
 
 // =========================================================================================
-// Small-M Q8_0 GEMM, streamed (5 <= m <= 64 tokens): the MoE expert kernel's pipeline for a
+// Small-M Q8_0 GEMM, streamed (5 <= m <= 32 tokens): the MoE expert kernel's pipeline for a
 // dense weight. Work item = (64 weight rows, K slice, pass of up to 16 tokens); one producer
 // lane streams per 256-byte K-chunk the item's weight rows (two 32-row groups x two
 // 128-byte boxes, 128-byte swizzle), their fp16 scales, the pass's 16 token rows of the
@@ -762,7 +762,7 @@ static int gs_slices(lq_ctx* ctx, int64_t n, int64_t k, int64_t m) {
 }
 
 static bool gs_supported(const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd, int64_t m) {
-    return m >= 5 && m <= 64 && w->k % GS_KC == 0 && w->n % 64 == 0 && w->n < (1ll << 31) &&
+    return m >= 5 && m <= 32 && w->k % GS_KC == 0 && w->n % 64 == 0 && w->n < (1ll << 31) &&
            ((uintptr_t)w->qs % 16) == 0 && ((uintptr_t)w->d % 16) == 0 && ((uintptr_t)xq % 16) == 0 &&
            ((uintptr_t)xd % 16) == 0 && !getenv("LQ_NO_GEMM_STREAM");
 }
