@@ -23,6 +23,8 @@
 #include "lq8_internal.cuh"
 #include "lq8_tma.cuh"
 
+#include <cstdlib>
+
 namespace lq {
 
 constexpr int MOE_MAX_E = 512;
@@ -172,6 +174,7 @@ struct MoeLists {
     int32_t* active;       // [E] active expert ids (ascending), then n_active at active[E]
     int32_t* pair_token;   // [rows*k] token of each pair, grouped by expert, tokens ascending
     int32_t* pair_slot;    // [rows][k] pair index of the token's jj-th expert (ascending expert)
+    int32_t* cum;          // [E+1] passes of the active experts before active index a (prefix)
 };
 
 // (expert parallelism: only experts [e_lo, e_hi) get lists; the other pairs keep slot -1)
@@ -180,11 +183,11 @@ struct MoeLists {
 // pair's place is its expert's offset + the pairs already placed + its rank among the
 // warp's lanes holding the same expert.
 __global__ void __launch_bounds__(1024) moe_dispatch_kernel(const int32_t* __restrict__ ids_g, int rows, int E,
-                                                            int top_k, MoeLists L, int e_lo, int e_hi) {
+                                                            int top_k, MoeLists L, int e_lo, int e_hi, int tok) {
     __shared__ int cnt[MOE_MAX_E];
     __shared__ int off[MOE_MAX_E];
     __shared__ int placed[MOE_MAX_E];
-    __shared__ int wsum[32], wact[32];
+    __shared__ int wsum[32], wact[32], wpas[32];
     extern __shared__ int ids_s[];  // [rows][top_k] staged from global
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int P = rows * top_k;
@@ -201,37 +204,45 @@ __global__ void __launch_bounds__(1024) moe_dispatch_kernel(const int32_t* __res
         if (e >= e_lo && e < e_hi) atomicAdd(&cnt[e], 1);
     }
     __syncthreads();
-    // exclusive scans of the counts and of the active flags (E <= 1024: one pass)
-    const int c = tid < E ? cnt[tid] : 0, a = c > 0;
-    int cs = c, as = a;
+    // exclusive scans of the counts, of the active flags and of the experts' passes of `tok`
+    // tokens (E <= 1024: one pass)
+    const int c = tid < E ? cnt[tid] : 0, a = c > 0, pc = (c + tok - 1) / tok;
+    int cs = c, as = a, ps = pc;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
         const int y = __shfl_up_sync(0xffffffffu, cs, o), z = __shfl_up_sync(0xffffffffu, as, o);
+        const int w = __shfl_up_sync(0xffffffffu, ps, o);
         if (lane >= o) {
             cs += y;
             as += z;
+            ps += w;
         }
     }
     if (lane == 31) {
         wsum[warp] = cs;
         wact[warp] = as;
+        wpas[warp] = ps;
     }
     __syncthreads();
     if (warp == 0) {
-        int ws = wsum[lane], wa = wact[lane];
+        int ws = wsum[lane], wa = wact[lane], wp = wpas[lane];
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const int y = __shfl_up_sync(0xffffffffu, ws, o), z = __shfl_up_sync(0xffffffffu, wa, o);
+            const int w = __shfl_up_sync(0xffffffffu, wp, o);
             if (lane >= o) {
                 ws += y;
                 wa += z;
+                wp += w;
             }
         }
         wsum[lane] = ws - wsum[lane];  // exclusive
         wact[lane] = wa - wact[lane];
+        wpas[lane] = wp - wpas[lane];
         if (lane == 31) {
             L.offsets[E] = ws;
             L.active[E] = wa;
+            L.cum[wa] = wp;
         }
     }
     __syncthreads();
@@ -240,7 +251,10 @@ __global__ void __launch_bounds__(1024) moe_dispatch_kernel(const int32_t* __res
         off[tid] = ex;
         L.offsets[tid] = ex;
         L.counts[tid] = c;
-        if (a) L.active[wact[warp] + as - 1] = tid;
+        if (a) {
+            L.active[wact[warp] + as - 1] = tid;
+            L.cum[wact[warp] + as - 1] = wpas[warp] + ps - pc;
+        }
     }
     __syncthreads();
     if (warp != 0) return;
@@ -266,15 +280,19 @@ __global__ void __launch_bounds__(1024) moe_dispatch_kernel(const int32_t* __res
 // ---------------------------------------------------------------------------------------
 // grouped expert GEMV on the int8 tensor cores (mma.sync m16n8k32, s8 x s8 -> s32)
 //
-// Work item = (active expert, a tile of output rows): gate/up streams 32 gate rows and the
-// 32 matching up rows (32 rows of h), down streams 64 rows of the down projection -- 64
-// weight rows either way. Each CTA takes a contiguous range of items, so consecutive items
-// mostly share the expert and its activations stay in shared memory. One producer lane
-// streams the item's rows in K-chunks of 256 bytes (8 Q8_0 blocks) into a shared-memory ring
-// with 2-D TMA loads: per 32-row group two 128-byte-wide boxes (128-byte swizzle) and one box
-// of the chunk's fp16 scales, 17 KiB per stage. Consumer warp w owns stage rows 16w..16w+15
-// (one m16 tile) and the pass's tokens as up to two n8 tiles (16 tokens per pass; more
-// tokens take more passes over the weights). One MMA covers one Q8_0 block of 16 rows x 8
+// Work unit = (active expert, a tile of output rows, a pass of up to TOK of the expert's
+// tokens): gate/up streams 32 gate rows and the 32 matching up rows (32 rows of h), down
+// streams 64 rows of the down projection -- 64 weight rows either way. Units are ordered by
+// expert, tile, pass (the dispatch writes each active expert's pass count as a prefix), and
+// each CTA takes an equal contiguous range of them: consecutive units mostly share the
+// expert, so its activations stay in shared memory, and an expert with many tokens spreads
+// over more CTAs (with routing skewed towards a few experts, item ranges would leave the
+// CTAs holding them last). Passes of one tile follow each other, so the later passes read
+// the weights from L2. One producer lane streams the unit's rows in K-chunks of 256 bytes (8
+// Q8_0 blocks) into a shared-memory ring with 2-D TMA loads: per 32-row group two
+// 128-byte-wide boxes (128-byte swizzle) and one box of the chunk's fp16 scales, 17 KiB per
+// stage. Consumer warp w owns stage rows 16w..16w+15 (one m16 tile) and the pass's tokens as
+// one or two n8 tiles. One MMA covers one Q8_0 block of 16 rows x 8
 // tokens; its int32 dots are scaled per block and added to f32 accumulators that each thread
 // keeps for fixed (row, token) pairs, in ascending block order with separately rounded
 // multiply and add: the oracle's order, so every output is bit-identical to it.
@@ -297,7 +315,7 @@ constexpr int ME_STAGE = ME_W_BYTES + 2 * ME_GRP * 16;  // + fp16 scales [64 row
 constexpr int ME_CONSUMERS = 4;
 constexpr int ME_THREADS = (ME_CONSUMERS + 1) * 32;
 constexpr int ME_MAX_STAGES = 8;
-constexpr int ME_TOK = 16;                            // tokens per pass (two n8 tiles)
+constexpr int ME_TOK = 16;                            // most tokens per pass (two n8 tiles)
 constexpr int ME_XCH = 33;                            // row stride (floats) of the gate/up exchange
 static_assert(ME_STAGE % 1024 == 0, "swizzled boxes need 1024-byte aligned stages");
 
@@ -312,6 +330,7 @@ struct MoeExpertParams {
     const int32_t* offsets;
     const int32_t* counts;
     const int32_t* active;   // [E] + n_active at [E]
+    const int32_t* cum;      // [n_active + 1] pass prefix over the active experts
     int E;
     int e_base;              // first expert held in the weight stack (expert parallelism)
     int8_t* hq;              // gate/up output [pairs][I]
@@ -321,9 +340,9 @@ struct MoeExpertParams {
 };
 
 // shared memory after the stages: barriers, the gate/up exchange, the pass's tokens
-__host__ __device__ constexpr size_t me_fixed_bytes(bool gu, int K) {
-    return (size_t)2 * ME_MAX_STAGES * 8 + (gu ? (size_t)2 * ME_TOK * ME_XCH * 4 : 0) +
-           (size_t)ME_TOK * (K + 16) + (size_t)(K / 32) * ME_TOK * 4;
+__host__ __device__ constexpr size_t me_fixed_bytes(bool gu, int K, int tok) {
+    return (size_t)2 * ME_MAX_STAGES * 8 + (gu ? (size_t)2 * tok * ME_XCH * 4 : 0) +
+           (size_t)tok * (K + 16) + (size_t)(K / 32) * tok * 4 + (size_t)(MOE_MAX_E + 4) * 4;
 }
 
 __device__ __forceinline__ float h2f_bits(uint32_t w, int hi) {
@@ -336,7 +355,7 @@ __device__ __forceinline__ float h2f_bits(uint32_t w, int hi) {
 template <int NT>
 __device__ __forceinline__ void me_blocks(float2 (&acc)[2][2], const uint2 (&wa)[8], const uint2 (&wb)[8],
                                           const uint4 sa, const uint4 sb, const int8_t* xb, int xstride,
-                                          const float* db) {
+                                          const float* db, int tok) {
 #pragma unroll
     for (int j = 0; j < 8; j++) {
         const uint32_t a[4] = {wa[j].x, wb[j].x, wa[j].y, wb[j].y};
@@ -352,7 +371,7 @@ __device__ __forceinline__ void me_blocks(float2 (&acc)[2][2], const uint2 (&wa)
             // gives (float)dot -- no int-to-float conversions
             int d[4];
             mma_s8_bias(d, a, b, 0x4B400000);
-            const float2 dx = *reinterpret_cast<const float2*>(db + j * ME_TOK + 8 * n);
+            const float2 dx = *reinterpret_cast<const float2*>(db + j * tok + 8 * n);
             const float f0 = __fsub_rn(__int_as_float(d[0]), 12582912.0f);
             const float f1 = __fsub_rn(__int_as_float(d[1]), 12582912.0f);
             const float f2 = __fsub_rn(__int_as_float(d[2]), 12582912.0f);
@@ -365,7 +384,10 @@ __device__ __forceinline__ void me_blocks(float2 (&acc)[2][2], const uint2 (&wa)
     }
 }
 
-template <bool GU>
+// TOK: tokens per pass (8: one n8 tile, a smaller activation buffer and three CTAs per SM,
+// for batches that give experts a few tokens each; 16: two tiles, for larger batches).
+// Measured at batch 64 (30B-A3B): the layer 143 us with 8, 162 us with 16.
+template <bool GU, int TOK>
 __global__ void __launch_bounds__(ME_THREADS, 2) moe_mma_kernel(const __grid_constant__ CUtensorMap mw,
                                                              const __grid_constant__ CUtensorMap md,
                                                              const MoeExpertParams p) {
@@ -375,9 +397,9 @@ __global__ void __launch_bounds__(ME_THREADS, 2) moe_mma_kernel(const __grid_con
     const int K = p.K, nb = K / 32, nchunks = K / ME_KC, S = p.stages, XS = K + 16;
     uint64_t* full = reinterpret_cast<uint64_t*>(sm + (size_t)S * ME_STAGE);
     uint64_t* empty = full + ME_MAX_STAGES;
-    float* xch = reinterpret_cast<float*>(empty + ME_MAX_STAGES);                 // [2][ME_TOK][ME_XCH]
-    int8_t* xs = reinterpret_cast<int8_t*>(xch + (GU ? 2 * ME_TOK * ME_XCH : 0));  // [ME_TOK][K + 16]
-    float* xdf = reinterpret_cast<float*>(xs + (size_t)ME_TOK * XS);               // [nb][ME_TOK]
+    float* xch = reinterpret_cast<float*>(empty + ME_MAX_STAGES);                 // [2][TOK][ME_XCH]
+    int8_t* xs = reinterpret_cast<int8_t*>(xch + (GU ? 2 * TOK * ME_XCH : 0));  // [TOK][K + 16]
+    float* xdf = reinterpret_cast<float*>(xs + (size_t)TOK * XS);               // [nb][TOK]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
@@ -386,30 +408,44 @@ __global__ void __launch_bounds__(ME_THREADS, 2) moe_mma_kernel(const __grid_con
         }
         mbar_fence_init();
     }
-    __syncthreads();
     pdl_wait();
     pdl_trigger();
+    // work units (active expert, row tile, pass of TOK tokens), ordered by expert, then tile,
+    // then pass; each CTA takes an equal contiguous range, so an expert with many tokens
+    // (several passes) spreads over more CTAs. The pass prefix is staged in shared memory.
+    int* scum = reinterpret_cast<int*>(xdf + (size_t)nb * TOK);  // [n_active + 1]
     const int n_active = p.active[p.E];
+    for (int i = threadIdx.x; i <= n_active; i += ME_THREADS) scum[i] = p.cum[i];
+    __syncthreads();
     const int item_rows = GU ? ME_GRP : 2 * ME_GRP;  // output rows per item
     const int tiles = p.out_rows / item_rows;
-    const long long items = (long long)n_active * tiles;
-    const long long i0 = items * blockIdx.x / gridDim.x, i1 = items * (blockIdx.x + 1) / gridDim.x;
+    const long long U = (long long)scum[n_active] * tiles;
+    const long long u0 = U * blockIdx.x / gridDim.x, u1 = U * (blockIdx.x + 1) / gridDim.x;
+    int a0 = 0;  // the active expert holding unit u0: the last a with cum[a] * tiles <= u0
+    if (u0 < u1) {
+        int hi = n_active - 1;
+        while (a0 < hi) {
+            const int mid = (a0 + hi + 1) >> 1;
+            if ((long long)scum[mid] * tiles <= u0) a0 = mid;
+            else hi = mid - 1;
+        }
+    }
 
     if (warp == ME_CONSUMERS) {
         // ---------------- producer (one lane) ----------------
         if (lane != 0) return;
         int it = 0;
-        int ai = -1, e = 0, passes = 0;
-        for (long long item = i0; item < i1; item++) {
-            if (item / tiles != ai) {  // consecutive items mostly share the expert
-                ai = (int)(item / tiles);
-                e = p.active[ai];
-                passes = (p.counts[e] + ME_TOK - 1) / ME_TOK;
+        int a = a0, cur_a = -1, e = 0;
+        for (long long u = u0; u < u1; u++) {
+            while (u >= (long long)scum[a + 1] * tiles) a++;
+            if (a != cur_a) {
+                cur_a = a;
+                e = p.active[a];
             }
-            const int r0 = (int)(item % tiles) * item_rows;
+            const int np = scum[a + 1] - scum[a];
+            const int r0 = (int)((u - (long long)scum[a] * tiles) / np) * item_rows;
             const int base = (e - p.e_base) * p.rows_per_expert;
-            for (int ps = 0; ps < passes; ps++)
-                for (int c = 0; c < nchunks; c++, it++) {
+            for (int c = 0; c < nchunks; c++, it++) {
                     const int s = it % S;
                     if (!mbar_wait(&empty[s], ((unsigned)(it / S) & 1u) ^ 1u)) {
                         atomicCAS(p.err, 0, 21);
@@ -436,17 +472,21 @@ __global__ void __launch_bounds__(ME_THREADS, 2) moe_mma_kernel(const __grid_con
     const int sc_off = ME_W_BYTES + q * ME_GRP * 16 + ra * 16;
     int it = 0, cur_e = -1, cur_g0 = -1;
     bool bad = false;
-    int ai = -1, e = 0, cnt = 0, p0 = 0;
-    for (long long item = i0; item < i1; item++) {
-        if (item / tiles != ai) {
-            ai = (int)(item / tiles);
-            e = p.active[ai];
+    int a = a0, cur_a = -1, e = 0, cnt = 0, p0 = 0;
+    for (long long u = u0; u < u1; u++) {
+        while (u >= (long long)scum[a + 1] * tiles) a++;
+        if (a != cur_a) {
+            cur_a = a;
+            e = p.active[a];
             cnt = p.counts[e];
             p0 = p.offsets[e];
         }
-        const int r0 = (int)(item % tiles) * item_rows;
-        for (int g0 = 0; g0 < cnt; g0 += ME_TOK) {
-            const int ng = min(ME_TOK, cnt - g0);
+        const int np = scum[a + 1] - scum[a];
+        const long long v = u - (long long)scum[a] * tiles;
+        const int r0 = (int)(v / np) * item_rows;
+        {
+            const int g0 = (int)(v % np) * TOK;
+            const int ng = min(TOK, cnt - g0);
             if (e != cur_e || g0 != cur_g0) {
                 group_sync<ME_CONSUMERS * 32, 1>();  // nobody still reads the previous tokens
                 for (int i = threadIdx.x; i < ng * (K / 16); i += ME_CONSUMERS * 32) {
@@ -458,7 +498,7 @@ __global__ void __launch_bounds__(ME_THREADS, 2) moe_mma_kernel(const __grid_con
                 for (int i = threadIdx.x; i < ng * nb; i += ME_CONSUMERS * 32) {
                     const int tk = i / nb, b = i % nb;
                     const int src = GU ? p.pair_token[p0 + g0 + tk] : p0 + g0 + tk;
-                    xdf[b * ME_TOK + tk] = h2f(p.xd[(size_t)src * nb + b]);
+                    xdf[b * TOK + tk] = h2f(p.xd[(size_t)src * nb + b]);
                 }
                 cp_async_wait<0>();
                 group_sync<ME_CONSUMERS * 32, 1>();
@@ -497,22 +537,22 @@ __global__ void __launch_bounds__(ME_THREADS, 2) moe_mma_kernel(const __grid_con
                 // straight-line code for the chunk's 8 blocks (the n8-tile count is decided
                 // once, outside), so loads and MMAs of different blocks can overlap
                 const int8_t* xb = xs + (size_t)g * XS + c * ME_KC + 8 * t;
-                const float* db = xdf + c * 8 * ME_TOK + 2 * t;
-                if (two) me_blocks<2>(acc, wa, wb, sa, sb, xb, 8 * XS, db);
-                else me_blocks<1>(acc, wa, wb, sa, sb, xb, 8 * XS, db);
+                const float* db = xdf + c * 8 * TOK + 2 * t;
+                if (TOK > 8 && two) me_blocks<2>(acc, wa, wb, sa, sb, xb, 8 * XS, db, TOK);
+                else me_blocks<1>(acc, wa, wb, sa, sb, xb, 8 * XS, db, TOK);
             }
             // epilogue: value v of n-tile n is (row ra + 8 (v >> 1), token 8n + 2t + (v & 1))
             if (GU) {
 #pragma unroll
-                for (int n = 0; n < 2; n++)
+                for (int n = 0; n < TOK / 8; n++)
 #pragma unroll
                     for (int v = 0; v < 4; v++)
-                        xch[(q * ME_TOK + 8 * n + 2 * t + (v & 1)) * ME_XCH + ra + 8 * (v >> 1)] =
+                        xch[(q * TOK + 8 * n + 2 * t + (v & 1)) * ME_XCH + ra + 8 * (v >> 1)] =
                             (v & 1) ? acc[n][v >> 1].y : acc[n][v >> 1].x;
                 group_sync<ME_CONSUMERS * 32, 1>();
                 if (!bad)
                     for (int tk = warp; tk < ng; tk += ME_CONSUMERS) {
-                        const float gv = xch[tk * ME_XCH + lane], uv = xch[(ME_TOK + tk) * ME_XCH + lane];
+                        const float gv = xch[tk * ME_XCH + lane], uv = xch[(TOK + tk) * ME_XCH + lane];
                         const float h = __fmul_rn(gv / (1.0f + expf(-gv)), uv);
                         const float amax = warp_max(fabsf(h));
                         float d, id;
@@ -525,7 +565,7 @@ __global__ void __launch_bounds__(ME_THREADS, 2) moe_mma_kernel(const __grid_con
             } else if (!bad) {
                 const int row = r0 + 32 * q + ra;
 #pragma unroll
-                for (int n = 0; n < 2; n++)
+                for (int n = 0; n < TOK / 8; n++)
 #pragma unroll
                     for (int v = 0; v < 4; v++) {
                         const int tk = 8 * n + 2 * t + (v & 1);
@@ -584,17 +624,19 @@ __global__ void moe_combine_kernel(const float* __restrict__ y, const int32_t* _
 // ---------------------------------------------------------------------------------------
 static size_t al256(size_t b) { return (b + 255) & ~(size_t)255; }
 
-template <bool GU>
+template <bool GU, int TOK>
 static int launch_moe_stream(lq_ctx* ctx, MoeExpertParams p, const int8_t* wq, const uint16_t* wd,
                              int64_t total_rows) {
-    // two CTAs per SM when their rings still hold three stages each, else one with a deeper ring
-    const size_t fixed = me_fixed_bytes(GU, p.K) + 1024 /*alignment*/;
-    const size_t pair_budget = 113 * 1024, solo_budget = 227 * 1024;
-    int per_sm = 2;
-    int stages = pair_budget > fixed ? (int)((pair_budget - fixed) / ME_STAGE) : 0;
-    if (stages < 3) {
-        per_sm = 1;
-        stages = solo_budget > fixed ? (int)((solo_budget - fixed) / ME_STAGE) : 0;
+    // the most CTAs per SM (3, 2, 1: 228 KB of shared memory per SM, 1 KB reserved per CTA)
+    // whose rings still hold three stages each
+    const size_t fixed = me_fixed_bytes(GU, p.K, TOK) + 1024 /*alignment*/;
+    const size_t solo_budget = 227 * 1024;
+    int per_sm = 1, stages = 0;
+    for (int n = 3; n >= 1; n--) {
+        const size_t budget = n == 1 ? solo_budget : (228 * 1024) / n - 1024;
+        stages = budget > fixed ? (int)((budget - fixed) / ME_STAGE) : 0;
+        per_sm = n;
+        if (stages >= 3) break;
     }
     stages = std::min(stages, ME_MAX_STAGES);
     if (stages < 2) return set_error(ctx, LQ_ERR_UNSUPPORTED, "moe: K=%d leaves no room for the weight ring", p.K);
@@ -607,23 +649,23 @@ static int launch_moe_stream(lq_ctx* ctx, MoeExpertParams p, const int8_t* wq, c
                             (uint64_t)(p.K / 32) * 2, 8, ME_GRP, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
     const size_t smem = (size_t)stages * ME_STAGE + fixed;
-    static bool attr[2][64] = {};
-    if (ctx->device < 0 || ctx->device >= 64 || !attr[GU][ctx->device]) {
-        LQ_CUDA(ctx, cudaFuncSetAttribute(moe_mma_kernel<GU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    static bool attr[64] = {};  // per instantiation (GU, TOK)
+    if (ctx->device < 0 || ctx->device >= 64 || !attr[ctx->device]) {
+        LQ_CUDA(ctx, cudaFuncSetAttribute(moe_mma_kernel<GU, TOK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           (int)solo_budget));
-        if (ctx->device >= 0 && ctx->device < 64) attr[GU][ctx->device] = true;
+        if (ctx->device >= 0 && ctx->device < 64) attr[ctx->device] = true;
     }
     int occ = 1;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, moe_mma_kernel<GU>, ME_THREADS, smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, moe_mma_kernel<GU, TOK>, ME_THREADS, smem);
     per_sm = std::max(1, std::min(per_sm, occ));
-    return launch_kernel(ctx, moe_mma_kernel<GU>, dim3(ctx->sm_count * per_sm), dim3(ME_THREADS), smem,
+    return launch_kernel(ctx, moe_mma_kernel<GU, TOK>, dim3(ctx->sm_count * per_sm), dim3(ME_THREADS), smem,
                          GU ? "moe_gate_up" : "moe_down", mw, md, p);
 }
 
 size_t moe_scratch_bytes(int64_t rows, int64_t E, int64_t top_k, int64_t H, int64_t inter) {
     const int64_t P = rows * top_k;
     return al256((size_t)P * 4) * 4 /*ids, wts, ids_sorted, w_sorted*/ + al256((size_t)E * 4) /*counts*/ +
-           al256((size_t)(E + 1) * 4) * 2 /*active, offsets*/ + al256((size_t)P * 4) * 2 /*pair lists*/ +
+           al256((size_t)(E + 1) * 4) * 3 /*active, offsets, cum*/ + al256((size_t)P * 4) * 2 /*pair lists*/ +
            al256((size_t)P * inter) + al256((size_t)P * (inter / 32) * 2) /*h as Q8_0*/ +
            al256((size_t)P * H * 4) /*y*/;
 }
@@ -650,6 +692,7 @@ int launch_moe(lq_ctx* ctx, const lq_q8_tensor* router, const lq_q8_tensor* gate
     L.offsets = (int32_t*)take((size_t)(E + 1) * 4);
     L.pair_token = (int32_t*)take((size_t)P * 4);
     L.pair_slot = (int32_t*)take((size_t)P * 4);
+    L.cum = (int32_t*)take((size_t)(E + 1) * 4);
     int8_t* hq = (int8_t*)take((size_t)P * inter);
     uint16_t* hd = (uint16_t*)take((size_t)P * (inter / 32) * 2);
     float* y = (float*)take((size_t)P * H * 4);
@@ -678,8 +721,12 @@ int launch_moe(lq_ctx* ctx, const lq_q8_tensor* router, const lq_q8_tensor* gate
             if (ctx->device >= 0 && ctx->device < 64) dattr[ctx->device] = true;
         }
     }
+    // 8 tokens per pass while experts get a few tokens each on average (most single-pass),
+    // else 16
+    const bool small = rows * top_k <= 6 * std::max<int64_t>(1, e_hi - e_lo);
     rc = launch_kernel(ctx, moe_dispatch_kernel, dim3(1), dim3(1024), disp_smem, "moe_dispatch",
-                       (const int32_t*)ids_sorted, (int)rows, (int)E, (int)top_k, L, (int)e_lo, (int)e_hi);
+                       (const int32_t*)ids_sorted, (int)rows, (int)E, (int)top_k, L, (int)e_lo, (int)e_hi,
+                       small ? 8 : 16);
     if (rc) return rc;
     MoeExpertParams p = {};
     p.E = (int)E;
@@ -687,6 +734,7 @@ int launch_moe(lq_ctx* ctx, const lq_q8_tensor* router, const lq_q8_tensor* gate
     p.offsets = L.offsets;
     p.counts = L.counts;
     p.active = L.active;
+    p.cum = L.cum;
     p.err = ctx->err_flag;
     p.e_base = (int)e_lo;
     // gate/up -> h = silu(g) * u as Q8_0 per pair
@@ -697,7 +745,8 @@ int launch_moe(lq_ctx* ctx, const lq_q8_tensor* router, const lq_q8_tensor* gate
     p.xd = xd;
     p.hq = hq;
     p.hd = hd;
-    rc = launch_moe_stream<true>(ctx, p, gate_up->qs, gate_up->d, gate_up->n);
+    rc = small ? launch_moe_stream<true, 8>(ctx, p, gate_up->qs, gate_up->d, gate_up->n)
+               : launch_moe_stream<true, 16>(ctx, p, gate_up->qs, gate_up->d, gate_up->n);
     if (rc) return rc;
     // down -> y (f32 per pair)
     p.rows_per_expert = (int)H;
@@ -706,7 +755,8 @@ int launch_moe(lq_ctx* ctx, const lq_q8_tensor* router, const lq_q8_tensor* gate
     p.xq = hq;
     p.xd = hd;
     p.y = y;
-    rc = launch_moe_stream<false>(ctx, p, down->qs, down->d, down->n);
+    rc = small ? launch_moe_stream<false, 8>(ctx, p, down->qs, down->d, down->n)
+               : launch_moe_stream<false, 16>(ctx, p, down->qs, down->d, down->n);
     if (rc) return rc;
     return launch_kernel(ctx, moe_combine_kernel, dim3((unsigned)ceil_div(H, 1024), (unsigned)rows), dim3(256), 0,
                          "moe_combine", (const float*)y,
