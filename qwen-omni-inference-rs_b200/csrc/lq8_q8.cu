@@ -465,7 +465,7 @@ size_t gemm_split_bytes(lq_ctx* ctx, int64_t n, int64_t k, int64_t m) {
     // the streamed GEMM's slices when the shape qualifies (its alignment is checked per call, so
     // the mma.sync GEMM's need counts too)
     size_t gs = 0;
-    if (m <= 32 && k % 256 == 0 && n % 64 == 0) {
+    if (k % 256 == 0 && n % 64 == 0) {
         const int s0 = gs_slices(ctx, n, k, m);
         const int64_t chunks = k / 256, ks = ((chunks + s0 - 1) / s0) * 256;
         if (s0 > 1) gs = (size_t)((k + ks - 1) / ks) * m * n * 4;
@@ -530,13 +530,13 @@ static int gemv_rows(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const
 }
 
 // =========================================================================================
-// Small-M Q8_0 GEMM, streamed (5 <= m <= 32 tokens): the MoE expert kernel's pipeline for a
-// dense weight. Work item = (64 weight rows, K slice, pass of up to 16 tokens); one producer
-// lane streams per 256-byte K-chunk the item's weight rows (two 32-row groups x two
-// 128-byte boxes, 128-byte swizzle), their fp16 scales, the pass's 16 token rows of the
+// Small-M Q8_0 GEMM, streamed (5 <= m <= 64 tokens): the MoE expert kernel's pipeline for a
+// dense weight. Work item = (64 weight rows, K slice, pass of TOK = 16 or 32 tokens); one
+// producer lane streams per 256-byte K-chunk the item's weight rows (two 32-row groups x two
+// 128-byte boxes, 128-byte swizzle), their fp16 scales, the pass's TOK token rows of the
 // quantized activations (two swizzled boxes; rows past m read as zeros) and the tokens'
-// scales into a shared-memory ring, 22 KiB per stage. Eight consumer warps each own 16 weight
-// rows (one m16 tile) and 8 of the pass's tokens (one n8 tile); each m16n8k32 MMA is one Q8_0
+// scales into a shared-memory ring (22 or 26 KiB per stage). Eight consumer warps each own 16
+// weight rows (one m16 tile) and TOK/16 of the pass's n8 tiles; each m16n8k32 MMA is one Q8_0
 // block, its int32 dots become floats by the 1.5*2^23 bias (the MMA accumulates onto it) and
 // are scaled and added per (row, token) in ascending block order with separately rounded
 // multiply and add: the oracle's order, bit-identical to it when K is not split. Passes of
@@ -544,19 +544,25 @@ static int gemv_rows(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const
 // tiles for the SMs split K into slices whose partials gemm_split_reduce adds in order.
 // =========================================================================================
 constexpr int GS_KC = 256;
-constexpr int GS_TOK = 16;
 constexpr int GS_CONS = 8;
 constexpr int GS_THREADS = (GS_CONS + 1) * 32;
 constexpr int GS_STAGES = 4;
 constexpr int GS_BOXW = 32 * 128;                   // one weight box: 32 rows x 128 bytes
 constexpr int GS_W = 4 * GS_BOXW;                   // 16 KiB: [group][half][32][128]
-constexpr int GS_BOXX = GS_TOK * 128;               // one activation box: 16 rows x 128 bytes
-constexpr int GS_X = 2 * GS_BOXX;                   // 4 KiB
 constexpr int GS_WD = 64 * 16;                      // weight scales [64][8] fp16
-constexpr int GS_XD = GS_TOK * 16;                  // token scales [16][8] fp16
-constexpr int GS_BYTES = GS_W + GS_X + GS_WD + GS_XD;  // bytes landing per stage
-constexpr int GS_STAGE = (GS_BYTES + 1023) / 1024 * 1024;
-constexpr size_t GS_SMEM = (size_t)GS_STAGES * GS_STAGE + 2 * GS_STAGES * 8 + 64 * 8 + 1024;
+
+// TOK tokens per pass: activation boxes [2][TOK][128 B], token scales [TOK][8] fp16; each
+// consumer warp takes TOK / 16 of the pass's n8 tiles
+template <int TOK>
+struct GsCfg {
+    static constexpr int BOXX = TOK * 128;
+    static constexpr int X = 2 * BOXX;
+    static constexpr int XD = TOK * 16;
+    static constexpr int BYTES = GS_W + X + GS_WD + XD;  // bytes landing per stage
+    static constexpr int STAGE = (BYTES + 1023) / 1024 * 1024;
+    static constexpr size_t SMEM = (size_t)GS_STAGES * STAGE + 2 * GS_STAGES * 8 + 64 * 8 + 1024;
+    static constexpr int NTW = TOK / 16;
+};
 
 struct GsParams {
     int N, K, M;
@@ -569,15 +575,17 @@ struct GsParams {
     int* err;
 };
 
+template <int TOK>
 __global__ void __launch_bounds__(GS_THREADS, 2) q8_gemm_stream_kernel(const __grid_constant__ CUtensorMap mw,
                                                                        const __grid_constant__ CUtensorMap mwd,
                                                                        const __grid_constant__ CUtensorMap mx,
                                                                        const __grid_constant__ CUtensorMap mxd,
                                                                        const GsParams p) {
+    using C = GsCfg<TOK>;
     extern __shared__ __align__(16) uint8_t smem_raw[];
     const uint32_t raw = smem_addr(smem_raw);
     uint8_t* sm = smem_raw + (((raw + 1023) & ~1023u) - raw);  // swizzled boxes need 1024-byte alignment
-    uint64_t* full = reinterpret_cast<uint64_t*>(sm + (size_t)GS_STAGES * GS_STAGE);
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + (size_t)GS_STAGES * C::STAGE);
     uint64_t* empty = full + GS_STAGES;
     unsigned long long* ckeys = reinterpret_cast<unsigned long long*>(empty + GS_STAGES);  // [64]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -609,21 +617,21 @@ __global__ void __launch_bounds__(GS_THREADS, 2) q8_gemm_stream_kernel(const __g
                     atomicCAS(p.err, 0, 24);
                     return;
                 }
-                uint8_t* st = sm + (size_t)s * GS_STAGE;
-                mbar_expect_tx(&full[s], (unsigned)GS_BYTES);
+                uint8_t* st = sm + (size_t)s * C::STAGE;
+                mbar_expect_tx(&full[s], (unsigned)C::BYTES);
                 for (int q = 0; q < 2; q++) {
                     const int row = rt * 64 + q * 32;
                     tma_load_2d(st + q * 2 * GS_BOXW, &mw, k, row, &full[s]);
                     tma_load_2d(st + q * 2 * GS_BOXW + GS_BOXW, &mw, k + 128, row, &full[s]);
-                    tma_load_2d(st + GS_W + GS_X + q * 32 * 16, &mwd, k / 32, row, &full[s]);
+                    tma_load_2d(st + GS_W + C::X + q * 32 * 16, &mwd, k / 32, row, &full[s]);
                 }
                 if (!waited) {  // the activations come from the preceding kernel
                     pdl_wait();
                     waited = true;
                 }
-                tma_load_2d(st + GS_W, &mx, k, ps * GS_TOK, &full[s]);
-                tma_load_2d(st + GS_W + GS_BOXX, &mx, k + 128, ps * GS_TOK, &full[s]);
-                tma_load_2d(st + GS_W + GS_X + GS_WD, &mxd, k / 32, ps * GS_TOK, &full[s]);
+                tma_load_2d(st + GS_W, &mx, k, ps * TOK, &full[s]);
+                tma_load_2d(st + GS_W + C::BOXX, &mx, k + 128, ps * TOK, &full[s]);
+                tma_load_2d(st + GS_W + C::X + GS_WD, &mxd, k / 32, ps * TOK, &full[s]);
             }
         }
         return;
@@ -631,14 +639,15 @@ __global__ void __launch_bounds__(GS_THREADS, 2) q8_gemm_stream_kernel(const __g
     // ---------------- consumers ----------------
     pdl_wait();  // resid / y / keys belong to the preceding kernels
     pdl_trigger();
+    constexpr int NTW = C::NTW;
     const int g = lane >> 2, t = lane & 3;
-    const int mt = warp & 3, n = warp >> 2;   // m16 tile (16 weight rows), n8 tile (8 tokens)
+    const int mt = warp & 3, n0 = (warp >> 2) * NTW;  // m16 tile (16 weight rows), first n8 tile
     const int q = mt >> 1;
-    const int ra = 16 * (mt & 1) + g;         // rows ra and ra + 8 of group q
+    const int ra = 16 * (mt & 1) + g;                  // rows ra and ra + 8 of group q
     const int a_off = q * 2 * GS_BOXW + ra * 128 + (t & 1) * 8;
-    const int b_off = GS_W + (8 * n + g) * 128 + (t & 1) * 8;
-    const int sc_off = GS_W + GS_X + (q * 32 + ra) * 16;
-    const int xd_off = GS_W + GS_X + GS_WD + (8 * n + 2 * t) * 16;
+    const int b_off = GS_W + (8 * n0 + g) * 128 + (t & 1) * 8;
+    const int sc_off = GS_W + C::X + (q * 32 + ra) * 16;
+    const int xd_off = GS_W + C::X + GS_WD + (8 * n0 + 2 * t) * 16;
     int it = 0;
     bool bad = false;
     for (long long item = i0; item < i1; item++) {
@@ -646,9 +655,11 @@ __global__ void __launch_bounds__(GS_THREADS, 2) q8_gemm_stream_kernel(const __g
         const int sl = (int)((item / p.passes) % p.slices);
         const int rt = (int)(item / ((long long)p.passes * p.slices));
         const int k0 = sl * p.kslice, k1 = min(p.K, k0 + p.kslice);
-        const int ntok = min(GS_TOK, p.M - ps * GS_TOK);
-        const bool active = 8 * n < ntok;  // warp-uniform: this warp's n-tile holds tokens
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        const int ntok = min(TOK, p.M - ps * TOK);
+        const int nact = min(NTW, max(0, (ntok - 8 * n0 + 7) / 8));  // this warp's tiles holding tokens
+        float acc[NTW][4];
+#pragma unroll
+        for (int i = 0; i < NTW; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
         for (int k = k0; k < k1; k += GS_KC, it++) {
             const int s = it % GS_STAGES;
             if (!bad) {
@@ -661,85 +672,111 @@ __global__ void __launch_bounds__(GS_THREADS, 2) q8_gemm_stream_kernel(const __g
                 }
             }
             if (bad) continue;
-            const uint8_t* st = sm + (size_t)s * GS_STAGE;
-            if (!active) {
+            const uint8_t* st = sm + (size_t)s * C::STAGE;
+            if (nact == 0) {
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[s]);
                 continue;
             }
-            uint2 wa[8], wb[8], xv[8];
+            // one n8 tile: the warp's whole slice of the stage into registers and the stage
+            // released at once; two tiles: the token fragments are read block by block and
+            // the stage released after the blocks (fewer live registers)
+            constexpr bool EARLY = NTW == 1;
+            uint2 wa[8], wb[8], xv[EARLY ? 8 : 1];
+            uint4 ua[NTW], ub[NTW];
 #pragma unroll
             for (int j = 0; j < 8; j++) {
                 const int ch = ((2 * (j & 3) + (t >> 1)) ^ g) << 4;
                 wa[j] = *reinterpret_cast<const uint2*>(st + a_off + (j >> 2) * GS_BOXW + ch);
                 wb[j] = *reinterpret_cast<const uint2*>(st + a_off + 8 * 128 + (j >> 2) * GS_BOXW + ch);
-                xv[j] = *reinterpret_cast<const uint2*>(st + b_off + (j >> 2) * GS_BOXX + ch);
+                if constexpr (EARLY) xv[j] = *reinterpret_cast<const uint2*>(st + b_off + (j >> 2) * C::BOXX + ch);
             }
             const uint4 sa = *reinterpret_cast<const uint4*>(st + sc_off);
             const uint4 sb = *reinterpret_cast<const uint4*>(st + sc_off + 8 * 16);
-            const uint4 ua = *reinterpret_cast<const uint4*>(st + xd_off);
-            const uint4 ub = *reinterpret_cast<const uint4*>(st + xd_off + 16);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+            for (int i = 0; i < NTW; i++) {
+                ua[i] = *reinterpret_cast<const uint4*>(st + xd_off + i * 8 * 16);
+                ub[i] = *reinterpret_cast<const uint4*>(st + xd_off + i * 8 * 16 + 16);
+            }
+            if constexpr (EARLY) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+            }
 #pragma unroll
             for (int j = 0; j < 8; j++) {
                 const uint32_t a[4] = {wa[j].x, wb[j].x, wa[j].y, wb[j].y};
-                const uint32_t b[2] = {xv[j].x, xv[j].y};
-                int d[4];
-                mma_s8_bias(d, a, b, 0x4B400000);
                 const uint32_t wsa = j < 2 ? sa.x : j < 4 ? sa.y : j < 6 ? sa.z : sa.w;
                 const uint32_t wsb = j < 2 ? sb.x : j < 4 ? sb.y : j < 6 ? sb.z : sb.w;
-                const uint32_t wx0 = j < 2 ? ua.x : j < 4 ? ua.y : j < 6 ? ua.z : ua.w;
-                const uint32_t wx1 = j < 2 ? ub.x : j < 4 ? ub.y : j < 6 ? ub.z : ub.w;
                 const float dwa = h2f((uint16_t)((j & 1) ? (wsa >> 16) : (wsa & 0xFFFFu)));
                 const float dwb = h2f((uint16_t)((j & 1) ? (wsb >> 16) : (wsb & 0xFFFFu)));
-                const float dx0 = h2f((uint16_t)((j & 1) ? (wx0 >> 16) : (wx0 & 0xFFFFu)));
-                const float dx1 = h2f((uint16_t)((j & 1) ? (wx1 >> 16) : (wx1 & 0xFFFFu)));
-                // the MMA added the dots to 1.5 * 2^23: one subtraction gives (float)dot exactly
-                const float f0 = __fsub_rn(__int_as_float(d[0]), 12582912.0f);
-                const float f1 = __fsub_rn(__int_as_float(d[1]), 12582912.0f);
-                const float f2 = __fsub_rn(__int_as_float(d[2]), 12582912.0f);
-                const float f3 = __fsub_rn(__int_as_float(d[3]), 12582912.0f);
-                acc[0] = __fadd_rn(acc[0], __fmul_rn(f0, __fmul_rn(dwa, dx0)));
-                acc[1] = __fadd_rn(acc[1], __fmul_rn(f1, __fmul_rn(dwa, dx1)));
-                acc[2] = __fadd_rn(acc[2], __fmul_rn(f2, __fmul_rn(dwb, dx0)));
-                acc[3] = __fadd_rn(acc[3], __fmul_rn(f3, __fmul_rn(dwb, dx1)));
+                const int ch = ((2 * (j & 3) + (t >> 1)) ^ g) << 4;
+#pragma unroll
+                for (int i = 0; i < NTW; i++) {
+                    if (i >= nact) break;
+                    const uint2 xj = EARLY ? xv[EARLY ? j : 0]
+                                           : *reinterpret_cast<const uint2*>(st + b_off + i * 8 * 128 +
+                                                                             (j >> 2) * C::BOXX + ch);
+                    const uint32_t b[2] = {xj.x, xj.y};
+                    int d[4];
+                    mma_s8_bias(d, a, b, 0x4B400000);
+                    const uint32_t wx0 = j < 2 ? ua[i].x : j < 4 ? ua[i].y : j < 6 ? ua[i].z : ua[i].w;
+                    const uint32_t wx1 = j < 2 ? ub[i].x : j < 4 ? ub[i].y : j < 6 ? ub[i].z : ub[i].w;
+                    const float dx0 = h2f((uint16_t)((j & 1) ? (wx0 >> 16) : (wx0 & 0xFFFFu)));
+                    const float dx1 = h2f((uint16_t)((j & 1) ? (wx1 >> 16) : (wx1 & 0xFFFFu)));
+                    // the MMA added the dots to 1.5 * 2^23: one subtraction gives (float)dot exactly
+                    const float f0 = __fsub_rn(__int_as_float(d[0]), 12582912.0f);
+                    const float f1 = __fsub_rn(__int_as_float(d[1]), 12582912.0f);
+                    const float f2 = __fsub_rn(__int_as_float(d[2]), 12582912.0f);
+                    const float f3 = __fsub_rn(__int_as_float(d[3]), 12582912.0f);
+                    acc[i][0] = __fadd_rn(acc[i][0], __fmul_rn(f0, __fmul_rn(dwa, dx0)));
+                    acc[i][1] = __fadd_rn(acc[i][1], __fmul_rn(f1, __fmul_rn(dwa, dx1)));
+                    acc[i][2] = __fadd_rn(acc[i][2], __fmul_rn(f2, __fmul_rn(dwb, dx0)));
+                    acc[i][3] = __fadd_rn(acc[i][3], __fmul_rn(f3, __fmul_rn(dwb, dx1)));
+                }
+            }
+            if constexpr (!EARLY) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
             }
         }
-        if (bad || !active) continue;
-        // epilogue: value v is (row ra + 8 (v >> 1) of group q, token 8n + 2t + (v & 1))
-        unsigned long long kk[2] = {0ull, 0ull};
+        if (bad || nact == 0) continue;
+        // epilogue: value v of tile i is (row ra + 8 (v >> 1) of group q, token 8 (n0 + i) + 2t + (v & 1))
 #pragma unroll
-        for (int v = 0; v < 4; v++) {
-            const int tk = 8 * n + 2 * t + (v & 1);
-            const int m = ps * GS_TOK + tk;
-            const int row = rt * 64 + q * 32 + ra + 8 * (v >> 1);
-            if (tk < ntok) {
-                if (p.part) {
-                    p.part[((size_t)sl * p.M + m) * p.N + row] = acc[v];
-                } else {
-                    const size_t o = (size_t)m * p.ldy + row;
-                    float val = acc[v];
-                    if (p.resid) val = __fadd_rn(p.resid[o], val);
-                    p.y[o] = val;
-                    if (p.keys) {
-                        const unsigned long long key = argmax_key(val, row);
-                        kk[v & 1] = key > kk[v & 1] ? key : kk[v & 1];
+        for (int i = 0; i < NTW; i++) {
+            if (i >= nact) break;
+            unsigned long long kk[2] = {0ull, 0ull};
+#pragma unroll
+            for (int v = 0; v < 4; v++) {
+                const int tk = 8 * (n0 + i) + 2 * t + (v & 1);
+                const int m = ps * TOK + tk;
+                const int row = rt * 64 + q * 32 + ra + 8 * (v >> 1);
+                if (tk < ntok) {
+                    if (p.part) {
+                        p.part[((size_t)sl * p.M + m) * p.N + row] = acc[i][v];
+                    } else {
+                        const size_t o = (size_t)m * p.ldy + row;
+                        float val = acc[i][v];
+                        if (p.resid) val = __fadd_rn(p.resid[o], val);
+                        p.y[o] = val;
+                        if (p.keys) {
+                            const unsigned long long key = argmax_key(val, row);
+                            kk[v & 1] = key > kk[v & 1] ? key : kk[v & 1];
+                        }
                     }
                 }
             }
-        }
-        if (p.keys && !p.part) {
+            if (p.keys && !p.part) {
 #pragma unroll
-            for (int h = 0; h < 2; h++) {
-                unsigned long long key = kk[h];
+                for (int h = 0; h < 2; h++) {
+                    unsigned long long key = kk[h];
 #pragma unroll
-                for (int o = 4; o < 32; o <<= 1) {
-                    const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
-                    key = other > key ? other : key;
+                    for (int o = 4; o < 32; o <<= 1) {
+                        const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+                        key = other > key ? other : key;
+                    }
+                    const int tk = 8 * (n0 + i) + 2 * t + h;
+                    if (g == 0 && tk < ntok && key) atomicMax(&ckeys[ps * TOK + tk], key);
                 }
-                const int tk = 8 * n + 2 * t + h;
-                if (g == 0 && tk < ntok && key) atomicMax(&ckeys[ps * GS_TOK + tk], key);
             }
         }
     }
@@ -750,10 +787,13 @@ __global__ void __launch_bounds__(GS_THREADS, 2) q8_gemm_stream_kernel(const __g
     }
 }
 
+// tokens per pass of the streamed GEMM: 16 up to 16 tokens, else 32 (one or two passes)
+static int gs_tok(int64_t m) { return m <= 16 ? 16 : 32; }
+
 // K slices for the streamed GEMM: about four items per CTA (two CTAs per SM), so that the
 // contiguous item ranges come out even, each slice at least 2 chunks of 256 bytes
 static int gs_slices(lq_ctx* ctx, int64_t n, int64_t k, int64_t m) {
-    const int64_t tiles = n / 64, passes = (m + GS_TOK - 1) / GS_TOK;
+    const int64_t tok = gs_tok(m), tiles = n / 64, passes = (m + tok - 1) / tok;
     const int64_t items = tiles * passes, target = 8 * (int64_t)ctx->sm_count;
     if (items >= target || getenv("LQ_GEMM_NO_SPLIT")) return 1;
     int64_t s = (target + items - 1) / items;
@@ -762,19 +802,21 @@ static int gs_slices(lq_ctx* ctx, int64_t n, int64_t k, int64_t m) {
 }
 
 static bool gs_supported(const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd, int64_t m) {
-    return m >= 5 && m <= 32 && w->k % GS_KC == 0 && w->n % 64 == 0 && w->n < (1ll << 31) &&
+    return m >= 5 && m <= 64 && w->k % GS_KC == 0 && w->n % 64 == 0 && w->n < (1ll << 31) &&
            ((uintptr_t)w->qs % 16) == 0 && ((uintptr_t)w->d % 16) == 0 && ((uintptr_t)xq % 16) == 0 &&
            ((uintptr_t)xd % 16) == 0 && !getenv("LQ_NO_GEMM_STREAM");
 }
 
-static int launch_gemm_stream(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd, int64_t m,
-                              float* y, const float* resid, int64_t ldy, unsigned long long* keys) {
+template <int TOK>
+static int launch_gemm_stream_t(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd,
+                                int64_t m, float* y, const float* resid, int64_t ldy, unsigned long long* keys) {
+    using C = GsCfg<TOK>;
     GsParams p = {};
     p.N = (int)w->n;
     p.K = (int)w->k;
     p.M = (int)m;
     p.tiles = (int)(w->n / 64);
-    p.passes = (int)((m + GS_TOK - 1) / GS_TOK);
+    p.passes = (int)((m + TOK - 1) / TOK);
     const int64_t chunks = w->k / GS_KC;
     int slices = gs_slices(ctx, w->n, w->k, m);
     p.kslice = (int)(((chunks + slices - 1) / slices) * GS_KC);
@@ -797,25 +839,31 @@ static int launch_gemm_stream(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* 
                                 (uint64_t)w->n, (uint64_t)(w->k / 32) * 2, 8, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (!rc)
         rc = make_tensor_map_2d(ctx, &mx, CU_TENSOR_MAP_DATA_TYPE_UINT8, xq, (uint64_t)w->k, (uint64_t)m,
-                                (uint64_t)w->k, 128, GS_TOK, CU_TENSOR_MAP_SWIZZLE_128B);
+                                (uint64_t)w->k, 128, TOK, CU_TENSOR_MAP_SWIZZLE_128B);
     if (!rc)
         rc = make_tensor_map_2d(ctx, &mxd, CU_TENSOR_MAP_DATA_TYPE_UINT16, xd, (uint64_t)(w->k / 32), (uint64_t)m,
-                                (uint64_t)(w->k / 32) * 2, 8, GS_TOK, CU_TENSOR_MAP_SWIZZLE_NONE);
+                                (uint64_t)(w->k / 32) * 2, 8, TOK, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
-    static bool attr = false;
+    static bool attr = false;  // one flag per instantiation
     if (!attr) {
-        LQ_CUDA(ctx, cudaFuncSetAttribute(q8_gemm_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)GS_SMEM));
+        LQ_CUDA(ctx, cudaFuncSetAttribute(q8_gemm_stream_kernel<TOK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)C::SMEM));
         attr = true;
     }
     const long long items = (long long)p.tiles * p.slices * p.passes;
     const int grid = (int)std::min<long long>(items, 2ll * ctx->sm_count);
-    rc = launch_kernel(ctx, q8_gemm_stream_kernel, dim3(grid), dim3(GS_THREADS), GS_SMEM, "q8_gemm_stream", mw, mwd,
-                       mx, mxd, p);
+    rc = launch_kernel(ctx, q8_gemm_stream_kernel<TOK>, dim3(grid), dim3(GS_THREADS), C::SMEM, "q8_gemm_stream", mw,
+                       mwd, mx, mxd, p);
     if (rc || p.slices == 1) return rc;
     return launch_kernel(ctx, gemm_split_reduce_kernel, dim3((unsigned)ceil_div(w->n, 1024), (unsigned)m), dim3(256), 0,
                          "gemm_split_reduce", (const float*)p.part, p.slices, (int)m, (int)w->n, resid, y, (int)ldy,
                          keys);
+}
+
+static int launch_gemm_stream(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd, int64_t m,
+                              float* y, const float* resid, int64_t ldy, unsigned long long* keys) {
+    return gs_tok(m) == 16 ? launch_gemm_stream_t<16>(ctx, w, xq, xd, m, y, resid, ldy, keys)
+                           : launch_gemm_stream_t<32>(ctx, w, xq, xd, m, y, resid, ldy, keys);
 }
 
 int launch_q8_matmul(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd,

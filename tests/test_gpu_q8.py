@@ -195,10 +195,10 @@ def test_matmul_residual_and_stride(ctx, lq8_lib, oracle, rng, monkeypatch, m):
         assert np.array_equal(y[:, :n], (resid[:, :n] + ref).astype(np.float32))
 
 
-@pytest.mark.parametrize("m", [5, 16, 23, 32])
+@pytest.mark.parametrize("m", [5, 16, 23, 40, 64])
 @pytest.mark.parametrize("split", [False, True])
 def test_gemm_stream_residual_and_stride(ctx, lq8_lib, oracle, rng, monkeypatch, m, split):
-    """The streamed small-M GEMM (5 <= m <= 32, n % 64 == 0, k % 256 == 0): passes of 16
+    """The streamed small-M GEMM (5 <= m <= 64, n % 64 == 0, k % 256 == 0): passes of 16 or 32
     tokens with a ragged last pass, y = residual + W.x into a wider row stride, columns past n
     untouched. Unsplit it is bit-identical to the oracle; with K slices (a 5-tile grid) within
     the regrouping bound and deterministic."""
