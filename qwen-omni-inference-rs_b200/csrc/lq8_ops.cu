@@ -216,6 +216,8 @@ __global__ void add_kernel(const float* a, const float* b, int64_t n, float* out
 }
 
 __global__ void keys_offset_kernel(unsigned long long* keys, int64_t n, long long offset) {
+    pdl_wait();  // the keys are the preceding LM-head kernel's
+    pdl_trigger();
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n && keys[i]) keys[i] += (unsigned long long)offset;
 }
