@@ -4,11 +4,11 @@
 // A CTA owns (one query row, one kv head, one chunk of ATT_C positions) and all G = Hq/Hkv
 // query heads that share the kv head. It stages the chunk's K and V rows into shared memory
 // with every 16-byte async copy in flight at once (rows of earlier positions before pdl_wait,
-// since earlier steps wrote them), computes the G score rows (each score is the reference's
-// sequential 128-term dot product, then the scale), a chunk softmax (max, exp, sum) and the
-// chunk's P.V. The last CTA of a (row, kv head) to finish -- found with an atomic counter --
-// merges the chunks (rescaling by exp(m_s - M)) and writes the [Hq*D] output row in f32
-// and/or Q8_0 for o_proj. One launch, no combine kernel.
+// since earlier steps wrote them), computes the G score rows (each score a 128-term dot in
+// dimension order, then the scale), a chunk softmax (max, exp, sum) and the chunk's P.V.
+// Fused decode variant: the last CTA of a (row, kv head) to finish -- found with an atomic
+// counter -- merges the chunks (rescaling by exp(m_s - M)) and writes the [Hq*D] output row
+// in f32 and/or Q8_0 for o_proj. Unfused variant: a merge kernel follows.
 //
 // The decode variant (FUSED) also performs the step before it: from the fused q|k|v
 // projection row it computes the G query heads' RMSNorm + RoPE into shared memory, and the
@@ -190,10 +190,11 @@ __device__ __forceinline__ void attn_chunk_fma(AttSmemR& S, int G, int cnt, floa
     }
 }
 
-// FUSED: the decode step's fused variant, every sum in the reference's order (sequential
-// 128-term dots, separately rounded multiply and add; the persistent decode kernel repeats it
-// bit for bit). Unfused: GT query heads per kv head (0: any G <= 8), dots and P.V with fused
-// multiply-add and each score's two 64-dim halves added at the end.
+// FUSED: the decode step's fused variant: each score one fused multiply-add chain over the 128
+// dimensions in order, each P.V output one chain over the positions in order (the persistent
+// decode kernel computes the same chains, bit for bit). Unfused: GT query heads per kv head
+// (0: any G <= 8), two-lane packed multiply-adds and each score's two 64-dim halves added at
+// the end.
 template <bool FUSED, int GT>
 __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const AttParams p) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -272,7 +273,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const AttParams
         attn_chunk_fma<GT ? GT : ATT_G>(S, G, cnt, scale, tid, p, ((int64_t)lrow * Hq + (int64_t)kvh * G) * nsplit + split,
                                         nsplit);
     } else {
-    // scores: thread -> (position pp, heads half, half+2, ...); sequential 128-term dot
+    // scores: thread -> (position pp, heads half, half+2, ...); one multiply-add chain over d
     {
         const int pp = tid % ATT_C, half = tid / ATT_C;
         float s[ATT_G / 2];
@@ -287,10 +288,10 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const AttParams
                     const int g = half + 2 * i;
                     if (g < G) {
                         const float4 q4 = *reinterpret_cast<const float4*>(&S.qs[g][4 * d4]);
-                        s[i] = __fadd_rn(s[i], __fmul_rn(q4.x, k4.x));
-                        s[i] = __fadd_rn(s[i], __fmul_rn(q4.y, k4.y));
-                        s[i] = __fadd_rn(s[i], __fmul_rn(q4.z, k4.z));
-                        s[i] = __fadd_rn(s[i], __fmul_rn(q4.w, k4.w));
+                        s[i] = fmaf(q4.x, k4.x, s[i]);
+                        s[i] = fmaf(q4.y, k4.y, s[i]);
+                        s[i] = fmaf(q4.z, k4.z, s[i]);
+                        s[i] = fmaf(q4.w, k4.w, s[i]);
                     }
                 }
             }
@@ -323,7 +324,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const AttParams
             const float vv = S.vs[j][d];
 #pragma unroll
             for (int g = 0; g < ATT_G; g++)
-                if (g < G) acc[g] = __fadd_rn(acc[g], __fmul_rn(S.ps[g][j], vv));
+                if (g < G) acc[g] = fmaf(S.ps[g][j], vv, acc[g]);
         }
         const int64_t hbase = ((int64_t)lrow * Hq + (int64_t)kvh * G) * nsplit + split;
 #pragma unroll

@@ -544,8 +544,8 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
         cp_async_wait<0>();
         pd_csync();
         // scores: thread -> position pp and heads q4, q4 + 4 (a warp shares one head, so its q
-        // reads are broadcasts); sequential 128-term dots, then the scale. K and q are read 32
-        // dims at a time into registers ahead of the add chain.
+        // reads are broadcasts); one multiply-add chain over the 128 dims, then the scale. K and
+        // q are read 32 dims at a time into registers ahead of the chain.
         {
             const int pp = tid % PD_ATT_C, q4 = tid / PD_ATT_C;
             float s[2] = {0.f, 0.f};
@@ -564,10 +564,10 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
                             for (int i = 0; i < 8; i++) qq[i] = *reinterpret_cast<const float4*>(&A.qs[g][d0 + 4 * i]);
 #pragma unroll
                             for (int i = 0; i < 8; i++) {
-                                s[h] = __fadd_rn(s[h], __fmul_rn(qq[i].x, kk[i].x));
-                                s[h] = __fadd_rn(s[h], __fmul_rn(qq[i].y, kk[i].y));
-                                s[h] = __fadd_rn(s[h], __fmul_rn(qq[i].z, kk[i].z));
-                                s[h] = __fadd_rn(s[h], __fmul_rn(qq[i].w, kk[i].w));
+                                s[h] = fmaf(qq[i].x, kk[i].x, s[h]);
+                                s[h] = fmaf(qq[i].y, kk[i].y, s[h]);
+                                s[h] = fmaf(qq[i].z, kk[i].z, s[h]);
+                                s[h] = fmaf(qq[i].w, kk[i].w, s[h]);
                             }
                         }
                     }
@@ -611,7 +611,7 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
                         const float4 pb = *reinterpret_cast<const float4*>(&A.ps[g][j0 + 4]);
                         const float pj[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
 #pragma unroll
-                        for (int j = 0; j < 8; j++) acc[i] = __fadd_rn(acc[i], __fmul_rn(pj[j], vv[j]));
+                        for (int j = 0; j < 8; j++) acc[i] = fmaf(pj[j], vv[j], acc[i]);
                     }
                 }
             }
@@ -620,7 +620,7 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
                     const int g = hh + 2 * i;
-                    if (g < G) acc[i] = __fadd_rn(acc[i], __fmul_rn(A.ps[g][j], vv));
+                    if (g < G) acc[i] = fmaf(A.ps[g][j], vv, acc[i]);
                 }
             }
 #pragma unroll
