@@ -418,14 +418,25 @@ __global__ void gemm_split_reduce_kernel(const float* __restrict__ part, int spl
                                          float* y, int ldy, unsigned long long* keys) {
     pdl_wait();
     pdl_trigger();
-    const int m = blockIdx.y;
+    // one column per thread; the slices' values are loaded 8 at a time ahead of the adds
+    const int m = blockIdx.y, n = blockIdx.x * blockDim.x + threadIdx.x;
     __shared__ unsigned long long ck;
     if (threadIdx.x == 0) ck = 0ull;
     __syncthreads();
     unsigned long long key = 0ull;
-    for (int n = blockIdx.x * blockDim.x + threadIdx.x; n < N; n += gridDim.x * blockDim.x) {
+    if (n < N) {
+        const float* pp = part + (size_t)m * N + n;
+        const size_t stride = (size_t)M * N;
         float v = 0.0f;
-        for (int s = 0; s < splits; s++) v = __fadd_rn(v, part[((size_t)s * M + m) * N + n]);
+        int s = 0;
+        for (; s + 8 <= splits; s += 8) {
+            float t[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) t[i] = pp[(size_t)(s + i) * stride];
+#pragma unroll
+            for (int i = 0; i < 8; i++) v = __fadd_rn(v, t[i]);
+        }
+        for (; s < splits; s++) v = __fadd_rn(v, pp[(size_t)s * stride]);
         const size_t o = (size_t)m * ldy + n;
         if (resid) v = __fadd_rn(resid[o], v);
         y[o] = v;
@@ -503,7 +514,7 @@ static int run_gemm(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const 
     int rc = launch_kernel(ctx, q8_gemm_mma_kernel<BW, BX, WW, WX>, grid, dim3(C::THREADS), C::SMEM, "q8_gemm_mma",
                            w->qs, w->d, (int)w->n, (int)w->k, xq, xd, (int)m, resid, y, (int)ldy, keys, kslice, part);
     if (rc || splits == 1) return rc;
-    return launch_kernel(ctx, gemm_split_reduce_kernel, dim3((unsigned)ceil_div(w->n, 1024), (unsigned)m), dim3(256), 0,
+    return launch_kernel(ctx, gemm_split_reduce_kernel, dim3((unsigned)ceil_div(w->n, 256), (unsigned)m), dim3(256), 0,
                          "gemm_split_reduce", (const float*)part, splits, (int)m, (int)w->n, resid, y, (int)ldy, keys);
 }
 
@@ -855,7 +866,7 @@ static int launch_gemm_stream_t(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t
     rc = launch_kernel(ctx, q8_gemm_stream_kernel<TOK>, dim3(grid), dim3(GS_THREADS), C::SMEM, "q8_gemm_stream", mw,
                        mwd, mx, mxd, p);
     if (rc || p.slices == 1) return rc;
-    return launch_kernel(ctx, gemm_split_reduce_kernel, dim3((unsigned)ceil_div(w->n, 1024), (unsigned)m), dim3(256), 0,
+    return launch_kernel(ctx, gemm_split_reduce_kernel, dim3((unsigned)ceil_div(w->n, 256), (unsigned)m), dim3(256), 0,
                          "gemm_split_reduce", (const float*)p.part, p.slices, (int)m, (int)w->n, resid, y, (int)ldy,
                          keys);
 }
