@@ -54,16 +54,32 @@ __device__ __forceinline__ void load4_any<uint16_t>(const uint16_t* p, float v[4
 // per 4*THREADS-wide pass, in pass order), a warp butterfly and a cross-warp sum in warp order
 // give the total; inv = 1/sqrt(sum/dim + eps); out = bf16((x*inv)*w). Optional outputs: the
 // bf16 row and/or its Q8_0 quantization (xq [dim], xd [dim/32]). red: >= 32 floats of smem.
-template <typename T, int THREADS, int BAR>
+template <typename T, int THREADS, int BAR, int RC = 0>
 __device__ __forceinline__ void rms_row(const T* __restrict__ xr, int dim, const uint16_t* __restrict__ w,
                                         float eps, int tid, float* red, uint16_t* out, int8_t* xq,
                                         uint16_t* xd) {
+    // RC > 0: rows of up to RC * THREADS * 4 elements stay in registers between the two passes
+    // (all their loads issued at once); otherwise (and for longer rows) the second pass reads the
+    // row again. The sum of squares runs in the same order either way.
+    float cache[RC > 0 ? RC : 1][4];
+    const bool cached = RC > 0 && dim <= RC * THREADS * 4;
+#pragma unroll
+    for (int c = 0; c < RC; c++) {
+        const int e = c * THREADS * 4 + tid * 4;
+        if (cached && e < dim) load4_any<T>(xr + e, cache[c]);
+    }
     float ss = 0.0f;
     for (int base = 0; base < dim; base += THREADS * 4) {
         const int e = base + tid * 4;
         if (e < dim) {
             float v[4];
-            load4_any<T>(xr + e, v);
+            if (cached) {
+#pragma unroll
+                for (int c = 0; c < RC; c++)
+                    if (c * THREADS * 4 == base) v[0] = cache[c][0], v[1] = cache[c][1], v[2] = cache[c][2], v[3] = cache[c][3];
+            } else {
+                load4_any<T>(xr + e, v);
+            }
 #pragma unroll
             for (int i = 0; i < 4; i++) {
                 const float r = round_bf16(v[i]);
@@ -85,7 +101,13 @@ __device__ __forceinline__ void rms_row(const T* __restrict__ xr, int dim, const
         const bool valid = e < dim;
         float v[4] = {0.f, 0.f, 0.f, 0.f};
         if (valid) {
-            load4_any<T>(xr + e, v);
+            if (cached) {
+#pragma unroll
+                for (int c = 0; c < RC; c++)
+                    if (c * THREADS * 4 == base) v[0] = cache[c][0], v[1] = cache[c][1], v[2] = cache[c][2], v[3] = cache[c][3];
+            } else {
+                load4_any<T>(xr + e, v);
+            }
             const uint2 wt = *reinterpret_cast<const uint2*>(w + e);
             const float wv[4] = {bf16_to_f32((uint16_t)(wt.x & 0xFFFF)), bf16_to_f32((uint16_t)(wt.x >> 16)),
                                  bf16_to_f32((uint16_t)(wt.y & 0xFFFF)), bf16_to_f32((uint16_t)(wt.y >> 16))};

@@ -28,7 +28,7 @@ rmsnorm_kernel(const T* __restrict__ x, int dim, const uint16_t* __restrict__ w,
     pdl_wait();
     pdl_trigger();
     const int64_t row = blockIdx.x;
-    rms_row<T, NORM_THREADS, 0>(x + row * dim, dim, w, eps, threadIdx.x, red, out ? out + row * dim : nullptr,
+    rms_row<T, NORM_THREADS, 0, 8>(x + row * dim, dim, w, eps, threadIdx.x, red, out ? out + row * dim : nullptr,
                                 xq ? xq + row * dim : nullptr, xq ? xd + row * (dim >> 5) : nullptr);
 }
 
@@ -105,16 +105,35 @@ silu_mul_kernel(const float* __restrict__ gu, int inter, float* __restrict__ h, 
                 uint16_t* __restrict__ xd) {
     pdl_wait();
     pdl_trigger();
+    // CTA (row, 1024-column chunk): one pass of the row function over its chunk (each 8-lane
+    // group quantizes one 32-element block, so the chunking does not change a value)
     const int64_t row = blockIdx.x;
-    silu_row<256>(gu + row * 2 * inter, inter, threadIdx.x, h ? h + row * inter : nullptr,
-                  xq ? xq + row * inter : nullptr, xq ? xd + row * (inter >> 5) : nullptr);
+    const int c0 = blockIdx.y * 1024, n = min(1024, inter - c0);
+    const float* g = gu + row * 2 * inter + c0;
+    const int e = threadIdx.x * 4;
+    const bool valid = e < n;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (valid) {
+        const float4 gg = *reinterpret_cast<const float4*>(g + e);
+        const float4 uu = *reinterpret_cast<const float4*>(g + inter + e);
+        v[0] = swiglu(gg.x, uu.x);
+        v[1] = swiglu(gg.y, uu.y);
+        v[2] = swiglu(gg.z, uu.z);
+        v[3] = swiglu(gg.w, uu.w);
+        if (h) *reinterpret_cast<float4*>(h + row * inter + c0 + e) = make_float4(v[0], v[1], v[2], v[3]);
+    }
+    if (xq) {
+        const int64_t o = row * inter + c0 + e;
+        const uint32_t q = quant_group8(v, threadIdx.x & 7, valid ? xd + (o >> 5) : nullptr);
+        if (valid) *reinterpret_cast<uint32_t*>(xq + o) = q;
+    }
 }
 
 int launch_silu_mul(lq_ctx* ctx, const float* gu, int64_t m, int64_t inter, float* h, int8_t* xq,
                     uint16_t* xd) {
     if (m == 0) return LQ_OK;
-    return launch_kernel(ctx, silu_mul_kernel, dim3((unsigned)m), dim3(256), 0, "silu_mul", gu, (int)inter, h, xq,
-                         xd);
+    return launch_kernel(ctx, silu_mul_kernel, dim3((unsigned)m, (unsigned)ceil_div(inter, 1024)), dim3(256), 0,
+                         "silu_mul", gu, (int)inter, h, xq, xd);
 }
 
 // =========================================================================================
