@@ -448,8 +448,16 @@ __global__ void __launch_bounds__(256, 4) attn_merge_kernel(const AttParams p) {
     for (int g = hh; g < G; g += 2) {
         const float* po = p.part_o + (hbase0 + (int64_t)g * nsplit) * ATT_D + d;
         float o = 0.0f;
-#pragma unroll 8
-        for (int s = 0; s < n_active; s++) o = __fadd_rn(o, __fmul_rn(cm[g][s], po[(int64_t)s * ATT_D]));
+        // the chunks' values loaded 16 at a time ahead of the ordered adds
+        int s = 0;
+        for (; s + 16 <= n_active; s += 16) {
+            float t[16];
+#pragma unroll
+            for (int i = 0; i < 16; i++) t[i] = po[(int64_t)(s + i) * ATT_D];
+#pragma unroll
+            for (int i = 0; i < 16; i++) o = __fadd_rn(o, __fmul_rn(cm[g][s + i], t[i]));
+        }
+        for (; s < n_active; s++) o = __fadd_rn(o, __fmul_rn(cm[g][s], po[(int64_t)s * ATT_D]));
         o = __fdiv_rn(o, cl[g]);
         const int64_t e = (int64_t)row * Hq * ATT_D + (int64_t)(kvh * G + g) * ATT_D + d;
         if (p.out) p.out[e] = o;

@@ -597,16 +597,20 @@ __global__ void moe_combine_kernel(const float* __restrict__ y, const int32_t* _
     __syncthreads();
     const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
     if (c >= H) return;
+    // every pair's row loaded before the ordered adds
+    float4 v[MOE_MAX_K];
+#pragma unroll
+    for (int jj = 0; jj < MOE_MAX_K; jj++)
+        if (jj < top_k && sp[jj] >= 0) v[jj] = *reinterpret_cast<const float4*>(y + (size_t)sp[jj] * H + c);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int jj = 0; jj < top_k; jj++) {
-        const int pr = sp[jj];
-        if (pr < 0) continue;  // an expert of another rank
+#pragma unroll
+    for (int jj = 0; jj < MOE_MAX_K; jj++) {
+        if (jj >= top_k || sp[jj] < 0) continue;  // past top-k, or an expert of another rank
         const float w = sw[jj];
-        const float4 v = *reinterpret_cast<const float4*>(y + (size_t)pr * H + c);
-        acc.x = __fadd_rn(acc.x, __fmul_rn(w, v.x));
-        acc.y = __fadd_rn(acc.y, __fmul_rn(w, v.y));
-        acc.z = __fadd_rn(acc.z, __fmul_rn(w, v.z));
-        acc.w = __fadd_rn(acc.w, __fmul_rn(w, v.w));
+        acc.x = __fadd_rn(acc.x, __fmul_rn(w, v[jj].x));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(w, v[jj].y));
+        acc.z = __fadd_rn(acc.z, __fmul_rn(w, v[jj].z));
+        acc.w = __fadd_rn(acc.w, __fmul_rn(w, v[jj].w));
     }
     const size_t o = (size_t)t * H + c;
     if (resid) {
