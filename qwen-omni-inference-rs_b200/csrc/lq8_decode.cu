@@ -94,9 +94,9 @@ struct PdAtt {
     float ks[PD_ATT_C][PD_KS];
     float vs[PD_ATT_C][128];
     float qraw[PD_MAX_G][128];
-    float qs[PD_MAX_G][128];
+    float qs[PD_MAX_G][PD_KS];  // padded like ks: the lanes of different heads hit different banks
     float kvraw[2][128];
-    float ps[PD_MAX_G][PD_ATT_C];
+    float ps[PD_MAX_G][PD_ATT_C + 4];  // padded: heads g and g' read position j in different banks
     float ml[PD_MAX_G][2];
     float cm[PD_MAX_G][PD_MAX_SPLITS];
     float cl[PD_MAX_G];
@@ -451,37 +451,34 @@ __device__ __forceinline__ bool pd_consume(PdSmem& S, const PdGemv& g, const int
 
 // ---- attention (the decode attention kernel's arithmetic, on 256 threads) ----
 
-// an attention item's K/V cache rows of earlier steps (those before the new position) into
-// the staging area, every copy in flight; they depend on nothing this step computes
-template <int M>
-__device__ __forceinline__ void pd_item_kv(const PdParams& p, const PdLayer& L, PdAtt& A, int p0, int nsplit,
-                                           int item) {
+// an attention item's K (which = 0) or V (which = 1) cache rows of earlier steps (those before
+// the new position) into the staging area, every copy in flight; they depend on nothing this
+// step computes
+__device__ __forceinline__ void pd_item_rows(const PdParams& p, const PdLayer& L, PdAtt& A, int p0, int nsplit,
+                                             int item, int which) {
     const int D = 128, Hkv = p.Hkv;
     const int split = item % nsplit, kvh = (item / nsplit) % Hkv, b = item / (nsplit * Hkv);
     const int j0 = split * PD_ATT_C;
-    const int cnt = min(PD_ATT_C, p0 + 1 - j0);
-    const int fresh = p0 - j0;
-    const float* kbase = L.kc + ((int64_t)b * Hkv + kvh) * (int64_t)p.ctx_max * D + (int64_t)j0 * D;
-    const float* vbase = L.vc + ((int64_t)b * Hkv + kvh) * (int64_t)p.ctx_max * D + (int64_t)j0 * D;
-    for (int i = threadIdx.x; i < cnt * (D / 4); i += PD_CTHREADS) {
+    const int rows = min(PD_ATT_C, p0 - j0);  // the new position's row is computed, not copied
+    const float* base = (which ? L.vc : L.kc) + ((int64_t)b * Hkv + kvh) * (int64_t)p.ctx_max * D + (int64_t)j0 * D;
+    for (int i = threadIdx.x; i < rows * (D / 4); i += PD_CTHREADS) {
         const int r = i / (D / 4), c = (i % (D / 4)) * 4;
-        if (r < fresh) {
-            cp_async16(&A.ks[r][c], kbase + (int64_t)r * D + c, true);
-            cp_async16(&A.vs[r][c], vbase + (int64_t)r * D + c, true);
-        }
+        cp_async16(which ? &A.vs[r][c] : &A.ks[r][c], base + (int64_t)r * D + c, true);
     }
     cp_async_commit();
 }
 
-// claims this CTA's first attention item of the layer and starts its cache-row copies (called
-// before the grid barrier that precedes attention, so the copies overlap it)
+// this CTA's first attention item of the layer is item blockIdx.x (later items are claimed from
+// the layer's counter, offset by the grid size); its cache-row copies start here, before the
+// grid barrier that precedes attention, so they overlap it
 template <int M>
-__device__ __forceinline__ int pd_attention_begin(const PdParams& p, const PdLayer& L, PdSmem& S, PdAtt& A, int p0,
-                                                  int nsplit, unsigned* ctr) {
-    if (threadIdx.x == 0) S.item = (int)atomicAdd(ctr, 1u);
-    pd_csync();
-    const int item = S.item;
-    if (item < M * p.Hkv * nsplit) pd_item_kv<M>(p, L, A, p0, nsplit, item);
+__device__ __forceinline__ int pd_attention_begin(const PdParams& p, const PdLayer& L, PdAtt& A, int p0,
+                                                  int nsplit) {
+    const int item = (int)blockIdx.x;
+    if (item < M * p.Hkv * nsplit) {
+        pd_item_rows(p, L, A, p0, nsplit, item, 0);
+        pd_item_rows(p, L, A, p0, nsplit, item, 1);
+    }
     return item;
 }
 
@@ -498,21 +495,20 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
     const float* cs = p.cos_t + (int64_t)p0 * (D / 2);
     const float* sn = p.sin_t + (int64_t)p0 * (D / 2);
-    // items are claimed from the phase counter; the next claim is issued while this item runs
+    // items after the first are claimed from the phase counter (claim c is item gridDim.x + c);
+    // the next claim is issued while this item runs, and the next item's K rows are copied in
+    // once this item's scores are done, its V rows once this item's P.V is done
     int item = first;
-    bool kv_issued = true;
     while (item < n_items) {
         int next = 0;
-        if (tid == 0) next = (int)atomicAdd(ctr, 1u);
+        if (tid == 0) next = (int)gridDim.x + (int)atomicAdd(ctr, 1u);
         const int split = item % nsplit, kvh = (item / nsplit) % Hkv, b = item / (nsplit * Hkv);
         const int j0 = split * PD_ATT_C;
         const int cnt = min(PD_ATT_C, p0 + 1 - j0);
         const int fresh = p0 - j0;  // chunk row of the new position (when < cnt)
         float* kbase = L.kc + ((int64_t)b * Hkv + kvh) * (int64_t)p.ctx_max * D + (int64_t)j0 * D;
         float* vbase = L.vc + ((int64_t)b * Hkv + kvh) * (int64_t)p.ctx_max * D + (int64_t)j0 * D;
-        pd_csync();  // the staging area is free
-        if (!kv_issued) pd_item_kv<M>(p, L, A, p0, nsplit, item);
-        kv_issued = false;
+        pd_csync();  // the previous item is done with q, the raw rows and the scores
         // this kv head's q heads (and, for the chunk of the new position, its k and v) from
         // the q|k|v rows
         const float* qrow = p.qkv + (int64_t)b * heads * D;
@@ -543,43 +539,38 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
         }
         cp_async_wait<0>();
         pd_csync();
-        // scores: thread -> position pp and heads q4, q4 + 4 (a warp shares one head, so its q
-        // reads are broadcasts); one multiply-add chain over the 128 dims, then the scale. K and
-        // q are read 32 dims at a time into registers ahead of the chain.
-        {
-            const int pp = tid % PD_ATT_C, q4 = tid / PD_ATT_C;
-            float s[2] = {0.f, 0.f};
+        // scores: thread -> (position pp, head g), heads fastest, so the G lanes of a position
+        // read the same K address and the lanes of a head the same q address (shared-memory
+        // broadcasts: a K row is fetched once for all heads of the group); one multiply-add chain
+        // over the 128 dims, then the scale. K and q are read 32 dims at a time into registers
+        // ahead of the chain.
+        for (int idx = tid; idx < PD_ATT_C * G; idx += PD_CTHREADS) {
+            const int pp = idx / G, g = idx - pp * G;
+            float s = 0.f;
             if (pp < cnt) {
 #pragma unroll
                 for (int d0 = 0; d0 < D; d0 += 32) {
-                    float4 kk[8];
+                    float4 kk[8], qq[8];
 #pragma unroll
                     for (int i = 0; i < 8; i++) kk[i] = *reinterpret_cast<const float4*>(&A.ks[pp][d0 + 4 * i]);
 #pragma unroll
-                    for (int h = 0; h < 2; h++) {
-                        const int g = q4 + 4 * h;
-                        if (g < G) {
-                            float4 qq[8];
+                    for (int i = 0; i < 8; i++) qq[i] = *reinterpret_cast<const float4*>(&A.qs[g][d0 + 4 * i]);
 #pragma unroll
-                            for (int i = 0; i < 8; i++) qq[i] = *reinterpret_cast<const float4*>(&A.qs[g][d0 + 4 * i]);
-#pragma unroll
-                            for (int i = 0; i < 8; i++) {
-                                s[h] = fmaf(qq[i].x, kk[i].x, s[h]);
-                                s[h] = fmaf(qq[i].y, kk[i].y, s[h]);
-                                s[h] = fmaf(qq[i].z, kk[i].z, s[h]);
-                                s[h] = fmaf(qq[i].w, kk[i].w, s[h]);
-                            }
-                        }
+                    for (int i = 0; i < 8; i++) {
+                        s = fmaf(qq[i].x, kk[i].x, s);
+                        s = fmaf(qq[i].y, kk[i].y, s);
+                        s = fmaf(qq[i].z, kk[i].z, s);
+                        s = fmaf(qq[i].w, kk[i].w, s);
                     }
                 }
             }
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-                const int g = q4 + 4 * h;
-                if (g < G) A.ps[g][pp] = pp < cnt ? __fmul_rn(s[h], scale) : -INFINITY;
-            }
+            A.ps[g][pp] = pp < cnt ? __fmul_rn(s, scale) : -INFINITY;
         }
+        if (tid == 0) S.item = next;
         pd_csync();
+        // K is free: the next item's K rows start loading
+        const int nx = S.item;
+        if (nx < n_items) pd_item_rows(p, L, A, p0, nsplit, nx, 0);
         // chunk softmax per head: max, exp(s - max), sum
         for (int g = warp; g < G; g += PD_CONS) {
             const float a = A.ps[g][lane], c = A.ps[g][lane + 32];
@@ -591,56 +582,54 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
             if (lane == 0) { A.ml[g][0] = mx; A.ml[g][1] = sum; }
         }
         pd_csync();
-        // chunk P.V: thread -> dim d and heads hh, hh + 2, ...
+        // chunk P.V: thread -> (dims 4c..4c+3, head g), heads fastest, so the G lanes of a dim
+        // group read the same V address and the lanes of a head the same P address; per output
+        // one multiply-add chain over the positions in order, 8 at a time with their V and P
+        // values read ahead
         const int64_t hb0 = ((int64_t)b * Hq + (int64_t)kvh * G) * PD_MAX_SPLITS;
         {
-            // positions in order, 8 at a time with their V and P values read ahead
-            const int d = tid & (D - 1), hh = tid >> 7;
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-            int j0 = 0;
+            for (int idx = tid; idx < (D / 4) * G; idx += PD_CTHREADS) {
+                const int c4 = idx / G, g = idx - c4 * G;
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                int j0 = 0;
 #pragma unroll 1
-            for (; j0 + 8 <= cnt; j0 += 8) {
-                float vv[8];
+                for (; j0 + 8 <= cnt; j0 += 8) {
+                    float4 vv[8];
 #pragma unroll
-                for (int j = 0; j < 8; j++) vv[j] = A.vs[j0 + j][d];
+                    for (int j = 0; j < 8; j++) vv[j] = *reinterpret_cast<const float4*>(&A.vs[j0 + j][4 * c4]);
+                    const float4 pa = *reinterpret_cast<const float4*>(&A.ps[g][j0]);
+                    const float4 pb = *reinterpret_cast<const float4*>(&A.ps[g][j0 + 4]);
+                    const float pj[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
 #pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const int g = hh + 2 * i;
-                    if (g < G) {
-                        const float4 pa = *reinterpret_cast<const float4*>(&A.ps[g][j0]);
-                        const float4 pb = *reinterpret_cast<const float4*>(&A.ps[g][j0 + 4]);
-                        const float pj[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
-#pragma unroll
-                        for (int j = 0; j < 8; j++) acc[i] = fmaf(pj[j], vv[j], acc[i]);
+                    for (int j = 0; j < 8; j++) {
+                        acc.x = fmaf(pj[j], vv[j].x, acc.x);
+                        acc.y = fmaf(pj[j], vv[j].y, acc.y);
+                        acc.z = fmaf(pj[j], vv[j].z, acc.z);
+                        acc.w = fmaf(pj[j], vv[j].w, acc.w);
                     }
                 }
-            }
-            for (int j = j0; j < cnt; j++) {
-                const float vv = A.vs[j][d];
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const int g = hh + 2 * i;
-                    if (g < G) acc[i] = fmaf(A.ps[g][j], vv, acc[i]);
+                for (int j = j0; j < cnt; j++) {
+                    const float4 vv = *reinterpret_cast<const float4*>(&A.vs[j][4 * c4]);
+                    const float pj = A.ps[g][j];
+                    acc.x = fmaf(pj, vv.x, acc.x);
+                    acc.y = fmaf(pj, vv.y, acc.y);
+                    acc.z = fmaf(pj, vv.z, acc.z);
+                    acc.w = fmaf(pj, vv.w, acc.w);
                 }
-            }
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const int g = hh + 2 * i;
-                if (g < G) p.part_o[(hb0 + (int64_t)g * PD_MAX_SPLITS + split) * D + d] = acc[i];
+                *reinterpret_cast<float4*>(&p.part_o[(hb0 + (int64_t)g * PD_MAX_SPLITS + split) * D + 4 * c4]) = acc;
             }
             if (tid < G) {
                 p.part_ml[(hb0 + (int64_t)tid * PD_MAX_SPLITS + split) * 2] = A.ml[tid][0];
                 p.part_ml[(hb0 + (int64_t)tid * PD_MAX_SPLITS + split) * 2 + 1] = A.ml[tid][1];
             }
         }
-        // the last chunk of this (row, kv head) to finish merges the chunks
         // publish the chunk: the (row, kv head)'s counter grows by nsplit per layer
         __threadfence();
         pd_csync();
         if (tid == 0) atomicAdd(p.bar + 1 + b * Hkv + kvh, 1u);
-        if (tid == 0) S.item = next;
-        pd_csync();
-        item = S.item;
+        // V is free: the next item's V rows start loading
+        if (nx < n_items) pd_item_rows(p, L, A, p0, nsplit, nx, 1);
+        item = nx;
     }
     // merge tasks (row, q head), claimed by CTAs that ran out of chunk items: wait until the
     // kv head's chunks of this layer are all published, then merge them (rescale by
@@ -800,7 +789,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
                            nullptr, p.err))
             return;
         // the first attention item's cache rows start loading before the barrier
-        const int first = pd_attention_begin<M>(p, L, S, A, p0, nsplit, pd_att_ctr(p, M, l, 0));
+        const int first = pd_attention_begin<M>(p, L, A, p0, nsplit);
         if (!pd_grid_barrier(p, S, epoch)) return;
         // attention -> Q8_0 rows
         pd_attention<M>(p, L, S, A, p0, nsplit, pd_att_ctr(p, M, l, 0), pd_att_ctr(p, M, l, 1),

@@ -65,6 +65,31 @@ def test_persistent_step_bit_identical(ctx, lq8_lib, oracle, monkeypatch, cfg_na
     ref.close()
 
 
+@pytest.mark.parametrize("cfg_name,B", [("wide", 1), ("wide", 3), ("tiny", 4), ("gqa8_ragged_vocab", 4)])
+def test_persistent_step_bit_identical_long_context(ctx, lq8_lib, oracle, monkeypatch, cfg_name, B):
+    """Contexts of ~1280 positions: 20-21 chunks per (row, kv head), so 80-480 attention items
+    against 148 SMs (GQA groups of 2, 4 and 8). CTAs take several items in turn, with the next
+    item's cache rows copied in while the current one is computed, and merge tasks wait on
+    chunks of other CTAs; decode positions 1276..1281 cross the chunk boundary at 1280."""
+    cfgd = CONFIGS[cfg_name]
+    seed, L, steps = 91, 1276, 6
+    per, ref = _pair(lq8_lib, ctx, cfgd, seed, B, 1296, monkeypatch)
+    prompts = np.stack([oracle.gen_tokens(seed, s, L, cfgd["vocab"]) for s in range(B)])
+    for m in (per, ref):
+        m.clear_kv_cache()
+        m.set_batch(B)
+    tok = per.prefill(prompts)
+    ref.prefill(prompts)
+    for i in range(steps):
+        a, la = per.decode_step(tok, want_logits=True)
+        b, lb = ref.decode_step(tok, want_logits=True)
+        assert np.array_equal(la, lb), (i, float(np.max(np.abs(la - lb))))
+        assert np.array_equal(a, b), i
+        tok = a
+    per.close()
+    ref.close()
+
+
 def test_persistent_step_matches_oracle(ctx, lq8_lib, oracle):
     """Teacher-forced decode through the persistent step against the oracle on the tiny
     config, with the per-layer decode path's tolerance (cosine >= 0.99999, max |diff| <=
