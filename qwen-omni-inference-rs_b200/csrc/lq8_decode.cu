@@ -288,6 +288,16 @@ __device__ __forceinline__ int pd_block_sum(const int4 wa, const int4 wb, const 
     return sum;
 }
 
+// the residual a consumer lane adds in unit u of a phase with nout outputs (lane 8r + m: row
+// 2w + r, token m); 0 for lanes without an output and for units past the phase's end
+template <int M>
+__device__ __forceinline__ float pd_res_lane(const float* out, int ldo, int nout, int u) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = u * PD_ROWS + 2 * warp + (lane >> 3);
+    if (lane < 16 && (lane & 7) < M && row < nout) return __ldcg(out + (size_t)(lane & 7) * ldo + row);
+    return 0.0f;
+}
+
 // the units of one GEMV phase that this CTA's producer claimed, against the activations
 // xs/xds in shared memory: out[m][row] (+ the residual already in out), logits + argmax keys,
 // or h = SiLU(gate)*up quantized to Q8_0 (hq, hd).
@@ -298,7 +308,8 @@ __device__ __forceinline__ int pd_block_sum(const int4 wa, const int4 wb, const 
 template <int M>
 __device__ __forceinline__ bool pd_consume(PdSmem& S, const PdGemv& g, const int8_t* xs, const uint16_t* xds,
                                            int& it, int& hn, float* out, int ldo, bool resid, bool keys,
-                                           int8_t* hq, uint16_t* hd, int* err) {
+                                           int8_t* hq, uint16_t* hd, int* err, int u_first = -1,
+                                           float res_first = 0.0f) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int sw = (lane >> 2) & 1;
     const int K = g.K, nb = K >> 5;
@@ -353,12 +364,15 @@ __device__ __forceinline__ bool pd_consume(PdSmem& S, const PdGemv& g, const int
                 failed = true;
             }
         }
-        // the residual of the output this lane writes (lane 8r + m: row 2w + r, token m), read
-        // now so that its L2 round trip overlaps the unit
+        // the residual of the output this lane writes: loaded ahead (the caller loads the first
+        // unit's before the phase, each unit the next one's), so no unit waits on its L2 round
+        // trip; units arrive in the dealt order u_first, u_first + gridDim.x, ...
         float res = 0.0f;
-        if (resid && !g.swi && (lane & 7) < M && 2 * warp + (lane >> 3) < min(PD_ROWS, nout - u * PD_ROWS) &&
-            lane < 16)
-            res = __ldcg(out + (size_t)(lane & 7) * ldo + u * PD_ROWS + 2 * warp + (lane >> 3));
+        if (resid && !g.swi) {
+            res = u == u_first ? res_first : pd_res_lane<M>(out, ldo, nout, u);
+            u_first = u + (int)gridDim.x;
+            res_first = pd_res_lane<M>(out, ldo, nout, u_first);
+        }
         for (int grp = 0; grp < halves && !failed; grp++)
         for (int half = 0; half < halves && !failed; half++) {
             const int r0 = u * pd_unit_rows(g) + grp * PD_ROWS;
@@ -780,6 +794,13 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
     };
     int it = 0, hn = 0;
     unsigned epoch = 0;
+    // the consumers' copy of the producer's running unit offset (phase k of layer l starts at
+    // position l * per_layer + before[k] of the dealt sequence)
+    unsigned per_layer = 0, before[4];
+    for (int k = PH_QKV; k <= PH_DN; k++) {
+        before[k] = per_layer;
+        per_layer += (unsigned)pd_units(pd_gemv(p, 0, k));
+    }
     pd_prefetch(nws, p.layers[0].in_norm, H * 2, tid);
     for (int l = 0; l < p.n_layers; l++) {
         const PdLayer& L = p.layers[l];
@@ -791,6 +812,9 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
         // the first attention item's cache rows start loading before the barrier
         const int first = pd_attention_begin<M>(p, L, A, p0, nsplit);
         if (!pd_grid_barrier(p, S, epoch)) return;
+        // x is final until the o phase writes it: the first o unit's residual loads now
+        const int u_o = pd_first((unsigned)l * per_layer + before[PH_O]);
+        const float res_o = pd_res_lane<M>(p.x, H, H, u_o);
         // attention -> Q8_0 rows
         pd_attention<M>(p, L, S, A, p0, nsplit, pd_att_ctr(p, M, l, 0), pd_att_ctr(p, M, l, 1),
                         (unsigned)((l + 1) * nsplit), first);
@@ -803,11 +827,14 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
             cp_async_wait<0>();
             pd_csync();
             if (!pd_consume<M>(S, pd_gemv(p, l, PH_O), xs, xds, it, hn, p.x, H, true, false, nullptr, nullptr,
-                               p.err))
+                               p.err, u_o, res_o))
                 return;
         }
         pd_prefetch(nws, L.post_norm, H * 2, tid);
         if (!pd_grid_barrier(p, S, epoch)) return;
+        // x is final until the down phase writes it: the first down unit's residual loads now
+        const int u_dn = pd_first((unsigned)l * per_layer + before[PH_DN]);
+        const float res_dn = pd_res_lane<M>(p.x, H, H, u_dn);
         // GU: post-attention RMSNorm, gate|up, SiLU(gate)*up -> h as Q8_0
         norm_rows();
         if (!pd_consume<M>(S, pd_gemv(p, l, PH_GU), xs, xds, it, hn, nullptr, 0, false, false, p.hq, p.hd, p.err))
@@ -818,7 +845,8 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
         pd_prefetch(xds, p.hd, M * (I / 32) * 2, tid);
         cp_async_wait<0>();
         pd_csync();
-        if (!pd_consume<M>(S, pd_gemv(p, l, PH_DN), xs, xds, it, hn, p.x, H, true, false, nullptr, nullptr, p.err))
+        if (!pd_consume<M>(S, pd_gemv(p, l, PH_DN), xs, xds, it, hn, p.x, H, true, false, nullptr, nullptr, p.err,
+                           u_dn, res_dn))
             return;
         pd_prefetch(nws, l + 1 < p.n_layers ? p.layers[l + 1].in_norm : p.final_norm, H * 2, tid);
         if (!pd_grid_barrier(p, S, epoch)) return;
