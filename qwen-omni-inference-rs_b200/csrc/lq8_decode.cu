@@ -13,10 +13,10 @@
 // The consumer warps walk the phases, with a grid barrier (a global counter, bounded spin)
 // wherever a phase reads what other CTAs wrote:
 //   QKV  RMSNorm + Q8_0 of x (every CTA, redundantly), q|k|v rows                      | barrier
-//   ATT  items (row, kv head, 64-position chunk): q/k RMSNorm + RoPE, the new position's
-//        k/v appended to the caches, scores, chunk softmax, P.V -> published partials;
-//        then merge tasks (row, q head), taken by CTAs out of items, each waiting for its
-//        kv head's chunks: merge, Q8_0 of the head's output                            | barrier
+//   ATT  runs of 64-position chunks of one (row, kv head): q/k RMSNorm + RoPE once per run,
+//        the new position's k/v appended to the caches, per chunk scores, softmax, P.V ->
+//        published partials; then merge tasks (row, q head), taken by CTAs out of runs, each
+//        waiting for its kv head's chunks: merge, Q8_0 of the head's output             | barrier
 //   O    o rows + residual -> x                                                       | barrier
 //   GU   RMSNorm prologue, gate|up rows, SiLU(gate)*up -> h, quantized per unit      | barrier
 //   DN   h (Q8_0) as activations, down rows + residual -> x                           | barrier
@@ -24,7 +24,7 @@
 // GEMV units (16 output rows; 32 for gate|up, one Q8_0 block of h) are dealt to CTAs
 // round-robin over one sequence that runs through all phases, so the CTAs' totals differ by
 // one unit; the producer tags each stage with its unit and closes each phase with a marker
-// stage. Attention items are claimed from a per-layer counter as CTAs become free.
+// stage. Attention runs are dealt statically (CTA c: runs c, c + gridDim.x, ...).
 // Every arithmetic step is the one of the five-kernel decode path (the same row functions,
 // the same per-lane block order and warp sums, the same attention order), so the logits are
 // bit-identical to it. Data written by other CTAs is read through L2 (ld.cg / cp.async.cg).
@@ -85,7 +85,8 @@ struct PdParams {
     float* logits;             // [M][V]
     unsigned long long* keys;  // [M]
     unsigned* bar;             // [0] grid barrier, [1 + b*Hkv + kvh] published-chunk counters,
-                               // then per layer the chunk-item and merge-task counters; zero at launch
+                               // then per layer two counters (the second: merge tasks; the first is
+                               // unused since runs are dealt statically); zero at launch
     int* err;
 };
 
@@ -96,6 +97,7 @@ struct PdAtt {
     float qraw[PD_MAX_G][128];
     float qs[PD_MAX_G][PD_KS];  // padded like ks: the lanes of different heads hit different banks
     float kvraw[2][128];
+    float knew[128];  // the new position's normed, rotated k
     float ps[PD_MAX_G][PD_ATT_C + 4];  // padded: heads g and g' read position j in different banks
     float ml[PD_MAX_G][2];
     float cm[PD_MAX_G][PD_MAX_SPLITS];
@@ -156,7 +158,7 @@ __device__ __forceinline__ int pd_units(const PdGemv& g) {
     const int nout = g.swi ? g.N / 2 : g.N;
     return (nout + pd_unit_rows(g) - 1) / pd_unit_rows(g);
 }
-// attention chunk-item (k = 0) and merge-task (k = 1) counters of layer l
+// the two per-layer counters of layer l (k = 1: merge tasks; k = 0 is unused)
 __device__ __forceinline__ unsigned* pd_att_ctr(const PdParams& p, int M, int l, int k) {
     return p.bar + 1 + M * p.Hkv + 2 * l + k;
 }
@@ -465,16 +467,36 @@ __device__ __forceinline__ bool pd_consume(PdSmem& S, const PdGemv& g, const int
 
 // ---- attention (the decode attention kernel's arithmetic, on 256 threads) ----
 
-// an attention item's K (which = 0) or V (which = 1) cache rows of earlier steps (those before
-// the new position) into the staging area, every copy in flight; they depend on nothing this
-// step computes
-__device__ __forceinline__ void pd_item_rows(const PdParams& p, const PdLayer& L, PdAtt& A, int p0, int nsplit,
-                                             int item, int which) {
-    const int D = 128, Hkv = p.Hkv;
-    const int split = item % nsplit, kvh = (item / nsplit) % Hkv, b = item / (nsplit * Hkv);
+// Attention work is split into runs: run r covers chunks [c0, c1) of one (row b, kv head) pair.
+// Runs are sized so that there are at most gridDim.x of them (about gridDim.x / (M * Hkv) runs
+// per pair), and CTA c takes runs c, c + gridDim.x, ...: q is loaded, normed and rotated once per
+// run, and the chunks of a run follow each other with the next chunk's cache rows copied in
+// while the current one is computed.
+struct PdRuns {
+    int len;      // chunks per run (the last run of a pair may hold fewer)
+    int per_seq;  // runs per (row, kv head) pair
+    int n;        // runs in all
+};
+__device__ __forceinline__ PdRuns pd_runs(int M, int Hkv, int nsplit) {
+    PdRuns r;
+    const int pairs = M * Hkv;
+    const int per_pair = max(1, (int)gridDim.x / pairs);
+    r.len = (nsplit + per_pair - 1) / per_pair;
+    r.per_seq = (nsplit + r.len - 1) / r.len;
+    r.n = pairs * r.per_seq;
+    return r;
+}
+
+// the K (which = 0) or V (which = 1) cache rows of earlier steps (those before the new
+// position) of chunk `split` of (row b, kv head kvh) into the staging area, every copy in
+// flight; they depend on nothing this step computes
+__device__ __forceinline__ void pd_chunk_rows(const PdParams& p, const PdLayer& L, PdAtt& A, int p0, int b, int kvh,
+                                              int split, int which) {
+    const int D = 128;
     const int j0 = split * PD_ATT_C;
     const int rows = min(PD_ATT_C, p0 - j0);  // the new position's row is computed, not copied
-    const float* base = (which ? L.vc : L.kc) + ((int64_t)b * Hkv + kvh) * (int64_t)p.ctx_max * D + (int64_t)j0 * D;
+    const float* base =
+        (which ? L.vc : L.kc) + ((int64_t)b * p.Hkv + kvh) * (int64_t)p.ctx_max * D + (int64_t)j0 * D;
     for (int i = threadIdx.x; i < rows * (D / 4); i += PD_CTHREADS) {
         const int r = i / (D / 4), c = (i % (D / 4)) * 4;
         cp_async16(which ? &A.vs[r][c] : &A.ks[r][c], base + (int64_t)r * D + c, true);
@@ -482,48 +504,43 @@ __device__ __forceinline__ void pd_item_rows(const PdParams& p, const PdLayer& L
     cp_async_commit();
 }
 
-// this CTA's first attention item of the layer is item blockIdx.x (later items are claimed from
-// the layer's counter, offset by the grid size); its cache-row copies start here, before the
-// grid barrier that precedes attention, so they overlap it
-template <int M>
-__device__ __forceinline__ int pd_attention_begin(const PdParams& p, const PdLayer& L, PdAtt& A, int p0,
-                                                  int nsplit) {
-    const int item = (int)blockIdx.x;
-    if (item < M * p.Hkv * nsplit) {
-        pd_item_rows(p, L, A, p0, nsplit, item, 0);
-        pd_item_rows(p, L, A, p0, nsplit, item, 1);
-    }
-    return item;
+// the first chunk of run `run` (if it exists): its K or V rows
+__device__ __forceinline__ void pd_run_rows(const PdParams& p, const PdLayer& L, PdAtt& A, int p0, const PdRuns& R,
+                                            int run, int which) {
+    if (run >= R.n) return;
+    const int pair = run / R.per_seq;
+    pd_chunk_rows(p, L, A, p0, pair / p.Hkv, pair % p.Hkv, (run % R.per_seq) * R.len, which);
 }
 
-// ctr / mctr: this layer's chunk-item and merge-task counters; target: the chunk counters'
-// value once this layer's chunks are all published ((layer + 1) * nsplit); first: the item
-// claimed by pd_attention_begin (its cache-row copies already in flight)
+// this CTA's first run of the layer is run blockIdx.x; its first chunk's cache-row copies start
+// here, before the grid barrier that precedes attention, so they overlap it
+template <int M>
+__device__ __forceinline__ void pd_attention_begin(const PdParams& p, const PdLayer& L, PdAtt& A, int p0,
+                                                   int nsplit) {
+    const PdRuns R = pd_runs(M, p.Hkv, nsplit);
+    pd_run_rows(p, L, A, p0, R, (int)blockIdx.x, 0);
+    pd_run_rows(p, L, A, p0, R, (int)blockIdx.x, 1);
+}
+
+// mctr: this layer's merge-task counter; target: the published-chunk counters' value once
+// this layer's chunks are all published ((layer + 1) * nsplit). The first run's first chunk
+// rows are already in flight (pd_attention_begin).
 template <int M>
 __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdAtt& A, int p0, int nsplit,
-                             unsigned* ctr, unsigned* mctr, unsigned target, int first) {
+                             unsigned* mctr, unsigned target) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int Hq = p.Hq, Hkv = p.Hkv, G = Hq / Hkv, D = 128;
     const int heads = Hq + 2 * Hkv;
-    const int n_items = M * Hkv * nsplit;
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
     const float* cs = p.cos_t + (int64_t)p0 * (D / 2);
     const float* sn = p.sin_t + (int64_t)p0 * (D / 2);
-    // items after the first are claimed from the phase counter (claim c is item gridDim.x + c);
-    // the next claim is issued while this item runs, and the next item's K rows are copied in
-    // once this item's scores are done, its V rows once this item's P.V is done
-    int item = first;
-    while (item < n_items) {
-        int next = 0;
-        if (tid == 0) next = (int)gridDim.x + (int)atomicAdd(ctr, 1u);
-        const int split = item % nsplit, kvh = (item / nsplit) % Hkv, b = item / (nsplit * Hkv);
-        const int j0 = split * PD_ATT_C;
-        const int cnt = min(PD_ATT_C, p0 + 1 - j0);
-        const int fresh = p0 - j0;  // chunk row of the new position (when < cnt)
-        float* kbase = L.kc + ((int64_t)b * Hkv + kvh) * (int64_t)p.ctx_max * D + (int64_t)j0 * D;
-        float* vbase = L.vc + ((int64_t)b * Hkv + kvh) * (int64_t)p.ctx_max * D + (int64_t)j0 * D;
-        pd_csync();  // the previous item is done with q, the raw rows and the scores
-        // this kv head's q heads (and, for the chunk of the new position, its k and v) from
+    const PdRuns R = pd_runs(M, Hkv, nsplit);
+    for (int run = (int)blockIdx.x; run < R.n; run += (int)gridDim.x) {
+        const int pair = run / R.per_seq, b = pair / Hkv, kvh = pair % Hkv;
+        const int c0 = (run % R.per_seq) * R.len, c1 = min(nsplit, c0 + R.len);
+        const bool has_new = c1 == nsplit;  // the run holds the chunk of the new position
+        pd_csync();  // the previous run is done with q and the raw rows
+        // this kv head's q heads (and, for the run holding the new position, its k and v) from
         // the q|k|v rows
         const float* qrow = p.qkv + (int64_t)b * heads * D;
         for (int i = tid; i < G * (D / 4); i += PD_CTHREADS) {
@@ -531,7 +548,6 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
             *reinterpret_cast<float4*>(&A.qraw[g][c]) =
                 __ldcg(reinterpret_cast<const float4*>(qrow + (int64_t)(kvh * G + g) * D + c));
         }
-        const bool has_new = fresh >= 0 && fresh < cnt;
         if (has_new && tid < 2 * (D / 4)) {
             const int which = tid / (D / 4), c = (tid % (D / 4)) * 4;  // 0: k, 1: v
             *reinterpret_cast<float4*>(&A.kvraw[which][c]) =
@@ -540,112 +556,123 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
         pd_csync();
         for (int g = warp; g < G; g += PD_CONS) head_norm_rope(A.qraw[g], L.q_norm, p.eps, cs, sn, lane, A.qs[g]);
         if (has_new) {
+            // the new position's k (normed, rotated) and v: into the caches now, into the
+            // staging rows when their chunk comes
+            const int64_t prow = ((int64_t)b * Hkv + kvh) * (int64_t)p.ctx_max * D + (int64_t)p0 * D;
             if (warp == 0) {
-                head_norm_rope(A.kvraw[0], L.k_norm, p.eps, cs, sn, lane, A.ks[fresh]);
+                head_norm_rope(A.kvraw[0], L.k_norm, p.eps, cs, sn, lane, A.knew);
                 __syncwarp();
-                const float4 kk = *reinterpret_cast<const float4*>(&A.ks[fresh][lane * 4]);
-                *reinterpret_cast<float4*>(kbase + (int64_t)fresh * D + lane * 4) = kk;
+                *reinterpret_cast<float4*>(L.kc + prow + lane * 4) = *reinterpret_cast<const float4*>(&A.knew[lane * 4]);
             } else if (warp == 1) {
-                const float4 vv = *reinterpret_cast<const float4*>(&A.kvraw[1][lane * 4]);
-                *reinterpret_cast<float4*>(&A.vs[fresh][lane * 4]) = vv;
-                *reinterpret_cast<float4*>(vbase + (int64_t)fresh * D + lane * 4) = vv;
+                *reinterpret_cast<float4*>(L.vc + prow + lane * 4) = *reinterpret_cast<const float4*>(&A.kvraw[1][lane * 4]);
             }
         }
-        cp_async_wait<0>();
-        pd_csync();
-        // scores: thread -> (position pp, head g), heads fastest, so the G lanes of a position
-        // read the same K address and the lanes of a head the same q address (shared-memory
-        // broadcasts: a K row is fetched once for all heads of the group); one multiply-add chain
-        // over the 128 dims, then the scale. K and q are read 32 dims at a time into registers
-        // ahead of the chain.
-        for (int idx = tid; idx < PD_ATT_C * G; idx += PD_CTHREADS) {
-            const int pp = idx / G, g = idx - pp * G;
-            float s = 0.f;
-            if (pp < cnt) {
+        for (int split = c0; split < c1; split++) {
+            const int j0 = split * PD_ATT_C;
+            const int cnt = min(PD_ATT_C, p0 + 1 - j0);
+            const int fresh = p0 - j0;  // chunk row of the new position (when < cnt)
+            cp_async_wait<0>();
+            pd_csync();  // q (and the new k) ready, the chunk's rows landed
+            if (fresh < cnt && tid < 2 * (D / 4)) {
+                const int which = tid / (D / 4), c = (tid % (D / 4)) * 4;
+                const float4 v = *reinterpret_cast<const float4*>(which ? &A.kvraw[1][c] : &A.knew[c]);
+                *reinterpret_cast<float4*>(which ? &A.vs[fresh][c] : &A.ks[fresh][c]) = v;
+            }
+            if (fresh < cnt) pd_csync();
+            // scores: thread -> (position pp, head g), heads fastest, so the G lanes of a position
+            // read the same K address and the lanes of a head the same q address (shared-memory
+            // broadcasts: a K row is fetched once for all heads of the group); one multiply-add chain
+            // over the 128 dims, then the scale. K and q are read 32 dims at a time into registers
+            // ahead of the chain.
+            for (int idx = tid; idx < PD_ATT_C * G; idx += PD_CTHREADS) {
+                const int pp = idx / G, g = idx - pp * G;
+                float s = 0.f;
+                if (pp < cnt) {
 #pragma unroll
-                for (int d0 = 0; d0 < D; d0 += 32) {
-                    float4 kk[8], qq[8];
+                    for (int d0 = 0; d0 < D; d0 += 32) {
+                        float4 kk[8], qq[8];
 #pragma unroll
-                    for (int i = 0; i < 8; i++) kk[i] = *reinterpret_cast<const float4*>(&A.ks[pp][d0 + 4 * i]);
+                        for (int i = 0; i < 8; i++) kk[i] = *reinterpret_cast<const float4*>(&A.ks[pp][d0 + 4 * i]);
 #pragma unroll
-                    for (int i = 0; i < 8; i++) qq[i] = *reinterpret_cast<const float4*>(&A.qs[g][d0 + 4 * i]);
+                        for (int i = 0; i < 8; i++) qq[i] = *reinterpret_cast<const float4*>(&A.qs[g][d0 + 4 * i]);
 #pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        s = fmaf(qq[i].x, kk[i].x, s);
-                        s = fmaf(qq[i].y, kk[i].y, s);
-                        s = fmaf(qq[i].z, kk[i].z, s);
-                        s = fmaf(qq[i].w, kk[i].w, s);
+                        for (int i = 0; i < 8; i++) {
+                            s = fmaf(qq[i].x, kk[i].x, s);
+                            s = fmaf(qq[i].y, kk[i].y, s);
+                            s = fmaf(qq[i].z, kk[i].z, s);
+                            s = fmaf(qq[i].w, kk[i].w, s);
+                        }
                     }
                 }
+                A.ps[g][pp] = pp < cnt ? __fmul_rn(s, scale) : -INFINITY;
             }
-            A.ps[g][pp] = pp < cnt ? __fmul_rn(s, scale) : -INFINITY;
-        }
-        if (tid == 0) S.item = next;
-        pd_csync();
-        // K is free: the next item's K rows start loading
-        const int nx = S.item;
-        if (nx < n_items) pd_item_rows(p, L, A, p0, nsplit, nx, 0);
-        // chunk softmax per head: max, exp(s - max), sum
-        for (int g = warp; g < G; g += PD_CONS) {
-            const float a = A.ps[g][lane], c = A.ps[g][lane + 32];
-            const float mx = warp_max(fmaxf(a, c));
-            const float ea = expf(__fsub_rn(a, mx)), ec = expf(__fsub_rn(c, mx));
-            A.ps[g][lane] = ea;
-            A.ps[g][lane + 32] = ec;
-            const float sum = warp_sum(__fadd_rn(ea, ec));
-            if (lane == 0) { A.ml[g][0] = mx; A.ml[g][1] = sum; }
-        }
-        pd_csync();
-        // chunk P.V: thread -> (dims 4c..4c+3, head g), heads fastest, so the G lanes of a dim
-        // group read the same V address and the lanes of a head the same P address; per output
-        // one multiply-add chain over the positions in order, 8 at a time with their V and P
-        // values read ahead
-        const int64_t hb0 = ((int64_t)b * Hq + (int64_t)kvh * G) * PD_MAX_SPLITS;
-        {
-            for (int idx = tid; idx < (D / 4) * G; idx += PD_CTHREADS) {
-                const int c4 = idx / G, g = idx - c4 * G;
-                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                int j0 = 0;
+            pd_csync();
+            // K is free: the next chunk's K rows start loading (this run's next chunk, else the
+            // first chunk of this CTA's next run)
+            if (split + 1 < c1) pd_chunk_rows(p, L, A, p0, b, kvh, split + 1, 0);
+            else pd_run_rows(p, L, A, p0, R, run + (int)gridDim.x, 0);
+            // chunk softmax per head: max, exp(s - max), sum
+            for (int g = warp; g < G; g += PD_CONS) {
+                const float a = A.ps[g][lane], c = A.ps[g][lane + 32];
+                const float mx = warp_max(fmaxf(a, c));
+                const float ea = expf(__fsub_rn(a, mx)), ec = expf(__fsub_rn(c, mx));
+                A.ps[g][lane] = ea;
+                A.ps[g][lane + 32] = ec;
+                const float sum = warp_sum(__fadd_rn(ea, ec));
+                if (lane == 0) { A.ml[g][0] = mx; A.ml[g][1] = sum; }
+            }
+            pd_csync();
+            // chunk P.V: thread -> (dims 4c..4c+3, head g), heads fastest, so the G lanes of a dim
+            // group read the same V address and the lanes of a head the same P address; per output
+            // one multiply-add chain over the positions in order, 8 at a time with their V and P
+            // values read ahead
+            const int64_t hb0 = ((int64_t)b * Hq + (int64_t)kvh * G) * PD_MAX_SPLITS;
+            {
+                for (int idx = tid; idx < (D / 4) * G; idx += PD_CTHREADS) {
+                    const int c4 = idx / G, g = idx - c4 * G;
+                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                    int j0 = 0;
 #pragma unroll 1
-                for (; j0 + 8 <= cnt; j0 += 8) {
-                    float4 vv[8];
+                    for (; j0 + 8 <= cnt; j0 += 8) {
+                        float4 vv[8];
 #pragma unroll
-                    for (int j = 0; j < 8; j++) vv[j] = *reinterpret_cast<const float4*>(&A.vs[j0 + j][4 * c4]);
-                    const float4 pa = *reinterpret_cast<const float4*>(&A.ps[g][j0]);
-                    const float4 pb = *reinterpret_cast<const float4*>(&A.ps[g][j0 + 4]);
-                    const float pj[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+                        for (int j = 0; j < 8; j++) vv[j] = *reinterpret_cast<const float4*>(&A.vs[j0 + j][4 * c4]);
+                        const float4 pa = *reinterpret_cast<const float4*>(&A.ps[g][j0]);
+                        const float4 pb = *reinterpret_cast<const float4*>(&A.ps[g][j0 + 4]);
+                        const float pj[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
 #pragma unroll
-                    for (int j = 0; j < 8; j++) {
-                        acc.x = fmaf(pj[j], vv[j].x, acc.x);
-                        acc.y = fmaf(pj[j], vv[j].y, acc.y);
-                        acc.z = fmaf(pj[j], vv[j].z, acc.z);
-                        acc.w = fmaf(pj[j], vv[j].w, acc.w);
+                        for (int j = 0; j < 8; j++) {
+                            acc.x = fmaf(pj[j], vv[j].x, acc.x);
+                            acc.y = fmaf(pj[j], vv[j].y, acc.y);
+                            acc.z = fmaf(pj[j], vv[j].z, acc.z);
+                            acc.w = fmaf(pj[j], vv[j].w, acc.w);
+                        }
                     }
+                    for (int j = j0; j < cnt; j++) {
+                        const float4 vv = *reinterpret_cast<const float4*>(&A.vs[j][4 * c4]);
+                        const float pj = A.ps[g][j];
+                        acc.x = fmaf(pj, vv.x, acc.x);
+                        acc.y = fmaf(pj, vv.y, acc.y);
+                        acc.z = fmaf(pj, vv.z, acc.z);
+                        acc.w = fmaf(pj, vv.w, acc.w);
+                    }
+                    *reinterpret_cast<float4*>(&p.part_o[(hb0 + (int64_t)g * PD_MAX_SPLITS + split) * D + 4 * c4]) = acc;
                 }
-                for (int j = j0; j < cnt; j++) {
-                    const float4 vv = *reinterpret_cast<const float4*>(&A.vs[j][4 * c4]);
-                    const float pj = A.ps[g][j];
-                    acc.x = fmaf(pj, vv.x, acc.x);
-                    acc.y = fmaf(pj, vv.y, acc.y);
-                    acc.z = fmaf(pj, vv.z, acc.z);
-                    acc.w = fmaf(pj, vv.w, acc.w);
+                if (tid < G) {
+                    p.part_ml[(hb0 + (int64_t)tid * PD_MAX_SPLITS + split) * 2] = A.ml[tid][0];
+                    p.part_ml[(hb0 + (int64_t)tid * PD_MAX_SPLITS + split) * 2 + 1] = A.ml[tid][1];
                 }
-                *reinterpret_cast<float4*>(&p.part_o[(hb0 + (int64_t)g * PD_MAX_SPLITS + split) * D + 4 * c4]) = acc;
             }
-            if (tid < G) {
-                p.part_ml[(hb0 + (int64_t)tid * PD_MAX_SPLITS + split) * 2] = A.ml[tid][0];
-                p.part_ml[(hb0 + (int64_t)tid * PD_MAX_SPLITS + split) * 2 + 1] = A.ml[tid][1];
-            }
+            pd_csync();  // V is free: the next chunk's V rows start loading
+            if (split + 1 < c1) pd_chunk_rows(p, L, A, p0, b, kvh, split + 1, 1);
+            else pd_run_rows(p, L, A, p0, R, run + (int)gridDim.x, 1);
         }
-        // publish the chunk: the (row, kv head)'s counter grows by nsplit per layer
+        // publish the run's chunks: the (row, kv head)'s counter grows by nsplit per layer
         __threadfence();
         pd_csync();
-        if (tid == 0) atomicAdd(p.bar + 1 + b * Hkv + kvh, 1u);
-        // V is free: the next item's V rows start loading
-        if (nx < n_items) pd_item_rows(p, L, A, p0, nsplit, nx, 1);
-        item = nx;
+        if (tid == 0) atomicAdd(p.bar + 1 + b * Hkv + kvh, (unsigned)(c1 - c0));
     }
-    // merge tasks (row, q head), claimed by CTAs that ran out of chunk items: wait until the
+    // merge tasks (row, q head), claimed by CTAs that ran out of runs: wait until the
     // kv head's chunks of this layer are all published, then merge them (rescale by
     // exp(m_s - max), sum in chunk order, divide) and write the head's Q8_0 output
     const int n_tasks = M * Hq;
@@ -810,14 +837,13 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
                            nullptr, p.err))
             return;
         // the first attention item's cache rows start loading before the barrier
-        const int first = pd_attention_begin<M>(p, L, A, p0, nsplit);
+        pd_attention_begin<M>(p, L, A, p0, nsplit);
         if (!pd_grid_barrier(p, S, epoch)) return;
         // x is final until the o phase writes it: the first o unit's residual loads now
         const int u_o = pd_first((unsigned)l * per_layer + before[PH_O]);
         const float res_o = pd_res_lane<M>(p.x, H, H, u_o);
         // attention -> Q8_0 rows
-        pd_attention<M>(p, L, S, A, p0, nsplit, pd_att_ctr(p, M, l, 0), pd_att_ctr(p, M, l, 1),
-                        (unsigned)((l + 1) * nsplit), first);
+        pd_attention<M>(p, L, S, A, p0, nsplit, pd_att_ctr(p, M, l, 1), (unsigned)((l + 1) * nsplit));
         if (!pd_grid_barrier(p, S, epoch)) return;
         // O: the attention output as activations, residual into x
         {
