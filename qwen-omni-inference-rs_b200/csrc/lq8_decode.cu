@@ -84,9 +84,8 @@ struct PdParams {
     float* part_ml;            // [M][Hq][PD_MAX_SPLITS][2]
     float* logits;             // [M][V]
     unsigned long long* keys;  // [M]
-    unsigned* bar;             // [0] grid barrier, [1 + b*Hkv + kvh] published-chunk counters,
-                               // then per layer two counters (the second: merge tasks; the first is
-                               // unused since runs are dealt statically); zero at launch
+    unsigned* bar;             // [0] grid barrier, [1 + b*Hkv + kvh] published-chunk counters;
+                               // zero at launch
     int* err;
 };
 
@@ -115,7 +114,6 @@ struct alignas(128) PdSmem {
     uint64_t hfull[2];     // gate|up: hbuf[b] written by the 8 consumer warps
     uint64_t hfree[2];     // gate|up: hbuf[b] quantized by warp 0
     float hbuf[2][4][32];  // gate|up: one Q8_0 block of SiLU(gate)*up per row (two units in turn)
-    int item;              // attention: the next item of this CTA
     int flag;  // grid barrier outcome
     int fail;  // a consumer warp gave up waiting for a stage
     int pad_[2];
@@ -157,10 +155,6 @@ __device__ __forceinline__ int pd_unit_rows(const PdGemv& g) { return g.swi ? 2 
 __device__ __forceinline__ int pd_units(const PdGemv& g) {
     const int nout = g.swi ? g.N / 2 : g.N;
     return (nout + pd_unit_rows(g) - 1) / pd_unit_rows(g);
-}
-// the two per-layer counters of layer l (k = 1: merge tasks; k = 0 is unused)
-__device__ __forceinline__ unsigned* pd_att_ctr(const PdParams& p, int M, int l, int k) {
-    return p.bar + 1 + M * p.Hkv + 2 * l + k;
 }
 
 __device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
@@ -522,12 +516,12 @@ __device__ __forceinline__ void pd_attention_begin(const PdParams& p, const PdLa
     pd_run_rows(p, L, A, p0, R, (int)blockIdx.x, 1);
 }
 
-// mctr: this layer's merge-task counter; target: the published-chunk counters' value once
+// target: the published-chunk counters' value once
 // this layer's chunks are all published ((layer + 1) * nsplit). The first run's first chunk
 // rows are already in flight (pd_attention_begin).
 template <int M>
 __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdAtt& A, int p0, int nsplit,
-                             unsigned* mctr, unsigned target) {
+                             unsigned target) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int Hq = p.Hq, Hkv = p.Hkv, G = Hq / Hkv, D = 128;
     const int heads = Hq + 2 * Hkv;
@@ -571,8 +565,8 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
             const int j0 = split * PD_ATT_C;
             const int cnt = min(PD_ATT_C, p0 + 1 - j0);
             const int fresh = p0 - j0;  // chunk row of the new position (when < cnt)
-            cp_async_wait<0>();
-            pd_csync();  // q (and the new k) ready, the chunk's rows landed
+            cp_async_wait<1>();  // the chunk's K rows (its V rows, committed after them, may still fly)
+            pd_csync();  // q (and the new k) ready, the chunk's K rows landed
             if (fresh < cnt && tid < 2 * (D / 4)) {
                 const int which = tid / (D / 4), c = (tid % (D / 4)) * 4;
                 const float4 v = *reinterpret_cast<const float4*>(which ? &A.kvraw[1][c] : &A.knew[c]);
@@ -621,6 +615,7 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
                 const float sum = warp_sum(__fadd_rn(ea, ec));
                 if (lane == 0) { A.ml[g][0] = mx; A.ml[g][1] = sum; }
             }
+            cp_async_wait<0>();  // the chunk's V rows
             pd_csync();
             // chunk P.V: thread -> (dims 4c..4c+3, head g), heads fastest, so the G lanes of a dim
             // group read the same V address and the lanes of a head the same P address; per output
@@ -672,16 +667,13 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
         pd_csync();
         if (tid == 0) atomicAdd(p.bar + 1 + b * Hkv + kvh, (unsigned)(c1 - c0));
     }
-    // merge tasks (row, q head), claimed by CTAs that ran out of runs: wait until the
-    // kv head's chunks of this layer are all published, then merge them (rescale by
-    // exp(m_s - max), sum in chunk order, divide) and write the head's Q8_0 output
+    // merge tasks (row, q head), dealt from the highest CTA down (CTA c: task gridDim.x - 1 - c,
+    // then every gridDim.x-th), so the CTAs without runs take the first ones and no CTA holds two
+    // while another holds none: wait until the kv head's chunks of this layer are all published,
+    // then merge them (rescale by exp(m_s - max), sum in chunk order, divide) and write the head's
+    // Q8_0 output
     const int n_tasks = M * Hq;
-    if (tid == 0) S.item = (int)atomicAdd(mctr, 1u);
-    pd_csync();
-    int task = S.item;
-    while (task < n_tasks) {
-        int next = 0;
-        if (tid == 0) next = (int)atomicAdd(mctr, 1u);
+    for (int task = (int)gridDim.x - 1 - (int)blockIdx.x; task < n_tasks; task += (int)gridDim.x) {
         const int b = task / Hq, head = task % Hq, kvh = head / G;
         const int64_t hb = ((int64_t)b * Hq + head) * PD_MAX_SPLITS;
         if (tid == 0) {
@@ -745,9 +737,7 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
                 pd_quant_warp32(o, lane, p.att_q + (e - lane), p.att_d + (e >> 5));
             }
         }
-        if (tid == 0) S.item = next;
-        pd_csync();
-        task = S.item;
+        pd_csync();  // the staging area is free for the next task
     }
 }
 
@@ -843,7 +833,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
         const int u_o = pd_first((unsigned)l * per_layer + before[PH_O]);
         const float res_o = pd_res_lane<M>(p.x, H, H, u_o);
         // attention -> Q8_0 rows
-        pd_attention<M>(p, L, S, A, p0, nsplit, pd_att_ctr(p, M, l, 1), (unsigned)((l + 1) * nsplit));
+        pd_attention<M>(p, L, S, A, p0, nsplit, (unsigned)((l + 1) * nsplit));
         if (!pd_grid_barrier(p, S, epoch)) return;
         // O: the attention output as activations, residual into x
         {
@@ -910,7 +900,8 @@ bool decode_persist_supported(lq_ctx* ctx, int64_t m, int64_t H, int64_t Hq, int
 size_t decode_persist_desc_bytes(int64_t n_layers) { return (size_t)(n_layers + 1) * sizeof(PdLayer); }
 size_t decode_persist_part_bytes(int64_t m, int64_t Hq) { return (size_t)(m * Hq * PD_MAX_SPLITS) * (128 + 2) * 4; }
 size_t decode_persist_counter_bytes(int64_t m, int64_t Hkv, int64_t n_layers) {
-    return (size_t)(1 + m * Hkv + 2 * n_layers) * 4;
+    (void)n_layers;
+    return (size_t)(1 + m * Hkv) * 4;
 }
 
 static int pd_map(lq_ctx* ctx, PdMat* out, const lq_q8_tensor& w) {
