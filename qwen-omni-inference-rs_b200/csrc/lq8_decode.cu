@@ -483,27 +483,33 @@ __device__ __forceinline__ PdRuns pd_runs(int M, int Hkv, int nsplit) {
 
 // the K (which = 0) or V (which = 1) cache rows of earlier steps (those before the new
 // position) of chunk `split` of (row b, kv head kvh) into the staging area, every copy in
-// flight; they depend on nothing this step computes
+// flight, issued by the consumer threads from t0 on; they depend on nothing this step
+// computes. Every consumer thread commits one cp.async group per call (an empty one when it
+// issues nothing), so the groups line up across threads and cp_async_wait<1> means "all but
+// the most recent call's copies".
 __device__ __forceinline__ void pd_chunk_rows(const PdParams& p, const PdLayer& L, PdAtt& A, int p0, int b, int kvh,
-                                              int split, int which) {
+                                              int split, int which, int t0) {
     const int D = 128;
     const int j0 = split * PD_ATT_C;
     const int rows = min(PD_ATT_C, p0 - j0);  // the new position's row is computed, not copied
     const float* base =
         (which ? L.vc : L.kc) + ((int64_t)b * p.Hkv + kvh) * (int64_t)p.ctx_max * D + (int64_t)j0 * D;
-    for (int i = threadIdx.x; i < rows * (D / 4); i += PD_CTHREADS) {
+    for (int i = threadIdx.x - t0; i >= 0 && i < rows * (D / 4); i += PD_CTHREADS - t0) {
         const int r = i / (D / 4), c = (i % (D / 4)) * 4;
         cp_async16(which ? &A.vs[r][c] : &A.ks[r][c], base + (int64_t)r * D + c, true);
     }
     cp_async_commit();
 }
 
-// the first chunk of run `run` (if it exists): its K or V rows
+// the first chunk of run `run`: its K or V rows (an empty group when the run does not exist)
 __device__ __forceinline__ void pd_run_rows(const PdParams& p, const PdLayer& L, PdAtt& A, int p0, const PdRuns& R,
-                                            int run, int which) {
-    if (run >= R.n) return;
+                                            int run, int which, int t0) {
+    if (run >= R.n) {
+        cp_async_commit();
+        return;
+    }
     const int pair = run / R.per_seq;
-    pd_chunk_rows(p, L, A, p0, pair / p.Hkv, pair % p.Hkv, (run % R.per_seq) * R.len, which);
+    pd_chunk_rows(p, L, A, p0, pair / p.Hkv, pair % p.Hkv, (run % R.per_seq) * R.len, which, t0);
 }
 
 // this CTA's first run of the layer is run blockIdx.x; its first chunk's cache-row copies start
@@ -512,8 +518,8 @@ template <int M>
 __device__ __forceinline__ void pd_attention_begin(const PdParams& p, const PdLayer& L, PdAtt& A, int p0,
                                                    int nsplit) {
     const PdRuns R = pd_runs(M, p.Hkv, nsplit);
-    pd_run_rows(p, L, A, p0, R, (int)blockIdx.x, 0);
-    pd_run_rows(p, L, A, p0, R, (int)blockIdx.x, 1);
+    pd_run_rows(p, L, A, p0, R, (int)blockIdx.x, 0, 0);
+    pd_run_rows(p, L, A, p0, R, (int)blockIdx.x, 1, 0);
 }
 
 // target: the published-chunk counters' value once
@@ -529,6 +535,7 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
     const float* cs = p.cos_t + (int64_t)p0 * (D / 2);
     const float* sn = p.sin_t + (int64_t)p0 * (D / 2);
     const PdRuns R = pd_runs(M, Hkv, nsplit);
+    const int kt0 = G < PD_CONS ? G * 32 : 0;  // the softmax runs on warps 0..G-1
     for (int run = (int)blockIdx.x; run < R.n; run += (int)gridDim.x) {
         const int pair = run / R.per_seq, b = pair / Hkv, kvh = pair % Hkv;
         const int c0 = (run % R.per_seq) * R.len, c1 = min(nsplit, c0 + R.len);
@@ -602,9 +609,9 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
             }
             pd_csync();
             // K is free: the next chunk's K rows start loading (this run's next chunk, else the
-            // first chunk of this CTA's next run)
-            if (split + 1 < c1) pd_chunk_rows(p, L, A, p0, b, kvh, split + 1, 0);
-            else pd_run_rows(p, L, A, p0, R, run + (int)gridDim.x, 0);
+            // first chunk of this CTA's next run), issued by the warps the softmax leaves idle
+            if (split + 1 < c1) pd_chunk_rows(p, L, A, p0, b, kvh, split + 1, 0, kt0);
+            else pd_run_rows(p, L, A, p0, R, run + (int)gridDim.x, 0, kt0);
             // chunk softmax per head: max, exp(s - max), sum
             for (int g = warp; g < G; g += PD_CONS) {
                 const float a = A.ps[g][lane], c = A.ps[g][lane + 32];
@@ -615,7 +622,7 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
                 const float sum = warp_sum(__fadd_rn(ea, ec));
                 if (lane == 0) { A.ml[g][0] = mx; A.ml[g][1] = sum; }
             }
-            cp_async_wait<0>();  // the chunk's V rows
+            cp_async_wait<1>();  // the chunk's V rows (the next chunk's K rows may still fly)
             pd_csync();
             // chunk P.V: thread -> (dims 4c..4c+3, head g), heads fastest, so the G lanes of a dim
             // group read the same V address and the lanes of a head the same P address; per output
@@ -659,8 +666,8 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
                 }
             }
             pd_csync();  // V is free: the next chunk's V rows start loading
-            if (split + 1 < c1) pd_chunk_rows(p, L, A, p0, b, kvh, split + 1, 1);
-            else pd_run_rows(p, L, A, p0, R, run + (int)gridDim.x, 1);
+            if (split + 1 < c1) pd_chunk_rows(p, L, A, p0, b, kvh, split + 1, 1, 0);
+            else pd_run_rows(p, L, A, p0, R, run + (int)gridDim.x, 1, 0);
         }
         // publish the run's chunks: the (row, kv head)'s counter grows by nsplit per layer
         __threadfence();
