@@ -221,13 +221,19 @@ __device__ __forceinline__ bool pd_produce(PdSmem& S, const PdGemv& g, unsigned 
 // ---- consumers ----
 __device__ __forceinline__ void pd_csync() { group_sync<PD_CTHREADS, 1>(); }
 
-// grid barrier of the consumer groups: the k-th barrier completes when the counter reaches
-// k * gridDim.x. Returns false when it gave up (~2 s) or another CTA flagged an error.
-__device__ __forceinline__ bool pd_grid_barrier(const PdParams& p, PdSmem& S, unsigned& epoch) {
+// grid barrier of the consumer groups, split in two: pd_grid_arrive publishes this CTA's
+// writes (release) and counts it in; pd_grid_wait returns once every CTA has arrived (the k-th
+// barrier completes when the counter reaches k * gridDim.x). Work that depends on no other
+// CTA's writes may run between the two. The wait returns false when it gave up (~2 s) or
+// another CTA flagged an error.
+__device__ __forceinline__ void pd_grid_arrive(const PdParams& p, unsigned& epoch) {
     pd_csync();
     epoch++;
+    if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
+}
+
+__device__ __forceinline__ bool pd_grid_wait(const PdParams& p, PdSmem& S, unsigned epoch) {
     if (threadIdx.x == 0) {
-        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
         const unsigned target = epoch * gridDim.x;
         const uint64_t t0 = global_ns();
         int ok = 1;
@@ -244,6 +250,11 @@ __device__ __forceinline__ bool pd_grid_barrier(const PdParams& p, PdSmem& S, un
     }
     pd_csync();
     return S.flag != 0;
+}
+
+__device__ __forceinline__ bool pd_grid_barrier(const PdParams& p, PdSmem& S, unsigned& epoch) {
+    pd_grid_arrive(p, epoch);
+    return pd_grid_wait(p, S, epoch);
 }
 
 // `bytes` (a multiple of 16) into shared memory through L2 with every 16-byte copy in flight;
@@ -834,8 +845,9 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
                            nullptr, p.err))
             return;
         // the first attention item's cache rows start loading before the barrier
+        pd_grid_arrive(p, epoch);
         pd_attention_begin<M>(p, L, A, p0, nsplit);
-        if (!pd_grid_barrier(p, S, epoch)) return;
+        if (!pd_grid_wait(p, S, epoch)) return;
         // x is final until the o phase writes it: the first o unit's residual loads now
         const int u_o = pd_first((unsigned)l * per_layer + before[PH_O]);
         const float res_o = pd_res_lane<M>(p.x, H, H, u_o);
@@ -853,8 +865,9 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
                                p.err, u_o, res_o))
                 return;
         }
+        pd_grid_arrive(p, epoch);
         pd_prefetch(nws, L.post_norm, H * 2, tid);
-        if (!pd_grid_barrier(p, S, epoch)) return;
+        if (!pd_grid_wait(p, S, epoch)) return;
         // x is final until the down phase writes it: the first down unit's residual loads now
         const int u_dn = pd_first((unsigned)l * per_layer + before[PH_DN]);
         const float res_dn = pd_res_lane<M>(p.x, H, H, u_dn);
@@ -871,8 +884,9 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
         if (!pd_consume<M>(S, pd_gemv(p, l, PH_DN), xs, xds, it, hn, p.x, H, true, false, nullptr, nullptr, p.err,
                            u_dn, res_dn))
             return;
+        pd_grid_arrive(p, epoch);
         pd_prefetch(nws, l + 1 < p.n_layers ? p.layers[l + 1].in_norm : p.final_norm, H * 2, tid);
-        if (!pd_grid_barrier(p, S, epoch)) return;
+        if (!pd_grid_wait(p, S, epoch)) return;
     }
     // LM head: final RMSNorm, logits, greedy argmax keys
     norm_rows();
