@@ -97,6 +97,8 @@ struct PdAtt {
     float qs[PD_MAX_G][PD_KS];  // padded like ks: the lanes of different heads hit different banks
     float kvraw[2][128];
     float knew[128];  // the new position's normed, rotated k
+    uint16_t qn[128], kn[128];  // the layer's q/k RMSNorm weights (bf16)
+    float cs[64], sn[64];       // the RoPE cos/sin row of the new position
     float ps[PD_MAX_G][PD_ATT_C + 4];  // padded: heads g and g' read position j in different banks
     float ml[PD_MAX_G][2];
     float cm[PD_MAX_G][PD_MAX_SPLITS];
@@ -529,6 +531,16 @@ template <int M>
 __device__ __forceinline__ void pd_attention_begin(const PdParams& p, const PdLayer& L, PdAtt& A, int p0,
                                                    int nsplit) {
     const PdRuns R = pd_runs(M, p.Hkv, nsplit);
+    // the q/k norm weights and the new position's cos/sin row: one group committed before the
+    // K and V groups, so the run waits for it with cp_async_wait<2>
+    {
+        const int t = threadIdx.x;
+        if (t < 16) cp_async16(&A.qn[t * 8], L.q_norm + t * 8, true);
+        else if (t < 32) cp_async16(&A.kn[(t - 16) * 8], L.k_norm + (t - 16) * 8, true);
+        else if (t < 48) cp_async16(&A.cs[(t - 32) * 4], p.cos_t + (int64_t)p0 * 64 + (t - 32) * 4, true);
+        else if (t < 64) cp_async16(&A.sn[(t - 48) * 4], p.sin_t + (int64_t)p0 * 64 + (t - 48) * 4, true);
+        cp_async_commit();
+    }
     pd_run_rows(p, L, A, p0, R, (int)blockIdx.x, 0, 0);
     pd_run_rows(p, L, A, p0, R, (int)blockIdx.x, 1, 0);
 }
@@ -543,8 +555,6 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
     const int Hq = p.Hq, Hkv = p.Hkv, G = Hq / Hkv, D = 128;
     const int heads = Hq + 2 * Hkv;
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
-    const float* cs = p.cos_t + (int64_t)p0 * (D / 2);
-    const float* sn = p.sin_t + (int64_t)p0 * (D / 2);
     const PdRuns R = pd_runs(M, Hkv, nsplit);
     const int kt0 = G < PD_CONS ? G * 32 : 0;  // the softmax runs on warps 0..G-1
     for (int run = (int)blockIdx.x; run < R.n; run += (int)gridDim.x) {
@@ -565,14 +575,15 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
             *reinterpret_cast<float4*>(&A.kvraw[which][c]) =
                 __ldcg(reinterpret_cast<const float4*>(qrow + (int64_t)(Hq + which * Hkv + kvh) * D + c));
         }
+        cp_async_wait<2>();  // the norm weights and cos/sin (the first chunk's K and V may still fly)
         pd_csync();
-        for (int g = warp; g < G; g += PD_CONS) head_norm_rope(A.qraw[g], L.q_norm, p.eps, cs, sn, lane, A.qs[g]);
+        for (int g = warp; g < G; g += PD_CONS) head_norm_rope(A.qraw[g], A.qn, p.eps, A.cs, A.sn, lane, A.qs[g]);
         if (has_new) {
             // the new position's k (normed, rotated) and v: into the caches now, into the
             // staging rows when their chunk comes
             const int64_t prow = ((int64_t)b * Hkv + kvh) * (int64_t)p.ctx_max * D + (int64_t)p0 * D;
             if (warp == 0) {
-                head_norm_rope(A.kvraw[0], L.k_norm, p.eps, cs, sn, lane, A.knew);
+                head_norm_rope(A.kvraw[0], A.kn, p.eps, A.cs, A.sn, lane, A.knew);
                 __syncwarp();
                 *reinterpret_cast<float4*>(L.kc + prow + lane * 4) = *reinterpret_cast<const float4*>(&A.knew[lane * 4]);
             } else if (warp == 1) {
