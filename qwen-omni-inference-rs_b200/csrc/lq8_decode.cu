@@ -10,7 +10,8 @@
 // fills with the next matrix's tiles, so HBM keeps streaming across the phase boundaries that
 // separate kernels elsewhere.
 //
-// The consumer warps walk the phases, with a grid barrier (a global counter, bounded spin)
+// The consumer warps walk the phases, with a grid barrier (a global counter, bounded spin;
+// split into arrive and wait where work that reads nothing of other CTAs fits in between)
 // wherever a phase reads what other CTAs wrote:
 //   QKV  RMSNorm + Q8_0 of x (every CTA, redundantly), q|k|v rows                      | barrier
 //   ATT  runs of 64-position chunks of one (row, kv head): q/k RMSNorm + RoPE once per run,
@@ -525,8 +526,9 @@ __device__ __forceinline__ void pd_run_rows(const PdParams& p, const PdLayer& L,
     pd_chunk_rows(p, L, A, p0, pair / p.Hkv, pair % p.Hkv, (run % R.per_seq) * R.len, which, t0);
 }
 
-// this CTA's first run of the layer is run blockIdx.x; its first chunk's cache-row copies start
-// here, before the grid barrier that precedes attention, so they overlap it
+// this CTA's first run of the layer is run blockIdx.x; the layer's q/k norm weights, the new
+// position's cos/sin row and the run's first chunk's cache rows start loading here, between
+// the arrive and the wait of the grid barrier that precedes attention, so they overlap it
 template <int M>
 __device__ __forceinline__ void pd_attention_begin(const PdParams& p, const PdLayer& L, PdAtt& A, int p0,
                                                    int nsplit) {
