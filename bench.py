@@ -165,27 +165,41 @@ def time_gemv_launches(lq8, ctx, model, cfg, B, reps=2):
     return shapes
 
 
-def cpu_baseline_sample(O, cfgd, threads=1):
+def cpu_baseline_sample(O, cfgd, threads=1, samples=5, layer_counts=(2, 4)):
     """The oracle (reference CPU path restated in C) on a bounded sample of the decode step:
-    one decode token after a 16-token prompt through the first 1 and 2 layers + LM head;
-    per-layer time = t2 - t1, extrapolated to the full layer count."""
+    models truncated to 2 and 4 layers (+ the LM head) each decode `samples` tokens one at a
+    time after a 16-token prompt (one untimed token first); per-layer time = the difference of
+    the two models' median token times / 2, extrapolated to the full layer count. A
+    non-positive difference makes the sample invalid (None) instead of being clamped."""
     cfg = O.make_config(**cfgd)
     saved = O.get_threads()
-    times = {}
-    for nl in (1, 2):
-        O.set_threads(saved)
-        m = O.Qwen3Model(cfg, SEED, layers_limit=nl, ctx_max=32)
-        prompt = O.gen_tokens(SEED, 0, 16, cfg.vocab)
+    med, raw = {}, {}
+    for nl in layer_counts:
+        O.set_threads(saved)  # weight generation on every core; the timed tokens on `threads`
+        m = O.Qwen3Model(cfg, SEED, layers_limit=nl, ctx_max=16 + samples + 2)
+        prompt = O.gen_tokens(SEED, 0, 16 + samples + 1, cfg.vocab)
         O.set_threads(threads)
-        m.forward(prompt[:15], 0)
-        t0 = time.perf_counter()
-        m.forward(prompt[15:16], 15)
-        times[nl] = time.perf_counter() - t0
+        m.forward(prompt[:16], 0)
+        m.forward(prompt[16:17], 16)
+        ts = []
+        for i in range(samples):
+            t0 = time.perf_counter()
+            m.forward(prompt[17 + i:18 + i], 17 + i)
+            ts.append(time.perf_counter() - t0)
         m.close()
+        med[nl] = statistics.median(ts)
+        raw[nl] = [round(t, 5) for t in ts]
     O.set_threads(saved)
-    per_layer = max(times[2] - times[1], 1e-9)
-    step = times[1] - per_layer + cfgd["layers"] * per_layer
-    return 1.0 / step, {"t_1layer_s": times[1], "t_2layer_s": times[2], "per_layer_s": per_layer}
+    lo, hi = layer_counts
+    per_layer = (med[hi] - med[lo]) / (hi - lo)
+    det = {"samples_s": {f"{nl}_layers": raw[nl] for nl in layer_counts},
+           "median_s": {f"{nl}_layers": med[nl] for nl in layer_counts}, "per_layer_s": per_layer}
+    if per_layer <= 0:
+        det["invalid"] = "the deeper model's median token time is not above the shallower one's"
+        return None, det
+    step = med[lo] + (cfgd["layers"] - lo) * per_layer
+    det["step_s"] = step
+    return 1.0 / step, det
 
 
 # ------------------------------------------------------------------------------ arms
@@ -451,9 +465,11 @@ def finish(args, cfgd, world, rank, L, B, K, W, ms, value, e2e, ms_e2e, clk, lau
         v, det = cpu_baseline_sample(O, cfgd, threads=1)
         cpu = {"value": v, "unit": "tok/s", "cores": 1, "kind": "port",
                "sample": (f"oracle (C restatement of the reference's single-threaded Rust CPU path with Q8_0 "
-                          f"linears), 1 thread: one decode token after a 16-token prompt through 1 and 2 of "
-                          f"{cfgd['layers']} layers + LM head, per-layer time extrapolated to the full model; "
-                          f"context 16 instead of {L} (attention over the longer context is left out)"),
+                          f"linears), 1 thread, batch 1 (the reference decodes one sequence): 5 decode tokens "
+                          f"each through models of 2 and 4 of {cfgd['layers']} layers + LM head after a 16-token "
+                          f"prompt; per-layer time from the difference of the median token times, extrapolated "
+                          f"to the full model; context 16 instead of {L} (attention over the longer context is "
+                          f"left out)"),
                "detail": det}
 
     if rank == 0:

@@ -3,8 +3,8 @@
  *
  * This is the drop-in boundary for the lluda-inference crate. Each entry point names the
  * reference interface it replaces (paths inside the reference project, crate
- * lluda-inference). The reference binds nothing like this today; INTEGRATION.md shows the
- * Rust `extern "C"` block a maintainer adds.
+ * lluda-inference). The reference binds nothing like this today; the Rust crate lluda-cuda-sys
+ * (rust/lluda-cuda-sys in this repository) carries the matching `extern "C"` block.
  *
  * Conventions
  *  - Every function returns an int status: LQ_OK (0) or a negative lq_status. Nothing aborts
@@ -114,16 +114,19 @@ int lq_q8_0_matmul(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq_dev,
 int lq_q8_0_linear(lq_ctx* ctx, const lq_q8_tensor* w, const void* x_dev, lq_dtype x_dtype,
                    int64_t m, float* y_dev);
 /* lq_q8_0_linear that allocates no device memory. It has no counterpart in the reference.
- * lq_q8_0_linear grows its scratch with cudaMalloc/cudaFree, which some callers cannot allow
- * (a latency-bound decode loop -- both calls can synchronise the whole device -- or a host
- * whose device memory all belongs to its own pool allocator). This variant quantizes x into a
- * fixed 4 MiB array inside the library's device image instead (present on every GPU that
- * loads liblq8, until process exit), so m*k + 2*m*(k/32), rounded up to 256, must be at most
- * 4 MiB; larger calls fail with LQ_ERR_INVALID_ARG. The first call on a device looks the
- * array's address up (cudaGetSymbolAddress); make that first call before any stream capture.
- * All calls on a device share the one array, so calls that overlap on the GPU (different
- * streams or contexts of the same device) race; each call writes every scratch byte it
- * reads, so nothing needs clearing between calls. Output equals lq_q8_0_linear's. */
+ * lq_q8_0_linear grows its scratch (the quantized rows, and the K-split partial sums of the
+ * 5..64-row GEMM) with cudaMalloc/cudaFree, which some callers cannot allow: a latency-bound
+ * decode loop (both calls can synchronise the whole device), or a host whose device memory
+ * all belongs to its own pool allocator. This variant keeps all of it in a fixed 4 MiB array
+ * inside the library's device image instead (present on every GPU that loads liblq8, until
+ * process exit). A call needs, each part rounded up to 256 bytes, m*k bytes of quantized rows,
+ * 2*m*(k/32) bytes of scales and, for 5..64 rows on a weight with few 64-row tiles, the K-split
+ * partials (slices*m*n*4 bytes); calls that need more than 4 MiB fail with LQ_ERR_INVALID_ARG.
+ * The first call on a device looks the array's address up (cudaGetSymbolAddress). All calls
+ * on a device share the one array, so calls that overlap on the GPU (different streams or
+ * contexts of the same device) race; each call writes every scratch byte before it reads it,
+ * so nothing needs clearing between calls. The kernels are lq_q8_0_linear's: the output is
+ * bit-identical to it. */
 int lq_q8_0_linear_noalloc(lq_ctx* ctx, const lq_q8_tensor* w, const void* x_dev,
                            lq_dtype x_dtype, int64_t m, float* y_dev);
 
@@ -308,11 +311,11 @@ int lq_qwen3_weight_bytes(lq_model* model, int64_t* bytes);
  * of a layer; layer -1 with kind 24 final norm, 25 embedding table [vocab][hidden]. *dev_out
  * aliases the model's buffer (load a checkpoint by writing into it); *count = elements. */
 int lq_qwen3_tensor(lq_model* model, int64_t layer, int kind, uint16_t** dev_out, int64_t* count);
-/* Kernel launches in one decode step (kernel nodes of the captured CUDA graph; 0 before the
- * first decode step or lq_qwen3_set_batch). */
 /* MoE weights of a layer: kind 10 router (expert ignored), 11 gate, 12 up, 13 down of
  * `expert` (views into the stacked expert tensors). */
 int lq_qwen3_expert(lq_model* model, int64_t layer, int64_t expert, int kind, lq_q8_tensor* out);
+/* Kernel launches in one decode step (kernel nodes of the captured CUDA graph; 0 before the
+ * first decode step or lq_qwen3_set_batch). */
 int lq_qwen3_graph_kernels(lq_model* model, int64_t* n);
 
 #ifdef __cplusplus

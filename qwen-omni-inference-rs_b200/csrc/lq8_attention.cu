@@ -483,11 +483,9 @@ static int launch_chunks(lq_ctx* ctx, AttParams p, int64_t rows, void* scratch, 
     p.part_ml = (float*)((uint8_t*)scratch + ATT_COUNTER_BYTES);
     const size_t ml = ((size_t)(slice * p.Hq * p.nsplit * 2) * 4 + 255) & ~(size_t)255;
     p.part_o = (float*)((uint8_t*)scratch + ATT_COUNTER_BYTES + ml);
-    static bool attr = false;
-    if (!attr) {
-        LQ_CUDA(ctx, cudaFuncSetAttribute(attn_chunk_kernel<FUSED, GT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)sizeof(Smem)));
-        attr = true;
+    {
+        const int rc = ensure_func_smem(ctx, (const void*)attn_chunk_kernel<FUSED, GT>, sizeof(Smem));
+        if (rc) return rc;
     }
     if (zero_counters)
         LQ_CUDA(ctx, cudaMemsetAsync(p.counters, 0, (size_t)(slice * p.Hkv) * 4, ctx->stream));

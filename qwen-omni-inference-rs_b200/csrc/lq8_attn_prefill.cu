@@ -263,12 +263,7 @@ int launch_attention_prefill(lq_ctx* ctx, const float* q, const float* kc, const
     p.out = out;
     p.xq = xq;
     p.xd = xd;
-    static bool attr[64] = {};
-    if (ctx->device < 0 || ctx->device >= 64 || !attr[ctx->device]) {
-        LQ_CUDA(ctx, cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)sizeof(PfSmem)));
-        if (ctx->device >= 0 && ctx->device < 64) attr[ctx->device] = true;
-    }
+    if (const int rc = ensure_func_smem(ctx, (const void*)attn_prefill_kernel, sizeof(PfSmem))) return rc;
     const dim3 grid((unsigned)p.ntiles, (unsigned)Hkv, (unsigned)B);
     return launch_kernel(ctx, attn_prefill_kernel, grid, dim3(PF_THREADS), sizeof(PfSmem), "attn_prefill", p);
 }

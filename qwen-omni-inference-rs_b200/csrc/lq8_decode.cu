@@ -977,11 +977,7 @@ int decode_persist_write_desc(lq_ctx* ctx, void* dev, const PdHostLayer* layers,
 template <int M>
 static int launch_pd(lq_ctx* ctx, const PdParams& p, size_t smem) {
     auto kern = decode_step_kernel<M>;
-    static bool attr[64] = {};
-    if (ctx->device < 0 || ctx->device >= 64 || !attr[ctx->device]) {
-        LQ_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-        if (ctx->device >= 0 && ctx->device < 64) attr[ctx->device] = true;
-    }
+    if (const int rc = ensure_func_smem(ctx, (const void*)kern, 227 * 1024)) return rc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ctx->sm_count);
     cfg.blockDim = dim3(PD_THREADS);

@@ -364,11 +364,7 @@ int launch_gemm_tc(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const u
     if ((rc = make_tensor_map_2d(ctx, &mdx, CU_TENSOR_MAP_DATA_TYPE_UINT16, xd, nb, m, nb * 2, 8, TC_BN,
                        CU_TENSOR_MAP_SWIZZLE_NONE)))
         return rc;
-    static bool attr[64] = {};
-    if (ctx->device < 0 || ctx->device >= 64 || !attr[ctx->device]) {
-        LQ_CUDA(ctx, cudaFuncSetAttribute(q8_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM));
-        if (ctx->device >= 0 && ctx->device < 64) attr[ctx->device] = true;
-    }
+    if (const int rc = ensure_func_smem(ctx, (const void*)q8_gemm_tc_kernel, TC_SMEM)) return rc;
     TcParams p;
     p.N = (int)N;
     p.K = (int)K;

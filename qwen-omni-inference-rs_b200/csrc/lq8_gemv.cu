@@ -327,11 +327,7 @@ static int run_stream(lq_ctx* ctx, GvParams p, int ctas) {
     const size_t smem = stage_smem(STAGES, M, p.K);
     if (smem > GV_SMEM_MAX) return set_error(ctx, LQ_ERR_UNSUPPORTED, "gemv: K=%d too large for M=%d", p.K, M);
     auto kern = q8_gemv_stream_kernel<M, PRO, STAGES, SWI>;
-    static bool attr = false;  // per process: the attribute is set for the largest size
-    if (!attr) {
-        LQ_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GV_SMEM_MAX));
-        attr = true;
-    }
+    if (const int rc = ensure_func_smem(ctx, (const void*)kern, GV_SMEM_MAX)) return rc;
     // never more CTAs per SM than can be resident together (registers, threads, smem): a
     // persistent grid that spills into a second wave would serialise
     int resident = 0;

@@ -47,6 +47,9 @@ int ensure_split(lq_ctx* ctx, size_t bytes);
 size_t gemm_split_bytes(lq_ctx* ctx, int64_t n, int64_t k, int64_t m);
 // read + clear the device error flag (synchronises the stream)
 int consume_device_error(lq_ctx* ctx, const char* what);
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) for `func` on ctx->device, once per
+// (function, device) and again only when a launch needs more than was set before
+int ensure_func_smem(lq_ctx* ctx, const void* func, size_t bytes);
 
 }  // namespace lq
 
@@ -189,9 +192,15 @@ inline int launch_kernel(lq_ctx* ctx, void (*kern)(KArgs...), dim3 grid, dim3 bl
 namespace lq {
 int launch_quantize_rows(lq_ctx* ctx, const void* src, lq_dtype dt, int64_t rows, int64_t k,
                          int8_t* qs, uint16_t* d);
+// a caller-owned buffer for the K-split partial sums of the small-M GEMM: when given, the
+// matmul uses it instead of growing ctx->split (and fails with LQ_ERR_STATE if it is short)
+struct SplitBuf {
+    float* p;
+    size_t bytes;
+};
 int launch_q8_matmul(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd,
                      int64_t m, float* y, const float* resid, int64_t ldy,
-                     unsigned long long* argmax_keys);
+                     unsigned long long* argmax_keys, const SplitBuf* split = nullptr);
 bool gemv_stream_supported(int64_t K);
 // prefill GEMM on tcgen05 (m >= 64 tokens, K % 256 == 0, 16-byte aligned operands)
 bool gemm_tc_supported(int64_t m, int64_t K, const void* wq, const void* xq, const void* wd, const void* xd);

@@ -653,12 +653,7 @@ static int launch_moe_stream(lq_ctx* ctx, MoeExpertParams p, const int8_t* wq, c
                             (uint64_t)(p.K / 32) * 2, 8, ME_GRP, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
     const size_t smem = (size_t)stages * ME_STAGE + fixed;
-    static bool attr[64] = {};  // per instantiation (GU, TOK)
-    if (ctx->device < 0 || ctx->device >= 64 || !attr[ctx->device]) {
-        LQ_CUDA(ctx, cudaFuncSetAttribute(moe_mma_kernel<GU, TOK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)solo_budget));
-        if (ctx->device >= 0 && ctx->device < 64) attr[ctx->device] = true;
-    }
+    if (const int rc = ensure_func_smem(ctx, (const void*)moe_mma_kernel<GU, TOK>, solo_budget)) return rc;
     int occ = 1;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, moe_mma_kernel<GU, TOK>, ME_THREADS, smem);
     per_sm = std::max(1, std::min(per_sm, occ));
@@ -705,12 +700,7 @@ int launch_moe(lq_ctx* ctx, const lq_q8_tensor* router, const lq_q8_tensor* gate
     const size_t route_smem = (size_t)H + (size_t)(H / 32) * 4 + (size_t)E * 8 +
                               (size_t)(route_threads / 32) * 4 * (size_t)(H / 32 + 1) * 4;
     if (route_smem > 48 * 1024) {
-        static bool rattr[64] = {};
-        if (ctx->device < 0 || ctx->device >= 64 || !rattr[ctx->device]) {
-            LQ_CUDA(ctx, cudaFuncSetAttribute(moe_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              200 * 1024));
-            if (ctx->device >= 0 && ctx->device < 64) rattr[ctx->device] = true;
-        }
+        if (const int rc = ensure_func_smem(ctx, (const void*)moe_route_kernel, 200 * 1024)) return rc;
     }
     int rc = launch_kernel(ctx, moe_route_kernel, dim3((unsigned)rows), dim3(route_threads), route_smem, "moe_route",
                            xq, xd, (int)H, router->qs, router->d, (int)E, (int)top_k, norm_topk,
@@ -718,12 +708,7 @@ int launch_moe(lq_ctx* ctx, const lq_q8_tensor* router, const lq_q8_tensor* gate
     if (rc) return rc;
     const size_t disp_smem = (size_t)rows * top_k * 4;
     if (disp_smem > 48 * 1024) {
-        static bool dattr[64] = {};
-        if (ctx->device < 0 || ctx->device >= 64 || !dattr[ctx->device]) {
-            LQ_CUDA(ctx, cudaFuncSetAttribute(moe_dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              200 * 1024));
-            if (ctx->device >= 0 && ctx->device < 64) dattr[ctx->device] = true;
-        }
+        if (const int rc = ensure_func_smem(ctx, (const void*)moe_dispatch_kernel, 200 * 1024)) return rc;
     }
     // 8 tokens per pass while experts get a few tokens each on average (most single-pass),
     // else 16

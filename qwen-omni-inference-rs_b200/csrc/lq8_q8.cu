@@ -488,17 +488,27 @@ size_t gemm_split_bytes(lq_ctx* ctx, int64_t n, int64_t k, int64_t m) {
     return std::max(gs, (size_t)splits * m * n * 4);
 }
 
+// K-split partials: the caller's fixed buffer when given, else the context's split buffer
+static int split_partials(lq_ctx* ctx, const SplitBuf* fixed, size_t bytes, float** out) {
+    if (fixed) {
+        if (bytes > fixed->bytes)
+            return set_error(ctx, LQ_ERR_STATE, "K-split partials need %zu bytes; the fixed buffer holds %zu", bytes,
+                             fixed->bytes);
+        *out = fixed->p;
+        return LQ_OK;
+    }
+    const int rc = ensure_split(ctx, bytes);
+    if (rc) return rc;
+    *out = reinterpret_cast<float*>(ctx->split);
+    return LQ_OK;
+}
+
 template <int BW, int BX, int WW, int WX>
 static int run_gemm(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd,
                     int64_t m, float* y, const float* resid, int64_t ldy,
-                    unsigned long long* keys) {
+                    unsigned long long* keys, const SplitBuf* fixed) {
     using C = GemmCfg<BW, BX, WW, WX>;
-    static bool attr_done = false;  // per process; the attribute is per device function
-    if (!attr_done) {
-        LQ_CUDA(ctx, cudaFuncSetAttribute(q8_gemm_mma_kernel<BW, BX, WW, WX>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-        attr_done = true;
-    }
+    if (const int rc = ensure_func_smem(ctx, (const void*)q8_gemm_mma_kernel<BW, BX, WW, WX>, C::SMEM)) return rc;
     const int64_t tiles = (int64_t)ceil_div(w->n, BW) * ceil_div(m, BX);
     int splits = gemm_splits(ctx, tiles, w->k, m);
     int kslice = 0;
@@ -506,9 +516,8 @@ static int run_gemm(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const 
     if (splits > 1) {
         kslice = split_slice(w->k, splits);
         splits = ceil_div(w->k, kslice);
-        const int rc = ensure_split(ctx, (size_t)splits * m * w->n * 4);
+        const int rc = split_partials(ctx, fixed, (size_t)splits * m * w->n * 4, &part);
         if (rc) return rc;
-        part = reinterpret_cast<float*>(ctx->split);
     }
     dim3 grid(ceil_div(w->n, BW), ceil_div(m, BX), splits);
     int rc = launch_kernel(ctx, q8_gemm_mma_kernel<BW, BX, WW, WX>, grid, dim3(C::THREADS), C::SMEM, "q8_gemm_mma",
@@ -820,7 +829,8 @@ static bool gs_supported(const lq_q8_tensor* w, const int8_t* xq, const uint16_t
 
 template <int TOK>
 static int launch_gemm_stream_t(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd,
-                                int64_t m, float* y, const float* resid, int64_t ldy, unsigned long long* keys) {
+                                int64_t m, float* y, const float* resid, int64_t ldy, unsigned long long* keys,
+                                const SplitBuf* fixed) {
     using C = GsCfg<TOK>;
     GsParams p = {};
     p.N = (int)w->n;
@@ -838,9 +848,8 @@ static int launch_gemm_stream_t(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t
     p.keys = keys;
     p.err = ctx->err_flag;
     if (p.slices > 1) {
-        const int rc = ensure_split(ctx, (size_t)p.slices * m * w->n * 4);
+        const int rc = split_partials(ctx, fixed, (size_t)p.slices * m * w->n * 4, &p.part);
         if (rc) return rc;
-        p.part = reinterpret_cast<float*>(ctx->split);
     }
     CUtensorMap mw, mwd, mx, mxd;
     int rc = make_tensor_map_2d(ctx, &mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->qs, (uint64_t)w->k, (uint64_t)w->n,
@@ -855,12 +864,7 @@ static int launch_gemm_stream_t(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t
         rc = make_tensor_map_2d(ctx, &mxd, CU_TENSOR_MAP_DATA_TYPE_UINT16, xd, (uint64_t)(w->k / 32), (uint64_t)m,
                                 (uint64_t)(w->k / 32) * 2, 8, TOK, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
-    static bool attr = false;  // one flag per instantiation
-    if (!attr) {
-        LQ_CUDA(ctx, cudaFuncSetAttribute(q8_gemm_stream_kernel<TOK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)C::SMEM));
-        attr = true;
-    }
+    if ((rc = ensure_func_smem(ctx, (const void*)q8_gemm_stream_kernel<TOK>, C::SMEM))) return rc;
     const long long items = (long long)p.tiles * p.slices * p.passes;
     const int grid = (int)std::min<long long>(items, 2ll * ctx->sm_count);
     rc = launch_kernel(ctx, q8_gemm_stream_kernel<TOK>, dim3(grid), dim3(GS_THREADS), C::SMEM, "q8_gemm_stream", mw,
@@ -872,14 +876,15 @@ static int launch_gemm_stream_t(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t
 }
 
 static int launch_gemm_stream(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd, int64_t m,
-                              float* y, const float* resid, int64_t ldy, unsigned long long* keys) {
-    return gs_tok(m) == 16 ? launch_gemm_stream_t<16>(ctx, w, xq, xd, m, y, resid, ldy, keys)
-                           : launch_gemm_stream_t<32>(ctx, w, xq, xd, m, y, resid, ldy, keys);
+                              float* y, const float* resid, int64_t ldy, unsigned long long* keys,
+                              const SplitBuf* fixed) {
+    return gs_tok(m) == 16 ? launch_gemm_stream_t<16>(ctx, w, xq, xd, m, y, resid, ldy, keys, fixed)
+                           : launch_gemm_stream_t<32>(ctx, w, xq, xd, m, y, resid, ldy, keys, fixed);
 }
 
 int launch_q8_matmul(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd,
                      int64_t m, float* y, const float* resid, int64_t ldy,
-                     unsigned long long* keys) {
+                     unsigned long long* keys, const SplitBuf* split) {
     if (m <= 0 || w->n <= 0) return LQ_OK;
     if (m <= 4 && gemv_stream_supported(w->k) && ((uintptr_t)xq % 16) == 0 && ((uintptr_t)xd % 16) == 0 &&
         gemv_stream_smem(m, w->k) <= 227 * 1024)
@@ -893,11 +898,11 @@ int launch_q8_matmul(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const
     }
     if (!keys && m > 64 && gemm_tc_supported(m, w->k, w->qs, xq, w->d, xd))
         return launch_gemm_tc(ctx, w, xq, xd, m, y, resid, ldy);
-    if (gs_supported(w, xq, xd, m)) return launch_gemm_stream(ctx, w, xq, xd, m, y, resid, ldy, keys);
-    if (m <= 16) return run_gemm<128, 16, 8, 1>(ctx, w, xq, xd, m, y, resid, ldy, keys);
-    if (m <= 32) return run_gemm<128, 32, 8, 1>(ctx, w, xq, xd, m, y, resid, ldy, keys);
-    if (m <= 64) return run_gemm<128, 64, 4, 2>(ctx, w, xq, xd, m, y, resid, ldy, keys);
-    return run_gemm<128, 128, 4, 2>(ctx, w, xq, xd, m, y, resid, ldy, keys);
+    if (gs_supported(w, xq, xd, m)) return launch_gemm_stream(ctx, w, xq, xd, m, y, resid, ldy, keys, split);
+    if (m <= 16) return run_gemm<128, 16, 8, 1>(ctx, w, xq, xd, m, y, resid, ldy, keys, split);
+    if (m <= 32) return run_gemm<128, 32, 8, 1>(ctx, w, xq, xd, m, y, resid, ldy, keys, split);
+    if (m <= 64) return run_gemm<128, 64, 4, 2>(ctx, w, xq, xd, m, y, resid, ldy, keys, split);
+    return run_gemm<128, 128, 4, 2>(ctx, w, xq, xd, m, y, resid, ldy, keys, split);
 }
 
 // =========================================================================================
@@ -1061,13 +1066,18 @@ int lq_fill_bf16(lq_ctx* ctx, uint64_t seed, uint64_t tid, int64_t offset, int64
 // lq_q8_0_linear_noalloc: lq_q8_0_linear for callers that must not allocate device memory.
 //
 // lq_q8_0_linear quantizes x into context scratch that it grows with cudaMalloc (and frees
-// the old buffer with cudaFree) when a call needs more. Some callers cannot allow that: a
-// decode loop with a latency budget (both calls may synchronise the whole device), or a host
-// that has handed all device memory to its own pool and forbids allocations behind its back.
-// This variant keeps the quantized activations in one fixed array in the library's device
-// image instead, so it allocates nothing. The array is 4 MiB on every GPU that loads the
-// library, held until the process exits; it bounds m*k: m*k + m*(k/32)*2 (rounded up to 256)
-// must fit, or the call fails with LQ_ERR_INVALID_ARG.
+// the old buffer with cudaFree) when a call needs more, and the small-M GEMM it dispatches to
+// keeps its K-split partial sums in a second context buffer grown the same way. Some callers
+// cannot allow that: a decode loop with a latency budget (both calls may synchronise the whole
+// device), or a host that has handed all device memory to its own pool and forbids
+// allocations behind its back. This variant keeps both in one fixed array in the library's
+// device image instead, so it allocates nothing. The array is 4 MiB on every GPU that loads
+// the library, held until the process exits. A call needs, each part rounded up to 256 bytes:
+// m*k bytes of quantized rows, m*(k/32)*2 bytes of their scales, and for 5..64 rows on a
+// weight with few row tiles the GEMM's K-split partials (slices*m*n*4 bytes, the amount
+// lq::gemm_split_bytes reports); calls that need more than the array fail with
+// LQ_ERR_INVALID_ARG. The kernels and their order are lq_q8_0_linear's, so the output is
+// bit-identical to it.
 // =========================================================================================
 #include <mutex>
 
@@ -1099,6 +1109,8 @@ int noalloc_scratch(lq_ctx* ctx, void** out) {
     *out = g_noalloc_addr[ctx->device];
     return LQ_OK;
 }
+
+inline size_t al256(size_t b) { return (b + 255) & ~(size_t)255; }
 }  // namespace
 
 extern "C" int lq_q8_0_linear_noalloc(lq_ctx* ctx, const lq_q8_tensor* w, const void* x, lq_dtype dt, int64_t m,
@@ -1111,19 +1123,23 @@ extern "C" int lq_q8_0_linear_noalloc(lq_ctx* ctx, const lq_q8_tensor* w, const 
     LQ_REQUIRE(ctx, m >= 0 && m < (1 << 24), "lq_q8_0_linear_noalloc: m=%lld out of range", (long long)m);
     if (m == 0) return LQ_OK;
     LQ_REQUIRE(ctx, x && y, "lq_q8_0_linear_noalloc: NULL pointer");
-    const size_t off = ((size_t)(m * w->k) + 255) & ~(size_t)255;
-    const size_t need = off + (size_t)(m * (w->k / 32)) * 2;
+    const size_t q_bytes = al256((size_t)(m * w->k));
+    const size_t d_bytes = al256((size_t)(m * (w->k / 32)) * 2);
+    const size_t split_bytes = al256(lq::gemm_split_bytes(ctx, w->n, w->k, m));
+    const size_t need = q_bytes + d_bytes + split_bytes;
     LQ_REQUIRE(ctx, need <= kNoAllocScratchBytes,
-               "lq_q8_0_linear_noalloc: m=%lld x k=%lld needs %zu bytes of scratch; the fixed scratch holds "
+               "lq_q8_0_linear_noalloc: m=%lld, n=%lld, k=%lld needs %zu bytes of scratch; the fixed scratch holds "
                "%zu (use lq_q8_0_linear, or split the rows)",
-               (long long)m, (long long)w->k, need, kNoAllocScratchBytes);
+               (long long)m, (long long)w->n, (long long)w->k, need, kNoAllocScratchBytes);
     void* scratch = nullptr;
     rc = noalloc_scratch(ctx, &scratch);
     if (rc) return rc;
-    // every byte the matmul reads is written by the quantization first: nothing to clear
+    // every byte the matmul reads is written first in the same call (the quantized rows by the
+    // quantization, each K-split partial by its slice before the reduce): nothing to clear
     int8_t* xq = (int8_t*)scratch;
-    uint16_t* xd = (uint16_t*)((uint8_t*)scratch + off);
+    uint16_t* xd = (uint16_t*)((uint8_t*)scratch + q_bytes);
+    lq::SplitBuf split = {reinterpret_cast<float*>((uint8_t*)scratch + q_bytes + d_bytes), split_bytes};
     rc = lq::launch_quantize_rows(ctx, x, dt, m, w->k, xq, xd);
     if (rc) return rc;
-    return lq::launch_q8_matmul(ctx, w, xq, xd, m, y, nullptr, w->n, nullptr);
+    return lq::launch_q8_matmul(ctx, w, xq, xd, m, y, nullptr, w->n, nullptr, &split);
 }

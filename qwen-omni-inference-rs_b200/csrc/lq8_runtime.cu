@@ -4,6 +4,9 @@
 #include <cstdarg>
 #include <cstdlib>
 #include <cstring>
+#include <map>
+#include <mutex>
+#include <utility>
 
 namespace {
 thread_local std::string g_init_error;  // lq_last_error(NULL)
@@ -46,6 +49,10 @@ bool fault_injected(const char* entry) {
 
 int ensure_scratch(lq_ctx* ctx, size_t bytes) {
     if (bytes <= ctx->scratch_bytes) return LQ_OK;
+    // LQ_FAULT=ensure_scratch turns every scratch allocation into an error (tests use it to
+    // show that a path allocates nothing)
+    if (fault_injected("ensure_scratch"))
+        return set_error(ctx, LQ_ERR_INJECTED, "ensure_scratch: injected fault (LQ_FAULT), %zu bytes", bytes);
     // the old scratch may still be in use by queued work
     LQ_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
     if (ctx->scratch) LQ_CUDA(ctx, cudaFree(ctx->scratch));
@@ -59,6 +66,8 @@ int ensure_scratch(lq_ctx* ctx, size_t bytes) {
 
 int ensure_split(lq_ctx* ctx, size_t bytes) {
     if (bytes <= ctx->split_bytes) return LQ_OK;
+    if (fault_injected("ensure_split"))
+        return set_error(ctx, LQ_ERR_INJECTED, "ensure_split: injected fault (LQ_FAULT), %zu bytes", bytes);
     cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
     LQ_CUDA(ctx, cudaStreamIsCapturing(ctx->stream, &st));
     if (st != cudaStreamCaptureStatusNone)
@@ -70,6 +79,19 @@ int ensure_split(lq_ctx* ctx, size_t bytes) {
     size_t sz = (bytes + 0xFFFFF) & ~(size_t)0xFFFFF;
     LQ_CUDA(ctx, cudaMalloc(&ctx->split, sz));
     ctx->split_bytes = sz;
+    return LQ_OK;
+}
+
+int ensure_func_smem(lq_ctx* ctx, const void* func, size_t bytes) {
+    // the attribute belongs to the function on one device; contexts on several devices (or
+    // threads driving them) share this table
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, size_t> set_bytes;
+    std::lock_guard<std::mutex> lock(mu);
+    size_t& have = set_bytes[std::make_pair(func, ctx->device)];
+    if (have >= bytes) return LQ_OK;
+    LQ_CUDA(ctx, cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+    have = bytes;
     return LQ_OK;
 }
 

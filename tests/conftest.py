@@ -1,5 +1,6 @@
 """Shared fixtures. `-m gpu` tests need a B200 and call liblq8.so through its C ABI; the rest
 run on CPU (oracle vs golden vectors, host logic, ABI surface)."""
+import json
 import os
 import sys
 
@@ -51,3 +52,24 @@ def cos_sim(a, b) -> float:
     a = np.asarray(a, dtype=np.float64).ravel()
     b = np.asarray(b, dtype=np.float64).ravel()
     return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b) + 1e-300))
+
+
+def parity_metrics(got, ref) -> dict:
+    """The reference's validation metrics for one output vector (tests/validation.rs:46-67 of
+    lluda-inference reports MSE, cosine, max-abs and mean-abs per layer), plus max-abs
+    relative to the largest reference magnitude."""
+    g = np.asarray(got, dtype=np.float64).ravel()
+    r = np.asarray(ref, dtype=np.float64).ravel()
+    d = np.abs(g - r)
+    return {"cos": cos_sim(g, r), "max_abs": float(d.max()), "max_rel": float(d.max() / (np.abs(r).max() + 1e-300)),
+            "mse": float(np.mean(d * d)), "mean_abs": float(d.mean())}
+
+
+def record(test: str, **fields) -> None:
+    """Appends one JSON line of measured parity figures to $LQ_PARITY_LOG (when set), so a GPU
+    run keeps the numbers the assertions were made on."""
+    path = os.environ.get("LQ_PARITY_LOG")
+    if not path:
+        return
+    with open(path, "a") as f:
+        f.write(json.dumps({"test": test, **fields}) + "\n")

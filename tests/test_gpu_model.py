@@ -9,7 +9,7 @@ exceed the logit tolerance before requiring equality).
 import numpy as np
 import pytest
 
-from conftest import cos_sim
+from conftest import cos_sim, parity_metrics, record
 from test_gpu_q8 import H
 
 pytestmark = pytest.mark.gpu
@@ -141,6 +141,8 @@ def test_qwen3_0_6b_greedy_tokens(ctx, lq8_lib, oracle):
             olg = om.forward(np.array([tok]), 16 + step - 1)
             tok = oracle.argmax(olg)
         d = float(np.max(np.abs(lg[0] - olg)))
+        record("0.6b_teacher_forced", step=step, margin=float(_margin(olg)), same_token=bool(nxt[0] == tok),
+               **parity_metrics(lg[0], olg))
         assert cos_sim(lg[0], olg) >= DEEP_COS, step
         assert d <= DEEP_MAXREL * np.max(np.abs(olg)), step
         in_band = _margin(olg) <= 2 * d
@@ -153,6 +155,8 @@ def test_qwen3_0_6b_greedy_tokens(ctx, lq8_lib, oracle):
     assert matches >= 29
     otoks, _ = om.generate(prompt, 32)
     toks = gm.generate(prompt, 32)[0]
+    record("0.6b_free_running", teacher_forced_matches=matches, first_band=first_band,
+           identical=int(np.sum(np.cumprod(toks == otoks))), gpu=toks.tolist(), oracle=otoks.tolist())
     upto = 32 if first_band is None else first_band
     assert np.array_equal(toks[:upto], otoks[:upto])
 
