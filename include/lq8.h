@@ -98,6 +98,12 @@ int lq_memset(lq_ctx* ctx, void* dst_dev, int value, size_t bytes);
  * planned Tensor::quantize_q8_0() / QTensor constructor. */
 int lq_q8_0_quantize(lq_ctx* ctx, const void* src_dev, lq_dtype src_dtype, int64_t rows,
                      int64_t k, int8_t* qs_dev, uint16_t* d_dev);
+/* Host mirror of lq_q8_0_quantize (same bits): src_host [rows][k] f32 or bf16 into qs_host
+ * [rows][k] and d_host [rows][k/32]. Needs no context and no GPU (the planned
+ * Tensor::quantize_q8_0() on the CPU side of the crate, e.g. for checkpoint packing);
+ * failures are reported through lq_last_error(NULL). */
+int lq_q8_0_quantize_host(const void* src_host, lq_dtype src_dtype, int64_t rows, int64_t k,
+                          int8_t* qs_host, uint16_t* d_host);
 int lq_q8_0_pack_blocks(lq_ctx* ctx, const int8_t* qs_dev, const uint16_t* d_dev, int64_t rows,
                         int64_t k, uint8_t* blocks_dev);
 int lq_q8_0_unpack_blocks(lq_ctx* ctx, const uint8_t* blocks_dev, int64_t rows, int64_t k,

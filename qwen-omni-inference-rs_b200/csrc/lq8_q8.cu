@@ -4,6 +4,8 @@
 // row-major. Both the decode GEMV and the GEMM read this one layout; weights are written
 // once at load.
 #include "lq8_internal.cuh"
+
+#include <cmath>
 #include "lq8_async.cuh"
 #include "lq8_fused.cuh"
 #include "lq8_tma.cuh"
@@ -989,6 +991,47 @@ int lq_q8_0_quantize(lq_ctx* ctx, const void* src, lq_dtype dt, int64_t rows, in
     if (rows == 0 || k == 0) return LQ_OK;
     LQ_REQUIRE(ctx, src && qs && d, "lq_q8_0_quantize: NULL pointer");
     return lq::launch_quantize_rows(ctx, src, dt, rows, k, qs, d);
+}
+
+// GGML's quantize_row_q8_0_ref on the host, one block at a time: amax, d = amax/127 (IEEE f32
+// divide), id = d ? 1/d : 0, q = round-half-away(x*id) (|x*id| <= 127 by construction, clamped
+// anyway as the device does), d stored as fp16 (round to nearest even). bf16 inputs are widened
+// exactly. Same bits as lq_q8_0_quantize.
+int lq_q8_0_quantize_host(const void* src, lq_dtype dt, int64_t rows, int64_t k, int8_t* qs, uint16_t* d) {
+    if (lq::fault_injected("lq_q8_0_quantize_host"))
+        return lq::set_error(nullptr, LQ_ERR_INJECTED, "lq_q8_0_quantize_host: injected fault (LQ_FAULT)");
+    if (dt != LQ_DTYPE_F32 && dt != LQ_DTYPE_BF16)
+        return lq::set_error(nullptr, LQ_ERR_INVALID_ARG, "lq_q8_0_quantize_host: source dtype must be F32 or BF16");
+    if (rows < 0 || k < 0 || k % 32 != 0)
+        return lq::set_error(nullptr, LQ_ERR_INVALID_ARG, "lq_q8_0_quantize_host: k=%lld must be a multiple of 32",
+                             (long long)k);
+    if (rows == 0 || k == 0) return LQ_OK;
+    if (!src || !qs || !d) return lq::set_error(nullptr, LQ_ERR_INVALID_ARG, "lq_q8_0_quantize_host: NULL pointer");
+    const float* sf = static_cast<const float*>(src);
+    const uint16_t* sb = static_cast<const uint16_t*>(src);
+    const int64_t nb = k / 32;
+    for (int64_t r = 0; r < rows; r++)
+        for (int64_t b = 0; b < nb; b++) {
+            const int64_t e0 = r * k + b * 32;
+            float x[32];
+            float amax = 0.0f;
+            for (int i = 0; i < 32; i++) {
+                x[i] = dt == LQ_DTYPE_F32 ? sf[e0 + i] : lq::bf16_to_f32(sb[e0 + i]);
+                amax = std::max(amax, std::fabs(x[i]));
+            }
+            const float dd = amax / 127.0f;
+            const float id = dd != 0.0f ? 1.0f / dd : 0.0f;
+            for (int i = 0; i < 32; i++) {
+                float q = std::round(x[i] * id);
+                q = std::min(std::max(q, -127.0f), 127.0f);
+                qs[e0 + i] = (int8_t)(int)q;
+            }
+            const __half h = __float2half_rn(dd);
+            uint16_t hb;
+            memcpy(&hb, &h, 2);
+            d[r * nb + b] = hb;
+        }
+    return LQ_OK;
 }
 
 int lq_q8_0_pack_blocks(lq_ctx* ctx, const int8_t* qs, const uint16_t* d, int64_t rows, int64_t k,

@@ -158,3 +158,28 @@ def test_prefill_equals_incremental_decode(oracle):
     for i, t in enumerate(prompt):
         lb = b.forward(np.array([t]), i)
     assert np.array_equal(la, lb)
+
+
+@pytest.mark.parametrize("name", ["w", "x", "xb", "edge"])
+def test_host_quantizer_of_the_c_abi_matches_gguf_fixture(lq8_lib, oracle, gguf_fx, name):
+    """lq_q8_0_quantize_host (the C ABI's host mirror of the device quantizer; no GPU needed)
+    against the gguf-py fixtures, from f32 and from the bf16 rounding of the same rows."""
+    import ctypes as C
+    lib = lq8_lib.load()
+    a = np.ascontiguousarray(gguf_fx[f"{name}_in"], dtype=np.float32)
+    rows, k = a.shape
+    for src, dt in ((a, lq8_lib.DTYPE_F32), (oracle.f32_to_bf16(a), lq8_lib.DTYPE_BF16)):
+        src = np.ascontiguousarray(src)
+        qs = np.empty((rows, k), np.int8)
+        d = np.empty((rows, k // 32), np.uint16)
+        assert lib.lq_q8_0_quantize_host(src.ctypes.data, dt, rows, k, qs.ctypes.data, d.ctypes.data) == 0
+        oq, od = oracle.q8_0_quantize(src)
+        assert np.array_equal(qs, oq) and np.array_equal(d, od)
+        if dt == lq8_lib.DTYPE_F32:
+            assert np.array_equal(oracle.q8_0_pack(qs, d), gguf_fx[f"{name}_blocks"])
+
+
+def test_host_quantizer_rejects_bad_shapes(lq8_lib):
+    lib = lq8_lib.load()
+    assert lib.lq_q8_0_quantize_host(None, 0, 1, 33, None, None) == -1
+    assert b"multiple of 32" in lib.lq_last_error(None)
