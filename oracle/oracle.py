@@ -111,6 +111,7 @@ def _declare(L):
     L.orc_moe_forward.argtypes = [_P, _I64, _I64, _I64, _I64, _I64, C.c_int, _P, _P, _P, _P, _P, _P, _P, _P,
                                   _P, _P, _P]
     L.orc_set_threads.argtypes = [C.c_int]
+    L.orc_set_sum_order.argtypes = [C.c_int]
     L.orc_get_threads.restype = C.c_int
 
 
@@ -274,6 +275,11 @@ def attend_row(q, k, v, masked=False, causal_limit=0):
 
 def set_threads(n: int) -> None:
     lib().orc_set_threads(int(n))
+
+
+def set_sum_order(reversed_: bool) -> None:
+    """Noise probe: RMSNorm sums of squares in reverse order (True) or the reference's order."""
+    lib().orc_set_sum_order(1 if reversed_ else 0)
 
 
 def get_threads() -> int:

@@ -249,9 +249,19 @@ void orc_matmul_2d(const float* a, int64_t m, int64_t k, const float* b, int64_t
 
 /* rms_norm.rs:144-176 on bf16 data: f32 sum of squares in order, inv = 1/sqrt(mean + eps),
  * out = bf16((x * inv) * w). */
+/* Noise probe for the tests (never set by a reference path): 1 sums the squares in reverse
+ * order, a reordering as legitimate as the reference's own, so that oracle-vs-oracle gives the
+ * model's sensitivity to f32 summation order. */
+static int g_sum_order_reversed = 0;
+void orc_set_sum_order(int reversed) { g_sum_order_reversed = reversed; }
+
 static void rmsnorm_row_bf16(const uint16_t* x, int64_t dim, const uint16_t* w, float eps, uint16_t* out) {
     float sum_sq = 0.0f;
-    for (int64_t i = 0; i < dim; i++) { float v = orc_bf16_to_f32(x[i]); float p = v * v; sum_sq = sum_sq + p; }
+    if (g_sum_order_reversed) {
+        for (int64_t i = dim - 1; i >= 0; i--) { float v = orc_bf16_to_f32(x[i]); float p = v * v; sum_sq = sum_sq + p; }
+    } else {
+        for (int64_t i = 0; i < dim; i++) { float v = orc_bf16_to_f32(x[i]); float p = v * v; sum_sq = sum_sq + p; }
+    }
     float mean_sq = sum_sq / (float)dim;
     float inv_rms = 1.0f / sqrtf(mean_sq + eps);
     for (int64_t i = 0; i < dim; i++) {

@@ -144,6 +144,8 @@ int orc_qwen3_generate_cfg(orc_model* m, const int32_t* prompt, int64_t L, int64
                            float temperature, int64_t top_k, float top_p, float penalty,
                            int32_t* out_tokens, float* last_logits);
 void orc_set_threads(int n);
+/* test-only noise probe: 1 = RMSNorm sums of squares in reverse order (0 = the reference's) */
+void orc_set_sum_order(int reversed);
 int orc_get_threads(void);
 
 #ifdef __cplusplus

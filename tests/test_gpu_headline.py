@@ -41,9 +41,13 @@ QWEN3_30B_A3B_2L = dict(hidden=2048, layers=2, n_heads=32, n_kv_heads=4, head_di
                         max_pos=40960, tied=0, eps=1e-6, theta=1e6, init_std=0.02, norm_std=0.0, n_experts=128,
                         top_k=8, moe_inter=768, norm_topk=1)
 
-# 2-layer dense models at these widths and contexts (measured maxima on B200 are recorded
-# by the test through LQ_PARITY_LOG); the op-level tests pin the kernels far tighter
-DENSE_COS, DENSE_MAXREL = 0.9999, 1e-2
+# The noise floor of these models: the oracle against itself with only its RMSNorm sums of
+# squares reversed (orc_set_sum_order, as legitimate an order as the reference's) differs by
+# cosine 0.99979 and max-relative 2.2e-2 on the 8B shapes (2 layers, 256-token prompt) and by
+# 0.99994 / 1.1e-2 on the 32B shapes; the GPU measured 0.99979 / 2.05e-2 and 0.99993 / 1.1e-2
+# (2.5e-2 on the TP4 shard's shapes). The bound is about twice the floor; the op-level tests
+# pin the kernels themselves far tighter (bit-exact or the f32 reordering bound).
+DENSE_COS, DENSE_MAXREL = 0.9995, 5e-2
 # MoE: a router near-tie can pick another expert for one token (see test_gpu_moe.py)
 MOE_COS, MOE_MAXREL = 0.99, 0.15
 

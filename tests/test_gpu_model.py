@@ -125,8 +125,9 @@ def test_qwen3_0_6b_greedy_tokens(ctx, lq8_lib, oracle):
     Teacher-forced (both sides fed the oracle's token), every step: logits within the
     deep-model tolerance; the greedy token equal to the oracle's at >= 29 of 32 steps, and
     any mismatch only where the oracle's top-1/top-2 margin lies inside the step's measured
-    noise band 2*max|dlogit|. Free-running: identical tokens up to the first step whose
-    margin lies inside its band (where the trajectories can first part)."""
+    noise band 2*max|dlogit|. Free-running: all 32 greedy tokens identical to the oracle's
+    (measured on B200: 32 of 32, although step 3's margin lies inside its noise band; the
+    kernels are deterministic, so the same inputs give the same tokens on every run)."""
     cfgd = dict(lq8_lib.QWEN3_0_6B)
     gm, ocfg = _models(lq8_lib, oracle, ctx, 1234, cfgd, ctx_max=64)
     om = oracle.Qwen3Model(ocfg, 1234, ctx_max=64)
@@ -157,8 +158,7 @@ def test_qwen3_0_6b_greedy_tokens(ctx, lq8_lib, oracle):
     toks = gm.generate(prompt, 32)[0]
     record("0.6b_free_running", teacher_forced_matches=matches, first_band=first_band,
            identical=int(np.sum(np.cumprod(toks == otoks))), gpu=toks.tolist(), oracle=otoks.tolist())
-    upto = 32 if first_band is None else first_band
-    assert np.array_equal(toks[:upto], otoks[:upto])
+    assert np.array_equal(toks, otoks), (toks.tolist(), otoks.tolist())
 
 
 def test_prefill_after_decode_is_reproducible(ctx, lq8_lib, oracle):
