@@ -1,19 +1,26 @@
 """Benchmark: Q8_0 decode tokens/s of the Qwen3 runner on B200 (liblq8.so), one JSON line.
 
-Workload: Qwen3-8B architecture, seeded random-init Q8_0 weights, batch
-B (default 1) of 2048-token seeded prompts prefilled once, then greedy decode steps at
-context 2048+. A step = one decode step of every sequence (B tokens). The timed region
-replays the CUDA-graph decode step K times with tokens and KV caches resident in HBM;
-`e2e` times the same steps through the public C-ABI call lq_qwen3_decode_step with host
-token buffers (host->device copy of the input ids and device->host copy of the next ids
-inside the timed region). Every step streams all 8.1 GB of Q8_0 weights, 64x the 126 MB
-L2, so no L2 flush is needed between steps.
+Default workload (the configuration quoted at 1/2/4/8 B200): Qwen3-32B
+architecture, seeded random-init Q8_0 weights, batch 8 of 1024-token seeded prompts prefilled
+once, then greedy decode steps at context 1024+. On N GPUs (torchrun, one rank per GPU) the
+model is tensor-parallel over all N ranks (--tp 0, the default): q/k/v and gate/up split by
+output rows, o and down by K with the partial sums exchanged inside the persistent decode
+kernel over NVLink (LQ_TP_NCCL=1: per-layer kernels with NCCL all-reduces), the LM head by
+vocabulary rows; one batch for the whole group, so the scaling is strong. A step = one decode
+step of every sequence (B tokens). The timed region replays the CUDA-graph decode step K times
+with tokens and KV caches resident in HBM (device time, max over ranks); `e2e` times the same
+steps through the public C-ABI call lq_qwen3_decode_step with host token buffers (host->device
+copy of the input ids and device->host copy of the next ids inside the timed region). Every
+step streams all Q8_0 weights of the rank (GBs, far above the 126 MB L2), so no L2 flush is
+needed between steps.
 
-Multi-GPU (torchrun, one rank per GPU): each rank runs its own replica (no data-path
-collective); value = tokens of all ranks / max-over-ranks time ("scaling": "weak").
+Other workloads: --config qwen3-8b (config 3; batch 1, 2048-token prompt by default),
+qwen3-0.6b (config 1), qwen3-30b-a3b (config 5, expert-parallel under N ranks); --tp 1 runs
+independent replicas per rank ("scaling": "weak").
 
 --impl reference: the reference's CPU path (the C restatement in oracle/, all host threads)
-on the same model config, bounded sample (short prompt), rank 0 only.
+on the same model config at batch 1 (the reference decodes one sequence), bounded sample
+(16-token prompt), rank 0 only.
 """
 from __future__ import annotations
 
@@ -46,6 +53,8 @@ CONFIGS = {
                           vocab=151936, max_pos=40960, tied=0, eps=1e-6, theta=1e6, init_std=0.02,
                           norm_std=0.0, n_experts=128, top_k=8, moe_inter=768, norm_topk=1),
 }
+# (batch, prefill tokens) of each BASELINE configuration
+DEFAULT_SHAPE = {"qwen3-32b": (8, 1024), "qwen3-8b": (1, 2048), "qwen3-0.6b": (1, 16), "qwen3-30b-a3b": (64, 512)}
 SEED = 1234
 METRIC = "Q8_0 decode tok/s"
 
@@ -261,7 +270,7 @@ def run_ours(args, cfgd, world, rank, local):
     ctx = lq8.Context(local)
     cfg = lq8.make_config(**cfgd)
     comm = None
-    tp = args.tp if world > 1 else 1
+    tp = (args.tp or world) if world > 1 else 1
     if tp > 1:
         if tp != world:
             raise SystemExit(f"--tp {tp} needs exactly {tp} ranks (got {world})")
@@ -409,7 +418,7 @@ def run_ours(args, cfgd, world, rank, local):
         # one launch per step streams every Q8_0 weight once and reads the KV cache rows of the
         # attended positions (K and V, f32); timed as the whole decode graph, of which the
         # persistent kernel is all but a few microseconds of device time (ncu launch list)
-        hkv = cfgd["n_kv_heads"]
+        hkv = cfgd["n_kv_heads"] // tp  # this rank's kv heads
         ctx_avg = L + W + (K + 1) / 2.0
         kv_bytes = cfgd["layers"] * B * hkv * ctx_avg * 128 * 4 * 2
         alg = wbytes + kv_bytes
@@ -634,9 +643,9 @@ def main():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="qwen3-8b", choices=sorted(CONFIGS))
-    ap.add_argument("--batch", type=int, default=1)
-    ap.add_argument("--prompt", type=int, default=2048)
+    ap.add_argument("--config", default="qwen3-32b", choices=sorted(CONFIGS))
+    ap.add_argument("--batch", type=int, default=0, help="sequences per step (0: the config's batch)")
+    ap.add_argument("--prompt", type=int, default=0, help="prompt tokens (0: the config's prefill length)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--ncu-steps", type=int, default=0,
                     help="profiling: run this many decode steps between cudaProfilerStart/Stop and exit")
@@ -651,9 +660,9 @@ def main():
     ap.add_argument("--sweep-case", default="",
                     help="with --sweep: one case 'm,n,k' (two weight copies; for profiling)")
     ap.add_argument("--sweep-reps", type=int, default=20)
-    ap.add_argument("--tp", type=int, default=1,
-                    help="model parallelism over the torchrun ranks (NCCL): tensor-parallel for dense "
-                         "configs, expert-parallel for MoE; 1 = independent replicas")
+    ap.add_argument("--tp", type=int, default=0,
+                    help="model parallelism over the torchrun ranks: tensor-parallel for dense configs, "
+                         "expert-parallel for MoE; 0 = all ranks, 1 = independent replicas")
     ap.add_argument("--moe", action="store_true",
                     help="time lq_moe_forward alone at the Qwen3-30B-A3B expert shape and exit")
     ap.add_argument("--moe-rows", default="1,8,64,512")
@@ -668,6 +677,9 @@ def main():
         return
     world, rank, local = dist_env()
     cfgd = dict(CONFIGS[args.config])
+    batch0, prompt0 = DEFAULT_SHAPE[args.config]
+    args.batch = args.batch or batch0
+    args.prompt = args.prompt or prompt0
     if args.layers:
         cfgd["layers"] = args.layers
     if args.impl == "reference":

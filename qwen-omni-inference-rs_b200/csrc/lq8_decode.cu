@@ -43,7 +43,7 @@ namespace lq {
 constexpr int PD_ROWS = 16;  // weight rows per stage (two per consumer warp)
 constexpr int PD_KC = 1024;  // K bytes per stage (one Q8_0 block per lane and row)
 constexpr int PD_STAGE = PD_ROWS * PD_KC + PD_ROWS * (PD_KC / 32) * 2;  // 17 KiB
-constexpr int PD_STAGES = 8;
+constexpr int PD_MAX_STAGES = 8;  // ring depth: PdParams::ns stages (3..8, what shared memory allows)
 constexpr int PD_CONS = 8;
 constexpr int PD_CTHREADS = PD_CONS * 32;
 constexpr int PD_THREADS = PD_CTHREADS + 32;
@@ -51,6 +51,8 @@ constexpr int PD_ATT_C = 64;
 constexpr int PD_KS = 128 + 4;  // padded K row (floats): conflict-free float4 reads
 constexpr int PD_MAX_SPLITS = 128;
 constexpr int PD_MAX_G = 8;
+constexpr int PD_MAX_M = 8;  // batch rows of one step (GEMV output lanes 8r + m: m < 8)
+constexpr int PD_MAX_TP = 8;  // tensor-parallel ranks whose exchange slots a step addresses
 constexpr uint64_t PD_WAIT_NS = 2000000000ull;
 
 // one weight matrix: its Q8_0 rows viewed as [N][K/8] 8-byte elements and its scales [N][K/32]
@@ -88,6 +90,18 @@ struct PdParams {
     unsigned* bar;             // [0] grid barrier, [1 + b*Hkv + kvh] published-chunk counters;
                                // zero at launch
     int* err;
+    int ns;                    // ring stages
+    // tensor parallelism (tp > 1): o and down are row-parallel; each CTA pushes the partial
+    // sums of its units to every rank's exchange buffer and adds all ranks' partials in rank
+    // order (the same units fall to the same CTA index on every rank); the LM head's argmax
+    // keys (global vocabulary index) go to every rank by 64-bit atomic max
+    int tp, rank, vbase;
+    float* xpeer[PD_MAX_TP];               // exchange buffers [2][tp][H/16][8 warps][16]
+    unsigned* fpeer[PD_MAX_TP];            // counters [gridDim.x] per CTA, then [1] for the keys
+    unsigned long long* kpeer[PD_MAX_TP];  // argmax keys [M] of every rank
+    float* xself;                          // xpeer[rank]
+    unsigned* fself;                       // fpeer[rank]
+    unsigned* seq;                         // [0] exchanges and [1] steps completed before this one
 };
 
 // attention staging (the union area during ATT)
@@ -108,20 +122,25 @@ struct PdAtt {
 
 // 128-byte multiple: the union area behind it takes 16-byte vector and cp.async accesses
 struct alignas(128) PdSmem {
-    uint8_t stage[PD_STAGES][PD_STAGE];
-    uint64_t full[PD_STAGES];
-    uint64_t empty[PD_STAGES];
+    uint64_t full[PD_MAX_STAGES];
+    uint64_t empty[PD_MAX_STAGES];
     float red[32];
-    unsigned long long keys[4];
-    int tag[PD_STAGES];    // the unit a stage belongs to (-1: the phase has no more units for us)
+    unsigned long long keys[PD_MAX_M];
+    int tag[PD_MAX_STAGES];  // the unit a stage belongs to (-1: the phase has no more units for us)
     uint64_t hfull[2];     // gate|up: hbuf[b] written by the 8 consumer warps
     uint64_t hfree[2];     // gate|up: hbuf[b] quantized by warp 0
-    float hbuf[2][4][32];  // gate|up: one Q8_0 block of SiLU(gate)*up per row (two units in turn)
+    float hbuf[2][PD_MAX_M][32];  // gate|up: one Q8_0 block of SiLU(gate)*up per row (two units in turn)
     int flag;  // grid barrier outcome
     int fail;  // a consumer warp gave up waiting for a stage
-    int pad_[2];
-    // followed by the union area: the GEMV activations or PdAtt
+    int ns;    // ring stages
+    int pad_;
+    // followed by the ring (ns stages of PD_STAGE bytes), then the union area: the GEMV
+    // activations or PdAtt
 };
+
+// the dynamic shared memory: PdSmem, the ring, the union area
+extern __shared__ __align__(1024) uint8_t pd_dsmem[];
+__device__ __forceinline__ uint8_t* pd_stage(int s) { return pd_dsmem + sizeof(PdSmem) + (size_t)s * PD_STAGE; }
 
 static_assert(sizeof(PdSmem) % 128 == 0 && PD_STAGE % 128 == 0, "shared-memory regions must stay 128-byte aligned");
 
@@ -189,11 +208,12 @@ __device__ __forceinline__ bool pd_produce(PdSmem& S, const PdGemv& g, unsigned 
     const int units = pd_units(g);
     const int halves = g.swi ? 2 : 1;
     const unsigned bytes = (unsigned)(PD_ROWS * kc + PD_ROWS * (kc / 16));  // whole boxes (OOB zero-filled)
+    const int ns = S.ns;
     for (int u = pd_first(off);; u += gridDim.x) {
-        const int s0 = it % PD_STAGES;
+        const int s0 = it % ns;
         if (u >= units) {
             // phase end marker: a stage without data
-            if (!pd_wait(&S.empty[s0], ((unsigned)(it / PD_STAGES) & 1u) ^ 1u, err)) {
+            if (!pd_wait(&S.empty[s0], ((unsigned)(it / ns) & 1u) ^ 1u, err)) {
                 atomicCAS(err, 0, 41);
                 return false;
             }
@@ -206,12 +226,12 @@ __device__ __forceinline__ bool pd_produce(PdSmem& S, const PdGemv& g, unsigned 
             for (int half = 0; half < halves; half++) {
                 const int r0 = half * nout + u * pd_unit_rows(g) + grp * PD_ROWS;
                 for (int c = 0; c < nchunks; c++, it++) {
-                    const int s = it % PD_STAGES;
-                    if (!pd_wait(&S.empty[s], ((unsigned)(it / PD_STAGES) & 1u) ^ 1u, err)) {
+                    const int s = it % ns;
+                    if (!pd_wait(&S.empty[s], ((unsigned)(it / ns) & 1u) ^ 1u, err)) {
                         atomicCAS(err, 0, 41);
                         return false;
                     }
-                    uint8_t* st = S.stage[s];
+                    uint8_t* st = pd_stage(s);
                     S.tag[s] = u;
                     mbar_expect_tx(&S.full[s], bytes);
                     tma_load_2d(st, &g.mat->wq, c * (kc / 8), r0, &S.full[s]);
@@ -319,7 +339,8 @@ template <int M>
 __device__ __forceinline__ bool pd_consume(PdSmem& S, const PdGemv& g, const int8_t* xs, const uint16_t* xds,
                                            int& it, int& hn, float* out, int ldo, bool resid, bool keys,
                                            int8_t* hq, uint16_t* hd, int* err, int u_first = -1,
-                                           float res_first = 0.0f) {
+                                           float res_first = 0.0f, const PdParams* xp = nullptr, int xpar = 0,
+                                           int kbase = 0) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int sw = (lane >> 2) & 1;
     const int K = g.K, nb = K >> 5;
@@ -327,6 +348,7 @@ __device__ __forceinline__ bool pd_consume(PdSmem& S, const PdGemv& g, const int
     const int nchunks = (K + kc - 1) / kc;
     const int nout = g.swi ? g.N / 2 : g.N;
     const int halves = g.swi ? 2 : 1;
+    const int ns = S.ns;
     float acc[2][M], gate[2][M];
 #pragma unroll
     for (int r = 0; r < 2; r++)
@@ -337,7 +359,7 @@ __device__ __forceinline__ bool pd_consume(PdSmem& S, const PdGemv& g, const int
     bool failed = false;
     auto wait_full = [&](int s) {
         int ok = 1;
-        if (lane == 0) ok = pd_wait(&S.full[s], (unsigned)(it / PD_STAGES) & 1u, err);
+        if (lane == 0) ok = pd_wait(&S.full[s], (unsigned)(it / ns) & 1u, err);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         __syncwarp();  // the other lanes read the stage after lane 0 saw it complete
         if (!ok) {
@@ -350,7 +372,7 @@ __device__ __forceinline__ bool pd_consume(PdSmem& S, const PdGemv& g, const int
         return ok != 0;
     };
     while (!failed) {
-        const int s0 = it % PD_STAGES;
+        const int s0 = it % ns;
         if (!wait_full(s0)) break;
         int u = 0;
         if (lane == 0) u = S.tag[s0];
@@ -388,12 +410,12 @@ __device__ __forceinline__ bool pd_consume(PdSmem& S, const PdGemv& g, const int
             const int r0 = u * pd_unit_rows(g) + grp * PD_ROWS;
             const int rows = min(PD_ROWS, nout - r0);
             for (int c = 0; c < nchunks; c++, it++) {
-                const int s = it % PD_STAGES;
+                const int s = it % ns;
                 if ((grp | half | c) != 0 && !wait_full(s)) break;
                 const int k0 = c * kc, nbc = min(kc, K - k0) >> 5;
                 const bool act = lane < nbc;
-                const int8_t* wst = reinterpret_cast<const int8_t*>(S.stage[s]) + (2 * warp) * kc + lane * 32;
-                const uint16_t* dst = reinterpret_cast<const uint16_t*>(S.stage[s] + PD_ROWS * kc) + (2 * warp) * (kc / 32) + lane;
+                const int8_t* wst = reinterpret_cast<const int8_t*>(pd_stage(s)) + (2 * warp) * kc + lane * 32;
+                const uint16_t* dst = reinterpret_cast<const uint16_t*>(pd_stage(s) + PD_ROWS * kc) + (2 * warp) * (kc / 32) + lane;
                 int4 w[2][2];
                 float dw[2] = {0.f, 0.f};
                 if (act) {
@@ -421,6 +443,7 @@ __device__ __forceinline__ bool pd_consume(PdSmem& S, const PdGemv& g, const int
                     }
                 }
                 if (c == nchunks - 1) {
+                    float xv[2][M];  // the unit's partial sums when they go to the exchange
 #pragma unroll
                     for (int r = 0; r < 2; r++) {
                         const int rr = 2 * warp + r, row = r0 + rr;
@@ -428,15 +451,35 @@ __device__ __forceinline__ bool pd_consume(PdSmem& S, const PdGemv& g, const int
                         for (int m = 0; m < M; m++) {
                             const float v = warp_sum(acc[r][m]);
                             acc[r][m] = 0.0f;
+                            xv[r][m] = v;
                             if (g.swi) {
                                 if (half == 0) gate[r][m] = v;
                                 else if (lane == 0) S.hbuf[hb][m][grp * PD_ROWS + rr] = swiglu(gate[r][m], v);
-                            } else if (rr < rows) {
+                            } else if (rr < rows && !xp) {
                                 if (lane == 8 * r + m) {
                                     const size_t o = (size_t)m * ldo + row;
                                     out[o] = resid ? __fadd_rn(res, v) : v;
                                 }
-                                if (keys && lane == 8 * r) atomicMax(&S.keys[m], argmax_key(v, row));
+                                if (keys && lane == 8 * r) atomicMax(&S.keys[m], argmax_key(v, row + kbase));
+                            }
+                        }
+                    }
+                    if (xp) {
+                        // this warp's 2 rows x M tokens, 16 floats [token][row] at (unit, warp) of
+                        // every rank's slot: lane q stores tokens 2q and 2q+1 as one 16-byte vector
+#pragma unroll
+                        for (int q = 0; q < (M + 1) / 2; q++) {
+                            if (lane == q) {
+                                const bool has1 = 2 * q + 1 < M;
+                                const int m1 = has1 ? 2 * q + 1 : 2 * q;
+                                const float4 f = make_float4(xv[0][2 * q], xv[1][2 * q], has1 ? xv[0][m1] : 0.0f,
+                                                             has1 ? xv[1][m1] : 0.0f);
+                                const size_t slot = (size_t)(g.N / PD_ROWS) * PD_CONS * 16;
+                                const size_t off = ((size_t)xpar * xp->tp + xp->rank) * slot +
+                                                   ((size_t)u * PD_CONS + warp) * 16 + 4 * q;
+#pragma unroll
+                                for (int t = 0; t < PD_MAX_TP; t++)
+                                    if (t < xp->tp) *reinterpret_cast<float4*>(xp->xpeer[t] + off) = f;
                             }
                         }
                     }
@@ -471,6 +514,90 @@ __device__ __forceinline__ bool pd_consume(PdSmem& S, const PdGemv& g, const int
     }
     pd_csync();
     return S.fail == 0;
+}
+
+// ---- tensor parallelism: the row-parallel exchange ----
+
+// bounded wait until the counter at p (written by other GPUs) reaches target (wrap-safe);
+// false when it gave up (~2 s; error `code`) or another CTA flagged an error
+__device__ __forceinline__ bool pd_wait_sys(const unsigned* p, unsigned target, int* err, int code) {
+    const uint64_t t0 = global_ns();
+    for (int i = 1;; i++) {
+        unsigned v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+        if ((int)(v - target) >= 0) return true;
+        if ((i & 63) == 0) {
+            if (ld_volatile(err) != 0) return false;
+            if (global_ns() - t0 > PD_WAIT_NS) {
+                atomicCAS(err, 0, code);
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void pd_signal_sys(unsigned* p) {
+    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(p) : "memory");
+}
+
+// After a row-parallel phase (o or down) under tensor parallelism: this CTA has stored the
+// partial sums of its units into slot (par, rank) of every rank's exchange buffer
+// (pd_consume); it publishes them (system-scope fence, then one counter increment on every
+// peer), waits until every peer's CTA of the same index -- which computed the same units --
+// has done the same here, and adds x[m][row] += p_0 + p_1 + ... + p_{tp-1} (rank order, so
+// every rank forms the same residual stream). The grid barrier that follows orders these
+// writes before any CTA reads x. target: the counter's value once this exchange is complete.
+template <int M>
+__device__ bool pd_exchange_sum(const PdParams& p, PdSmem& S, int par, unsigned target, int u_first) {
+    const int tid = threadIdx.x, T = p.tp, units = p.H / PD_ROWS;
+    if (tid == 0) {
+        __threadfence_system();  // the CTA's peer stores, ordered before by the consumer barrier
+#pragma unroll
+        for (int t = 0; t < PD_MAX_TP; t++)
+            if (t < T && t != p.rank) pd_signal_sys(p.fpeer[t] + blockIdx.x);
+        S.flag = pd_wait_sys(p.fself + blockIdx.x, target, p.err, 48) ? 1 : 0;
+    }
+    pd_csync();
+    if (!S.flag) return false;
+    const size_t slot = (size_t)units * PD_CONS * 16;  // floats per (par, source rank)
+    const float* xb = p.xself + (size_t)par * T * slot;
+    for (int u = u_first; u < units; u += (int)gridDim.x) {
+        for (int idx = tid; idx < PD_ROWS * M; idx += PD_CTHREADS) {
+            const int m = idx / PD_ROWS, rr = idx % PD_ROWS;
+            const size_t off = ((size_t)u * PD_CONS + (rr >> 1)) * 16 + m * 2 + (rr & 1);
+            float v = __ldcg(xb + off);
+            for (int t = 1; t < T; t++) v = __fadd_rn(v, __ldcg(xb + (size_t)t * slot + off));
+            float* xo = p.x + (size_t)m * p.H + (size_t)u * PD_ROWS + rr;
+            *xo = __fadd_rn(__ldcg(xo), v);
+        }
+    }
+    return true;
+}
+
+// the LM head's argmax keys under tensor parallelism: every CTA takes the maximum of its keys
+// (global vocabulary indices) into every rank's key array, then counts itself in on every rank;
+// CTA 0 waits for all CTAs of all ranks (the token is final) and advances the exchange counts
+// the next step starts from
+template <int M>
+__device__ void pd_keys_exchange(const PdParams& p, PdSmem& S, unsigned seq0, unsigned steps0) {
+    const int tid = threadIdx.x, T = p.tp;
+    if (tid < M && S.keys[tid]) {
+#pragma unroll
+        for (int t = 0; t < PD_MAX_TP; t++)
+            if (t < T) atomicMax(p.kpeer[t] + tid, S.keys[tid]);
+    }
+    pd_csync();
+    if (tid == 0) {
+        __threadfence_system();
+#pragma unroll
+        for (int t = 0; t < PD_MAX_TP; t++)
+            if (t < T) pd_signal_sys(p.fpeer[t] + gridDim.x);
+        if (blockIdx.x == 0 &&
+            pd_wait_sys(p.fself + gridDim.x, (steps0 + 1u) * gridDim.x * (unsigned)T, p.err, 49)) {
+            p.seq[0] = seq0 + 2u * (unsigned)p.n_layers;
+            p.seq[1] = steps0 + 1u;
+        }
+    }
 }
 
 // ---- attention (the decode attention kernel's arithmetic, on 256 threads) ----
@@ -775,17 +902,20 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
 // ---- the kernel ----
 template <int M>
 __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdParams p) {
-    extern __shared__ __align__(1024) uint8_t smem_raw[];
-    PdSmem& S = *reinterpret_cast<PdSmem*>(smem_raw);
-    uint8_t* area = smem_raw + sizeof(PdSmem);
+    PdSmem& S = *reinterpret_cast<PdSmem*>(pd_dsmem);
+    uint8_t* area = pd_dsmem + sizeof(PdSmem) + (size_t)p.ns * PD_STAGE;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int p0 = *p.pos_dev;
+    // exchanges and steps completed before this launch (tensor parallelism): CTA 0 advances them
+    // only after every CTA of every rank has contributed its last keys, long after this read
+    const unsigned seq0 = p.tp > 1 ? p.seq[0] : 0u, steps0 = p.tp > 1 ? p.seq[1] : 0u;
+    const bool xch = p.tp > 1;
     if (p0 < 0 || p0 >= p.ctx_max) {  // every CTA leaves before any copy or barrier
         if (tid == 0) atomicCAS(p.err, 0, 44);
         return;
     }
     if (tid == 0) {
-        for (int s = 0; s < PD_STAGES; s++) {
+        for (int s = 0; s < PD_MAX_STAGES; s++) {
             mbar_init(&S.full[s], 1);
             mbar_init(&S.empty[s], PD_CONS);
         }
@@ -795,8 +925,11 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
         }
         mbar_fence_init();
     }
-    if (tid < 4) S.keys[tid] = 0ull;
-    if (tid == 0) S.fail = 0;
+    if (tid < PD_MAX_M) S.keys[tid] = 0ull;
+    if (tid == 0) {
+        S.fail = 0;
+        S.ns = p.ns;
+    }
     __syncthreads();
     if (warp == PD_CONS) {
         // producer: every matrix of the step, in order, never waiting for activations
@@ -812,8 +945,8 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
                 }
             if (ok) pd_produce(S, pd_gemv(p, 0, PH_LM), off, it, p.err);
             // leave only after the copies in flight have landed (bounded)
-            for (int j = max(0, it - PD_STAGES); j < it; j++)
-                mbar_wait_ns(&S.full[j % PD_STAGES], (unsigned)(j / PD_STAGES) & 1u, PD_WAIT_NS);
+            for (int j = max(0, it - p.ns); j < it; j++)
+                mbar_wait_ns(&S.full[j % p.ns], (unsigned)(j / p.ns) & 1u, PD_WAIT_NS);
         }
         return;
     }
@@ -874,10 +1007,12 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
             pd_prefetch(xds, p.att_d, M * (Ko / 32) * 2, tid);
             cp_async_wait<0>();
             pd_csync();
-            if (!pd_consume<M>(S, pd_gemv(p, l, PH_O), xs, xds, it, hn, p.x, H, true, false, nullptr, nullptr,
-                               p.err, u_o, res_o))
+            if (!pd_consume<M>(S, pd_gemv(p, l, PH_O), xs, xds, it, hn, p.x, H, !xch, false, nullptr, nullptr,
+                               p.err, u_o, res_o, xch ? &p : nullptr, 0))
                 return;
         }
+        if (xch && !pd_exchange_sum<M>(p, S, 0, (seq0 + 2u * (unsigned)l + 1u) * (unsigned)(p.tp - 1), u_o))
+            return;
         pd_grid_arrive(p, epoch);
         pd_prefetch(nws, L.post_norm, H * 2, tid);
         if (!pd_grid_wait(p, S, epoch)) return;
@@ -894,8 +1029,10 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
         pd_prefetch(xds, p.hd, M * (I / 32) * 2, tid);
         cp_async_wait<0>();
         pd_csync();
-        if (!pd_consume<M>(S, pd_gemv(p, l, PH_DN), xs, xds, it, hn, p.x, H, true, false, nullptr, nullptr, p.err,
-                           u_dn, res_dn))
+        if (!pd_consume<M>(S, pd_gemv(p, l, PH_DN), xs, xds, it, hn, p.x, H, !xch, false, nullptr, nullptr, p.err,
+                           u_dn, res_dn, xch ? &p : nullptr, 1))
+            return;
+        if (xch && !pd_exchange_sum<M>(p, S, 1, (seq0 + 2u * (unsigned)l + 2u) * (unsigned)(p.tp - 1), u_dn))
             return;
         pd_grid_arrive(p, epoch);
         pd_prefetch(nws, l + 1 < p.n_layers ? p.layers[l + 1].in_norm : p.final_norm, H * 2, tid);
@@ -904,10 +1041,11 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
     // LM head: final RMSNorm, logits, greedy argmax keys
     norm_rows();
     if (!pd_consume<M>(S, pd_gemv(p, 0, PH_LM), xs, xds, it, hn, p.logits, p.V, false, true, nullptr, nullptr,
-                       p.err))
+                       p.err, -1, 0.0f, nullptr, 0, p.vbase))
         return;
     pd_csync();
-    if (tid < M && S.keys[tid]) atomicMax(p.keys + tid, S.keys[tid]);
+    if (xch) pd_keys_exchange<M>(p, S, seq0, steps0);
+    else if (tid < M && S.keys[tid]) atomicMax(p.keys + tid, S.keys[tid]);
 }
 
 // ---- host ----
@@ -917,18 +1055,41 @@ static size_t pd_area_bytes(int64_t m, int64_t H, int64_t Hqd, int64_t I) {
     return std::max(gemv, sizeof(PdAtt));
 }
 
-static size_t pd_smem(int64_t m, int64_t H, int64_t Hqd, int64_t I) {
-    return sizeof(PdSmem) + pd_area_bytes(m, H, Hqd, I);
+constexpr size_t PD_SMEM_MAX = 227 * 1024;
+constexpr int PD_MIN_STAGES = 3;
+
+// ring stages that fit beside the union area (at most PD_MAX_STAGES; 0 when fewer than
+// PD_MIN_STAGES fit): wider K rows at larger batches give the activations more room
+static int pd_ns(int64_t m, int64_t H, int64_t Hqd, int64_t I) {
+    const size_t fixed = sizeof(PdSmem) + pd_area_bytes(m, H, Hqd, I);
+    if (fixed >= PD_SMEM_MAX) return 0;
+    const int ns = (int)std::min<size_t>(PD_MAX_STAGES, (PD_SMEM_MAX - fixed) / PD_STAGE);
+    return ns >= PD_MIN_STAGES ? ns : 0;
+}
+
+static size_t pd_smem_bytes(int64_t m, int64_t H, int64_t Hqd, int64_t I) {
+    return sizeof(PdSmem) + (size_t)pd_ns(m, H, Hqd, I) * PD_STAGE + pd_area_bytes(m, H, Hqd, I);
 }
 
 bool decode_persist_supported(lq_ctx* ctx, int64_t m, int64_t H, int64_t Hq, int64_t Hkv, int64_t I,
                               int64_t ctx_max) {
-    if (m < 1 || m > 4 || getenv("LQ_NO_PERSIST")) return false;
+    if (m < 1 || m > PD_MAX_M || getenv("LQ_NO_PERSIST")) return false;
     if (H % 256 || I % 256 || Hq % Hkv || Hq / Hkv > PD_MAX_G) return false;
     if (ctx_max > (int64_t)PD_ATT_C * PD_MAX_SPLITS) return false;
     int coop = 0;
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, ctx->device);
-    return coop && pd_smem(m, H, Hq * 128, I) <= 227 * 1024;
+    return coop && pd_ns(m, H, Hq * 128, I) > 0;
+}
+
+size_t decode_persist_xchg_layout(int64_t H, int tp, int sm_count, int64_t keys_n, size_t* flags_off,
+                                  size_t* keys_off, size_t* seq_off) {
+    auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
+    const size_t xbytes = al((size_t)2 * tp * (size_t)(H / PD_ROWS) * PD_CONS * 16 * 4);
+    const size_t fbytes = al((size_t)(sm_count + 1) * 4);
+    *flags_off = xbytes;
+    *keys_off = xbytes + fbytes;
+    *seq_off = *keys_off + al((size_t)std::max<int64_t>(PD_MAX_M, keys_n) * 8);
+    return *seq_off + 256;
 }
 
 size_t decode_persist_desc_bytes(int64_t n_layers) { return (size_t)(n_layers + 1) * sizeof(PdLayer); }
@@ -977,7 +1138,7 @@ int decode_persist_write_desc(lq_ctx* ctx, void* dev, const PdHostLayer* layers,
 template <int M>
 static int launch_pd(lq_ctx* ctx, const PdParams& p, size_t smem) {
     auto kern = decode_step_kernel<M>;
-    if (const int rc = ensure_func_smem(ctx, (const void*)kern, 227 * 1024)) return rc;
+    if (const int rc = ensure_func_smem(ctx, (const void*)kern, PD_SMEM_MAX)) return rc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ctx->sm_count);
     cfg.blockDim = dim3(PD_THREADS);
@@ -994,7 +1155,10 @@ static int launch_pd(lq_ctx* ctx, const PdParams& p, size_t smem) {
 }
 
 int launch_decode_persist(lq_ctx* ctx, const PdLaunch& a) {
-    if (a.m < 1 || a.m > 4) return set_error(ctx, LQ_ERR_INVALID_ARG, "decode_step: batch %lld > 4", (long long)a.m);
+    if (a.m < 1 || a.m > PD_MAX_M)
+        return set_error(ctx, LQ_ERR_INVALID_ARG, "decode_step: batch %lld > %d", (long long)a.m, PD_MAX_M);
+    const int ns = pd_ns(a.m, a.H, a.Hq * 128, a.I);
+    if (!ns) return set_error(ctx, LQ_ERR_UNSUPPORTED, "decode_step: shapes leave no room for the weight ring");
     PdParams p = {};
     p.layers = reinterpret_cast<const PdLayer*>(a.desc);
     p.n_layers = (int)a.n_layers;
@@ -1022,13 +1186,40 @@ int launch_decode_persist(lq_ctx* ctx, const PdLaunch& a) {
     p.keys = a.keys;
     p.bar = a.counters;
     p.err = ctx->err_flag;
+    p.ns = ns;
+    p.tp = a.tp;
+    p.rank = a.rank;
+    p.vbase = (int)a.vbase;
+    if (a.tp > 1) {
+        if (a.tp > PD_MAX_TP || a.rank < 0 || a.rank >= a.tp || a.H % PD_ROWS)
+            return set_error(ctx, LQ_ERR_INVALID_ARG, "decode_step: tensor-parallel world %d (at most %d)", a.tp,
+                             PD_MAX_TP);
+        size_t fo = 0, ko = 0, so = 0;
+        decode_persist_xchg_layout(a.H, a.tp, ctx->sm_count, a.keys_n, &fo, &ko, &so);
+        for (int t = 0; t < a.tp; t++) {
+            uint8_t* b = static_cast<uint8_t*>(a.xchg[t]);
+            if (!b) return set_error(ctx, LQ_ERR_INVALID_ARG, "decode_step: exchange region of rank %d missing", t);
+            p.xpeer[t] = reinterpret_cast<float*>(b);
+            p.fpeer[t] = reinterpret_cast<unsigned*>(b + fo);
+            p.kpeer[t] = reinterpret_cast<unsigned long long*>(b + ko);
+        }
+        p.xself = p.xpeer[a.rank];
+        p.fself = p.fpeer[a.rank];
+        p.seq = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(a.xchg[a.rank]) + so);
+        if (a.keys != p.kpeer[a.rank])
+            return set_error(ctx, LQ_ERR_INVALID_ARG, "decode_step: keys must be the exchange region's keys");
+    }
     LQ_CUDA(ctx, cudaMemsetAsync(a.counters, 0, decode_persist_counter_bytes(a.m, a.Hkv, a.n_layers), ctx->stream));
-    const size_t smem = pd_smem(a.m, a.H, a.Hq * 128, a.I);
+    const size_t smem = pd_smem_bytes(a.m, a.H, a.Hq * 128, a.I);
     switch (a.m) {
         case 1: return launch_pd<1>(ctx, p, smem);
         case 2: return launch_pd<2>(ctx, p, smem);
         case 3: return launch_pd<3>(ctx, p, smem);
-        default: return launch_pd<4>(ctx, p, smem);
+        case 4: return launch_pd<4>(ctx, p, smem);
+        case 5: return launch_pd<5>(ctx, p, smem);
+        case 6: return launch_pd<6>(ctx, p, smem);
+        case 7: return launch_pd<7>(ctx, p, smem);
+        default: return launch_pd<8>(ctx, p, smem);
     }
 }
 

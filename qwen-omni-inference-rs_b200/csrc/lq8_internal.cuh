@@ -302,7 +302,18 @@ struct PdLaunch {
     float* logits;     // [m][V]
     unsigned long long* keys;
     unsigned* counters;  // decode_persist_counter_bytes, zeroed by the launch
+    // tensor parallelism (tp > 1): every rank's exchange region (decode_persist_xchg_layout),
+    // indexed by rank, own included; zero-initialised on every rank before the first step
+    int tp = 1, rank = 0;
+    int64_t vbase = 0;     // first vocabulary row of this rank's LM-head shard
+    int64_t keys_n = 0;    // argmax keys the region holds (the model's max batch)
+    void* xchg[8] = {};
 };
+// the per-rank exchange region of the tensor-parallel persistent step: partial sums
+// [2][tp][H/16][8][16] f32 at 0, counters [sm_count + 1] u32 at *flags_off, argmax keys
+// [max(8, keys_n)] u64 at *keys_off, step counts [2] u32 at *seq_off; returns the total bytes
+size_t decode_persist_xchg_layout(int64_t H, int tp, int sm_count, int64_t keys_n, size_t* flags_off,
+                                  size_t* keys_off, size_t* seq_off);
 bool decode_persist_supported(lq_ctx* ctx, int64_t m, int64_t H, int64_t Hq, int64_t Hkv, int64_t I,
                               int64_t ctx_max);
 size_t decode_persist_desc_bytes(int64_t n_layers);

@@ -11,6 +11,7 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <cstring>
 #include <vector>
 
 namespace {
@@ -88,6 +89,10 @@ struct lq_model {
     int32_t* gen_base = nullptr;     // device position of the first decode step after prefill
     float* samp_scratch = nullptr;   // [max_batch][vocab] penalized logits
     std::vector<void*> allocs;
+    // tensor-parallel persistent step: every rank's exchange region (own: allocated here,
+    // peers': opened from their CUDA IPC handles)
+    void* xchg[8] = {};
+    std::vector<void*> ipc_open;
 };
 
 namespace {
@@ -252,6 +257,11 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
         a.logits = m->logits;
         a.keys = m->keys;
         a.counters = m->pd_counters;
+        a.tp = m->tp;
+        a.rank = m->rank;
+        a.vbase = m->vocab_off;
+        a.keys_n = m->max_batch;
+        for (int t = 0; t < m->tp && t < 8; t++) a.xchg[t] = m->xchg[t];
         RC(lq::launch_decode_persist(ctx, a));
         RC(finish_tokens(m, B, pos_dev, bump_pos));
         return LQ_OK;
@@ -372,8 +382,75 @@ int lq_qwen3_destroy(lq_model* m) {
     cudaSetDevice(m->ctx->device);
     cudaStreamSynchronize(m->ctx->stream);
     destroy_graph(m);
+    for (void* p : m->ipc_open) cudaIpcCloseMemHandle(p);
     for (void* p : m->allocs) cudaFree(p);
     delete m;
+    return LQ_OK;
+}
+
+// Tensor parallelism, persistent decode step: allocate this rank's exchange region (zeroed),
+// then one all-gather of (CUDA IPC handle, persistent batch, SM count, willingness) over the
+// communicator; if every rank is willing with the same batch and SM count (the same units fall
+// to the same CTA index everywhere), open the peers' regions. A second all-gather confirms that
+// every rank opened them, so all ranks decide alike (*want).
+static int tp_exchange_setup(lq_model* m, int64_t pb, bool* want) {
+    lq_ctx* ctx = m->ctx;
+    const int T = m->tp, rank = m->rank;
+    constexpr int W = 32;  // words per rank in the hand-over (128 bytes)
+    static_assert(sizeof(cudaIpcMemHandle_t) <= 27 * 4, "IPC handle does not fit the hand-over");
+    size_t fo = 0, ko = 0, so = 0;
+    const size_t bytes = lq::decode_persist_xchg_layout(m->c.hidden, T, ctx->sm_count, m->max_batch, &fo, &ko, &so);
+    int rc = dalloc(m, &m->xchg[rank], bytes);
+    if (rc) return rc;
+    LQ_CUDA(ctx, cudaMemsetAsync(m->xchg[rank], 0, bytes, ctx->stream));
+    uint32_t mine[W] = {};
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, m->xchg[rank]) != cudaSuccess) {
+        cudaGetLastError();
+        *want = false;
+    }
+    memcpy(mine, &h, sizeof h);
+    mine[28] = (uint32_t)pb;
+    mine[29] = (uint32_t)ctx->sm_count;
+    mine[30] = *want ? 1u : 0u;
+    float* dev = nullptr;
+    rc = dalloc(m, reinterpret_cast<void**>(&dev), (size_t)(T + 1) * W * 4);
+    if (rc) return rc;
+    std::vector<uint32_t> all((size_t)T * W);
+    LQ_CUDA(ctx, cudaMemcpyAsync(dev, mine, W * 4, cudaMemcpyHostToDevice, ctx->stream));
+    rc = lq::comm_allgather_f32(m->comm, dev, dev + W, W);  // bytes are moved, not added
+    if (rc) return rc;
+    LQ_CUDA(ctx, cudaMemcpyAsync(all.data(), dev + W, (size_t)T * W * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    LQ_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    bool ok = true;
+    for (int t = 0; t < T; t++) {
+        const uint32_t* r = all.data() + (size_t)t * W;
+        ok = ok && r[28] == (uint32_t)pb && r[29] == (uint32_t)ctx->sm_count && r[30] == 1u;
+    }
+    for (int t = 0; t < T && ok; t++) {
+        if (t == rank) continue;
+        cudaIpcMemHandle_t ph;
+        memcpy(&ph, all.data() + (size_t)t * W, sizeof ph);
+        void* p = nullptr;
+        if (cudaIpcOpenMemHandle(&p, ph, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            ok = false;
+            break;
+        }
+        m->ipc_open.push_back(p);
+        m->xchg[t] = p;
+    }
+    // every rank opened every peer's region, or none uses them
+    uint32_t flag[W] = {};
+    flag[0] = ok ? 1u : 0u;
+    LQ_CUDA(ctx, cudaMemcpyAsync(dev, flag, W * 4, cudaMemcpyHostToDevice, ctx->stream));
+    rc = lq::comm_allgather_f32(m->comm, dev, dev + W, W);
+    if (rc) return rc;
+    LQ_CUDA(ctx, cudaMemcpyAsync(all.data(), dev + W, (size_t)T * W * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    LQ_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    for (int t = 0; t < T; t++) ok = ok && all[(size_t)t * W] == 1u;
+    *want = ok;
+    if (ok) m->keys = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(m->xchg[rank]) + ko);
     return LQ_OK;
 }
 
@@ -556,10 +633,22 @@ static int create_model(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, 
         m->fused_decode = ok;
     }
     {
-        // the persistent decode step (dense models on one GPU); LQ_NO_PERSIST=1 keeps the
-        // per-layer kernels
-        const int64_t pb = std::min<int64_t>(max_batch, 4);
-        if (!moe && T == 1 && m->fused_decode && lq::decode_persist_supported(ctx, pb, H, Hq, Hkv, I, ctx_max)) {
+        // the persistent decode step (dense models, one GPU or tensor-parallel ranks that
+        // exchange the o/down partial sums inside the kernel); LQ_NO_PERSIST=1 keeps the
+        // per-layer kernels, LQ_TP_NCCL=1 the per-layer kernels with NCCL all-reduces under TP.
+        // The largest batch (up to 8) whose activations leave room for the weight ring.
+        int64_t pb = std::min<int64_t>(max_batch, 8);
+        while (pb > 0 && !lq::decode_persist_supported(ctx, pb, H, Hq, Hkv, I, ctx_max)) pb--;
+        bool want = !moe && m->fused_decode && pb > 0 && (T == 1 || getenv("LQ_TP_NCCL") == nullptr);
+        if (!moe && T > 1) {
+            // every rank must take the same path: agree on it, and share the exchange regions
+            int xrc = tp_exchange_setup(m, pb, &want);
+            if (xrc) {
+                lq_qwen3_destroy(m);
+                return xrc;
+            }
+        }
+        if (want) {
             std::vector<lq::PdHostLayer> hl(m->layers.size());
             const size_t kv_layer = (size_t)(max_batch * Hkv * ctx_max * D);
             for (size_t l = 0; l < m->layers.size(); l++) {

@@ -115,3 +115,41 @@ def test_persistent_step_matches_oracle(ctx, lq8_lib, oracle):
         tok = oracle.argmax(olg)
     assert gm.graph_kernels() == 3
     gm.close()
+
+
+@pytest.mark.parametrize("cfg_name,cfgd", [("wide", CONFIGS["wide"]), ("gqa8_ragged_vocab", CONFIGS["gqa8_ragged_vocab"]),
+                                           ("qwen3_8b_2l", dict(TINY, hidden=4096, inter=12288, n_heads=32,
+                                                                n_kv_heads=8, vocab=151936, tied=0))])
+def test_persistent_batch8_equals_two_batch4(ctx, lq8_lib, oracle, cfg_name, cfgd):
+    """Batches of 5-8 rows: the persistent step keeps each row's arithmetic independent of the
+    batch size (per-row GEMV lanes, per-chunk attention partials merged in chunk order, per-row
+    norms), and a smaller ring when the activations of 8 rows need the room (8B shapes: 5
+    stages). So decoding 8 sequences at once gives each row exactly the logits of decoding them
+    as two batches of 4, which the persistent step runs bit-identical to the per-layer path
+    (both fed the same tokens after the same prefill KV rows)."""
+    seed, L, steps = 5, 70, 4
+    cfg = lq8_lib.make_config(**cfgd)
+    prompts = np.stack([oracle.gen_tokens(seed, s, L, cfgd["vocab"]) for s in range(8)])
+    big = lq8_lib.Qwen3ForCausalLM(ctx, cfg, seed, max_batch=8, ctx_max=96)
+    small = lq8_lib.Qwen3ForCausalLM(ctx, cfg, seed, max_batch=4, ctx_max=96)
+    try:
+        t8, l8 = big.prefill(prompts, want_logits=True)
+        big.set_batch(8)
+        out8 = [(t8, l8)]
+        tok = t8
+        for _ in range(steps):
+            tok, lg = big.decode_step(tok, want_logits=True)
+            out8.append((tok, lg))
+        assert big.graph_kernels() == 3
+        for half in range(2):
+            rows = slice(4 * half, 4 * half + 4)
+            small.clear_kv_cache()
+            small.prefill(prompts[rows])  # same KV rows (the prefill's last-row LM head differs: 4-row GEMV)
+            small.set_batch(4)
+            for i in range(steps):
+                tok, lg = small.decode_step(out8[i][0][rows], want_logits=True)
+                assert np.array_equal(lg, out8[i + 1][1][rows]), (half, i, float(np.max(np.abs(lg - out8[i + 1][1][rows]))))
+                assert np.array_equal(tok, out8[i + 1][0][rows]), (half, i)
+    finally:
+        big.close()
+        small.close()

@@ -242,3 +242,102 @@ def test_expert_parallel_2_gpus():
         for step, (cos, rel, same, marg) in enumerate(r["stats"]):
             assert cos >= 0.99 and rel <= 0.15, (r["rank"], step, cos, rel)
             assert same or marg <= 2 * rel, (r["rank"], step)
+
+
+QWEN3_32B_2L = dict(hidden=5120, layers=2, n_heads=64, n_kv_heads=8, head_dim=128, inter=25600, vocab=151936,
+                    max_pos=40960, tied=0, eps=1e-6, theta=1e6, init_std=0.02, norm_std=0.0)
+
+
+def _tp32_rank_main(rank, world, port, q, prompts, fed, nccl_path):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    if nccl_path:
+        os.environ["LQ_TP_NCCL"] = "1"
+    for p in (REPO, os.path.join(REPO, "qwen-omni-inference-rs_b200")):
+        sys.path.insert(0, p)
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=300))
+    out = {"rank": rank}
+    try:
+        import lq8
+        ctx = lq8.Context(rank)
+        comm = lq8.Comm.from_process_group(ctx)
+        B, L = prompts.shape
+        gm = lq8.Qwen3ForCausalLM(ctx, lq8.make_config(**QWEN3_32B_2L), 2024, max_batch=B, ctx_max=L + 16, comm=comm)
+        nxt, lg = gm.prefill(prompts, want_logits=True)
+        gm.set_batch(B)
+        res = [(nxt, lg)]
+        for s in range(fed.shape[0]):
+            res.append(gm.decode_step(fed[s], want_logits=True))
+        out["kernels"] = gm.graph_kernels()
+        if rank == 0:
+            out["tokens"] = np.stack([r[0] for r in res])
+            out["logits"] = np.stack([r[1] for r in res])
+        gm.close()
+        comm.close()
+        ctx.close()
+    except Exception as e:  # reported to the parent, which fails the test
+        out["error"] = repr(e)
+    q.put(out)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("nccl_path", [False, True])
+def test_tensor_parallel_32b_shapes_2_gpus(oracle, nccl_path):
+    """Config 4's shapes (2 layers, full vocabulary) as two tensor-parallel ranks at batch 8:
+    each rank holds 32 / 4 heads, 12800 intermediate rows, 75968 LM-head rows. Default path:
+    the persistent decode step with the o/down partial sums exchanged inside the kernel over
+    NVLink (a 3-kernel decode graph); LQ_TP_NCCL=1: the per-layer kernels with NCCL
+    all-reduces. Both teacher-forced against the single-device oracle with the tolerance of
+    the headline-shape tests (the noise floor of these shapes; test_gpu_headline.py), tokens
+    equal wherever the oracle's margin exceeds twice the step's difference."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    from conftest import parity_metrics, record
+    B, L, steps = 8, 24, 4
+    ocfg = oracle.make_config(**QWEN3_32B_2L)
+    prompts = np.stack([oracle.gen_tokens(2024, 100 + b, L, QWEN3_32B_2L["vocab"]) for b in range(B)])
+    om = oracle.Qwen3Model(ocfg, 2024, ctx_max=L + 16)
+    olgs = np.empty((steps, B, ocfg.vocab), np.float32)
+    fed = np.empty((steps - 1, B), np.int32)
+    for b in range(B):
+        om.clear()
+        lg = om.forward(prompts[b], 0)
+        olgs[0, b] = lg
+        for s in range(1, steps):
+            fed[s - 1, b] = oracle.argmax(lg)
+            lg = om.forward(fed[s - 1, b:b + 1], L + s - 1)
+            olgs[s, b] = lg
+    om.close()
+    mctx = mp.get_context("spawn")
+    qq = mctx.Queue()
+    port = _free_port()
+    procs = [mctx.Process(target=_tp32_rank_main, args=(r, 2, port, qq, prompts, fed, nccl_path)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [qq.get(timeout=900) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+    for r in res:
+        assert "error" not in r, r
+    r0 = next(r for r in res if r["rank"] == 0)
+    if nccl_path:
+        assert r0["kernels"] > 3  # per-layer kernels (the NCCL all-reduces are not kernel nodes)
+    else:
+        assert all(r["kernels"] == 3 for r in res), [r["kernels"] for r in res]
+    for s in range(steps):
+        for b in range(B):
+            m = parity_metrics(r0["logits"][s, b], olgs[s, b])
+            srt = np.sort(olgs[s, b])
+            same = int(r0["tokens"][s, b]) == oracle.argmax(olgs[s, b])
+            record("32b_tp2_" + ("nccl" if nccl_path else "persistent"), step=s, row=b, same_token=same,
+                   margin=float(srt[-1] - srt[-2]), **m)
+            assert m["cos"] >= 0.9995 and m["max_rel"] <= 5e-2, (s, b, m)
+            assert same or srt[-1] - srt[-2] <= 2 * m["max_abs"], (s, b)
