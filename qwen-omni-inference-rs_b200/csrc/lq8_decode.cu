@@ -52,13 +52,15 @@ constexpr int PD_KS = 128 + 4;  // padded K row (floats): conflict-free float4 r
 constexpr int PD_MAX_SPLITS = 128;
 constexpr int PD_MAX_G = 8;
 constexpr int PD_MAX_M = 8;  // batch rows of one step (GEMV output lanes 8r + m: m < 8)
-constexpr int PD_MAX_TP = 8;  // tensor-parallel ranks whose exchange slots a step addresses
+constexpr int PD_MAX_TP = 8;
+constexpr int PD_XPAD = 32;  // batches of 5-8: activation row padding (conflict-free MMA token fragments)  // tensor-parallel ranks whose exchange slots a step addresses
 constexpr uint64_t PD_WAIT_NS = 2000000000ull;
 
 // one weight matrix: its Q8_0 rows viewed as [N][K/8] 8-byte elements and its scales [N][K/32]
 struct alignas(64) PdMat {
     CUtensorMap wq;
     CUtensorMap wd;
+    CUtensorMap wsw;  // the rows as bytes in [16][128 B] boxes with the 128-byte swizzle (batches 5-8)
 };
 
 // the device descriptor of one layer; the LM head is mat[0] of the entry after the last layer
@@ -121,7 +123,7 @@ struct PdAtt {
 };
 
 // 128-byte multiple: the union area behind it takes 16-byte vector and cp.async accesses
-struct alignas(128) PdSmem {
+struct alignas(1024) PdSmem {
     uint64_t full[PD_MAX_STAGES];
     uint64_t empty[PD_MAX_STAGES];
     float red[32];
@@ -134,6 +136,9 @@ struct alignas(128) PdSmem {
     int fail;  // a consumer warp gave up waiting for a stage
     int ns;    // ring stages
     int pad_;
+    float mred[2][PD_CONS][PD_ROWS][8];  // batches of 5-8: the warps' partial sums of a row group
+    uint64_t rfull[2];                   // mred[b] written by the 8 consumer warps
+    uint64_t rfree[2];                   // mred[b] read by the 8 consumer warps
     // followed by the ring (ns stages of PD_STAGE bytes), then the union area: the GEMV
     // activations or PdAtt
 };
@@ -142,7 +147,8 @@ struct alignas(128) PdSmem {
 extern __shared__ __align__(1024) uint8_t pd_dsmem[];
 __device__ __forceinline__ uint8_t* pd_stage(int s) { return pd_dsmem + sizeof(PdSmem) + (size_t)s * PD_STAGE; }
 
-static_assert(sizeof(PdSmem) % 128 == 0 && PD_STAGE % 128 == 0, "shared-memory regions must stay 128-byte aligned");
+static_assert(sizeof(PdSmem) % 1024 == 0 && PD_STAGE % 1024 == 0,
+              "the ring's stages must stay 1024-byte aligned (128-byte swizzled boxes)");
 
 enum { PH_QKV = 0, PH_O = 1, PH_GU = 2, PH_DN = 3, PH_LM = 4 };
 
@@ -200,7 +206,7 @@ __device__ __forceinline__ int pd_first(unsigned off) {
 // ---- producer: the units of one GEMV phase dealt to this CTA, their tiles streamed ----
 // (Claiming units from a counter instead balanced worse: the producers claim ahead by up to a
 // ring of tiles, so the first CTAs to reach a phase took most of its units.)
-__device__ __forceinline__ bool pd_produce(PdSmem& S, const PdGemv& g, unsigned off, int& it, int* err) {
+__device__ __forceinline__ bool pd_produce(PdSmem& S, const PdGemv& g, unsigned off, int& it, int* err, bool sw) {
     const int K = g.K;
     const int kc = K < PD_KC ? K : PD_KC;
     const int nchunks = (K + kc - 1) / kc;
@@ -233,8 +239,16 @@ __device__ __forceinline__ bool pd_produce(PdSmem& S, const PdGemv& g, unsigned 
                     }
                     uint8_t* st = pd_stage(s);
                     S.tag[s] = u;
-                    mbar_expect_tx(&S.full[s], bytes);
-                    tma_load_2d(st, &g.mat->wq, c * (kc / 8), r0, &S.full[s]);
+                    if (sw) {
+                        // one swizzled box per 128 bytes of K that exist (the consumers skip the rest)
+                        const int nbox = min(kc, K - c * kc) / 128;
+                        mbar_expect_tx(&S.full[s], (unsigned)(nbox * PD_ROWS * 128 + PD_ROWS * (kc / 16)));
+                        for (int b = 0; b < nbox; b++)
+                            tma_load_2d(st + b * (PD_ROWS * 128), &g.mat->wsw, c * kc + b * 128, r0, &S.full[s]);
+                    } else {
+                        mbar_expect_tx(&S.full[s], bytes);
+                        tma_load_2d(st, &g.mat->wq, c * (kc / 8), r0, &S.full[s]);
+                    }
                     tma_load_2d(st + PD_ROWS * kc, &g.mat->wd, c * (kc / 32), r0, &S.full[s]);
                 }
             }
@@ -514,6 +528,262 @@ __device__ __forceinline__ bool pd_consume(PdSmem& S, const PdGemv& g, const int
     }
     pd_csync();
     return S.fail == 0;
+}
+
+// Batches of 5-8 rows on the tensor cores. The dp4a consumer above reads the activations of
+// every token once per 2 weight rows, so at 8 tokens shared memory, not HBM, sets its pace;
+// here each warp runs int8 MMAs that reuse a weight fragment across the 8 tokens and a token
+// fragment across the 16 rows. The stage arrives as kc/128 boxes of [16 rows][128 B] with the
+// 128-byte swizzle (16-byte chunk c of row r at c ^ (r & 7)); box w holds Q8_0 blocks
+// 4w..4w+3 of the chunk and belongs to warp w. Per block one mma.sync m16n8k32 (s8; rows x
+// tokens), its accumulator starting at 1.5*2^23 so the int32 dot read as a float is
+// 1.5*2^23 + dot, then dot*(d_w*d_x) added per (row, token) with separately rounded operations
+// in block order. At the end of each 16-row group the eight warps' partial sums meet in shared
+// memory (double-buffered: one consumer barrier per group) and warp w finishes rows 2w, 2w+1
+// (lanes 0-3: tokens 2q, 2q+1), adding the warps' sums in warp order: the output, the
+// residual, the tensor-parallel exchange push (one 16-byte vector per lane), SwiGLU with the
+// h handoff of the dp4a consumer, or the argmax keys. Activation rows are ldx = K + 32 bytes
+// apart (conflict-free token fragments).
+template <int M>
+__device__ __forceinline__ bool pd_consume_mma(PdSmem& S, const PdGemv& g, const int8_t* xs, int ldx,
+                                               const uint16_t* xds, int& it, int& hn, int& rn, float* out, int ldo,
+                                               bool resid, bool keys, int8_t* hq, uint16_t* hd, int* err,
+                                               const PdParams* xp, int xpar, int kbase) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gq = lane >> 2, t = lane & 3;
+    const int ns = S.ns;
+    const int K = g.K, nb = K >> 5;
+    const int kc = K < PD_KC ? K : PD_KC;
+    const int nchunks = (K + kc - 1) / kc;
+    const int nout = g.swi ? g.N / 2 : g.N;
+    const int halves = g.swi ? 2 : 1;
+    bool failed = false;
+    auto wait_full = [&](int s) {
+        int ok = 1;
+        if (lane == 0) ok = pd_wait(&S.full[s], (unsigned)(it / ns) & 1u, err);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        __syncwarp();
+        if (!ok) {
+            if (lane == 0) {
+                atomicCAS(err, 0, 43);
+                S.fail = 1;
+            }
+            failed = true;
+        }
+        return ok != 0;
+    };
+    float gate[4] = {0.f, 0.f, 0.f, 0.f};
+    while (!failed) {
+        const int s0 = it % ns;
+        if (!wait_full(s0)) break;
+        int u = 0;
+        if (lane == 0) u = S.tag[s0];
+        u = __shfl_sync(0xffffffffu, u, 0);
+        if (u < 0) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.empty[s0]);
+            it++;
+            break;
+        }
+        const int hb = hn & 1, huse = hn >> 1;
+        if (g.swi && huse > 0) {  // warp 0 is done with this buffer's previous unit
+            int ok = 1;
+            if (lane == 0) ok = pd_wait(&S.hfree[hb], (unsigned)(huse - 1) & 1u, err);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) {
+                if (lane == 0) {
+                    atomicCAS(err, 0, 45);
+                    S.fail = 1;
+                }
+                failed = true;
+            }
+        }
+        for (int grp = 0; grp < halves && !failed; grp++)
+        for (int half = 0; half < halves && !failed; half++) {
+            const int o0 = u * pd_unit_rows(g) + grp * PD_ROWS;  // first output of the group
+            // this lane's outputs after the group: rows 2w, 2w+1 x tokens 2t, 2t+1 (lanes 0-3)
+            float res[4] = {0.f, 0.f, 0.f, 0.f};
+            if (resid && !xp && lane < 4) {
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int row = o0 + 2 * warp + (i & 1), tok = 2 * lane + (i >> 1);
+                    if (tok < M && row < nout) res[i] = __ldcg(out + (size_t)tok * ldo + row);
+                }
+            }
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int c = 0; c < nchunks; c++, it++) {
+                const int s = it % ns;
+                if ((grp | half | c) != 0 && !wait_full(s)) break;
+                const int k0 = c * kc, nbc = min(kc, K - k0) >> 5;
+                const uint8_t* st = pd_stage(s);
+                const bool act = 4 * warp < nbc;
+                uint2 wa[4], wb[4], swa = make_uint2(0u, 0u), swb = make_uint2(0u, 0u);
+                if (act) {
+                    const uint8_t* box = st + warp * (PD_ROWS * 128);
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const int ch = (((2 * j + (t >> 1)) ^ gq) << 4) + (t & 1) * 8;
+                        wa[j] = *reinterpret_cast<const uint2*>(box + gq * 128 + ch);
+                        wb[j] = *reinterpret_cast<const uint2*>(box + (gq + 8) * 128 + ch);
+                    }
+                    const uint16_t* sc = reinterpret_cast<const uint16_t*>(st + PD_ROWS * kc);
+                    swa = *reinterpret_cast<const uint2*>(sc + gq * (kc / 32) + 4 * warp);
+                    swb = *reinterpret_cast<const uint2*>(sc + (gq + 8) * (kc / 32) + 4 * warp);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.empty[s]);
+                if (act) {
+                    const int gb0 = (k0 >> 5) + 4 * warp;
+                    uint2 xv[4];
+                    uint2 dxa = make_uint2(0u, 0u), dxb = make_uint2(0u, 0u);
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+                        xv[j] = gq < M ? *reinterpret_cast<const uint2*>(xs + (size_t)gq * ldx + (gb0 + j) * 32 + 8 * t)
+                                       : make_uint2(0u, 0u);
+                    if (2 * t < M) dxa = *reinterpret_cast<const uint2*>(xds + (size_t)(2 * t) * nb + gb0);
+                    if (2 * t + 1 < M) dxb = *reinterpret_cast<const uint2*>(xds + (size_t)(2 * t + 1) * nb + gb0);
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        if (4 * warp + j >= nbc) break;
+                        const uint32_t a[4] = {wa[j].x, wb[j].x, wa[j].y, wb[j].y};
+                        const uint32_t b[2] = {xv[j].x, xv[j].y};
+                        int d[4];
+                        mma_s8_bias(d, a, b, 0x4B400000);
+                        const uint32_t wsa = j < 2 ? swa.x : swa.y, wsb = j < 2 ? swb.x : swb.y;
+                        const uint32_t xsa = j < 2 ? dxa.x : dxa.y, xsb = j < 2 ? dxb.x : dxb.y;
+                        const float dwa = h2f((uint16_t)((j & 1) ? (wsa >> 16) : (wsa & 0xFFFFu)));
+                        const float dwb = h2f((uint16_t)((j & 1) ? (wsb >> 16) : (wsb & 0xFFFFu)));
+                        const float dx0 = h2f((uint16_t)((j & 1) ? (xsa >> 16) : (xsa & 0xFFFFu)));
+                        const float dx1 = h2f((uint16_t)((j & 1) ? (xsb >> 16) : (xsb & 0xFFFFu)));
+                        const float f0 = __fsub_rn(__int_as_float(d[0]), 12582912.0f);
+                        const float f1 = __fsub_rn(__int_as_float(d[1]), 12582912.0f);
+                        const float f2 = __fsub_rn(__int_as_float(d[2]), 12582912.0f);
+                        const float f3 = __fsub_rn(__int_as_float(d[3]), 12582912.0f);
+                        acc[0] = __fadd_rn(acc[0], __fmul_rn(f0, __fmul_rn(dwa, dx0)));
+                        acc[1] = __fadd_rn(acc[1], __fmul_rn(f1, __fmul_rn(dwa, dx1)));
+                        acc[2] = __fadd_rn(acc[2], __fmul_rn(f2, __fmul_rn(dwb, dx0)));
+                        acc[3] = __fadd_rn(acc[3], __fmul_rn(f3, __fmul_rn(dwb, dx1)));
+                    }
+                }
+            }
+            if (failed) break;
+            // the warps' partial sums: C fragment value i is (row gq + 8 (i >> 1), token 2t + (i & 1)).
+            // Buffer b of the two holds every other group: written once all warps have read it
+            // (rfree), read once all warps have written it (rfull); the waits are bounded
+            const int buf = rn & 1, use = rn >> 1;  // rn: row groups of the step so far
+            float(*red)[PD_ROWS][8] = S.mred[buf];
+            int rok = 1;
+            if (use > 0) {
+                if (lane == 0) rok = pd_wait(&S.rfree[buf], (unsigned)(use - 1) & 1u, err);
+                rok = __shfl_sync(0xffffffffu, rok, 0);
+            }
+            if (rok) {
+                red[warp][gq][2 * t] = acc[0];
+                red[warp][gq][2 * t + 1] = acc[1];
+                red[warp][gq + 8][2 * t] = acc[2];
+                red[warp][gq + 8][2 * t + 1] = acc[3];
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.rfull[buf]);
+                if (lane == 0) rok = pd_wait(&S.rfull[buf], (unsigned)use & 1u, err);
+                rok = __shfl_sync(0xffffffffu, rok, 0);
+                __syncwarp();
+            }
+            if (!rok) {
+                if (lane == 0) {
+                    atomicCAS(err, 0, 50);
+                    S.fail = 1;
+                }
+                failed = true;
+                break;
+            }
+            rn++;
+            if (lane < 4) {
+                float v[4];  // rows 2w + (i & 1), tokens 2 lane + (i >> 1)
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int rr = 2 * warp + (i & 1), tok = 2 * lane + (i >> 1);
+                    float a = red[0][rr][tok];
+#pragma unroll
+                    for (int w = 1; w < PD_CONS; w++) a = __fadd_rn(a, red[w][rr][tok]);
+                    v[i] = a;
+                }
+                if (g.swi) {
+                    if (half == 0) {
+#pragma unroll
+                        for (int i = 0; i < 4; i++) gate[i] = v[i];
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            const int tok = 2 * lane + (i >> 1);
+                            if (tok < M) S.hbuf[hb][tok][grp * PD_ROWS + 2 * warp + (i & 1)] = swiglu(gate[i], v[i]);
+                        }
+                    }
+                } else if (xp) {
+                    // exchange layout per (unit, row pair w): 16 floats [token][row of the pair]
+                    const size_t slot = (size_t)(g.N / PD_ROWS) * PD_CONS * 16;
+                    const size_t off = ((size_t)xpar * xp->tp + xp->rank) * slot + ((size_t)u * PD_CONS + warp) * 16 +
+                                       4 * lane;
+                    const float4 f4 = make_float4(v[0], v[1], v[2], v[3]);
+#pragma unroll
+                    for (int tt = 0; tt < PD_MAX_TP; tt++)
+                        if (tt < xp->tp) *reinterpret_cast<float4*>(xp->xpeer[tt] + off) = f4;
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const int row = o0 + 2 * warp + (i & 1), tok = 2 * lane + (i >> 1);
+                        if (tok < M && row < nout) {
+                            out[(size_t)tok * ldo + row] = resid ? __fadd_rn(res[i], v[i]) : v[i];
+                            if (keys) atomicMax(&S.keys[tok], argmax_key(v[i], row + kbase));
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.rfree[buf]);  // this warp is done reading the buffer
+        }
+        if (g.swi && !failed) {
+            // h's 32 values per token are one Q8_0 block: warp 0 quantizes once every warp
+            // has written its rows
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.hfull[hb]);
+            if (warp == 0) {
+                int ok = 1;
+                if (lane == 0) ok = pd_wait(&S.hfull[hb], (unsigned)huse & 1u, err);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                __syncwarp();
+                if (ok) {
+#pragma unroll
+                    for (int m = 0; m < M; m++) {
+                        const size_t e = (size_t)m * nout + (size_t)u * 32;
+                        pd_quant_warp32(S.hbuf[hb][m][lane], lane, hq + e, hd + (e >> 5));
+                    }
+                } else if (lane == 0) {
+                    atomicCAS(err, 0, 46);
+                    S.fail = 1;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.hfree[hb]);
+            }
+        }
+        if (g.swi) hn++;
+    }
+    pd_csync();
+    return S.fail == 0;
+}
+
+// the GEMV of one phase: the dp4a consumer for batches of 1-4 (bit-identical to the per-layer
+// decode path), the MMA consumer for 5-8 (activation rows K + PD_XPAD bytes apart)
+template <int M>
+__device__ __forceinline__ bool pd_phase(PdSmem& S, const PdGemv& g, const int8_t* xs, const uint16_t* xds, int& it,
+                                         int& hn, int& rn, float* out, int ldo, bool resid, bool keys, int8_t* hq,
+                                         uint16_t* hd, int* err, int u_first = -1, float res_first = 0.0f,
+                                         const PdParams* xp = nullptr, int xpar = 0, int kbase = 0) {
+    if constexpr (M > 4)
+        return pd_consume_mma<M>(S, g, xs, g.K + PD_XPAD, xds, it, hn, rn, out, ldo, resid, keys, hq, hd, err, xp, xpar,
+                                 kbase);
+    else
+        return pd_consume<M>(S, g, xs, xds, it, hn, out, ldo, resid, keys, hq, hd, err, u_first, res_first, xp, xpar,
+                             kbase);
 }
 
 // ---- tensor parallelism: the row-parallel exchange ----
@@ -922,6 +1192,8 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
         for (int b = 0; b < 2; b++) {
             mbar_init(&S.hfull[b], PD_CONS);
             mbar_init(&S.hfree[b], 1);
+            mbar_init(&S.rfull[b], PD_CONS);
+            mbar_init(&S.rfree[b], PD_CONS);
         }
         mbar_fence_init();
     }
@@ -940,10 +1212,10 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
             for (int l = 0; l < p.n_layers && ok; l++)
                 for (int k = PH_QKV; k <= PH_DN && ok; k++) {
                     const PdGemv g = pd_gemv(p, l, k);
-                    ok = pd_produce(S, g, off, it, p.err);
+                    ok = pd_produce(S, g, off, it, p.err, M > 4);
                     off += (unsigned)pd_units(g);
                 }
-            if (ok) pd_produce(S, pd_gemv(p, 0, PH_LM), off, it, p.err);
+            if (ok) pd_produce(S, pd_gemv(p, 0, PH_LM), off, it, p.err, M > 4);
             // leave only after the copies in flight have landed (bounded)
             for (int j = max(0, it - p.ns); j < it; j++)
                 mbar_wait_ns(&S.full[j % p.ns], (unsigned)(j / p.ns) & 1u, PD_WAIT_NS);
@@ -956,9 +1228,18 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
     // union area, GEMV phases: activations xs [M][K] int8 and xds [M][K/32] fp16, the norm
     // weight nws [H] bf16 (prefetched before the barrier that precedes its prologue) and the
     // f32 staging row xrow [H]
+    constexpr int XP = M > 4 ? PD_XPAD : 0;  // activation row padding (MMA consumer)
     int8_t* xs = reinterpret_cast<int8_t*>(area);
-    uint16_t* xds = reinterpret_cast<uint16_t*>(area + (size_t)M * Kmax);
-    uint16_t* nws = reinterpret_cast<uint16_t*>(area + (size_t)M * Kmax + (size_t)M * (Kmax / 32) * 2);
+    uint16_t* xds = reinterpret_cast<uint16_t*>(area + (size_t)M * (Kmax + XP));
+    uint16_t* nws = reinterpret_cast<uint16_t*>(area + (size_t)M * (Kmax + XP) + (size_t)M * (Kmax / 32) * 2);
+    // M rows of K bytes from global memory into xs (rows K + XP apart)
+    auto stage_rows = [&](const int8_t* src, int K) {
+        if (XP == 0) {
+            pd_prefetch(xs, src, M * K, tid);
+        } else {
+            for (int m = 0; m < M; m++) pd_prefetch(xs + (size_t)m * (K + XP), src + (size_t)m * K, K, tid);
+        }
+    };
     float* xrow = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(nws) + (size_t)H * 2);
     PdAtt& A = *reinterpret_cast<PdAtt*>(area);
     // RMSNorm + Q8_0 of the M rows of x (written by other CTAs) into xs/xds; the norm weight's
@@ -968,12 +1249,12 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
             pd_csync();
             pd_stage_f32(xrow, p.x + (size_t)m * H, H, tid);
             pd_csync();
-            rms_row<float, PD_CTHREADS, 1>(xrow, H, nws, p.eps, tid, S.red, nullptr, xs + (size_t)m * H,
+            rms_row<float, PD_CTHREADS, 1>(xrow, H, nws, p.eps, tid, S.red, nullptr, xs + (size_t)m * (H + XP),
                                            xds + (size_t)m * (H / 32));
         }
         pd_csync();
     };
-    int it = 0, hn = 0;
+    int it = 0, hn = 0, rn = 0;
     unsigned epoch = 0;
     // the consumers' copy of the producer's running unit offset (phase k of layer l starts at
     // position l * per_layer + before[k] of the dealt sequence)
@@ -987,7 +1268,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
         const PdLayer& L = p.layers[l];
         // QKV: input RMSNorm + Q8_0 of x, the q|k|v rows
         norm_rows();
-        if (!pd_consume<M>(S, pd_gemv(p, l, PH_QKV), xs, xds, it, hn, p.qkv, p.Nqkv, false, false, nullptr,
+        if (!pd_phase<M>(S, pd_gemv(p, l, PH_QKV), xs, xds, it, hn, rn, p.qkv, p.Nqkv, false, false, nullptr,
                            nullptr, p.err))
             return;
         // the first attention item's cache rows start loading before the barrier
@@ -1003,11 +1284,11 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
         // O: the attention output as activations, residual into x
         {
             const int Ko = p.Hq * 128;
-            pd_prefetch(xs, p.att_q, M * Ko, tid);
+            stage_rows(p.att_q, Ko);
             pd_prefetch(xds, p.att_d, M * (Ko / 32) * 2, tid);
             cp_async_wait<0>();
             pd_csync();
-            if (!pd_consume<M>(S, pd_gemv(p, l, PH_O), xs, xds, it, hn, p.x, H, !xch, false, nullptr, nullptr,
+            if (!pd_phase<M>(S, pd_gemv(p, l, PH_O), xs, xds, it, hn, rn, p.x, H, !xch, false, nullptr, nullptr,
                                p.err, u_o, res_o, xch ? &p : nullptr, 0))
                 return;
         }
@@ -1021,15 +1302,15 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
         const float res_dn = pd_res_lane<M>(p.x, H, H, u_dn);
         // GU: post-attention RMSNorm, gate|up, SiLU(gate)*up -> h as Q8_0
         norm_rows();
-        if (!pd_consume<M>(S, pd_gemv(p, l, PH_GU), xs, xds, it, hn, nullptr, 0, false, false, p.hq, p.hd, p.err))
+        if (!pd_phase<M>(S, pd_gemv(p, l, PH_GU), xs, xds, it, hn, rn, nullptr, 0, false, false, p.hq, p.hd, p.err))
             return;
         if (!pd_grid_barrier(p, S, epoch)) return;
         // DN: h (already Q8_0) as activations, residual into x
-        pd_prefetch(xs, p.hq, M * I, tid);
+        stage_rows(p.hq, I);
         pd_prefetch(xds, p.hd, M * (I / 32) * 2, tid);
         cp_async_wait<0>();
         pd_csync();
-        if (!pd_consume<M>(S, pd_gemv(p, l, PH_DN), xs, xds, it, hn, p.x, H, !xch, false, nullptr, nullptr, p.err,
+        if (!pd_phase<M>(S, pd_gemv(p, l, PH_DN), xs, xds, it, hn, rn, p.x, H, !xch, false, nullptr, nullptr, p.err,
                            u_dn, res_dn, xch ? &p : nullptr, 1))
             return;
         if (xch && !pd_exchange_sum<M>(p, S, 1, (seq0 + 2u * (unsigned)l + 2u) * (unsigned)(p.tp - 1), u_dn))
@@ -1040,7 +1321,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
     }
     // LM head: final RMSNorm, logits, greedy argmax keys
     norm_rows();
-    if (!pd_consume<M>(S, pd_gemv(p, 0, PH_LM), xs, xds, it, hn, p.logits, p.V, false, true, nullptr, nullptr,
+    if (!pd_phase<M>(S, pd_gemv(p, 0, PH_LM), xs, xds, it, hn, rn, p.logits, p.V, false, true, nullptr, nullptr,
                        p.err, -1, 0.0f, nullptr, 0, p.vbase))
         return;
     pd_csync();
@@ -1051,7 +1332,8 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
 // ---- host ----
 static size_t pd_area_bytes(int64_t m, int64_t H, int64_t Hqd, int64_t I) {
     const int64_t Kmax = std::max({H, Hqd, I});
-    const size_t gemv = (size_t)(m * Kmax + m * (Kmax / 32) * 2 + H * 2 + H * 4);
+    const int64_t xp = m > 4 ? PD_XPAD : 0;
+    const size_t gemv = (size_t)(m * (Kmax + xp) + m * (Kmax / 32) * 2 + H * 2 + H * 4);
     return std::max(gemv, sizeof(PdAtt));
 }
 
@@ -1104,6 +1386,9 @@ static int pd_map(lq_ctx* ctx, PdMat* out, const lq_q8_tensor& w) {
     const uint32_t kc = (uint32_t)std::min<int64_t>(K, PD_KC);
     int rc = make_tensor_map_2d(ctx, &out->wq, CU_TENSOR_MAP_DATA_TYPE_UINT64, w.qs, (uint64_t)(K / 8), (uint64_t)N,
                                 (uint64_t)K, kc / 8, PD_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    rc = make_tensor_map_2d(ctx, &out->wsw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.qs, (uint64_t)K, (uint64_t)N, (uint64_t)K,
+                            128, PD_ROWS, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
     return make_tensor_map_2d(ctx, &out->wd, CU_TENSOR_MAP_DATA_TYPE_UINT16, w.d, (uint64_t)nb, (uint64_t)N,
                               (uint64_t)(nb * 2), kc / 32, PD_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
