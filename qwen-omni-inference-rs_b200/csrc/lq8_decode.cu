@@ -771,6 +771,38 @@ __device__ __forceinline__ bool pd_consume_mma(PdSmem& S, const PdGemv& g, const
     return S.fail == 0;
 }
 
+// RmsNorm::forward of one f32 row (written by other CTAs: read through L2) by one warp, with
+// Q8_0 of the bf16 result (rms_norm.rs:144-176): the input rounded to bf16, lane l sums the
+// squares of elements 128i + 4l .. +3 in pass order, a butterfly gives the total, inv =
+// 1/sqrt(sum/dim + eps), out = bf16((x*inv)*w), quantized per 32-element block by the block's 8
+// lanes. The second pass reads the row again (from L2).
+__device__ __forceinline__ void pd_norm_row_warp(const float* __restrict__ xr, int dim, const uint16_t* nw, float eps,
+                                                 int lane, int8_t* xq, uint16_t* xd) {
+    float ss = 0.0f;
+#pragma unroll 4
+    for (int e = lane * 4; e < dim; e += 128) {
+        const float4 t = __ldcg(reinterpret_cast<const float4*>(xr + e));
+        const float v[4] = {round_bf16(t.x), round_bf16(t.y), round_bf16(t.z), round_bf16(t.w)};
+#pragma unroll
+        for (int i = 0; i < 4; i++) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+    }
+    ss = warp_sum(ss);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), eps)));
+#pragma unroll 4
+    for (int e = lane * 4; e < dim; e += 128) {
+        const float4 t = __ldcg(reinterpret_cast<const float4*>(xr + e));
+        const uint2 wt = *reinterpret_cast<const uint2*>(nw + e);
+        const float x4[4] = {t.x, t.y, t.z, t.w};
+        const float wv[4] = {bf16_to_f32((uint16_t)(wt.x & 0xFFFF)), bf16_to_f32((uint16_t)(wt.x >> 16)),
+                             bf16_to_f32((uint16_t)(wt.y & 0xFFFF)), bf16_to_f32((uint16_t)(wt.y >> 16))};
+        float v[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) v[i] = round_bf16(__fmul_rn(__fmul_rn(round_bf16(x4[i]), inv), wv[i]));
+        const uint32_t q = quant_group8(v, lane & 7, xd + (e >> 5));
+        *reinterpret_cast<uint32_t*>(xq + e) = q;
+    }
+}
+
 // the GEMV of one phase: the dp4a consumer for batches of 1-4 (bit-identical to the per-layer
 // decode path), the MMA consumer for 5-8 (activation rows K + PD_XPAD bytes apart)
 template <int M>
@@ -1245,6 +1277,15 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
     // RMSNorm + Q8_0 of the M rows of x (written by other CTAs) into xs/xds; the norm weight's
     // copies are already in flight
     auto norm_rows = [&]() {
+        if constexpr (M > 4) {
+            // batches of 5-8: warp w normalises row w on its own (warp sums only, every load of
+            // a pass in flight), all rows at once
+            pd_csync();
+            if (warp < M) pd_norm_row_warp(p.x + (size_t)warp * H, H, nws, p.eps, lane, xs + (size_t)warp * (H + XP),
+                                           xds + (size_t)warp * (H / 32));
+            pd_csync();
+            return;
+        }
         for (int m = 0; m < M; m++) {
             pd_csync();
             pd_stage_f32(xrow, p.x + (size_t)m * H, H, tid);
