@@ -93,6 +93,7 @@ struct PdParams {
                                // zero at launch
     int* err;
     int ns;                    // ring stages
+    int ring_off;              // byte offset of the ring in shared memory
     // tensor parallelism (tp > 1): o and down are row-parallel; each CTA pushes the partial
     // sums of its units to every rank's exchange buffer and adds all ranks' partials in rank
     // order (the same units fall to the same CTA index on every rank); the LM head's argmax
@@ -123,7 +124,7 @@ struct PdAtt {
 };
 
 // 128-byte multiple: the union area behind it takes 16-byte vector and cp.async accesses
-struct alignas(1024) PdSmem {
+struct alignas(128) PdSmem {
     uint64_t full[PD_MAX_STAGES];
     uint64_t empty[PD_MAX_STAGES];
     float red[32];
@@ -134,21 +135,41 @@ struct alignas(1024) PdSmem {
     float hbuf[2][PD_MAX_M][32];  // gate|up: one Q8_0 block of SiLU(gate)*up per row (two units in turn)
     int flag;  // grid barrier outcome
     int fail;  // a consumer warp gave up waiting for a stage
-    int ns;    // ring stages
-    int pad_;
-    float mred[2][PD_CONS][PD_ROWS][8];  // batches of 5-8: the warps' partial sums of a row group
-    uint64_t rfull[2];                   // mred[b] written by the 8 consumer warps
-    uint64_t rfree[2];                   // mred[b] read by the 8 consumer warps
+    int ns;        // ring stages
+    int ring_off;  // byte offset of the ring (1024-aligned for the swizzled boxes of batches 5-8)
+    uint64_t rfull[2];  // batches of 5-8: partial-sum buffer b written by the 8 consumer warps
+    uint64_t rfree[2];  // ... and read by them
     // followed by the ring (ns stages of PD_STAGE bytes), then the union area: the GEMV
     // activations or PdAtt
 };
 
+__device__ __forceinline__ uint8_t* pd_align128(uint8_t* p) {
+    return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 127) & ~(uintptr_t)127);
+}
+
 // the dynamic shared memory: PdSmem, the ring, the union area
 extern __shared__ __align__(1024) uint8_t pd_dsmem[];
-__device__ __forceinline__ uint8_t* pd_stage(int s) { return pd_dsmem + sizeof(PdSmem) + (size_t)s * PD_STAGE; }
+// a position in the ring, carried from stage to stage (no division by the run-time depth on the
+// path of every stage): count of stages passed, slot, and the slot's mbarrier phase parity
+struct PdRing {
+    int it;
+    int s;
+    unsigned ph;
+};
+__device__ __forceinline__ void pd_next(PdRing& r, int ns) {
+    r.it++;
+    if (++r.s == ns) {
+        r.s = 0;
+        r.ph ^= 1u;
+    }
+}
+__device__ __forceinline__ uint8_t* pd_ring(const PdSmem& S) { return pd_dsmem + S.ring_off; }
+// batches of 5-8: the warps' partial sums of one 16-row group, two groups in turn (in the union
+// area, after the GEMV activations)
+typedef float PdRed[2][PD_CONS][PD_ROWS][8];
 
-static_assert(sizeof(PdSmem) % 1024 == 0 && PD_STAGE % 1024 == 0,
-              "the ring's stages must stay 1024-byte aligned (128-byte swizzled boxes)");
+static_assert(sizeof(PdSmem) % 128 == 0 && PD_STAGE % 1024 == 0,
+              "regions must stay 128-byte aligned, ring stages 1024-byte aligned (swizzled boxes)");
 
 enum { PH_QKV = 0, PH_O = 1, PH_GU = 2, PH_DN = 3, PH_LM = 4 };
 
@@ -206,7 +227,7 @@ __device__ __forceinline__ int pd_first(unsigned off) {
 // ---- producer: the units of one GEMV phase dealt to this CTA, their tiles streamed ----
 // (Claiming units from a counter instead balanced worse: the producers claim ahead by up to a
 // ring of tiles, so the first CTAs to reach a phase took most of its units.)
-__device__ __forceinline__ bool pd_produce(PdSmem& S, const PdGemv& g, unsigned off, int& it, int* err, bool sw) {
+__device__ __forceinline__ bool pd_produce(PdSmem& S, const PdGemv& g, unsigned off, PdRing& r, int* err, bool sw) {
     const int K = g.K;
     const int kc = K < PD_KC ? K : PD_KC;
     const int nchunks = (K + kc - 1) / kc;
@@ -215,29 +236,30 @@ __device__ __forceinline__ bool pd_produce(PdSmem& S, const PdGemv& g, unsigned 
     const int halves = g.swi ? 2 : 1;
     const unsigned bytes = (unsigned)(PD_ROWS * kc + PD_ROWS * (kc / 16));  // whole boxes (OOB zero-filled)
     const int ns = S.ns;
+    uint8_t* const ring = pd_ring(S);
     for (int u = pd_first(off);; u += gridDim.x) {
-        const int s0 = it % ns;
+        const int s0 = r.s;
         if (u >= units) {
             // phase end marker: a stage without data
-            if (!pd_wait(&S.empty[s0], ((unsigned)(it / ns) & 1u) ^ 1u, err)) {
+            if (!pd_wait(&S.empty[s0], r.ph ^ 1u, err)) {
                 atomicCAS(err, 0, 41);
                 return false;
             }
             S.tag[s0] = -1;
             mbar_arrive(&S.full[s0]);
-            it++;
+            pd_next(r, ns);
             return true;
         }
         for (int grp = 0; grp < halves; grp++)
             for (int half = 0; half < halves; half++) {
                 const int r0 = half * nout + u * pd_unit_rows(g) + grp * PD_ROWS;
-                for (int c = 0; c < nchunks; c++, it++) {
-                    const int s = it % ns;
-                    if (!pd_wait(&S.empty[s], ((unsigned)(it / ns) & 1u) ^ 1u, err)) {
+                for (int c = 0; c < nchunks; c++, pd_next(r, ns)) {
+                    const int s = r.s;
+                    if (!pd_wait(&S.empty[s], r.ph ^ 1u, err)) {
                         atomicCAS(err, 0, 41);
                         return false;
                     }
-                    uint8_t* st = pd_stage(s);
+                    uint8_t* st = ring + (size_t)s * PD_STAGE;
                     S.tag[s] = u;
                     if (sw) {
                         // one swizzled box per 128 bytes of K that exist (the consumers skip the rest)
@@ -351,7 +373,7 @@ __device__ __forceinline__ float pd_res_lane(const float* out, int ldo, int nout
 // hn counts this CTA's gate|up units over the whole step (it indexes the h handoff buffers).
 template <int M>
 __device__ __forceinline__ bool pd_consume(PdSmem& S, const PdGemv& g, const int8_t* xs, const uint16_t* xds,
-                                           int& it, int& hn, float* out, int ldo, bool resid, bool keys,
+                                           PdRing& r, int& hn, float* out, int ldo, bool resid, bool keys,
                                            int8_t* hq, uint16_t* hd, int* err, int u_first = -1,
                                            float res_first = 0.0f, const PdParams* xp = nullptr, int xpar = 0,
                                            int kbase = 0) {
@@ -363,6 +385,7 @@ __device__ __forceinline__ bool pd_consume(PdSmem& S, const PdGemv& g, const int
     const int nout = g.swi ? g.N / 2 : g.N;
     const int halves = g.swi ? 2 : 1;
     const int ns = S.ns;
+    const uint8_t* const ring = pd_ring(S);
     float acc[2][M], gate[2][M];
 #pragma unroll
     for (int r = 0; r < 2; r++)
@@ -373,7 +396,7 @@ __device__ __forceinline__ bool pd_consume(PdSmem& S, const PdGemv& g, const int
     bool failed = false;
     auto wait_full = [&](int s) {
         int ok = 1;
-        if (lane == 0) ok = pd_wait(&S.full[s], (unsigned)(it / ns) & 1u, err);
+        if (lane == 0) ok = pd_wait(&S.full[s], r.ph, err);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         __syncwarp();  // the other lanes read the stage after lane 0 saw it complete
         if (!ok) {
@@ -386,7 +409,7 @@ __device__ __forceinline__ bool pd_consume(PdSmem& S, const PdGemv& g, const int
         return ok != 0;
     };
     while (!failed) {
-        const int s0 = it % ns;
+        const int s0 = r.s;
         if (!wait_full(s0)) break;
         int u = 0;
         if (lane == 0) u = S.tag[s0];
@@ -394,7 +417,7 @@ __device__ __forceinline__ bool pd_consume(PdSmem& S, const PdGemv& g, const int
         if (u < 0) {  // no more units: release the marker stage
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.empty[s0]);
-            it++;
+            pd_next(r, ns);
             break;
         }
         const int hb = hn & 1, huse = hn >> 1;
@@ -423,13 +446,13 @@ __device__ __forceinline__ bool pd_consume(PdSmem& S, const PdGemv& g, const int
         for (int half = 0; half < halves && !failed; half++) {
             const int r0 = u * pd_unit_rows(g) + grp * PD_ROWS;
             const int rows = min(PD_ROWS, nout - r0);
-            for (int c = 0; c < nchunks; c++, it++) {
-                const int s = it % ns;
+            for (int c = 0; c < nchunks; c++, pd_next(r, ns)) {
+                const int s = r.s;
                 if ((grp | half | c) != 0 && !wait_full(s)) break;
                 const int k0 = c * kc, nbc = min(kc, K - k0) >> 5;
                 const bool act = lane < nbc;
-                const int8_t* wst = reinterpret_cast<const int8_t*>(pd_stage(s)) + (2 * warp) * kc + lane * 32;
-                const uint16_t* dst = reinterpret_cast<const uint16_t*>(pd_stage(s) + PD_ROWS * kc) + (2 * warp) * (kc / 32) + lane;
+                const int8_t* wst = reinterpret_cast<const int8_t*>((ring + (size_t)s * PD_STAGE)) + (2 * warp) * kc + lane * 32;
+                const uint16_t* dst = reinterpret_cast<const uint16_t*>((ring + (size_t)s * PD_STAGE) + PD_ROWS * kc) + (2 * warp) * (kc / 32) + lane;
                 int4 w[2][2];
                 float dw[2] = {0.f, 0.f};
                 if (act) {
@@ -543,24 +566,56 @@ __device__ __forceinline__ bool pd_consume(PdSmem& S, const PdGemv& g, const int
 // (lanes 0-3: tokens 2q, 2q+1), adding the warps' sums in warp order: the output, the
 // residual, the tensor-parallel exchange push (one 16-byte vector per lane), SwiGLU with the
 // h handoff of the dp4a consumer, or the argmax keys. Activation rows are ldx = K + 32 bytes
-// apart (conflict-free token fragments).
-template <int M>
+// apart in shared memory (conflict-free token fragments), or, with GX (the down phase, whose h
+// rows would take the ring's room), are read from global memory (L2: other CTAs wrote them)
+// straight into the token fragments, two chunks ahead of the stage they serve: a warp's chunk
+// sequence in a phase is 0, 1, ..., nchunks - 1 for every unit, so the next chunk is known
+// before its stage arrives.
+template <int M, bool GX>
 __device__ __forceinline__ bool pd_consume_mma(PdSmem& S, const PdGemv& g, const int8_t* xs, int ldx,
-                                               const uint16_t* xds, int& it, int& hn, int& rn, float* out, int ldo,
-                                               bool resid, bool keys, int8_t* hq, uint16_t* hd, int* err,
-                                               const PdParams* xp, int xpar, int kbase) {
+                                               const uint16_t* xds, PdRed* mred, PdRing& r, int& hn, int& rn,
+                                               float* out, int ldo, bool resid, bool keys, int8_t* hq, uint16_t* hd,
+                                               int* err, const PdParams* xp, int xpar, int kbase) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gq = lane >> 2, t = lane & 3;
     const int ns = S.ns;
+    const uint8_t* const ring = pd_ring(S);
     const int K = g.K, nb = K >> 5;
     const int kc = K < PD_KC ? K : PD_KC;
     const int nchunks = (K + kc - 1) / kc;
     const int nout = g.swi ? g.N / 2 : g.N;
     const int halves = g.swi ? 2 : 1;
     bool failed = false;
+    // the token fragments and scales of chunk c for this lane (zeros for tokens >= M)
+    struct Frag {
+        uint2 xv[4], dxa, dxb;
+    };
+    auto load_frag = [&](int c, Frag& f) {
+        const int gb0 = c * (kc >> 5) + 4 * warp;
+        const bool act = 4 * warp < (min(kc, K - c * kc) >> 5);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int8_t* src = xs + (size_t)gq * ldx + (gb0 + j) * 32 + 8 * t;
+            f.xv[j] = (act && gq < M) ? (GX ? __ldcg(reinterpret_cast<const uint2*>(src))
+                                            : *reinterpret_cast<const uint2*>(src))
+                                      : make_uint2(0u, 0u);
+        }
+        const uint16_t* sa = xds + (size_t)(2 * t) * nb + gb0;
+        const uint16_t* sb = sa + nb;
+        f.dxa = (act && 2 * t < M) ? (GX ? __ldcg(reinterpret_cast<const uint2*>(sa)) : *reinterpret_cast<const uint2*>(sa))
+                                   : make_uint2(0u, 0u);
+        f.dxb = (act && 2 * t + 1 < M) ? (GX ? __ldcg(reinterpret_cast<const uint2*>(sb))
+                                             : *reinterpret_cast<const uint2*>(sb))
+                                       : make_uint2(0u, 0u);
+    };
+    Frag f0{}, f1{};
+    if (GX) {  // the first two chunks, in flight while the first stage is awaited
+        load_frag(0, f0);
+        load_frag(1 % nchunks, f1);
+    }
     auto wait_full = [&](int s) {
         int ok = 1;
-        if (lane == 0) ok = pd_wait(&S.full[s], (unsigned)(it / ns) & 1u, err);
+        if (lane == 0) ok = pd_wait(&S.full[s], r.ph, err);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         __syncwarp();
         if (!ok) {
@@ -574,7 +629,7 @@ __device__ __forceinline__ bool pd_consume_mma(PdSmem& S, const PdGemv& g, const
     };
     float gate[4] = {0.f, 0.f, 0.f, 0.f};
     while (!failed) {
-        const int s0 = it % ns;
+        const int s0 = r.s;
         if (!wait_full(s0)) break;
         int u = 0;
         if (lane == 0) u = S.tag[s0];
@@ -582,7 +637,7 @@ __device__ __forceinline__ bool pd_consume_mma(PdSmem& S, const PdGemv& g, const
         if (u < 0) {
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.empty[s0]);
-            it++;
+            pd_next(r, ns);
             break;
         }
         const int hb = hn & 1, huse = hn >> 1;
@@ -611,11 +666,11 @@ __device__ __forceinline__ bool pd_consume_mma(PdSmem& S, const PdGemv& g, const
                 }
             }
             float acc[4] = {0.f, 0.f, 0.f, 0.f};
-            for (int c = 0; c < nchunks; c++, it++) {
-                const int s = it % ns;
+            for (int c = 0; c < nchunks; c++, pd_next(r, ns)) {
+                const int s = r.s;
                 if ((grp | half | c) != 0 && !wait_full(s)) break;
                 const int k0 = c * kc, nbc = min(kc, K - k0) >> 5;
-                const uint8_t* st = pd_stage(s);
+                const uint8_t* st = (ring + (size_t)s * PD_STAGE);
                 const bool act = 4 * warp < nbc;
                 uint2 wa[4], wb[4], swa = make_uint2(0u, 0u), swb = make_uint2(0u, 0u);
                 if (act) {
@@ -632,21 +687,21 @@ __device__ __forceinline__ bool pd_consume_mma(PdSmem& S, const PdGemv& g, const
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&S.empty[s]);
+                Frag fc;
+                if (GX) {
+                    fc = f0;
+                    f0 = f1;
+                    load_frag((c + 2) % nchunks, f1);  // the chunk two stages on (of this or the next unit)
+                } else {
+                    load_frag(c, fc);
+                }
                 if (act) {
-                    const int gb0 = (k0 >> 5) + 4 * warp;
-                    uint2 xv[4];
-                    uint2 dxa = make_uint2(0u, 0u), dxb = make_uint2(0u, 0u);
-#pragma unroll
-                    for (int j = 0; j < 4; j++)
-                        xv[j] = gq < M ? *reinterpret_cast<const uint2*>(xs + (size_t)gq * ldx + (gb0 + j) * 32 + 8 * t)
-                                       : make_uint2(0u, 0u);
-                    if (2 * t < M) dxa = *reinterpret_cast<const uint2*>(xds + (size_t)(2 * t) * nb + gb0);
-                    if (2 * t + 1 < M) dxb = *reinterpret_cast<const uint2*>(xds + (size_t)(2 * t + 1) * nb + gb0);
+                    const uint2 dxa = fc.dxa, dxb = fc.dxb;
 #pragma unroll
                     for (int j = 0; j < 4; j++) {
                         if (4 * warp + j >= nbc) break;
                         const uint32_t a[4] = {wa[j].x, wb[j].x, wa[j].y, wb[j].y};
-                        const uint32_t b[2] = {xv[j].x, xv[j].y};
+                        const uint32_t b[2] = {fc.xv[j].x, fc.xv[j].y};
                         int d[4];
                         mma_s8_bias(d, a, b, 0x4B400000);
                         const uint32_t wsa = j < 2 ? swa.x : swa.y, wsb = j < 2 ? swb.x : swb.y;
@@ -671,7 +726,7 @@ __device__ __forceinline__ bool pd_consume_mma(PdSmem& S, const PdGemv& g, const
             // Buffer b of the two holds every other group: written once all warps have read it
             // (rfree), read once all warps have written it (rfull); the waits are bounded
             const int buf = rn & 1, use = rn >> 1;  // rn: row groups of the step so far
-            float(*red)[PD_ROWS][8] = S.mred[buf];
+            float(*red)[PD_ROWS][8] = (*mred)[buf];
             int rok = 1;
             if (use > 0) {
                 if (lane == 0) rok = pd_wait(&S.rfree[buf], (unsigned)(use - 1) & 1u, err);
@@ -775,11 +830,12 @@ __device__ __forceinline__ bool pd_consume_mma(PdSmem& S, const PdGemv& g, const
 // Q8_0 of the bf16 result (rms_norm.rs:144-176): the input rounded to bf16, lane l sums the
 // squares of elements 128i + 4l .. +3 in pass order, a butterfly gives the total, inv =
 // 1/sqrt(sum/dim + eps), out = bf16((x*inv)*w), quantized per 32-element block by the block's 8
-// lanes. The second pass reads the row again (from L2).
+// lanes. The second pass reads the row again (from L2). A row's arithmetic does not depend on
+// the batch size.
 __device__ __forceinline__ void pd_norm_row_warp(const float* __restrict__ xr, int dim, const uint16_t* nw, float eps,
                                                  int lane, int8_t* xq, uint16_t* xd) {
     float ss = 0.0f;
-#pragma unroll 4
+#pragma unroll 8
     for (int e = lane * 4; e < dim; e += 128) {
         const float4 t = __ldcg(reinterpret_cast<const float4*>(xr + e));
         const float v[4] = {round_bf16(t.x), round_bf16(t.y), round_bf16(t.z), round_bf16(t.w)};
@@ -788,7 +844,7 @@ __device__ __forceinline__ void pd_norm_row_warp(const float* __restrict__ xr, i
     }
     ss = warp_sum(ss);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), eps)));
-#pragma unroll 4
+#pragma unroll 8
     for (int e = lane * 4; e < dim; e += 128) {
         const float4 t = __ldcg(reinterpret_cast<const float4*>(xr + e));
         const uint2 wt = *reinterpret_cast<const uint2*>(nw + e);
@@ -806,15 +862,15 @@ __device__ __forceinline__ void pd_norm_row_warp(const float* __restrict__ xr, i
 // the GEMV of one phase: the dp4a consumer for batches of 1-4 (bit-identical to the per-layer
 // decode path), the MMA consumer for 5-8 (activation rows K + PD_XPAD bytes apart)
 template <int M>
-__device__ __forceinline__ bool pd_phase(PdSmem& S, const PdGemv& g, const int8_t* xs, const uint16_t* xds, int& it,
-                                         int& hn, int& rn, float* out, int ldo, bool resid, bool keys, int8_t* hq,
+__device__ __forceinline__ bool pd_phase(PdSmem& S, const PdGemv& g, const int8_t* xs, const uint16_t* xds,
+                                         PdRed* mred, PdRing& r, int& hn, int& rn, float* out, int ldo, bool resid, bool keys, int8_t* hq,
                                          uint16_t* hd, int* err, int u_first = -1, float res_first = 0.0f,
                                          const PdParams* xp = nullptr, int xpar = 0, int kbase = 0) {
     if constexpr (M > 4)
-        return pd_consume_mma<M>(S, g, xs, g.K + PD_XPAD, xds, it, hn, rn, out, ldo, resid, keys, hq, hd, err, xp, xpar,
-                                 kbase);
+        return pd_consume_mma<M, false>(S, g, xs, g.K + PD_XPAD, xds, mred, r, hn, rn, out, ldo, resid, keys, hq, hd, err,
+                                        xp, xpar, kbase);
     else
-        return pd_consume<M>(S, g, xs, xds, it, hn, out, ldo, resid, keys, hq, hd, err, u_first, res_first, xp, xpar,
+        return pd_consume<M>(S, g, xs, xds, r, hn, out, ldo, resid, keys, hq, hd, err, u_first, res_first, xp, xpar,
                              kbase);
 }
 
@@ -1205,7 +1261,7 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, PdSmem& S, PdA
 template <int M>
 __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdParams p) {
     PdSmem& S = *reinterpret_cast<PdSmem*>(pd_dsmem);
-    uint8_t* area = pd_dsmem + sizeof(PdSmem) + (size_t)p.ns * PD_STAGE;
+    uint8_t* area = pd_dsmem + p.ring_off + (size_t)p.ns * PD_STAGE;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int p0 = *p.pos_dev;
     // exchanges and steps completed before this launch (tensor parallelism): CTA 0 advances them
@@ -1233,30 +1289,32 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
     if (tid == 0) {
         S.fail = 0;
         S.ns = p.ns;
+        S.ring_off = p.ring_off;
     }
     __syncthreads();
     if (warp == PD_CONS) {
         // producer: every matrix of the step, in order, never waiting for activations
         if (lane == 0) {
-            int it = 0;
+            PdRing r = {0, 0, 0u};
             unsigned off = 0;
             bool ok = true;
             for (int l = 0; l < p.n_layers && ok; l++)
                 for (int k = PH_QKV; k <= PH_DN && ok; k++) {
                     const PdGemv g = pd_gemv(p, l, k);
-                    ok = pd_produce(S, g, off, it, p.err, M > 4);
+                    ok = pd_produce(S, g, off, r, p.err, M > 4);
                     off += (unsigned)pd_units(g);
                 }
-            if (ok) pd_produce(S, pd_gemv(p, 0, PH_LM), off, it, p.err, M > 4);
+            if (ok) pd_produce(S, pd_gemv(p, 0, PH_LM), off, r, p.err, M > 4);
             // leave only after the copies in flight have landed (bounded)
-            for (int j = max(0, it - p.ns); j < it; j++)
+            for (int j = max(0, r.it - p.ns); j < r.it; j++)
                 mbar_wait_ns(&S.full[j % p.ns], (unsigned)(j / p.ns) & 1u, PD_WAIT_NS);
         }
         return;
     }
     const int nsplit = p0 / PD_ATT_C + 1;
     const int H = p.H, I = p.I;
-    const int Kmax = max(max(H, p.Hq * 128), I);
+    // the widest activation row kept in shared memory (batches of 5-8 stream h from L2)
+    const int Kmax = M > 4 ? max(H, p.Hq * 128) : max(max(H, p.Hq * 128), I);
     // union area, GEMV phases: activations xs [M][K] int8 and xds [M][K/32] fp16, the norm
     // weight nws [H] bf16 (prefetched before the barrier that precedes its prologue) and the
     // f32 staging row xrow [H]
@@ -1273,13 +1331,13 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
         }
     };
     float* xrow = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(nws) + (size_t)H * 2);
+    PdRed* mred = M > 4 ? reinterpret_cast<PdRed*>(pd_align128(reinterpret_cast<uint8_t*>(xrow + H))) : nullptr;
     PdAtt& A = *reinterpret_cast<PdAtt*>(area);
     // RMSNorm + Q8_0 of the M rows of x (written by other CTAs) into xs/xds; the norm weight's
     // copies are already in flight
     auto norm_rows = [&]() {
         if constexpr (M > 4) {
-            // batches of 5-8: warp w normalises row w on its own (warp sums only, every load of
-            // a pass in flight), all rows at once
+            // batches of 5-8: warp w normalises row w on its own (warp sums only), all rows at once
             pd_csync();
             if (warp < M) pd_norm_row_warp(p.x + (size_t)warp * H, H, nws, p.eps, lane, xs + (size_t)warp * (H + XP),
                                            xds + (size_t)warp * (H / 32));
@@ -1295,7 +1353,8 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
         }
         pd_csync();
     };
-    int it = 0, hn = 0, rn = 0;
+    PdRing ring = {0, 0, 0u};
+    int hn = 0, rn = 0;
     unsigned epoch = 0;
     // the consumers' copy of the producer's running unit offset (phase k of layer l starts at
     // position l * per_layer + before[k] of the dealt sequence)
@@ -1309,7 +1368,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
         const PdLayer& L = p.layers[l];
         // QKV: input RMSNorm + Q8_0 of x, the q|k|v rows
         norm_rows();
-        if (!pd_phase<M>(S, pd_gemv(p, l, PH_QKV), xs, xds, it, hn, rn, p.qkv, p.Nqkv, false, false, nullptr,
+        if (!pd_phase<M>(S, pd_gemv(p, l, PH_QKV), xs, xds, mred, ring, hn, rn, p.qkv, p.Nqkv, false, false, nullptr,
                            nullptr, p.err))
             return;
         // the first attention item's cache rows start loading before the barrier
@@ -1329,7 +1388,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
             pd_prefetch(xds, p.att_d, M * (Ko / 32) * 2, tid);
             cp_async_wait<0>();
             pd_csync();
-            if (!pd_phase<M>(S, pd_gemv(p, l, PH_O), xs, xds, it, hn, rn, p.x, H, !xch, false, nullptr, nullptr,
+            if (!pd_phase<M>(S, pd_gemv(p, l, PH_O), xs, xds, mred, ring, hn, rn, p.x, H, !xch, false, nullptr, nullptr,
                                p.err, u_o, res_o, xch ? &p : nullptr, 0))
                 return;
         }
@@ -1343,17 +1402,22 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
         const float res_dn = pd_res_lane<M>(p.x, H, H, u_dn);
         // GU: post-attention RMSNorm, gate|up, SiLU(gate)*up -> h as Q8_0
         norm_rows();
-        if (!pd_phase<M>(S, pd_gemv(p, l, PH_GU), xs, xds, it, hn, rn, nullptr, 0, false, false, p.hq, p.hd, p.err))
+        if (!pd_phase<M>(S, pd_gemv(p, l, PH_GU), xs, xds, mred, ring, hn, rn, nullptr, 0, false, false, p.hq, p.hd, p.err))
             return;
         if (!pd_grid_barrier(p, S, epoch)) return;
         // DN: h (already Q8_0) as activations, residual into x
-        stage_rows(p.hq, I);
+        if (M <= 4) stage_rows(p.hq, I);
         pd_prefetch(xds, p.hd, M * (I / 32) * 2, tid);
         cp_async_wait<0>();
         pd_csync();
-        if (!pd_phase<M>(S, pd_gemv(p, l, PH_DN), xs, xds, it, hn, rn, p.x, H, !xch, false, nullptr, nullptr, p.err,
-                           u_dn, res_dn, xch ? &p : nullptr, 1))
-            return;
+        bool dn_ok;
+        if constexpr (M > 4)
+            dn_ok = pd_consume_mma<M, true>(S, pd_gemv(p, l, PH_DN), p.hq, I, p.hd, mred, ring, hn, rn, p.x, H, !xch,
+                                            false, nullptr, nullptr, p.err, xch ? &p : nullptr, 1, 0);
+        else
+            dn_ok = pd_phase<M>(S, pd_gemv(p, l, PH_DN), xs, xds, mred, ring, hn, rn, p.x, H, !xch, false, nullptr,
+                                nullptr, p.err, u_dn, res_dn, xch ? &p : nullptr, 1);
+        if (!dn_ok) return;
         if (xch && !pd_exchange_sum<M>(p, S, 1, (seq0 + 2u * (unsigned)l + 2u) * (unsigned)(p.tp - 1), u_dn))
             return;
         pd_grid_arrive(p, epoch);
@@ -1362,7 +1426,7 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
     }
     // LM head: final RMSNorm, logits, greedy argmax keys
     norm_rows();
-    if (!pd_phase<M>(S, pd_gemv(p, 0, PH_LM), xs, xds, it, hn, rn, p.logits, p.V, false, true, nullptr, nullptr,
+    if (!pd_phase<M>(S, pd_gemv(p, 0, PH_LM), xs, xds, mred, ring, hn, rn, p.logits, p.V, false, true, nullptr, nullptr,
                        p.err, -1, 0.0f, nullptr, 0, p.vbase))
         return;
     pd_csync();
@@ -1372,26 +1436,35 @@ __global__ void __launch_bounds__(PD_THREADS, 1) decode_step_kernel(const PdPara
 
 // ---- host ----
 static size_t pd_area_bytes(int64_t m, int64_t H, int64_t Hqd, int64_t I) {
-    const int64_t Kmax = std::max({H, Hqd, I});
-    const int64_t xp = m > 4 ? PD_XPAD : 0;
-    const size_t gemv = (size_t)(m * (Kmax + xp) + m * (Kmax / 32) * 2 + H * 2 + H * 4);
+    // GEMV phases: activations [m][Kmax (+ pad)], their scales, the norm weight, the f32 row and,
+    // for batches of 5-8 (whose h streams from L2 instead), the partial-sum buffers
+    const bool mma = m > 4;
+    const int64_t Kmax = mma ? std::max(H, Hqd) : std::max({H, Hqd, I});
+    size_t gemv = (size_t)(m * (Kmax + (mma ? PD_XPAD : 0)) + m * (Kmax / 32) * 2 + H * 2 + H * 4);
+    if (mma) gemv = ((gemv + 127) & ~(size_t)127) + sizeof(PdRed);
     return std::max(gemv, sizeof(PdAtt));
 }
 
 constexpr size_t PD_SMEM_MAX = 227 * 1024;
 constexpr int PD_MIN_STAGES = 3;
 
+// the ring starts after PdSmem, 1024-aligned (the swizzled boxes of batches 5-8 need it)
+static size_t pd_ring_off(int64_t m) {
+    (void)m;
+    return (sizeof(PdSmem) + 1023) & ~(size_t)1023;
+}
+
 // ring stages that fit beside the union area (at most PD_MAX_STAGES; 0 when fewer than
-// PD_MIN_STAGES fit): wider K rows at larger batches give the activations more room
+// PD_MIN_STAGES fit)
 static int pd_ns(int64_t m, int64_t H, int64_t Hqd, int64_t I) {
-    const size_t fixed = sizeof(PdSmem) + pd_area_bytes(m, H, Hqd, I);
+    const size_t fixed = pd_ring_off(m) + pd_area_bytes(m, H, Hqd, I);
     if (fixed >= PD_SMEM_MAX) return 0;
     const int ns = (int)std::min<size_t>(PD_MAX_STAGES, (PD_SMEM_MAX - fixed) / PD_STAGE);
     return ns >= PD_MIN_STAGES ? ns : 0;
 }
 
 static size_t pd_smem_bytes(int64_t m, int64_t H, int64_t Hqd, int64_t I) {
-    return sizeof(PdSmem) + (size_t)pd_ns(m, H, Hqd, I) * PD_STAGE + pd_area_bytes(m, H, Hqd, I);
+    return pd_ring_off(m) + (size_t)pd_ns(m, H, Hqd, I) * PD_STAGE + pd_area_bytes(m, H, Hqd, I);
 }
 
 bool decode_persist_supported(lq_ctx* ctx, int64_t m, int64_t H, int64_t Hq, int64_t Hkv, int64_t I,
@@ -1513,6 +1586,7 @@ int launch_decode_persist(lq_ctx* ctx, const PdLaunch& a) {
     p.bar = a.counters;
     p.err = ctx->err_flag;
     p.ns = ns;
+    p.ring_off = (int)pd_ring_off(a.m);
     p.tp = a.tp;
     p.rank = a.rank;
     p.vbase = (int)a.vbase;

@@ -636,8 +636,12 @@ static int create_model(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, 
         // the persistent decode step (dense models, one GPU or tensor-parallel ranks that
         // exchange the o/down partial sums inside the kernel); LQ_NO_PERSIST=1 keeps the
         // per-layer kernels, LQ_TP_NCCL=1 the per-layer kernels with NCCL all-reduces under TP.
-        // The largest batch (up to 8) whose activations leave room for the weight ring.
-        int64_t pb = std::min<int64_t>(max_batch, 8);
+        // The largest batch whose activations leave room for the weight ring: up to 4 by default
+        // (the dp4a consumers, bit-identical to the per-layer path); LQ_PERSIST_MAX_BATCH=8 also
+        // takes batches of 5-8 (tensor-core consumers; slower than the per-layer kernels today).
+        int64_t pmax = 4;
+        if (const char* e = getenv("LQ_PERSIST_MAX_BATCH")) pmax = std::max<int64_t>(1, std::min<int64_t>(8, atoll(e)));
+        int64_t pb = std::min<int64_t>(max_batch, pmax);
         while (pb > 0 && !lq::decode_persist_supported(ctx, pb, H, Hq, Hkv, I, ctx_max)) pb--;
         bool want = !moe && m->fused_decode && pb > 0 && (T == 1 || getenv("LQ_TP_NCCL") == nullptr);
         if (!moe && T > 1) {

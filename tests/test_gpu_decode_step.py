@@ -120,7 +120,7 @@ def test_persistent_step_matches_oracle(ctx, lq8_lib, oracle):
 @pytest.mark.parametrize("cfg_name,cfgd", [("wide", CONFIGS["wide"]), ("gqa8_ragged_vocab", CONFIGS["gqa8_ragged_vocab"]),
                                            ("qwen3_8b_2l", dict(TINY, hidden=4096, inter=12288, n_heads=32,
                                                                 n_kv_heads=8, vocab=151936, tied=0))])
-def test_persistent_batch_rows_are_independent(ctx, lq8_lib, oracle, cfg_name, cfgd):
+def test_persistent_batch_rows_are_independent(ctx, lq8_lib, oracle, monkeypatch, cfg_name, cfgd):
     """Batches of 5-8 rows run the persistent step's tensor-core consumer: each token is its own
     MMA column with its own scales, the warps' partial sums are added in warp order, and
     attention and the norms work per row, so a row's logits do not depend on the batch size.
@@ -130,8 +130,10 @@ def test_persistent_batch_rows_are_independent(ctx, lq8_lib, oracle, cfg_name, c
     seed, L, steps = 5, 70, 4
     cfg = lq8_lib.make_config(**cfgd)
     prompts = np.stack([oracle.gen_tokens(seed, s, L, cfgd["vocab"]) for s in range(8)])
+    monkeypatch.setenv("LQ_PERSIST_MAX_BATCH", "8")  # batches of 5-8 are opt-in
     big = lq8_lib.Qwen3ForCausalLM(ctx, cfg, seed, max_batch=8, ctx_max=96)
     small = lq8_lib.Qwen3ForCausalLM(ctx, cfg, seed, max_batch=5, ctx_max=96)
+    monkeypatch.delenv("LQ_PERSIST_MAX_BATCH")
     try:
         t8 = big.prefill(prompts)
         big.set_batch(8)

@@ -156,11 +156,16 @@ def test_qwen3_8b_free_running_tokens(ctx, lq8_lib, oracle):
         record("8b_free_running", identical=n)
 
 
-def test_qwen3_8b_batch8_vs_oracle(ctx, lq8_lib, oracle):
-    """Config 3's shapes at batch 8: the persistent step's tensor-core consumer (5-8 rows),
-    its 5-stage ring and padded activation rows, against the oracle teacher-forced."""
-    kernels = _dense_vs_oracle("8b_batch8", ctx, lq8_lib, oracle, QWEN3_8B_2L, B=8, L=40, steps=4)
+def test_qwen3_8b_batch8_vs_oracle(ctx, lq8_lib, oracle, monkeypatch):
+    """Config 3's shapes at batch 8: the persistent step's tensor-core consumer (5-8 rows, opt-in
+    with LQ_PERSIST_MAX_BATCH), h streamed from L2, against the oracle teacher-forced; and the
+    default per-layer kernels at the same batch."""
+    monkeypatch.setenv("LQ_PERSIST_MAX_BATCH", "8")
+    kernels = _dense_vs_oracle("8b_batch8_persistent", ctx, lq8_lib, oracle, QWEN3_8B_2L, B=8, L=40, steps=4)
     assert kernels == 3
+    monkeypatch.delenv("LQ_PERSIST_MAX_BATCH")
+    kernels = _dense_vs_oracle("8b_batch8", ctx, lq8_lib, oracle, QWEN3_8B_2L, B=8, L=40, steps=4)
+    assert kernels > 3
 
 
 @pytest.mark.parametrize("B", [1, 4])

@@ -248,11 +248,13 @@ QWEN3_32B_2L = dict(hidden=5120, layers=2, n_heads=64, n_kv_heads=8, head_dim=12
                     max_pos=40960, tied=0, eps=1e-6, theta=1e6, init_std=0.02, norm_std=0.0)
 
 
-def _tp32_rank_main(rank, world, port, q, prompts, fed, nccl_path):
+def _tp32_rank_main(rank, world, port, q, prompts, fed, path):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    if nccl_path:
+    if path == "nccl":
         os.environ["LQ_TP_NCCL"] = "1"
+    elif path == "persistent":
+        os.environ["LQ_PERSIST_MAX_BATCH"] = "8"
     for p in (REPO, os.path.join(REPO, "qwen-omni-inference-rs_b200")):
         sys.path.insert(0, p)
     import datetime
@@ -287,15 +289,17 @@ def _tp32_rank_main(rank, world, port, q, prompts, fed, nccl_path):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("nccl_path", [False, True])
-def test_tensor_parallel_32b_shapes_2_gpus(oracle, nccl_path):
+@pytest.mark.parametrize("path", ["persistent", "nccl"])
+def test_tensor_parallel_32b_shapes_2_gpus(oracle, path):
     """Config 4's shapes (2 layers, full vocabulary) as two tensor-parallel ranks at batch 8:
-    each rank holds 32 / 4 heads, 12800 intermediate rows, 75968 LM-head rows. Default path:
-    the persistent decode step with the o/down partial sums exchanged inside the kernel over
-    NVLink (a 3-kernel decode graph); LQ_TP_NCCL=1: the per-layer kernels with NCCL
-    all-reduces. Both teacher-forced against the single-device oracle with the tolerance of
-    the headline-shape tests (the noise floor of these shapes; test_gpu_headline.py), tokens
-    equal wherever the oracle's margin exceeds twice the step's difference."""
+    each rank holds 32 / 4 heads, 12800 intermediate rows, 75968 LM-head rows. "persistent"
+    (LQ_PERSIST_MAX_BATCH=8): the persistent decode step with the o/down partial sums exchanged
+    inside the kernel over NVLink (a 3-kernel decode graph); "nccl": the per-layer kernels with
+    NCCL all-reduces (the default at batch 8). Both teacher-forced against the single-device
+    oracle with the tolerance of the headline-shape tests (the noise floor of these shapes;
+    test_gpu_headline.py), tokens equal wherever the oracle's margin exceeds twice the step's
+    difference."""
+    nccl_path = path == "nccl"
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -319,7 +323,7 @@ def test_tensor_parallel_32b_shapes_2_gpus(oracle, nccl_path):
     mctx = mp.get_context("spawn")
     qq = mctx.Queue()
     port = _free_port()
-    procs = [mctx.Process(target=_tp32_rank_main, args=(r, 2, port, qq, prompts, fed, nccl_path)) for r in range(2)]
+    procs = [mctx.Process(target=_tp32_rank_main, args=(r, 2, port, qq, prompts, fed, path)) for r in range(2)]
     for p in procs:
         p.start()
     res = [qq.get(timeout=900) for _ in procs]
@@ -337,7 +341,7 @@ def test_tensor_parallel_32b_shapes_2_gpus(oracle, nccl_path):
             m = parity_metrics(r0["logits"][s, b], olgs[s, b])
             srt = np.sort(olgs[s, b])
             same = int(r0["tokens"][s, b]) == oracle.argmax(olgs[s, b])
-            record("32b_tp2_" + ("nccl" if nccl_path else "persistent"), step=s, row=b, same_token=same,
+            record("32b_tp2_" + path, step=s, row=b, same_token=same,
                    margin=float(srt[-1] - srt[-2]), **m)
             assert m["cos"] >= 0.9995 and m["max_rel"] <= 5e-2, (s, b, m)
             assert same or srt[-1] - srt[-2] <= 2 * m["max_abs"], (s, b)
