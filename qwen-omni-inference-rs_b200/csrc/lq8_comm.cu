@@ -5,6 +5,7 @@
 // rank 0 makes a unique id (lq_comm_unique_id), the host side hands it to the other ranks
 // (e.g. torch.distributed over gloo), every rank calls lq_comm_init. Collectives run on the
 // context's stream, so they order with the kernels and can be captured in the decode graph.
+#include "lq8_async.cuh"
 #include "lq8_internal.cuh"
 
 #include <dlfcn.h>
@@ -80,6 +81,112 @@ int comm_allgather_f32(lq_comm* c, const float* send, float* recv, int64_t count
     }
     return nccl_check(c->ctx, nccl().all_gather(send, recv, (size_t)count, ncclFloat32, c->comm, c->ctx->stream),
                       "ncclAllGather");
+}
+
+// ---- one-shot all-reduce over the ranks' CUDA-IPC exchange regions (decode-sized rows) ----
+//
+// Each CTA owns a column slice of the rows: it stores its slice of this rank's partial sums
+// into slot (parity, rank) of every rank's buffer with 16-byte peer stores, publishes them
+// (system-scope fence, one counter increment per peer), waits (bounded) until every peer's CTA
+// of the same index has done the same, and writes x = p_0 + p_1 + ... in rank order, so every
+// rank holds the same sums. The buffer parity alternates per launch (each CTA counts its own
+// launches): a rank can be at most one all-reduce ahead of a peer, so it never overwrites what
+// the peer still reads.
+struct ArDevice {
+    float* buf[ALLREDUCE_MAX_TP];        // every rank's buffer [2][tp][ALLREDUCE_ROWS][H]
+    unsigned* flags[ALLREDUCE_MAX_TP];   // every rank's counters [ALLREDUCE_CTAS]
+    unsigned* done;                      // this rank's launches per CTA [ALLREDUCE_CTAS]
+    int tp, rank;
+};
+
+__device__ __forceinline__ bool ar_wait(const unsigned* p, unsigned target, int* err) {
+    const uint64_t t0 = global_ns();
+    for (int i = 1;; i++) {
+        unsigned v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+        if ((int)(v - target) >= 0) return true;
+        if ((i & 63) == 0) {
+            if (*reinterpret_cast<volatile const int*>(err) != 0) return false;
+            if (global_ns() - t0 > 2000000000ull) {
+                atomicCAS(err, 0, 60);
+                return false;
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) xchg_allreduce_kernel(const float* __restrict__ part, int rows, int H,
+                                                               float* __restrict__ x, ArDevice a, int* err) {
+    __shared__ unsigned sdone;
+    __shared__ int ok;
+    pdl_wait();  // the partial sums are the preceding kernel's
+    const int c = blockIdx.x, T = a.tp;
+    const int per = ((H / 4 + (int)gridDim.x - 1) / (int)gridDim.x) * 4;
+    const int c0 = c * per, c1 = min(H, c0 + per), w4 = max(0, c1 - c0) / 4;
+    if (threadIdx.x == 0) sdone = a.done[c];
+    __syncthreads();
+    const unsigned done = sdone;
+    const size_t slot = (size_t)ALLREDUCE_ROWS * H;  // floats per (parity, source rank)
+    const size_t mine = ((size_t)(done & 1u) * T + a.rank) * slot;
+    for (int i = threadIdx.x; i < rows * w4; i += blockDim.x) {
+        const int r = i / w4, col = c0 + 4 * (i % w4);
+        const float4 v = *reinterpret_cast<const float4*>(part + (size_t)r * H + col);
+#pragma unroll
+        for (int t = 0; t < ALLREDUCE_MAX_TP; t++)
+            if (t < T) *reinterpret_cast<float4*>(a.buf[t] + mine + (size_t)r * H + col) = v;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();  // this CTA's peer stores, ordered before by the barrier
+#pragma unroll
+        for (int t = 0; t < ALLREDUCE_MAX_TP; t++)
+            if (t < T && t != a.rank) asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a.flags[t] + c) : "memory");
+        ok = ar_wait(a.flags[a.rank] + c, (done + 1u) * (unsigned)(T - 1), err) ? 1 : 0;
+        if (ok) a.done[c] = done + 1u;
+    }
+    __syncthreads();
+    pdl_trigger();
+    if (!ok) return;
+    const float* b = a.buf[a.rank] + (size_t)(done & 1u) * T * slot;
+    for (int i = threadIdx.x; i < rows * w4; i += blockDim.x) {
+        const int r = i / w4, col = c0 + 4 * (i % w4);
+        float4 v = __ldcg(reinterpret_cast<const float4*>(b + (size_t)r * H + col));
+        for (int t = 1; t < T; t++) {
+            const float4 u = __ldcg(reinterpret_cast<const float4*>(b + (size_t)t * slot + (size_t)r * H + col));
+            v.x = __fadd_rn(v.x, u.x);
+            v.y = __fadd_rn(v.y, u.y);
+            v.z = __fadd_rn(v.z, u.z);
+            v.w = __fadd_rn(v.w, u.w);
+        }
+        *reinterpret_cast<float4*>(x + (size_t)r * H + col) = v;
+    }
+}
+
+int launch_xchg_allreduce(lq_ctx* ctx, const AllreduceRegions& ar, const float* part, int64_t rows, int64_t H,
+                          float* x) {
+    if (rows < 1 || rows > ALLREDUCE_ROWS || H % 4 || ar.tp < 2 || ar.tp > ALLREDUCE_MAX_TP)
+        return set_error(ctx, LQ_ERR_INVALID_ARG, "all-reduce over the exchange regions: %lld rows of %lld",
+                         (long long)rows, (long long)H);
+    size_t fo = 0, dn = 0;
+    allreduce_layout(H, ar.tp, &fo, &dn);
+    ArDevice a = {};
+    a.tp = ar.tp;
+    a.rank = ar.rank;
+    for (int t = 0; t < ar.tp; t++) {
+        a.buf[t] = static_cast<float*>(ar.region[t]);
+        a.flags[t] = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ar.region[t]) + fo);
+    }
+    a.done = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ar.region[ar.rank]) + dn);
+    return launch_kernel(ctx, xchg_allreduce_kernel, dim3(ALLREDUCE_CTAS), dim3(256), 0, "xchg_allreduce", part,
+                         (int)rows, (int)H, x, a, ctx->err_flag);
+}
+
+size_t allreduce_layout(int64_t H, int tp, size_t* flags_off, size_t* done_off) {
+    auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
+    const size_t bbytes = al((size_t)2 * tp * ALLREDUCE_ROWS * (size_t)H * 4);
+    *flags_off = bbytes;
+    *done_off = bbytes + al(ALLREDUCE_CTAS * 4);
+    return *done_off + al(ALLREDUCE_CTAS * 4);
 }
 
 int comm_rank(const lq_comm* c) { return c ? c->rank : 0; }

@@ -248,6 +248,19 @@ int comm_allreduce_sum_f32(lq_comm* c, const float* send, float* recv, int64_t c
 int comm_allreduce_max_u64(lq_comm* c, unsigned long long* buf, int64_t count);
 int comm_allgather_f32(lq_comm* c, const float* send, float* recv, int64_t count);
 int comm_rank(const lq_comm* c);
+// one-shot all-reduce of up to ALLREDUCE_ROWS rows over CUDA-IPC exchange regions (every rank's
+// region mapped by every rank; layout from allreduce_layout, zeroed before first use):
+// x [rows][H] = sum over ranks of part (rank order); replaces the NCCL all-reduce of decode rows
+constexpr int ALLREDUCE_ROWS = 8;
+constexpr int ALLREDUCE_CTAS = 32;
+constexpr int ALLREDUCE_MAX_TP = 8;
+struct AllreduceRegions {
+    void* region[ALLREDUCE_MAX_TP];
+    int tp, rank;
+};
+size_t allreduce_layout(int64_t H, int tp, size_t* flags_off, size_t* done_off);
+int launch_xchg_allreduce(lq_ctx* ctx, const AllreduceRegions& ar, const float* part, int64_t rows, int64_t H,
+                          float* x);
 int comm_world(const lq_comm* c);
 lq_ctx* comm_ctx(const lq_comm* c);
 // add `offset` to the index half of the non-zero argmax keys (a vocabulary shard's base)

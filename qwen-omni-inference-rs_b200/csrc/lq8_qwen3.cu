@@ -93,6 +93,10 @@ struct lq_model {
     // peers': opened from their CUDA IPC handles)
     void* xchg[8] = {};
     std::vector<void*> ipc_open;
+    // tensor parallelism, decode rows (<= 8) of the per-layer path: the one-shot all-reduce over
+    // every rank's CUDA-IPC region instead of NCCL (LQ_TP_NCCL=1 keeps NCCL)
+    bool ar_ok = false;
+    lq::AllreduceRegions ar{};
 };
 
 namespace {
@@ -154,6 +158,8 @@ inline const float* rp_resid(lq_model* m, bool moe_layer = false) {
 }
 inline int rp_reduce(lq_model* m, int64_t rows, bool moe_layer = false) {
     if (!split_out(m, moe_layer)) return LQ_OK;
+    if (m->ar_ok && rows <= lq::ALLREDUCE_ROWS)
+        return lq::launch_xchg_allreduce(m->ctx, m->ar, m->part, rows, m->c.hidden, m->x);
     return lq::comm_allreduce_sum_f32(m->comm, m->part, m->x, rows * m->c.hidden);
 }
 // greedy argmax over the vocabulary shards (dense TP): global indices, max over ranks
@@ -396,23 +402,29 @@ int lq_qwen3_destroy(lq_model* m) {
 static int tp_exchange_setup(lq_model* m, int64_t pb, bool* want) {
     lq_ctx* ctx = m->ctx;
     const int T = m->tp, rank = m->rank;
-    constexpr int W = 32;  // words per rank in the hand-over (128 bytes)
-    static_assert(sizeof(cudaIpcMemHandle_t) <= 27 * 4, "IPC handle does not fit the hand-over");
-    size_t fo = 0, ko = 0, so = 0;
+    constexpr int W = 48;  // words per rank in the hand-over: two IPC handles (16 words each), then metadata
+    static_assert(sizeof(cudaIpcMemHandle_t) <= 16 * 4, "IPC handle does not fit the hand-over");
+    size_t fo = 0, ko = 0, so = 0, afo = 0, ado = 0;
     const size_t bytes = lq::decode_persist_xchg_layout(m->c.hidden, T, ctx->sm_count, m->max_batch, &fo, &ko, &so);
+    const size_t abytes = lq::allreduce_layout(m->c.hidden, T, &afo, &ado);
     int rc = dalloc(m, &m->xchg[rank], bytes);
+    if (!rc) rc = dalloc(m, &m->ar.region[rank], abytes);
     if (rc) return rc;
     LQ_CUDA(ctx, cudaMemsetAsync(m->xchg[rank], 0, bytes, ctx->stream));
+    LQ_CUDA(ctx, cudaMemsetAsync(m->ar.region[rank], 0, abytes, ctx->stream));
     uint32_t mine[W] = {};
-    cudaIpcMemHandle_t h;
-    if (cudaIpcGetMemHandle(&h, m->xchg[rank]) != cudaSuccess) {
+    cudaIpcMemHandle_t h, ha;
+    bool ipc = true;
+    if (cudaIpcGetMemHandle(&h, m->xchg[rank]) != cudaSuccess || cudaIpcGetMemHandle(&ha, m->ar.region[rank]) != cudaSuccess) {
         cudaGetLastError();
-        *want = false;
+        ipc = false;
     }
     memcpy(mine, &h, sizeof h);
-    mine[28] = (uint32_t)pb;
-    mine[29] = (uint32_t)ctx->sm_count;
-    mine[30] = *want ? 1u : 0u;
+    memcpy(mine + 16, &ha, sizeof ha);
+    mine[40] = (uint32_t)pb;
+    mine[41] = (uint32_t)ctx->sm_count;
+    mine[42] = *want ? 1u : 0u;
+    mine[43] = ipc ? 1u : 0u;
     float* dev = nullptr;
     rc = dalloc(m, reinterpret_cast<void**>(&dev), (size_t)(T + 1) * W * 4);
     if (rc) return rc;
@@ -422,25 +434,29 @@ static int tp_exchange_setup(lq_model* m, int64_t pb, bool* want) {
     if (rc) return rc;
     LQ_CUDA(ctx, cudaMemcpyAsync(all.data(), dev + W, (size_t)T * W * 4, cudaMemcpyDeviceToHost, ctx->stream));
     LQ_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
-    bool ok = true;
+    bool ok = true;   // every rank can share its regions
+    bool pers = true;  // ... and takes the persistent step with the same batch and SM count
     for (int t = 0; t < T; t++) {
         const uint32_t* r = all.data() + (size_t)t * W;
-        ok = ok && r[28] == (uint32_t)pb && r[29] == (uint32_t)ctx->sm_count && r[30] == 1u;
+        ok = ok && r[43] == 1u;
+        pers = pers && r[40] == (uint32_t)pb && r[41] == (uint32_t)ctx->sm_count && r[42] == 1u;
     }
     for (int t = 0; t < T && ok; t++) {
         if (t == rank) continue;
-        cudaIpcMemHandle_t ph;
-        memcpy(&ph, all.data() + (size_t)t * W, sizeof ph);
-        void* p = nullptr;
-        if (cudaIpcOpenMemHandle(&p, ph, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
-            cudaGetLastError();
-            ok = false;
-            break;
+        for (int k = 0; k < 2 && ok; k++) {
+            cudaIpcMemHandle_t ph;
+            memcpy(&ph, all.data() + (size_t)t * W + 16 * k, sizeof ph);
+            void* p = nullptr;
+            if (cudaIpcOpenMemHandle(&p, ph, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                cudaGetLastError();
+                ok = false;
+                break;
+            }
+            m->ipc_open.push_back(p);
+            (k == 0 ? m->xchg[t] : m->ar.region[t]) = p;
         }
-        m->ipc_open.push_back(p);
-        m->xchg[t] = p;
     }
-    // every rank opened every peer's region, or none uses them
+    // every rank opened every peer's regions, or none uses them
     uint32_t flag[W] = {};
     flag[0] = ok ? 1u : 0u;
     LQ_CUDA(ctx, cudaMemcpyAsync(dev, flag, W * 4, cudaMemcpyHostToDevice, ctx->stream));
@@ -449,8 +465,11 @@ static int tp_exchange_setup(lq_model* m, int64_t pb, bool* want) {
     LQ_CUDA(ctx, cudaMemcpyAsync(all.data(), dev + W, (size_t)T * W * 4, cudaMemcpyDeviceToHost, ctx->stream));
     LQ_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
     for (int t = 0; t < T; t++) ok = ok && all[(size_t)t * W] == 1u;
-    *want = ok;
-    if (ok) m->keys = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(m->xchg[rank]) + ko);
+    *want = ok && pers;
+    if (*want) m->keys = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(m->xchg[rank]) + ko);
+    m->ar.tp = T;
+    m->ar.rank = rank;
+    m->ar_ok = ok && T <= lq::ALLREDUCE_MAX_TP && getenv("LQ_TP_NCCL") == nullptr;
     return LQ_OK;
 }
 
@@ -644,7 +663,8 @@ static int create_model(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, 
         int64_t pb = std::min<int64_t>(max_batch, pmax);
         while (pb > 0 && !lq::decode_persist_supported(ctx, pb, H, Hq, Hkv, I, ctx_max)) pb--;
         bool want = !moe && m->fused_decode && pb > 0 && (T == 1 || getenv("LQ_TP_NCCL") == nullptr);
-        if (!moe && T > 1) {
+        if (T > 8) want = false;
+        if (!moe && T > 1 && T <= 8) {
             // every rank must take the same path: agree on it, and share the exchange regions
             int xrc = tp_exchange_setup(m, pb, &want);
             if (xrc) {

@@ -289,17 +289,17 @@ def _tp32_rank_main(rank, world, port, q, prompts, fed, path):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("path", ["persistent", "nccl"])
+@pytest.mark.parametrize("path", ["persistent", "default", "nccl"])
 def test_tensor_parallel_32b_shapes_2_gpus(oracle, path):
     """Config 4's shapes (2 layers, full vocabulary) as two tensor-parallel ranks at batch 8:
     each rank holds 32 / 4 heads, 12800 intermediate rows, 75968 LM-head rows. "persistent"
     (LQ_PERSIST_MAX_BATCH=8): the persistent decode step with the o/down partial sums exchanged
-    inside the kernel over NVLink (a 3-kernel decode graph); "nccl": the per-layer kernels with
-    NCCL all-reduces (the default at batch 8). Both teacher-forced against the single-device
+    inside the kernel over NVLink (a 3-kernel decode graph); "default": the per-layer kernels with
+    the one-shot all-reduce over the ranks' CUDA-IPC regions; "nccl" (LQ_TP_NCCL=1): the
+    per-layer kernels with NCCL all-reduces. All teacher-forced against the single-device
     oracle with the tolerance of the headline-shape tests (the noise floor of these shapes;
     test_gpu_headline.py), tokens equal wherever the oracle's margin exceeds twice the step's
     difference."""
-    nccl_path = path == "nccl"
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -332,10 +332,10 @@ def test_tensor_parallel_32b_shapes_2_gpus(oracle, path):
     for r in res:
         assert "error" not in r, r
     r0 = next(r for r in res if r["rank"] == 0)
-    if nccl_path:
-        assert r0["kernels"] > 3  # per-layer kernels (the NCCL all-reduces are not kernel nodes)
-    else:
+    if path == "persistent":
         assert all(r["kernels"] == 3 for r in res), [r["kernels"] for r in res]
+    else:
+        assert r0["kernels"] > 3  # per-layer kernels
     for s in range(steps):
         for b in range(B):
             m = parity_metrics(r0["logits"][s, b], olgs[s, b])
