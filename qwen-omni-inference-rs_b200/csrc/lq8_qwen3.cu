@@ -394,6 +394,90 @@ int lq_qwen3_destroy(lq_model* m) {
     return LQ_OK;
 }
 
+// the persistent step's device descriptor: per layer the tensor maps of its four matrices, its
+// norm weights and its KV-cache slices (rewritten when the caches move)
+static int write_persist_desc(lq_model* m) {
+    const int64_t D = m->c.head_dim;
+    std::vector<lq::PdHostLayer> hl(m->layers.size());
+    const size_t kv_layer = (size_t)(m->max_batch * m->Hkv_l * m->ctx_max * D);
+    for (size_t l = 0; l < m->layers.size(); l++) {
+        const Layer& ly = m->layers[l];
+        hl[l] = {&ly.qkv, &ly.o, &ly.gate_up, &ly.down, ly.in_norm, ly.post_norm, ly.q_norm, ly.k_norm,
+                 m->kc + l * kv_layer, m->vc + l * kv_layer};
+    }
+    return lq::decode_persist_write_desc(m->ctx, m->pd_desc, hl.data(), m->c.layers, &m->lm_head);
+}
+
+// replace a tracked allocation (the old one is freed)
+static void swap_alloc(lq_model* m, void* old_p, void* new_p) {
+    for (auto& p : m->allocs)
+        if (p == old_p) p = new_p;
+    cudaFree(old_p);
+}
+
+// KvCache::append grows the reference's cache without a fixed limit (attention.rs:463-592):
+// when a prefill or decode step needs more than ctx_max positions, the caches (and the RoPE
+// tables, the generated-token history and the attention scratch, all sized by it) move to
+// buffers of max(need, 2 ctx_max) positions, up to max_pos and the attention's limit; the
+// positions written so far are copied, the decode graph is rebuilt at the next step and the
+// persistent step's descriptors are rewritten. Every rank of a tensor-parallel group grows at
+// the same call (they make the same calls).
+static int grow_context(lq_model* m, int64_t need) {
+    if (need <= m->ctx_max) return LQ_OK;
+    lq_ctx* ctx = m->ctx;
+    const lq_qwen3_config& c = m->c;
+    int64_t limit = lq::attention_max_ctx();
+    if (c.max_pos > 0) limit = std::min<int64_t>(limit, c.max_pos);
+    if (need > limit)
+        return lq::set_error(ctx, LQ_ERR_INVALID_ARG, "context of %lld positions exceeds the limit %lld (max_pos, "
+                             "attention chunks)", (long long)need, (long long)limit);
+    const int64_t old = m->ctx_max, nc = std::min(limit, std::max(need, 2 * old));
+    const int64_t D = c.head_dim, rows = c.layers * m->max_batch * m->Hkv_l;
+    const int64_t att_rows = std::max<int64_t>(m->max_batch, std::min<int64_t>(m->rows_cap, nc));
+    const size_t att_bytes = lq::attention_scratch_bytes(att_rows, m->Hq_l, nc, D);
+    LQ_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    void* nb[6] = {};
+    const size_t sizes[6] = {(size_t)(rows * nc * D) * 4, (size_t)(rows * nc * D) * 4, (size_t)(nc * D / 2) * 4,
+                             (size_t)(nc * D / 2) * 4, (size_t)(m->max_batch * nc) * 4, att_bytes};
+    for (int i = 0; i < 6; i++) {
+        const cudaError_t e = cudaMalloc(&nb[i], sizes[i]);
+        if (e != cudaSuccess) {
+            for (int j = 0; j < i; j++) cudaFree(nb[j]);
+            return lq::check_cuda(ctx, e, "cudaMalloc (growing the context)");
+        }
+    }
+    float *kc = (float*)nb[0], *vc = (float*)nb[1], *cs = (float*)nb[2], *sn = (float*)nb[3];
+    int32_t* gen = (int32_t*)nb[4];
+    const size_t ob = (size_t)(old * D) * 4, nbytes = (size_t)(nc * D) * 4;
+    LQ_CUDA(ctx, cudaMemcpy2DAsync(kc, nbytes, m->kc, ob, ob, (size_t)rows, cudaMemcpyDeviceToDevice, ctx->stream));
+    LQ_CUDA(ctx, cudaMemcpy2DAsync(vc, nbytes, m->vc, ob, ob, (size_t)rows, cudaMemcpyDeviceToDevice, ctx->stream));
+    LQ_CUDA(ctx, cudaMemcpy2DAsync(gen, (size_t)nc * 4, m->gen, (size_t)old * 4, (size_t)old * 4, (size_t)m->max_batch,
+                                   cudaMemcpyDeviceToDevice, ctx->stream));
+    LQ_CUDA(ctx, cudaMemsetAsync(nb[5], 0, att_bytes, ctx->stream));  // chunk counters start at zero
+    int rc = lq_rope_tables(ctx, D, nc, c.theta, cs, sn);
+    if (rc) return rc;
+    LQ_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    destroy_graph(m);
+    swap_alloc(m, m->kc, kc);
+    swap_alloc(m, m->vc, vc);
+    swap_alloc(m, m->cos_t, cs);
+    swap_alloc(m, m->sin_t, sn);
+    swap_alloc(m, m->gen, gen);
+    swap_alloc(m, m->att_scratch, nb[5]);
+    m->kc = kc;
+    m->vc = vc;
+    m->cos_t = cs;
+    m->sin_t = sn;
+    m->gen = gen;
+    m->att_scratch = nb[5];
+    m->att_scratch_bytes = att_bytes;
+    m->ctx_max = nc;
+    // the persistent step reads the caches through its descriptors (its attention takes the same
+    // context limit as the growth)
+    if (m->persist) return write_persist_desc(m);
+    return LQ_OK;
+}
+
 // Tensor parallelism, persistent decode step: allocate this rank's exchange region (zeroed),
 // then one all-gather of (CUDA IPC handle, persistent batch, SM count, willingness) over the
 // communicator; if every rank is willing with the same batch and SM count (the same units fall
@@ -673,18 +757,11 @@ static int create_model(lq_ctx* ctx, const lq_qwen3_config* cfg, uint64_t seed, 
             }
         }
         if (want) {
-            std::vector<lq::PdHostLayer> hl(m->layers.size());
-            const size_t kv_layer = (size_t)(max_batch * Hkv * ctx_max * D);
-            for (size_t l = 0; l < m->layers.size(); l++) {
-                const Layer& ly = m->layers[l];
-                hl[l] = {&ly.qkv, &ly.o, &ly.gate_up, &ly.down, ly.in_norm, ly.post_norm, ly.q_norm, ly.k_norm,
-                         m->kc + l * kv_layer, m->vc + l * kv_layer};
-            }
             int prc = dalloc(m, &m->pd_desc, lq::decode_persist_desc_bytes(c.layers));
             if (!prc) prc = dalloc(m, reinterpret_cast<void**>(&m->pd_part), lq::decode_persist_part_bytes(pb, Hq));
             if (!prc)
                 prc = dalloc(m, reinterpret_cast<void**>(&m->pd_counters), lq::decode_persist_counter_bytes(pb, Hkv, c.layers));
-            if (!prc) prc = lq::decode_persist_write_desc(ctx, m->pd_desc, hl.data(), c.layers, &m->lm_head);
+            if (!prc) prc = write_persist_desc(m);
             if (prc) {
                 lq_qwen3_destroy(m);
                 return prc;
@@ -742,8 +819,9 @@ int lq_qwen3_prefill(lq_model* m, const int32_t* ids, int64_t B, int64_t L, int3
     LQ_REQUIRE(ctx, ids && next, "lq_qwen3_prefill: NULL argument");
     LQ_REQUIRE(ctx, B > 0 && B <= m->max_batch && L > 0, "lq_qwen3_prefill: B=%lld (max %lld), L=%lld",
                (long long)B, (long long)m->max_batch, (long long)L);
-    LQ_REQUIRE(ctx, L <= m->ctx_max && L <= m->rows_cap, "lq_qwen3_prefill: L=%lld exceeds ctx_max %lld",
-               (long long)L, (long long)m->ctx_max);
+    LQ_REQUIRE(ctx, L <= m->rows_cap, "lq_qwen3_prefill: L=%lld exceeds the %lld rows of one pass", (long long)L,
+               (long long)m->rows_cap);
+    if (int rc = grow_context(m, L)) return rc;
     for (int64_t i = 0; i < B * L; i++)
         LQ_REQUIRE(ctx, ids[i] >= 0 && ids[i] < m->c.vocab, "lq_qwen3_prefill: token id %d out of range", ids[i]);
     // whole sequences per pass; the KV caches of sequence b live at batch slot b
@@ -794,7 +872,7 @@ int lq_qwen3_decode_step(lq_model* m, const int32_t* ids, int32_t* next, float* 
     LQ_ENTRY(ctx, "lq_qwen3_decode_step");
     LQ_REQUIRE(ctx, ids && next, "lq_qwen3_decode_step: NULL argument");
     const int64_t B = m->graph_batch ? m->graph_batch : m->max_batch;
-    LQ_REQUIRE(ctx, m->pos < m->ctx_max, "lq_qwen3_decode_step: context full (%lld)", (long long)m->ctx_max);
+    if (int rc = grow_context(m, m->pos + 1)) return rc;
     for (int64_t i = 0; i < B; i++)
         LQ_REQUIRE(ctx, ids[i] >= 0 && ids[i] < m->c.vocab, "lq_qwen3_decode_step: token id %d out of range", ids[i]);
     int rc = decode_prepare(m, B);
@@ -818,9 +896,8 @@ int lq_qwen3_decode_device(lq_model* m, int64_t n_steps) {
     lq_ctx* ctx = m->ctx;
     LQ_ENTRY(ctx, "lq_qwen3_decode_device");
     const int64_t B = m->graph_batch ? m->graph_batch : m->max_batch;
-    LQ_REQUIRE(ctx, n_steps >= 0 && m->pos + n_steps <= m->ctx_max,
-               "lq_qwen3_decode_device: %lld steps from position %lld exceed ctx_max %lld", (long long)n_steps,
-               (long long)m->pos, (long long)m->ctx_max);
+    LQ_REQUIRE(ctx, n_steps >= 0, "lq_qwen3_decode_device: n_steps=%lld", (long long)n_steps);
+    if (int rc = grow_context(m, m->pos + n_steps)) return rc;
     int rc = decode_prepare(m, B);
     if (rc) return rc;
     for (int64_t s = 0; s < n_steps; s++) LQ_CUDA(ctx, cudaGraphLaunch(m->exec, ctx->stream));

@@ -203,12 +203,47 @@ def test_fused_decode_equals_separate_kernels(ctx, lq8_lib, oracle, monkeypatch,
     assert np.array_equal(outs[0], outs[1])
 
 
-def test_decode_past_context_is_an_error(ctx, lq8_lib, oracle):
-    gm, ocfg = _models(lq8_lib, oracle, ctx, 5, TINY, ctx_max=8)
+@pytest.mark.parametrize("B", [1, 3])
+def test_context_grows_past_ctx_max(ctx, lq8_lib, oracle, B):
+    """The reference's KvCache grows without a fixed limit (attention.rs:463-592): a model created
+    for 8 positions decodes 60 steps past them (the caches, RoPE tables, history and attention
+    scratch move to 16, 32, 64, 128 positions; the decode graph and the persistent step's
+    descriptors follow) with logits bit-identical, step by step, to a model created for 128
+    positions; device-side steps grow it too."""
+    prompts = np.stack([oracle.gen_tokens(5, s, 6, 1000) for s in range(B)])
+    small = lq8_lib.Qwen3ForCausalLM(ctx, lq8_lib.make_config(**TINY), 5, max_batch=B, ctx_max=8)
+    big = lq8_lib.Qwen3ForCausalLM(ctx, lq8_lib.make_config(**TINY), 5, max_batch=B, ctx_max=128)
+    try:
+        t1, l1 = small.prefill(prompts, want_logits=True)
+        t2, l2 = big.prefill(prompts, want_logits=True)
+        assert np.array_equal(l1, l2)
+        small.set_batch(B)
+        big.set_batch(B)
+        for i in range(60):
+            t1, l1 = small.decode_step(t1, want_logits=True)
+            t2, l2 = big.decode_step(t2, want_logits=True)
+            assert np.array_equal(l1, l2), i
+            assert np.array_equal(t1, t2), i
+        small.decode_device(30)
+        big.decode_device(30)
+        assert small.position() == big.position() == 6 + 90
+        ctx.synchronize()
+        buf1 = lq8_lib.wrap_device(small.token_buffer_ptr(), (B,), "<i4")
+        buf2 = lq8_lib.wrap_device(big.token_buffer_ptr(), (B,), "<i4")
+        assert H(buf1).tolist() == H(buf2).tolist()
+    finally:
+        small.close()
+        big.close()
+
+
+def test_context_beyond_max_pos_is_an_error(ctx, lq8_lib, oracle):
+    """Growth stops at max_pos (and the attention's limit): decoding past it is an error, as is a
+    prompt longer than one pass's rows."""
+    gm, ocfg = _models(lq8_lib, oracle, ctx, 5, dict(TINY, max_pos=10), ctx_max=8)
     prompt = oracle.gen_tokens(5, 0, 6, ocfg.vocab)
     nxt = gm.prefill(prompt)
-    nxt = gm.decode_step(nxt)
-    nxt = gm.decode_step(nxt)
+    for _ in range(4):
+        nxt = gm.decode_step(nxt)
     with pytest.raises(lq8_lib.LQ8Error):
         gm.decode_step(nxt)
     with pytest.raises(lq8_lib.LQ8Error):
