@@ -515,8 +515,9 @@ def finish(args, cfgd, world, rank, L, B, K, W, ms, value, e2e, ms_e2e, clk, lau
         dist.destroy_process_group()
 
 
-SWEEP_M = (1, 16, 128, 512, 2048)
-SWEEP_KN = ((1024, 3072), (3072, 1024), (4096, 12288), (12288, 4096), (5120, 25600))
+SWEEP_M = (1, 8, 16, 128, 512, 2048)
+SWEEP_KN = ((1024, 3072), (3072, 1024), (4096, 12288), (12288, 4096), (5120, 25600), (5120, 51200),
+            (25600, 5120))
 
 
 def run_sweep(args):

@@ -35,22 +35,24 @@ constexpr int ATT_MAX_KV = 64;
 // one scratch never overlap counters with another launch's partials.
 constexpr size_t ATT_COUNTER_BYTES = (size_t)ATT_SLICE * ATT_MAX_KV * 4;
 
+constexpr int ATT_CM_FLOATS = ATT_G * ATT_MAX_SPLITS;  // merge weights [G][ATT_MAX_SPLITS]
+
 struct AttSmem {
     float ks[ATT_C][ATT_KS];
     float vs[ATT_C][ATT_D];
     float qs[ATT_G][ATT_D];
     float ps[ATT_G][ATT_C];
     float ml[ATT_G][2];
-    float cm[ATT_G][ATT_MAX_SPLITS];  // combine: per-chunk weights exp(m_s - M)
     float cl[ATT_G];                  // combine: total denominator
     int last;
 };
 
-// The unfused variant (query rows from a q tensor: batched decode and short prefills) has its
-// own layout: q heads with the second half of the dims shifted by 4 floats (so that the two
-// halves of a warp read q with one broadcast wavefront), scores by position (so that P.V reads
-// a position's 8 probabilities with two broadcast loads). Its merge weights live in the last
-// 4 KiB of the V staging area, which keeps the struct small enough for three CTAs per SM.
+// The unfused variant (query rows from a q tensor: short prefills) has its own layout: q heads
+// with the second half of the dims shifted by 4 floats (so that the two halves of a warp read q
+// with one broadcast wavefront), scores by position (so that P.V reads a position's 8
+// probabilities with two broadcast loads). Both variants keep the merge weights
+// exp(m_s - M) in the last 4 KiB of the V staging area (free once the chunk's P.V is done),
+// which keeps each struct small enough for three CTAs per SM.
 struct AttSmemR {
     float ks[ATT_C][ATT_KS];
     float vs[ATT_C][ATT_D];
@@ -60,7 +62,6 @@ struct AttSmemR {
     float cl[ATT_G];
     int last;
 };
-constexpr int ATT_CM_FLOATS = ATT_G * ATT_MAX_SPLITS;
 
 struct AttParams {
     const float* q;        // [B][Hq][L][D] (unfused)
@@ -101,7 +102,7 @@ __device__ __forceinline__ void quant_warp32(float v, int lane, int8_t* q_out, u
     if (lane == 0) *d_out = f2h(d);
 }
 
-__device__ __forceinline__ float* att_cm(AttSmem& S) { return &S.cm[0][0]; }
+__device__ __forceinline__ float* att_cm(AttSmem& S) { return &S.vs[0][0] + ATT_C * ATT_D - ATT_CM_FLOATS; }
 __device__ __forceinline__ float* att_cm(AttSmemR& S) { return &S.vs[0][0] + ATT_C * ATT_D - ATT_CM_FLOATS; }
 
 // Unfused chunk: scores (thread -> position tid/2 and one 64-dim half, all GN heads; the halves
@@ -356,7 +357,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const AttParams
     float* po = &S.ks[0][0];
     float* cm = att_cm(S);  // [G][ATT_MAX_SPLITS]
     const size_t head_floats = (size_t)n_active * ATT_D;
-    const bool staged = 2 * head_floats * 4 <= sizeof(S.ks) + sizeof(S.vs) - (FUSED ? 0 : ATT_CM_FLOATS * 4);
+    const bool staged = 2 * head_floats * 4 <= sizeof(S.ks) + sizeof(S.vs) - ATT_CM_FLOATS * 4;
     auto stage_head = [&](int g) {
         float* dst = po + (size_t)(g & 1) * head_floats;
         for (int i = tid; i < n_active * (ATT_D / 4); i += ATT_THREADS) {

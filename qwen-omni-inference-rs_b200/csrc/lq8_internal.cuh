@@ -13,6 +13,8 @@
 // ------------------------------------------------------------------------------------------
 // context
 // ------------------------------------------------------------------------------------------
+constexpr int kTileCounters = 1024;
+
 struct lq_ctx {
     int device = 0;
     int sm_count = 0;
@@ -28,6 +30,9 @@ struct lq_ctx {
     void* split = nullptr;
     size_t split_bytes = 0;
     int* err_flag = nullptr;      // device int[4]: kernels report bad inputs here
+    // device unsigned[kTileCounters], zero between launches: arrivals of the CTAs that share a
+    // GEMM tile (the skinny GEMM's stream-K combine; the last CTA resets its counter)
+    unsigned* tile_cnt = nullptr;
     // launch kernels with programmatic stream serialization (PDL): every kernel of the library
     // calls pdl_wait() before it touches data written by earlier kernels
     bool pdl = true;

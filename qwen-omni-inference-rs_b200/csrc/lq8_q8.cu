@@ -472,6 +472,8 @@ static int split_slice(int64_t K, int splits) {
 
 // mirrors run_gemm's choice (128-row tiles; 16/32/64-token tiles for m <= 64)
 static int gs_slices(lq_ctx* ctx, int64_t n, int64_t k, int64_t m);
+// the skinny (5-8 token) GEMM's partial buffer for an (n, k) weight (0 if it does not apply)
+static size_t sk_partial_bytes(lq_ctx* ctx, int64_t n, int64_t k);
 
 size_t gemm_split_bytes(lq_ctx* ctx, int64_t n, int64_t k, int64_t m) {
     if (m <= 4 || m > 64) return 0;
@@ -483,6 +485,8 @@ size_t gemm_split_bytes(lq_ctx* ctx, int64_t n, int64_t k, int64_t m) {
         const int64_t chunks = k / 256, ks = ((chunks + s0 - 1) / s0) * 256;
         if (s0 > 1) gs = (size_t)((k + ks - 1) / ks) * m * n * 4;
     }
+    // the skinny GEMM's partial buffer (its alignment too is checked per call)
+    if (m <= 8) gs = std::max(gs, sk_partial_bytes(ctx, n, k));
     const int64_t bx = m <= 16 ? 16 : m <= 32 ? 32 : 64;
     const int splits0 = gemm_splits(ctx, (int64_t)ceil_div(n, 128) * ceil_div(m, bx), k, m);
     if (splits0 <= 1) return gs;
@@ -884,6 +888,331 @@ static int launch_gemm_stream(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* 
                            : launch_gemm_stream_t<32>(ctx, w, xq, xd, m, y, resid, ldy, keys, fixed);
 }
 
+// =========================================================================================
+// Skinny Q8_0 GEMM (5 <= m <= 8 tokens: decode batches), one CTA per SM, stream-K.
+// A tile is 128 weight rows; a unit is one 256-byte K chunk of a tile (8 Q8_0 blocks). The
+// tiles' units, in tile-major order, are dealt to the CTAs in equal contiguous ranges, so every
+// SM streams the same number of weight bytes whatever the shape. One producer lane loads per
+// unit the tile's two 128-byte column boxes (128 rows each, 128-byte swizzle), their fp16
+// scales, the m token rows (8-row boxes; rows past m read as zeros) and the tokens' scales into
+// a 6-stage ring of 37 KiB. Eight consumer warps each own 16 rows of the tile and all 8 tokens:
+// one m16n8k32 MMA per Q8_0 block, its int32 dots turned into floats by the 1.5*2^23 bias the
+// MMA accumulates onto, then scaled and added per (row, token) in ascending block order with
+// separately rounded multiply and add (the oracle's order). A tile whose units all fall to one
+// CTA is written directly: bit-identical to the oracle. A tile cut between CTAs leaves one
+// partial sum per CTA in the partial buffer; the CTA that arrives last (a per-tile counter,
+// indexed by the tile's first CTA and reset by that last CTA) adds them in CTA order and writes
+// the tile, so the result is deterministic and within the regrouping bound. No CTA waits for
+// another. LQ_GEMM_NO_SPLIT=1 deals whole tiles instead.
+// =========================================================================================
+constexpr int SK_ROWS = 128;
+constexpr int SK_KC = 256;
+constexpr int SK_CONS = 8;
+constexpr int SK_THREADS = (SK_CONS + 1) * 32;
+constexpr int SK_STAGES = 6;
+constexpr int SK_WBOX = SK_ROWS * 128;                 // 128 rows x 128 bytes
+constexpr int SK_XBOX = 8 * 128;                       // 8 token rows x 128 bytes
+constexpr int SK_OFF_X = 2 * SK_WBOX;
+constexpr int SK_OFF_WD = SK_OFF_X + 2 * SK_XBOX;      // weight scales [128][8] fp16
+constexpr int SK_OFF_XD = SK_OFF_WD + SK_ROWS * 16;    // token scales [8][8] fp16
+constexpr int SK_BYTES = SK_OFF_XD + 8 * 16;           // bytes landing per stage
+constexpr int SK_STAGE = (SK_BYTES + 1023) / 1024 * 1024;
+constexpr size_t SK_SMEM = (size_t)SK_STAGES * SK_STAGE + 1024 + 256;
+static_assert(SK_SMEM <= 227 * 1024, "skinny GEMM ring exceeds the shared memory of one CTA");
+static_assert(SK_OFF_X % 1024 == 0 && SK_XBOX % 1024 == 0, "swizzled boxes need 1024-byte alignment");
+
+struct SkParams {
+    int N, K, M;
+    int tiles, chunks;            // 128-row tiles; 256-byte units per tile
+    int whole;                    // 1: whole tiles per CTA (no split)
+    long long units;              // tiles * chunks
+    const float* resid;
+    float* y;
+    int ldy;
+    float4* part;                 // [grid][2 slots][256 consumer threads] partial sums
+    unsigned* cnt;                // [grid] arrivals at the tile that starts in that CTA
+    unsigned long long* keys;     // fused greedy argmax per token
+    int* err;
+};
+
+// first unit of CTA b
+__device__ __forceinline__ long long sk_start(const SkParams& p, int b) {
+    const long long G = gridDim.x;
+    return p.whole ? (long long)p.tiles * b / G * p.chunks : p.units * b / G;
+}
+// the CTA whose range holds unit u (split mode)
+__device__ __forceinline__ int sk_owner(const SkParams& p, long long u) {
+    return (int)(((u + 1) * (long long)gridDim.x - 1) / p.units);
+}
+
+__global__ void __launch_bounds__(SK_THREADS, 1) q8_gemm_skinny_kernel(const __grid_constant__ CUtensorMap mw,
+                                                                       const __grid_constant__ CUtensorMap mwd,
+                                                                       const __grid_constant__ CUtensorMap mx,
+                                                                       const __grid_constant__ CUtensorMap mxd,
+                                                                       const SkParams p) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    const uint32_t raw = smem_addr(smem_raw);
+    uint8_t* sm = smem_raw + (((raw + 1023) & ~1023u) - raw);
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + (size_t)SK_STAGES * SK_STAGE);
+    uint64_t* empty = full + SK_STAGES;
+    unsigned long long* ckeys = reinterpret_cast<unsigned long long*>(empty + SK_STAGES);  // [8]
+    int* last_flag = reinterpret_cast<int*>(ckeys + 8);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < SK_STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], SK_CONS);
+        }
+        mbar_fence_init();
+    }
+    if (threadIdx.x < 8) ckeys[threadIdx.x] = 0ull;
+    __syncthreads();
+    const int b = blockIdx.x;
+    const long long u0 = sk_start(p, b), u1 = b + 1 == (int)gridDim.x ? p.units : sk_start(p, b + 1);
+
+    if (warp == SK_CONS) {
+        // ---------------- producer (one lane); weights may stream before pdl_wait ----------------
+        if (lane != 0) return;
+        int s = 0;
+        unsigned ph = 0;
+        bool waited = false;
+        for (long long u = u0; u < u1;) {
+            const int t = (int)(u / p.chunks);
+            const long long ts = (long long)t * p.chunks;
+            const long long e = min(u1, ts + p.chunks);
+            const int row = t * SK_ROWS;
+            for (int c = (int)(u - ts); c < (int)(e - ts); c++) {
+                if (!mbar_wait(&empty[s], ph ^ 1u)) {
+                    atomicCAS(p.err, 0, 26);
+                    return;
+                }
+                uint8_t* st = sm + (size_t)s * SK_STAGE;
+                const int k = c * SK_KC;
+                mbar_expect_tx(&full[s], (unsigned)SK_BYTES);
+                tma_load_2d(st, &mw, k, row, &full[s]);
+                tma_load_2d(st + SK_WBOX, &mw, k + 128, row, &full[s]);
+                tma_load_2d(st + SK_OFF_WD, &mwd, k / 32, row, &full[s]);
+                if (!waited) {  // the activations come from the preceding kernel
+                    pdl_wait();
+                    waited = true;
+                }
+                tma_load_2d(st + SK_OFF_X, &mx, k, 0, &full[s]);
+                tma_load_2d(st + SK_OFF_X + SK_XBOX, &mx, k + 128, 0, &full[s]);
+                tma_load_2d(st + SK_OFF_XD, &mxd, k / 32, 0, &full[s]);
+                if (++s == SK_STAGES) {
+                    s = 0;
+                    ph ^= 1u;
+                }
+            }
+            u = e;
+        }
+        return;
+    }
+    // ---------------- consumers ----------------
+    pdl_wait();  // resid / y / keys / the partial buffer and counters belong to preceding kernels
+    pdl_trigger();
+    const int g = lane >> 2, t4 = lane & 3, tid = threadIdx.x;
+    const int ra = 16 * warp + g;                        // rows ra and ra + 8 of the tile
+    const int a_off = ra * 128 + (t4 & 1) * 8;
+    const int b_off = SK_OFF_X + g * 128 + (t4 & 1) * 8;
+    const int sc_off = SK_OFF_WD + ra * 16;
+    const int xd_off = SK_OFF_XD + 2 * t4 * 16;
+    int s = 0;
+    unsigned ph = 0;
+    bool bad = false;
+    bool first_seg = true;
+    for (long long u = u0; u < u1; first_seg = false) {
+        const int t = (int)(u / p.chunks);
+        const long long ts = (long long)t * p.chunks;
+        const long long e = min(u1, ts + p.chunks);
+        const int c0 = (int)(u - ts), c1 = (int)(e - ts);
+        u = e;
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int c = c0; c < c1; c++) {
+            const int cs = s;
+            const unsigned cph = ph;
+            if (++s == SK_STAGES) {
+                s = 0;
+                ph ^= 1u;
+            }
+            if (bad) continue;
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait(&full[cs], cph);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) {
+                if (lane == 0) atomicCAS(p.err, 0, 27);
+                bad = true;
+                continue;
+            }
+            const uint8_t* st = sm + (size_t)cs * SK_STAGE;
+            // the warp's whole slice of the stage into registers, then the stage is released
+            uint2 wa[8], wb[8], xv[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int ch = ((2 * (j & 3) + (t4 >> 1)) ^ g) << 4;
+                wa[j] = *reinterpret_cast<const uint2*>(st + (j >> 2) * SK_WBOX + a_off + ch);
+                wb[j] = *reinterpret_cast<const uint2*>(st + (j >> 2) * SK_WBOX + a_off + 8 * 128 + ch);
+                xv[j] = *reinterpret_cast<const uint2*>(st + b_off + (j >> 2) * SK_XBOX + ch);
+            }
+            const uint4 sa = *reinterpret_cast<const uint4*>(st + sc_off);
+            const uint4 sb = *reinterpret_cast<const uint4*>(st + sc_off + 8 * 16);
+            const uint4 ua = *reinterpret_cast<const uint4*>(st + xd_off);
+            const uint4 ub = *reinterpret_cast<const uint4*>(st + xd_off + 16);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[cs]);
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const uint32_t a[4] = {wa[j].x, wb[j].x, wa[j].y, wb[j].y};
+                const uint32_t bb[2] = {xv[j].x, xv[j].y};
+                int d[4];
+                mma_s8_bias(d, a, bb, 0x4B400000);
+                const uint32_t wsa = j < 2 ? sa.x : j < 4 ? sa.y : j < 6 ? sa.z : sa.w;
+                const uint32_t wsb = j < 2 ? sb.x : j < 4 ? sb.y : j < 6 ? sb.z : sb.w;
+                const uint32_t wx0 = j < 2 ? ua.x : j < 4 ? ua.y : j < 6 ? ua.z : ua.w;
+                const uint32_t wx1 = j < 2 ? ub.x : j < 4 ? ub.y : j < 6 ? ub.z : ub.w;
+                const int sh = (j & 1) * 16;
+                const float dwa = h2f((uint16_t)(wsa >> sh)), dwb = h2f((uint16_t)(wsb >> sh));
+                const float dx0 = h2f((uint16_t)(wx0 >> sh)), dx1 = h2f((uint16_t)(wx1 >> sh));
+                // the MMA added the dots to 1.5 * 2^23: one subtraction gives (float)dot exactly
+                const float f0 = __fsub_rn(__int_as_float(d[0]), 12582912.0f);
+                const float f1 = __fsub_rn(__int_as_float(d[1]), 12582912.0f);
+                const float f2 = __fsub_rn(__int_as_float(d[2]), 12582912.0f);
+                const float f3 = __fsub_rn(__int_as_float(d[3]), 12582912.0f);
+                acc[0] = __fadd_rn(acc[0], __fmul_rn(f0, __fmul_rn(dwa, dx0)));
+                acc[1] = __fadd_rn(acc[1], __fmul_rn(f1, __fmul_rn(dwa, dx1)));
+                acc[2] = __fadd_rn(acc[2], __fmul_rn(f2, __fmul_rn(dwb, dx0)));
+                acc[3] = __fadd_rn(acc[3], __fmul_rn(f3, __fmul_rn(dwb, dx1)));
+            }
+        }
+        // ---- segment end: a whole tile is written; a cut tile goes through the partial buffer ----
+        float v[4] = {acc[0], acc[1], acc[2], acc[3]};
+        if (!(c0 == 0 && c1 == p.chunks)) {
+            const int slot = first_seg ? 0 : 1;
+            __stcg(p.part + ((size_t)b * 2 + slot) * (SK_CONS * 32) + tid, make_float4(v[0], v[1], v[2], v[3]));
+            __threadfence();
+            asm volatile("bar.sync 1, %0;" ::"n"(SK_CONS * 32));
+            const int bf = sk_owner(p, ts), bl = sk_owner(p, ts + p.chunks - 1);
+            if (tid == 0) {
+                const unsigned old = atomicAdd(&p.cnt[bf], 1u);
+                const int last = old == (unsigned)(bl - bf);
+                if (last) p.cnt[bf] = 0u;  // every CTA of the tile has arrived: ready for the next launch
+                *last_flag = last;
+            }
+            asm volatile("bar.sync 1, %0;" ::"n"(SK_CONS * 32));
+            if (!*last_flag) continue;
+            __threadfence();
+            for (int q = bf; q <= bl; q++) {
+                // the tile is the last range piece of its first CTA (slot 1 if that CTA began in
+                // an earlier tile) and the first piece of every later CTA (slot 0)
+                const int sl = (q == bf && sk_start(p, q) < ts) ? 1 : 0;
+                float4 o;
+                if (q == b) {
+                    o = make_float4(acc[0], acc[1], acc[2], acc[3]);
+                } else {
+                    o = __ldcg(p.part + ((size_t)q * 2 + sl) * (SK_CONS * 32) + tid);
+                }
+                if (q == bf) {
+                    v[0] = o.x, v[1] = o.y, v[2] = o.z, v[3] = o.w;
+                } else {
+                    v[0] = __fadd_rn(v[0], o.x), v[1] = __fadd_rn(v[1], o.y);
+                    v[2] = __fadd_rn(v[2], o.z), v[3] = __fadd_rn(v[3], o.w);
+                }
+            }
+        }
+        if (bad) continue;
+        // value i: row ra + 8 (i >> 1) of tile t, token 2 t4 + (i & 1)
+        unsigned long long kk[2] = {0ull, 0ull};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int tk = 2 * t4 + (i & 1);
+            const int row = t * SK_ROWS + ra + 8 * (i >> 1);
+            if (tk < p.M && row < p.N) {
+                const size_t o = (size_t)tk * p.ldy + row;
+                float val = v[i];
+                if (p.resid) val = __fadd_rn(p.resid[o], val);
+                p.y[o] = val;
+                if (p.keys) {
+                    const unsigned long long key = argmax_key(val, row);
+                    kk[i & 1] = key > kk[i & 1] ? key : kk[i & 1];
+                }
+            }
+        }
+        if (p.keys) {
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                unsigned long long key = kk[h];
+#pragma unroll
+                for (int o = 4; o < 32; o <<= 1) {
+                    const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+                    key = other > key ? other : key;
+                }
+                if (g == 0 && key) atomicMax(&ckeys[2 * t4 + h], key);
+            }
+        }
+    }
+    if (p.keys) {
+        asm volatile("bar.sync 1, %0;" ::"n"(SK_CONS * 32));
+        if (tid < p.M && ckeys[tid]) atomicMax(p.keys + tid, ckeys[tid]);
+    }
+}
+
+static bool sk_supported(const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd, int64_t m) {
+    return m >= 5 && m <= 8 && w->k % SK_KC == 0 && w->n % 64 == 0 && w->n < (1ll << 31) &&
+           ((uintptr_t)w->qs % 16) == 0 && ((uintptr_t)w->d % 16) == 0 && ((uintptr_t)xq % 16) == 0 &&
+           ((uintptr_t)xd % 16) == 0 && !getenv("LQ_NO_GEMM_SKINNY");
+}
+
+// CTAs of the skinny GEMM: one per SM, never more than the units (or tiles, unsplit)
+static int sk_grid(lq_ctx* ctx, int64_t n, int64_t k, bool whole) {
+    const int64_t tiles = (n + SK_ROWS - 1) / SK_ROWS, units = tiles * (k / SK_KC);
+    return (int)std::min<int64_t>(std::min<int64_t>(ctx->sm_count, kTileCounters), whole ? tiles : units);
+}
+
+static size_t sk_partial_bytes(lq_ctx* ctx, int64_t n, int64_t k) {
+    if (k % SK_KC != 0 || n % 64 != 0) return 0;
+    return (size_t)sk_grid(ctx, n, k, false) * 2 * SK_CONS * 32 * sizeof(float4);
+}
+
+static int launch_gemm_skinny(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd, int64_t m,
+                              float* y, const float* resid, int64_t ldy, unsigned long long* keys,
+                              const SplitBuf* fixed) {
+    SkParams p = {};
+    p.N = (int)w->n;
+    p.K = (int)w->k;
+    p.M = (int)m;
+    p.tiles = (int)((w->n + SK_ROWS - 1) / SK_ROWS);
+    p.chunks = (int)(w->k / SK_KC);
+    p.units = (long long)p.tiles * p.chunks;
+    p.whole = getenv("LQ_GEMM_NO_SPLIT") ? 1 : 0;
+    const int grid = sk_grid(ctx, w->n, w->k, p.whole != 0);
+    p.resid = resid;
+    p.y = y;
+    p.ldy = (int)ldy;
+    p.keys = keys;
+    p.cnt = ctx->tile_cnt;
+    p.err = ctx->err_flag;
+    float* part = nullptr;
+    int rc = split_partials(ctx, fixed, (size_t)grid * 2 * SK_CONS * 32 * sizeof(float4), &part);
+    if (rc) return rc;
+    p.part = reinterpret_cast<float4*>(part);
+    CUtensorMap mw, mwd, mx, mxd;
+    rc = make_tensor_map_2d(ctx, &mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->qs, (uint64_t)w->k, (uint64_t)w->n,
+                            (uint64_t)w->k, 128, SK_ROWS, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!rc)
+        rc = make_tensor_map_2d(ctx, &mwd, CU_TENSOR_MAP_DATA_TYPE_UINT16, w->d, (uint64_t)(w->k / 32),
+                                (uint64_t)w->n, (uint64_t)(w->k / 32) * 2, 8, SK_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (!rc)
+        rc = make_tensor_map_2d(ctx, &mx, CU_TENSOR_MAP_DATA_TYPE_UINT8, xq, (uint64_t)w->k, (uint64_t)m,
+                                (uint64_t)w->k, 128, 8, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!rc)
+        rc = make_tensor_map_2d(ctx, &mxd, CU_TENSOR_MAP_DATA_TYPE_UINT16, xd, (uint64_t)(w->k / 32), (uint64_t)m,
+                                (uint64_t)(w->k / 32) * 2, 8, 8, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    if ((rc = ensure_func_smem(ctx, (const void*)q8_gemm_skinny_kernel, SK_SMEM))) return rc;
+    return launch_kernel(ctx, q8_gemm_skinny_kernel, dim3(grid), dim3(SK_THREADS), SK_SMEM, "q8_gemm_skinny", mw,
+                         mwd, mx, mxd, p);
+}
+
 int launch_q8_matmul(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd,
                      int64_t m, float* y, const float* resid, int64_t ldy,
                      unsigned long long* keys, const SplitBuf* split) {
@@ -900,6 +1229,7 @@ int launch_q8_matmul(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const
     }
     if (!keys && m > 64 && gemm_tc_supported(m, w->k, w->qs, xq, w->d, xd))
         return launch_gemm_tc(ctx, w, xq, xd, m, y, resid, ldy);
+    if (sk_supported(w, xq, xd, m)) return launch_gemm_skinny(ctx, w, xq, xd, m, y, resid, ldy, keys, split);
     if (gs_supported(w, xq, xd, m)) return launch_gemm_stream(ctx, w, xq, xd, m, y, resid, ldy, keys, split);
     if (m <= 16) return run_gemm<128, 16, 8, 1>(ctx, w, xq, xd, m, y, resid, ldy, keys, split);
     if (m <= 32) return run_gemm<128, 32, 8, 1>(ctx, w, xq, xd, m, y, resid, ldy, keys, split);

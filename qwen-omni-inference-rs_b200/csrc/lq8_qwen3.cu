@@ -298,6 +298,11 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
         RC(finish_tokens(m, B, pos_dev, bump_pos));
         return LQ_OK;
     }
+    // decode steps with a device position (graph replays) of more rows than the fused GEMV path
+    // takes: the separate q/k-norm + RoPE + KV append, chunk and merge kernels; LQ_ATT_FUSED=1
+    // takes the fused attention kernel instead (one launch, its last chunk CTA merging; slower
+    // at 32B batch 8 today: 11.31 against 11.21 ms per step)
+    const bool fused_att = L == 1 && pos_dev && m->fused_decode && B <= 256 && getenv("LQ_ATT_FUSED") != nullptr;
     for (size_t li = 0; li < m->layers.size(); li++) {
         Layer& ly = m->layers[li];
         float* kc = m->kc + li * kv_layer;
@@ -306,6 +311,12 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
         RC(lq::launch_rmsnorm(ctx, m->x, LQ_DTYPE_F32, rows, H, ly.in_norm, c.eps, nullptr, m->xq, m->xd));
         // fused q/k/v projection
         RC(lq::launch_q8_matmul(ctx, &ly.qkv, m->xq, m->xd, rows, m->qkv, nullptr, m->Nqkv, nullptr));
+        if (fused_att) {
+            // batched decode: q/k norm, RoPE, KV append, attention and the chunk merge -> Q8_0
+            // rows in one kernel (the chunks' last CTA merges)
+            RC(lq::launch_attention_decode_fused(ctx, m->qkv, ly.q_norm, ly.k_norm, c.eps, m->cos_t, m->sin_t, kc,
+                                                 vc, B, Hq, Hkv, pos_dev, m->ctx_max, m->xq, m->xd, m->att_scratch));
+        } else {
         RC(lq::launch_qk_norm_rope_kv(ctx, m->qkv, B, L, Hq, Hkv, D, ly.q_norm, ly.k_norm, c.eps, m->cos_t,
                                       m->sin_t, pos0, pos_dev, m->q_rot, kc, vc, m->ctx_max));
         // attention -> Q8_0 rows [rows][Hq*D]
@@ -320,6 +331,7 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
                                         D, nullptr, m->xq + b * L * m->Hqd, m->xd + b * L * (m->Hqd / 32),
                                         m->att_scratch, false));
             }
+        }
         }
         // o_proj + residual (transformer.rs:194)
         RC(lq::launch_q8_matmul(ctx, &ly.o, m->xq, m->xd, rows, rp_out(m), rp_resid(m), H, nullptr));

@@ -101,6 +101,8 @@ int consume_device_error(lq_ctx* ctx, const char* what) {
     LQ_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
     if (h[0] != 0) {
         LQ_CUDA(ctx, cudaMemsetAsync(ctx->err_flag, 0, sizeof h, ctx->stream));
+        // a kernel that gave up may have left tile counters mid-count
+        LQ_CUDA(ctx, cudaMemsetAsync(ctx->tile_cnt, 0, kTileCounters * sizeof(unsigned), ctx->stream));
         return set_error(ctx, LQ_ERR_INVALID_ARG, "%s: device check failed (code %d, value %d)",
                          what, h[0], h[1]);
     }
@@ -141,7 +143,12 @@ int lq_init(int device, lq_ctx** out) {
     c->sm_count = prop.multiProcessorCount;
     if (cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaMalloc(&c->err_flag, 4 * sizeof(int)) != cudaSuccess ||
-        cudaMemset(c->err_flag, 0, 4 * sizeof(int)) != cudaSuccess) {
+        cudaMemset(c->err_flag, 0, 4 * sizeof(int)) != cudaSuccess ||
+        cudaMalloc(&c->tile_cnt, kTileCounters * sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(c->tile_cnt, 0, kTileCounters * sizeof(unsigned)) != cudaSuccess) {
+        if (c->err_flag) cudaFree(c->err_flag);
+        if (c->tile_cnt) cudaFree(c->tile_cnt);
+        if (c->own_stream) cudaStreamDestroy(c->own_stream);
         delete c;
         return lq::set_error(nullptr, LQ_ERR_CUDA, "lq_init: stream/flag allocation failed");
     }
@@ -159,6 +166,7 @@ int lq_destroy(lq_ctx* ctx) {
     if (ctx->scratch) cudaFree(ctx->scratch);
     if (ctx->split) cudaFree(ctx->split);
     if (ctx->err_flag) cudaFree(ctx->err_flag);
+    if (ctx->tile_cnt) cudaFree(ctx->tile_cnt);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
     return LQ_OK;

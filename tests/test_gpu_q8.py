@@ -111,7 +111,7 @@ def test_gemv_within_reorder_bound(ctx, lq8_lib, oracle, rng, m, n, k):
     assert np.all(np.abs(y - ref) <= bound), float(np.max(np.abs(y - ref) / bound))
 
 
-@pytest.mark.parametrize("m", [5, 16, 17, 33, 64, 100, 257])
+@pytest.mark.parametrize("m", [5, 8, 16, 17, 33, 64, 100, 257])
 @pytest.mark.parametrize("n,k", [(1, 32), (17, 96), (300, 1024), (640, 3072)])
 def test_gemm_bit_exact(ctx, lq8_lib, oracle, rng, monkeypatch, m, n, k):
     """Without the K split (LQ_GEMM_NO_SPLIT=1) every GEMM output is one thread's sum in the
@@ -135,6 +135,38 @@ def test_gemm_small_m_split_within_reorder_bound(ctx, lq8_lib, oracle, rng, m, n
     bound = 2.0 * (k // 32 + 1) * 2.0 ** -24 * absum + 1e-30
     assert np.all(np.abs(y - ref) <= bound), float(np.max(np.abs(y - ref) / bound))
     assert np.array_equal(y, _matmul(ctx, lq8_lib, wq, wd, xq, xd))  # deterministic
+
+
+@pytest.mark.parametrize("m,n,k", [(5, 320, 2048), (6, 1280, 5120), (7, 64, 256), (8, 320, 2048), (8, 1280, 5120),
+                                   (8, 5120, 25600), (5, 10240, 5120), (8, 10240, 5120), (7, 3200, 5120)])
+def test_gemm_skinny_stream_k_within_reorder_bound(ctx, lq8_lib, oracle, rng, m, n, k):
+    """The 5-8-token GEMM deals 256-byte K units of 128-row tiles evenly over one CTA per SM,
+    so tiles are cut between CTAs at arbitrary units (the decode shapes of Qwen3-32B and its
+    tensor-parallel shards here); the last CTA of a cut tile adds the pieces in CTA order.
+    Every output is written (NaN-filled y), within the regrouping bound, and deterministic."""
+    wq, wd = _weights(oracle, rng, n, k)
+    xq, xd = oracle.q8_0_quantize(rng.standard_normal((m, k)).astype(np.float32))
+    y = _matmul(ctx, lq8_lib, wq, wd, xq, xd)
+    assert not np.isnan(y).any()
+    ref, absum = oracle.q8_0_matmul(xq, xd, wq, wd, with_abs=True)
+    bound = 2.0 * (k // 32 + 1) * 2.0 ** -24 * absum + 1e-30
+    assert np.all(np.abs(y - ref) <= bound), float(np.max(np.abs(y - ref) / bound))
+    assert np.array_equal(y, _matmul(ctx, lq8_lib, wq, wd, xq, xd))
+
+
+def test_gemm_skinny_counters_reset_between_launches(ctx, lq8_lib, oracle, rng):
+    """The per-tile arrival counters of the stream-K combine are reset by each tile's last CTA:
+    shapes with different cut points launched in turn, three rounds, give the same bits every
+    round (a counter left mid-count would skip or double a combine)."""
+    cases = []
+    for n, k in [(1280, 5120), (5120, 25600), (640, 3072), (10240, 5120)]:
+        wq, wd = _weights(oracle, rng, n, k)
+        xq, xd = oracle.q8_0_quantize(rng.standard_normal((8, k)).astype(np.float32))
+        cases.append((wq, wd, xq, xd))
+    first = [_matmul(ctx, lq8_lib, *c) for c in cases]
+    for _ in range(2):
+        for c, y0 in zip(cases, first):
+            assert np.array_equal(_matmul(ctx, lq8_lib, *c), y0)
 
 
 @pytest.mark.parametrize("m", [65, 127, 128, 300, 513])
@@ -195,10 +227,11 @@ def test_matmul_residual_and_stride(ctx, lq8_lib, oracle, rng, monkeypatch, m):
         assert np.array_equal(y[:, :n], (resid[:, :n] + ref).astype(np.float32))
 
 
-@pytest.mark.parametrize("m", [5, 16, 23, 40, 64])
+@pytest.mark.parametrize("m", [5, 8, 16, 23, 40, 64])
 @pytest.mark.parametrize("split", [False, True])
 def test_gemm_stream_residual_and_stride(ctx, lq8_lib, oracle, rng, monkeypatch, m, split):
-    """The streamed small-M GEMM (5 <= m <= 64, n % 64 == 0, k % 256 == 0): passes of 16 or 32
+    """The streamed small-M GEMMs (5 <= m <= 64, n % 64 == 0, k % 256 == 0; 5-8 tokens take the
+    skinny stream-K GEMM, whose last 128-row tile is half past n here): passes of 16 or 32
     tokens with a ragged last pass, y = residual + W.x into a wider row stride, columns past n
     untouched. Unsplit it is bit-identical to the oracle; with K slices (a 5-tile grid) within
     the regrouping bound and deterministic."""
