@@ -82,6 +82,8 @@ struct AttParams {
     float* out;
     int8_t* xq;
     uint16_t* xd;
+    int rows;              // query rows of the launch (streamed decode kernel)
+    int* err;
 };
 
 // two-lane fused multiply-add (sm_100 packed f32x2): (a.x*b.x + c.x, a.y*b.y + c.y)
@@ -107,8 +109,10 @@ __device__ __forceinline__ float* att_cm(AttSmemR& S) { return &S.vs[0][0] + ATT
 
 // Unfused chunk: scores (thread -> position tid/2 and one 64-dim half, all GN heads; the halves
 // meet by a shuffle), per-head chunk softmax, P.V (thread -> dim, all heads), partials out.
-template <int GN>
-__device__ __forceinline__ void attn_chunk_fma(AttSmemR& S, int G, int cnt, float scale, int tid,
+// S: AttSmemR, or a view with the same members (ks, vs, qp, pt, ml) over one ring stage; BAR:
+// 0 = __syncthreads, else the named barrier of the ATT_THREADS computing threads
+template <int GN, int BAR = 0, typename SM>
+__device__ __forceinline__ void attn_chunk_fma(SM& S, int G, int cnt, float scale, int tid,
                                                const AttParams& p, int64_t hbase, int nsplit) {
     const int lane = tid & 31, warp = tid >> 5;
     {
@@ -148,7 +152,7 @@ __device__ __forceinline__ void attn_chunk_fma(AttSmemR& S, int G, int cnt, floa
             if (g < G) S.pt[pp][g] = pp < cnt ? __fmul_rn(v, scale) : -INFINITY;
         }
     }
-    __syncthreads();
+    group_sync<ATT_THREADS, BAR>();
     for (int g = warp; g < G; g += ATT_THREADS / 32) {
         const float a = S.pt[lane][g], c = S.pt[lane + 32][g];
         const float m = warp_max(fmaxf(a, c));
@@ -158,7 +162,7 @@ __device__ __forceinline__ void attn_chunk_fma(AttSmemR& S, int G, int cnt, floa
         const float sum = warp_sum(__fadd_rn(ea, ec));
         if (lane == 0) { S.ml[g][0] = m; S.ml[g][1] = sum; }
     }
-    __syncthreads();
+    group_sync<ATT_THREADS, BAR>();
     {
         const int d = tid;
         float acc[GN];
@@ -421,8 +425,8 @@ __global__ void __launch_bounds__(256, 4) attn_merge_kernel(const AttParams p) {
     const int Hq = p.Hq, Hkv = p.Hkv, L = p.L, nsplit = p.nsplit, G = Hq / Hkv;
     const int kvh = blockIdx.x, lrow = blockIdx.y;
     const int row = p.row0 + lrow, l = row % L;
+    pdl_trigger();  // early: the next kernel (a weight stream) may start; it waits for us in pdl_wait
     pdl_wait();
-    pdl_trigger();
     const int p0 = p.pos0_dev ? *p.pos0_dev : p.pos0;
     const int limit = p0 + l;
     if (limit < 0 || limit >= p.ctx_max) return;
@@ -464,6 +468,270 @@ __global__ void __launch_bounds__(256, 4) attn_merge_kernel(const AttParams p) {
         if (p.out) p.out[e] = o;
         if (p.xq) quant_warp32(o, lane, p.xq + (e - lane), p.xd + (e >> 5));
     }
+}
+
+// =========================================================================================
+// Batched decode attention, streamed (one query row per sequence, L == 1, G <= 8 query heads per
+// kv head). The 32-position chunks of all (row, kv head) pairs are dealt in equal contiguous
+// ranges to one CTA per SM. A producer warp fills a 5-stage ring with bulk copies (each K row
+// into its padded slot, the chunk's V rows in one copy, the pair's G query heads); eight
+// consumer warps compute a chunk while the next ones land: scores (one thread per (position,
+// head): four interleaved multiply-add chains over the 128 dimensions, added pairwise, then the
+// scale), an online softmax per head over the CTA's chunks of the pair (running max and
+// denominator; the P.V accumulators rescaled by exp(m_old - m_new)) and P.V (one thread per
+// (dimension, 4 heads)). At the end of its chunks of a pair a CTA leaves (m, l, o) in the
+// partial buffer; the CTA that completes the pair's chunk count (an atomic per pair, reset by
+// that CTA) merges the pieces in CTA order (weights exp(m_c - M)) and writes the output row
+// (f32 and/or Q8_0). The key/value stream never waits on the arithmetic, and no merge kernel
+// follows.
+// =========================================================================================
+constexpr int AV_P = 32;                      // positions per chunk (one per producer lane)
+constexpr int AV_STAGES = 5;
+constexpr int AV_CONS = 256;                  // eight consumer warps
+constexpr int AV_THREADS = AV_CONS + 32;      // + the producer warp
+
+struct AvStage {
+    float ks[AV_P][ATT_KS];
+    float vs[AV_P][ATT_D];
+    float qs[ATT_G][ATT_KS];
+};
+struct AvSmem {
+    AvStage st[AV_STAGES];
+    float pt[AV_P][ATT_G];                    // scores, then probabilities
+    float mr[ATT_G], lr[ATT_G], al[ATT_G];    // running max and denominator; this chunk's rescale
+    uint64_t full[AV_STAGES];
+    uint64_t empty[AV_STAGES];
+    int last;
+};
+
+// partial pieces: CTA b's j-th pair at slot b * jmax + j: o [G][D] unnormalised, (m, l) [G][2]
+struct AvRange {
+    long long units, u0, u1;
+    int nch;
+};
+
+template <int GT>
+__global__ void __launch_bounds__(AV_THREADS, 1) attn_decode_stream_kernel(const AttParams p) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    AvSmem& S = *reinterpret_cast<AvSmem*>(smem_raw);
+    const int Hq = p.Hq, Hkv = p.Hkv, ctx_max = p.ctx_max, jmax = p.nsplit;
+    const int G = GT ? GT : Hq / Hkv;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int i = 0; i < AV_STAGES; i++) {
+            mbar_init(&S.full[i], 1);
+            mbar_init(&S.empty[i], 1);
+        }
+        mbar_fence_init();
+    }
+    if (tid < ATT_G) {
+        S.mr[tid] = -INFINITY;
+        S.lr[tid] = 0.0f;
+    }
+    __syncthreads();
+    const int p0 = p.pos0_dev ? *p.pos0_dev : p.pos0;  // written by an earlier step: safe before pdl_wait
+    if (p0 < 0 || p0 >= ctx_max) return;
+    const int nch = p0 / AV_P + 1;
+    const long long units = (long long)p.rows * Hkv * nch, GG = gridDim.x;
+    const long long u0 = units * blockIdx.x / GG, u1 = units * (blockIdx.x + 1) / GG;
+
+    if (warp == AV_CONS / 32) {
+        // ---------------- producer warp ----------------
+        pdl_wait();  // the query rows and this step's K/V rows come from the preceding kernel
+        int s = 0;
+        unsigned ph = 0;
+        for (long long u = u0; u < u1; u++) {
+            const int pair = (int)(u / nch), c = (int)(u - (long long)pair * nch);
+            const int lrow = pair / Hkv, kvh = pair - lrow * Hkv;
+            const int b = p.row0 + lrow;
+            const int j0 = c * AV_P, cnt = min(AV_P, p0 + 1 - j0);
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait(&S.empty[s], ph ^ 1u);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) {
+                if (lane == 0 && p.err) atomicCAS(p.err, 0, 70);
+                return;
+            }
+            AvStage& T = S.st[s];
+            if (lane == 0) mbar_expect_tx(&S.full[s], (unsigned)((2 * cnt + G) * ATT_D * 4));
+            __syncwarp();
+            const int64_t kv0 = (((int64_t)b * Hkv + kvh) * ctx_max + j0) * ATT_D;
+            if (lane < cnt) bulk_g2s(&T.ks[lane][0], p.kc + kv0 + (int64_t)lane * ATT_D, ATT_D * 4, &S.full[s]);
+            if (lane == 0) bulk_g2s(&T.vs[0][0], p.vc + kv0, (unsigned)(cnt * ATT_D * 4), &S.full[s]);
+            if (lane < G)  // q rows [B][Hq][1][D]
+                bulk_g2s(&T.qs[lane][0], p.q + ((int64_t)b * Hq + kvh * G + lane) * ATT_D, ATT_D * 4, &S.full[s]);
+            if (++s == AV_STAGES) {
+                s = 0;
+                ph ^= 1u;
+            }
+        }
+        return;
+    }
+    // ---------------- consumers: 256 threads, named barrier 1 ----------------
+    pdl_wait();  // the partial buffer and counters of the previous launch are done with
+    pdl_trigger();
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)ATT_D));
+    const int sp = tid >> 3, sg = tid & 7;             // score: (position, head)
+    const int d = tid & (ATT_D - 1), h0 = 4 * (tid >> 7);  // P.V: dimension d, heads h0..h0+3
+    const long long first_pair = u0 / nch;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    int s = 0, done = 0;
+    unsigned ph = 0;
+    bool bad = false;
+    for (long long u = u0; u < u1; u++) {
+        const int pair = (int)(u / nch), c = (int)(u - (long long)pair * nch);
+        const int cnt = min(AV_P, p0 + 1 - c * AV_P);
+        const int cs = s;
+        const unsigned cph = ph;
+        if (++s == AV_STAGES) {
+            s = 0;
+            ph ^= 1u;
+        }
+        if (!bad) {
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait(&S.full[cs], cph);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) {
+                if (lane == 0 && p.err) atomicCAS(p.err, 0, 71);
+                bad = true;  // keeps computing (on whatever is there) so that the barriers still meet
+            }
+        }
+        const AvStage& T = S.st[cs];
+        {
+            float sc = -INFINITY;
+            if (sp < cnt && sg < G) {
+                const float* kr = T.ks[sp];
+                const float* qr = T.qs[sg];
+                float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll 8
+                for (int d4 = 0; d4 < ATT_D / 4; d4++) {
+                    const float4 k4 = *reinterpret_cast<const float4*>(kr + 4 * d4);
+                    const float4 q4 = *reinterpret_cast<const float4*>(qr + 4 * d4);
+                    a0 = fmaf(q4.x, k4.x, a0);
+                    a1 = fmaf(q4.y, k4.y, a1);
+                    a2 = fmaf(q4.z, k4.z, a2);
+                    a3 = fmaf(q4.w, k4.w, a3);
+                }
+                sc = __fmul_rn(__fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)), scale);
+            }
+            S.pt[sp][sg] = sc;
+        }
+        group_sync<AV_CONS, 1>();
+        if (warp < G) {
+            // online softmax of head g over this chunk: lane = position
+            const int g = warp;
+            const float sv = S.pt[lane][g];
+            const float mo = S.mr[g];
+            const float mn = fmaxf(mo, warp_max(sv));
+            const float pv = expf(__fsub_rn(sv, mn));
+            const float ps = warp_sum(pv);
+            S.pt[lane][g] = pv;
+            if (lane == 0) {
+                const float a = expf(__fsub_rn(mo, mn));  // 0 on the pair's first chunk (mo = -inf)
+                S.al[g] = a;
+                S.lr[g] = __fadd_rn(__fmul_rn(S.lr[g], a), ps);
+                S.mr[g] = mn;
+            }
+        }
+        group_sync<AV_CONS, 1>();
+        {
+#pragma unroll
+            for (int i = 0; i < 4; i++) acc[i] = h0 + i < G ? __fmul_rn(acc[i], S.al[h0 + i]) : 0.0f;
+            for (int j = 0; j < cnt; j++) {
+                const float vv = T.vs[j][d];
+                const float4 pj = *reinterpret_cast<const float4*>(&S.pt[j][h0]);
+                acc[0] = fmaf(pj.x, vv, acc[0]);
+                acc[1] = fmaf(pj.y, vv, acc[1]);
+                acc[2] = fmaf(pj.z, vv, acc[2]);
+                acc[3] = fmaf(pj.w, vv, acc[3]);
+            }
+        }
+        group_sync<AV_CONS, 1>();  // the stage and pt are free again
+        if (tid == 0) mbar_arrive(&S.empty[cs]);
+        done++;
+        if (c != nch - 1 && u + 1 != u1) continue;
+        // ---- this CTA's piece of the pair: (m, l, o) out; the CTA completing the count merges ----
+        {
+            const size_t slot = (size_t)blockIdx.x * jmax + (size_t)(pair - first_pair);
+            float* po = p.part_o + slot * G * ATT_D;
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                if (h0 + i < G) __stcg(po + (h0 + i) * ATT_D + d, acc[i]);
+            if (tid < G) {
+                __stcg(p.part_ml + (slot * G + tid) * 2, S.mr[tid]);
+                __stcg(p.part_ml + (slot * G + tid) * 2 + 1, S.lr[tid]);
+            }
+        }
+        __threadfence();
+        group_sync<AV_CONS, 1>();
+        int* cnt_p = p.counters + pair;
+        if (tid == 0) {
+            const int prev = atomicAdd(cnt_p, done);
+            S.last = prev + done == nch;
+        }
+        group_sync<AV_CONS, 1>();
+        if (tid < ATT_G) {  // running state of the next pair (read after the next scores barrier)
+            S.mr[tid] = -INFINITY;
+            S.lr[tid] = 0.0f;
+        }
+        acc[0] = acc[1] = acc[2] = acc[3] = 0.0f;
+        done = 0;
+        if (!S.last) continue;
+        __threadfence();
+        // contributors: the CTAs whose ranges hold the pair's first and last chunks, and those between
+        const long long pu0 = (long long)pair * nch;
+        const int bf = (int)(((pu0 + 1) * GG - 1) / units), bl = (int)(((pu0 + nch) * GG - 1) / units);
+        const int lrow = pair / Hkv, kvh = pair - lrow * Hkv;
+        const int64_t row = p.row0 + lrow;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int h = h0 + i;
+            if (h >= G) break;  // uniform per warp
+            float M = -INFINITY;
+            for (int q = bf; q <= bl; q++) {
+                const size_t sl = (size_t)q * jmax + (size_t)(pair - units * q / GG / nch);
+                M = fmaxf(M, __ldcg(p.part_ml + (sl * G + h) * 2));
+            }
+            float Ls = 0.0f, O = 0.0f;
+            for (int q = bf; q <= bl; q++) {
+                const size_t sl = (size_t)q * jmax + (size_t)(pair - units * q / GG / nch);
+                const float w = expf(__fsub_rn(__ldcg(p.part_ml + (sl * G + h) * 2), M));
+                Ls = __fadd_rn(Ls, __fmul_rn(w, __ldcg(p.part_ml + (sl * G + h) * 2 + 1)));
+                O = __fadd_rn(O, __fmul_rn(w, __ldcg(p.part_o + (sl * G + h) * ATT_D + d)));
+            }
+            const float o = __fdiv_rn(O, Ls);
+            const int64_t e = row * Hq * ATT_D + (int64_t)(kvh * G + h) * ATT_D + d;
+            if (p.out) p.out[e] = o;
+            if (p.xq) quant_warp32(o, lane, p.xq + (e - lane), p.xd + (e >> 5));
+        }
+        if (tid == 0) *cnt_p = 0;  // ready for the next launch
+    }
+}
+
+// partial-buffer slots per CTA: the most (row, kv head) pairs one CTA's range can touch
+static int av_jmax(int64_t pairs, int grid) { return (int)((pairs + grid - 1) / grid + 1); }
+
+static size_t av_scratch_bytes(int64_t pairs, int grid, int G) {
+    const size_t slots = (size_t)grid * av_jmax(pairs, grid);
+    return ATT_COUNTER_BYTES + ((slots * G * 2 * 4 + 255) & ~(size_t)255) + slots * G * ATT_D * 4;
+}
+
+template <int GT>
+static int launch_decode_stream(lq_ctx* ctx, AttParams p, int64_t rows, void* scratch, bool zero_counters) {
+    const int grid = ctx->sm_count, G = p.Hq / p.Hkv;
+    const int64_t pairs = rows * p.Hkv;
+    const size_t slots = (size_t)grid * av_jmax(pairs, grid);
+    p.counters = (int*)scratch;
+    p.part_ml = (float*)((uint8_t*)scratch + ATT_COUNTER_BYTES);
+    p.part_o = (float*)((uint8_t*)scratch + ATT_COUNTER_BYTES + ((slots * G * 2 * 4 + 255) & ~(size_t)255));
+    p.nsplit = av_jmax(pairs, grid);  // the kernel's partial slots per CTA
+    p.row0 = 0;
+    p.rows = (int)rows;
+    p.err = ctx->err_flag;
+    if (const int rc = ensure_func_smem(ctx, (const void*)attn_decode_stream_kernel<GT>, sizeof(AvSmem))) return rc;
+    if (zero_counters) LQ_CUDA(ctx, cudaMemsetAsync(p.counters, 0, (size_t)pairs * 4, ctx->stream));
+    return launch_kernel(ctx, attn_decode_stream_kernel<GT>, dim3((unsigned)grid), dim3(AV_THREADS), sizeof(AvSmem),
+                         "attn_decode_stream", p);
 }
 
 int attention_max_ctx() { return ATT_C * ATT_MAX_SPLITS; }
@@ -532,6 +800,18 @@ int launch_attention(lq_ctx* ctx, const float* q, const float* kc, const float* 
     p.out = out;
     p.xq = xq;
     p.xd = xd;
+    if (L == 1 && rows <= ATT_SLICE && getenv("LQ_ATT_STREAM") != nullptr &&
+        av_scratch_bytes(rows * Hkv, ctx->sm_count, (int)(Hq / Hkv)) <= attention_scratch_bytes(rows, Hq, ctx_max, D)) {
+        // decode rows, LQ_ATT_STREAM=1: the streamed kernel (slower than one CTA per 64-key
+        // chunk + the merge kernel at 32B batch 8 today)
+        switch (Hq / Hkv) {
+            case 8: return launch_decode_stream<8>(ctx, p, rows, scratch, zero_counters);
+            case 4: return launch_decode_stream<4>(ctx, p, rows, scratch, zero_counters);
+            case 2: return launch_decode_stream<2>(ctx, p, rows, scratch, zero_counters);
+            case 1: return launch_decode_stream<1>(ctx, p, rows, scratch, zero_counters);
+            default: return launch_decode_stream<0>(ctx, p, rows, scratch, zero_counters);
+        }
+    }
     switch (Hq / Hkv) {
         case 8: return launch_chunks<false, 8>(ctx, p, rows, scratch, zero_counters);
         case 4: return launch_chunks<false, 4>(ctx, p, rows, scratch, zero_counters);

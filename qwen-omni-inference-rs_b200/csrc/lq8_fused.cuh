@@ -62,11 +62,15 @@ __device__ __forceinline__ void rms_row(const T* __restrict__ xr, int dim, const
     // (all their loads issued at once); otherwise (and for longer rows) the second pass reads the
     // row again. The sum of squares runs in the same order either way.
     float cache[RC > 0 ? RC : 1][4];
+    uint2 wcache[RC > 0 ? RC : 1];  // the norm weights too: their loads overlap the reduction
     const bool cached = RC > 0 && dim <= RC * THREADS * 4;
 #pragma unroll
     for (int c = 0; c < RC; c++) {
         const int e = c * THREADS * 4 + tid * 4;
-        if (cached && e < dim) load4_any<T>(xr + e, cache[c]);
+        if (cached && e < dim) {
+            load4_any<T>(xr + e, cache[c]);
+            wcache[c] = *reinterpret_cast<const uint2*>(w + e);
+        }
     }
     float ss = 0.0f;
     for (int base = 0; base < dim; base += THREADS * 4) {
@@ -108,7 +112,14 @@ __device__ __forceinline__ void rms_row(const T* __restrict__ xr, int dim, const
             } else {
                 load4_any<T>(xr + e, v);
             }
-            const uint2 wt = *reinterpret_cast<const uint2*>(w + e);
+            uint2 wt;
+            if (cached) {
+#pragma unroll
+                for (int c = 0; c < RC; c++)
+                    if (c * THREADS * 4 == base) wt = wcache[c];
+            } else {
+                wt = *reinterpret_cast<const uint2*>(w + e);
+            }
             const float wv[4] = {bf16_to_f32((uint16_t)(wt.x & 0xFFFF)), bf16_to_f32((uint16_t)(wt.x >> 16)),
                                  bf16_to_f32((uint16_t)(wt.y & 0xFFFF)), bf16_to_f32((uint16_t)(wt.y >> 16))};
             uint16_t o[4];

@@ -25,8 +25,8 @@ __global__ void __launch_bounds__(NORM_THREADS)
 rmsnorm_kernel(const T* __restrict__ x, int dim, const uint16_t* __restrict__ w, float eps,
                uint16_t* __restrict__ out, int8_t* __restrict__ xq, uint16_t* __restrict__ xd) {
     __shared__ float red[32];
+    pdl_trigger();  // early: the next kernel (a weight stream) may start; it waits for us in pdl_wait
     pdl_wait();
-    pdl_trigger();
     const int64_t row = blockIdx.x;
     rms_row<T, NORM_THREADS, 0, 8>(x + row * dim, dim, w, eps, threadIdx.x, red, out ? out + row * dim : nullptr,
                                 xq ? xq + row * dim : nullptr, xq ? xd + row * (dim >> 5) : nullptr);
@@ -54,8 +54,8 @@ qk_norm_rope_kv_kernel(const float* __restrict__ qkv, int B, int L, int Hq, int 
                        int pos0, const int32_t* __restrict__ pos0_dev, float* __restrict__ q_out,
                        float* __restrict__ kc, float* __restrict__ vc, int ctx_max, int* err) {
     constexpr int D = 128, RD = 64;
+    pdl_trigger();  // early: the next kernel (a weight stream) may start; it waits for us in pdl_wait
     pdl_wait();
-    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int heads = Hq + 2 * Hkv;
@@ -103,8 +103,8 @@ int launch_qk_norm_rope_kv(lq_ctx* ctx, const float* qkv, int64_t B, int64_t L, 
 __global__ void __launch_bounds__(256)
 silu_mul_kernel(const float* __restrict__ gu, int inter, float* __restrict__ h, int8_t* __restrict__ xq,
                 uint16_t* __restrict__ xd) {
+    pdl_trigger();  // early: the next kernel (a weight stream) may start; it waits for us in pdl_wait
     pdl_wait();
-    pdl_trigger();
     // CTA (row, 1024-column chunk): one pass of the row function over its chunk (each 8-lane
     // group quantizes one 32-element block, so the chunking does not change a value)
     const int64_t row = blockIdx.x;

@@ -418,8 +418,8 @@ q8_gemm_mma_kernel(const int8_t* __restrict__ wq, const uint16_t* __restrict__ w
 // argmax keys (if any) per token over the CTA's outputs
 __global__ void gemm_split_reduce_kernel(const float* __restrict__ part, int splits, int M, int N, const float* resid,
                                          float* y, int ldy, unsigned long long* keys) {
+    pdl_trigger();  // early: the next kernel (a weight stream) may start; it waits for us in pdl_wait
     pdl_wait();
-    pdl_trigger();
     // one column per thread; the slices' values are loaded 8 at a time ahead of the adds
     const int m = blockIdx.y, n = blockIdx.x * blockDim.x + threadIdx.x;
     __shared__ unsigned long long ck;
@@ -925,6 +925,7 @@ struct SkParams {
     int N, K, M;
     int tiles, chunks;            // 128-row tiles; 256-byte units per tile
     int whole;                    // 1: whole tiles per CTA (no split)
+    int narrow;                   // 1: (units + 1) * grid < 2^32 (32-bit unit arithmetic)
     long long units;              // tiles * chunks
     const float* resid;
     float* y;
@@ -935,14 +936,23 @@ struct SkParams {
     int* err;
 };
 
-// first unit of CTA b
+// first unit of CTA b (32-bit division when units * grid fits 32 bits, as it does for every
+// decode shape: it sits on the path to the first weight load)
 __device__ __forceinline__ long long sk_start(const SkParams& p, int b) {
+    if (p.narrow)
+        return p.whole ? (long long)((unsigned)p.tiles * (unsigned)b / gridDim.x) * p.chunks
+                       : (long long)((unsigned)p.units * (unsigned)b / gridDim.x);
     const long long G = gridDim.x;
     return p.whole ? (long long)p.tiles * b / G * p.chunks : p.units * b / G;
 }
 // the CTA whose range holds unit u (split mode)
 __device__ __forceinline__ int sk_owner(const SkParams& p, long long u) {
+    if (p.narrow) return (int)((((unsigned)u + 1u) * gridDim.x - 1u) / (unsigned)p.units);
     return (int)(((u + 1) * (long long)gridDim.x - 1) / p.units);
+}
+// tile of unit u
+__device__ __forceinline__ int sk_tile(const SkParams& p, long long u) {
+    return p.narrow ? (int)((unsigned)u / (unsigned)p.chunks) : (int)(u / p.chunks);
 }
 
 __global__ void __launch_bounds__(SK_THREADS, 1) q8_gemm_skinny_kernel(const __grid_constant__ CUtensorMap mw,
@@ -973,11 +983,15 @@ __global__ void __launch_bounds__(SK_THREADS, 1) q8_gemm_skinny_kernel(const __g
     if (warp == SK_CONS) {
         // ---------------- producer (one lane); weights may stream before pdl_wait ----------------
         if (lane != 0) return;
+        tma_prefetch_map(&mw);
+        tma_prefetch_map(&mwd);
+        tma_prefetch_map(&mx);
+        tma_prefetch_map(&mxd);
         int s = 0;
         unsigned ph = 0;
         bool waited = false;
         for (long long u = u0; u < u1;) {
-            const int t = (int)(u / p.chunks);
+            const int t = sk_tile(p, u);
             const long long ts = (long long)t * p.chunks;
             const long long e = min(u1, ts + p.chunks);
             const int row = t * SK_ROWS;
@@ -1022,7 +1036,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) q8_gemm_skinny_kernel(const __g
     bool bad = false;
     bool first_seg = true;
     for (long long u = u0; u < u1; first_seg = false) {
-        const int t = (int)(u / p.chunks);
+        const int t = sk_tile(p, u);
         const long long ts = (long long)t * p.chunks;
         const long long e = min(u1, ts + p.chunks);
         const int c0 = (int)(u - ts), c1 = (int)(e - ts);
@@ -1185,6 +1199,7 @@ static int launch_gemm_skinny(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* 
     p.units = (long long)p.tiles * p.chunks;
     p.whole = getenv("LQ_GEMM_NO_SPLIT") ? 1 : 0;
     const int grid = sk_grid(ctx, w->n, w->k, p.whole != 0);
+    p.narrow = (uint64_t)(p.units + 1) * (uint64_t)grid < (1ull << 32) ? 1 : 0;
     p.resid = resid;
     p.y = y;
     p.ldy = (int)ldy;

@@ -129,6 +129,57 @@ def test_attention_vs_oracle(ctx, lq8_lib, oracle, rng, B, L, pos0, ctx_max, Hq,
     assert np.array_equal(H(xq), oq) and np.array_equal(H(xd, np.uint16), od)
 
 
+@pytest.mark.parametrize("B,pos0,ctx_max,Hq,Hkv,dev_pos", [(8, 1030, 2048, 64, 8, True), (1, 0, 64, 32, 8, False),
+                                                        (3, 63, 128, 16, 8, True), (5, 64, 256, 32, 4, False),
+                                                        (2, 4095, 4096, 8, 1, True), (8, 700, 1024, 32, 8, False)])
+def test_attention_decode_stream_vs_oracle(ctx, lq8_lib, oracle, rng, monkeypatch, B, pos0, ctx_max, Hq, Hkv,
+                                           dev_pos):
+    """The streamed decode attention (LQ_ATT_STREAM=1): the 32-key chunks of every (row, kv head)
+    pair dealt over one CTA per SM through a bulk-copy ring, an online softmax over a CTA's
+    chunks of a pair, and the pieces of a pair merged by the CTA that completes it. Every row
+    against the oracle (the position also read from device memory, as the graph-replay decode
+    does), the same bits on a second call, the Q8_0 output the quantization of the f32 output,
+    and within the same bound of the chunk kernel (the default)."""
+    import torch
+    D = 128
+    G = Hq // Hkv
+    T_ = pos0 + 1
+    q = rng.standard_normal((B, Hq, 1, D)).astype(np.float32)
+    kc = np.zeros((B, Hkv, ctx_max, D), np.float32)
+    vc = np.zeros((B, Hkv, ctx_max, D), np.float32)
+    kc[:, :, :T_] = rng.standard_normal((B, Hkv, T_, D))
+    vc[:, :, :T_] = rng.standard_normal((B, Hkv, T_, D))
+    keep = [T(a) for a in (q, kc, vc)]
+    pos_t = torch.tensor([pos0], dtype=torch.int32, device="cuda")
+
+    def run():
+        out = torch.full((B, Hq * D), float("nan"), dtype=torch.float32, device="cuda")
+        xq = torch.empty((B, Hq * D), dtype=torch.int8, device="cuda")
+        xd = torch.empty((B, Hq * D // 32), dtype=torch.int16, device="cuda")
+        ctx.call("lq_attention", keep[0].data_ptr(), keep[1].data_ptr(), keep[2].data_ptr(), B, Hq, Hkv, 1,
+                 0 if dev_pos else pos0, pos_t.data_ptr() if dev_pos else None, ctx_max, D, out.data_ptr(),
+                 xq.data_ptr(), xd.data_ptr())
+        ctx.synchronize()
+        return H(out), H(xq), H(xd, np.uint16)
+
+    monkeypatch.setenv("LQ_ATT_STREAM", "1")
+    got = run()
+    again = run()
+    for a, r in zip(got, again):
+        assert np.array_equal(a.view(np.uint8), r.view(np.uint8))
+    out = got[0].reshape(B, Hq, D)
+    for b in range(B):
+        for h in range(Hq):
+            want = oracle.attend_row(q[b, h, 0], kc[b, h // G, :T_], vc[b, h // G, :T_], masked=False,
+                                     causal_limit=pos0)
+            np.testing.assert_allclose(out[b, h], want, rtol=0, atol=2e-5 * np.abs(want).max())
+    oq, od = oracle.q8_0_quantize(got[0])
+    assert np.array_equal(got[1], oq) and np.array_equal(got[2], od)
+    monkeypatch.delenv("LQ_ATT_STREAM")
+    ref = run()[0].reshape(B, Hq, D)
+    np.testing.assert_allclose(out, ref, rtol=0, atol=4e-5 * np.abs(ref).max())
+
+
 @pytest.mark.parametrize("B,L,pos0,ctx_max", [(1, 16, 0, 64), (2, 47, 0, 128), (1, 200, 70, 300),
                                               (2, 129, 5, 2304), (1, 2048, 0, 2304)])
 @pytest.mark.parametrize("Hq,Hkv", [(16, 8), (32, 8), (64, 8), (32, 4), (8, 8)])
