@@ -287,6 +287,26 @@ def run_ours(args, cfgd, world, rank, local):
     t_pre = time.perf_counter() - t_pre
     model.set_batch(B)
     stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", local))
+    if args.prefill_reps:
+        # prefill timing: the same prompts again (the first call above was the warm-up), CUDA
+        # events on the model's stream around each call; the median
+        times = []
+        for _ in range(args.prefill_reps):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            model.prefill(prompts)
+            b.record(stream)
+            ctx.synchronize()
+            times.append(a.elapsed_time(b))
+        ms = statistics.median(times)
+        if rank == 0:
+            print(json.dumps({"metric": "prefill tok/s", "value": B * L / (ms / 1000.0), "unit": "tok/s",
+                              "ms": ms, "samples_ms": times, "batch": B, "prompt": L, "config": args.config,
+                              "kernel": "exact" if os.environ.get("LQ_PREFILL_EXACT") else "fp16 operands"}))
+        model.close()
+        ctx.close()
+        return
 
     def barrier():
         ctx.synchronize()
@@ -652,6 +672,8 @@ def main():
                     help="profiling: run this many decode steps between cudaProfilerStart/Stop and exit")
     ap.add_argument("--ncu-gemv", action="store_true",
                     help="profiling: also replay the decode GEMV launches inside the profiled range")
+    ap.add_argument("--prefill-reps", type=int, default=0,
+                    help="time this many prefills of the config's prompts (median, CUDA events) and exit")
     ap.add_argument("--trace", type=int, default=0,
                     help="timeline: run this many decode steps under torch.profiler and print a summary")
     ap.add_argument("--layers", type=int, default=0,

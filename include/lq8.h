@@ -115,6 +115,16 @@ int lq_q8_0_unpack_blocks(lq_ctx* ctx, const uint8_t* blocks_dev, int64_t rows, 
 int lq_q8_0_matmul(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq_dev,
                    const uint16_t* xd_dev, int64_t m, float* y_dev, const float* residual_dev,
                    int64_t ldy);
+/* The same product for prefill rows (m >= 128, k % 64 == 0), computed through fp16 operands:
+ * the weight blocks dequantized once per call to fp16(q * d), the activation rows to
+ * fp16(q * d * 2^-e) with a per-row power of two that keeps them in range, one fp16
+ * tensor-core GEMM with f32 accumulation over the whole K. Within 2^-10 * sum_k |w_k x_k| of
+ * lq_q8_0_matmul (which is exact) and several times faster at prefill sizes; other shapes
+ * take lq_q8_0_matmul. Allocates the fp16 operands in the context on first use. Same
+ * arguments as lq_q8_0_matmul. */
+int lq_q8_0_matmul_prefill(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq_dev,
+                           const uint16_t* xd_dev, int64_t m, float* y_dev, const float* residual_dev,
+                           int64_t ldy);
 /* Linear::forward (attention.rs:101-136) with a Q8_0 weight: x [m][k] f32 or bf16 is
  * quantized into the context's scratch, then multiplied; y [m][n] f32. */
 int lq_q8_0_linear(lq_ctx* ctx, const lq_q8_tensor* w, const void* x_dev, lq_dtype x_dtype,

@@ -17,7 +17,7 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "liblq8.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
-SOURCES = ["lq8_runtime.cu", "lq8_q8.cu", "lq8_gemv.cu", "lq8_gemm_tc.cu", "lq8_attn_prefill.cu", "lq8_moe.cu", "lq8_comm.cu", "lq8_ops.cu", "lq8_attention.cu", "lq8_decode.cu", "lq8_sample.cu", "lq8_qwen3.cu"]
+SOURCES = ["lq8_runtime.cu", "lq8_q8.cu", "lq8_gemv.cu", "lq8_gemm_tc.cu", "lq8_gemm_f16.cu", "lq8_attn_prefill.cu", "lq8_moe.cu", "lq8_comm.cu", "lq8_ops.cu", "lq8_attention.cu", "lq8_decode.cu", "lq8_sample.cu", "lq8_qwen3.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -29,6 +29,10 @@ struct lq_ctx {
     // GEMM's activations); reserved ahead by models so that graph capture never allocates
     void* split = nullptr;
     size_t split_bytes = 0;
+    // fp16 operands of the prefill GEMM (weights and activations dequantized from Q8_0); grown
+    // on demand outside graph capture
+    void* wide = nullptr;
+    size_t wide_bytes = 0;
     int* err_flag = nullptr;      // device int[4]: kernels report bad inputs here
     // device unsigned[kTileCounters], zero between launches: arrivals of the CTAs that share a
     // GEMM tile (the skinny GEMM's stream-K combine; the last CTA resets its counter)
@@ -48,6 +52,8 @@ bool fault_injected(const char* entry);
 int ensure_scratch(lq_ctx* ctx, size_t bytes);
 // grows ctx->split (an error while the stream is capturing a graph)
 int ensure_split(lq_ctx* ctx, size_t bytes);
+// grows ctx->wide (an error while the stream is capturing a graph)
+int ensure_wide(lq_ctx* ctx, size_t bytes);
 // partial-sum bytes the M x (N, K) Q8_0 GEMM needs when it splits K (0: no split)
 size_t gemm_split_bytes(lq_ctx* ctx, int64_t n, int64_t k, int64_t m);
 // read + clear the device error flag (synchronises the stream)
@@ -209,6 +215,15 @@ int launch_q8_matmul(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const
 bool gemv_stream_supported(int64_t K);
 // prefill GEMM on tcgen05 (m >= 64 tokens, K % 256 == 0, 16-byte aligned operands)
 bool gemm_tc_supported(int64_t m, int64_t K, const void* wq, const void* xq, const void* wd, const void* xd);
+// prefill GEMM through fp16 operands (m >= 128 rows, K % 64 == 0): weights and activations
+// dequantized from Q8_0 into ctx->wide, one fp16 tcgen05 GEMM with f32 accumulation. Returns
+// LQ_ERR_UNSUPPORTED (nothing launched) when the shape does not qualify.
+int launch_gemm_f16(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd, int64_t m, float* y,
+                    const float* resid, int64_t ldy);
+// the prefill projections: launch_gemm_f16 when it qualifies (LQ_PREFILL_EXACT=1 turns it off),
+// else launch_q8_matmul
+int launch_q8_matmul_prefill(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd, int64_t m,
+                             float* y, const float* resid, int64_t ldy);
 int launch_gemm_tc(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd, int64_t m, float* y,
                    const float* resid, int64_t ldy);
 size_t gemv_stream_smem(int64_t m, int64_t K);

@@ -310,7 +310,7 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
         // input_layernorm -> Q8_0
         RC(lq::launch_rmsnorm(ctx, m->x, LQ_DTYPE_F32, rows, H, ly.in_norm, c.eps, nullptr, m->xq, m->xd));
         // fused q/k/v projection
-        RC(lq::launch_q8_matmul(ctx, &ly.qkv, m->xq, m->xd, rows, m->qkv, nullptr, m->Nqkv, nullptr));
+        RC(lq::launch_q8_matmul_prefill(ctx, &ly.qkv, m->xq, m->xd, rows, m->qkv, nullptr, m->Nqkv));
         if (fused_att) {
             // batched decode: q/k norm, RoPE, KV append, attention and the chunk merge -> Q8_0
             // rows in one kernel (the chunks' last CTA merges)
@@ -334,7 +334,7 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
         }
         }
         // o_proj + residual (transformer.rs:194)
-        RC(lq::launch_q8_matmul(ctx, &ly.o, m->xq, m->xd, rows, rp_out(m), rp_resid(m), H, nullptr));
+        RC(lq::launch_q8_matmul_prefill(ctx, &ly.o, m->xq, m->xd, rows, rp_out(m), rp_resid(m), H));
         RC(rp_reduce(m, rows));
         if (m->moe) {
             RC(moe_mlp(m, ly, rows));
@@ -342,9 +342,9 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
         }
         // post_attention_layernorm -> Q8_0, gate/up, silu*up -> Q8_0, down + residual
         RC(lq::launch_rmsnorm(ctx, m->x, LQ_DTYPE_F32, rows, H, ly.post_norm, c.eps, nullptr, m->xq, m->xd));
-        RC(lq::launch_q8_matmul(ctx, &ly.gate_up, m->xq, m->xd, rows, m->gu, nullptr, 2 * I, nullptr));
+        RC(lq::launch_q8_matmul_prefill(ctx, &ly.gate_up, m->xq, m->xd, rows, m->gu, nullptr, 2 * I));
         RC(lq::launch_silu_mul(ctx, m->gu, rows, I, nullptr, m->xq, m->xd));
-        RC(lq::launch_q8_matmul(ctx, &ly.down, m->xq, m->xd, rows, rp_out(m), rp_resid(m), H, nullptr));
+        RC(lq::launch_q8_matmul_prefill(ctx, &ly.down, m->xq, m->xd, rows, rp_out(m), rp_resid(m), H));
         RC(rp_reduce(m, rows));
     }
     // final norm on the last row of each sequence (model.rs:194, :357-358)

@@ -64,6 +64,24 @@ int ensure_scratch(lq_ctx* ctx, size_t bytes) {
     return LQ_OK;
 }
 
+int ensure_wide(lq_ctx* ctx, size_t bytes) {
+    if (bytes <= ctx->wide_bytes) return LQ_OK;
+    if (fault_injected("ensure_wide"))
+        return set_error(ctx, LQ_ERR_INJECTED, "ensure_wide: injected fault (LQ_FAULT), %zu bytes", bytes);
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    LQ_CUDA(ctx, cudaStreamIsCapturing(ctx->stream, &st));
+    if (st != cudaStreamCaptureStatusNone)
+        return set_error(ctx, LQ_ERR_STATE, "fp16 operand buffer (%zu bytes) too small while capturing a graph", bytes);
+    LQ_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    if (ctx->wide) LQ_CUDA(ctx, cudaFree(ctx->wide));
+    ctx->wide = nullptr;
+    ctx->wide_bytes = 0;
+    size_t sz = (bytes + 0xFFFFF) & ~(size_t)0xFFFFF;
+    LQ_CUDA(ctx, cudaMalloc(&ctx->wide, sz));
+    ctx->wide_bytes = sz;
+    return LQ_OK;
+}
+
 int ensure_split(lq_ctx* ctx, size_t bytes) {
     if (bytes <= ctx->split_bytes) return LQ_OK;
     if (fault_injected("ensure_split"))
@@ -165,6 +183,7 @@ int lq_destroy(lq_ctx* ctx) {
     cudaStreamSynchronize(ctx->stream);
     if (ctx->scratch) cudaFree(ctx->scratch);
     if (ctx->split) cudaFree(ctx->split);
+    if (ctx->wide) cudaFree(ctx->wide);
     if (ctx->err_flag) cudaFree(ctx->err_flag);
     if (ctx->tile_cnt) cudaFree(ctx->tile_cnt);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);

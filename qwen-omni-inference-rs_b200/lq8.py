@@ -114,6 +114,7 @@ SIGNATURES = {
     "lq_q8_0_pack_blocks": (C.c_int, [_P, _P, _P, _I64, _I64, _P]),
     "lq_q8_0_unpack_blocks": (C.c_int, [_P, _P, _I64, _I64, _P, _P]),
     "lq_q8_0_matmul": (C.c_int, [_P, C.POINTER(Q8Tensor), _P, _P, _I64, _P, _P, _I64]),
+    "lq_q8_0_matmul_prefill": (C.c_int, [_P, C.POINTER(Q8Tensor), _P, _P, _I64, _P, _P, _I64]),
     "lq_q8_0_linear": (C.c_int, [_P, C.POINTER(Q8Tensor), _P, C.c_int, _I64, _P]),
     "lq_q8_0_linear_noalloc": (C.c_int, [_P, C.POINTER(Q8Tensor), _P, C.c_int, _I64, _P]),
     "lq_q8_0_quantize_host": (C.c_int, [_P, C.c_int, _I64, _I64, _P, _P]),

@@ -11,7 +11,7 @@ use std::path::{Path, PathBuf};
 use std::process::Command;
 
 const SOURCES: &[&str] = &[
-    "lq8_runtime.cu", "lq8_q8.cu", "lq8_gemv.cu", "lq8_gemm_tc.cu", "lq8_attn_prefill.cu", "lq8_moe.cu",
+    "lq8_runtime.cu", "lq8_q8.cu", "lq8_gemv.cu", "lq8_gemm_tc.cu", "lq8_gemm_f16.cu", "lq8_attn_prefill.cu", "lq8_moe.cu",
     "lq8_comm.cu", "lq8_ops.cu", "lq8_attention.cu", "lq8_decode.cu", "lq8_sample.cu", "lq8_qwen3.cu",
 ];
 

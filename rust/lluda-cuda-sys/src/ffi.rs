@@ -121,6 +121,7 @@ extern "C" {
     pub fn lq_q8_0_pack_blocks(ctx: *mut LqCtx, qs_dev: *const i8, d_dev: *const u16, rows: i64, k: i64, blocks_dev: *mut u8) -> c_int;
     pub fn lq_q8_0_unpack_blocks(ctx: *mut LqCtx, blocks_dev: *const u8, rows: i64, k: i64, qs_dev: *mut i8, d_dev: *mut u16) -> c_int;
     pub fn lq_q8_0_matmul(ctx: *mut LqCtx, w: *const LqQ8Tensor, xq_dev: *const i8, xd_dev: *const u16, m: i64, y_dev: *mut f32, residual_dev: *const f32, ldy: i64) -> c_int;
+    pub fn lq_q8_0_matmul_prefill(ctx: *mut LqCtx, w: *const LqQ8Tensor, xq_dev: *const i8, xd_dev: *const u16, m: i64, y_dev: *mut f32, residual_dev: *const f32, ldy: i64) -> c_int;
     pub fn lq_q8_0_linear(ctx: *mut LqCtx, w: *const LqQ8Tensor, x_dev: *const c_void, x_dtype: c_int, m: i64, y_dev: *mut f32) -> c_int;
     pub fn lq_q8_0_linear_noalloc(ctx: *mut LqCtx, w: *const LqQ8Tensor, x_dev: *const c_void, x_dtype: c_int, m: i64, y_dev: *mut f32) -> c_int;
     pub fn lq_rmsnorm(ctx: *mut LqCtx, x_dev: *const c_void, x_dtype: c_int, rows: i64, dim: i64, w_bf16_dev: *const u16, eps: f32, out_bf16_dev: *mut u16, xq_dev: *mut i8, xd_dev: *mut u16) -> c_int;

@@ -169,6 +169,84 @@ def test_gemm_skinny_counters_reset_between_launches(ctx, lq8_lib, oracle, rng):
             assert np.array_equal(_matmul(ctx, lq8_lib, *c), y0)
 
 
+def _matmul_prefill(ctx, lq8, wq, wd, xq, xd, resid=None, ldy=None):
+    import torch
+    m, n = xq.shape[0], wq.shape[0]
+    ldy = ldy or n
+    y = torch.full((m, ldy), float("nan"), dtype=torch.float32, device="cuda")
+    r = T(resid) if resid is not None else None
+    if r is not None:
+        y.copy_(r)
+    wq_t, wd_t, xq_t, xd_t = T(wq), T(wd), T(xq), T(xd)
+    w = lq8.Q8Tensor(n, wq.shape[1], wq_t.data_ptr(), wd_t.data_ptr())
+    ctx.call("lq_q8_0_matmul_prefill", C.byref(w), xq_t.data_ptr(), xd_t.data_ptr(), m, y.data_ptr(),
+             y.data_ptr() if r is not None else None, ldy)
+    ctx.synchronize()
+    return H(y)
+
+
+def _prefill_bound(oracle, xq, xd, absum, k):
+    """fp16 operands: 2^-11 relative rounding each (2^-10 per product), the f32 regrouping bound,
+    and the fp16 subnormal range of the weights (an absolute 2^-25 per weight times |x|)."""
+    x = xq.astype(np.float32).reshape(xq.shape[0], -1, 32) * xd.view(np.float16).astype(np.float32)[:, :, None]
+    xabs = np.abs(x).reshape(xq.shape[0], -1).sum(axis=1)[:, None]
+    return (2.0 ** -10 + 2.0 * (k // 32 + 1) * 2.0 ** -24) * absum + 2.0 ** -24 * xabs + 1e-30
+
+
+@pytest.mark.parametrize("m,n,k,scale", [(128, 640, 3072, 1.0), (300, 1000, 1024, 1.0), (257, 384, 2048, 3e4),
+                                         (513, 256, 4096, 1.0)])
+def test_gemm_prefill_f16_within_bound(ctx, lq8_lib, oracle, rng, m, n, k, scale):
+    """lq_q8_0_matmul_prefill (m >= 128): the weights and activations dequantized to fp16 (a
+    power-of-two row scale keeps large activations, here up to ~1e5, in range) and one fp16
+    tcgen05 GEMM with f32 accumulation. Ragged token and row tiles; every output against the
+    oracle within the fp16 operand bound; deterministic."""
+    wq, wd = _weights(oracle, rng, n, k)
+    xq, xd = oracle.q8_0_quantize((rng.standard_normal((m, k)) * scale).astype(np.float32))
+    y = _matmul_prefill(ctx, lq8_lib, wq, wd, xq, xd)
+    assert not np.isnan(y).any()
+    ref, absum = oracle.q8_0_matmul(xq, xd, wq, wd, with_abs=True)
+    bound = _prefill_bound(oracle, xq, xd, absum, k)
+    assert np.all(np.abs(y - ref) <= bound), float(np.max(np.abs(y - ref) / bound))
+    assert np.array_equal(y, _matmul_prefill(ctx, lq8_lib, wq, wd, xq, xd))
+
+
+@pytest.mark.parametrize("m,n,k", [(512, 12288, 4096), (512, 5120, 25600), (2048, 4096, 12288)])
+def test_gemm_prefill_config2_shapes(ctx, lq8_lib, oracle, rng, m, n, k):
+    """The prefill GEMM shapes of Qwen3-8B and -32B (gate|up / down sizes) at 512 and 2048
+    tokens, through both prefill kernels: the exact tcgen05 GEMM (lq_q8_0_matmul) against the
+    oracle bit for bit, and the fp16-operand GEMM within its bound, on 48 token rows."""
+    wq, wd = _weights(oracle, rng, n, k)
+    xq, xd = oracle.q8_0_quantize(rng.standard_normal((m, k)).astype(np.float32))
+    y_exact = _matmul(ctx, lq8_lib, wq, wd, xq, xd)
+    y_fast = _matmul_prefill(ctx, lq8_lib, wq, wd, xq, xd)
+    rows = np.unique(np.concatenate([np.arange(16), rng.choice(m, 16, replace=False), np.arange(m - 16, m)]))
+    ref, absum = oracle.q8_0_matmul(xq[rows], xd[rows], wq, wd, with_abs=True)
+    assert np.array_equal(y_exact[rows], ref)
+    bound = _prefill_bound(oracle, xq[rows], xd[rows], absum, k)
+    assert np.all(np.abs(y_fast[rows] - ref) <= bound), float(np.max(np.abs(y_fast[rows] - ref) / bound))
+    assert not np.isnan(y_fast).any()
+
+
+def test_gemm_prefill_residual_stride_and_fallback(ctx, lq8_lib, oracle, rng, monkeypatch):
+    """y = residual + x.W^T into a wider row stride (columns past n untouched); fewer than 128
+    rows, or LQ_PREFILL_EXACT=1, take the exact kernels (bit-identical to lq_q8_0_matmul)."""
+    n, k, ldy = 320, 2048, 384
+    wq, wd = _weights(oracle, rng, n, k)
+    for m in (200, 100):
+        xq, xd = oracle.q8_0_quantize(rng.standard_normal((m, k)).astype(np.float32))
+        resid = rng.standard_normal((m, ldy)).astype(np.float32)
+        y = _matmul_prefill(ctx, lq8_lib, wq, wd, xq, xd, resid=resid, ldy=ldy)
+        assert np.array_equal(y[:, n:], resid[:, n:])
+        ref, absum = oracle.q8_0_matmul(xq, xd, wq, wd, with_abs=True)
+        bound = _prefill_bound(oracle, xq, xd, absum, k) + 2.0 ** -23 * np.abs(resid[:, :n] + ref)
+        assert np.all(np.abs(y[:, :n] - (resid[:, :n] + ref)) <= bound)
+        if m < 128:
+            assert np.array_equal(y, _matmul(ctx, lq8_lib, wq, wd, xq, xd, resid=resid, ldy=ldy))
+    monkeypatch.setenv("LQ_PREFILL_EXACT", "1")
+    xq, xd = oracle.q8_0_quantize(rng.standard_normal((200, k)).astype(np.float32))
+    assert np.array_equal(_matmul_prefill(ctx, lq8_lib, wq, wd, xq, xd), _matmul(ctx, lq8_lib, wq, wd, xq, xd))
+
+
 @pytest.mark.parametrize("m", [65, 127, 128, 300, 513])
 @pytest.mark.parametrize("n,k", [(128, 256), (129, 512), (1000, 4096), (4096, 1024)])
 def test_gemm_tcgen05_bit_exact(ctx, lq8_lib, oracle, rng, m, n, k):

@@ -300,9 +300,21 @@ def test_tensor_parallel_32b_shapes_2_gpus(oracle, path):
     oracle with the tolerance of the headline-shape tests (the noise floor of these shapes;
     test_gpu_headline.py), tokens equal wherever the oracle's margin exceeds twice the step's
     difference."""
+    _tp32_check(oracle, path, 2)
+
+
+@pytest.mark.parametrize("world", [4, 8])
+@pytest.mark.parametrize("path", ["persistent", "default"])
+def test_tensor_parallel_32b_shapes_4_8_gpus(oracle, path, world):
+    """The same check with 4 and 8 tensor-parallel ranks (the scaling run's shards: 16 or 8 heads,
+    2 or 1 kv heads, 6400 or 3200 intermediate rows, 37984 or 18992 LM-head rows per rank)."""
+    _tp32_check(oracle, path, world)
+
+
+def _tp32_check(oracle, path, world):
     import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     from conftest import parity_metrics, record
     B, L, steps = 8, 24, 4
@@ -323,7 +335,7 @@ def test_tensor_parallel_32b_shapes_2_gpus(oracle, path):
     mctx = mp.get_context("spawn")
     qq = mctx.Queue()
     port = _free_port()
-    procs = [mctx.Process(target=_tp32_rank_main, args=(r, 2, port, qq, prompts, fed, path)) for r in range(2)]
+    procs = [mctx.Process(target=_tp32_rank_main, args=(r, world, port, qq, prompts, fed, path)) for r in range(world)]
     for p in procs:
         p.start()
     res = [qq.get(timeout=900) for _ in procs]
@@ -332,16 +344,18 @@ def test_tensor_parallel_32b_shapes_2_gpus(oracle, path):
     for r in res:
         assert "error" not in r, r
     r0 = next(r for r in res if r["rank"] == 0)
-    if path == "persistent":
+    if path == "persistent" and (QWEN3_32B_2L["inter"] // world) % 256 == 0:
         assert all(r["kernels"] == 3 for r in res), [r["kernels"] for r in res]
-    else:
+    elif path != "persistent":
         assert r0["kernels"] > 3  # per-layer kernels
+    # (8 ranks: 3200 intermediate rows per rank are not whole 256-byte stages, so the persistent
+    # step declines and the per-layer kernels run)
     for s in range(steps):
         for b in range(B):
             m = parity_metrics(r0["logits"][s, b], olgs[s, b])
             srt = np.sort(olgs[s, b])
             same = int(r0["tokens"][s, b]) == oracle.argmax(olgs[s, b])
-            record("32b_tp2_" + path, step=s, row=b, same_token=same,
+            record(f"32b_tp{world}_" + path, step=s, row=b, same_token=same,
                    margin=float(srt[-1] - srt[-2]), **m)
             assert m["cos"] >= 0.9995 and m["max_rel"] <= 5e-2, (s, b, m)
             assert same or srt[-1] - srt[-2] <= 2 * m["max_abs"], (s, b)
