@@ -415,15 +415,192 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const AttParams
     if (tid == 0) p.counters[lrow * Hkv + kvh] = 0;  // ready for the next launch
 }
 
-// the unfused path's merge: one CTA per (kv head, query row) rescales its chunks' partials by
-// exp(m_s - M), adds them in chunk order and divides by the summed denominators (the same
-// arithmetic as the fused kernel's last-CTA merge). A kernel of its own, so that the chunk
-// CTAs end without a fence and an atomic.
-__global__ void __launch_bounds__(256, 4) attn_merge_kernel(const AttParams p) {
-    __shared__ float cm[ATT_G][ATT_MAX_SPLITS];
-    __shared__ float cl[ATT_G];
+// =========================================================================================
+// Unfused chunk kernel (query rows from a q tensor: batched decode rows and short prefills).
+// One CTA of 256 threads per (query row, kv head, 64-position chunk), three CTAs per SM. The
+// chunk's K rows arrive by one bulk copy per row into padded slots and its V rows by one bulk
+// copy, each set on its own mbarrier, so the scores start as soon as K has landed while V is
+// still in flight; the rows written before this step are requested before pdl_wait, the rows of
+// this launch's positions after it. Scores: thread -> (position, 64-dim half, 4 heads), two-lane
+// packed multiply-adds, the halves added by a shuffle, then the scale; a chunk softmax per head
+// (one warp per head); P.V: thread -> (dimension, 32-position half, all heads), the halves
+// added through shared memory. Partials (o, m, l) per (head, chunk) for attn_merge_kernel.
+// =========================================================================================
+constexpr int ATB_THREADS = 256;
+constexpr int ATB_QS = ATT_D + 12;  // q row stride: halves 4 floats apart (one broadcast wavefront)
+
+struct AttSmemB {
+    float ks[ATT_C][ATT_KS];          // K rows, padded: conflict-free float4 reads by position
+    float vs[ATT_C][ATT_D];
+    float qp[ATT_G][ATB_QS];          // query heads; reused for the P.V half sums
+    float pt[ATT_C][ATT_G];           // scores by position, then probabilities
+    float ml[ATT_G][2];
+    uint64_t bar[2];                  // K rows, V rows
+    int ok_k, ok_v;
+};
+
+template <int GT>
+__global__ void __launch_bounds__(ATB_THREADS, 3) attn_chunk_bulk_kernel(const AttParams p) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    AttSmemB& S = *reinterpret_cast<AttSmemB*>(smem_raw);
+    constexpr int GN = GT ? GT : ATT_G;
+    const int Hq = p.Hq, Hkv = p.Hkv, L = p.L, ctx_max = p.ctx_max, nsplit = p.nsplit;
+    const int G = GT ? GT : Hq / Hkv;
+    const int split = blockIdx.x, kvh = blockIdx.y, lrow = blockIdx.z;
+    const int row = p.row0 + lrow;  // b*L + l
+    const int b = row / L, l = row - (row / L) * L;
+    const int p0 = p.pos0_dev ? *p.pos0_dev : p.pos0;  // written by an earlier step: safe before pdl_wait
+    const int limit = p0 + l;  // last visible position
+    if (limit < 0 || limit >= ctx_max) return;
+    const int n_active = min(limit / ATT_C + 1, nsplit);
+    if (split >= n_active) return;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int j0 = split * ATT_C;
+    const int cnt = min(ATT_C, limit + 1 - j0);
+    const int64_t slab = ((int64_t)b * Hkv + kvh) * (int64_t)ctx_max * ATT_D + (int64_t)j0 * ATT_D;
+    const float* kbase = p.kc + slab;
+    const float* vbase = p.vc + slab;
+    // rows r >= fresh hold this launch's positions (written by the preceding kernel)
+    const int fresh = max(0, min(cnt, p0 - j0));
+    if (tid == 0) {
+        mbar_init(&S.bar[0], 1);
+        mbar_init(&S.bar[1], 1);
+        mbar_fence_init();
+        mbar_expect_tx(&S.bar[0], (unsigned)(cnt * ATT_D * 4));
+        mbar_expect_tx(&S.bar[1], (unsigned)(cnt * ATT_D * 4));
+    }
+    __syncthreads();
+    if (tid < fresh) bulk_g2s(&S.ks[tid][0], kbase + (int64_t)tid * ATT_D, ATT_D * 4, &S.bar[0]);
+    if (tid == 64 && fresh > 0) bulk_g2s(&S.vs[0][0], vbase, (unsigned)(fresh * ATT_D * 4), &S.bar[1]);
+    pdl_wait();
+    pdl_trigger();
+    if (tid >= fresh && tid < cnt) bulk_g2s(&S.ks[tid][0], kbase + (int64_t)tid * ATT_D, ATT_D * 4, &S.bar[0]);
+    if (tid == 96 && fresh < cnt)
+        bulk_g2s(&S.vs[fresh][0], vbase + (int64_t)fresh * ATT_D, (unsigned)((cnt - fresh) * ATT_D * 4), &S.bar[1]);
+    // query heads (the second half of each row 4 floats further on)
+    for (int i = tid; i < G * ATT_D; i += ATB_THREADS) {
+        const int g = i / ATT_D, d = i % ATT_D;
+        S.qp[g][d + (d >= ATT_D / 2 ? 4 : 0)] = p.q[(((int64_t)b * Hq + kvh * G + g) * L + l) * ATT_D + d];
+    }
+    if (tid == 0) S.ok_k = mbar_wait_ns(&S.bar[0], 0, 2000000000ull);
+    __syncthreads();
+    if (!S.ok_k) {
+        // K never landed: report, wait (bounded) for the V copies, leave
+        if (tid == 0) {
+            if (p.err) atomicCAS(p.err, 0, 72);
+            mbar_wait_ns(&S.bar[1], 0, 2000000000ull);
+        }
+        return;
+    }
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)ATT_D));
+    {
+        const int hf = tid & 1, pp = (tid >> 1) & (ATT_C - 1), gh = tid >> 7;
+        float2 s2[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) s2[i] = make_float2(0.0f, 0.0f);
+        if (pp < cnt && 4 * gh < G) {
+            const float* kr = &S.ks[pp][hf * (ATT_D / 2)];
+            const float* qr = &S.qp[4 * gh][hf * (ATT_D / 2 + 4)];
+#pragma unroll 4
+            for (int d4 = 0; d4 < ATT_D / 8; d4++) {
+                const float4 k4 = *reinterpret_cast<const float4*>(kr + 4 * d4);
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    if (i < GN && 4 * gh + i < G) {
+                        const float4 q4 = *reinterpret_cast<const float4*>(qr + i * ATB_QS + 4 * d4);
+                        s2[i] = fma2(make_float2(q4.x, q4.y), make_float2(k4.x, k4.y), s2[i]);
+                        s2[i] = fma2(make_float2(q4.z, q4.w), make_float2(k4.z, k4.w), s2[i]);
+                    }
+                }
+            }
+        }
+        float sc[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            sc[i] = __fadd_rn(s2[i].x, s2[i].y);
+            sc[i] = __fadd_rn(sc[i], __shfl_xor_sync(0xffffffffu, sc[i], 1));
+        }
+        // half 0 stores heads 4gh, 4gh+1; half 1 heads 4gh+2, 4gh+3
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            const int g = 4 * gh + 2 * hf + i;
+            const float v = hf ? sc[2 + i] : sc[i];
+            if (g < G) S.pt[pp][g] = pp < cnt ? __fmul_rn(v, scale) : -INFINITY;
+        }
+    }
+    if (tid == 0) S.ok_v = mbar_wait_ns(&S.bar[1], 0, 2000000000ull);
+    __syncthreads();
+    if (!S.ok_v) {
+        if (tid == 0 && p.err) atomicCAS(p.err, 0, 73);
+        return;
+    }
+    for (int g = warp; g < G; g += ATB_THREADS / 32) {
+        const float a = S.pt[lane][g], c = S.pt[lane + 32][g];
+        const float m = warp_max(fmaxf(a, c));
+        const float ea = expf(__fsub_rn(a, m)), ec = expf(__fsub_rn(c, m));
+        S.pt[lane][g] = ea;
+        S.pt[lane + 32][g] = ec;
+        const float sum = warp_sum(__fadd_rn(ea, ec));
+        if (lane == 0) { S.ml[g][0] = m; S.ml[g][1] = sum; }
+    }
+    __syncthreads();
+    {
+        const int d = tid & (ATT_D - 1), ph = tid >> 7;
+        constexpr int GP = (GN + 1) / 2;  // head pairs (two-lane fused multiply-add)
+        float2 a2[GP];
+#pragma unroll
+        for (int i = 0; i < GP; i++) a2[i] = make_float2(0.0f, 0.0f);
+        const int je = min(cnt, 32 * ph + 32);
+#pragma unroll 4
+        for (int j = 32 * ph; j < je; j++) {
+            const float vv = S.vs[j][d];
+            const float2 v2 = make_float2(vv, vv);
+            const float4 pa = *reinterpret_cast<const float4*>(&S.pt[j][0]);
+            a2[0] = fma2(make_float2(pa.x, pa.y), v2, a2[0]);
+            if constexpr (GN > 2) a2[1] = fma2(make_float2(pa.z, pa.w), v2, a2[1]);
+            if constexpr (GN > 4) {
+                const float4 pb = *reinterpret_cast<const float4*>(&S.pt[j][4]);
+                a2[2] = fma2(make_float2(pb.x, pb.y), v2, a2[2]);
+                a2[3] = fma2(make_float2(pb.z, pb.w), v2, a2[3]);
+            }
+        }
+        float acc[GN];
+#pragma unroll
+        for (int g = 0; g < GN; g++) acc[g] = (g & 1) ? a2[g >> 1].y : a2[g >> 1].x;
+        // the two position halves: half 0 finishes heads [0, GN/2), half 1 the rest; each
+        // hands the other its sums of those heads (q rows are no longer read)
+        constexpr int GH = (GN + 1) / 2;
+        float* red = &S.qp[0][0];  // [GN][ATT_D]
+#pragma unroll
+        for (int g = 0; g < GN; g++)
+            if ((g < GH) == (ph == 1)) red[g * ATT_D + d] = acc[g];
+        __syncthreads();
+        const int64_t hbase = ((int64_t)lrow * Hq + (int64_t)kvh * G) * nsplit + split;
+#pragma unroll
+        for (int g = 0; g < GN; g++) {
+            if ((g < GH) == (ph == 0) && g < G) {
+                // positions 0..31 first, then 32..63
+                const float o = ph == 0 ? __fadd_rn(acc[g], red[g * ATT_D + d]) : __fadd_rn(red[g * ATT_D + d], acc[g]);
+                p.part_o[(hbase + (int64_t)g * nsplit) * ATT_D + d] = o;
+            }
+        }
+        if (tid < G) {
+            p.part_ml[(hbase + (int64_t)tid * nsplit) * 2] = S.ml[tid][0];
+            p.part_ml[(hbase + (int64_t)tid * nsplit) * 2 + 1] = S.ml[tid][1];
+        }
+    }
+}
+
+// the unfused path's merge: one CTA per (kv head, query row, query head) rescales that head's
+// chunk partials by exp(m_s - M), adds them in chunk order and divides by the summed
+// denominators (the same arithmetic as the fused kernel's last-CTA merge). A kernel of its own,
+// so that the chunk CTAs end without a fence and an atomic; one head per CTA, so that a batch
+// of decode rows spreads its G * Hkv * rows merges over every SM.
+__global__ void __launch_bounds__(ATT_D) attn_merge_kernel(const AttParams p) {
+    __shared__ float cm[ATT_MAX_SPLITS];
+    __shared__ float cl;
     const int Hq = p.Hq, Hkv = p.Hkv, L = p.L, nsplit = p.nsplit, G = Hq / Hkv;
-    const int kvh = blockIdx.x, lrow = blockIdx.y;
+    const int kvh = blockIdx.x, lrow = blockIdx.y, g = blockIdx.z;
     const int row = p.row0 + lrow, l = row % L;
     pdl_trigger();  // early: the next kernel (a weight stream) may start; it waits for us in pdl_wait
     pdl_wait();
@@ -432,42 +609,39 @@ __global__ void __launch_bounds__(256, 4) attn_merge_kernel(const AttParams p) {
     if (limit < 0 || limit >= p.ctx_max) return;
     const int n_active = min(limit / ATT_C + 1, nsplit);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int64_t hbase0 = ((int64_t)lrow * Hq + (int64_t)kvh * G) * nsplit;
-    if (warp < G) {
-        const int g = warp;
-        const float* ml = p.part_ml + (hbase0 + (int64_t)g * nsplit) * 2;
+    const int64_t hb = ((int64_t)lrow * Hq + (int64_t)kvh * G + g) * nsplit;
+    if (warp == 0) {
+        const float* ml = p.part_ml + hb * 2;
         float m = -INFINITY;
         for (int s = lane; s < n_active; s += 32) m = fmaxf(m, ml[2 * s]);
         m = warp_max(m);
         float lsum = 0.0f;
         for (int s = lane; s < n_active; s += 32) {
             const float w = expf(__fsub_rn(ml[2 * s], m));
-            cm[g][s] = w;
+            cm[s] = w;
             lsum = __fadd_rn(lsum, __fmul_rn(w, ml[2 * s + 1]));
         }
         lsum = warp_sum(lsum);
-        if (lane == 0) cl[g] = lsum;
+        if (lane == 0) cl = lsum;
     }
     __syncthreads();
-    const int d = tid & (ATT_D - 1), hh = tid >> 7;
-    for (int g = hh; g < G; g += 2) {
-        const float* po = p.part_o + (hbase0 + (int64_t)g * nsplit) * ATT_D + d;
-        float o = 0.0f;
-        // the chunks' values loaded 16 at a time ahead of the ordered adds
-        int s = 0;
-        for (; s + 16 <= n_active; s += 16) {
-            float t[16];
+    const int d = tid;
+    const float* po = p.part_o + hb * ATT_D + d;
+    float o = 0.0f;
+    // the chunks' values loaded 16 at a time ahead of the ordered adds
+    int s = 0;
+    for (; s + 16 <= n_active; s += 16) {
+        float t[16];
 #pragma unroll
-            for (int i = 0; i < 16; i++) t[i] = po[(int64_t)(s + i) * ATT_D];
+        for (int i = 0; i < 16; i++) t[i] = po[(int64_t)(s + i) * ATT_D];
 #pragma unroll
-            for (int i = 0; i < 16; i++) o = __fadd_rn(o, __fmul_rn(cm[g][s + i], t[i]));
-        }
-        for (; s < n_active; s++) o = __fadd_rn(o, __fmul_rn(cm[g][s], po[(int64_t)s * ATT_D]));
-        o = __fdiv_rn(o, cl[g]);
-        const int64_t e = (int64_t)row * Hq * ATT_D + (int64_t)(kvh * G + g) * ATT_D + d;
-        if (p.out) p.out[e] = o;
-        if (p.xq) quant_warp32(o, lane, p.xq + (e - lane), p.xd + (e >> 5));
+        for (int i = 0; i < 16; i++) o = __fadd_rn(o, __fmul_rn(cm[s + i], t[i]));
     }
+    for (; s < n_active; s++) o = __fadd_rn(o, __fmul_rn(cm[s], po[(int64_t)s * ATT_D]));
+    o = __fdiv_rn(o, cl);
+    const int64_t e = (int64_t)row * Hq * ATT_D + (int64_t)(kvh * G + g) * ATT_D + d;
+    if (p.out) p.out[e] = o;
+    if (p.xq) quant_warp32(o, lane, p.xq + (e - lane), p.xd + (e >> 5));
 }
 
 // =========================================================================================
@@ -758,15 +932,25 @@ static int launch_chunks(lq_ctx* ctx, AttParams p, int64_t rows, void* scratch, 
     }
     if (zero_counters)
         LQ_CUDA(ctx, cudaMemsetAsync(p.counters, 0, (size_t)(slice * p.Hkv) * 4, ctx->stream));
+    // unfused: the bulk-copy chunk kernel (LQ_ATT_CP=1: the cp.async one)
+    const bool bulk = !FUSED && getenv("LQ_ATT_CP") == nullptr;
+    p.err = ctx->err_flag;
+    if (bulk) {
+        const int rc = ensure_func_smem(ctx, (const void*)attn_chunk_bulk_kernel<GT>, sizeof(AttSmemB));
+        if (rc) return rc;
+    }
     for (int64_t r0 = 0; r0 < rows; r0 += slice) {
         const int64_t n = std::min(slice, rows - r0);
         p.row0 = (int)r0;
         const dim3 grid(p.nsplit, (unsigned)p.Hkv, (unsigned)n);
-        int rc = launch_kernel(ctx, attn_chunk_kernel<FUSED, GT>, grid, dim3(ATT_THREADS), sizeof(Smem),
-                               "attn_chunk", p);
+        int rc = bulk ? launch_kernel(ctx, attn_chunk_bulk_kernel<GT>, grid, dim3(ATB_THREADS), sizeof(AttSmemB),
+                                      "attn_chunk_bulk", p)
+                      : launch_kernel(ctx, attn_chunk_kernel<FUSED, GT>, grid, dim3(ATT_THREADS), sizeof(Smem),
+                                      "attn_chunk", p);
         if (rc) return rc;
         if (!FUSED) {
-            rc = launch_kernel(ctx, attn_merge_kernel, dim3((unsigned)p.Hkv, (unsigned)n), dim3(256), 0,
+            rc = launch_kernel(ctx, attn_merge_kernel, dim3((unsigned)p.Hkv, (unsigned)n, (unsigned)(p.Hq / p.Hkv)),
+                               dim3(ATT_D), 0,
                                "attn_merge", p);
             if (rc) return rc;
         }

@@ -180,6 +180,60 @@ def test_attention_decode_stream_vs_oracle(ctx, lq8_lib, oracle, rng, monkeypatc
     np.testing.assert_allclose(out, ref, rtol=0, atol=4e-5 * np.abs(ref).max())
 
 
+@pytest.mark.parametrize("B,L,pos0,ctx_max,dev_pos", [(8, 1, 1030, 2048, True), (3, 1, 63, 128, True),
+                                                      (2, 1, 64, 256, False), (1, 1, 4095, 4096, True),
+                                                      (2, 5, 60, 128, True), (1, 11, 0, 64, False)])
+@pytest.mark.parametrize("Hq,Hkv", [(64, 8), (32, 8), (16, 8), (8, 8), (24, 8), (56, 8)])
+def test_attention_chunk_bulk_vs_oracle(ctx, lq8_lib, oracle, rng, monkeypatch, B, L, pos0, ctx_max, Hq, Hkv,
+                                        dev_pos):
+    """The default chunk kernel of batched decode rows and short prefills: each 64-position chunk's
+    K rows by one bulk copy per row and its V rows by one bulk copy (the rows before the step's
+    positions requested before the preceding kernel is waited on), then scores, chunk softmax and
+    P.V over 256 threads, merged per query head by the merge kernel. Every row against the
+    oracle (the position also from device memory, as graph replays pass it), chunks whose new
+    rows start mid-chunk or fill it, every group size 1..8 incl. the generic ones, the same bits
+    on a second call, the Q8_0 output the quantization of the f32 output, and the cp.async chunk
+    kernel (LQ_ATT_CP=1) within the same bound."""
+    import torch
+    D = 128
+    G = Hq // Hkv
+    T_ = pos0 + L
+    q = rng.standard_normal((B, Hq, L, D)).astype(np.float32)
+    kc = np.zeros((B, Hkv, ctx_max, D), np.float32)
+    vc = np.zeros((B, Hkv, ctx_max, D), np.float32)
+    kc[:, :, :T_] = rng.standard_normal((B, Hkv, T_, D))
+    vc[:, :, :T_] = rng.standard_normal((B, Hkv, T_, D))
+    keep = [T(a) for a in (q, kc, vc)]
+    pos_t = torch.tensor([pos0], dtype=torch.int32, device="cuda")
+
+    def run():
+        out = torch.full((B * L, Hq * D), float("nan"), dtype=torch.float32, device="cuda")
+        xq = torch.empty((B * L, Hq * D), dtype=torch.int8, device="cuda")
+        xd = torch.empty((B * L, Hq * D // 32), dtype=torch.int16, device="cuda")
+        ctx.call("lq_attention", keep[0].data_ptr(), keep[1].data_ptr(), keep[2].data_ptr(), B, Hq, Hkv, L,
+                 0 if dev_pos else pos0, pos_t.data_ptr() if dev_pos else None, ctx_max, D, out.data_ptr(),
+                 xq.data_ptr(), xd.data_ptr())
+        ctx.synchronize()
+        return H(out), H(xq), H(xd, np.uint16)
+
+    got = run()
+    again = run()
+    for a, r in zip(got, again):
+        assert np.array_equal(a.view(np.uint8), r.view(np.uint8))
+    out = got[0].reshape(B, L, Hq, D)
+    for b in range(B):
+        for l in range(L):
+            for h in range(Hq):
+                want = oracle.attend_row(q[b, h, l], kc[b, h // G, :T_], vc[b, h // G, :T_], masked=L > 1,
+                                         causal_limit=pos0 + l)
+                np.testing.assert_allclose(out[b, l, h], want, rtol=0, atol=2e-5 * np.abs(want).max())
+    oq, od = oracle.q8_0_quantize(got[0])
+    assert np.array_equal(got[1], oq) and np.array_equal(got[2], od)
+    monkeypatch.setenv("LQ_ATT_CP", "1")
+    ref = run()[0].reshape(B, L, Hq, D)
+    np.testing.assert_allclose(out, ref, rtol=0, atol=4e-5 * np.abs(ref).max())
+
+
 @pytest.mark.parametrize("B,L,pos0,ctx_max", [(1, 16, 0, 64), (2, 47, 0, 128), (1, 200, 70, 300),
                                               (2, 129, 5, 2304), (1, 2048, 0, 2304)])
 @pytest.mark.parametrize("Hq,Hkv", [(16, 8), (32, 8), (64, 8), (32, 4), (8, 8)])
