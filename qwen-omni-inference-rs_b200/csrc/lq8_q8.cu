@@ -989,15 +989,34 @@ __global__ void __launch_bounds__(SK_THREADS, 1) q8_gemm_skinny_kernel(const __g
         tma_prefetch_map(&mxd);
         int s = 0;
         unsigned ph = 0;
+        // the activations come from the preceding kernel: until pdl_wait has returned, only the
+        // weights of the first stages go out (the whole ring, while that kernel finishes), and
+        // their activation boxes follow in one batch after the wait
         bool waited = false;
+        int npend = 0;
+        int pend_k[SK_STAGES];
+        auto load_x = [&](int stage, int k) {
+            uint8_t* st = sm + (size_t)stage * SK_STAGE;
+            tma_load_2d(st + SK_OFF_X, &mx, k, 0, &full[stage]);
+            tma_load_2d(st + SK_OFF_X + SK_XBOX, &mx, k + 128, 0, &full[stage]);
+            tma_load_2d(st + SK_OFF_XD, &mxd, k / 32, 0, &full[stage]);
+        };
+        auto flush = [&]() {
+            pdl_wait();
+            waited = true;
+            for (int i = 0; i < npend; i++) load_x(i, pend_k[i]);  // stages 0 .. npend-1
+            npend = 0;
+        };
         for (long long u = u0; u < u1;) {
             const int t = sk_tile(p, u);
             const long long ts = (long long)t * p.chunks;
             const long long e = min(u1, ts + p.chunks);
             const int row = t * SK_ROWS;
             for (int c = (int)(u - ts); c < (int)(e - ts); c++) {
+                if (!waited && npend == SK_STAGES) flush();
                 if (!mbar_wait(&empty[s], ph ^ 1u)) {
                     atomicCAS(p.err, 0, 26);
+                    if (!waited) pdl_wait();
                     return;
                 }
                 uint8_t* st = sm + (size_t)s * SK_STAGE;
@@ -1006,13 +1025,10 @@ __global__ void __launch_bounds__(SK_THREADS, 1) q8_gemm_skinny_kernel(const __g
                 tma_load_2d(st, &mw, k, row, &full[s]);
                 tma_load_2d(st + SK_WBOX, &mw, k + 128, row, &full[s]);
                 tma_load_2d(st + SK_OFF_WD, &mwd, k / 32, row, &full[s]);
-                if (!waited) {  // the activations come from the preceding kernel
-                    pdl_wait();
-                    waited = true;
-                }
-                tma_load_2d(st + SK_OFF_X, &mx, k, 0, &full[s]);
-                tma_load_2d(st + SK_OFF_X + SK_XBOX, &mx, k + 128, 0, &full[s]);
-                tma_load_2d(st + SK_OFF_XD, &mxd, k / 32, 0, &full[s]);
+                if (waited)
+                    load_x(s, k);
+                else
+                    pend_k[npend++] = k;
                 if (++s == SK_STAGES) {
                     s = 0;
                     ph ^= 1u;
@@ -1020,6 +1036,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) q8_gemm_skinny_kernel(const __g
             }
             u = e;
         }
+        if (!waited) flush();
         return;
     }
     // ---------------- consumers ----------------
