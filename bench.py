@@ -342,15 +342,22 @@ def run_ours(args, cfgd, world, rank, local):
                 ce = max(ce, e)
         busy += ce - cs
         agg = {}
+        prev_end = ks[0][0]
         for s, e, n in ks:
-            a = agg.setdefault(n, [0, 0.0])
+            a = agg.setdefault(n, [0, 0.0, 0.0])
             a[0] += 1
             a[1] += e - s
+            # with programmatic dependent launch a kernel starts before its predecessor ends but
+            # cannot end before it: end-to-end deltas split the step among the kernels
+            a[2] += max(0.0, e - prev_end)
+            prev_end = max(prev_end, e)
         print(json.dumps({"trace_steps": args.trace, "us_per_step": span / args.trace,
                           "busy_us": busy, "idle_us": span - busy,
-                          "kernels": {n: {"launches": c, "us_per_launch": t / c}
-                                      for n, (c, t) in sorted(agg.items(), key=lambda x: -x[1][1])},
-                          "order": [[round(s - ks[0][0], 2), round(e - s, 2), n] for s, e, n in ks[:12]]}))
+                          "kernels": {n: {"launches": c, "us_per_launch": t / c, "end_delta_us_per_step": d / args.trace}
+                                      for n, (c, t, d) in sorted(agg.items(), key=lambda x: -x[1][2])},
+                          "order": [[round(s - ks[0][0], 2), round(e - s, 2),
+                                     round(e - (max(x[1] for x in ks[:i]) if i else s), 2), n]
+                                    for i, (s, e, n) in enumerate(ks[:24])]}))
         model.close()
         ctx.close()
         return

@@ -99,6 +99,26 @@ __device__ __forceinline__ bool mbar_wait_ns(uint64_t* bar, unsigned parity, uin
         if (global_ns() - t0 > limit_ns) return false;
     }
 }
+// try_wait with a suspend-time hint: the thread sleeps until the phase completes or about
+// `hint_ns` pass, instead of spinning
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, unsigned parity, unsigned hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait (wall time on the global timer) that sleeps between checks.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, unsigned parity, uint64_t limit_ns) {
+    if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
+        if (global_ns() - t0 > limit_ns) return false;
+    }
+}
 // one bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned); no multicast
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
     asm volatile(

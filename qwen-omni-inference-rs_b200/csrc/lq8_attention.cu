@@ -83,18 +83,13 @@ struct AttParams {
     int8_t* xq;
     uint16_t* xd;
     int rows;              // query rows of the launch (streamed decode kernel)
+    int ring;              // 1: chunk partials of the ring kernel (ranges of 32-position sub-chunks)
     int* err;
 };
 
-// two-lane fused multiply-add (sm_100 packed f32x2): (a.x*b.x + c.x, a.y*b.y + c.y)
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
-    float2 r;
-    asm("{\n .reg .b64 ra, rb, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
-        " mov.b64 rc, {%6, %7};\n fma.rn.f32x2 rd, ra, rb, rc;\n mov.b64 {%0, %1}, rd;\n}"
-        : "=f"(r.x), "=f"(r.y)
-        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-    return r;
-}
+// two-lane fused multiply-add (sm_100 packed f32x2): (a.x*b.x + c.x, a.y*b.y + c.y), through the
+// compiler's builtin so that the operand pairs stay where the register allocator puts them
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 
 __device__ __forceinline__ void quant_warp32(float v, int lane, int8_t* q_out, uint16_t* d_out) {
     float amax = warp_max(fabsf(v));
@@ -417,33 +412,48 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const AttParams
 
 // =========================================================================================
 // Unfused chunk kernel (query rows from a q tensor: batched decode rows and short prefills).
-// One CTA of 256 threads per (query row, kv head, 64-position chunk), three CTAs per SM. The
-// chunk's K rows arrive by one bulk copy per row into padded slots and its V rows by one bulk
-// copy, each set on its own mbarrier, so the scores start as soon as K has landed while V is
-// still in flight; the rows written before this step are requested before pdl_wait, the rows of
-// this launch's positions after it. Scores: thread -> (position, 64-dim half, 4 heads), two-lane
-// packed multiply-adds, the halves added by a shuffle, then the scale; a chunk softmax per head
-// (one warp per head); P.V: thread -> (dimension, 32-position half, all heads), the halves
-// added through shared memory. Partials (o, m, l) per (head, chunk) for attn_merge_kernel.
+// A fixed number of CTAs per (query row, kv head) -- nsplit, about three CTAs per SM over all
+// pairs -- each owns a contiguous range of the visible positions, cut into 32-position
+// sub-chunks that stream through a two-stage ring in shared memory: a sub-chunk's K rows (one
+// bulk copy per row, into padded slots) and V rows (one bulk copy) land on the stage's two
+// mbarriers while the other stage is computed, so one CTA's copies and arithmetic overlap and
+// its fixed costs (position read, barrier set-up, query load) are paid once per range. The rows
+// written before this step are requested before pdl_wait, the rows of this launch's positions
+// after it. Per sub-chunk: scores (thread -> (position, 64-dim half, 2 heads), two-lane packed
+// multiply-adds; the halves added through shared memory, then the scale), an online softmax
+// per head (one warp per head: running max m and sum l, the P.V sums rescaled by
+// exp(m_old - m_new)) and P.V (thread -> (dimension, 4 heads)). Out: one partial (o, m, l) per
+// (head, range) for attn_merge_kernel (ring mode). 256 threads, three CTAs per SM.
 // =========================================================================================
 constexpr int ATB_THREADS = 256;
 constexpr int ATB_QS = ATT_D + 12;  // q row stride: halves 4 floats apart (one broadcast wavefront)
+constexpr int ATB_P = 32;           // positions per sub-chunk
+constexpr int ATB_CTAS_PER_SM = 3;
 
 struct AttSmemB {
-    float ks[ATT_C][ATT_KS];          // K rows, padded: conflict-free float4 reads by position
-    float vs[ATT_C][ATT_D];
-    float qp[ATT_G][ATB_QS];          // query heads; reused for the P.V half sums
-    float pt[ATT_C][ATT_G];           // scores by position, then probabilities
-    float ml[ATT_G][2];
-    uint64_t bar[2];                  // K rows, V rows
-    int ok_k, ok_v;
+    float ks[2][ATB_P][ATT_KS];       // K rows, padded: conflict-free float4 reads by position
+    float vs[2][ATB_P][ATT_D];
+    float qp[ATT_G][ATB_QS];          // query heads
+    float sp[2][ATB_P][ATT_G];        // partial scores of the two dim halves
+    float pt[ATB_P][ATT_G];           // probabilities of the current sub-chunk
+    float al[ATT_G];                  // rescale of the running P.V sums
+    float kn[ATT_D], vn[ATT_D];       // QKV: the new position's k (normalised, rotated) and v
+    uint64_t kbar[2], vbar[2];        // per stage: K rows, V rows
+    int fail;
 };
 
-template <int GT>
-__global__ void __launch_bounds__(ATB_THREADS, 3) attn_chunk_bulk_kernel(const AttParams p) {
+// sub-chunks of 32 positions per CTA range (ring mode), from the number to attend
+__device__ __forceinline__ int ring_per(int nsub, int nsplit) { return (nsub + nsplit - 1) / nsplit; }
+
+// QKV (decode rows, L == 1, device position): the kernel also does the step before it, from the
+// fused q|k|v projection rows: the G query heads' RMSNorm + RoPE into shared memory, and, in the
+// CTA whose range holds the new position, that position's k (RMSNorm + RoPE) and v, used from
+// shared memory and appended to the caches. Every cache row it copies then predates this step,
+// so all its copies go out before pdl_wait.
+template <int GT, bool QKV>
+__global__ void __launch_bounds__(ATB_THREADS, ATB_CTAS_PER_SM) attn_chunk_bulk_kernel(const AttParams p) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     AttSmemB& S = *reinterpret_cast<AttSmemB*>(smem_raw);
-    constexpr int GN = GT ? GT : ATT_G;
     const int Hq = p.Hq, Hkv = p.Hkv, L = p.L, ctx_max = p.ctx_max, nsplit = p.nsplit;
     const int G = GT ? GT : Hq / Hkv;
     const int split = blockIdx.x, kvh = blockIdx.y, lrow = blockIdx.z;
@@ -452,142 +462,166 @@ __global__ void __launch_bounds__(ATB_THREADS, 3) attn_chunk_bulk_kernel(const A
     const int p0 = p.pos0_dev ? *p.pos0_dev : p.pos0;  // written by an earlier step: safe before pdl_wait
     const int limit = p0 + l;  // last visible position
     if (limit < 0 || limit >= ctx_max) return;
-    const int n_active = min(limit / ATT_C + 1, nsplit);
-    if (split >= n_active) return;
+    const int nsub = limit / ATB_P + 1;
+    const int per = ring_per(nsub, nsplit);
+    const int j0 = split * per, j1 = min(nsub, j0 + per);
+    if (j0 >= j1) return;
+    const int nj = j1 - j0;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int j0 = split * ATT_C;
-    const int cnt = min(ATT_C, limit + 1 - j0);
-    const int64_t slab = ((int64_t)b * Hkv + kvh) * (int64_t)ctx_max * ATT_D + (int64_t)j0 * ATT_D;
-    const float* kbase = p.kc + slab;
-    const float* vbase = p.vc + slab;
-    // rows r >= fresh hold this launch's positions (written by the preceding kernel)
-    const int fresh = max(0, min(cnt, p0 - j0));
+    const int64_t slab = ((int64_t)b * Hkv + kvh) * (int64_t)ctx_max * ATT_D;
+    float* kbase = p.kc + slab;
+    float* vbase = p.vc + slab;
+    auto cnt_of = [&](int j) { return min(ATB_P, limit + 1 - ATB_P * j); };
+    // rows copied from the caches: QKV leaves out the new position (computed here)
+    auto copied_of = [&](int j) { return cnt_of(j) - (QKV && ATB_P * j + cnt_of(j) - 1 >= p0 ? 1 : 0); };
     if (tid == 0) {
-        mbar_init(&S.bar[0], 1);
-        mbar_init(&S.bar[1], 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&S.kbar[i], 1);
+            mbar_init(&S.vbar[i], 1);
+        }
         mbar_fence_init();
-        mbar_expect_tx(&S.bar[0], (unsigned)(cnt * ATT_D * 4));
-        mbar_expect_tx(&S.bar[1], (unsigned)(cnt * ATT_D * 4));
+        for (int i = 0; i < 2 && i < nj; i++) {
+            mbar_expect_tx(&S.kbar[i], (unsigned)(copied_of(j0 + i) * ATT_D * 4));
+            mbar_expect_tx(&S.vbar[i], (unsigned)(copied_of(j0 + i) * ATT_D * 4));
+        }
+        S.fail = 0;
     }
     __syncthreads();
-    if (tid < fresh) bulk_g2s(&S.ks[tid][0], kbase + (int64_t)tid * ATT_D, ATT_D * 4, &S.bar[0]);
-    if (tid == 64 && fresh > 0) bulk_g2s(&S.vs[0][0], vbase, (unsigned)(fresh * ATT_D * 4), &S.bar[1]);
+    // copies of sub-chunk j into stage st: K row r by thread r, V rows by thread 64 + st; rows of
+    // positions before p0 (earlier steps) when pass 0, from p0 on (this launch's) when pass 1, all
+    // when pass 2 (QKV: never the row of p0)
+    auto issue = [&](int j, int st, int pass) {
+        const int c = cnt_of(j), base = ATB_P * j;
+        if (tid < c) {
+            const bool pre = base + tid < p0;
+            if ((pass == 2 || (pass == 0) == pre) && !(QKV && base + tid >= p0))
+                bulk_g2s(&S.ks[st][tid][0], kbase + (int64_t)(base + tid) * ATT_D, ATT_D * 4, &S.kbar[st]);
+        }
+        if (tid == 64 + st) {
+            const int r0 = pass == 1 ? max(base, p0) : base;
+            const int r1 = (pass == 0 || QKV) ? min(base + c, p0) : base + c;
+            if (r1 > r0)
+                bulk_g2s(&S.vs[st][r0 - base][0], vbase + (int64_t)r0 * ATT_D, (unsigned)((r1 - r0) * ATT_D * 4),
+                         &S.vbar[st]);
+        }
+    };
+    for (int i = 0; i < 2 && i < nj; i++) issue(j0 + i, i, 0);
     pdl_wait();
     pdl_trigger();
-    if (tid >= fresh && tid < cnt) bulk_g2s(&S.ks[tid][0], kbase + (int64_t)tid * ATT_D, ATT_D * 4, &S.bar[0]);
-    if (tid == 96 && fresh < cnt)
-        bulk_g2s(&S.vs[fresh][0], vbase + (int64_t)fresh * ATT_D, (unsigned)((cnt - fresh) * ATT_D * 4), &S.bar[1]);
-    // query heads (the second half of each row 4 floats further on)
-    for (int i = tid; i < G * ATT_D; i += ATB_THREADS) {
-        const int g = i / ATT_D, d = i % ATT_D;
-        S.qp[g][d + (d >= ATT_D / 2 ? 4 : 0)] = p.q[(((int64_t)b * Hq + kvh * G + g) * L + l) * ATT_D + d];
-    }
-    if (tid == 0) S.ok_k = mbar_wait_ns(&S.bar[0], 0, 2000000000ull);
-    __syncthreads();
-    if (!S.ok_k) {
-        // K never landed: report, wait (bounded) for the V copies, leave
-        if (tid == 0) {
-            if (p.err) atomicCAS(p.err, 0, 72);
-            mbar_wait_ns(&S.bar[1], 0, 2000000000ull);
+    if constexpr (QKV) {
+        // q heads: per-head RMSNorm + RoPE at position p0 (the second half 4 floats further on)
+        const int heads = Hq + 2 * Hkv;
+        const float* qrow = p.qkv + (int64_t)b * heads * ATT_D;
+        const float* cs = p.cos_t + (int64_t)p0 * (ATT_D / 2);
+        const float* sn = p.sin_t + (int64_t)p0 * (ATT_D / 2);
+        if (warp < G) head_norm_rope(qrow + (int64_t)(kvh * G + warp) * ATT_D, p.qn, p.eps, cs, sn, lane, S.qp[warp],
+                                     ATT_D / 2 + 4);
+        if (j1 == nsub) {  // this range holds the new position: its k and v, appended to the caches
+            if (warp == 0) {
+                head_norm_rope(qrow + (int64_t)(Hq + kvh) * ATT_D, p.kn, p.eps, cs, sn, lane, S.kn);
+                __syncwarp();
+                *reinterpret_cast<float4*>(kbase + (int64_t)p0 * ATT_D + 4 * lane) =
+                    *reinterpret_cast<const float4*>(&S.kn[4 * lane]);
+            } else if (warp == 1) {
+                const float4 vv = *reinterpret_cast<const float4*>(qrow + (int64_t)(Hq + Hkv + kvh) * ATT_D + 4 * lane);
+                *reinterpret_cast<float4*>(&S.vn[4 * lane]) = vv;
+                *reinterpret_cast<float4*>(vbase + (int64_t)p0 * ATT_D + 4 * lane) = vv;
+            }
         }
-        return;
+    } else {
+        for (int i = 0; i < 2 && i < nj; i++) issue(j0 + i, i, 1);
+        // query heads (the second half of each row 4 floats further on)
+        for (int i = tid; i < G * ATT_D; i += ATB_THREADS) {
+            const int g = i / ATT_D, d = i % ATT_D;
+            S.qp[g][d + (d >= ATT_D / 2 ? 4 : 0)] = p.q[(((int64_t)b * Hq + kvh * G + g) * L + l) * ATT_D + d];
+        }
     }
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)ATT_D));
-    {
-        const int hf = tid & 1, pp = (tid >> 1) & (ATT_C - 1), gh = tid >> 7;
-        float2 s2[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) s2[i] = make_float2(0.0f, 0.0f);
-        if (pp < cnt && 4 * gh < G) {
-            const float* kr = &S.ks[pp][hf * (ATT_D / 2)];
-            const float* qr = &S.qp[4 * gh][hf * (ATT_D / 2 + 4)];
+    float m_run = -INFINITY, l_run = 0.0f;  // warp g < G: head g's running max and sum
+    float2 a2[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+    const int sd = tid & (ATT_D - 1), sgh = tid >> 7;  // P.V: dimension, heads 4 sgh .. 4 sgh + 3
+    // bounded waits by thread 0; after a failure the kernel still waits (briefly) for every copy it
+    // issued and finishes on whatever landed, so no copy outlives the CTA; the error is reported
+    auto wait_bar = [&](uint64_t* bar, unsigned par) {
+        if (tid == 0 && !mbar_wait_sleep(bar, par, S.fail ? 1000000ull : 2000000000ull)) {
+            if (!S.fail && p.err) atomicCAS(p.err, 0, 72);
+            S.fail = 1;
+        }
+    };
+#pragma unroll 1
+    for (int i = 0; i < nj; i++) {
+        const int st = i & 1, j = j0 + i, ch = cnt_of(j);
+        const unsigned par = (unsigned)(i >> 1) & 1u;
+        wait_bar(&S.kbar[st], par);
+        __syncthreads();
+        {
+            const int pp = lane, hf = warp & 1, gq = warp >> 1;  // position, dim half, heads 2gq, 2gq+1
+            float2 s2[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+            if (pp < ch && 2 * gq < G) {
+                const float* kr = (QKV && ATB_P * j + pp == p0) ? &S.kn[hf * (ATT_D / 2)] : &S.ks[st][pp][hf * (ATT_D / 2)];
+                const float* qr = &S.qp[2 * gq][hf * (ATT_D / 2 + 4)];
 #pragma unroll 4
-            for (int d4 = 0; d4 < ATT_D / 8; d4++) {
-                const float4 k4 = *reinterpret_cast<const float4*>(kr + 4 * d4);
+                for (int d4 = 0; d4 < ATT_D / 8; d4++) {
+                    const float4 k4 = *reinterpret_cast<const float4*>(kr + 4 * d4);
 #pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    if (i < GN && 4 * gh + i < G) {
-                        const float4 q4 = *reinterpret_cast<const float4*>(qr + i * ATB_QS + 4 * d4);
-                        s2[i] = fma2(make_float2(q4.x, q4.y), make_float2(k4.x, k4.y), s2[i]);
-                        s2[i] = fma2(make_float2(q4.z, q4.w), make_float2(k4.z, k4.w), s2[i]);
+                    for (int e = 0; e < 2; e++) {
+                        if (2 * gq + e < G) {
+                            const float4 q4 = *reinterpret_cast<const float4*>(qr + e * ATB_QS + 4 * d4);
+                            s2[e] = fma2(make_float2(q4.x, q4.y), make_float2(k4.x, k4.y), s2[e]);
+                            s2[e] = fma2(make_float2(q4.z, q4.w), make_float2(k4.z, k4.w), s2[e]);
+                        }
                     }
                 }
             }
+#pragma unroll
+            for (int e = 0; e < 2; e++)
+                if (2 * gq + e < G) S.sp[hf][pp][2 * gq + e] = __fadd_rn(s2[e].x, s2[e].y);
         }
-        float sc[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            sc[i] = __fadd_rn(s2[i].x, s2[i].y);
-            sc[i] = __fadd_rn(sc[i], __shfl_xor_sync(0xffffffffu, sc[i], 1));
-        }
-        // half 0 stores heads 4gh, 4gh+1; half 1 heads 4gh+2, 4gh+3
-#pragma unroll
-        for (int i = 0; i < 2; i++) {
-            const int g = 4 * gh + 2 * hf + i;
-            const float v = hf ? sc[2 + i] : sc[i];
-            if (g < G) S.pt[pp][g] = pp < cnt ? __fmul_rn(v, scale) : -INFINITY;
-        }
-    }
-    if (tid == 0) S.ok_v = mbar_wait_ns(&S.bar[1], 0, 2000000000ull);
-    __syncthreads();
-    if (!S.ok_v) {
-        if (tid == 0 && p.err) atomicCAS(p.err, 0, 73);
-        return;
-    }
-    for (int g = warp; g < G; g += ATB_THREADS / 32) {
-        const float a = S.pt[lane][g], c = S.pt[lane + 32][g];
-        const float m = warp_max(fmaxf(a, c));
-        const float ea = expf(__fsub_rn(a, m)), ec = expf(__fsub_rn(c, m));
-        S.pt[lane][g] = ea;
-        S.pt[lane + 32][g] = ec;
-        const float sum = warp_sum(__fadd_rn(ea, ec));
-        if (lane == 0) { S.ml[g][0] = m; S.ml[g][1] = sum; }
-    }
-    __syncthreads();
-    {
-        const int d = tid & (ATT_D - 1), ph = tid >> 7;
-        constexpr int GP = (GN + 1) / 2;  // head pairs (two-lane fused multiply-add)
-        float2 a2[GP];
-#pragma unroll
-        for (int i = 0; i < GP; i++) a2[i] = make_float2(0.0f, 0.0f);
-        const int je = min(cnt, 32 * ph + 32);
-#pragma unroll 4
-        for (int j = 32 * ph; j < je; j++) {
-            const float vv = S.vs[j][d];
-            const float2 v2 = make_float2(vv, vv);
-            const float4 pa = *reinterpret_cast<const float4*>(&S.pt[j][0]);
-            a2[0] = fma2(make_float2(pa.x, pa.y), v2, a2[0]);
-            if constexpr (GN > 2) a2[1] = fma2(make_float2(pa.z, pa.w), v2, a2[1]);
-            if constexpr (GN > 4) {
-                const float4 pb = *reinterpret_cast<const float4*>(&S.pt[j][4]);
-                a2[2] = fma2(make_float2(pb.x, pb.y), v2, a2[2]);
-                a2[3] = fma2(make_float2(pb.z, pb.w), v2, a2[3]);
-            }
-        }
-        float acc[GN];
-#pragma unroll
-        for (int g = 0; g < GN; g++) acc[g] = (g & 1) ? a2[g >> 1].y : a2[g >> 1].x;
-        // the two position halves: half 0 finishes heads [0, GN/2), half 1 the rest; each
-        // hands the other its sums of those heads (q rows are no longer read)
-        constexpr int GH = (GN + 1) / 2;
-        float* red = &S.qp[0][0];  // [GN][ATT_D]
-#pragma unroll
-        for (int g = 0; g < GN; g++)
-            if ((g < GH) == (ph == 1)) red[g * ATT_D + d] = acc[g];
         __syncthreads();
-        const int64_t hbase = ((int64_t)lrow * Hq + (int64_t)kvh * G) * nsplit + split;
-#pragma unroll
-        for (int g = 0; g < GN; g++) {
-            if ((g < GH) == (ph == 0) && g < G) {
-                // positions 0..31 first, then 32..63
-                const float o = ph == 0 ? __fadd_rn(acc[g], red[g * ATT_D + d]) : __fadd_rn(red[g * ATT_D + d], acc[g]);
-                p.part_o[(hbase + (int64_t)g * nsplit) * ATT_D + d] = o;
+        if (warp < G) {
+            const int g = warp;
+            const float sv = lane < ch ? __fmul_rn(__fadd_rn(S.sp[0][lane][g], S.sp[1][lane][g]), scale) : -INFINITY;
+            const float mn = fmaxf(m_run, warp_max(sv));
+            const float pv = expf(__fsub_rn(sv, mn));
+            const float ps = warp_sum(pv);
+            const float a = expf(__fsub_rn(m_run, mn));  // 0 on the first sub-chunk (m_run = -inf)
+            S.pt[lane][g] = pv;
+            if (lane == 0) S.al[g] = a;
+            l_run = __fadd_rn(__fmul_rn(l_run, a), ps);
+            m_run = mn;
+        }
+        wait_bar(&S.vbar[st], par);
+        __syncthreads();
+        if (4 * sgh < G) {
+            const float4 al4 = *reinterpret_cast<const float4*>(&S.al[4 * sgh]);
+            a2[0] = make_float2(__fmul_rn(a2[0].x, al4.x), __fmul_rn(a2[0].y, al4.y));
+            a2[1] = make_float2(__fmul_rn(a2[1].x, al4.z), __fmul_rn(a2[1].y, al4.w));
+#pragma unroll 4
+            for (int r = 0; r < ch; r++) {
+                const float vv = (QKV && ATB_P * j + r == p0) ? S.vn[sd] : S.vs[st][r][sd];
+                const float2 v2 = make_float2(vv, vv);
+                const float4 pr = *reinterpret_cast<const float4*>(&S.pt[r][4 * sgh]);
+                a2[0] = fma2(make_float2(pr.x, pr.y), v2, a2[0]);
+                a2[1] = fma2(make_float2(pr.z, pr.w), v2, a2[1]);
             }
         }
-        if (tid < G) {
-            p.part_ml[(hbase + (int64_t)tid * nsplit) * 2] = S.ml[tid][0];
-            p.part_ml[(hbase + (int64_t)tid * nsplit) * 2 + 1] = S.ml[tid][1];
+        const bool refill = i + 2 < nj;
+        if (refill && tid == 0) {
+            mbar_expect_tx(&S.kbar[st], (unsigned)(copied_of(j + 2) * ATT_D * 4));
+            mbar_expect_tx(&S.vbar[st], (unsigned)(copied_of(j + 2) * ATT_D * 4));
         }
+        __syncthreads();  // stage st, pt, al and sp are free again
+        if (refill) issue(j + 2, st, 2);
+    }
+    const int64_t hbase = ((int64_t)lrow * Hq + (int64_t)kvh * G) * nsplit + split;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int g = 4 * sgh + i;
+        if (g < G) p.part_o[(hbase + (int64_t)g * nsplit) * ATT_D + sd] = (i & 1) ? a2[i >> 1].y : a2[i >> 1].x;
+    }
+    if (warp < G && lane == 0) {
+        p.part_ml[(hbase + (int64_t)warp * nsplit) * 2] = m_run;
+        p.part_ml[(hbase + (int64_t)warp * nsplit) * 2 + 1] = l_run;
     }
 }
 
@@ -607,7 +641,11 @@ __global__ void __launch_bounds__(ATT_D) attn_merge_kernel(const AttParams p) {
     const int p0 = p.pos0_dev ? *p.pos0_dev : p.pos0;
     const int limit = p0 + l;
     if (limit < 0 || limit >= p.ctx_max) return;
-    const int n_active = min(limit / ATT_C + 1, nsplit);
+    int n_active = min(limit / ATT_C + 1, nsplit);
+    if (p.ring) {
+        const int nsub = limit / ATB_P + 1;
+        n_active = (nsub + ring_per(nsub, nsplit) - 1) / ring_per(nsub, nsplit);
+    }
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t hb = ((int64_t)lrow * Hq + (int64_t)kvh * G + g) * nsplit;
     if (warp == 0) {
@@ -918,7 +956,7 @@ size_t attention_scratch_bytes(int64_t rows, int64_t Hq, int64_t ctx_max, int64_
     return ATT_COUNTER_BYTES + ml + (size_t)(slice * Hq * nsplit * ATT_D) * 4;
 }
 
-template <bool FUSED, int GT>
+template <bool FUSED, int GT, bool QKV = false>
 static int launch_chunks(lq_ctx* ctx, AttParams p, int64_t rows, void* scratch, bool zero_counters) {
     using Smem = typename std::conditional<FUSED, AttSmem, AttSmemR>::type;
     const int64_t slice = std::min<int64_t>(rows, ATT_SLICE);
@@ -932,18 +970,24 @@ static int launch_chunks(lq_ctx* ctx, AttParams p, int64_t rows, void* scratch, 
     }
     if (zero_counters)
         LQ_CUDA(ctx, cudaMemsetAsync(p.counters, 0, (size_t)(slice * p.Hkv) * 4, ctx->stream));
-    // unfused: the bulk-copy chunk kernel (LQ_ATT_CP=1: the cp.async one)
-    const bool bulk = !FUSED && getenv("LQ_ATT_CP") == nullptr;
+    // unfused: the ring kernel (LQ_ATT_CP=1: the cp.async chunk kernel), nsplit CTAs per (row,
+    // kv head): about ATB_CTAS_PER_SM per SM over the pairs of a slice, at most the 64-position
+    // chunks the scratch holds
+    const bool bulk = QKV || (!FUSED && getenv("LQ_ATT_CP") == nullptr);
     p.err = ctx->err_flag;
     if (bulk) {
-        const int rc = ensure_func_smem(ctx, (const void*)attn_chunk_bulk_kernel<GT>, sizeof(AttSmemB));
+        const int rc = ensure_func_smem(ctx, (const void*)attn_chunk_bulk_kernel<GT, QKV>, sizeof(AttSmemB));
         if (rc) return rc;
+        const int64_t pairs = std::max<int64_t>(1, slice * p.Hkv);
+        const int64_t want = ((int64_t)ATB_CTAS_PER_SM * ctx->sm_count + pairs - 1) / pairs;
+        p.nsplit = (int)std::max<int64_t>(1, std::min<int64_t>(want, p.nsplit));
+        p.ring = 1;
     }
     for (int64_t r0 = 0; r0 < rows; r0 += slice) {
         const int64_t n = std::min(slice, rows - r0);
         p.row0 = (int)r0;
         const dim3 grid(p.nsplit, (unsigned)p.Hkv, (unsigned)n);
-        int rc = bulk ? launch_kernel(ctx, attn_chunk_bulk_kernel<GT>, grid, dim3(ATB_THREADS), sizeof(AttSmemB),
+        int rc = bulk ? launch_kernel(ctx, attn_chunk_bulk_kernel<GT, QKV>, grid, dim3(ATB_THREADS), sizeof(AttSmemB),
                                       "attn_chunk_bulk", p)
                       : launch_kernel(ctx, attn_chunk_kernel<FUSED, GT>, grid, dim3(ATT_THREADS), sizeof(Smem),
                                       "attn_chunk", p);
@@ -1028,6 +1072,39 @@ int launch_attention_decode_fused(lq_ctx* ctx, const float* qkv, const uint16_t*
     p.xq = xq;
     p.xd = xd;
     return launch_chunks<true, 0>(ctx, p, B, scratch, false);
+}
+
+// Batched decode rows (L == 1, device position) straight from the fused q|k|v projection: q/k
+// RMSNorm + RoPE, the KV append and attention in the ring kernel, then the merge kernel.
+int launch_attention_decode_qkv(lq_ctx* ctx, const float* qkv, const uint16_t* qn, const uint16_t* kn, float eps,
+                                const float* cos_t, const float* sin_t, float* kc, float* vc, int64_t B, int64_t Hq,
+                                int64_t Hkv, const int32_t* pos_dev, int64_t ctx_max, int8_t* xq, uint16_t* xd,
+                                void* scratch) {
+    if (B == 0) return LQ_OK;
+    AttParams p = {};
+    p.qkv = qkv;
+    p.qn = qn;
+    p.kn = kn;
+    p.eps = eps;
+    p.cos_t = cos_t;
+    p.sin_t = sin_t;
+    p.kc = kc;
+    p.vc = vc;
+    p.Hq = (int)Hq;
+    p.Hkv = (int)Hkv;
+    p.L = 1;
+    p.pos0_dev = pos_dev;
+    p.ctx_max = (int)ctx_max;
+    p.nsplit = ceil_div(ctx_max, ATT_C);
+    p.xq = xq;
+    p.xd = xd;
+    switch (Hq / Hkv) {
+        case 8: return launch_chunks<false, 8, true>(ctx, p, B, scratch, false);
+        case 4: return launch_chunks<false, 4, true>(ctx, p, B, scratch, false);
+        case 2: return launch_chunks<false, 2, true>(ctx, p, B, scratch, false);
+        case 1: return launch_chunks<false, 1, true>(ctx, p, B, scratch, false);
+        default: return launch_chunks<false, 0, true>(ctx, p, B, scratch, false);
+    }
 }
 
 }  // namespace lq

@@ -6,6 +6,7 @@
 // (e.g. torch.distributed over gloo), every rank calls lq_comm_init. Collectives run on the
 // context's stream, so they order with the kernels and can be captured in the decode graph.
 #include "lq8_async.cuh"
+#include "lq8_fused.cuh"
 #include "lq8_internal.cuh"
 
 #include <dlfcn.h>
@@ -115,14 +116,13 @@ __device__ __forceinline__ bool ar_wait(const unsigned* p, unsigned target, int*
     }
 }
 
-__global__ void __launch_bounds__(256) xchg_allreduce_kernel(const float* __restrict__ part, int rows, int H,
-                                                               float* __restrict__ x, ArDevice a, int* err) {
-    __shared__ unsigned sdone;
-    __shared__ int ok;
-    pdl_wait();  // the partial sums are the preceding kernel's
-    const int c = blockIdx.x, T = a.tp;
-    const int per = ((H / 4 + (int)gridDim.x - 1) / (int)gridDim.x) * 4;
-    const int c0 = c * per, c1 = min(H, c0 + per), w4 = max(0, c1 - c0) / 4;
+// The exchange of one launch, CTA c (column slice [c0, c0 + 4 w4)): this rank's slice of the
+// partial sums into slot (parity, rank) of every rank's buffer, published by a system-scope
+// fence and one counter increment per peer; then a bounded wait until every peer's CTA c has
+// done the same. Leaves the launch count and the outcome in shared memory for the CTA.
+__device__ __forceinline__ void ar_exchange(const float* __restrict__ part, int rows, int H, const ArDevice& a,
+                                            int* err, int c, int c0, int w4, unsigned& sdone, int& ok) {
+    const int T = a.tp;
     if (threadIdx.x == 0) sdone = a.done[c];
     __syncthreads();
     const unsigned done = sdone;
@@ -145,20 +145,147 @@ __global__ void __launch_bounds__(256) xchg_allreduce_kernel(const float* __rest
         if (ok) a.done[c] = done + 1u;
     }
     __syncthreads();
+}
+
+// x[r][col] for one item (4 columns): the partial sums of every rank added in rank order
+__device__ __forceinline__ float4 ar_sum(const ArDevice& a, int H, unsigned done, int r, int col) {
+    const int T = a.tp;
+    const size_t slot = (size_t)ALLREDUCE_ROWS * H;
+    const float* b = a.buf[a.rank] + (size_t)(done & 1u) * T * slot;
+    float4 v = __ldcg(reinterpret_cast<const float4*>(b + (size_t)r * H + col));
+    for (int t = 1; t < T; t++) {
+        const float4 u = __ldcg(reinterpret_cast<const float4*>(b + (size_t)t * slot + (size_t)r * H + col));
+        v.x = __fadd_rn(v.x, u.x);
+        v.y = __fadd_rn(v.y, u.y);
+        v.z = __fadd_rn(v.z, u.z);
+        v.w = __fadd_rn(v.w, u.w);
+    }
+    return v;
+}
+
+__global__ void __launch_bounds__(256) xchg_allreduce_kernel(const float* __restrict__ part, int rows, int H,
+                                                               float* __restrict__ x, ArDevice a, int* err) {
+    __shared__ unsigned sdone;
+    __shared__ int ok;
+    pdl_wait();  // the partial sums are the preceding kernel's
+    const int c = blockIdx.x;
+    const int per = ((H / 4 + (int)gridDim.x - 1) / (int)gridDim.x) * 4;
+    const int c0 = c * per, c1 = min(H, c0 + per), w4 = max(0, c1 - c0) / 4;
+    ar_exchange(part, rows, H, a, err, c, c0, w4, sdone, ok);
     pdl_trigger();
     if (!ok) return;
-    const float* b = a.buf[a.rank] + (size_t)(done & 1u) * T * slot;
     for (int i = threadIdx.x; i < rows * w4; i += blockDim.x) {
         const int r = i / w4, col = c0 + 4 * (i % w4);
-        float4 v = __ldcg(reinterpret_cast<const float4*>(b + (size_t)r * H + col));
-        for (int t = 1; t < T; t++) {
-            const float4 u = __ldcg(reinterpret_cast<const float4*>(b + (size_t)t * slot + (size_t)r * H + col));
-            v.x = __fadd_rn(v.x, u.x);
-            v.y = __fadd_rn(v.y, u.y);
-            v.z = __fadd_rn(v.z, u.z);
-            v.w = __fadd_rn(v.w, u.w);
+        *reinterpret_cast<float4*>(x + (size_t)r * H + col) = ar_sum(a, H, sdone, r, col);
+    }
+}
+
+// The same all-reduce fused with the RMSNorm + Q8_0 quantization that follows it in the layer
+// (post-attention norm after o_proj, the next layer's input norm or the final norm after down;
+// rms_norm.rs:123-177). The 32 CTAs own column slices of whole Q8_0 blocks (H % 1024 == 0).
+// Each CTA writes its slice of x, adds its slice's squares of the bf16-rounded values (items of 4
+// in order, then the items in column order) into a per-row partial, and joins a counter of the
+// launch's CTAs (bounded wait; every CTA of the launch is resident: 32 small CTAs). Every CTA then
+// adds the 32 partials of a row in CTA order, so all use the same sum, and writes its slice of
+// bf16(bf16(x) * inv_rms * w) as Q8_0 blocks. The sum is grouped differently from the unfused
+// RMSNorm kernel's (a tolerance-level difference).
+struct ArNorm {
+    const uint16_t* w;   // [H] bf16 norm weights
+    float eps;
+    int8_t* xq;          // [rows][H]
+    uint16_t* xd;        // [rows][H / 32] fp16
+    float* sq;           // [2][ALLREDUCE_ROWS][ALLREDUCE_CTAS] per-row partial sums (this rank)
+    unsigned* cnt;       // arrivals of the launches' CTAs (monotonic)
+    unsigned* ndone;     // fused launches per CTA [ALLREDUCE_CTAS]
+};
+
+constexpr int ARN_ITEMS = 2;  // items of 4 columns per thread (8 rows x H/128 items <= 512)
+
+__global__ void __launch_bounds__(256) xchg_allreduce_norm_kernel(const float* __restrict__ part, int rows, int H,
+                                                                    float* __restrict__ x, ArDevice a, ArNorm n,
+                                                                    int* err) {
+    __shared__ unsigned sdone;
+    __shared__ int ok, nok;
+    __shared__ float sqi[256 * ARN_ITEMS];
+    __shared__ float inv[ALLREDUCE_ROWS];
+    pdl_wait();  // the partial sums are the preceding kernel's
+    const int c = blockIdx.x, C = (int)gridDim.x, tid = threadIdx.x;
+    const int per = H / C, c0 = c * per, w4 = per / 4, items = rows * w4;
+    ar_exchange(part, rows, H, a, err, c, c0, w4, sdone, ok);
+    pdl_trigger();
+    const unsigned nd = n.ndone[c];  // the same count in every CTA of the launch
+    float4 v[ARN_ITEMS];
+#pragma unroll
+    for (int k = 0; k < ARN_ITEMS; k++) {
+        const int i = tid + 256 * k;
+        v[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (i < items) {
+            const int r = i / w4, col = c0 + 4 * (i % w4);
+            if (ok) v[k] = ar_sum(a, H, sdone, r, col);
+            *reinterpret_cast<float4*>(x + (size_t)r * H + col) = v[k];
+            const float e0 = round_bf16(v[k].x), e1 = round_bf16(v[k].y), e2 = round_bf16(v[k].z), e3 = round_bf16(v[k].w);
+            float q = __fmul_rn(e0, e0);
+            q = __fadd_rn(q, __fmul_rn(e1, e1));
+            q = __fadd_rn(q, __fmul_rn(e2, e2));
+            q = __fadd_rn(q, __fmul_rn(e3, e3));
+            sqi[i] = q;
         }
-        *reinterpret_cast<float4*>(x + (size_t)r * H + col) = v;
+    }
+    __syncthreads();
+    float* sq = n.sq + (size_t)(nd & 1u) * ALLREDUCE_ROWS * ALLREDUCE_CTAS;
+    if (tid < rows) {
+        float ss = 0.0f;
+        for (int k = 0; k < w4; k++) ss = __fadd_rn(ss, sqi[tid * w4 + k]);
+        __stcg(sq + tid * ALLREDUCE_CTAS + c, ss);
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(n.cnt) : "memory");
+        const unsigned target = (nd + 1u) * (unsigned)C;
+        const uint64_t t0 = global_ns();
+        nok = 1;
+        for (int it = 1;; it++) {
+            unsigned got;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(got) : "l"(n.cnt) : "memory");
+            if ((int)(got - target) >= 0) break;
+            if ((it & 63) == 0 && global_ns() - t0 > 2000000000ull) {
+                atomicCAS(err, 0, 61);
+                nok = 0;
+                break;
+            }
+        }
+        n.ndone[c] = nd + 1u;
+    }
+    __syncthreads();
+    if (!ok || !nok) return;
+    if (tid < rows) {
+        float tot = 0.0f;
+        for (int q = 0; q < C; q++) tot = __fadd_rn(tot, __ldcg(sq + tid * ALLREDUCE_CTAS + q));
+        const float mean = __fdiv_rn(tot, (float)H);
+        inv[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, n.eps)));
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < ARN_ITEMS; k++) {
+        const int i = tid + 256 * k;  // 8 consecutive items = one Q8_0 block (w4 % 8 == 0)
+        const bool valid = i < items;
+        float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const int r = valid ? i / w4 : 0, col = c0 + 4 * (valid ? i % w4 : 0);
+        if (valid) {
+            const uint2 wt = *reinterpret_cast<const uint2*>(n.w + col);
+            const float wv[4] = {bf16_to_f32((uint16_t)(wt.x & 0xFFFF)), bf16_to_f32((uint16_t)(wt.x >> 16)),
+                                 bf16_to_f32((uint16_t)(wt.y & 0xFFFF)), bf16_to_f32((uint16_t)(wt.y >> 16))};
+            const float e[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                o[j] = bf16_to_f32(f32_to_bf16(__fmul_rn(__fmul_rn(round_bf16(e[j]), inv[r]), wv[j])));
+        }
+        if (256 * k < items) {  // uniform per warp group of 8: every lane joins the shuffles
+            const size_t e0 = (size_t)r * H + col;
+            const uint32_t q = quant_group8(o, tid & 7, valid ? n.xd + (e0 >> 5) : nullptr);
+            if (valid) *reinterpret_cast<uint32_t*>(n.xq + e0) = q;
+        }
     }
 }
 
@@ -181,12 +308,49 @@ int launch_xchg_allreduce(lq_ctx* ctx, const AllreduceRegions& ar, const float* 
                          (int)rows, (int)H, x, a, ctx->err_flag);
 }
 
-size_t allreduce_layout(int64_t H, int tp, size_t* flags_off, size_t* done_off) {
+size_t allreduce_layout(int64_t H, int tp, size_t* flags_off, size_t* done_off, size_t* norm_off) {
     auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
     const size_t bbytes = al((size_t)2 * tp * ALLREDUCE_ROWS * (size_t)H * 4);
     *flags_off = bbytes;
     *done_off = bbytes + al(ALLREDUCE_CTAS * 4);
-    return *done_off + al(ALLREDUCE_CTAS * 4);
+    const size_t no = *done_off + al(ALLREDUCE_CTAS * 4);
+    if (norm_off) *norm_off = no;
+    // fused norm (this rank only): row partials [2][ROWS][CTAS], a counter, launches per CTA
+    return no + al((size_t)2 * ALLREDUCE_ROWS * ALLREDUCE_CTAS * 4) + al(4) + al(ALLREDUCE_CTAS * 4);
+}
+
+bool xchg_allreduce_norm_supported(int64_t rows, int64_t H) {
+    return rows >= 1 && rows <= ALLREDUCE_ROWS && H % (32 * ALLREDUCE_CTAS) == 0 &&
+           rows * (H / ALLREDUCE_CTAS / 4) <= 256 * ARN_ITEMS && getenv("LQ_AR_NORM") != nullptr;
+}
+
+int launch_xchg_allreduce_norm(lq_ctx* ctx, const AllreduceRegions& ar, const float* part, int64_t rows, int64_t H,
+                               float* x, const uint16_t* w, float eps, int8_t* xq, uint16_t* xd) {
+    if (!xchg_allreduce_norm_supported(rows, H) || ar.tp < 2 || ar.tp > ALLREDUCE_MAX_TP)
+        return set_error(ctx, LQ_ERR_INVALID_ARG, "fused all-reduce + RMSNorm: %lld rows of %lld", (long long)rows,
+                         (long long)H);
+    size_t fo = 0, dn = 0, no = 0;
+    allreduce_layout(H, ar.tp, &fo, &dn, &no);
+    ArDevice a = {};
+    a.tp = ar.tp;
+    a.rank = ar.rank;
+    for (int t = 0; t < ar.tp; t++) {
+        a.buf[t] = static_cast<float*>(ar.region[t]);
+        a.flags[t] = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ar.region[t]) + fo);
+    }
+    uint8_t* mine = static_cast<uint8_t*>(ar.region[ar.rank]);
+    a.done = reinterpret_cast<unsigned*>(mine + dn);
+    ArNorm n = {};
+    n.w = w;
+    n.eps = eps;
+    n.xq = xq;
+    n.xd = xd;
+    n.sq = reinterpret_cast<float*>(mine + no);
+    const size_t sqb = ((size_t)2 * ALLREDUCE_ROWS * ALLREDUCE_CTAS * 4 + 255) & ~(size_t)255;
+    n.cnt = reinterpret_cast<unsigned*>(mine + no + sqb);
+    n.ndone = reinterpret_cast<unsigned*>(mine + no + sqb + 256);
+    return launch_kernel(ctx, xchg_allreduce_norm_kernel, dim3(ALLREDUCE_CTAS), dim3(256), 0, "xchg_allreduce_norm",
+                         part, (int)rows, (int)H, x, a, n, ctx->err_flag);
 }
 
 int comm_rank(const lq_comm* c) { return c ? c->rank : 0; }

@@ -187,10 +187,11 @@ __device__ __forceinline__ void quant_row(const float* __restrict__ x, int dim, 
 // Per-head RMSNorm + RoPE of one 128-dim q or k head vector by one warp (attention.rs:350-361,
 // rope.rs:245-303): lane p holds dims (2p, 2p+1) and (64+2p, 64+2p+1) -- one rotation pair
 // set, so the rotation is lane-local. src: the f32 projection output of the head; out gets
-// the rotated f32 vector.
+// the rotated f32 vector, its dims 64..127 starting at out + hi_off.
 __device__ __forceinline__ void head_norm_rope(const float* __restrict__ src, const uint16_t* __restrict__ nw,
                                                float eps, const float* __restrict__ cos_row,
-                                               const float* __restrict__ sin_row, int lane, float* out) {
+                                               const float* __restrict__ sin_row, int lane, float* out,
+                                               int hi_off = 64) {
     constexpr int D = 128, RD = 64;
     const int d0 = 2 * lane;
     const float2 a = *reinterpret_cast<const float2*>(src + d0);
@@ -209,7 +210,7 @@ __device__ __forceinline__ void head_norm_rope(const float* __restrict__ src, co
     const float r2 = __fadd_rn(__fmul_rn(v[2], cs), __fmul_rn(v[0], sn));
     const float r3 = __fadd_rn(__fmul_rn(v[3], cs), __fmul_rn(v[1], sn));
     *reinterpret_cast<float2*>(out + d0) = make_float2(r0, r1);
-    *reinterpret_cast<float2*>(out + RD + d0) = make_float2(r2, r3);
+    *reinterpret_cast<float2*>(out + hi_off + d0) = make_float2(r2, r3);  // the second half (dims 64..)
 }
 
 }  // namespace lq

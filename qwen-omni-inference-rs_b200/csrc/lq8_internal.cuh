@@ -246,6 +246,11 @@ int launch_attention_decode_fused(lq_ctx* ctx, const float* qkv, const uint16_t*
                                   float eps, const float* cos_t, const float* sin_t, float* kc, float* vc,
                                   int64_t B, int64_t Hq, int64_t Hkv, const int32_t* pos_dev, int64_t ctx_max,
                                   int8_t* xq, uint16_t* xd, void* scratch);
+// the same steps for batched decode rows through the ring chunk kernel and the merge kernel
+int launch_attention_decode_qkv(lq_ctx* ctx, const float* qkv, const uint16_t* qn, const uint16_t* kn, float eps,
+                                const float* cos_t, const float* sin_t, float* kc, float* vc, int64_t B, int64_t Hq,
+                                int64_t Hkv, const int32_t* pos_dev, int64_t ctx_max, int8_t* xq, uint16_t* xd,
+                                void* scratch);
 int launch_fill_bf16(lq_ctx* ctx, uint64_t seed, uint64_t tid, int64_t offset, int64_t count,
                      float scale, uint16_t* out);
 // rows x cols slice, at (row0, col0), of the generated tensor `tid` whose rows are src_ld long
@@ -278,9 +283,15 @@ struct AllreduceRegions {
     void* region[ALLREDUCE_MAX_TP];
     int tp, rank;
 };
-size_t allreduce_layout(int64_t H, int tp, size_t* flags_off, size_t* done_off);
+size_t allreduce_layout(int64_t H, int tp, size_t* flags_off, size_t* done_off, size_t* norm_off = nullptr);
 int launch_xchg_allreduce(lq_ctx* ctx, const AllreduceRegions& ar, const float* part, int64_t rows, int64_t H,
                           float* x);
+// the same all-reduce fused with the RMSNorm (bf16 weights w) + Q8_0 quantization of the summed
+// rows into xq/xd: rows <= ALLREDUCE_ROWS, H % 1024 == 0; opt-in (LQ_AR_NORM=1): slower than
+// the all-reduce kernel followed by the RMSNorm kernel at 32B tp2 batch 8 (933.5 vs 984.5 tok/s)
+bool xchg_allreduce_norm_supported(int64_t rows, int64_t H);
+int launch_xchg_allreduce_norm(lq_ctx* ctx, const AllreduceRegions& ar, const float* part, int64_t rows, int64_t H,
+                               float* x, const uint16_t* w, float eps, int8_t* xq, uint16_t* xd);
 int comm_world(const lq_comm* c);
 lq_ctx* comm_ctx(const lq_comm* c);
 // add `offset` to the index half of the non-zero argmax keys (a vocabulary shard's base)

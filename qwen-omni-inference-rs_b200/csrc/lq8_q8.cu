@@ -631,16 +631,35 @@ __global__ void __launch_bounds__(GS_THREADS, 2) q8_gemm_stream_kernel(const __g
         // ---------------- producer (one lane); weights may stream before pdl_wait ----------------
         if (lane != 0) return;
         int it = 0;
+        // the activations come from the preceding kernel: until pdl_wait has returned, only the
+        // weights of the first stages go out (the whole ring, while that kernel finishes), and
+        // their activation boxes follow in one batch after the wait
         bool waited = false;
+        int npend = 0;
+        int pend_k[GS_STAGES], pend_p[GS_STAGES];
+        auto load_x = [&](int s, int k, int ps) {
+            uint8_t* st = sm + (size_t)s * C::STAGE;
+            tma_load_2d(st + GS_W, &mx, k, ps * TOK, &full[s]);
+            tma_load_2d(st + GS_W + C::BOXX, &mx, k + 128, ps * TOK, &full[s]);
+            tma_load_2d(st + GS_W + C::X + GS_WD, &mxd, k / 32, ps * TOK, &full[s]);
+        };
+        auto flush = [&]() {
+            pdl_wait();
+            waited = true;
+            for (int i = 0; i < npend; i++) load_x(i, pend_k[i], pend_p[i]);  // stages 0 .. npend-1
+            npend = 0;
+        };
         for (long long item = i0; item < i1; item++) {
             const int ps = (int)(item % p.passes);
             const int sl = (int)((item / p.passes) % p.slices);
             const int rt = (int)(item / ((long long)p.passes * p.slices));
             const int k0 = sl * p.kslice, k1 = min(p.K, k0 + p.kslice);
             for (int k = k0; k < k1; k += GS_KC, it++) {
+                if (!waited && npend == GS_STAGES) flush();
                 const int s = it % GS_STAGES;
                 if (!mbar_wait(&empty[s], ((unsigned)(it / GS_STAGES) & 1u) ^ 1u)) {
                     atomicCAS(p.err, 0, 24);
+                    if (!waited) pdl_wait();
                     return;
                 }
                 uint8_t* st = sm + (size_t)s * C::STAGE;
@@ -651,15 +670,16 @@ __global__ void __launch_bounds__(GS_THREADS, 2) q8_gemm_stream_kernel(const __g
                     tma_load_2d(st + q * 2 * GS_BOXW + GS_BOXW, &mw, k + 128, row, &full[s]);
                     tma_load_2d(st + GS_W + C::X + q * 32 * 16, &mwd, k / 32, row, &full[s]);
                 }
-                if (!waited) {  // the activations come from the preceding kernel
-                    pdl_wait();
-                    waited = true;
+                if (waited) {
+                    load_x(s, k, ps);
+                } else {
+                    pend_k[npend] = k;
+                    pend_p[npend] = ps;
+                    npend++;
                 }
-                tma_load_2d(st + GS_W, &mx, k, ps * TOK, &full[s]);
-                tma_load_2d(st + GS_W + C::BOXX, &mx, k + 128, ps * TOK, &full[s]);
-                tma_load_2d(st + GS_W + C::X + GS_WD, &mxd, k / 32, ps * TOK, &full[s]);
             }
         }
+        if (!waited) flush();
         return;
     }
     // ---------------- consumers ----------------

@@ -162,6 +162,18 @@ inline int rp_reduce(lq_model* m, int64_t rows, bool moe_layer = false) {
         return lq::launch_xchg_allreduce(m->ctx, m->ar, m->part, rows, m->c.hidden, m->x);
     return lq::comm_allreduce_sum_f32(m->comm, m->part, m->x, rows * m->c.hidden);
 }
+// dense row-parallel output followed by an RMSNorm with weights w: the sum over ranks, the norm
+// and the Q8_0 quantization into xq/xd in one kernel over the exchange regions when it applies
+// (*normed then true), else the plain reduction (the caller normalises)
+inline int rp_reduce_norm(lq_model* m, int64_t rows, const uint16_t* w, bool* normed) {
+    *normed = false;
+    if (split_out(m, false) && m->ar_ok && lq::xchg_allreduce_norm_supported(rows, m->c.hidden)) {
+        *normed = true;
+        return lq::launch_xchg_allreduce_norm(m->ctx, m->ar, m->part, rows, m->c.hidden, m->x, w, m->c.eps, m->xq,
+                                              m->xd);
+    }
+    return rp_reduce(m, rows);
+}
 // greedy argmax over the vocabulary shards (dense TP): global indices, max over ranks
 inline int lm_keys_reduce(lq_model* m, int64_t B) {
     if (m->tp == 1 || m->ep) return LQ_OK;
@@ -303,12 +315,18 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
     // takes the fused attention kernel instead (one launch, its last chunk CTA merging; slower
     // at 32B batch 8 today: 11.31 against 11.21 ms per step)
     const bool fused_att = L == 1 && pos_dev && m->fused_decode && B <= 256 && getenv("LQ_ATT_FUSED") != nullptr;
+    // decode rows with a device position: the ring attention kernel takes the q|k|v rows
+    // directly (LQ_ATT_QKV_OFF=1 or LQ_ATT_CP=1: the separate q/k norm + RoPE + append kernel)
+    const bool qkv_att = L == 1 && pos_dev && B <= 256 && !fused_att && getenv("LQ_UNFUSED") == nullptr &&
+                         getenv("LQ_ATT_QKV_OFF") == nullptr && getenv("LQ_ATT_CP") == nullptr;
+    bool normed = false;  // xq/xd already hold the next norm's output (fused with the TP all-reduce)
     for (size_t li = 0; li < m->layers.size(); li++) {
         Layer& ly = m->layers[li];
         float* kc = m->kc + li * kv_layer;
         float* vc = m->vc + li * kv_layer;
         // input_layernorm -> Q8_0
-        RC(lq::launch_rmsnorm(ctx, m->x, LQ_DTYPE_F32, rows, H, ly.in_norm, c.eps, nullptr, m->xq, m->xd));
+        if (!normed) RC(lq::launch_rmsnorm(ctx, m->x, LQ_DTYPE_F32, rows, H, ly.in_norm, c.eps, nullptr, m->xq, m->xd));
+        normed = false;
         // fused q/k/v projection
         RC(lq::launch_q8_matmul_prefill(ctx, &ly.qkv, m->xq, m->xd, rows, m->qkv, nullptr, m->Nqkv));
         if (fused_att) {
@@ -316,6 +334,10 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
             // rows in one kernel (the chunks' last CTA merges)
             RC(lq::launch_attention_decode_fused(ctx, m->qkv, ly.q_norm, ly.k_norm, c.eps, m->cos_t, m->sin_t, kc,
                                                  vc, B, Hq, Hkv, pos_dev, m->ctx_max, m->xq, m->xd, m->att_scratch));
+        } else if (qkv_att) {
+            // batched decode: q/k norm, RoPE and the KV append inside the ring attention kernel
+            RC(lq::launch_attention_decode_qkv(ctx, m->qkv, ly.q_norm, ly.k_norm, c.eps, m->cos_t, m->sin_t, kc, vc,
+                                               B, Hq, Hkv, pos_dev, m->ctx_max, m->xq, m->xd, m->att_scratch));
         } else {
         RC(lq::launch_qk_norm_rope_kv(ctx, m->qkv, B, L, Hq, Hkv, D, ly.q_norm, ly.k_norm, c.eps, m->cos_t,
                                       m->sin_t, pos0, pos_dev, m->q_rot, kc, vc, m->ctx_max));
@@ -335,17 +357,25 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
         }
         // o_proj + residual (transformer.rs:194)
         RC(lq::launch_q8_matmul_prefill(ctx, &ly.o, m->xq, m->xd, rows, rp_out(m), rp_resid(m), H));
-        RC(rp_reduce(m, rows));
         if (m->moe) {
+            RC(rp_reduce(m, rows));
             RC(moe_mlp(m, ly, rows));
             continue;
         }
+        // (TP: the all-reduce of the o partial sums with post_attention_layernorm -> Q8_0)
+        RC(rp_reduce_norm(m, rows, ly.post_norm, &normed));
         // post_attention_layernorm -> Q8_0, gate/up, silu*up -> Q8_0, down + residual
-        RC(lq::launch_rmsnorm(ctx, m->x, LQ_DTYPE_F32, rows, H, ly.post_norm, c.eps, nullptr, m->xq, m->xd));
+        if (!normed) RC(lq::launch_rmsnorm(ctx, m->x, LQ_DTYPE_F32, rows, H, ly.post_norm, c.eps, nullptr, m->xq, m->xd));
         RC(lq::launch_q8_matmul_prefill(ctx, &ly.gate_up, m->xq, m->xd, rows, m->gu, nullptr, 2 * I));
         RC(lq::launch_silu_mul(ctx, m->gu, rows, I, nullptr, m->xq, m->xd));
         RC(lq::launch_q8_matmul_prefill(ctx, &ly.down, m->xq, m->xd, rows, rp_out(m), rp_resid(m), H));
-        RC(rp_reduce(m, rows));
+        // (TP: the all-reduce of the down partial sums with the next input norm, or with the final
+        // norm when every row is the last of its sequence)
+        const bool last = li + 1 == m->layers.size();
+        if (!last || L == 1)
+            RC(rp_reduce_norm(m, rows, last ? m->final_norm : m->layers[li + 1].in_norm, &normed));
+        else
+            RC(rp_reduce(m, rows));
     }
     // final norm on the last row of each sequence (model.rs:194, :357-358)
     const float* xlast = m->x;
@@ -354,7 +384,7 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
                                        H * sizeof(float), B, cudaMemcpyDeviceToDevice, ctx->stream));
         xlast = m->x_last;
     }
-    RC(lq::launch_rmsnorm(ctx, xlast, LQ_DTYPE_F32, B, H, m->final_norm, c.eps, nullptr, m->xq, m->xd));
+    if (!normed) RC(lq::launch_rmsnorm(ctx, xlast, LQ_DTYPE_F32, B, H, m->final_norm, c.eps, nullptr, m->xq, m->xd));
     // LM head with the greedy argmax fused into its epilogue
     RC(lq::launch_q8_matmul(ctx, &m->lm_head, m->xq, m->xd, B, m->logits, nullptr, m->V_l, m->keys));
     RC(lm_keys_reduce(m, B));

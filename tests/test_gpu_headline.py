@@ -216,3 +216,38 @@ def test_qwen3_30b_a3b_shapes_vs_oracle(ctx, lq8_lib, oracle):
     attention (32 / 4 heads), 2 layers, batch 64 decode after 8-token prompts."""
     _dense_vs_oracle("30b_a3b_batch64", ctx, lq8_lib, oracle, QWEN3_30B_A3B_2L, B=64, L=8, steps=3,
                      cos_min=MOE_COS, rel_max=MOE_MAXREL)
+
+
+@pytest.mark.parametrize("name,cfgd", [("32b", QWEN3_32B_2L), ("32b_tp8_shard", QWEN3_32B_TP8_SHARD)])
+def test_batched_decode_qkv_attention_equals_separate_kernels(ctx, lq8_lib, oracle, monkeypatch, name, cfgd):
+    """Batched decode (batch 8) takes the q|k|v projection rows straight into the ring attention
+    kernel (per-head RMSNorm + RoPE of q in shared memory, the new position's k and v computed,
+    used from shared memory and appended by the CTA whose range holds it). Against the path with
+    the separate q/k norm + RoPE + KV-append kernel (LQ_ATT_QKV_OFF=1): the same arithmetic, so
+    identical logits and tokens at every step, one kernel fewer per layer."""
+    B, L, steps = 8, 70, 4  # positions 70.. : the new row mid-way through a 32-position sub-chunk
+    cfg = lq8_lib.make_config(**cfgd)
+    prompts = np.stack([oracle.gen_tokens(SEED, 300 + b, L, cfgd["vocab"]) for b in range(B)])
+
+    def run():
+        gm = lq8_lib.Qwen3ForCausalLM(ctx, cfg, SEED, max_batch=B, ctx_max=L + steps + 4)
+        try:
+            tok = gm.prefill(prompts)
+            gm.set_batch(B)
+            out = [tok]
+            for _ in range(steps):
+                tok, lg = gm.decode_step(tok, want_logits=True)
+                out.append((tok, lg))
+            return out, gm.graph_kernels()
+        finally:
+            gm.close()
+
+    monkeypatch.setenv("LQ_ATT_QKV_OFF", "1")
+    ref, k_ref = run()
+    monkeypatch.delenv("LQ_ATT_QKV_OFF")
+    new, k_new = run()
+    assert np.array_equal(ref[0], new[0])
+    for i in range(1, steps + 1):
+        assert np.array_equal(new[i][1], ref[i][1]), (i, float(np.max(np.abs(new[i][1] - ref[i][1]))))
+        assert np.array_equal(new[i][0], ref[i][0]), i
+    assert k_ref - k_new == cfgd["layers"], (k_ref, k_new)

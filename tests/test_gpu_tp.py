@@ -255,6 +255,8 @@ def _tp32_rank_main(rank, world, port, q, prompts, fed, path):
         os.environ["LQ_TP_NCCL"] = "1"
     elif path == "persistent":
         os.environ["LQ_PERSIST_MAX_BATCH"] = "8"
+    elif path == "arnorm":
+        os.environ["LQ_AR_NORM"] = "1"
     for p in (REPO, os.path.join(REPO, "qwen-omni-inference-rs_b200")):
         sys.path.insert(0, p)
     import datetime
@@ -289,14 +291,15 @@ def _tp32_rank_main(rank, world, port, q, prompts, fed, path):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("path", ["persistent", "default", "nccl"])
+@pytest.mark.parametrize("path", ["persistent", "default", "nccl", "arnorm"])
 def test_tensor_parallel_32b_shapes_2_gpus(oracle, path):
     """Config 4's shapes (2 layers, full vocabulary) as two tensor-parallel ranks at batch 8:
     each rank holds 32 / 4 heads, 12800 intermediate rows, 75968 LM-head rows. "persistent"
     (LQ_PERSIST_MAX_BATCH=8): the persistent decode step with the o/down partial sums exchanged
     inside the kernel over NVLink (a 3-kernel decode graph); "default": the per-layer kernels with
     the one-shot all-reduce over the ranks' CUDA-IPC regions; "nccl" (LQ_TP_NCCL=1): the
-    per-layer kernels with NCCL all-reduces. All teacher-forced against the single-device
+    per-layer kernels with NCCL all-reduces; "arnorm" (LQ_AR_NORM=1): the one-shot all-reduce
+    fused with the RMSNorm + Q8_0 quantization that follows it. All teacher-forced against the single-device
     oracle with the tolerance of the headline-shape tests (the noise floor of these shapes;
     test_gpu_headline.py), tokens equal wherever the oracle's margin exceeds twice the step's
     difference."""
