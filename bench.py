@@ -606,6 +606,50 @@ def run_sweep(args):
         torch.cuda.empty_cache()
 
 
+def run_prefill_gemm(args):
+    """Prefill GEMM: the exact tcgen05 kernel (lq_q8_0_matmul) against the fp16-operand kernel
+    (lq_q8_0_matmul_prefill) at the config-2 prefill shapes, on the same pre-quantized operands
+    (random Q8_0 weights and activation rows); median of per-launch CUDA-event times after
+    warm-up, TOPS = 2 m n k / time. One JSON line per (case, kernel)."""
+    import ctypes as C
+
+    import torch
+
+    import build
+    import lq8
+    build.build()
+    ctx = lq8.Context(0)
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=dev)
+    cases = ([tuple(int(v) for v in args.prefill_gemm_case.split(","))] if args.prefill_gemm_case else
+             [(m, n, k) for m in (512, 2048) for (n, k) in ((6144, 4096), (4096, 4096), (24576, 4096), (4096, 12288),
+                                                           (10240, 5120), (51200, 5120), (5120, 25600))])
+    reps = max(args.sweep_reps, 3)
+    g = torch.Generator(device=dev).manual_seed(SEED)
+    for (m, n, k) in cases:
+        w = lq8.QTensor.quantize(ctx, (torch.randn((n, k), generator=g, device=dev) * 0.02).to(torch.bfloat16))
+        xq = torch.randint(-127, 128, (m, k), dtype=torch.int8, device=dev, generator=g)
+        xd = torch.full((m, k // 32), 0x2000, dtype=torch.int16, device=dev)  # fp16 0.0078
+        y = torch.empty((m, n), dtype=torch.float32, device=dev)
+        ws = w.struct()
+        for name in ("lq_q8_0_matmul", "lq_q8_0_matmul_prefill"):
+            for _ in range(3):
+                ctx.call(name, C.byref(ws), xq.data_ptr(), xd.data_ptr(), m, y.data_ptr(), None, n)
+            ctx.synchronize()
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+            for i in range(reps):
+                ev[i][0].record(stream)
+                ctx.call(name, C.byref(ws), xq.data_ptr(), xd.data_ptr(), m, y.data_ptr(), None, n)
+                ev[i][1].record(stream)
+            ctx.synchronize()
+            us = statistics.median(a.elapsed_time(b) for a, b in ev) * 1e3
+            print(json.dumps({"prefill_gemm": "exact" if name == "lq_q8_0_matmul" else "fp16 operands", "m": m,
+                              "n": n, "k": k, "us": round(us, 2), "TOPS": round(2.0 * m * n * k / us / 1e6, 1)}),
+                  flush=True)
+        del w
+        torch.cuda.empty_cache()
+
+
 def run_moe(args):
     """MoE layer alone: lq_moe_forward (router, top-k, grouped expert GEMVs, combine) at the
     Qwen3-30B-A3B expert shape (128 experts, hidden 2048, moe_inter 768, top-8) with random
@@ -690,6 +734,9 @@ def main():
     ap.add_argument("--sweep-case", default="",
                     help="with --sweep: one case 'm,n,k' (two weight copies; for profiling)")
     ap.add_argument("--sweep-reps", type=int, default=20)
+    ap.add_argument("--prefill-gemm", action="store_true",
+                    help="time the exact and the fp16-operand prefill GEMMs at the config-2 prefill shapes and exit")
+    ap.add_argument("--prefill-gemm-case", default="", help="with --prefill-gemm: one case 'm,n,k'")
     ap.add_argument("--tp", type=int, default=0,
                     help="model parallelism over the torchrun ranks: tensor-parallel for dense configs, "
                          "expert-parallel for MoE; 0 = all ranks, 1 = independent replicas")
@@ -699,6 +746,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.prefill_gemm:
+        run_prefill_gemm(args)
+        return
     if args.sweep:
         run_sweep(args)
         return

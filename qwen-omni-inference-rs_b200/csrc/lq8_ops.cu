@@ -26,6 +26,9 @@ rmsnorm_kernel(const T* __restrict__ x, int dim, const uint16_t* __restrict__ w,
                uint16_t* __restrict__ out, int8_t* __restrict__ xq, uint16_t* __restrict__ xd) {
     __shared__ float red[32];
     pdl_trigger();  // early: the next kernel (a weight stream) may start; it waits for us in pdl_wait
+    // the norm weights do not depend on the preceding kernel: bring them into L2 while it ends
+    for (int b = threadIdx.x * 64; b < dim; b += NORM_THREADS * 64)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(w + b));
     pdl_wait();
     const int64_t row = blockIdx.x;
     rms_row<T, NORM_THREADS, 0, 8>(x + row * dim, dim, w, eps, threadIdx.x, red, out ? out + row * dim : nullptr,

@@ -946,6 +946,7 @@ struct SkParams {
     int tiles, chunks;            // 128-row tiles; 256-byte units per tile
     int whole;                    // 1: whole tiles per CTA (no split)
     int narrow;                   // 1: (units + 1) * grid < 2^32 (32-bit unit arithmetic)
+    int early;                    // ring stages whose weights go out before pdl_wait (1..SK_STAGES)
     long long units;              // tiles * chunks
     const float* resid;
     float* y;
@@ -1033,7 +1034,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) q8_gemm_skinny_kernel(const __g
             const long long e = min(u1, ts + p.chunks);
             const int row = t * SK_ROWS;
             for (int c = (int)(u - ts); c < (int)(e - ts); c++) {
-                if (!waited && npend == SK_STAGES) flush();
+                if (!waited && npend == p.early) flush();
                 if (!mbar_wait(&empty[s], ph ^ 1u)) {
                     atomicCAS(p.err, 0, 26);
                     if (!waited) pdl_wait();
@@ -1237,6 +1238,8 @@ static int launch_gemm_skinny(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* 
     p.whole = getenv("LQ_GEMM_NO_SPLIT") ? 1 : 0;
     const int grid = sk_grid(ctx, w->n, w->k, p.whole != 0);
     p.narrow = (uint64_t)(p.units + 1) * (uint64_t)grid < (1ull << 32) ? 1 : 0;
+    p.early = SK_STAGES;
+    if (const char* e = getenv("LQ_SK_EARLY")) p.early = std::max(1, std::min(SK_STAGES, atoi(e)));
     p.resid = resid;
     p.y = y;
     p.ldy = (int)ldy;
