@@ -625,6 +625,260 @@ __global__ void __launch_bounds__(ATB_THREADS, ATB_CTAS_PER_SM) attn_chunk_bulk_
     }
 }
 
+// =========================================================================================
+// The ring kernel's arithmetic on the tensor cores (the default for batched decode rows; the
+// f32 FMA kernel above with LQ_ATT_FMA=1). Same ranges, two-stage ring, copies, online softmax
+// and partials; scores and P.V are `mma.sync.m16n8k8` TF32 products with f32 accumulation, each
+// f32 operand split as x = big + small (big = tf32(x), small = tf32(x - big)) and every product
+// formed as small·big + big·small + big·big, so it keeps ~22 bits of each operand (the dropped
+// small·small term is below 2^-22 of the product; the attention tolerance is 2e-5 of the row's
+// max). Scores: S^T[position][head] = K·q^T, warp w owns 16 positions (w & 1) and 32 dims
+// (w >> 1): 4 k-steps whose K fragments come by ldmatrix from the padded K rows and whose q
+// fragments sit in registers for the whole range; the four dim groups' partial scores meet in
+// shared memory. P.V: O^T[dim][head] = V^T·P^T, warp w owns 16 dims, 4 k-steps of 8 positions;
+// the accumulators stay in registers across the range, rescaled by exp(m_old - m_new). V rows
+// arrive one bulk copy per row into slots of 136 floats, so the transposed fragment loads hit
+// 32 different banks.
+// =========================================================================================
+constexpr int ATM_VS = ATT_D + 8;   // V row stride (floats)
+
+struct AttSmemM {
+    float ks[2][ATB_P][ATT_KS];       // K rows (stride 132: ldmatrix rows in 8 bank groups)
+    float vs[2][ATB_P][ATM_VS];       // V rows
+    union {
+        float qs[ATT_G][ATT_KS];      // query heads (read once into registers)
+        float sp[4][ATB_P][ATT_G + 1]; // the four dim groups' partial scores (padded)
+    } u;
+    float pt[ATT_G][ATB_P + 4];       // probabilities, [head][position]
+    float al[ATT_G];                  // rescale of the running P.V sums
+    float kn[ATT_D], vn[ATT_D];       // QKV: the new position's k (normalised, rotated) and v
+    uint64_t kbar[2], vbar[2];
+    int fail;
+};
+
+static_assert((sizeof(AttSmemM) + 1024) * ATB_CTAS_PER_SM <= 228 * 1024, "three MMA ring CTAs must fit one SM");
+static_assert((sizeof(AttSmemB) + 1024) * ATB_CTAS_PER_SM <= 228 * 1024, "three FMA ring CTAs must fit one SM");
+
+__device__ __forceinline__ uint32_t tf32_big(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+// x = big + small (both tf32)
+__device__ __forceinline__ void tf32_split(float x, uint32_t& big, uint32_t& small) {
+    big = tf32_big(x);
+    small = tf32_big(__fsub_rn(x, __uint_as_float(big)));
+}
+// D += A(16x8 tf32, row) * B(8x8 tf32, col), f32 accumulate
+__device__ __forceinline__ void mma_tf32(float d[4], const uint32_t a[4], const uint32_t b[2]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+// D += A*B with both operands split: small*big + big*small + big*big
+__device__ __forceinline__ void mma_tf32x3(float d[4], const uint32_t ab[4], const uint32_t as[4], const uint32_t bb[2],
+                                           const uint32_t bs[2]) {
+    mma_tf32(d, as, bb);
+    mma_tf32(d, ab, bs);
+    mma_tf32(d, ab, bb);
+}
+
+template <int GT, bool QKV>
+__global__ void __launch_bounds__(ATB_THREADS, ATB_CTAS_PER_SM) attn_chunk_mma_kernel(const AttParams p) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    AttSmemM& S = *reinterpret_cast<AttSmemM*>(smem_raw);
+    const int Hq = p.Hq, Hkv = p.Hkv, L = p.L, ctx_max = p.ctx_max, nsplit = p.nsplit;
+    const int G = GT ? GT : Hq / Hkv;
+    const int split = blockIdx.x, kvh = blockIdx.y, lrow = blockIdx.z;
+    const int row = p.row0 + lrow;  // b*L + l
+    const int b = row / L, l = row - (row / L) * L;
+    const int p0 = p.pos0_dev ? *p.pos0_dev : p.pos0;  // written by an earlier step: safe before pdl_wait
+    const int limit = p0 + l;  // last visible position
+    if (limit < 0 || limit >= ctx_max) return;
+    const int nsub = limit / ATB_P + 1;
+    const int per = ring_per(nsub, nsplit);
+    const int j0 = split * per, j1 = min(nsub, j0 + per);
+    if (j0 >= j1) return;
+    const int nj = j1 - j0;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;  // fragment row group, thread in group
+    const int64_t slab = ((int64_t)b * Hkv + kvh) * (int64_t)ctx_max * ATT_D;
+    float* kbase = p.kc + slab;
+    float* vbase = p.vc + slab;
+    auto cnt_of = [&](int j) { return min(ATB_P, limit + 1 - ATB_P * j); };
+    auto copied_of = [&](int j) { return cnt_of(j) - (QKV && ATB_P * j + cnt_of(j) - 1 >= p0 ? 1 : 0); };
+    if (tid == 0) {
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&S.kbar[i], 1);
+            mbar_init(&S.vbar[i], 1);
+        }
+        mbar_fence_init();
+        for (int i = 0; i < 2 && i < nj; i++) {
+            mbar_expect_tx(&S.kbar[i], (unsigned)(copied_of(j0 + i) * ATT_D * 4));
+            mbar_expect_tx(&S.vbar[i], (unsigned)(copied_of(j0 + i) * ATT_D * 4));
+        }
+        S.fail = 0;
+    }
+    __syncthreads();
+    // copies of sub-chunk j into stage st: K row r by thread r, V row r by thread 64 + r; rows of
+    // positions before p0 when pass 0, from p0 on when pass 1, all when pass 2 (QKV: never p0's)
+    auto issue = [&](int j, int st, int pass) {
+        const int c = cnt_of(j), base = ATB_P * j;
+        const int r = tid & 63;
+        if (r < c && tid < 128) {
+            const bool pre = base + r < p0;
+            if ((pass == 2 || (pass == 0) == pre) && !(QKV && base + r >= p0)) {
+                if (tid < 64)
+                    bulk_g2s(&S.ks[st][r][0], kbase + (int64_t)(base + r) * ATT_D, ATT_D * 4, &S.kbar[st]);
+                else
+                    bulk_g2s(&S.vs[st][r][0], vbase + (int64_t)(base + r) * ATT_D, ATT_D * 4, &S.vbar[st]);
+            }
+        }
+    };
+    for (int i = 0; i < 2 && i < nj; i++) issue(j0 + i, i, 0);
+    pdl_wait();
+    pdl_trigger();
+    if constexpr (QKV) {
+        const int heads = Hq + 2 * Hkv;
+        const float* qrow = p.qkv + (int64_t)b * heads * ATT_D;
+        const float* cs = p.cos_t + (int64_t)p0 * (ATT_D / 2);
+        const float* sn = p.sin_t + (int64_t)p0 * (ATT_D / 2);
+        if (warp < G) head_norm_rope(qrow + (int64_t)(kvh * G + warp) * ATT_D, p.qn, p.eps, cs, sn, lane, S.u.qs[warp]);
+        if (j1 == nsub) {  // this range holds the new position: its k and v, appended to the caches
+            if (warp == 0) {
+                head_norm_rope(qrow + (int64_t)(Hq + kvh) * ATT_D, p.kn, p.eps, cs, sn, lane, S.kn);
+                __syncwarp();
+                *reinterpret_cast<float4*>(kbase + (int64_t)p0 * ATT_D + 4 * lane) =
+                    *reinterpret_cast<const float4*>(&S.kn[4 * lane]);
+            } else if (warp == 1) {
+                const float4 vv = *reinterpret_cast<const float4*>(qrow + (int64_t)(Hq + Hkv + kvh) * ATT_D + 4 * lane);
+                *reinterpret_cast<float4*>(&S.vn[4 * lane]) = vv;
+                *reinterpret_cast<float4*>(vbase + (int64_t)p0 * ATT_D + 4 * lane) = vv;
+            }
+        }
+    } else {
+        for (int i = 0; i < 2 && i < nj; i++) issue(j0 + i, i, 1);
+        for (int i = tid; i < G * ATT_D; i += ATB_THREADS) {
+            const int hh = i / ATT_D, d = i % ATT_D;
+            S.u.qs[hh][d] = p.q[(((int64_t)b * Hq + kvh * G + hh) * L + l) * ATT_D + d];
+        }
+    }
+    __syncthreads();
+    // this warp's q fragments for its four k-steps (B[k][n] = q[head n][dim k]; heads >= G are 0)
+    const int mt = warp & 1, kg = warp >> 1;  // scores: positions 16 mt .., dims 32 kg ..
+    uint32_t qb[4][2], qsm[4][2];
+#pragma unroll
+    for (int ks = 0; ks < 4; ks++) {
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const float v = g < G ? S.u.qs[g][32 * kg + 8 * ks + t + 4 * h] : 0.0f;
+            tf32_split(v, qb[ks][h], qsm[ks][h]);
+        }
+    }
+    __syncthreads();  // q is in registers: the union now holds partial scores
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)ATT_D));
+    float m_run = -INFINITY, l_run = 0.0f;  // warp h < G: head h's running max and sum
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // O^T rows (dims) 16 warp + g, + 8; cols (heads) 2t, 2t+1
+    auto wait_bar = [&](uint64_t* bar, unsigned par) {
+        if (tid == 0 && !mbar_wait_sleep(bar, par, S.fail ? 1000000ull : 2000000000ull)) {
+            if (!S.fail && p.err) atomicCAS(p.err, 0, 74);
+            S.fail = 1;
+        }
+    };
+    const int lr = 16 * mt + (lane & 7) + 8 * ((lane >> 3) & 1);  // the K row this lane addresses
+#pragma unroll 1
+    for (int i = 0; i < nj; i++) {
+        const int st = i & 1, j = j0 + i, ch = cnt_of(j);
+        const unsigned par = (unsigned)(i >> 1) & 1u;
+        const int fr = (QKV && p0 >= ATB_P * j && p0 < ATB_P * j + ATB_P) ? p0 - ATB_P * j : -1;  // new row
+        wait_bar(&S.kbar[st], par);
+        __syncthreads();
+        {
+            float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            const float* krow = (lr == fr) ? S.kn : &S.ks[st][lr][0];
+#pragma unroll
+            for (int ks = 0; ks < 4; ks++) {
+                uint32_t a[4], ab[4], as[4];
+                ldmatrix_x4(a, krow + 32 * kg + 8 * ks + 4 * (lane >> 4));
+#pragma unroll
+                for (int e = 0; e < 4; e++) tf32_split(__uint_as_float(a[e]), ab[e], as[e]);
+                mma_tf32x3(c, ab, as, qb[ks], qsm[ks]);
+            }
+            S.u.sp[kg][16 * mt + g][2 * t] = c[0];
+            S.u.sp[kg][16 * mt + g][2 * t + 1] = c[1];
+            S.u.sp[kg][16 * mt + g + 8][2 * t] = c[2];
+            S.u.sp[kg][16 * mt + g + 8][2 * t + 1] = c[3];
+        }
+        __syncthreads();
+        if (warp < G) {
+            const int h = warp;
+            float sv = -INFINITY;
+            if (lane < ch) {
+                const float s01 = __fadd_rn(S.u.sp[0][lane][h], S.u.sp[1][lane][h]);
+                const float s23 = __fadd_rn(S.u.sp[2][lane][h], S.u.sp[3][lane][h]);
+                sv = __fmul_rn(__fadd_rn(s01, s23), scale);
+            }
+            const float mn = fmaxf(m_run, warp_max(sv));
+            const float pv = expf(__fsub_rn(sv, mn));
+            const float ps = warp_sum(pv);
+            const float a = expf(__fsub_rn(m_run, mn));  // 0 on the first sub-chunk (m_run = -inf)
+            S.pt[h][lane] = pv;
+            if (lane == 0) S.al[h] = a;
+            l_run = __fadd_rn(__fmul_rn(l_run, a), ps);
+            m_run = mn;
+        }
+        wait_bar(&S.vbar[st], par);
+        __syncthreads();
+        {
+            // rescale the running sums of heads 2t, 2t+1 (heads >= G are never written)
+            const float s0 = 2 * t < G ? S.al[2 * t] : 0.0f, s1 = 2 * t + 1 < G ? S.al[2 * t + 1] : 0.0f;
+            acc[0] = __fmul_rn(acc[0], s0);
+            acc[1] = __fmul_rn(acc[1], s1);
+            acc[2] = __fmul_rn(acc[2], s0);
+            acc[3] = __fmul_rn(acc[3], s1);
+            const int d0 = 16 * warp + g;
+#pragma unroll
+            for (int ks = 0; ks < 4; ks++) {
+                const int k0 = 8 * ks;
+                if (k0 < ch) {  // uniform
+                    const int r0 = k0 + t, r1 = k0 + t + 4;
+                    auto vget = [&](int r, int d) -> float {
+                        if (r >= ch) return 0.0f;
+                        return r == fr ? S.vn[d] : S.vs[st][r][d];
+                    };
+                    const float va[4] = {vget(r0, d0), vget(r0, d0 + 8), vget(r1, d0), vget(r1, d0 + 8)};
+                    uint32_t ab[4], as[4], bb[2], bs[2];
+#pragma unroll
+                    for (int e = 0; e < 4; e++) tf32_split(va[e], ab[e], as[e]);
+                    tf32_split(g < G ? S.pt[g][r0] : 0.0f, bb[0], bs[0]);
+                    tf32_split(g < G ? S.pt[g][r1] : 0.0f, bb[1], bs[1]);
+                    mma_tf32x3(acc, ab, as, bb, bs);
+                }
+            }
+        }
+        const bool refill = i + 2 < nj;
+        if (refill && tid == 0) {
+            mbar_expect_tx(&S.kbar[st], (unsigned)(copied_of(j + 2) * ATT_D * 4));
+            mbar_expect_tx(&S.vbar[st], (unsigned)(copied_of(j + 2) * ATT_D * 4));
+        }
+        __syncthreads();  // stage st, pt, al and the partial scores are free again
+        if (refill) issue(j + 2, st, 2);
+    }
+    const int64_t hbase = ((int64_t)lrow * Hq + (int64_t)kvh * G) * nsplit + split;
+    const int d0 = 16 * warp + g;
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        const int h = 2 * t + (e & 1), d = d0 + 8 * (e >> 1);
+        if (h < G) p.part_o[(hbase + (int64_t)h * nsplit) * ATT_D + d] = acc[e];
+    }
+    if (warp < G && lane == 0) {
+        p.part_ml[(hbase + (int64_t)warp * nsplit) * 2] = m_run;
+        p.part_ml[(hbase + (int64_t)warp * nsplit) * 2 + 1] = l_run;
+    }
+}
+
 // the unfused path's merge: one CTA per (kv head, query row, query head) rescales that head's
 // chunk partials by exp(m_s - M), adds them in chunk order and divides by the summed
 // denominators (the same arithmetic as the fused kernel's last-CTA merge). A kernel of its own,
@@ -974,9 +1228,12 @@ static int launch_chunks(lq_ctx* ctx, AttParams p, int64_t rows, void* scratch, 
     // kv head): about ATB_CTAS_PER_SM per SM over the pairs of a slice, at most the 64-position
     // chunks the scratch holds
     const bool bulk = QKV || (!FUSED && getenv("LQ_ATT_CP") == nullptr);
+    // the ring's arithmetic on the tensor cores (3xTF32), or on the CUDA cores (LQ_ATT_FMA=1)
+    const bool mma = bulk && getenv("LQ_ATT_FMA") == nullptr;
     p.err = ctx->err_flag;
     if (bulk) {
-        const int rc = ensure_func_smem(ctx, (const void*)attn_chunk_bulk_kernel<GT, QKV>, sizeof(AttSmemB));
+        const int rc = mma ? ensure_func_smem(ctx, (const void*)attn_chunk_mma_kernel<GT, QKV>, sizeof(AttSmemM))
+                           : ensure_func_smem(ctx, (const void*)attn_chunk_bulk_kernel<GT, QKV>, sizeof(AttSmemB));
         if (rc) return rc;
         const int64_t pairs = std::max<int64_t>(1, slice * p.Hkv);
         const int64_t want = ((int64_t)ATB_CTAS_PER_SM * ctx->sm_count + pairs - 1) / pairs;
@@ -987,7 +1244,9 @@ static int launch_chunks(lq_ctx* ctx, AttParams p, int64_t rows, void* scratch, 
         const int64_t n = std::min(slice, rows - r0);
         p.row0 = (int)r0;
         const dim3 grid(p.nsplit, (unsigned)p.Hkv, (unsigned)n);
-        int rc = bulk ? launch_kernel(ctx, attn_chunk_bulk_kernel<GT, QKV>, grid, dim3(ATB_THREADS), sizeof(AttSmemB),
+        int rc = mma ? launch_kernel(ctx, attn_chunk_mma_kernel<GT, QKV>, grid, dim3(ATB_THREADS), sizeof(AttSmemM),
+                                     "attn_chunk_mma", p)
+                 : bulk ? launch_kernel(ctx, attn_chunk_bulk_kernel<GT, QKV>, grid, dim3(ATB_THREADS), sizeof(AttSmemB),
                                       "attn_chunk_bulk", p)
                       : launch_kernel(ctx, attn_chunk_kernel<FUSED, GT>, grid, dim3(ATT_THREADS), sizeof(Smem),
                                       "attn_chunk", p);

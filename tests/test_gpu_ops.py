@@ -186,14 +186,16 @@ def test_attention_decode_stream_vs_oracle(ctx, lq8_lib, oracle, rng, monkeypatc
 @pytest.mark.parametrize("Hq,Hkv", [(64, 8), (32, 8), (16, 8), (8, 8), (24, 8), (56, 8)])
 def test_attention_chunk_bulk_vs_oracle(ctx, lq8_lib, oracle, rng, monkeypatch, B, L, pos0, ctx_max, Hq, Hkv,
                                         dev_pos):
-    """The default chunk kernel of batched decode rows and short prefills: each 64-position chunk's
-    K rows by one bulk copy per row and its V rows by one bulk copy (the rows before the step's
-    positions requested before the preceding kernel is waited on), then scores, chunk softmax and
-    P.V over 256 threads, merged per query head by the merge kernel. Every row against the
-    oracle (the position also from device memory, as graph replays pass it), chunks whose new
-    rows start mid-chunk or fill it, every group size 1..8 incl. the generic ones, the same bits
-    on a second call, the Q8_0 output the quantization of the f32 output, and the cp.async chunk
-    kernel (LQ_ATT_CP=1) within the same bound."""
+    """The ring kernel of batched decode rows and short prefills: per (row, kv head) a few CTAs,
+    each streaming its range of 32-position sub-chunks through a two-stage ring (K and V rows by
+    bulk copies; the rows before the step's positions requested before the preceding kernel is
+    waited on), scores and P.V as 3xTF32 tensor-core products (default) or f32 FMAs
+    (LQ_ATT_FMA=1), an online softmax, one partial per range merged per query head by the merge
+    kernel. Every row against the oracle (the position also from device memory, as graph replays
+    pass it), ranges whose new rows start mid-sub-chunk or fill it, every group size 1..8 incl.
+    the generic ones, the same bits on a second call, the Q8_0 output the quantization of the
+    f32 output; the FMA variant and the cp.async chunk kernel (LQ_ATT_CP=1) within the same
+    bound."""
     import torch
     D = 128
     G = Hq // Hkv
@@ -229,6 +231,15 @@ def test_attention_chunk_bulk_vs_oracle(ctx, lq8_lib, oracle, rng, monkeypatch, 
                 np.testing.assert_allclose(out[b, l, h], want, rtol=0, atol=2e-5 * np.abs(want).max())
     oq, od = oracle.q8_0_quantize(got[0])
     assert np.array_equal(got[1], oq) and np.array_equal(got[2], od)
+    monkeypatch.setenv("LQ_ATT_FMA", "1")
+    fma = run()[0].reshape(B, L, Hq, D)
+    for b in range(B):
+        for l in range(L):
+            for h in range(Hq):
+                want = oracle.attend_row(q[b, h, l], kc[b, h // G, :T_], vc[b, h // G, :T_], masked=L > 1,
+                                         causal_limit=pos0 + l)
+                np.testing.assert_allclose(fma[b, l, h], want, rtol=0, atol=2e-5 * np.abs(want).max())
+    monkeypatch.delenv("LQ_ATT_FMA")
     monkeypatch.setenv("LQ_ATT_CP", "1")
     ref = run()[0].reshape(B, L, Hq, D)
     np.testing.assert_allclose(out, ref, rtol=0, atol=4e-5 * np.abs(ref).max())
