@@ -366,14 +366,16 @@ int forward(lq_model* m, int64_t B, int64_t L, int64_t pos0, const int32_t* pos_
         RC(rp_reduce_norm(m, rows, ly.post_norm, &normed));
         // post_attention_layernorm -> Q8_0, gate/up, silu*up -> Q8_0, down + residual
         if (!normed) RC(lq::launch_rmsnorm(ctx, m->x, LQ_DTYPE_F32, rows, H, ly.post_norm, c.eps, nullptr, m->xq, m->xd));
+        normed = false;  // consumed: xq / xd now feed gate|up
         RC(lq::launch_q8_matmul_prefill(ctx, &ly.gate_up, m->xq, m->xd, rows, m->gu, nullptr, 2 * I));
         RC(lq::launch_silu_mul(ctx, m->gu, rows, I, nullptr, m->xq, m->xd));
-        RC(lq::launch_q8_matmul_prefill(ctx, &ly.down, m->xq, m->xd, rows, rp_out(m), rp_resid(m), H));
         // (TP: the all-reduce of the down partial sums with the next input norm, or with the final
         // norm when every row is the last of its sequence)
         const bool last = li + 1 == m->layers.size();
+        const uint16_t* next_norm = last ? m->final_norm : m->layers[li + 1].in_norm;
+        RC(lq::launch_q8_matmul_prefill(ctx, &ly.down, m->xq, m->xd, rows, rp_out(m), rp_resid(m), H));
         if (!last || L == 1)
-            RC(rp_reduce_norm(m, rows, last ? m->final_norm : m->layers[li + 1].in_norm, &normed));
+            RC(rp_reduce_norm(m, rows, next_norm, &normed));
         else
             RC(rp_reduce(m, rows));
     }
