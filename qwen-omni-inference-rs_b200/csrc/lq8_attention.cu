@@ -664,9 +664,10 @@ __device__ __forceinline__ uint32_t tf32_big(float x) {
     asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
     return r;
 }
-// x = big + small (both tf32)
+// x = big + small (both tf32): big = x with its low 13 mantissa bits cleared (exact), small =
+// the remainder (exact in f32, at most 2^-10 |x|) rounded to tf32: |x - big - small| <= 2^-22 |x|
 __device__ __forceinline__ void tf32_split(float x, uint32_t& big, uint32_t& small) {
-    big = tf32_big(x);
+    big = __float_as_uint(x) & 0xFFFFE000u;
     small = tf32_big(__fsub_rn(x, __uint_as_float(big)));
 }
 // D += A(16x8 tf32, row) * B(8x8 tf32, col), f32 accumulate
@@ -844,11 +845,22 @@ __global__ void __launch_bounds__(ATB_THREADS, ATB_CTAS_PER_SM) attn_chunk_mma_k
                 const int k0 = 8 * ks;
                 if (k0 < ch) {  // uniform
                     const int r0 = k0 + t, r1 = k0 + t + 4;
-                    auto vget = [&](int r, int d) -> float {
-                        if (r >= ch) return 0.0f;
-                        return r == fr ? S.vn[d] : S.vs[st][r][d];
-                    };
-                    const float va[4] = {vget(r0, d0), vget(r0, d0 + 8), vget(r1, d0), vget(r1, d0 + 8)};
+                    float va[4];
+                    if (k0 + 8 <= ch && fr < 0) {  // uniform: a full k-step of cache rows
+                        va[0] = S.vs[st][r0][d0];
+                        va[1] = S.vs[st][r0][d0 + 8];
+                        va[2] = S.vs[st][r1][d0];
+                        va[3] = S.vs[st][r1][d0 + 8];
+                    } else {
+                        auto vget = [&](int r, int d) -> float {
+                            if (r >= ch) return 0.0f;
+                            return r == fr ? S.vn[d] : S.vs[st][r][d];
+                        };
+                        va[0] = vget(r0, d0);
+                        va[1] = vget(r0, d0 + 8);
+                        va[2] = vget(r1, d0);
+                        va[3] = vget(r1, d0 + 8);
+                    }
                     uint32_t ab[4], as[4], bb[2], bs[2];
 #pragma unroll
                     for (int e = 0; e < 4; e++) tf32_split(va[e], ab[e], as[e]);

@@ -1209,7 +1209,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) q8_gemm_skinny_kernel(const __g
 }
 
 static bool sk_supported(const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd, int64_t m) {
-    return m >= 5 && m <= 8 && w->k % SK_KC == 0 && w->n % 64 == 0 && w->n < (1ll << 31) &&
+    return m >= 5 && m <= 8 && w->k % SK_KC == 0 && w->n % 8 == 0 && w->n < (1ll << 31) &&
            ((uintptr_t)w->qs % 16) == 0 && ((uintptr_t)w->d % 16) == 0 && ((uintptr_t)xq % 16) == 0 &&
            ((uintptr_t)xd % 16) == 0 && !getenv("LQ_NO_GEMM_SKINNY");
 }
@@ -1221,7 +1221,7 @@ static int sk_grid(lq_ctx* ctx, int64_t n, int64_t k, bool whole) {
 }
 
 static size_t sk_partial_bytes(lq_ctx* ctx, int64_t n, int64_t k) {
-    if (k % SK_KC != 0 || n % 64 != 0) return 0;
+    if (k % SK_KC != 0 || n % 8 != 0) return 0;
     return (size_t)sk_grid(ctx, n, k, false) * 2 * SK_CONS * 32 * sizeof(float4);
 }
 

@@ -138,11 +138,13 @@ def test_gemm_small_m_split_within_reorder_bound(ctx, lq8_lib, oracle, rng, m, n
 
 
 @pytest.mark.parametrize("m,n,k", [(5, 320, 2048), (6, 1280, 5120), (7, 64, 256), (8, 320, 2048), (8, 1280, 5120),
-                                   (8, 5120, 25600), (5, 10240, 5120), (8, 10240, 5120), (7, 3200, 5120)])
+                                   (8, 5120, 25600), (5, 10240, 5120), (8, 10240, 5120), (7, 3200, 5120),
+                                   (5, 1000, 2048), (8, 18992, 5120)])
 def test_gemm_skinny_stream_k_within_reorder_bound(ctx, lq8_lib, oracle, rng, m, n, k):
     """The 5-8-token GEMM deals 256-byte K units of 128-row tiles evenly over one CTA per SM,
     so tiles are cut between CTAs at arbitrary units (the decode shapes of Qwen3-32B and its
-    tensor-parallel shards here); the last CTA of a cut tile adds the pieces in CTA order.
+    tensor-parallel shards here, incl. the tp8 rank's 18992-row LM head, whose last tile is
+    ragged); the last CTA of a cut tile adds the pieces in CTA order.
     Every output is written (NaN-filled y), within the regrouping bound, and deterministic."""
     wq, wd = _weights(oracle, rng, n, k)
     xq, xd = oracle.q8_0_quantize(rng.standard_normal((m, k)).astype(np.float32))
