@@ -976,7 +976,10 @@ __device__ __forceinline__ int sk_tile(const SkParams& p, long long u) {
     return p.narrow ? (int)((unsigned)u / (unsigned)p.chunks) : (int)(u / p.chunks);
 }
 
-__global__ void __launch_bounds__(SK_THREADS, 1) q8_gemm_skinny_kernel(const __grid_constant__ CUtensorMap mw,
+// ST ring stages, MINB CTAs per SM: (6, 1) by default; (3, 2) with LQ_SK_DUAL=1 (two CTAs per SM,
+// sixteen consumer warps per SM, each CTA with a 3-stage ring)
+template <int ST, int MINB>
+__global__ void __launch_bounds__(SK_THREADS, MINB) q8_gemm_skinny_kernel(const __grid_constant__ CUtensorMap mw,
                                                                        const __grid_constant__ CUtensorMap mwd,
                                                                        const __grid_constant__ CUtensorMap mx,
                                                                        const __grid_constant__ CUtensorMap mxd,
@@ -984,13 +987,13 @@ __global__ void __launch_bounds__(SK_THREADS, 1) q8_gemm_skinny_kernel(const __g
     extern __shared__ __align__(16) uint8_t smem_raw[];
     const uint32_t raw = smem_addr(smem_raw);
     uint8_t* sm = smem_raw + (((raw + 1023) & ~1023u) - raw);
-    uint64_t* full = reinterpret_cast<uint64_t*>(sm + (size_t)SK_STAGES * SK_STAGE);
-    uint64_t* empty = full + SK_STAGES;
-    unsigned long long* ckeys = reinterpret_cast<unsigned long long*>(empty + SK_STAGES);  // [8]
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + (size_t)ST * SK_STAGE);
+    uint64_t* empty = full + ST;
+    unsigned long long* ckeys = reinterpret_cast<unsigned long long*>(empty + ST);  // [8]
     int* last_flag = reinterpret_cast<int*>(ckeys + 8);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < SK_STAGES; s++) {
+        for (int s = 0; s < ST; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], SK_CONS);
         }
@@ -1015,7 +1018,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) q8_gemm_skinny_kernel(const __g
         // their activation boxes follow in one batch after the wait
         bool waited = false;
         int npend = 0;
-        int pend_k[SK_STAGES];
+        int pend_k[ST];
         auto load_x = [&](int stage, int k) {
             uint8_t* st = sm + (size_t)stage * SK_STAGE;
             tma_load_2d(st + SK_OFF_X, &mx, k, 0, &full[stage]);
@@ -1050,7 +1053,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) q8_gemm_skinny_kernel(const __g
                     load_x(s, k);
                 else
                     pend_k[npend++] = k;
-                if (++s == SK_STAGES) {
+                if (++s == ST) {
                     s = 0;
                     ph ^= 1u;
                 }
@@ -1083,7 +1086,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) q8_gemm_skinny_kernel(const __g
         for (int c = c0; c < c1; c++) {
             const int cs = s;
             const unsigned cph = ph;
-            if (++s == SK_STAGES) {
+            if (++s == ST) {
                 s = 0;
                 ph ^= 1u;
             }
@@ -1215,14 +1218,17 @@ static bool sk_supported(const lq_q8_tensor* w, const int8_t* xq, const uint16_t
 }
 
 // CTAs of the skinny GEMM: one per SM, never more than the units (or tiles, unsplit)
-static int sk_grid(lq_ctx* ctx, int64_t n, int64_t k, bool whole) {
+// CTAs of the skinny GEMM: `per_sm` per SM, never more than the units (or tiles, unsplit)
+static int sk_grid(lq_ctx* ctx, int64_t n, int64_t k, bool whole, int per_sm = 1) {
     const int64_t tiles = (n + SK_ROWS - 1) / SK_ROWS, units = tiles * (k / SK_KC);
-    return (int)std::min<int64_t>(std::min<int64_t>(ctx->sm_count, kTileCounters), whole ? tiles : units);
+    return (int)std::min<int64_t>(std::min<int64_t>((int64_t)per_sm * ctx->sm_count, kTileCounters),
+                                  whole ? tiles : units);
 }
 
+// partial-sum bytes of either configuration (sized for two CTAs per SM)
 static size_t sk_partial_bytes(lq_ctx* ctx, int64_t n, int64_t k) {
     if (k % SK_KC != 0 || n % 8 != 0) return 0;
-    return (size_t)sk_grid(ctx, n, k, false) * 2 * SK_CONS * 32 * sizeof(float4);
+    return (size_t)sk_grid(ctx, n, k, false, 2) * 2 * SK_CONS * 32 * sizeof(float4);
 }
 
 static int launch_gemm_skinny(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd, int64_t m,
@@ -1236,10 +1242,12 @@ static int launch_gemm_skinny(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* 
     p.chunks = (int)(w->k / SK_KC);
     p.units = (long long)p.tiles * p.chunks;
     p.whole = getenv("LQ_GEMM_NO_SPLIT") ? 1 : 0;
-    const int grid = sk_grid(ctx, w->n, w->k, p.whole != 0);
+    const bool dual = getenv("LQ_SK_DUAL") != nullptr;
+    const int stages = dual ? 3 : SK_STAGES;
+    const int grid = sk_grid(ctx, w->n, w->k, p.whole != 0, dual ? 2 : 1);
     p.narrow = (uint64_t)(p.units + 1) * (uint64_t)grid < (1ull << 32) ? 1 : 0;
-    p.early = SK_STAGES;
-    if (const char* e = getenv("LQ_SK_EARLY")) p.early = std::max(1, std::min(SK_STAGES, atoi(e)));
+    p.early = stages;
+    if (const char* e = getenv("LQ_SK_EARLY")) p.early = std::max(1, std::min(stages, atoi(e)));
     p.resid = resid;
     p.y = y;
     p.ldy = (int)ldy;
@@ -1263,9 +1271,15 @@ static int launch_gemm_skinny(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* 
         rc = make_tensor_map_2d(ctx, &mxd, CU_TENSOR_MAP_DATA_TYPE_UINT16, xd, (uint64_t)(w->k / 32), (uint64_t)m,
                                 (uint64_t)(w->k / 32) * 2, 8, 8, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
-    if ((rc = ensure_func_smem(ctx, (const void*)q8_gemm_skinny_kernel, SK_SMEM))) return rc;
-    return launch_kernel(ctx, q8_gemm_skinny_kernel, dim3(grid), dim3(SK_THREADS), SK_SMEM, "q8_gemm_skinny", mw,
-                         mwd, mx, mxd, p);
+    if (dual) {
+        const size_t smem = (size_t)3 * SK_STAGE + 1024 + 256;
+        if ((rc = ensure_func_smem(ctx, (const void*)q8_gemm_skinny_kernel<3, 2>, smem))) return rc;
+        return launch_kernel(ctx, q8_gemm_skinny_kernel<3, 2>, dim3(grid), dim3(SK_THREADS), smem, "q8_gemm_skinny",
+                             mw, mwd, mx, mxd, p);
+    }
+    if ((rc = ensure_func_smem(ctx, (const void*)q8_gemm_skinny_kernel<SK_STAGES, 1>, SK_SMEM))) return rc;
+    return launch_kernel(ctx, q8_gemm_skinny_kernel<SK_STAGES, 1>, dim3(grid), dim3(SK_THREADS), SK_SMEM,
+                         "q8_gemm_skinny", mw, mwd, mx, mxd, p);
 }
 
 int launch_q8_matmul(lq_ctx* ctx, const lq_q8_tensor* w, const int8_t* xq, const uint16_t* xd,
