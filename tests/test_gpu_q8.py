@@ -156,6 +156,21 @@ def test_gemm_skinny_stream_k_within_reorder_bound(ctx, lq8_lib, oracle, rng, m,
     assert np.array_equal(y, _matmul(ctx, lq8_lib, wq, wd, xq, xd))
 
 
+@pytest.mark.parametrize("m,n,k", [(8, 10240, 5120), (5, 1000, 2048), (8, 5120, 25600)])
+def test_gemm_skinny_two_ctas_per_sm(ctx, lq8_lib, oracle, rng, monkeypatch, m, n, k):
+    """The opt-in configuration with two CTAs per SM and 3-stage rings (LQ_SK_DUAL=1): twice the
+    CTAs, so tiles are cut at other units; within the regrouping bound and deterministic."""
+    monkeypatch.setenv("LQ_SK_DUAL", "1")
+    wq, wd = _weights(oracle, rng, n, k)
+    xq, xd = oracle.q8_0_quantize(rng.standard_normal((m, k)).astype(np.float32))
+    y = _matmul(ctx, lq8_lib, wq, wd, xq, xd)
+    assert not np.isnan(y).any()
+    ref, absum = oracle.q8_0_matmul(xq, xd, wq, wd, with_abs=True)
+    bound = 2.0 * (k // 32 + 1) * 2.0 ** -24 * absum + 1e-30
+    assert np.all(np.abs(y - ref) <= bound), float(np.max(np.abs(y - ref) / bound))
+    assert np.array_equal(y, _matmul(ctx, lq8_lib, wq, wd, xq, xd))
+
+
 def test_gemm_skinny_counters_reset_between_launches(ctx, lq8_lib, oracle, rng):
     """The per-tile arrival counters of the stream-K combine are reset by each tile's last CTA:
     shapes with different cut points launched in turn, three rounds, give the same bits every
